@@ -1,0 +1,218 @@
+/*
+ * minicpmo_gpu.h -- C ABI of libminicpmo_gpu_helper.so, the B200 (sm_100a)
+ * drop-in for the GPU helper of uya-lang/minicpm-o-uya.
+ *
+ * Part 1 is the reference helper ABI, symbol for symbol: the reference's
+ * bridge (src/minicpmo/gpu_bridge.c:72-90) dlmopen()s
+ * <exe dir>/libminicpmo_gpu_helper.so and requires exactly these 19 symbols
+ * (gpu_bridge.c:146-176); each declaration cites the reference
+ * implementation it replaces (src/minicpmo/gpu_shim.c).  Conventions are the
+ * reference's: functions return 1 on success and 0 on error, copying an
+ * "error: ..." message into (error, error_cap); dtype integers are the Uya
+ * TensorDType ordinals F32=0, F16=1, Q8_0=6, Q4_K=10, Q6_K=12, BF16=20
+ * (src/minicpmo/tensor.uya:31-54); weight tensors are keyed by the caller's
+ * host pointer (gpu_shim.c:1592-1600); 2-D tensors pass cols = shape[0]
+ * (contiguous) and rows = shape[1] (src/minicpmo/gpu.uya:137-148).
+ *
+ * Part 2 holds versioned extensions (discover with dlsym; old hosts ignore
+ * them): device embedding lookup and greedy sampler, the fused whole-token
+ * Qwen3 decode step, batched decode, tensor-parallel contexts, and
+ * measurement/parity helpers.
+ */
+#ifndef MINICPMO_GPU_H
+#define MINICPMO_GPU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MINICPMO_API __attribute__((visibility("default")))
+#else
+#define MINICPMO_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* gpu_bridge.c:11-25 / gpu_shim.c:129-143: 13 x u64, layout fixed (the
+ * caller allocates it). */
+typedef struct minicpmo_gpu_stats {
+    uint64_t backend_init_us;
+    uint64_t host_to_device_bytes;
+    uint64_t device_to_host_bytes;
+    uint64_t weight_upload_bytes;
+    uint64_t scratch_x_bytes;
+    uint64_t scratch_y_bytes;
+    uint64_t uploaded_weight_count;
+    uint64_t native_quant_matvec_count;
+    uint64_t staged_quant_matvec_count;
+    uint64_t q8_1_x_bytes;
+    uint64_t attention_kernel_calls;
+    uint64_t kv_device_bytes;
+    uint64_t kv_host_to_device_bytes;
+} minicpmo_gpu_stats;
+
+/* ===================== Part 1: reference helper ABI ===================== */
+
+/* gpu_shim.c:2207-2345 */
+MINICPMO_API int minicpmo_gpu_context_create(unsigned int device_index, int debug, void **out_handle, char *error, size_t error_cap);
+/* gpu_shim.c:2347-2423 (NULL-safe) */
+MINICPMO_API void minicpmo_gpu_context_destroy(void *handle);
+/* gpu_shim.c:2425-2454 */
+MINICPMO_API int minicpmo_gpu_context_smoke(void *handle, char *error, size_t error_cap);
+/* gpu_shim.c:2456-2527 */
+MINICPMO_API int minicpmo_gpu_context_upload_tensor(void *handle, const char *name, const void *host_ptr, size_t bytes, int dtype,
+                                       size_t rows, size_t cols, char *error, size_t error_cap);
+/* gpu_shim.c:2529-2719 (host x in, host dst out) */
+MINICPMO_API int minicpmo_gpu_context_matvec(void *handle, const char *tensor_name, const void *host_ptr, int dtype, const float *x,
+                                size_t in_dim, size_t out_dim, float *dst, char *error, size_t error_cap);
+/* gpu_shim.c:1385-1454 */
+MINICPMO_API int minicpmo_gpu_context_prepare_attention(void *handle, size_t layer_count, size_t context_capacity, size_t kv_dim,
+                                           char *error, size_t error_cap);
+/* gpu_shim.c:1456-1590 (host q/k/v in, host dst out; appends k/v at pos) */
+MINICPMO_API int minicpmo_gpu_context_attention(void *handle, const float *q, const float *k, const float *v, size_t layer, size_t pos,
+                                   size_t head_count, size_t kv_head_count, size_t head_dim, size_t context_capacity,
+                                   float *dst, char *error, size_t error_cap);
+/* gpu_shim.c:2721-2747 */
+MINICPMO_API int minicpmo_gpu_context_slot_upload_f32(void *handle, unsigned int slot, const float *src, size_t len, char *error,
+                                         size_t error_cap);
+/* gpu_shim.c:2749-2774 (synchronises) */
+MINICPMO_API int minicpmo_gpu_context_slot_download_f32(void *handle, unsigned int slot, float *dst, size_t len, char *error,
+                                           size_t error_cap);
+/* gpu_shim.c:2776-3008 */
+MINICPMO_API int minicpmo_gpu_context_slot_matvec(void *handle, unsigned int dst_slot, const char *tensor_name, const void *host_ptr,
+                                     int dtype, unsigned int src_slot, size_t in_dim, size_t out_dim, char *error,
+                                     size_t error_cap);
+/* gpu_shim.c:3233-3255 */
+MINICPMO_API int minicpmo_gpu_context_slot_matvec2(void *handle, unsigned int dst_slot0, const char *tensor_name0,
+                                      const void *host_ptr0, int dtype0, size_t out_dim0, unsigned int dst_slot1,
+                                      const char *tensor_name1, const void *host_ptr1, int dtype1, size_t out_dim1,
+                                      unsigned int src_slot, size_t in_dim, char *error, size_t error_cap);
+/* gpu_shim.c:3257-3284 */
+MINICPMO_API int minicpmo_gpu_context_slot_matvec3(void *handle, unsigned int dst_slot0, const char *tensor_name0,
+                                      const void *host_ptr0, int dtype0, size_t out_dim0, unsigned int dst_slot1,
+                                      const char *tensor_name1, const void *host_ptr1, int dtype1, size_t out_dim1,
+                                      unsigned int dst_slot2, const char *tensor_name2, const void *host_ptr2,
+                                      int dtype2, size_t out_dim2, unsigned int src_slot, size_t in_dim, char *error,
+                                      size_t error_cap);
+/* gpu_shim.c:3286-3368 */
+MINICPMO_API int minicpmo_gpu_context_slot_rms_norm(void *handle, unsigned int dst_slot, unsigned int src_slot,
+                                       const void *weight_host_ptr, size_t n, float eps, char *error, size_t error_cap);
+/* gpu_shim.c:3370-3448 (in place, eps 1e-6) */
+MINICPMO_API int minicpmo_gpu_context_slot_head_norm(void *handle, unsigned int slot, const void *weight_host_ptr, size_t head_count,
+                                        size_t head_dim, char *error, size_t error_cap);
+/* gpu_shim.c:3450-3526 (table keyed by host pointer; NULL tables -> computed) */
+MINICPMO_API int minicpmo_gpu_context_slot_rope(void *handle, unsigned int slot, size_t head_count, size_t head_dim, size_t pos,
+                                   float freq_base, float freq_scale, const float *rope_cos, const float *rope_sin,
+                                   size_t rope_context, char *error, size_t error_cap);
+/* gpu_shim.c:3528-3577 */
+MINICPMO_API int minicpmo_gpu_context_slot_add_inplace(void *handle, unsigned int dst_slot, unsigned int src_slot, size_t len,
+                                          char *error, size_t error_cap);
+/* gpu_shim.c:3579-3633 */
+MINICPMO_API int minicpmo_gpu_context_slot_silu_mul(void *handle, unsigned int dst_slot, unsigned int gate_slot,
+                                       unsigned int up_slot, size_t len, char *error, size_t error_cap);
+/* gpu_shim.c:3635-3743 (appends k/v at pos, then attends) */
+MINICPMO_API int minicpmo_gpu_context_attention_slots(void *handle, unsigned int dst_slot, unsigned int q_slot, unsigned int k_slot,
+                                         unsigned int v_slot, size_t layer, size_t pos, size_t head_count,
+                                         size_t kv_head_count, size_t head_dim, size_t context_capacity, char *error,
+                                         size_t error_cap);
+/* gpu_shim.c:3745-3753 */
+MINICPMO_API void minicpmo_gpu_context_snapshot(void *handle, minicpmo_gpu_stats *stats);
+
+/* ========================= Part 2: extensions =========================== */
+
+#define MINICPMO_GPU_ABI_VERSION 1
+
+/* No reference counterpart: lets a host detect the extensions. */
+MINICPMO_API int minicpmo_gpu_abi_version(void);
+
+/* Stream the context enqueues on (cudaStream_t as void*).  The reference uses
+ * the legacy NULL stream (gpu_shim.c:1238-1248); this helper owns a
+ * non-blocking stream.  set_stream adopts a caller stream (not owned). */
+MINICPMO_API void *minicpmo_gpu_context_stream(void *handle);
+MINICPMO_API int minicpmo_gpu_context_set_stream(void *handle, void *stream, char *error, size_t error_cap);
+
+/* Device token-embedding dequant lookup into a slot (replaces the host
+ * qwen3_copy_embedding, src/minicpmo/qwen3.uya:1164-1174, and its 4*h byte
+ * upload per token, qwen3.uya:1876). */
+MINICPMO_API int minicpmo_gpu_context_embed_lookup(void *handle, unsigned int dst_slot, const void *host_ptr, int dtype,
+                                      uint32_t token, size_t hidden, char *error, size_t error_cap);
+
+/* Device greedy sampler over a slot (replaces the host
+ * qwen3_argmax_penalized, qwen3.uya:1734-1752, and its 4*V byte download):
+ * first maximum of the penalised values, plus the gap to the second best. */
+MINICPMO_API int minicpmo_gpu_context_argmax_penalized(void *handle, unsigned int slot, size_t n, const uint32_t *seen,
+                                          size_t seen_count, float penalty, uint32_t *out_id, float *out_top2_gap,
+                                          char *error, size_t error_cap);
+
+/* Whole-model decode step (replaces the ~20 calls per layer of
+ * qwen3_forward_embedding_runtime_cuda, qwen3.uya:1865-1918, with one CUDA
+ * graph launch).  Tensors are found in the upload registry by their GGUF
+ * names (blk.N.attn_q.weight, ...; output.weight, then lm_head.weight, then
+ * token_embd.weight for the lm_head as tensor_lookup_root_output,
+ * src/minicpmo/tensor.uya:503-509). */
+typedef struct minicpmo_qwen3_config {
+    uint32_t layers, hidden, heads, kv_heads, head_dim, ffn, vocab, context;
+    float rms_eps;          /* the reference forward uses 1e-6 (qwen3.uya:108) */
+    float rope_freq_base;   /* qwen3.rope.freq_base, default 1e6 */
+    float rope_freq_scale;  /* 1/linear factor (qwen3.uya:1578-1603) */
+    const float *rope_cos;  /* host tables [context][head_dim/2] or NULL: */
+    const float *rope_sin;  /*   then built as qwen3_precompute_rope (qwen3.uya:1633-1662) */
+    int kv_f16;             /* 0: f32 KV cache (reference); 1: f16 */
+    int max_batch;          /* sequences for forward_batch (0 -> 1) */
+    int reserved[6];
+} minicpmo_qwen3_config;
+
+MINICPMO_API int minicpmo_gpu_context_qwen3_bind(void *handle, const minicpmo_qwen3_config *config, char *error, size_t error_cap);
+
+/* Forward `token` at `pos` (qwen3_forward_token_runtime, qwen3.uya:1991-1995)
+ * and sample greedily on the device.  flags bit 0: skip the lm_head and the
+ * sampler (prompt tokens that need no logits).  logits_out (may be NULL)
+ * receives the vocab logits; hidden_out (may be NULL) the final hidden
+ * state.  repeat_penalty <= 1 disables the penalty (qwen3.uya:1734-1752);
+ * every forwarded token joins the penalty's seen set. */
+MINICPMO_API int minicpmo_gpu_context_qwen3_forward(void *handle, uint32_t token, size_t pos, int flags, float repeat_penalty,
+                                       uint32_t *out_token, float *out_top2_gap, float *logits_out, float *hidden_out,
+                                       char *error, size_t error_cap);
+/* Clears the sampler's seen set (a new session, qwen3.uya:2999-3007). */
+MINICPMO_API int minicpmo_gpu_context_qwen3_reset(void *handle, char *error, size_t error_cap);
+
+/* Greedy decode of n_steps tokens entirely on the device, feeding each
+ * sampled token back (the generate loop, qwen3.uya:2559-2639, without host
+ * round trips).  tokens_out[n_steps] receives the sampled ids. */
+MINICPMO_API int minicpmo_gpu_context_qwen3_decode(void *handle, uint32_t first_token, size_t first_pos, size_t n_steps,
+                                      float repeat_penalty, uint32_t *tokens_out, char *error, size_t error_cap);
+
+/* ---- parity and measurement helpers (no reference counterpart) ---- */
+
+/* Device Q8_1 quantisation of host f32 values (36-byte blocks, the
+ * reference's host quantiser gpu_shim.c:336-401 bit for bit). */
+MINICPMO_API int minicpmo_gpu_context_q8_1_quantize(void *handle, const float *x, size_t n, void *xq_out, char *error,
+                                       size_t error_cap);
+/* Device RMSNorm -> Q8_1 producer of the decode step on host data:
+ * out = x * (1/sqrtf(sum(x^2)/n + eps)) * w with the sum in the order of
+ * gpu_shim.c:694-718; the weight is an uploaded tensor. */
+MINICPMO_API int minicpmo_gpu_context_rms_norm_q8_1(void *handle, const float *x, const void *weight_host_ptr, size_t n, float eps,
+                                       float *out, void *xq_out, char *error, size_t error_cap);
+/* GEMV of an uploaded quantised tensor with caller-given Q8_1 activations;
+ * dots_out (may be NULL) receives every per-block int32 dot, row-major
+ * [out_dim][in_dim/32] (Q4_K, Q8_0) or [out_dim][in_dim/16] (Q6_K). */
+MINICPMO_API int minicpmo_gpu_context_matvec_q8_1(void *handle, const void *host_ptr, const void *xq, size_t in_dim, size_t out_dim,
+                                     float *y_out, int32_t *dots_out, char *error, size_t error_cap);
+/* Runs the GEMV of an uploaded tensor `iters` times back to back on
+ * device-resident activations and reports the mean kernel time (CUDA
+ * events on the context stream). */
+MINICPMO_API int minicpmo_gpu_context_time_matvec(void *handle, const void *host_ptr, size_t in_dim, size_t out_dim, int iters,
+                                     float *avg_us, char *error, size_t error_cap);
+/* Device time of n_steps auto-advancing decode steps (graph replays, no host
+ * copies); reports the total milliseconds. */
+MINICPMO_API int minicpmo_gpu_context_qwen3_time_decode(void *handle, uint32_t first_token, size_t first_pos, size_t n_steps,
+                                           float *total_ms, char *error, size_t error_cap);
+/* Bytes of device memory held by the uploaded copy of a tensor. */
+MINICPMO_API size_t minicpmo_gpu_context_tensor_device_bytes(void *handle, const void *host_ptr);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,41 @@
+// attention.cuh -- decode attention launch descriptor.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace mcpo {
+
+struct AttnArgs {
+  // inputs for the current position
+  const float* q;  // [n_head*head_dim]
+  const float* k;  // [n_kv*head_dim]
+  const float* v;  // [n_kv*head_dim]
+  // fused path: QK-RMSNorm (eps 1e-6) + NeoX RoPE + KV append before attention.
+  int fuse_norm_rope_append;
+  const void* q_norm; int q_norm_dtype;  // may be null
+  const void* k_norm; int k_norm_dtype;  // may be null
+  const float* rope_cos;                 // [rope_ctx][head_dim/2] or null
+  const float* rope_sin;
+  float rope_base, rope_scale;           // used when the tables are null
+  // cache of this layer: [ctx][kv_dim], f32 or f16
+  void* k_cache;
+  void* v_cache;
+  int kv_f16;
+  const int* pos_ptr;  // device position (graph replay) or null
+  int pos_static;
+  int n_head, n_kv, head_dim, ctx;
+  int n_split;
+  float scale;
+  // scratch
+  float* partial;      // [n_head][n_split][head_dim + 2]
+  unsigned* counters;  // [n_kv], zero at rest
+  // outputs
+  float* out;          // [n_head*head_dim]
+  uint8_t* out_q8;     // optional Q8_1 of out (needs head_dim % 32 == 0)
+};
+
+size_t attn_partial_floats(int n_head, int n_split, int head_dim);
+cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st);
+
+}  // namespace mcpo

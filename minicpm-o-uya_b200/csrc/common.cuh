@@ -1,0 +1,120 @@
+// common.cuh -- device helpers shared by the sm_100a kernels of
+// libminicpmo_gpu_helper.so.
+//
+// Data formats (GGUF block layouts used by the reference,
+// src/minicpmo/qwen3.uya:847-1000, gpu_shim.c:37-41):
+//   Q4_K  256 values / 144 B : f16 d, f16 dmin, u8 scales[12], u8 qs[128]
+//   Q6_K  256 values / 210 B : u8 ql[128], u8 qh[64], i8 sc[16], f16 d
+//   Q8_0   32 values /  34 B : f16 d, i8 qs[32]
+//   Q8_1   32 values /  36 B : f16 d, f16 s, i8 qs[32]  (activations)
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace mcpo {
+
+// Uya TensorDType ordinals, the dtype integers of the reference ABI
+// (src/minicpmo/tensor.uya:31-54; the shim tests 10/12, gpu_shim.c:323).
+enum DType : int { kF32 = 0, kF16 = 1, kQ8_0 = 6, kQ4_K = 10, kQ6_K = 12, kBF16 = 20 };
+
+constexpr int kGemvWarps = 8;           // consumer warps per GEMV CTA
+constexpr int kGemvThreads = kGemvWarps * 32;
+
+// ---------------------------------------------------------------------
+// f16 conversions with the reference's rounding.
+// f16 -> f32 is exact; the hardware conversion gives the same bits as
+// kernels.uya:48-78.  f32 -> f16 follows kernels.uya:79-108 /
+// gpu_shim.c:2157-2192: truncate, then add one unit when the first dropped
+// bit is set (ties away from zero, not IEEE round-to-nearest-even).
+// ---------------------------------------------------------------------
+__device__ __forceinline__ float f16_to_f32(uint16_t b) {
+  return __half2float(__ushort_as_half(b));
+}
+
+__device__ __forceinline__ uint16_t f32_to_f16_ref(float v) {
+  uint32_t u = __float_as_uint(v);
+  uint32_t sign = (u >> 16) & 0x8000u;
+  uint32_t e = (u >> 23) & 0xffu;
+  uint32_t frac = u & 0x7fffffu;
+  if (e == 255u) return (uint16_t)(sign | (frac != 0u ? 0x7e00u : 0x7c00u));
+  if (e > 142u) return (uint16_t)(sign | 0x7c00u);
+  if (e < 113u) {
+    if (e < 103u) return (uint16_t)sign;
+    frac |= 0x800000u;
+    uint16_t out = (uint16_t)(sign | (frac >> (126u - e)));
+    if ((frac >> (125u - e)) & 1u) out = (uint16_t)(out + 1u);
+    return out;
+  }
+  uint16_t out = (uint16_t)(sign | ((e - 112u) << 10) | (frac >> 13));
+  if (frac & 0x1000u) out = (uint16_t)(out + 1u);
+  return out;
+}
+
+__device__ __forceinline__ float bf16_to_f32(uint16_t b) { return __uint_as_float((uint32_t)b << 16); }
+
+__device__ __forceinline__ float load_weight(const void* w, int dtype, int i) {
+  if (dtype == kF32) return reinterpret_cast<const float*>(w)[i];
+  if (dtype == kBF16) return bf16_to_f32(reinterpret_cast<const uint16_t*>(w)[i]);
+  return f16_to_f32(reinterpret_cast<const uint16_t*>(w)[i]);
+}
+
+__device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
+
+// 16-byte streaming load that bypasses L1 (weights are read once per token).
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Q8_1 quantisation of one 32-value block held one value per lane
+// (gpu_shim.c:336-378, "variant B"): d = amax/127 (IEEE division),
+// q = trunc(x/d +- 0.5) clamped to [-128, 127].  Returns q for this lane and
+// the f16 bits of d in *d_bits (0 when amax == 0).  Every lane gets the same
+// d_bits.  Uses only round-to-nearest IEEE operations so the result is
+// bit-identical to the reference's host quantiser.
+__device__ __forceinline__ int q8_1_quant_lane(float x, uint16_t* d_bits) {
+  float amax = warp_max(fabsf(x));
+  if (amax == 0.0f) {
+    *d_bits = 0;
+    return 0;
+  }
+  float d = __fdiv_rn(amax, 127.0f);
+  *d_bits = f32_to_f16_ref(d);
+  float v = __fdiv_rn(x, d);
+  int q = __float2int_rz(v >= 0.0f ? __fadd_rn(v, 0.5f) : __fsub_rn(v, 0.5f));
+  q = q > 127 ? 127 : q;
+  q = q < -128 ? -128 : q;
+  return q;
+}
+
+// Sequential x0 + x1 + ... + x31 across lanes (the reference's s field),
+// result valid in every lane.
+__device__ __forceinline__ float warp_seq_sum(float x) {
+  float s = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) s = __fadd_rn(s, __shfl_sync(0xffffffffu, x, i));
+  return s;
+}
+
+// Bounded spin helper: every wait in this library gives up after a limit
+// and reports through an error word instead of hanging the GPU.
+constexpr long long kSpinLimit = 1ll << 26;
+
+}  // namespace mcpo

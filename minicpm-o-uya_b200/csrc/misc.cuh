@@ -1,0 +1,41 @@
+// misc.cuh -- launchers for the small kernels of the decode step.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "layout.cuh"
+
+namespace mcpo {
+
+// Device-resident step state read by the captured decode graph.  The host
+// writes token/pos before a replay (or sets auto_advance so the sampler
+// feeds its own output back), the sampler writes next_token/best/gap.
+struct StepState {
+  int token;
+  int pos;
+  int next_token;
+  float best;
+  float gap;
+  int auto_advance;
+  float penalty;    // repeat penalty (<= 1: off)
+  int history_len;  // tokens appended to the history buffer while auto-advancing
+  int err;
+};
+
+cudaError_t launch_relayout(const uint8_t* src, uint8_t* dst, const TileGeom& g, size_t row_bytes, cudaStream_t st);
+// token (from tok_ptr when non-null) outside [0, rows) yields zeros.
+cudaError_t launch_embed(const uint8_t* w, const TileGeom& g, int dtype, int rows, int hidden, const int* tok_ptr, int tok,
+                         float* out, cudaStream_t st);
+// grid CTAs; scratch holds 3 floats per CTA; counter is zero at rest.
+// history (may be null) receives next_token at history_len when auto-advancing.
+cudaError_t launch_argmax(const float* logits, int n, const uint32_t* seen_bits, float* scratch, unsigned* counter,
+                          StepState* st, int* history, int history_cap, int grid, cudaStream_t s);
+cudaError_t launch_mark_seen(uint32_t* bits, const StepState* st, int vocab, cudaStream_t s);
+cudaError_t launch_add_inplace(float* dst, const float* src, int n, cudaStream_t st);
+cudaError_t launch_silu_mul(float* dst, const float* gate, const float* up, int n, cudaStream_t st);
+cudaError_t launch_head_norm_rope(float* vec, int n_head, int hd, const void* w, int w_dtype, int do_rope,
+                                  const float* cos_t, const float* sin_t, float base, float fscale, int pos,
+                                  cudaStream_t st);
+
+}  // namespace mcpo
