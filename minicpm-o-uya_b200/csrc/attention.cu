@@ -155,15 +155,15 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a)
           if (g < G) {
             float p = 0.0f;
 #pragma unroll
-            for (int j = 0; j < J; ++j) p = fmaf(qv[g][j], kv[j], p);
-            const float s = warp_sum(p) * a.scale;
+            for (int j = 0; j < J; ++j) p = __fmaf_rn(qv[g][j], kv[j], p);
+            const float s = __fmul_rn(__shfl_sync(0xffffffffu, warp_sum(p), 0), a.scale);
             const float mn = fmaxf(m[g], s);
-            const float alpha = expf(m[g] - mn);  // m = -inf -> 0
-            const float beta = expf(s - mn);
-            l[g] = l[g] * alpha + beta;
+            const float alpha = expf_det(__fsub_rn(m[g], mn));  // m = -inf -> 0
+            const float beta = expf_det(__fsub_rn(s, mn));
+            l[g] = __fadd_rn(__fmul_rn(l[g], alpha), beta);
             m[g] = mn;
 #pragma unroll
-            for (int j = 0; j < J; ++j) acc[g][j] = acc[g][j] * alpha + beta * vv[j];
+            for (int j = 0; j < J; ++j) acc[g][j] = __fadd_rn(__fmul_rn(acc[g][j], alpha), __fmul_rn(beta, vv[j]));
           }
         }
       }
@@ -190,13 +190,13 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a)
         float wt[kAttnWarps];
         for (int w = 0; w < kAttnWarps; ++w) {
           const float mw = sm.rm[w * kGMax + g];
-          wt[w] = mw == -INFINITY ? 0.0f : expf(mw - M);
-          L += wt[w] * sm.rl[w * kGMax + g];
+          wt[w] = mw == -INFINITY ? 0.0f : expf_det(__fsub_rn(mw, M));
+          L = __fadd_rn(L, __fmul_rn(wt[w], sm.rl[w * kGMax + g]));
         }
         float* dst = a.partial + ((size_t)(g0 + g) * a.n_split + split) * stride_part;
         for (int d = lane; d < hd; d += 32) {
           float s = 0.0f;
-          for (int w = 0; w < kAttnWarps; ++w) s += wt[w] * sm.racc[(w * kGMax + g) * hd + d];
+          for (int w = 0; w < kAttnWarps; ++w) s = __fadd_rn(s, __fmul_rn(wt[w], sm.racc[(w * kGMax + g) * hd + d]));
           dst[2 + d] = s;
         }
         if (lane == 0) {
@@ -224,25 +224,27 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a)
     float L = 0.0f;
     for (int s = 0; s < n_active; ++s) {
       const float ms = __ldcg(ph + (size_t)s * stride_part);
-      if (ms != -INFINITY) L += expf(ms - M) * __ldcg(ph + (size_t)s * stride_part + 1);
+      if (ms != -INFINITY) L = __fadd_rn(L, __fmul_rn(expf_det(__fsub_rn(ms, M)), __ldcg(ph + (size_t)s * stride_part + 1)));
     }
-    const float invL = L > 0.0f ? 1.0f / L : 0.0f;
+    const float invL = L > 0.0f ? __fdiv_rn(1.0f, L) : 0.0f;
     for (int d0 = 0; d0 < hd; d0 += 32) {
       const int d = d0 + lane;
       float o = 0.0f;
       if (d < hd) {
         for (int s = 0; s < n_active; ++s) {
           const float ms = __ldcg(ph + (size_t)s * stride_part);
-          if (ms != -INFINITY) o += expf(ms - M) * __ldcg(ph + (size_t)s * stride_part + 2 + d);
+          if (ms != -INFINITY)
+            o = __fadd_rn(o, __fmul_rn(expf_det(__fsub_rn(ms, M)), __ldcg(ph + (size_t)s * stride_part + 2 + d)));
         }
-        o *= invL;
+        o = __fmul_rn(o, invL);
         a.out[(size_t)h * hd + d] = o;
       }
       if (a.out_q8 && (hd % 32) == 0) {
         uint16_t dbits;
-        const int q = q8_1_quant_lane(o, &dbits);
+        bool zero;
+        const int q = q8_1_quant_lane(o, &dbits, &zero);
         const float sum = warp_seq_sum(o);
-        const uint16_t sbits = dbits == 0 ? (uint16_t)0 : f32_to_f16_ref(sum);
+        const uint16_t sbits = zero ? (uint16_t)0 : f32_to_f16_ref(sum);
         uint32_t word = ((uint32_t)(q & 0xff)) << (8 * (lane & 3));
         word |= __shfl_xor_sync(0xffffffffu, word, 1);
         word |= __shfl_xor_sync(0xffffffffu, word, 2);

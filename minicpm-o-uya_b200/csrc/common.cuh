@@ -71,10 +71,19 @@ __device__ __forceinline__ uint4 ldg_stream(const void* p) {
   return r;
 }
 
+// Butterfly sum (xor 16, 8, 4, 2, 1).  Lanes may end with differently
+// ordered totals; callers that need one value broadcast lane 0's.
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
   return v;
+}
+
+// Number of KV splits of the decode attention: a function of the kv-head
+// count only, so results do not depend on the GPU's SM count.
+__host__ __device__ inline int attn_n_split(int n_kv) {
+  int s = (256 + n_kv - 1) / n_kv;
+  return s < 1 ? 1 : (s > 64 ? 64 : s);
 }
 
 __device__ __forceinline__ float warp_max(float v) {
@@ -86,11 +95,15 @@ __device__ __forceinline__ float warp_max(float v) {
 // Q8_1 quantisation of one 32-value block held one value per lane
 // (gpu_shim.c:336-378, "variant B"): d = amax/127 (IEEE division),
 // q = trunc(x/d +- 0.5) clamped to [-128, 127].  Returns q for this lane and
-// the f16 bits of d in *d_bits (0 when amax == 0).  Every lane gets the same
-// d_bits.  Uses only round-to-nearest IEEE operations so the result is
-// bit-identical to the reference's host quantiser.
-__device__ __forceinline__ int q8_1_quant_lane(float x, uint16_t* d_bits) {
+// the f16 bits of d in *d_bits; *all_zero is set when amax == 0 (then the
+// block is all zeros, s included).  d may underflow to f16 zero while
+// amax > 0: the quants are still computed with the f32 d, as the reference
+// does.  Every lane gets the same d_bits.  Uses only round-to-nearest IEEE
+// operations so the result is bit-identical to the reference's host
+// quantiser.
+__device__ __forceinline__ int q8_1_quant_lane(float x, uint16_t* d_bits, bool* all_zero) {
   float amax = warp_max(fabsf(x));
+  *all_zero = amax == 0.0f;
   if (amax == 0.0f) {
     *d_bits = 0;
     return 0;
@@ -111,6 +124,44 @@ __device__ __forceinline__ float warp_seq_sum(float x) {
 #pragma unroll
   for (int i = 0; i < 32; ++i) s = __fadd_rn(s, __shfl_sync(0xffffffffu, x, i));
   return s;
+}
+
+// Deterministic exp: Cody-Waite argument reduction x = k*ln2 + r (ln2 split
+// into a 15-bit head and a tail, so k*LN2_HI is exact) and the degree-7
+// Taylor polynomial of e^r on |r| <= ln2/2 in Horner form, then an exact
+// scaling by 2^k.  Every step is a correctly rounded IEEE operation (rint,
+// fma, mul), so the CPU oracle's C restatement returns the same bits.
+// Relative error below 2 ulp over the float range.
+__device__ __forceinline__ float expf_det(float x) {
+  if (x != x) return x;
+  if (x >= 88.72283935546875f) return __int_as_float(0x7f800000);
+  if (x <= -103.97208404541015625f) return 0.0f;
+  const float k = rintf(__fmul_rn(x, 1.44269502162933349609375f));
+  float r = __fmaf_rn(-k, 0.693145751953125f, x);
+  r = __fmaf_rn(-k, 1.428606765330187045e-06f, r);
+  float p = 1.98412698412698e-4f;
+  p = __fmaf_rn(p, r, 1.38888888888889e-3f);
+  p = __fmaf_rn(p, r, 8.33333333333333e-3f);
+  p = __fmaf_rn(p, r, 4.16666666666667e-2f);
+  p = __fmaf_rn(p, r, 1.66666666666667e-1f);
+  p = __fmaf_rn(p, r, 0.5f);
+  p = __fmaf_rn(p, r, 1.0f);
+  p = __fmaf_rn(p, r, 1.0f);
+  int ki = (int)k;
+  if (ki > 127) {
+    p = __fmul_rn(p, 2.0f);
+    ki = 127;
+  }
+  if (ki < -126) {
+    p = __fmul_rn(p, 5.42101086242752217e-20f);  // 2^-64
+    ki += 64;
+  }
+  return __fmul_rn(p, __int_as_float((ki + 127) << 23));
+}
+
+// silu(g) * u with the deterministic exp (kernels.uya:198: g / (1 + e^-g)).
+__device__ __forceinline__ float silu_mul_det(float g, float u) {
+  return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf_det(-g))), u);
 }
 
 // Bounded spin helper: every wait in this library gives up after a limit

@@ -76,14 +76,16 @@ __device__ __forceinline__ float sb_dot_q4k(const uint4* c, const XShared& x, in
     const int s0 = (scw >> (8 * (j0 & 3))) & 0xff, s1 = (scw >> (8 * (j1 & 3))) & 0xff;
     const int m0 = (mnw >> (8 * (j0 & 3))) & 0xff, m1 = (mnw >> (8 * (j1 & 3))) & 0xff;
     const int xb = sb * 8;
-    sum_d += (float)s0 * x.xd[xb + j0] * (float)dlo + (float)s1 * x.xd[xb + j1] * (float)dhi;
-    sum_m += (float)m0 * x.xds[xb + j0] + (float)m1 * x.xds[xb + j1];
+    const float t0 = __fmul_rn(__fmul_rn((float)s0, x.xd[xb + j0]), (float)dlo);
+    const float t1 = __fmul_rn(__fmul_rn((float)s1, x.xd[xb + j1]), (float)dhi);
+    sum_d = __fadd_rn(sum_d, __fadd_rn(t0, t1));
+    sum_m = __fadd_rn(sum_m, __fadd_rn(__fmul_rn((float)m0, x.xds[xb + j0]), __fmul_rn((float)m1, x.xds[xb + j1])));
     if (kDots && dots) {
       dots[sb * 8 + j0] = dlo;
       dots[sb * 8 + j1] = dhi;
     }
   }
-  return d * sum_d - dmin * sum_m;
+  return __fsub_rn(__fmul_rn(d, sum_d), __fmul_rn(dmin, sum_m));
 }
 
 // ---- Q6_K super-block: c[0..7] = ql, c[8..11] = qh, c[12] = sc, d separate ----
@@ -107,12 +109,12 @@ __device__ __forceinline__ float sb_dot_q6k(const uint4* c, uint16_t dbits, cons
         const int raw = dot4(or4(lo, hi), x.xs[g * x.nb + sb], 0);
         const int dotg = raw - 32 * x.xs16[sb * 16 + g];
         const int scale = (int)(int8_t)((scw[g >> 2] >> (8 * (g & 3))) & 0xff);
-        sum += x.xd[sb * 8 + (g >> 1)] * ((float)dotg * (float)scale);
+        sum = __fadd_rn(sum, __fmul_rn(x.xd[sb * 8 + (g >> 1)], __fmul_rn((float)dotg, (float)scale)));
         if (kDots && dots) dots[sb * 16 + g] = dotg;
       }
     }
   }
-  return d * sum;
+  return __fmul_rn(d, sum);
 }
 
 // ---- Q8_0 256-value group: c[0] = 8 f16 d's, c[1..16] = qs ----
@@ -126,7 +128,7 @@ __device__ __forceinline__ float sb_dot_q80(const uint4* c, const XShared& x, in
     int acc = dot4(c[1 + 2 * b], x.xs[(2 * b) * x.nb + sb], 0);
     acc = dot4(c[2 + 2 * b], x.xs[(2 * b + 1) * x.nb + sb], acc);
     const float dwf = f16_to_f32((uint16_t)((dw[b >> 1] >> (16 * (b & 1))) & 0xffffu));
-    sum += dwf * x.xd[sb * 8 + b] * (float)acc;
+    sum = __fadd_rn(sum, __fmul_rn(__fmul_rn(dwf, x.xd[sb * 8 + b]), (float)acc));
     if (kDots && dots) dots[sb * 8 + b] = acc;
   }
   return sum;
@@ -145,12 +147,12 @@ __device__ __forceinline__ float lane_row_dot(const uint8_t* tile_base, const Ge
     for (int i = 0; i < kChunks; ++i) c[i] = ldg_stream(blk + i * 512 + lane * 16);
     const int sb = k * s.lpr + lane_in_row;
     if (kDtype == kQ4_K) {
-      acc += sb_dot_q4k<kDots>(c, x, sb, dots);
+      acc = __fadd_rn(acc, sb_dot_q4k<kDots>(c, x, sb, dots));
     } else if (kDtype == kQ6_K) {
       const uint16_t db = *reinterpret_cast<const uint16_t*>(blk + 13 * 512 + lane * 2);
-      acc += sb_dot_q6k<kDots>(c, db, x, sb, dots);
+      acc = __fadd_rn(acc, sb_dot_q6k<kDots>(c, db, x, sb, dots));
     } else {
-      acc += sb_dot_q80<kDots>(c, x, sb, dots);
+      acc = __fadd_rn(acc, sb_dot_q80<kDots>(c, x, sb, dots));
     }
   }
   return acc;
@@ -164,13 +166,11 @@ __device__ __forceinline__ float seg_row_dot(const uint8_t* tile_base, const Gem
   return lane_row_dot<kQ8_0, kDots>(tile_base, s, warp, lane, lane_in_row, x, dots);
 }
 
+// Butterfly over the lpr lanes of a row (xor lpr/2 .. 1); the row's value is
+// the one of its first lane.
 __device__ __forceinline__ float reduce_row(float v, int lpr) {
-  for (int o = lpr >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  for (int o = lpr >> 1; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
   return v;
-}
-
-__device__ __forceinline__ float silu_mul(float g, float u) {
-  return (g / (1.0f + expf(-g))) * u;
 }
 
 template <bool kDots>
@@ -198,7 +198,7 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv(const GemvArgs a) {
     for (int i = 4; i < 8; ++i) s_hi = dp4a((int)q[i], 0x01010101, s_hi);
     const float d8 = f16_to_f32((uint16_t)(hdr & 0xffffu));
     xd[b] = d8;
-    xds[b] = d8 * (float)(s_lo + s_hi);
+    xds[b] = __fmul_rn(d8, (float)(s_lo + s_hi));
     xs16[2 * b] = s_lo;
     xs16[2 * b + 1] = s_hi;
     const int sb = b >> 3, c = (b & 7) * 2;
@@ -229,10 +229,10 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv(const GemvArgs a) {
       const uint8_t* tb2 = s.w2 + (size_t)lt * s.cta_tile_bytes;
       float up = seg_row_dot<false>(tb2, s, warp, lane, lane_in_row, x, nullptr);
       up = reduce_row(up, s.lpr);
-      if (lane_in_row == 0 && row < s.rows) s.y[row] = silu_mul(acc, up);
+      if (lane_in_row == 0 && row < s.rows) s.y[row] = silu_mul_det(acc, up);
     } else if (lane_in_row == 0 && row < s.rows) {
       if (s.epi == kEpiAdd)
-        s.y[row] = s.y[row] + acc;
+        s.y[row] = __fadd_rn(s.y[row], acc);
       else
         s.y[row] = acc;
     }
@@ -247,9 +247,10 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv(const GemvArgs a) {
 // sequential f16 sum s (gpu_shim.c:343-378).
 __device__ __forceinline__ void quant_block_warp(float v, uint8_t* dst, int lane) {
   uint16_t dbits;
-  const int q = q8_1_quant_lane(v, &dbits);
+  bool zero;
+  const int q = q8_1_quant_lane(v, &dbits, &zero);
   const float s = warp_seq_sum(v);
-  const uint16_t sbits = dbits == 0 ? (uint16_t)0 : f32_to_f16_ref(s);
+  const uint16_t sbits = zero ? (uint16_t)0 : f32_to_f16_ref(s);
   // pack 4 quants per lane group into words
   const uint32_t qb = (uint32_t)(q & 0xff);
   uint32_t word = qb << (8 * (lane & 3));

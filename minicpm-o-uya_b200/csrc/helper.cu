@@ -304,7 +304,7 @@ bool ensure_xq(Ctx* c, size_t cols, char* err, size_t cap) {
 // ---------------------------------------------------------------------
 int run_attention(Ctx* c, const float* q, float* dst, size_t layer, size_t pos, size_t n_head, size_t n_kv, size_t hd,
                   char* err, size_t cap) {
-  const int n_split = (int)((2 * c->sm_count + n_kv - 1) / n_kv) > 64 ? 64 : (int)((2 * c->sm_count + n_kv - 1) / n_kv);
+  const int n_split = attn_n_split((int)n_kv);
   if (!ensure(c, &c->attn_partial, &c->attn_partial_bytes, attn_partial_floats((int)n_head, n_split, (int)hd) * 4,
               "attention_partial_malloc", err, cap))
     return 0;
@@ -570,8 +570,7 @@ int bind_model(Ctx* c, const minicpmo_qwen3_config* cfg, char* err, size_t cap) 
   const size_t maxd = std::max(std::max(h, f), m.qd);
   m.kv_layer_elems = (size_t)cf.context * m.kvd;
   const size_t esz = cf.kv_f16 ? 2 : 4;
-  m.n_split = (int)((2 * c->sm_count + cf.kv_heads - 1) / cf.kv_heads);
-  if (m.n_split > 64) m.n_split = 64;
+  m.n_split = attn_n_split((int)cf.kv_heads);
   m.am_grid = c->sm_count;
   m.history_cap = 1 << 16;
   struct A {

@@ -226,15 +226,12 @@ __global__ void k_mark_seen(uint32_t* bits, const StepState* st, int vocab) {
 // ---------------------------------------------------------------------
 __global__ void k_add_inplace(float* dst, const float* src, int n) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < n) dst[i] = dst[i] + src[i];
+  if (i < n) dst[i] = __fadd_rn(dst[i], src[i]);
 }
 
 __global__ void k_silu_mul(float* dst, const float* gate, const float* up, int n) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < n) {
-    const float g = gate[i];
-    dst[i] = (g / (1.0f + expf(-g))) * up[i];
-  }
+  if (i < n) dst[i] = silu_mul_det(gate[i], up[i]);
 }
 
 // In-place per-head RMSNorm and/or RoPE, one warp per head.

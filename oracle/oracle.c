@@ -546,6 +546,294 @@ uint32_t orc_argmax_penalized(const float *values, size_t n, const uint32_t *see
     return (uint32_t) best;
 }
 
+
+/* ------------------------------------------------------------------ */
+/* device evaluation order (bit-exact contract with the B200 kernels)  */
+/* ------------------------------------------------------------------ */
+
+/* Cody-Waite reduction + degree-7 Taylor polynomial (Horner, fmaf), exact
+ * scaling by 2^k; every step correctly rounded, so the CUDA build of the
+ * same steps returns the same bits. */
+float orc_expf_det(float x) {
+    float k, r, p, sc;
+    int ki;
+    uint32_t bits;
+    if (x != x) return x;
+    if (x >= 88.72283935546875f) return INFINITY;
+    if (x <= -103.97208404541015625f) return 0.0f;
+    k = rintf(x * 1.44269502162933349609375f);
+    r = fmaf(-k, 0.693145751953125f, x);
+    r = fmaf(-k, 1.428606765330187045e-06f, r);
+    p = 1.98412698412698e-4f;
+    p = fmaf(p, r, 1.38888888888889e-3f);
+    p = fmaf(p, r, 8.33333333333333e-3f);
+    p = fmaf(p, r, 4.16666666666667e-2f);
+    p = fmaf(p, r, 1.66666666666667e-1f);
+    p = fmaf(p, r, 0.5f);
+    p = fmaf(p, r, 1.0f);
+    p = fmaf(p, r, 1.0f);
+    ki = (int) k;
+    if (ki > 127) { p = p * 2.0f; ki = 127; }
+    if (ki < -126) { p = p * 5.42101086242752217e-20f; ki += 64; }
+    bits = (uint32_t) (ki + 127) << 23;
+    memcpy(&sc, &bits, 4);
+    return p * sc;
+}
+
+int orc_attn_n_split(int n_kv) {
+    int s = (256 + n_kv - 1) / n_kv;
+    return s < 1 ? 1 : (s > 64 ? 64 : s);
+}
+
+uint16_t orc_f32_to_f16_rne(float v) {
+    uint32_t u, sign, e, m, out, rem, half;
+    int ex;
+    memcpy(&u, &v, 4);
+    sign = (u >> 16) & 0x8000u;
+    e = (u >> 23) & 0xffu;
+    m = u & 0x7fffffu;
+    if (e == 255u) return (uint16_t) (sign | 0x7c00u | (m ? 0x200u : 0u));
+    ex = (int) e - 127 + 15;
+    if (ex >= 31) return (uint16_t) (sign | 0x7c00u);
+    if (ex <= 0) {
+        int shift;
+        if (ex < -10) return (uint16_t) sign;
+        m |= 0x800000u;
+        shift = 14 - ex;
+        out = m >> shift;
+        rem = m & ((1u << shift) - 1u);
+        half = 1u << (shift - 1);
+        if (rem > half || (rem == half && (out & 1u))) out += 1u;
+        return (uint16_t) (sign | out);
+    }
+    out = ((uint32_t) ex << 10) | (m >> 13);
+    rem = m & 0x1fffu;
+    if (rem > 0x1000u || (rem == 0x1000u && (out & 1u))) out += 1u;
+    return (uint16_t) (sign | out);
+}
+
+static int lanes_per_row(size_t cols) {
+    size_t nb = cols / 256;
+    int lpr = 32;
+    while (lpr > 1 && (nb % (size_t) lpr) != 0) lpr >>= 1;
+    return lpr;
+}
+
+static float butterfly(float *v, int n) {
+    float nv[32];
+    int o, i;
+    for (o = n >> 1; o > 0; o >>= 1) {
+        for (i = 0; i < n; ++i) nv[i] = v[i] + v[i ^ o];
+        for (i = 0; i < n; ++i) v[i] = nv[i];
+    }
+    return v[0];
+}
+
+/* one super-block (256 values) in the kernel's operation order */
+static float sb_dev(int dtype, const uint8_t *row, size_t sb, const uint8_t *xq) {
+    int32_t q8s[8];
+    float xd[8], xds[8];
+    int j;
+    for (j = 0; j < 8; ++j) {
+        int i;
+        int32_t s = 0;
+        for (i = 0; i < 32; ++i) s += q8_1_q(xq, sb * 8 + j, i);
+        q8s[j] = s;
+        xd[j] = q8_1_d(xq, sb * 8 + j);
+        xds[j] = xd[j] * (float) s;
+    }
+    if (dtype == ORC_Q4_K) {
+        const uint8_t *b = row + sb * 144;
+        float d = orc_f16_to_f32(rd16(b)), dmin = orc_f16_to_f32(rd16(b + 2));
+        float sum_d = 0.0f, sum_m = 0.0f;
+        int g;
+        for (g = 0; g < 4; ++g) {
+            uint8_t s0, m0, s1, m1;
+            int32_t dlo = 0, dhi = 0;
+            int l;
+            q4k_scale_min(2 * g, b + 4, &s0, &m0);
+            q4k_scale_min(2 * g + 1, b + 4, &s1, &m1);
+            for (l = 0; l < 32; ++l) {
+                dlo += (b[16 + g * 32 + l] & 15) * q8_1_q(xq, sb * 8 + 2 * g, l);
+                dhi += (b[16 + g * 32 + l] >> 4) * q8_1_q(xq, sb * 8 + 2 * g + 1, l);
+            }
+            {
+                float t0 = ((float) s0 * xd[2 * g]) * (float) dlo;
+                float t1 = ((float) s1 * xd[2 * g + 1]) * (float) dhi;
+                sum_d = sum_d + (t0 + t1);
+                sum_m = sum_m + ((float) m0 * xds[2 * g] + (float) m1 * xds[2 * g + 1]);
+            }
+        }
+        return d * sum_d - dmin * sum_m;
+    }
+    if (dtype == ORC_Q6_K) {
+        const uint8_t *b = row + sb * 210;
+        float d = orc_f16_to_f32(rd16(b + 208)), sum = 0.0f;
+        int n, qq, h;
+        for (n = 0; n < 2; ++n)
+            for (qq = 0; qq < 4; ++qq)
+                for (h = 0; h < 2; ++h) {
+                    int g = 8 * n + 2 * qq + h, l;
+                    int32_t dd = 0;
+                    for (l = 0; l < 16; ++l) {
+                        int e = g * 16 + l;
+                        dd += q6k_value(b, e, NULL) * q8_1_q(xq, sb * 8 + e / 32, e % 32);
+                    }
+                    sum = sum + xd[g >> 1] * ((float) dd * (float) q6k_group_scale(b, g));
+                }
+        (void) q8s;
+        return d * sum;
+    }
+    {
+        float sum = 0.0f;
+        int blk;
+        for (blk = 0; blk < 8; ++blk) {
+            const uint8_t *b = row + (sb * 8 + blk) * 34;
+            int32_t dd = 0;
+            int l;
+            for (l = 0; l < 32; ++l) dd += (int8_t) b[2 + l] * q8_1_q(xq, sb * 8 + blk, l);
+            sum = sum + (orc_f16_to_f32(rd16(b)) * xd[blk]) * (float) dd;
+        }
+        return sum;
+    }
+}
+
+int orc_matvec_q8_1_dev(int dtype, const uint8_t *w, size_t rows, size_t cols, const uint8_t *xq, float *y) {
+    size_t rb = orc_row_bytes(dtype, cols), r;
+    int lpr, li;
+    size_t nb, ks, k;
+    if (rb == 0 || cols % 256 || (dtype != ORC_Q4_K && dtype != ORC_Q6_K && dtype != ORC_Q8_0)) return 0;
+    lpr = lanes_per_row(cols);
+    nb = cols / 256;
+    ks = nb / (size_t) lpr;
+    for (r = 0; r < rows; ++r) {
+        float v[32];
+        for (li = 0; li < lpr; ++li) {
+            float acc = 0.0f;
+            for (k = 0; k < ks; ++k) acc = acc + sb_dev(dtype, w + r * rb, k * (size_t) lpr + (size_t) li, xq);
+            v[li] = acc;
+        }
+        y[r] = butterfly(v, lpr);
+    }
+    return 1;
+}
+
+/* warp per row, lane l sums w[i]*x[i] for i = l, l+32, ... with fmaf, then
+ * the 32-lane butterfly. */
+int orc_matvec_dense_dev(int dtype, const uint8_t *w, size_t rows, size_t cols, const float *x, float *y) {
+    size_t rb = orc_row_bytes(dtype, cols), r, i;
+    if (rb == 0 || (dtype != ORC_F32 && dtype != ORC_F16 && dtype != ORC_BF16)) return 0;
+    for (r = 0; r < rows; ++r) {
+        float v[32];
+        int l;
+        for (l = 0; l < 32; ++l) {
+            float acc = 0.0f;
+            for (i = (size_t) l; i < cols; i += 32) acc = fmaf(weight_at(w + r * rb, dtype, i), x[i], acc);
+            v[l] = acc;
+        }
+        y[r] = butterfly(v, 32);
+    }
+    return 1;
+}
+
+void orc_silu_mul_dev(float *dst, const float *gate, const float *up, size_t n) {
+    size_t i;
+    for (i = 0; i < n; ++i) dst[i] = (gate[i] / (1.0f + orc_expf_det(-gate[i]))) * up[i];
+}
+
+#define ATT_WARPS 4
+
+int orc_attention_dev(float *out, const float *q, const float *k_cache, const float *v_cache, const float *cur_k,
+                      const float *cur_v, size_t layer, size_t pos, size_t head_count, size_t kv_head_count,
+                      size_t head_dim, size_t context) {
+    const size_t hd = head_dim, kv_dim = kv_head_count * hd;
+    const int n_split = orc_attn_n_split((int) kv_head_count);
+    const int J = hd <= 32 ? 1 : (int) (hd / 32);
+    const float scale = 1.0f / sqrtf((float) hd);
+    const size_t n_pos = pos + 1;
+    size_t chunk = (n_pos + (size_t) n_split - 1) / (size_t) n_split;
+    size_t n_active, kvh;
+    float *pm, *pl, *pacc;
+    if (!(hd == 64 || hd == 128 || hd == 256 || hd <= 32)) return 0;
+    if (chunk < 32) chunk = 32;
+    n_active = (n_pos + chunk - 1) / chunk;
+    pm = (float *) malloc(n_active * sizeof(float));
+    pl = (float *) malloc(n_active * sizeof(float));
+    pacc = (float *) malloc(n_active * hd * sizeof(float));
+    if (!pm || !pl || !pacc) { free(pm); free(pl); free(pacc); return 0; }
+    for (kvh = 0; kvh < kv_head_count; ++kvh) {
+        size_t hb = (kvh * head_count + kv_head_count - 1) / kv_head_count;
+        size_t he = ((kvh + 1) * head_count + kv_head_count - 1) / kv_head_count, h;
+        for (h = hb; h < he; ++h) {
+            const float *qh = q + h * hd;
+            size_t s;
+            for (s = 0; s < n_active; ++s) {
+                const size_t t0 = s * chunk, t1 = t0 + chunk < n_pos ? t0 + chunk : n_pos;
+                float wm[ATT_WARPS], wl[ATT_WARPS], *wacc = (float *) calloc((size_t) ATT_WARPS * hd, sizeof(float));
+                float M = -INFINITY, L = 0.0f, wt[ATT_WARPS];
+                int w;
+                size_t d;
+                for (w = 0; w < ATT_WARPS; ++w) {
+                    size_t t;
+                    wm[w] = -INFINITY;
+                    wl[w] = 0.0f;
+                    for (t = t0 + (size_t) w; t < t1; t += ATT_WARPS) {
+                        const int cur = t == pos;
+                        const float *krow = cur ? cur_k + kvh * hd : k_cache + (layer * context + t) * kv_dim + kvh * hd;
+                        const float *vrow = cur ? cur_v + kvh * hd : v_cache + (layer * context + t) * kv_dim + kvh * hd;
+                        float lanes[32], sc, mn, alpha, beta;
+                        int ln, j;
+                        for (ln = 0; ln < 32; ++ln) {
+                            float p = 0.0f;
+                            if ((size_t) (ln * J) < hd)
+                                for (j = 0; j < J; ++j) p = fmaf(qh[ln * J + j], krow[ln * J + j], p);
+                            lanes[ln] = p;
+                        }
+                        sc = butterfly(lanes, 32) * scale;
+                        mn = wm[w] > sc ? wm[w] : sc;
+                        alpha = orc_expf_det(wm[w] - mn);
+                        beta = orc_expf_det(sc - mn);
+                        wl[w] = wl[w] * alpha + beta;
+                        wm[w] = mn;
+                        for (d = 0; d < hd; ++d) wacc[w * hd + d] = wacc[w * hd + d] * alpha + beta * vrow[d];
+                    }
+                }
+                for (w = 0; w < ATT_WARPS; ++w) M = fmaxf(M, wm[w]);
+                for (w = 0; w < ATT_WARPS; ++w) {
+                    wt[w] = wm[w] == -INFINITY ? 0.0f : orc_expf_det(wm[w] - M);
+                    L = L + wt[w] * wl[w];
+                }
+                for (d = 0; d < hd; ++d) {
+                    float a = 0.0f;
+                    for (w = 0; w < ATT_WARPS; ++w) a = a + wt[w] * wacc[w * hd + d];
+                    pacc[s * hd + d] = a;
+                }
+                pm[s] = M;
+                pl[s] = L;
+                free(wacc);
+            }
+            {
+                float M = -INFINITY, L = 0.0f, inv;
+                size_t d;
+                for (s = 0; s < n_active; ++s) M = fmaxf(M, pm[s]);
+                for (s = 0; s < n_active; ++s)
+                    if (pm[s] != -INFINITY) L = L + orc_expf_det(pm[s] - M) * pl[s];
+                inv = L > 0.0f ? 1.0f / L : 0.0f;
+                for (d = 0; d < hd; ++d) {
+                    float o = 0.0f;
+                    for (s = 0; s < n_active; ++s)
+                        if (pm[s] != -INFINITY) o = o + orc_expf_det(pm[s] - M) * pacc[s * hd + d];
+                    out[h * hd + d] = o * inv;
+                }
+            }
+        }
+    }
+    free(pm);
+    free(pl);
+    free(pacc);
+    return 1;
+}
+
 /* ------------------------------------------------------------------ */
 /* forward                                                             */
 /* ------------------------------------------------------------------ */
@@ -558,8 +846,11 @@ static int mv(const orc_state *st, int dtype, const uint8_t *w, size_t rows, siz
               uint8_t *xq_scratch) {
     if (st->q8_1_activations && (dtype == ORC_Q4_K || dtype == ORC_Q6_K || dtype == ORC_Q8_0)) {
         if (!orc_q8_1_quantize(x, cols, xq_scratch)) return 0;
+        if (st->norm_order == 1) return orc_matvec_q8_1_dev(dtype, w, rows, cols, xq_scratch, y);
         return orc_matvec_q8_1(dtype, w, rows, cols, xq_scratch, y);
     }
+    if (st->norm_order == 1 && (dtype == ORC_F32 || dtype == ORC_F16 || dtype == ORC_BF16))
+        return orc_matvec_dense_dev(dtype, w, rows, cols, x, y);
     if (!st->q8_1_activations && st->matvec) return st->matvec(st->matvec_user, dtype, w, rows, cols, x, y);
     return orc_matvec_f32(dtype, w, rows, cols, x, y);
 }
@@ -599,13 +890,30 @@ int orc_forward_token(const orc_model *m, orc_state *st, uint32_t token, size_t 
         /* qwen3.uya:1668-1675 */
         memcpy(st->k_cache + ((size_t) L * m->context + pos) * kvd, k, kvd * 4);
         memcpy(st->v_cache + ((size_t) L * m->context + pos) * kvd, v, kvd * 4);
-        ok = ok && orc_attention(ctx, q, st->k_cache, st->v_cache, L, pos, m->heads, m->kv_heads, m->head_dim, m->context);
+        if (st->norm_order == 1) {
+            if (st->kv_f16) {
+                float *kc = st->k_cache + ((size_t) L * m->context + pos) * kvd;
+                float *vc = st->v_cache + ((size_t) L * m->context + pos) * kvd;
+                for (i = 0; i < kvd; ++i) {
+                    kc[i] = orc_f16_to_f32(orc_f32_to_f16_rne(kc[i]));
+                    vc[i] = orc_f16_to_f32(orc_f32_to_f16_rne(vc[i]));
+                }
+            }
+            ok = ok && orc_attention_dev(ctx, q, st->k_cache, st->v_cache, k, v, L, pos, m->heads, m->kv_heads,
+                                         m->head_dim, m->context);
+        } else {
+            ok = ok && orc_attention(ctx, q, st->k_cache, st->v_cache, L, pos, m->heads, m->kv_heads, m->head_dim,
+                                     m->context);
+        }
         ok = ok && mv(st, lw->o_dtype, lw->o, h, qd, ctx, ao, xq);
         for (i = 0; i < h; ++i) hid[i] = hid[i] + ao[i];
         ok = ok && orc_rms_norm(hid, lw->ffn_norm, lw->ffn_norm_dtype, h, m->eps, st->norm_order, nrm);
         ok = ok && mv(st, lw->gate_dtype, lw->gate, f, h, nrm, g, xq);
         ok = ok && mv(st, lw->up_dtype, lw->up, f, h, nrm, u, xq);
-        orc_silu_mul(fu, g, u, f);
+        if (st->norm_order == 1)
+            orc_silu_mul_dev(fu, g, u, f);
+        else
+            orc_silu_mul(fu, g, u, f);
         ok = ok && mv(st, lw->down_dtype, lw->down, h, f, fu, dn, xq);
         for (i = 0; i < h; ++i) hid[i] = hid[i] + dn[i];
     }

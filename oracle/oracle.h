@@ -8,7 +8,7 @@
  *
  * Every function cites the reference file:line it restates (paths are
  * relative to the reference project root).  Parity pins: see
- * oracle/ref_build.sh (reference sources compiled into oracle/_ref/) and
+ * oracle/Makefile (reference sources compiled into oracle/_ref/) and
  * tests/test_oracle_pins.py.
  */
 #ifndef MINICPMO_ORACLE_H
@@ -80,6 +80,32 @@ void orc_silu_mul(float *dst, const float *gate, const float *up, size_t n);
 uint32_t orc_argmax_penalized(const float *values, size_t n, const uint32_t *seen, size_t seen_count, float penalty,
                               float *top2_gap);
 
+/* ---- device evaluation order --------------------------------------------
+ * The reference fixes each operation's formula but not the order of float
+ * sums (its CPU and CUDA paths differ).  The B200 kernels evaluate in one
+ * documented order using only correctly rounded IEEE operations; the
+ * functions below restate that order so the whole decode step can be
+ * compared bit for bit.  Same formulas as the reference, fixed order:
+ *  - matvec: per row, LPR lanes (largest power of two <= 32 dividing
+ *    cols/256); lane l sums super-blocks l, l+LPR, ... in order; the lanes
+ *    are combined by an xor butterfly (LPR/2 .. 1) and lane 0 is the row;
+ *  - attention: split-K over attn_n_split(n_kv) position chunks of
+ *    max(32, ceil((pos+1)/splits)) positions, 4 interleaved warps per chunk,
+ *    online softmax per warp, merged warp by warp then split by split;
+ *  - exp: orc_expf_det (Cody-Waite reduction + degree-7 Taylor/Horner).
+ */
+float orc_expf_det(float x);
+int orc_attn_n_split(int n_kv);
+uint16_t orc_f32_to_f16_rne(float v); /* IEEE round-to-nearest-even (f16 KV cache) */
+int orc_matvec_q8_1_dev(int dtype, const uint8_t *w, size_t rows, size_t cols, const uint8_t *xq, float *y);
+int orc_matvec_dense_dev(int dtype, const uint8_t *w, size_t rows, size_t cols, const float *x, float *y);
+void orc_silu_mul_dev(float *dst, const float *gate, const float *up, size_t n);
+/* k_cache/v_cache hold f32 values (already rounded through f16 when the
+ * cache is f16); cur_k/cur_v are the current position's unrounded rows. */
+int orc_attention_dev(float *out, const float *q, const float *k_cache, const float *v_cache, const float *cur_k,
+                      const float *cur_v, size_t layer, size_t pos, size_t head_count, size_t kv_head_count,
+                      size_t head_dim, size_t context);
+
 /* ---- whole decode step (qwen3.uya:1920-1995) ---- */
 typedef struct orc_layer {
     const void *attn_norm; int attn_norm_dtype;
@@ -116,8 +142,10 @@ typedef struct orc_state {
     /* mode 1: Q8_1 activations + per-block int dots (the CUDA path);
      * mode 0: f32 activations (the CPU path). */
     int q8_1_activations;
-    /* norm reduction order, see orc_rms_norm */
+    /* 0: the reference CPU order (sequential sums, libm expf);
+     * 1: the device evaluation order above (bit-exact contract) */
     int norm_order;
+    int kv_f16; /* order 1 only: the KV cache stores f16 (RNE) values */
     orc_matvec_fn matvec; void *matvec_user; /* optional, mode 0 only */
 } orc_state;
 

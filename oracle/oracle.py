@@ -64,6 +64,13 @@ def orc() -> C.CDLL:
             "orc_pool_destroy": (None, [C.c_void_p]),
             "orc_pool_is_reference": (C.c_int, [C.c_void_p]),
             "orc_state_attach_pool": (None, [C.c_void_p, C.c_void_p]),
+            "orc_expf_det": (C.c_float, [C.c_float]),
+            "orc_attn_n_split": (C.c_int, [C.c_int]),
+            "orc_f32_to_f16_rne": (C.c_uint16, [C.c_float]),
+            "orc_matvec_q8_1_dev": (C.c_int, [C.c_int, u8p, sz, sz, u8p, fp]),
+            "orc_matvec_dense_dev": (C.c_int, [C.c_int, u8p, sz, sz, fp, fp]),
+            "orc_silu_mul_dev": (None, [fp, fp, fp, sz]),
+            "orc_attention_dev": (C.c_int, [fp, fp, fp, fp, fp, fp, sz, sz, sz, sz, sz, sz]),
         }
         for n, (r, a) in sig.items():
             fn = getattr(lib, n)
@@ -176,6 +183,44 @@ def attention(q, k_cache, v_cache, layer, pos, heads, kv_heads, head_dim, contex
     return out
 
 
+def expf_det(x: np.ndarray) -> np.ndarray:
+    return np.array([orc().orc_expf_det(float(v)) for v in np.asarray(x, np.float32).ravel()], np.float32)
+
+
+def matvec_q8_1_dev(dtype: int, w: np.ndarray, rows: int, cols: int, xq: np.ndarray) -> np.ndarray:
+    """Device evaluation order (bit-exact contract with the GEMV kernel)."""
+    y = np.empty(rows, np.float32)
+    assert orc().orc_matvec_q8_1_dev(dtype, _u8(w), rows, cols, _u8(xq), _f(y))
+    return y
+
+
+def matvec_dense_dev(dtype: int, w: np.ndarray, rows: int, cols: int, x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty(rows, np.float32)
+    assert orc().orc_matvec_dense_dev(dtype, _u8(w), rows, cols, _f(x), _f(y))
+    return y
+
+
+def silu_mul_dev(g: np.ndarray, u: np.ndarray) -> np.ndarray:
+    g = np.ascontiguousarray(g, dtype=np.float32)
+    u = np.ascontiguousarray(u, dtype=np.float32)
+    out = np.empty_like(g)
+    orc().orc_silu_mul_dev(_f(out), _f(g), _f(u), g.size)
+    return out
+
+
+def attention_dev(q, k_cache, v_cache, cur_k, cur_v, layer, pos, heads, kv_heads, head_dim, context) -> np.ndarray:
+    q = np.ascontiguousarray(q, dtype=np.float32)
+    kc = np.ascontiguousarray(k_cache, dtype=np.float32)
+    vc = np.ascontiguousarray(v_cache, dtype=np.float32)
+    ck = np.ascontiguousarray(cur_k, dtype=np.float32)
+    cv = np.ascontiguousarray(cur_v, dtype=np.float32)
+    out = np.empty(heads * head_dim, np.float32)
+    assert orc().orc_attention_dev(_f(out), _f(q), _f(kc), _f(vc), _f(ck), _f(cv), layer, pos, heads, kv_heads,
+                                   head_dim, context)
+    return out
+
+
 def silu_mul(g: np.ndarray, u: np.ndarray) -> np.ndarray:
     g = np.ascontiguousarray(g, dtype=np.float32)
     u = np.ascontiguousarray(u, dtype=np.float32)
@@ -227,21 +272,22 @@ class OrcModel(C.Structure):
 class OrcState(C.Structure):
     _fields_ = [
         ("k_cache", fp), ("v_cache", fp), ("q8_1_activations", C.c_int), ("norm_order", C.c_int),
-        ("matvec", C.c_void_p), ("matvec_user", C.c_void_p),
+        ("kv_f16", C.c_int), ("matvec", C.c_void_p), ("matvec_user", C.c_void_p),
     ]
 
 
 class OracleModel:
     """CPU decode of a model given as {name: (dtype, rows, cols, bytes)}.
 
-    q8_1=True: the reference CUDA path's arithmetic (Q8_1 activations, norm
-    reduction order of the GPU shim); q8_1=False: the reference CPU path
-    (f32 activations, sequential norms), optionally through a threaded pool
-    calling the reference's own native matvec.
+    q8_1=True: the reference CUDA path's arithmetic (Q8_1 activations) in the
+    device evaluation order (device_order=True, the bit-exact contract) or
+    in natural order with libm expf (device_order=False); q8_1=False: the
+    reference CPU path (f32 activations, sequential norms), optionally through
+    a threaded pool calling the reference's own native matvec.
     """
 
     def __init__(self, shape, tensors: Dict[str, tuple], context: int, q8_1: bool = True, pool_threads: int = 0,
-                 use_reference_matvec: bool = False):
+                 use_reference_matvec: bool = False, device_order: bool = True, kv_f16: bool = False):
         self.shape = shape
         self.context = context
         self._keep = {k: np.ascontiguousarray(v[3]) for k, v in tensors.items()}
@@ -281,7 +327,8 @@ class OracleModel:
         st = OrcState()
         st.k_cache, st.v_cache = _f(self.kc), _f(self.vc)
         st.q8_1_activations = int(q8_1)
-        st.norm_order = 1 if q8_1 else 0
+        st.norm_order = 1 if (q8_1 and device_order) else 0
+        st.kv_f16 = int(kv_f16)
         self.state = st
         self.pool = None
         if pool_threads and not q8_1:

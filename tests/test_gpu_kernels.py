@@ -1,8 +1,11 @@
 """Parity of the sm_100a kernels with the CPU oracle, through the C ABI.
 
-Integer and byte work is bit-exact (Q8_1 blocks, per-block int32 dots,
-embedding dequant, norms/RoPE which use only round-to-nearest IEEE ops in a
-fixed order); float reductions are held to the tolerances stated below.
+Everything is bit-exact against the oracle's device-order restatement:
+integer and byte work by construction (Q8_1 blocks, per-block int32 dots,
+embedding dequant), float work because the kernels use only correctly
+rounded IEEE operations in the documented order (oracle/oracle.h, "device
+evaluation order").  Against the reference's natural summation order the
+float results are held to the stated tolerances.
 """
 from __future__ import annotations
 
@@ -72,8 +75,8 @@ def test_matvec_dots_bit_exact_and_rows_close(pkg, gpu_ctx, O, dt, rows, cols):
     xq = O.q8_1_quantize(rvec(cols, cols))
     y, dots = gpu_ctx.matvec_q8_1(t, xq, dots=True)
     assert np.array_equal(dots, O.block_dots(dt, t.data, rows, cols, xq))
-    ref = O.matvec_q8_1(dt, t.data, rows, cols, xq)
-    assert rel_row_err(y, ref) < MATVEC_TOL
+    assert np.array_equal(y, O.matvec_q8_1_dev(dt, t.data, rows, cols, xq))
+    assert rel_row_err(y, O.matvec_q8_1(dt, t.data, rows, cols, xq)) < MATVEC_TOL
 
 
 @pytest.mark.parametrize("dt", [Q4_K, Q6_K])
@@ -106,7 +109,9 @@ def test_dense_matvec(pkg, gpu_ctx, O, dt):
     t, _ = make_tensor(pkg, f"dense{dt}", dt, rows, cols, seed=dt + 7)
     gpu_ctx.upload_tensor(t)
     x = rvec(cols, 9)
-    assert rel_row_err(gpu_ctx.matvec(t, x), O.matvec_f32(dt, t.data, rows, cols, x)) < 1e-5
+    y = gpu_ctx.matvec(t, x)
+    assert np.array_equal(y, O.matvec_dense_dev(dt, t.data, rows, cols, x))
+    assert rel_row_err(y, O.matvec_f32(dt, t.data, rows, cols, x)) < 1e-5
 
 
 def test_grouped_slot_matvec_mixed_dtypes(pkg, gpu_ctx, O):
@@ -122,9 +127,9 @@ def test_grouped_slot_matvec_mixed_dtypes(pkg, gpu_ctx, O):
     gpu_ctx.slot_matvec3(3, tq, 4, tk, 5, tv, 1)
     xq = O.q8_1_quantize(x)
     for slot, t in ((3, tq), (4, tk), (5, tv)):
-        assert rel_row_err(gpu_ctx.slot_download(slot, t.rows), O.matvec_q8_1(t.dtype, t.data, t.rows, h, xq)) < MATVEC_TOL
+        assert np.array_equal(gpu_ctx.slot_download(slot, t.rows), O.matvec_q8_1_dev(t.dtype, t.data, t.rows, h, xq))
     gpu_ctx.slot_matvec2(6, tk, 7, tv, 1)
-    assert rel_row_err(gpu_ctx.slot_download(7, tv.rows), O.matvec_q8_1(Q6_K, tv.data, tv.rows, h, xq)) < MATVEC_TOL
+    assert np.array_equal(gpu_ctx.slot_download(7, tv.rows), O.matvec_q8_1_dev(Q6_K, tv.data, tv.rows, h, xq))
 
 
 # -------------------------------------------------------------- slot ops
@@ -160,7 +165,9 @@ def test_slot_add_silu(gpu_ctx, O):
     gpu_ctx.slot_upload(10, g)
     gpu_ctx.slot_upload(11, u)
     gpu_ctx.slot_silu_mul(12, 10, 11, 3000)
-    assert np.allclose(gpu_ctx.slot_download(12, 3000), O.silu_mul(g, u), rtol=2e-6, atol=1e-7)
+    out = gpu_ctx.slot_download(12, 3000)
+    assert np.array_equal(out, O.silu_mul_dev(g, u))
+    assert np.allclose(out, O.silu_mul(g, u), rtol=4e-7 * 4, atol=1e-30)  # within a few ulp of libm expf
     gpu_ctx.slot_add_inplace(10, 11, 3000)
     assert np.array_equal(gpu_ctx.slot_download(10, 3000), g + u)
 
@@ -185,6 +192,8 @@ def test_attention_slots_vs_oracle(gpu_ctx, O, heads, kv, hd):
             gpu_ctx.slot_upload(2, v)
             gpu_ctx.attention_slots(3, 0, 1, 2, layer, pos, heads, kv, hd, ctx)
             out = gpu_ctx.slot_download(3, heads * hd)
+            dev = O.attention_dev(q, kc, vc, kc[layer, pos], vc[layer, pos], layer, pos, heads, kv, hd, ctx)
+            assert np.array_equal(out, dev), (pos, np.abs(out - dev).max())
             ref = O.attention(q, kc, vc, layer, pos, heads, kv, hd, ctx)
             assert np.allclose(out, ref, rtol=1e-4, atol=1e-5), (pos, np.abs(out - ref).max())
         else:
@@ -192,8 +201,8 @@ def test_attention_slots_vs_oracle(gpu_ctx, O, heads, kv, hd):
             q = rng.standard_normal(heads * hd).astype(np.float32)
             out = gpu_ctx.attention(q, k, v, layer, pos, heads, kv, hd, ctx)
             if pos % 64 == 5:
-                ref = O.attention(q, kc, vc, layer, pos, heads, kv, hd, ctx)
-                assert np.allclose(out, ref, rtol=1e-4, atol=1e-5)
+                dev = O.attention_dev(q, kc, vc, kc[layer, pos], vc[layer, pos], layer, pos, heads, kv, hd, ctx)
+                assert np.array_equal(out, dev)
 
 
 @pytest.mark.parametrize("dt,rows,cols", [(Q6_K, 64, 1024), (Q4_K, 50, 512), (Q8_0, 33, 768), (F16, 20, 96), (F32, 9, 40)])

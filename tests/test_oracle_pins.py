@@ -178,3 +178,17 @@ def test_cpu_matvec_live_vs_reference(O, pkg, dt):
     w = gguf.quantize(torch.randn((rows, cols), generator=torch.Generator().manual_seed(7)) * 0.02, dt).numpy()
     x = np.random.Generator(np.random.PCG64(8)).standard_normal(cols).astype(np.float32)
     assert rel_row_err(O.matvec_f32(dt, w, rows, cols, x), O.ref_cpu_matvec(dt, w, rows, cols, x)) < 1e-5
+
+
+# ------------------------------------------- 4. deterministic exp accuracy
+def test_expf_det_accuracy(O):
+    """orc_expf_det (shared by the kernels) stays within 2 ulp of libm expf."""
+    xs = np.concatenate([np.linspace(-103.9, 88.7, 20001, dtype=np.float32),
+                         np.random.Generator(np.random.PCG64(1)).uniform(-20, 20, 20000).astype(np.float32),
+                         np.array([0.0, -0.0, 1e-30, -1e-30, 88.72, -87.3, -100.0], np.float32)])
+    got = O.expf_det(xs)
+    ref = np.exp(xs.astype(np.float64))
+    ok = ref > np.finfo(np.float32).tiny
+    ulp = np.spacing(ref[ok].astype(np.float32)).astype(np.float64)
+    assert np.max(np.abs(got[ok] - ref[ok]) / ulp) <= 2.0
+    assert O.expf_det(np.array([-np.inf]))[0] == 0.0 and np.isinf(O.expf_det(np.array([np.inf]))[0])
