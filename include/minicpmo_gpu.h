@@ -209,6 +209,9 @@ MINICPMO_API int minicpmo_gpu_context_time_matvec(void *handle, const void *host
  * copies); reports the total milliseconds. */
 MINICPMO_API int minicpmo_gpu_context_qwen3_time_decode(void *handle, uint32_t first_token, size_t first_pos, size_t n_steps,
                                            float *total_ms, char *error, size_t error_cap);
+/* Kernel launches in one decode step's graph (with or without the lm_head
+ * and sampler); 0 when no model is bound. */
+MINICPMO_API int minicpmo_gpu_context_qwen3_step_kernels(void *handle, int with_logits);
 /* Bytes of device memory held by the uploaded copy of a tensor. */
 MINICPMO_API size_t minicpmo_gpu_context_tensor_device_bytes(void *handle, const void *host_ptr);
 

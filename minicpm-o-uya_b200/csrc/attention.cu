@@ -24,7 +24,9 @@
 #include <math.h>
 
 #include "common.cuh"
+#include "gemv.cuh"
 #include "rowops.cuh"
+#include "tma.cuh"
 
 namespace mcpo {
 
@@ -79,6 +81,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a)
   const AttnSmem sm = carve(smem_f, hd);
   const int kvh = blockIdx.x, split = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_wait();
+  pdl_launch_dependents();
   const int hb = (kvh * a.n_head + a.n_kv - 1) / a.n_kv;
   const int he = ((kvh + 1) * a.n_head + a.n_kv - 1) / a.n_kv;
   const int pos = a.pos_ptr ? *a.pos_ptr : a.pos_static;
@@ -262,19 +266,11 @@ size_t attn_smem_bytes(int hd) {
 }
 
 template <int J>
-cudaError_t launch_j(const AttnArgs& a, cudaStream_t st) {
+cudaError_t launch_j(const AttnArgs& a, cudaStream_t st, bool pdl) {
   const dim3 grid(a.n_kv, a.n_split);
   const size_t smem = attn_smem_bytes(a.head_dim);
-  if (a.kv_f16) {
-    if (smem > 48 * 1024)
-      cudaFuncSetAttribute(k_attention<J, __half>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    k_attention<J, __half><<<grid, kAttnWarps * 32, smem, st>>>(a);
-  } else {
-    if (smem > 48 * 1024)
-      cudaFuncSetAttribute(k_attention<J, float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    k_attention<J, float><<<grid, kAttnWarps * 32, smem, st>>>(a);
-  }
-  return cudaGetLastError();
+  if (a.kv_f16) return launch_k(k_attention<J, __half>, grid, dim3(kAttnWarps * 32), smem, st, pdl, a);
+  return launch_k(k_attention<J, float>, grid, dim3(kAttnWarps * 32), smem, st, pdl, a);
 }
 
 }  // namespace
@@ -283,13 +279,13 @@ size_t attn_partial_floats(int n_head, int n_split, int head_dim) {
   return (size_t)n_head * n_split * (head_dim + 2);
 }
 
-cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st) {
+cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st, bool pdl) {
   switch (a.head_dim) {
-    case 64: return launch_j<2>(a, st);
-    case 128: return launch_j<4>(a, st);
-    case 256: return launch_j<8>(a, st);
+    case 64: return launch_j<2>(a, st, pdl);
+    case 128: return launch_j<4>(a, st, pdl);
+    case 256: return launch_j<8>(a, st, pdl);
     default:
-      if (a.head_dim > 0 && a.head_dim <= 32) return launch_j<1>(a, st);
+      if (a.head_dim > 0 && a.head_dim <= 32) return launch_j<1>(a, st, pdl);
       return cudaErrorInvalidValue;
   }
 }

@@ -36,6 +36,6 @@ struct AttnArgs {
 };
 
 size_t attn_partial_floats(int n_head, int n_split, int head_dim);
-cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st);
+cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st, bool pdl = false);
 
 }  // namespace mcpo

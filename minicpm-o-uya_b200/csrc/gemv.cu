@@ -11,27 +11,43 @@
 // quantity as dp4a(0x01010101, q8) in gpu_shim.c:797-800.
 //
 // Design (batch-1 decode is a weight stream):
-//  * weights are pre-tiled at upload (layout.cuh) so that every warp load is
-//    a coalesced 512-byte 128-bit access with L1 bypass;
+//  * weights are pre-tiled at upload (layout.cuh) into 16-byte aligned step
+//    blocks; a persistent CTA per SM owns a contiguous range of warp-rows;
+//  * one producer thread streams step blocks with cp.async.bulk (TMA) into a
+//    ring of shared-memory slots per consumer warp (mbarrier full/empty
+//    handshake, bounded waits), keeping ~100+ KB per SM in flight, and starts
+//    before the previous kernel has finished (programmatic dependent launch:
+//    weights do not depend on it);
+//  * eight consumer warps read their slots with conflict-free 16-byte shared
+//    loads, decode scales in registers and reduce with dp4a and xor
+//    butterflies;
 //  * the Q8_1 activation vector lives in shared memory, transposed to
 //    [16-byte chunk][super-block] so lanes of a row read consecutive 16-byte
 //    words without bank conflicts;
-//  * up to three matrices sharing one input (q/k/v, gate/up) are one launch
-//    over a common tile space, dtype chosen per CTA tile;
+//  * up to three matrices sharing one input (q/k/v) are one launch over a
+//    common warp-row space, dtype chosen per warp-row;
 //  * epilogues: store, residual add, SwiGLU pairing of gate and up rows.
+// Float arithmetic uses only correctly rounded operations in a fixed order
+// (per lane over its super-blocks, then the butterfly), so results do not
+// depend on the launch shape.
 #include "gemv.cuh"
 
 #include <math.h>
+#include <stdlib.h>
+
+#include "tma.cuh"
 
 namespace mcpo {
 
 namespace {
 
+// All per-super-block arrays are stored [index within the SB][SB] so that
+// the lanes of a row (consecutive SBs) hit consecutive banks.
 struct XShared {
   const uint4* xs;    // [16][nb] 16-byte chunks of q8
-  const float* xd;    // [cols/32] d8 (f32 of the f16 d)
-  const float* xds;   // [cols/32] d8 * sum(q8)
-  const int* xs16;    // [cols/16] sum(q8) over 16 values
+  const float* xd;    // [8][nb]  d8 of each Q8_1 block (f32 of the f16 d)
+  const float* xds;   // [8][nb]  d8 * sum(q8)
+  const int* xs16;    // [16][nb] sum(q8) over each 16 values
   int nb;
 };
 
@@ -43,12 +59,27 @@ __device__ __forceinline__ int dot4(uint4 w, uint4 x, int acc) {
   return acc;
 }
 
-__device__ __forceinline__ uint4 and4(uint4 v, uint32_t m) { return make_uint4(v.x & m, v.y & m, v.z & m, v.w & m); }
-__device__ __forceinline__ uint4 shr4(uint4 v, int s) { return make_uint4(v.x >> s, v.y >> s, v.z >> s, v.w >> s); }
-__device__ __forceinline__ uint4 or4(uint4 a, uint4 b) { return make_uint4(a.x | b.x, a.y | b.y, a.z | b.z, a.w | b.w); }
-__device__ __forceinline__ uint4 shl4(uint4 v, int s) { return make_uint4(v.x << s, v.y << s, v.z << s, v.w << s); }
+
+// dp4a with the first operand as unsigned bytes (for masked high nibbles /
+// bit pairs that reach 0xf0 / 0xc0).
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+__device__ __forceinline__ int dot4_mask(uint4 w, uint4 x, uint32_t m, int acc) {
+  acc = dp4a_us(w.x & m, x.x, acc);
+  acc = dp4a_us(w.y & m, x.y, acc);
+  acc = dp4a_us(w.z & m, x.z, acc);
+  acc = dp4a_us(w.w & m, x.w, acc);
+  return acc;
+}
 
 // ---- Q4_K super-block: c[0] = {d, dmin, scales}, c[1..8] = qs ----
+// Per sub-block j: dot_j = sum q4*q8 (exact int); the row value is
+//   d*sum_j(d8_j*(sc_j*dot_j)) - dmin*sum_j(d8_j*sumq8_j*m_j)
+// evaluated as fma chains in j order (see the device-order oracle).
 template <bool kDots>
 __device__ __forceinline__ float sb_dot_q4k(const uint4* c, const XShared& x, int sb, int* dots) {
   const uint4 h = c[0];
@@ -67,28 +98,28 @@ __device__ __forceinline__ float sb_dot_q4k(const uint4* c, const XShared& x, in
     const uint4 x1 = x.xs[(4 * g + 1) * x.nb + sb];
     const uint4 x2 = x.xs[(4 * g + 2) * x.nb + sb];
     const uint4 x3 = x.xs[(4 * g + 3) * x.nb + sb];
-    int dlo = dot4(and4(q0, 0x0f0f0f0fu), x0, 0);
-    dlo = dot4(and4(q1, 0x0f0f0f0fu), x1, dlo);
-    int dhi = dot4(and4(shr4(q0, 4), 0x0f0f0f0fu), x2, 0);
-    dhi = dot4(and4(shr4(q1, 4), 0x0f0f0f0fu), x3, dhi);
+    const int dlo = dot4_mask(q1, x1, 0x0f0f0f0fu, dot4_mask(q0, x0, 0x0f0f0f0fu, 0));
+    const int dhi = dot4_mask(q1, x3, 0xf0f0f0f0u, dot4_mask(q0, x2, 0xf0f0f0f0u, 0)) >> 4;
     const int j0 = 2 * g, j1 = 2 * g + 1;
     const uint32_t scw = j0 < 4 ? sc_lo : sc_hi, mnw = j0 < 4 ? mn_lo : mn_hi;
     const int s0 = (scw >> (8 * (j0 & 3))) & 0xff, s1 = (scw >> (8 * (j1 & 3))) & 0xff;
     const int m0 = (mnw >> (8 * (j0 & 3))) & 0xff, m1 = (mnw >> (8 * (j1 & 3))) & 0xff;
-    const int xb = sb * 8;
-    const float t0 = __fmul_rn(__fmul_rn((float)s0, x.xd[xb + j0]), (float)dlo);
-    const float t1 = __fmul_rn(__fmul_rn((float)s1, x.xd[xb + j1]), (float)dhi);
-    sum_d = __fadd_rn(sum_d, __fadd_rn(t0, t1));
-    sum_m = __fadd_rn(sum_m, __fadd_rn(__fmul_rn((float)m0, x.xds[xb + j0]), __fmul_rn((float)m1, x.xds[xb + j1])));
+    sum_d = __fmaf_rn(x.xd[j0 * x.nb + sb], (float)(s0 * dlo), sum_d);
+    sum_d = __fmaf_rn(x.xd[j1 * x.nb + sb], (float)(s1 * dhi), sum_d);
+    sum_m = __fmaf_rn(x.xds[j0 * x.nb + sb], (float)m0, sum_m);
+    sum_m = __fmaf_rn(x.xds[j1 * x.nb + sb], (float)m1, sum_m);
     if (kDots && dots) {
       dots[sb * 8 + j0] = dlo;
       dots[sb * 8 + j1] = dhi;
     }
   }
-  return __fsub_rn(__fmul_rn(d, sum_d), __fmul_rn(dmin, sum_m));
+  return __fmaf_rn(d, sum_d, -__fmul_rn(dmin, sum_m));
 }
 
 // ---- Q6_K super-block: c[0..7] = ql, c[8..11] = qh, c[12] = sc, d separate ----
+// Per 16-value group g: dot_g = sum (q6-32)*q8, with q6 = lo4 + 16*hi2 taken
+// as two masked dp4a terms; the two groups of a Q8_1 block are combined in
+// integers: sum_b(d8_b * (sc_2b*dot_2b + sc_2b+1*dot_2b+1)), then times d.
 template <bool kDots>
 __device__ __forceinline__ float sb_dot_q6k(const uint4* c, uint16_t dbits, const XShared& x, int sb, int* dots) {
   const float d = f16_to_f32(dbits);
@@ -99,19 +130,34 @@ __device__ __forceinline__ float sb_dot_q6k(const uint4* c, uint16_t dbits, cons
   for (int n = 0; n < 2; ++n) {
 #pragma unroll
     for (int qq = 0; qq < 4; ++qq) {
+      int dg[2];
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int g = 8 * n + 2 * qq + h;
         const uint4 qlw = c[4 * n + ((qq & 1) ? 2 : 0) + h];
         const uint4 qhw = c[8 + 2 * n + h];
-        const uint4 lo = and4(shr4(qlw, (qq >= 2) ? 4 : 0), 0x0f0f0f0fu);
-        const uint4 hi = shl4(and4(shr4(qhw, 2 * qq), 0x03030303u), 4);
-        const int raw = dot4(or4(lo, hi), x.xs[g * x.nb + sb], 0);
-        const int dotg = raw - 32 * x.xs16[sb * 16 + g];
-        const int scale = (int)(int8_t)((scw[g >> 2] >> (8 * (g & 3))) & 0xff);
-        sum = __fadd_rn(sum, __fmul_rn(x.xd[sb * 8 + (g >> 1)], __fmul_rn((float)dotg, (float)scale)));
-        if (kDots && dots) dots[sb * 16 + g] = dotg;
+        const uint4 xv = x.xs[g * x.nb + sb];
+        int lo, hi;
+        if (qq == 0) {
+          lo = dot4_mask(qlw, xv, 0x0f0f0f0fu, 0);
+          hi = dot4_mask(qhw, xv, 0x03030303u, 0) * 16;
+        } else if (qq == 1) {
+          lo = dot4_mask(qlw, xv, 0x0f0f0f0fu, 0);
+          hi = dot4_mask(qhw, xv, 0x0c0c0c0cu, 0) * 4;
+        } else if (qq == 2) {
+          lo = dot4_mask(qlw, xv, 0xf0f0f0f0u, 0) >> 4;
+          hi = dot4_mask(qhw, xv, 0x30303030u, 0);
+        } else {
+          lo = dot4_mask(qlw, xv, 0xf0f0f0f0u, 0) >> 4;
+          hi = dot4_mask(qhw, xv, 0xc0c0c0c0u, 0) >> 2;
+        }
+        dg[h] = lo + hi - 32 * x.xs16[g * x.nb + sb];
+        if (kDots && dots) dots[sb * 16 + g] = dg[h];
       }
+      const int g0 = 8 * n + 2 * qq;
+      const int sc0 = (int)(int8_t)((scw[g0 >> 2] >> (8 * (g0 & 3))) & 0xff);
+      const int sc1 = (int)(int8_t)((scw[(g0 + 1) >> 2] >> (8 * ((g0 + 1) & 3))) & 0xff);
+      sum = __fmaf_rn(x.xd[(g0 >> 1) * x.nb + sb], (float)(sc0 * dg[0] + sc1 * dg[1]), sum);
     }
   }
   return __fmul_rn(d, sum);
@@ -128,42 +174,55 @@ __device__ __forceinline__ float sb_dot_q80(const uint4* c, const XShared& x, in
     int acc = dot4(c[1 + 2 * b], x.xs[(2 * b) * x.nb + sb], 0);
     acc = dot4(c[2 + 2 * b], x.xs[(2 * b + 1) * x.nb + sb], acc);
     const float dwf = f16_to_f32((uint16_t)((dw[b >> 1] >> (16 * (b & 1))) & 0xffffu));
-    sum = __fadd_rn(sum, __fmul_rn(__fmul_rn(dwf, x.xd[sb * 8 + b]), (float)acc));
+    sum = __fmaf_rn(__fmul_rn(dwf, x.xd[b * x.nb + sb]), (float)acc, sum);
     if (kDots && dots) dots[sb * 8 + b] = acc;
   }
   return sum;
 }
 
-// Dot of one lane tile row segment: the lane's super-blocks of one row.
-template <int kDtype, bool kDots>
-__device__ __forceinline__ float lane_row_dot(const uint8_t* tile_base, const GemvSeg& s, int warp, int lane,
-                                              int lane_in_row, const XShared& x, int* dots) {
-  constexpr int kChunks = kDtype == kQ4_K ? 9 : kDtype == kQ6_K ? 13 : 17;
-  float acc = 0.0f;
-  for (int k = 0; k < s.ks; ++k) {
-    const uint8_t* blk = tile_base + ((size_t)k * kGemvWarps + warp) * s.step_bytes;
-    uint4 c[kChunks];
+
+// Kernel instantiations by the dtypes they can meet (smaller code per kernel).
+enum GemvClass : int { kClassQ4K = 0, kClassQ6K = 1, kClassQ80 = 2, kClassQ4K6K = 3 };
+
+// Value of one super-block for this lane from its step block in shared memory.
+template <bool kDots>
+__device__ __forceinline__ float step_q4k(const uint8_t* blk, int lane, const XShared& x, int sb, int* dots) {
+  uint4 c[9];
 #pragma unroll
-    for (int i = 0; i < kChunks; ++i) c[i] = ldg_stream(blk + i * 512 + lane * 16);
-    const int sb = k * s.lpr + lane_in_row;
-    if (kDtype == kQ4_K) {
-      acc = __fadd_rn(acc, sb_dot_q4k<kDots>(c, x, sb, dots));
-    } else if (kDtype == kQ6_K) {
-      const uint16_t db = *reinterpret_cast<const uint16_t*>(blk + 13 * 512 + lane * 2);
-      acc = __fadd_rn(acc, sb_dot_q6k<kDots>(c, db, x, sb, dots));
-    } else {
-      acc = __fadd_rn(acc, sb_dot_q80<kDots>(c, x, sb, dots));
-    }
-  }
-  return acc;
+  for (int i = 0; i < 9; ++i) c[i] = *reinterpret_cast<const uint4*>(blk + i * 512 + lane * 16);
+  return sb_dot_q4k<kDots>(c, x, sb, dots);
 }
 
 template <bool kDots>
-__device__ __forceinline__ float seg_row_dot(const uint8_t* tile_base, const GemvSeg& s, int warp, int lane,
-                                             int lane_in_row, const XShared& x, int* dots) {
-  if (s.dtype == kQ4_K) return lane_row_dot<kQ4_K, kDots>(tile_base, s, warp, lane, lane_in_row, x, dots);
-  if (s.dtype == kQ6_K) return lane_row_dot<kQ6_K, kDots>(tile_base, s, warp, lane, lane_in_row, x, dots);
-  return lane_row_dot<kQ8_0, kDots>(tile_base, s, warp, lane, lane_in_row, x, dots);
+__device__ __forceinline__ float step_q6k(const uint8_t* blk, int lane, const XShared& x, int sb, int* dots) {
+  uint4 c[13];
+#pragma unroll
+  for (int i = 0; i < 13; ++i) c[i] = *reinterpret_cast<const uint4*>(blk + i * 512 + lane * 16);
+  const uint16_t db = *reinterpret_cast<const uint16_t*>(blk + 13 * 512 + lane * 2);
+  return sb_dot_q6k<kDots>(c, db, x, sb, dots);
+}
+
+template <bool kDots>
+__device__ __forceinline__ float step_q80(const uint8_t* blk, int lane, const XShared& x, int sb, int* dots) {
+  uint4 c[17];
+#pragma unroll
+  for (int i = 0; i < 17; ++i) c[i] = *reinterpret_cast<const uint4*>(blk + i * 512 + lane * 16);
+  return sb_dot_q80<kDots>(c, x, sb, dots);
+}
+
+template <int kClass, bool kDots>
+__device__ __forceinline__ float step_value(int dtype, const uint8_t* blk, int lane, const XShared& x, int sb,
+                                            int* dots) {
+  if constexpr (kClass == kClassQ4K) {
+    return step_q4k<kDots>(blk, lane, x, sb, dots);
+  } else if constexpr (kClass == kClassQ6K) {
+    return step_q6k<kDots>(blk, lane, x, sb, dots);
+  } else if constexpr (kClass == kClassQ80) {
+    return step_q80<kDots>(blk, lane, x, sb, dots);
+  } else {
+    if (dtype == kQ4_K) return step_q4k<kDots>(blk, lane, x, sb, dots);
+    return step_q6k<kDots>(blk, lane, x, sb, dots);
+  }
 }
 
 // Butterfly over the lpr lanes of a row (xor lpr/2 .. 1); the row's value is
@@ -173,9 +232,22 @@ __device__ __forceinline__ float reduce_row(float v, int lpr) {
   return v;
 }
 
-template <bool kDots>
-__global__ void __launch_bounds__(kGemvThreads) k_gemv(const GemvArgs a) {
-  extern __shared__ __align__(16) uint8_t smem[];
+__device__ __forceinline__ const GemvSeg& seg_of(const GemvArgs& a, int wr) {
+  if (a.nseg > 2 && wr >= a.seg[2].wr_begin) return a.seg[2];
+  if (a.nseg > 1 && wr >= a.seg[1].wr_begin) return a.seg[1];
+  return a.seg[0];
+}
+
+constexpr int kMaxConsumers = 16;  // consumer warps per CTA (+1 producer warp)
+
+__host__ __device__ inline size_t gemv_x_bytes(int cols) {
+  const size_t b = (size_t)cols + (size_t)(cols / 32) * 8 + (size_t)(cols / 16) * 4;
+  return (b + 127) / 128 * 128;
+}
+
+template <int kClass, bool kDots>
+__global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1) k_gemv(const GemvArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
   const int cols = a.cols;
   const int nb = cols / 256;
   const int nblk = cols / 32;
@@ -183,58 +255,119 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv(const GemvArgs a) {
   float* xd = reinterpret_cast<float*>(smem + cols);
   float* xds = xd + nblk;
   int* xs16 = reinterpret_cast<int*>(xds + nblk);
+  const int S = a.stages;
+  const int slot = a.slot_bytes;
+  const int NC = (int)(blockDim.x >> 5) - 1;  // consumer warps; the last warp produces
+  uint8_t* ring = smem + gemv_x_bytes(cols);
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + (size_t)NC * S * slot);
+  uint64_t* empty = full + NC * S;
 
-  // Prologue: Q8_1 blocks -> shared, transposed to [chunk][super-block].
-  for (int b = threadIdx.x; b < nblk; b += blockDim.x) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int T = a.total_wr, G = gridDim.x;
+  const int wr0 = (int)((long long)blockIdx.x * T / G);
+  const int wr1 = (int)((long long)(blockIdx.x + 1) * T / G);
+  const int nwr = wr1 - wr0;
+  const bool swiglu = a.seg[0].epi == kEpiSwiglu;
+  const int ks = a.seg[0].ks;
+  const int spi = ks * (swiglu ? 2 : 1);  // steps per warp-row
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NC * S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
+
+  if (warp == NC) {
+    // ---- producer warp: lane w streams consumer warp w's step blocks into
+    // that warp's ring (independent lanes, so one slow consumer never holds
+    // up the copies of another).  Needs nothing from the previous kernel, so
+    // it does not wait for it.
+    const int w = lane;
+    if (w >= NC) return;
+    const int steps = (nwr > w ? (nwr - w + NC - 1) / NC : 0) * spi;
+    bool ok = true;
+    for (int n = 0; n < steps; ++n) {
+      const int sidx = n % S;
+      if (n >= S && !mbar_wait(&empty[w * S + sidx], (uint32_t)((n / S) - 1) & 1u, a.err)) {
+        ok = false;
+        break;
+      }
+      const int item = n / spi, rem = n % spi, part = rem / ks, k = rem % ks;
+      const int wr = wr0 + w + NC * item;
+      const GemvSeg& s = seg_of(a, wr);
+      const uint8_t* src = (part ? s.w2 : s.w) + (size_t)(wr - s.wr_begin) * s.wr_bytes + (size_t)k * s.step_bytes;
+      mbar_arrive_expect_tx(&full[w * S + sidx], (uint32_t)s.step_bytes);
+      bulk_load(ring + (size_t)(w * S + sidx) * slot, src, (uint32_t)s.step_bytes, &full[w * S + sidx]);
+    }
+    // Leave only once every copy issued into this CTA's shared memory has
+    // landed (the consumers normally see to that; this covers their bail-out).
+    (void)ok;
+    for (int n = steps - S > 0 ? steps - S : 0; n < steps; ++n)
+      if (!mbar_wait(&full[w * S + n % S], (uint32_t)(n / S) & 1u, a.err)) return;
+    return;
+  }
+
+  // ---- consumers ----
+  pdl_wait();  // xq (and y for the residual add) come from earlier kernels
+  for (int b = threadIdx.x; b < nblk; b += NC * 32) {
     const uint32_t* src = reinterpret_cast<const uint32_t*>(a.xq + (size_t)b * 36);
-    const uint32_t hdr = __ldg(src);
+    const uint32_t hdr = src[0];
     uint32_t q[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) q[i] = __ldg(src + 1 + i);
+    for (int i = 0; i < 8; ++i) q[i] = src[1 + i];
     int s_lo = 0, s_hi = 0;
 #pragma unroll
     for (int i = 0; i < 4; ++i) s_lo = dp4a((int)q[i], 0x01010101, s_lo);
 #pragma unroll
     for (int i = 4; i < 8; ++i) s_hi = dp4a((int)q[i], 0x01010101, s_hi);
     const float d8 = f16_to_f32((uint16_t)(hdr & 0xffffu));
-    xd[b] = d8;
-    xds[b] = __fmul_rn(d8, (float)(s_lo + s_hi));
-    xs16[2 * b] = s_lo;
-    xs16[2 * b + 1] = s_hi;
-    const int sb = b >> 3, c = (b & 7) * 2;
+    const int sb = b >> 3, j = b & 7, c = j * 2;
+    xd[j * nb + sb] = d8;
+    xds[j * nb + sb] = __fmul_rn(d8, (float)(s_lo + s_hi));
+    xs16[c * nb + sb] = s_lo;
+    xs16[(c + 1) * nb + sb] = s_hi;
     xs[c * nb + sb] = make_uint4(q[0], q[1], q[2], q[3]);
     xs[(c + 1) * nb + sb] = make_uint4(q[4], q[5], q[6], q[7]);
   }
-  __syncthreads();
+  asm volatile("bar.sync 1, %0;" ::"r"(NC * 32) : "memory");
+  if (threadIdx.x == 0) pdl_launch_dependents();
   const XShared x{xs, xd, xds, xs16, nb};
 
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int tile = blockIdx.x; tile < a.total_tiles; tile += gridDim.x) {
-    GemvSeg s = a.seg[0];
-    if (a.nseg > 1 && tile >= a.seg[1].tile_begin) s = a.seg[1];
-    if (a.nseg > 2 && tile >= a.seg[2].tile_begin) s = a.seg[2];
-    const int lt = tile - s.tile_begin;
+  const int items = nwr > warp ? (nwr - warp + NC - 1) / NC : 0;
+  int n = 0;
+  for (int item = 0; item < items; ++item) {
+    const int wr = wr0 + warp + NC * item;
+    const GemvSeg s = seg_of(a, wr);
+    const int local = wr - s.wr_begin;
     const int row_in_warp = lane / s.lpr, lane_in_row = lane % s.lpr;
-    const int row = lt * (kGemvWarps * s.rpw) + warp * s.rpw + row_in_warp;
+    const int row = local * s.rpw + row_in_warp;
     int* dots = nullptr;
-    if (kDots) {
-      // only meaningful for single-segment launches (parity tests)
-      const int per_row = s.dtype == kQ6_K ? cols / 16 : cols / 32;
-      dots = a.dots + (size_t)(row < s.rows ? row : 0) * per_row;
+    if (kDots && row < s.rows) dots = a.dots + (size_t)row * (s.dtype == kQ6_K ? cols / 16 : cols / 32);
+    float acc[2] = {0.0f, 0.0f};
+    for (int part = 0; part < (swiglu ? 2 : 1); ++part) {
+      for (int k = 0; k < ks; ++k, ++n) {
+        const int sidx = n % S;
+        if (!mbar_wait(&full[warp * S + sidx], (uint32_t)(n / S) & 1u, a.err)) return;
+        const uint8_t* blk = ring + (size_t)(warp * S + sidx) * slot;
+        const float v =
+            step_value<kClass, kDots>(s.dtype, blk, lane, x, k * s.lpr + lane_in_row, part == 0 ? dots : nullptr);
+        acc[part] = __fadd_rn(acc[part], v);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[warp * S + sidx]);
+      }
     }
-    const uint8_t* tb = s.w + (size_t)lt * s.cta_tile_bytes;
-    float acc = seg_row_dot<kDots>(tb, s, warp, lane, lane_in_row, x, (kDots && row < s.rows) ? dots : nullptr);
-    acc = reduce_row(acc, s.lpr);
-    if (s.epi == kEpiSwiglu) {
-      const uint8_t* tb2 = s.w2 + (size_t)lt * s.cta_tile_bytes;
-      float up = seg_row_dot<false>(tb2, s, warp, lane, lane_in_row, x, nullptr);
-      up = reduce_row(up, s.lpr);
-      if (lane_in_row == 0 && row < s.rows) s.y[row] = silu_mul_det(acc, up);
+    const float g = reduce_row(acc[0], s.lpr);
+    if (swiglu) {
+      const float u = reduce_row(acc[1], s.lpr);
+      if (lane_in_row == 0 && row < s.rows) s.y[row] = silu_mul_det(g, u);
     } else if (lane_in_row == 0 && row < s.rows) {
       if (s.epi == kEpiAdd)
-        s.y[row] = __fadd_rn(s.y[row], acc);
+        s.y[row] = __fadd_rn(s.y[row], g);
       else
-        s.y[row] = acc;
+        s.y[row] = g;
     }
   }
 }
@@ -262,6 +395,8 @@ __device__ __forceinline__ void quant_block_warp(float v, uint8_t* dst, int lane
 }
 
 __global__ void k_quantize_q8_1(const float* __restrict__ x, int n, uint8_t* __restrict__ xq) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int warps = (blockDim.x >> 5) * gridDim.x;
   const int lane = threadIdx.x & 31;
   for (int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); b < n / 32; b += warps)
@@ -278,6 +413,8 @@ __global__ void __launch_bounds__(256) k_rmsnorm_q8_1(const float* __restrict__ 
   __shared__ float part[256];
   __shared__ float inv_s;
   const int t = threadIdx.x;
+  pdl_wait();
+  pdl_launch_dependents();
   float p = 0.0f;
   for (int i = t; i < n; i += 256) p = __fadd_rn(p, __fmul_rn(x[i], x[i]));
   part[t] = p;
@@ -314,6 +451,8 @@ __global__ void k_dense_gemv(const void* __restrict__ w, int dtype, int rows, in
                              float* __restrict__ y) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
+  pdl_wait();
+  pdl_launch_dependents();
   if (warp >= rows) return;
   float acc = 0.0f;
   if (dtype == kF32) {
@@ -332,56 +471,99 @@ __global__ void k_dense_gemv(const void* __restrict__ w, int dtype, int rows, in
 
 }  // namespace
 
-size_t gemv_smem_bytes(int cols) { return (size_t)cols + (size_t)(cols / 32) * 8 + (size_t)(cols / 16) * 4; }
+namespace {
+constexpr size_t kGemvSmemBudget = 220 * 1024;
 
-cudaError_t launch_gemv(GemvArgs& a, int grid, cudaStream_t st) {
-  int tiles = 0;
+// Tuning overrides (MCPO_GEMV_STAGES: ring slots per consumer warp,
+// MCPO_GEMV_CONSUMERS: consumer warps per CTA); read once.
+int env_int(const char* name, int fallback) {
+  const char* v = getenv(name);
+  return (v && *v) ? atoi(v) : fallback;
+}
+int stages_cfg() {
+  static const int v = env_int("MCPO_GEMV_STAGES", 2);
+  return v;
+}
+int consumers_cfg() {
+  static const int v = env_int("MCPO_GEMV_CONSUMERS", 16);
+  return v;
+}
+
+template <int kClass, bool kDots>
+cudaError_t set_smem_attr() {
+  return cudaFuncSetAttribute(k_gemv<kClass, kDots>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+}
+
+template <int kClass>
+cudaError_t launch_class(const GemvArgs& a, int grid, int nc, size_t smem, cudaStream_t st, bool pdl) {
+  const dim3 block((nc + 1) * 32);
+  if (a.dots) return launch_k(k_gemv<kClass, true>, dim3(grid), block, smem, st, pdl, a);
+  return launch_k(k_gemv<kClass, false>, dim3(grid), block, smem, st, pdl, a);
+}
+}  // namespace
+
+cudaError_t gemv_init() {
+  cudaError_t e = cudaSuccess;
+  const cudaError_t r[] = {set_smem_attr<kClassQ4K, false>(), set_smem_attr<kClassQ4K, true>(),
+                           set_smem_attr<kClassQ6K, false>(), set_smem_attr<kClassQ6K, true>(),
+                           set_smem_attr<kClassQ80, false>(), set_smem_attr<kClassQ80, true>(),
+                           set_smem_attr<kClassQ4K6K, false>(), set_smem_attr<kClassQ4K6K, true>()};
+  for (cudaError_t x : r)
+    if (x != cudaSuccess) e = x;
+  return e;
+}
+
+cudaError_t launch_gemv(GemvArgs& a, int grid, cudaStream_t st, bool pdl) {
+  int wr = 0, slot = 0;
+  bool has4 = false, has6 = false, has8 = false;
   for (int i = 0; i < a.nseg; ++i) {
-    a.seg[i].tile_begin = tiles;
-    tiles += a.seg[i].n_tiles;
+    a.seg[i].wr_begin = wr;
+    wr += a.seg[i].n_wr;
+    slot = a.seg[i].step_bytes > slot ? a.seg[i].step_bytes : slot;
+    has4 |= a.seg[i].dtype == kQ4_K;
+    has6 |= a.seg[i].dtype == kQ6_K;
+    has8 |= a.seg[i].dtype == kQ8_0;
+    if (a.seg[i].ks != a.seg[0].ks || a.seg[i].lpr != a.seg[0].lpr) return cudaErrorInvalidValue;
   }
-  a.total_tiles = tiles;
-  if (tiles == 0) return cudaSuccess;
-  const size_t smem = gemv_smem_bytes(a.cols);
-  if (grid <= 0 || grid > tiles) grid = tiles;
-  if (a.dots)
-    k_gemv<true><<<grid, kGemvThreads, smem, st>>>(a);
-  else
-    k_gemv<false><<<grid, kGemvThreads, smem, st>>>(a);
-  return cudaGetLastError();
+  if (a.seg[0].epi == kEpiSwiglu && a.nseg != 1) return cudaErrorInvalidValue;
+  if (has8 && (has4 || has6)) return cudaErrorInvalidValue;  // no mixed Q8_0 kernel
+  a.total_wr = wr;
+  a.slot_bytes = slot;
+  const int stages = stages_cfg() < 1 ? 1 : stages_cfg();
+  a.stages = stages;
+  if (wr == 0) return cudaSuccess;
+  const size_t xb = gemv_x_bytes(a.cols);
+  const size_t per_warp = (size_t)stages * (slot + 16);
+  int nc = kGemvSmemBudget > xb ? (int)((kGemvSmemBudget - xb) / per_warp) : 0;
+  const int want = consumers_cfg() > kMaxConsumers ? kMaxConsumers : consumers_cfg();
+  nc = nc > want ? want : nc;
+  if (nc < 1) return cudaErrorInvalidValue;
+  const size_t smem = xb + (size_t)nc * stages * slot + (size_t)2 * nc * stages * 8;
+  if (grid <= 0 || grid > wr) grid = wr;
+  if (has4 && has6) return launch_class<kClassQ4K6K>(a, grid, nc, smem, st, pdl);
+  if (has6) return launch_class<kClassQ6K>(a, grid, nc, smem, st, pdl);
+  if (has8) return launch_class<kClassQ80>(a, grid, nc, smem, st, pdl);
+  return launch_class<kClassQ4K>(a, grid, nc, smem, st, pdl);
 }
 
-int gemv_occupancy(int cols) {
-  const size_t smem = gemv_smem_bytes(cols);
-  if (smem > 48 * 1024) {
-    cudaFuncSetAttribute(k_gemv<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    cudaFuncSetAttribute(k_gemv<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  }
-  int n = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_gemv<false>, kGemvThreads, smem) != cudaSuccess) n = 1;
-  return n > 0 ? n : 1;
-}
-
-cudaError_t launch_quantize_q8_1(const float* x, int n, uint8_t* xq, cudaStream_t st) {
+cudaError_t launch_quantize_q8_1(const float* x, int n, uint8_t* xq, cudaStream_t st, bool pdl) {
   const int blocks = n / 32;
   const int grid = (blocks + 7) / 8;
-  k_quantize_q8_1<<<grid, 256, 0, st>>>(x, n, xq);
-  return cudaGetLastError();
+  return launch_k(k_quantize_q8_1, dim3(grid), dim3(256), 0, st, pdl, x, n, xq);
 }
 
 cudaError_t launch_rmsnorm_q8_1(const float* x, const void* w, int w_dtype, int n, float eps, float* out, uint8_t* xq,
-                                cudaStream_t st) {
+                                cudaStream_t st, bool pdl) {
   const int blocks = (n + 31) / 32;
   int grid = (blocks + 7) / 8;
   if (grid > 32) grid = 32;
-  k_rmsnorm_q8_1<<<grid, 256, 0, st>>>(x, w, w_dtype, n, eps, out, xq);
-  return cudaGetLastError();
+  return launch_k(k_rmsnorm_q8_1, dim3(grid), dim3(256), 0, st, pdl, x, w, w_dtype, n, eps, out, xq);
 }
 
-cudaError_t launch_dense_gemv(const void* w, int dtype, int rows, int cols, const float* x, float* y, cudaStream_t st) {
+cudaError_t launch_dense_gemv(const void* w, int dtype, int rows, int cols, const float* x, float* y, cudaStream_t st,
+                              bool pdl) {
   const int grid = (rows * 32 + 255) / 256;
-  k_dense_gemv<<<grid, 256, 0, st>>>(w, dtype, rows, cols, x, y);
-  return cudaGetLastError();
+  return launch_k(k_dense_gemv, dim3(grid), dim3(256), 0, st, pdl, w, dtype, rows, cols, x, y);
 }
 
 }  // namespace mcpo

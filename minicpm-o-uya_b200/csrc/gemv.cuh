@@ -23,21 +23,26 @@ struct GemvSeg {
   int rows;
   int lpr, rpw, ks;
   int step_bytes;
-  int tile_begin;     // first CTA tile of this segment in the launch's tile space
-  int n_tiles;
+  int n_wr;           // warp-rows
+  int wr_begin;       // first warp-row of this segment in the launch's warp-row space
   int epi;
-  size_t cta_tile_bytes;
+  size_t wr_bytes;
 };
 
 constexpr int kMaxSegs = 3;
 
+// All segments of one launch share the input width `cols` (hence lpr/ks);
+// a kEpiSwiglu launch has exactly one segment.
 struct GemvArgs {
   GemvSeg seg[kMaxSegs];
   int nseg;
   int cols;
-  int total_tiles;
+  int total_wr;
+  int stages;         // ring slots per consumer warp
+  int slot_bytes;     // max step block bytes over the segments
   const uint8_t* xq;  // Q8_1 activations, cols/32 blocks of 36 B
   int* dots;          // optional: per-block integer dots, [row][block] (parity tests)
+  int* err;           // set to 1 when a bounded wait gives up
 };
 
 // Fills seg from a tile geometry.
@@ -52,29 +57,46 @@ inline void gemv_seg_from_geom(const TileGeom& g, const uint8_t* w, const uint8_
   s->rpw = g.rpw;
   s->ks = g.ks;
   s->step_bytes = g.step_bytes;
-  s->n_tiles = g.n_cta_tiles;
+  s->n_wr = g.n_wr;
+  s->wr_begin = 0;
   s->epi = epi;
-  s->cta_tile_bytes = g.cta_tile_bytes;
-  s->tile_begin = 0;
+  s->wr_bytes = g.wr_bytes;
 }
 
-size_t gemv_smem_bytes(int cols);
-// CTAs of the GEMV kernel resident per SM for this input width (also opts the
-// kernel into the dynamic shared memory it needs; call before launching).
-int gemv_occupancy(int cols);
-cudaError_t launch_gemv(GemvArgs& a, int grid, cudaStream_t st);
+// One-time per-device setup (opts the GEMV kernels into large shared memory).
+cudaError_t gemv_init();
+// Launches over `grid` persistent CTAs (one per SM); fills wr_begin, total_wr,
+// stages and slot_bytes.  pdl: allow programmatic dependent launch.
+cudaError_t launch_gemv(GemvArgs& a, int grid, cudaStream_t st, bool pdl);
 
 // Q8_1 producers (36-byte blocks in the reference layout, gpu_shim.c:37-41).
 // x f32 [n] -> xq
-cudaError_t launch_quantize_q8_1(const float* x, int n, uint8_t* xq, cudaStream_t st);
+cudaError_t launch_quantize_q8_1(const float* x, int n, uint8_t* xq, cudaStream_t st, bool pdl = false);
 // RMSNorm(x) * w -> (optional f32 out) -> xq.  eps as given; reduction order
 // of gpu_shim.c:694-718 (256 strided partial sums, halving tree), exact
 // 1/sqrtf.  xq may be null (plain RMSNorm).
 cudaError_t launch_rmsnorm_q8_1(const float* x, const void* w, int w_dtype, int n, float eps, float* out,
-                                uint8_t* xq, cudaStream_t st);
+                                uint8_t* xq, cudaStream_t st, bool pdl = false);
 
 // Dense F32/F16/BF16 GEMV (row-major GGUF layout), f32 activations.
 cudaError_t launch_dense_gemv(const void* w, int dtype, int rows, int cols, const float* x, float* y,
-                              cudaStream_t st);
+                              cudaStream_t st, bool pdl = false);
+
+// Launch helper: programmatic dependent launch attribute when pdl is set.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
+                     Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
 
 }  // namespace mcpo

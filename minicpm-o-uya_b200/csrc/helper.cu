@@ -74,6 +74,8 @@ struct Model {
   int history_cap = 0;
   int grid_h = 1, grid_q = 1, grid_f = 1;
   cudaGraphExec_t exec[2] = {nullptr, nullptr};
+  int kernels[2] = {0, 0};  // kernel launches recorded in each graph
+  int* rec_count = nullptr;
 };
 
 struct Ctx {
@@ -123,6 +125,7 @@ struct Ctx {
   uint32_t* am_seen = nullptr;
   size_t am_seen_bytes = 0;
   std::unique_ptr<Model> model;
+  int* dev_err = nullptr;  // raised by a device-side bounded wait that gave up
   minicpmo_gpu_stats stats{};
   char last_error[512] = {0};
 };
@@ -289,10 +292,10 @@ int gemv_quant(Ctx* c, Upload** ups, float** ys, int n, const uint8_t* xq, int c
   a.cols = cols;
   a.xq = xq;
   a.dots = dots;
+  a.err = c->dev_err;
   for (int i = 0; i < n; ++i)
     gemv_seg_from_geom(ups[i]->geom, ups[i]->dev, up2 ? up2->dev : nullptr, ys[i], i == 0 ? epi : kEpiStore, &a.seg[i]);
-  const int grid = c->sm_count * gemv_occupancy(cols);
-  return cuda_ok(c, launch_gemv(a, grid, c->stream), "launch_quant_matvec", err, cap) ? 1 : 0;
+  return cuda_ok(c, launch_gemv(a, c->sm_count, c->stream, false), "launch_quant_matvec", err, cap) ? 1 : 0;
 }
 
 bool ensure_xq(Ctx* c, size_t cols, char* err, size_t cap) {
@@ -368,52 +371,56 @@ void free_model(Model* m) {
 
 // y (+)= W.x for one matrix of the model; quantised weights read xq,
 // dense ones the f32 input x.
-cudaError_t model_mv(Ctx* c, Upload* w, const float* x, const uint8_t* xq, float* y, int epi, float* tmp, int grid) {
+cudaError_t model_mv(Ctx* c, Upload* w, const float* x, const uint8_t* xq, float* y, int epi, float* tmp, int grid,
+                     int* err) {
   if (w->tiled) {
     GemvArgs a{};
     a.nseg = 1;
     a.cols = (int)w->cols;
     a.xq = xq;
+    a.err = err;
     gemv_seg_from_geom(w->geom, w->dev, nullptr, y, epi, &a.seg[0]);
-    return launch_gemv(a, grid, c->stream);
+    return launch_gemv(a, grid, c->stream, true);
   }
   if (epi == kEpiAdd) {
-    cudaError_t e = launch_dense_gemv(w->dev, w->dtype, (int)w->rows, (int)w->cols, x, tmp, c->stream);
+    cudaError_t e = launch_dense_gemv(w->dev, w->dtype, (int)w->rows, (int)w->cols, x, tmp, c->stream, true);
     if (e != cudaSuccess) return e;
     return launch_add_inplace(y, tmp, (int)w->rows, c->stream);
   }
-  return launch_dense_gemv(w->dev, w->dtype, (int)w->rows, (int)w->cols, x, y, c->stream);
+  return launch_dense_gemv(w->dev, w->dtype, (int)w->rows, (int)w->cols, x, y, c->stream, true);
 }
 
 #define REC(expr)                            \
   do {                                       \
     cudaError_t e_ = (expr);                 \
     if (e_ != cudaSuccess) return e_;        \
+    if (m.rec_count) ++*m.rec_count;         \
   } while (0)
 
 cudaError_t record_step(Ctx* c, Model& m, bool logits) {
   const auto& cf = m.cfg;
   const int h = (int)cf.hidden, f = (int)cf.ffn, hd = (int)cf.head_dim;
   const cudaStream_t s = c->stream;
-  REC(launch_embed(m.tok->dev, m.tok->geom, m.tok->dtype, (int)m.tok->rows, h, &m.st->token, 0, m.hidden, s));
-  REC(launch_mark_seen(m.seen, m.st, (int)cf.vocab, s));
+  REC(launch_embed(m.tok->dev, m.tok->geom, m.tok->dtype, (int)m.tok->rows, h, &m.st->token, 0, m.hidden, s, true));
+  REC(launch_mark_seen(m.seen, m.st, (int)cf.vocab, s, true));
   for (uint32_t li = 0; li < cf.layers; ++li) {
     const LayerW& L = m.layer[li];
     // attention block
-    REC(launch_rmsnorm_q8_1(m.hidden, L.attn_norm->dev, L.attn_norm->dtype, h, cf.rms_eps, m.normed, m.xq, s));
+    REC(launch_rmsnorm_q8_1(m.hidden, L.attn_norm->dev, L.attn_norm->dtype, h, cf.rms_eps, m.normed, m.xq, s, true));
     if (L.q->tiled && L.k->tiled && L.v->tiled) {
       Upload* ups[3] = {L.q, L.k, L.v};
       GemvArgs a{};
       a.nseg = 3;
       a.cols = h;
       a.xq = m.xq;
+      a.err = &m.st->err;
       float* ys[3] = {m.q, m.k, m.v};
       for (int i = 0; i < 3; ++i) gemv_seg_from_geom(ups[i]->geom, ups[i]->dev, nullptr, ys[i], kEpiStore, &a.seg[i]);
-      REC(launch_gemv(a, m.grid_h, s));
+      REC(launch_gemv(a, m.grid_h, s, true));
     } else {
-      REC(model_mv(c, L.q, m.normed, m.xq, m.q, kEpiStore, m.tmp, m.grid_h));
-      REC(model_mv(c, L.k, m.normed, m.xq, m.k, kEpiStore, m.tmp, m.grid_h));
-      REC(model_mv(c, L.v, m.normed, m.xq, m.v, kEpiStore, m.tmp, m.grid_h));
+      REC(model_mv(c, L.q, m.normed, m.xq, m.q, kEpiStore, m.tmp, m.grid_h, &m.st->err));
+      REC(model_mv(c, L.k, m.normed, m.xq, m.k, kEpiStore, m.tmp, m.grid_h, &m.st->err));
+      REC(model_mv(c, L.v, m.normed, m.xq, m.v, kEpiStore, m.tmp, m.grid_h, &m.st->err));
     }
     AttnArgs a{};
     a.q = m.q;
@@ -443,31 +450,32 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
     a.counters = m.counters;
     a.out = m.attn;
     a.out_q8 = (L.o->tiled && hd % 32 == 0) ? m.aq : nullptr;
-    REC(launch_attention(a, s));
-    if (L.o->tiled && hd % 32 != 0) REC(launch_quantize_q8_1(m.attn, (int)m.qd, m.aq, s));
-    REC(model_mv(c, L.o, m.attn, m.aq, m.hidden, kEpiAdd, m.tmp, m.grid_q));
+    REC(launch_attention(a, s, true));
+    if (L.o->tiled && hd % 32 != 0) REC(launch_quantize_q8_1(m.attn, (int)m.qd, m.aq, s, true));
+    REC(model_mv(c, L.o, m.attn, m.aq, m.hidden, kEpiAdd, m.tmp, m.grid_q, &m.st->err));
     // feed-forward block
-    REC(launch_rmsnorm_q8_1(m.hidden, L.ffn_norm->dev, L.ffn_norm->dtype, h, cf.rms_eps, m.normed, m.xq, s));
+    REC(launch_rmsnorm_q8_1(m.hidden, L.ffn_norm->dev, L.ffn_norm->dtype, h, cf.rms_eps, m.normed, m.xq, s, true));
     if (L.gate->tiled && L.up->tiled && L.gate->dtype == L.up->dtype && L.gate->rows == L.up->rows) {
       GemvArgs g{};
       g.nseg = 1;
       g.cols = h;
       g.xq = m.xq;
+      g.err = &m.st->err;
       gemv_seg_from_geom(L.gate->geom, L.gate->dev, L.up->dev, m.fused, kEpiSwiglu, &g.seg[0]);
-      REC(launch_gemv(g, m.grid_h, s));
+      REC(launch_gemv(g, m.grid_h, s, true));
     } else {
-      REC(model_mv(c, L.gate, m.normed, m.xq, m.gate, kEpiStore, m.tmp, m.grid_h));
-      REC(model_mv(c, L.up, m.normed, m.xq, m.up, kEpiStore, m.tmp, m.grid_h));
+      REC(model_mv(c, L.gate, m.normed, m.xq, m.gate, kEpiStore, m.tmp, m.grid_h, &m.st->err));
+      REC(model_mv(c, L.up, m.normed, m.xq, m.up, kEpiStore, m.tmp, m.grid_h, &m.st->err));
       REC(launch_silu_mul(m.fused, m.gate, m.up, f, s));
     }
-    if (L.down->tiled) REC(launch_quantize_q8_1(m.fused, f, m.fq, s));
-    REC(model_mv(c, L.down, m.fused, m.fq, m.hidden, kEpiAdd, m.tmp, m.grid_f));
+    if (L.down->tiled) REC(launch_quantize_q8_1(m.fused, f, m.fq, s, true));
+    REC(model_mv(c, L.down, m.fused, m.fq, m.hidden, kEpiAdd, m.tmp, m.grid_f, &m.st->err));
   }
   if (logits) {
-    REC(launch_rmsnorm_q8_1(m.hidden, m.out_norm->dev, m.out_norm->dtype, h, cf.rms_eps, m.normed, m.xq, s));
-    REC(model_mv(c, m.out, m.normed, m.xq, m.logits, kEpiStore, m.tmp, m.grid_h));
+    REC(launch_rmsnorm_q8_1(m.hidden, m.out_norm->dev, m.out_norm->dtype, h, cf.rms_eps, m.normed, m.xq, s, true));
+    REC(model_mv(c, m.out, m.normed, m.xq, m.logits, kEpiStore, m.tmp, m.grid_h, &m.st->err));
     REC(launch_argmax(m.logits, (int)cf.vocab, m.seen, m.am_scratch, m.am_counter, m.st, m.history, m.history_cap,
-                      m.am_grid, s));
+                      m.am_grid, s, true));
   }
   return cudaSuccess;
 }
@@ -476,7 +484,10 @@ int build_graph(Ctx* c, Model& m, int which, char* err, size_t cap) {
   cudaGraph_t g = nullptr;
   if (!cuda_ok(c, cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal), "graph_begin_capture", err, cap))
     return 0;
+  m.kernels[which] = 0;
+  m.rec_count = &m.kernels[which];
   cudaError_t rec = record_step(c, m, which == 0);
+  m.rec_count = nullptr;
   cudaError_t end = cudaStreamEndCapture(c->stream, &g);
   if (rec != cudaSuccess) {
     if (g) cudaGraphDestroy(g);
@@ -624,9 +635,7 @@ int bind_model(Ctx* c, const minicpmo_qwen3_config* cfg, char* err, size_t cap) 
     free_model(&m);
     return 0;
   }
-  m.grid_h = c->sm_count * gemv_occupancy((int)h);
-  m.grid_q = c->sm_count * gemv_occupancy((int)m.qd);
-  m.grid_f = c->sm_count * gemv_occupancy((int)f);
+  m.grid_h = m.grid_q = m.grid_f = c->sm_count;  // persistent GEMV: one CTA per SM
   c->stats.kv_device_bytes = 2 * cf.layers * m.kv_layer_elems * esz;
   c->stats.host_to_device_bytes += 2 * n_rope * 4;
   if (!cuda_ok(c, cudaStreamSynchronize(c->stream), "qwen3_bind_sync", err, cap) || !build_graph(c, m, 0, err, cap) ||
@@ -691,6 +700,14 @@ int minicpmo_gpu_context_create(unsigned int device_index, int debug, void** out
     return 0;
   }
   c->own_stream = true;
+  if (!cuda_ok(c, gemv_init(), "gemv_init", error, error_cap) ||
+      !cuda_ok(c, cudaMalloc((void**)&c->dev_err, sizeof(int)), "error_word_malloc", error, error_cap) ||
+      !cuda_ok(c, cudaMemset(c->dev_err, 0, sizeof(int)), "error_word_memset", error, error_cap)) {
+    if (c->dev_err) cudaFree(c->dev_err);
+    cudaStreamDestroy(c->stream);
+    delete c;
+    return 0;
+  }
   c->stats.backend_init_us = now_us() - t0;
   if (debug)
     fprintf(stderr, "minicpmo-gpu: create device=%u cc=%d.%d sms=%d init_us=%llu\n", device_index, prop.major, prop.minor,
@@ -713,7 +730,7 @@ void minicpmo_gpu_context_destroy(void* handle) {
     for (auto& s : c->slots)
       if (s.ptr) cudaFree(s.ptr);
     void* bufs[] = {c->stage, c->xq, c->sx, c->sy, c->dots, c->k_cache, c->v_cache, c->attn_partial, c->attn_counters,
-                    c->rope_cos, c->rope_sin, c->am_scratch, c->am_counter, c->am_state, c->am_seen};
+                    c->rope_cos, c->rope_sin, c->am_scratch, c->am_counter, c->am_state, c->am_seen, c->dev_err};
     for (void* p : bufs)
       if (p) cudaFree(p);
     if (c->am_state_host) cudaFreeHost(c->am_state_host);
@@ -1487,7 +1504,7 @@ int minicpmo_gpu_context_time_matvec(void* handle, const void* host_ptr, size_t 
          cuda_ok(c, cudaMemcpyAsync(bufs[i], u->dev, u->dev_bytes, cudaMemcpyDeviceToDevice, c->stream), "time_copy", error,
                  error_cap);
   }
-  const int grid = c->sm_count * gemv_occupancy((int)in_dim);
+  const int grid = c->sm_count;
   cudaEvent_t e0, e1;
   cudaEventCreate(&e0);
   cudaEventCreate(&e1);
@@ -1496,8 +1513,9 @@ int minicpmo_gpu_context_time_matvec(void* handle, const void* host_ptr, size_t 
     a.nseg = 1;
     a.cols = (int)in_dim;
     a.xq = c->xq;
+    a.err = c->dev_err;
     gemv_seg_from_geom(u->geom, bufs[i % copies], nullptr, c->sy, kEpiStore, &a.seg[0]);
-    return launch_gemv(a, grid, c->stream);
+    return launch_gemv(a, grid, c->stream, false);
   };
   for (int i = 0; ok && i < 3; ++i) ok = cuda_ok(c, launch(i), "time_warmup", error, error_cap);
   if (ok) cudaEventRecord(e0, c->stream);
@@ -1512,6 +1530,12 @@ int minicpmo_gpu_context_time_matvec(void* handle, const void* host_ptr, size_t 
     if (bufs[i]) cudaFree(bufs[i]);
   if (ok && avg_us) *avg_us = ms * 1000.0f / (float)iters;
   return ok ? 1 : 0;
+}
+
+int minicpmo_gpu_context_qwen3_step_kernels(void* handle, int with_logits) {
+  Ctx* c = (Ctx*)handle;
+  if (!c || !c->model) return 0;
+  return c->model->kernels[with_logits ? 0 : 1];
 }
 
 size_t minicpmo_gpu_context_tensor_device_bytes(void* handle, const void* host_ptr) {

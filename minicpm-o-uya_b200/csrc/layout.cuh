@@ -12,15 +12,16 @@
 //   chunk: 16 B of an SB.  Q4_K: chunk 0 = {d, dmin, scales[12]}, chunks 1..8 =
 //     qs.  Q6_K: chunks 0..7 = ql, 8..11 = qh, 12 = sc, plus a 2-byte d.
 //     Q8_0: chunk 0 = the 8 f16 d's, chunks 1..16 = the 256 int8 quants.
-//   lane tile: a warp processes RPW rows at a time, LPR lanes per row
+//   warp-row: a warp processes RPW rows at a time, LPR lanes per row
 //     (LPR = the largest power of two <= 32 dividing nb = cols/256); lane
 //     l covers row l/LPR and, at step k, SB k*LPR + l%LPR.  KS = nb/LPR steps.
 //   step block: for one step k, the chunks of all 32 lanes, chunk-major:
-//     [chunk c][lane] x 16 B (+ [lane] x 2 B of Q6_K d) = 32 * SB bytes.
-//   CTA tile: kGemvWarps warps x RPW rows, stored [step k][warp][step block],
-//     so one CTA tile is one contiguous range and each (k, warp) step block
-//     is 32 * SB contiguous bytes: every warp load is a fully coalesced 512 B.
-//   Rows are padded with zero bytes up to a whole number of CTA tiles.
+//     [chunk c][lane] x 16 B (+ [lane] x 2 B of Q6_K d) = 32 * SB bytes, so a
+//     warp reading one chunk reads 512 contiguous bytes.
+//   Warp-rows are stored one after another, each as its KS step blocks in
+//   order: a range of warp-rows is one contiguous byte range, and one step
+//   block is one 16-byte aligned bulk copy.
+//   Rows are padded with zero bytes up to a whole number of warp-rows.
 #pragma once
 
 #include <stddef.h>
@@ -39,10 +40,9 @@ struct TileGeom {
   int ks;        // steps per lane tile
   int sb_bytes;  // bytes per super-block
   int chunks;    // 16-byte chunks per super-block (excluding Q6_K's d)
-  int step_bytes;        // 32 * sb_bytes
-  int cta_rows;          // kGemvWarps * rpw
-  int n_cta_tiles;
-  size_t cta_tile_bytes; // ks * kGemvWarps * step_bytes
+  int step_bytes;   // 32 * sb_bytes
+  int n_wr;         // warp-rows, ceil(rows / rpw)
+  size_t wr_bytes;  // ks * step_bytes
   size_t total_bytes;
 };
 
@@ -84,23 +84,20 @@ __host__ __device__ inline bool make_geom(int dtype, int rows, int cols, TileGeo
   g->sb_bytes = sb_bytes_of(dtype);
   g->chunks = chunks_of(dtype);
   g->step_bytes = 32 * g->sb_bytes;
-  g->cta_rows = kGemvWarps * g->rpw;
-  g->n_cta_tiles = (rows + g->cta_rows - 1) / g->cta_rows;
-  g->cta_tile_bytes = (size_t)g->ks * kGemvWarps * g->step_bytes;
-  g->total_bytes = (size_t)g->n_cta_tiles * g->cta_tile_bytes;
+  g->n_wr = (rows + g->rpw - 1) / g->rpw;
+  g->wr_bytes = (size_t)g->ks * g->step_bytes;
+  g->total_bytes = (size_t)g->n_wr * g->wr_bytes;
   return true;
 }
 
 // Byte offset, inside the tiled buffer, of the step block holding SB `sb` of
 // row `row`, and the lane that owns it.
 __host__ __device__ inline size_t step_block_offset(const TileGeom& g, int row, int sb, int* lane) {
-  int tile = row / g.cta_rows;
-  int rr = row % g.cta_rows;
-  int warp = rr / g.rpw;
-  int riw = rr % g.rpw;
-  int k = sb / g.lpr;
+  const int wr = row / g.rpw;
+  const int riw = row % g.rpw;
+  const int k = sb / g.lpr;
   *lane = riw * g.lpr + sb % g.lpr;
-  return (size_t)tile * g.cta_tile_bytes + ((size_t)k * kGemvWarps + warp) * g.step_bytes;
+  return (size_t)wr * g.wr_bytes + (size_t)k * g.step_bytes;
 }
 
 // Address of byte `o` (0 <= o < sb_bytes, in GGUF SB order) of SB `sb` of

@@ -5,7 +5,9 @@
 
 #include <math.h>
 
+#include "gemv.cuh"
 #include "rowops.cuh"
+#include "tma.cuh"
 
 namespace mcpo {
 
@@ -68,6 +70,8 @@ __device__ __forceinline__ uint8_t tb(const uint8_t* w, const TileGeom& g, int r
 
 __global__ void k_embed(const uint8_t* __restrict__ w, TileGeom g, int dtype, int rows, int hidden, const int* tok_ptr,
                         int tok_static, float* __restrict__ out) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int token = tok_ptr ? *tok_ptr : tok_static;
   if (token < 0 || token >= rows) {  // never index outside the table; the host validates ids
     for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < hidden; e += gridDim.x * blockDim.x) out[e] = 0.0f;
@@ -159,6 +163,8 @@ __device__ __forceinline__ Top2 warp_merge(Top2 t) {
 __global__ void __launch_bounds__(256) k_argmax(const float* __restrict__ logits, int n, const uint32_t* seen_bits,
                                                 float* scratch, unsigned* counter, StepState* st, int* history,
                                                 int history_cap) {
+  pdl_wait();
+  pdl_launch_dependents();
   const float penalty = st->penalty;
   Top2 t{-INFINITY, 0x7fffffff, -INFINITY};
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
@@ -217,6 +223,8 @@ __global__ void __launch_bounds__(256) k_argmax(const float* __restrict__ logits
 }
 
 __global__ void k_mark_seen(uint32_t* bits, const StepState* st, int vocab) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int t = st->token;
   if (t >= 0 && t < vocab) atomicOr(&bits[t >> 5], 1u << (t & 31));
 }
@@ -261,22 +269,20 @@ cudaError_t launch_relayout(const uint8_t* src, uint8_t* dst, const TileGeom& g,
 }
 
 cudaError_t launch_embed(const uint8_t* w, const TileGeom& g, int dtype, int rows, int hidden, const int* tok_ptr, int tok,
-                         float* out, cudaStream_t st) {
+                         float* out, cudaStream_t st, bool pdl) {
   const int grid = (hidden + 255) / 256;
-  k_embed<<<grid, 256, 0, st>>>(w, g, dtype, rows, hidden, tok_ptr, tok, out);
-  return cudaGetLastError();
+  return launch_k(k_embed, dim3(grid), dim3(256), 0, st, pdl, w, g, dtype, rows, hidden, tok_ptr, tok, out);
 }
 
 cudaError_t launch_argmax(const float* logits, int n, const uint32_t* seen_bits, float* scratch, unsigned* counter,
-                          StepState* st, int* history, int history_cap, int grid, cudaStream_t s) {
+                          StepState* st, int* history, int history_cap, int grid, cudaStream_t s, bool pdl) {
   if (grid <= 0) grid = 1;
-  k_argmax<<<grid, 256, 0, s>>>(logits, n, seen_bits, scratch, counter, st, history, history_cap);
-  return cudaGetLastError();
+  return launch_k(k_argmax, dim3(grid), dim3(256), 0, s, pdl, logits, n, seen_bits, scratch, counter, st, history,
+                  history_cap);
 }
 
-cudaError_t launch_mark_seen(uint32_t* bits, const StepState* st, int vocab, cudaStream_t s) {
-  k_mark_seen<<<1, 1, 0, s>>>(bits, st, vocab);
-  return cudaGetLastError();
+cudaError_t launch_mark_seen(uint32_t* bits, const StepState* st, int vocab, cudaStream_t s, bool pdl) {
+  return launch_k(k_mark_seen, dim3(1), dim3(32), 0, s, pdl, bits, st, vocab);
 }
 
 cudaError_t launch_add_inplace(float* dst, const float* src, int n, cudaStream_t st) {

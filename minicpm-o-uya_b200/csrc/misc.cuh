@@ -26,12 +26,12 @@ struct StepState {
 cudaError_t launch_relayout(const uint8_t* src, uint8_t* dst, const TileGeom& g, size_t row_bytes, cudaStream_t st);
 // token (from tok_ptr when non-null) outside [0, rows) yields zeros.
 cudaError_t launch_embed(const uint8_t* w, const TileGeom& g, int dtype, int rows, int hidden, const int* tok_ptr, int tok,
-                         float* out, cudaStream_t st);
+                         float* out, cudaStream_t st, bool pdl = false);
 // grid CTAs; scratch holds 3 floats per CTA; counter is zero at rest.
 // history (may be null) receives next_token at history_len when auto-advancing.
 cudaError_t launch_argmax(const float* logits, int n, const uint32_t* seen_bits, float* scratch, unsigned* counter,
-                          StepState* st, int* history, int history_cap, int grid, cudaStream_t s);
-cudaError_t launch_mark_seen(uint32_t* bits, const StepState* st, int vocab, cudaStream_t s);
+                          StepState* st, int* history, int history_cap, int grid, cudaStream_t s, bool pdl = false);
+cudaError_t launch_mark_seen(uint32_t* bits, const StepState* st, int vocab, cudaStream_t s, bool pdl = false);
 cudaError_t launch_add_inplace(float* dst, const float* src, int n, cudaStream_t st);
 cudaError_t launch_silu_mul(float* dst, const float* gate, const float* up, int n, cudaStream_t st);
 cudaError_t launch_head_norm_rope(float* vec, int n_head, int hd, const void* w, int w_dtype, int do_rope,

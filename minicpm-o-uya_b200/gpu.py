@@ -132,6 +132,7 @@ SIGNATURES = {
     "minicpmo_gpu_context_time_matvec": (i32, [vp, vp, sz, sz, i32, fptr] + E),
     "minicpmo_gpu_context_qwen3_time_decode": (i32, [vp, u32, sz, sz, fptr] + E),
     "minicpmo_gpu_context_tensor_device_bytes": (sz, [vp, vp]),
+    "minicpmo_gpu_context_qwen3_step_kernels": (i32, [vp, i32]),
 }
 
 
@@ -361,6 +362,9 @@ class GpuContext:
         us = f32()
         self._call("minicpmo_gpu_context_time_matvec", t.ptr, t.cols, t.rows, iters, C.byref(us))
         return float(us.value)
+
+    def qwen3_step_kernels(self, with_logits: bool = True) -> int:
+        return int(self.lib.minicpmo_gpu_context_qwen3_step_kernels(self.handle, int(with_logits)))
 
     def tensor_device_bytes(self, t: Tensor) -> int:
         return int(self.lib.minicpmo_gpu_context_tensor_device_bytes(self.handle, t.ptr))

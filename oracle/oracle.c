@@ -629,16 +629,19 @@ static float butterfly(float *v, int n) {
     return v[0];
 }
 
-/* one super-block (256 values) in the kernel's operation order */
+/* one super-block (256 values) in the kernel's operation order:
+ *  Q4_K: sum_d = fma(d8_j, float(sc_j*dot_j), sum_d), sum_m = fma(d8_j*sumq_j,
+ *        float(m_j), sum_m) over j = 0..7; value = fma(d, sum_d, -(dmin*sum_m))
+ *  Q6_K: per Q8_1 block b (groups 2b, 2b+1): sum = fma(d8_b,
+ *        float(sc_2b*dot_2b + sc_2b+1*dot_2b+1), sum); value = d*sum
+ *  Q8_0: sum = fma(d_w*d8_b, float(dot_b), sum) over b */
 static float sb_dev(int dtype, const uint8_t *row, size_t sb, const uint8_t *xq) {
-    int32_t q8s[8];
     float xd[8], xds[8];
     int j;
     for (j = 0; j < 8; ++j) {
         int i;
         int32_t s = 0;
         for (i = 0; i < 32; ++i) s += q8_1_q(xq, sb * 8 + j, i);
-        q8s[j] = s;
         xd[j] = q8_1_d(xq, sb * 8 + j);
         xds[j] = xd[j] * (float) s;
     }
@@ -657,31 +660,31 @@ static float sb_dev(int dtype, const uint8_t *row, size_t sb, const uint8_t *xq)
                 dlo += (b[16 + g * 32 + l] & 15) * q8_1_q(xq, sb * 8 + 2 * g, l);
                 dhi += (b[16 + g * 32 + l] >> 4) * q8_1_q(xq, sb * 8 + 2 * g + 1, l);
             }
-            {
-                float t0 = ((float) s0 * xd[2 * g]) * (float) dlo;
-                float t1 = ((float) s1 * xd[2 * g + 1]) * (float) dhi;
-                sum_d = sum_d + (t0 + t1);
-                sum_m = sum_m + ((float) m0 * xds[2 * g] + (float) m1 * xds[2 * g + 1]);
-            }
+            sum_d = fmaf(xd[2 * g], (float) ((int32_t) s0 * dlo), sum_d);
+            sum_d = fmaf(xd[2 * g + 1], (float) ((int32_t) s1 * dhi), sum_d);
+            sum_m = fmaf(xds[2 * g], (float) m0, sum_m);
+            sum_m = fmaf(xds[2 * g + 1], (float) m1, sum_m);
         }
-        return d * sum_d - dmin * sum_m;
+        return fmaf(d, sum_d, -(dmin * sum_m));
     }
     if (dtype == ORC_Q6_K) {
         const uint8_t *b = row + sb * 210;
         float d = orc_f16_to_f32(rd16(b + 208)), sum = 0.0f;
-        int n, qq, h;
-        for (n = 0; n < 2; ++n)
-            for (qq = 0; qq < 4; ++qq)
-                for (h = 0; h < 2; ++h) {
-                    int g = 8 * n + 2 * qq + h, l;
-                    int32_t dd = 0;
-                    for (l = 0; l < 16; ++l) {
-                        int e = g * 16 + l;
-                        dd += q6k_value(b, e, NULL) * q8_1_q(xq, sb * 8 + e / 32, e % 32);
-                    }
-                    sum = sum + xd[g >> 1] * ((float) dd * (float) q6k_group_scale(b, g));
+        int blk;
+        for (blk = 0; blk < 8; ++blk) {
+            int32_t dd[2], h;
+            for (h = 0; h < 2; ++h) {
+                int g = 2 * blk + h, l;
+                int32_t acc = 0;
+                for (l = 0; l < 16; ++l) {
+                    int e = g * 16 + l;
+                    acc += q6k_value(b, e, NULL) * q8_1_q(xq, sb * 8 + e / 32, e % 32);
                 }
-        (void) q8s;
+                dd[h] = acc;
+            }
+            sum = fmaf(xd[blk], (float) (q6k_group_scale(b, 2 * blk) * dd[0] + q6k_group_scale(b, 2 * blk + 1) * dd[1]),
+                       sum);
+        }
         return d * sum;
     }
     {
@@ -692,7 +695,7 @@ static float sb_dev(int dtype, const uint8_t *row, size_t sb, const uint8_t *xq)
             int32_t dd = 0;
             int l;
             for (l = 0; l < 32; ++l) dd += (int8_t) b[2 + l] * q8_1_q(xq, sb * 8 + blk, l);
-            sum = sum + (orc_f16_to_f32(rd16(b)) * xd[blk]) * (float) dd;
+            sum = fmaf(orc_f16_to_f32(rd16(b)) * xd[blk], (float) dd, sum);
         }
         return sum;
     }
