@@ -33,17 +33,23 @@ namespace mcpo {
 namespace {
 
 constexpr int kAttnWarps = 4;
-constexpr int kGMax = 8;
+constexpr int kGMax = 8;     // q heads per kv head handled by one CTA (<= 2 per warp)
+constexpr int kSub = 32;     // positions per sub-chunk (one per lane)
+constexpr int kMaxSplit = 64;
 
 struct AttnSmem {
-  float* q;     // [kGMax][HD]
-  float* kpos;  // [HD]
-  float* vpos;  // [HD]
+  float* q;     // [kGMax][hd]
+  float* kpos;  // [hd]
+  float* vpos;  // [hd]
   float* sq;    // [kAttnWarps][256]
-  float* rm;    // [kAttnWarps][kGMax]
-  float* rl;    // [kAttnWarps][kGMax]
-  float* racc;  // [kAttnWarps][kGMax][HD]
+  float* kt;    // [kSub][hd + 1]
+  float* vt;    // [kSub][hd + 1]
+  float* w;     // [kAttnWarps][kMaxSplit] combine weights
 };
+
+__host__ __device__ inline size_t attn_smem_floats(int hd) {
+  return (size_t)kGMax * hd + 2 * hd + kAttnWarps * 256 + 2 * (size_t)kSub * (hd + 1) + kAttnWarps * kMaxSplit;
+}
 
 __device__ __forceinline__ AttnSmem carve(float* base, int hd) {
   AttnSmem s;
@@ -51,9 +57,9 @@ __device__ __forceinline__ AttnSmem carve(float* base, int hd) {
   s.kpos = s.q + kGMax * hd;
   s.vpos = s.kpos + hd;
   s.sq = s.vpos + hd;
-  s.rm = s.sq + kAttnWarps * 256;
-  s.rl = s.rm + kAttnWarps * kGMax;
-  s.racc = s.rl + kAttnWarps * kGMax;
+  s.kt = s.sq + kAttnWarps * 256;
+  s.vt = s.kt + kSub * (hd + 1);
+  s.w = s.vt + kSub * (hd + 1);
   return s;
 }
 
@@ -73,11 +79,23 @@ __device__ __forceinline__ void kv_store(void* p, size_t i, float v) {
     reinterpret_cast<float*>(p)[i] = v;
 }
 
-// J = elements per lane (hd = 32*J), or J = 1 with hd <= 32 (masked).
+// J = output elements per lane in the P.V phase (hd = 32*J), or J = 1 with
+// hd <= 32 (masked lanes).
+//
+// Per q head and KV chunk, in order over sub-chunks of 32 positions
+// (lane = position):
+//   s_t   = scale * sum_d q_d k_td            (sequential fma over d)
+//   m'    = max(m, max_t s_t)
+//   alpha = exp(m - m'),  p_t = exp(s_t - m')  (0 beyond the chunk)
+//   l     = l*alpha + butterfly_sum(p)
+//   acc_d = acc_d*alpha, then acc_d = fma(p_t, v_td, acc_d) for t in order
+// and the splits are merged as o_d = (sum_s w_s acc_sd) / (sum_s w_s l_s),
+// w_s = exp(m_s - max m), sums in split order with fma.
 template <int J, typename T>
 __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a) {
   extern __shared__ __align__(16) float smem_f[];
   const int hd = a.head_dim;
+  const int hs = hd + 1;  // padded row stride (conflict-free column reads)
   const AttnSmem sm = carve(smem_f, hd);
   const int kvh = blockIdx.x, split = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -85,6 +103,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a)
   pdl_launch_dependents();
   const int hb = (kvh * a.n_head + a.n_kv - 1) / a.n_kv;
   const int he = ((kvh + 1) * a.n_head + a.n_kv - 1) / a.n_kv;
+  const int G = he - hb;
   const int pos = a.pos_ptr ? *a.pos_ptr : a.pos_static;
   const int n_pos = pos + 1;
   int chunk = (n_pos + a.n_split - 1) / a.n_split;
@@ -95,121 +114,104 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a)
   const int kv_dim = a.n_kv * hd;
   const size_t kv_off = (size_t)kvh * hd;
   const int stride_part = hd + 2;
+  const bool fused = a.fuse_norm_rope_append != 0;
 
   // K/V of the current position (fused: normalised/rotated here and appended).
-  if (a.fuse_norm_rope_append) {
+  if (fused) {
     if (warp == 0) {
       for (int d = lane; d < hd; d += 32) sm.kpos[d] = a.k[kv_off + d];
       __syncwarp();
-      norm_rope_row(sm.kpos, sm.sq, hd, a.k_norm, a.k_norm_dtype, true, a.rope_cos, a.rope_sin, a.rope_base, a.rope_scale,
-                    pos, lane);
+      norm_rope_row(sm.kpos, sm.sq, hd, a.k_norm, a.k_norm_dtype, true, a.rope_cos, a.rope_sin, a.rope_base,
+                    a.rope_scale, pos, lane);
     } else if (warp == 1) {
       for (int d = lane; d < hd; d += 32) sm.vpos[d] = a.v[kv_off + d];
     }
-    __syncthreads();
-    if (split == 0) {
-      for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-        kv_store<T>(a.k_cache, (size_t)pos * kv_dim + kv_off + d, sm.kpos[d]);
-        kv_store<T>(a.v_cache, (size_t)pos * kv_dim + kv_off + d, sm.vpos[d]);
-      }
+  }
+  // q rows of this kv head's group
+  for (int g = warp; g < G; g += kAttnWarps) {
+    float* row = sm.q + g * hd;
+    for (int d = lane; d < hd; d += 32) row[d] = a.q[(size_t)(hb + g) * hd + d];
+    __syncwarp();
+    if (fused)
+      norm_rope_row(row, sm.sq + warp * 256, hd, a.q_norm, a.q_norm_dtype, true, a.rope_cos, a.rope_sin, a.rope_base,
+                    a.rope_scale, pos, lane);
+  }
+  __syncthreads();
+  if (fused && split == 0) {
+    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+      kv_store<T>(a.k_cache, (size_t)pos * kv_dim + kv_off + d, sm.kpos[d]);
+      kv_store<T>(a.v_cache, (size_t)pos * kv_dim + kv_off + d, sm.vpos[d]);
     }
   }
 
-  for (int g0 = hb; g0 < he; g0 += kGMax) {
-    const int G = min(kGMax, he - g0);
-    // q rows of this head batch
-    for (int g = warp; g < G; g += kAttnWarps) {
-      float* row = sm.q + g * hd;
-      for (int d = lane; d < hd; d += 32) row[d] = a.q[(size_t)(g0 + g) * hd + d];
-      __syncwarp();
-      if (a.fuse_norm_rope_append)
-        norm_rope_row(row, sm.sq + warp * 256, hd, a.q_norm, a.q_norm_dtype, true, a.rope_cos, a.rope_sin, a.rope_base,
-                      a.rope_scale, pos, lane);
-    }
-    __syncthreads();
-
-    float m[kGMax], l[kGMax], acc[kGMax][J];
+  if (split < n_active) {
+    // up to two heads per warp (G <= 8)
+    float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.0f, 0.0f}, acc[2][J];
 #pragma unroll
-    for (int g = 0; g < kGMax; ++g) {
-      m[g] = -INFINITY;
-      l[g] = 0.0f;
+    for (int i = 0; i < 2; ++i)
 #pragma unroll
-      for (int j = 0; j < J; ++j) acc[g][j] = 0.0f;
-    }
-    // lane element mapping: d = lane*J + j (hd == 32*J) or d = lane (J == 1, hd <= 32)
-    const bool act = (lane * J) < hd;
-    float qv[kGMax][J];
-#pragma unroll
-    for (int g = 0; g < kGMax; ++g)
-#pragma unroll
-      for (int j = 0; j < J; ++j) qv[g][j] = (g < G && act) ? sm.q[g * hd + lane * J + j] : 0.0f;
-
-    if (split < n_active) {
-      for (int t = t0 + warp; t < t1; t += kAttnWarps) {
-        float kv[J], vv[J];
-        const bool cur = a.fuse_norm_rope_append && t == pos;
-        const size_t base = (size_t)t * kv_dim + kv_off + lane * J;
-#pragma unroll
-        for (int j = 0; j < J; ++j) {
-          kv[j] = act ? (cur ? sm.kpos[lane * J + j] : kv_load<T>(a.k_cache, base + j)) : 0.0f;
-          vv[j] = act ? (cur ? sm.vpos[lane * J + j] : kv_load<T>(a.v_cache, base + j)) : 0.0f;
-        }
-#pragma unroll
-        for (int g = 0; g < kGMax; ++g) {
-          if (g < G) {
-            float p = 0.0f;
-#pragma unroll
-            for (int j = 0; j < J; ++j) p = __fmaf_rn(qv[g][j], kv[j], p);
-            const float s = __fmul_rn(__shfl_sync(0xffffffffu, warp_sum(p), 0), a.scale);
-            const float mn = fmaxf(m[g], s);
-            const float alpha = expf_det(__fsub_rn(m[g], mn));  // m = -inf -> 0
-            const float beta = expf_det(__fsub_rn(s, mn));
-            l[g] = __fadd_rn(__fmul_rn(l[g], alpha), beta);
-            m[g] = mn;
-#pragma unroll
-            for (int j = 0; j < J; ++j) acc[g][j] = __fadd_rn(__fmul_rn(acc[g][j], alpha), __fmul_rn(beta, vv[j]));
+      for (int j = 0; j < J; ++j) acc[i][j] = 0.0f;
+    const bool act = lane * J < hd;
+    for (int c0 = t0; c0 < t1; c0 += kSub) {
+      // stage K and V rows of this sub-chunk (the current position from smem)
+      for (int e = threadIdx.x; e < kSub * hd; e += blockDim.x) {
+        const int r = e / hd, d = e - r * hd, t = c0 + r;
+        float kv = 0.0f, vv = 0.0f;
+        if (t < t1) {
+          if (fused && t == pos) {
+            kv = sm.kpos[d];
+            vv = sm.vpos[d];
+          } else {
+            const size_t i = (size_t)t * kv_dim + kv_off + d;
+            kv = kv_load<T>(a.k_cache, i);
+            vv = kv_load<T>(a.v_cache, i);
           }
         }
+        sm.kt[r * hs + d] = kv;
+        sm.vt[r * hs + d] = vv;
       }
-    }
-    // merge the warps of this CTA
+      __syncthreads();
+      const int t = c0 + lane;
+      const bool valid = t < t1;
 #pragma unroll
-    for (int g = 0; g < kGMax; ++g) {
-      if (g < G) {
-        if (lane == 0) {
-          sm.rm[warp * kGMax + g] = m[g];
-          sm.rl[warp * kGMax + g] = l[g];
-        }
-        if (act)
+      for (int i = 0; i < 2; ++i) {
+        const int g = warp + i * kAttnWarps;
+        if (g >= G) break;
+        const float* qrow = sm.q + g * hd;
+        float sc = 0.0f;
+        for (int d = 0; d < hd; ++d) sc = __fmaf_rn(qrow[d], sm.kt[lane * hs + d], sc);
+        sc = valid ? __fmul_rn(sc, a.scale) : -INFINITY;
+        const float mx = warp_max(sc);
+        const float mn = fmaxf(m[i], mx);
+        const float alpha = expf_det(__fsub_rn(m[i], mn));
+        const float p = valid ? expf_det(__fsub_rn(sc, mn)) : 0.0f;
+        const float psum = __shfl_sync(0xffffffffu, warp_sum(p), 0);
+        l[i] = __fadd_rn(__fmul_rn(l[i], alpha), psum);
+        m[i] = mn;
 #pragma unroll
-          for (int j = 0; j < J; ++j) sm.racc[(warp * kGMax + g) * hd + lane * J + j] = acc[g][j];
-      }
-    }
-    __syncthreads();
-    if (split < n_active) {
-      for (int g = warp; g < G; g += kAttnWarps) {
-        float M = -INFINITY;
-        for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, sm.rm[w * kGMax + g]);
-        float L = 0.0f;
-        float wt[kAttnWarps];
-        for (int w = 0; w < kAttnWarps; ++w) {
-          const float mw = sm.rm[w * kGMax + g];
-          wt[w] = mw == -INFINITY ? 0.0f : expf_det(__fsub_rn(mw, M));
-          L = __fadd_rn(L, __fmul_rn(wt[w], sm.rl[w * kGMax + g]));
-        }
-        float* dst = a.partial + ((size_t)(g0 + g) * a.n_split + split) * stride_part;
-        for (int d = lane; d < hd; d += 32) {
-          float s = 0.0f;
-          for (int w = 0; w < kAttnWarps; ++w) s = __fadd_rn(s, __fmul_rn(wt[w], sm.racc[(w * kGMax + g) * hd + d]));
-          dst[2 + d] = s;
-        }
-        if (lane == 0) {
-          dst[0] = M;
-          dst[1] = L;
+        for (int j = 0; j < J; ++j) acc[i][j] = __fmul_rn(acc[i][j], alpha);
+        for (int tt = 0; tt < kSub; ++tt) {
+          const float pt = __shfl_sync(0xffffffffu, p, tt);
+          if (act)
+#pragma unroll
+            for (int j = 0; j < J; ++j) acc[i][j] = __fmaf_rn(pt, sm.vt[tt * hs + lane * J + j], acc[i][j]);
         }
       }
+      __syncthreads();
     }
-    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int g = warp + i * kAttnWarps;
+      if (g >= G) break;
+      float* dst = a.partial + ((size_t)(hb + g) * a.n_split + split) * stride_part;
+      if (act)
+#pragma unroll
+        for (int j = 0; j < J; ++j) dst[2 + lane * J + j] = acc[i][j];
+      if (lane == 0) {
+        dst[0] = m[i];
+        dst[1] = l[i];
+      }
+    }
   }
 
   // last CTA of this kv head merges the splits
@@ -221,25 +223,22 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a)
   if (ticket_s != (unsigned)(a.n_split - 1)) return;
   if (threadIdx.x == 0) atomicExch(&a.counters[kvh], 0u);
   __threadfence();
+  float* wsm = sm.w + warp * kMaxSplit;
   for (int h = hb + warp; h < he; h += kAttnWarps) {
     const float* ph = a.partial + (size_t)h * a.n_split * stride_part;
     float M = -INFINITY;
-    for (int s = 0; s < n_active; ++s) M = fmaxf(M, __ldcg(ph + (size_t)s * stride_part));
+    for (int s = lane; s < n_active; s += 32) M = fmaxf(M, __ldcg(ph + (size_t)s * stride_part));
+    M = warp_max(M);
+    for (int s = lane; s < n_active; s += 32) wsm[s] = expf_det(__fsub_rn(__ldcg(ph + (size_t)s * stride_part), M));
+    __syncwarp();
     float L = 0.0f;
-    for (int s = 0; s < n_active; ++s) {
-      const float ms = __ldcg(ph + (size_t)s * stride_part);
-      if (ms != -INFINITY) L = __fadd_rn(L, __fmul_rn(expf_det(__fsub_rn(ms, M)), __ldcg(ph + (size_t)s * stride_part + 1)));
-    }
+    for (int s = 0; s < n_active; ++s) L = __fmaf_rn(wsm[s], __ldcg(ph + (size_t)s * stride_part + 1), L);
     const float invL = L > 0.0f ? __fdiv_rn(1.0f, L) : 0.0f;
     for (int d0 = 0; d0 < hd; d0 += 32) {
       const int d = d0 + lane;
       float o = 0.0f;
       if (d < hd) {
-        for (int s = 0; s < n_active; ++s) {
-          const float ms = __ldcg(ph + (size_t)s * stride_part);
-          if (ms != -INFINITY)
-            o = __fadd_rn(o, __fmul_rn(expf_det(__fsub_rn(ms, M)), __ldcg(ph + (size_t)s * stride_part + 2 + d)));
-        }
+        for (int s = 0; s < n_active; ++s) o = __fmaf_rn(wsm[s], __ldcg(ph + (size_t)s * stride_part + 2 + d), o);
         o = __fmul_rn(o, invL);
         a.out[(size_t)h * hd + d] = o;
       }
@@ -257,13 +256,11 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a)
         if ((lane & 3) == 0) ob[1 + (lane >> 2)] = word;
       }
     }
+    __syncwarp();
   }
 }
 
-size_t attn_smem_bytes(int hd) {
-  return sizeof(float) * ((size_t)kGMax * hd + 2 * hd + kAttnWarps * 256 + 2 * kAttnWarps * kGMax +
-                          (size_t)kAttnWarps * kGMax * hd);
-}
+size_t attn_smem_bytes(int hd) { return sizeof(float) * attn_smem_floats(hd); }
 
 template <int J>
 cudaError_t launch_j(const AttnArgs& a, cudaStream_t st, bool pdl) {
@@ -273,13 +270,31 @@ cudaError_t launch_j(const AttnArgs& a, cudaStream_t st, bool pdl) {
   return launch_k(k_attention<J, float>, grid, dim3(kAttnWarps * 32), smem, st, pdl, a);
 }
 
+template <int J>
+cudaError_t init_j() {
+  const int mx = (int)attn_smem_bytes(256);
+  cudaError_t e = cudaFuncSetAttribute(k_attention<J, __half>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(k_attention<J, float>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
+  return e;
+}
+
 }  // namespace
 
 size_t attn_partial_floats(int n_head, int n_split, int head_dim) {
   return (size_t)n_head * n_split * (head_dim + 2);
 }
 
+cudaError_t attention_init() {
+  cudaError_t e = init_j<1>();
+  if (e == cudaSuccess) e = init_j<2>();
+  if (e == cudaSuccess) e = init_j<4>();
+  if (e == cudaSuccess) e = init_j<8>();
+  return e;
+}
+
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st, bool pdl) {
+  if (a.n_split > kMaxSplit || a.n_split < 1) return cudaErrorInvalidValue;
+  if (a.n_head > kGMax * a.n_kv) return cudaErrorInvalidValue;
   switch (a.head_dim) {
     case 64: return launch_j<2>(a, st, pdl);
     case 128: return launch_j<4>(a, st, pdl);

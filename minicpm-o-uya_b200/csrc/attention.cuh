@@ -36,6 +36,8 @@ struct AttnArgs {
 };
 
 size_t attn_partial_floats(int n_head, int n_split, int head_dim);
+// One-time per-device setup (opts the kernels into their shared memory).
+cudaError_t attention_init();
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st, bool pdl = false);
 
 }  // namespace mcpo

@@ -701,6 +701,7 @@ int minicpmo_gpu_context_create(unsigned int device_index, int debug, void** out
   }
   c->own_stream = true;
   if (!cuda_ok(c, gemv_init(), "gemv_init", error, error_cap) ||
+      !cuda_ok(c, attention_init(), "attention_init", error, error_cap) ||
       !cuda_ok(c, cudaMalloc((void**)&c->dev_err, sizeof(int)), "error_word_malloc", error, error_cap) ||
       !cuda_ok(c, cudaMemset(c->dev_err, 0, sizeof(int)), "error_word_memset", error, error_cap)) {
     if (c->dev_err) cudaFree(c->dev_err);

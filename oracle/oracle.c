@@ -744,88 +744,88 @@ void orc_silu_mul_dev(float *dst, const float *gate, const float *up, size_t n) 
     for (i = 0; i < n; ++i) dst[i] = (gate[i] / (1.0f + orc_expf_det(-gate[i]))) * up[i];
 }
 
-#define ATT_WARPS 4
-
+/* Flash-decode order of the attention kernel: per q head, per KV chunk of
+ * max(32, ceil((pos+1)/splits)) positions, sub-chunks of 32 positions: scores
+ * by sequential fma over d; m' = max(m, max s); alpha = exp(m - m'); p_t =
+ * exp(s_t - m'); l = l*alpha + butterfly(p); acc_d = acc_d*alpha then fma(p_t,
+ * v_td, acc_d) in t order.  Chunks merged as (sum_s w_s acc_s) * (1 / sum_s
+ * w_s l_s), w_s = exp(m_s - max m), fma in split order. */
 int orc_attention_dev(float *out, const float *q, const float *k_cache, const float *v_cache, const float *cur_k,
                       const float *cur_v, size_t layer, size_t pos, size_t head_count, size_t kv_head_count,
                       size_t head_dim, size_t context) {
     const size_t hd = head_dim, kv_dim = kv_head_count * hd;
     const int n_split = orc_attn_n_split((int) kv_head_count);
-    const int J = hd <= 32 ? 1 : (int) (hd / 32);
     const float scale = 1.0f / sqrtf((float) hd);
     const size_t n_pos = pos + 1;
     size_t chunk = (n_pos + (size_t) n_split - 1) / (size_t) n_split;
     size_t n_active, kvh;
-    float *pm, *pl, *pacc;
+    float *pm, *pl, *pacc, *acc;
     if (!(hd == 64 || hd == 128 || hd == 256 || hd <= 32)) return 0;
     if (chunk < 32) chunk = 32;
     n_active = (n_pos + chunk - 1) / chunk;
     pm = (float *) malloc(n_active * sizeof(float));
     pl = (float *) malloc(n_active * sizeof(float));
     pacc = (float *) malloc(n_active * hd * sizeof(float));
-    if (!pm || !pl || !pacc) { free(pm); free(pl); free(pacc); return 0; }
+    acc = (float *) malloc(hd * sizeof(float));
+    if (!pm || !pl || !pacc || !acc) { free(pm); free(pl); free(pacc); free(acc); return 0; }
     for (kvh = 0; kvh < kv_head_count; ++kvh) {
         size_t hb = (kvh * head_count + kv_head_count - 1) / kv_head_count;
         size_t he = ((kvh + 1) * head_count + kv_head_count - 1) / kv_head_count, h;
         for (h = hb; h < he; ++h) {
             const float *qh = q + h * hd;
-            size_t s;
+            size_t s, d;
             for (s = 0; s < n_active; ++s) {
                 const size_t t0 = s * chunk, t1 = t0 + chunk < n_pos ? t0 + chunk : n_pos;
-                float wm[ATT_WARPS], wl[ATT_WARPS], *wacc = (float *) calloc((size_t) ATT_WARPS * hd, sizeof(float));
-                float M = -INFINITY, L = 0.0f, wt[ATT_WARPS];
-                int w;
-                size_t d;
-                for (w = 0; w < ATT_WARPS; ++w) {
-                    size_t t;
-                    wm[w] = -INFINITY;
-                    wl[w] = 0.0f;
-                    for (t = t0 + (size_t) w; t < t1; t += ATT_WARPS) {
-                        const int cur = t == pos;
-                        const float *krow = cur ? cur_k + kvh * hd : k_cache + (layer * context + t) * kv_dim + kvh * hd;
-                        const float *vrow = cur ? cur_v + kvh * hd : v_cache + (layer * context + t) * kv_dim + kvh * hd;
-                        float lanes[32], sc, mn, alpha, beta;
-                        int ln, j;
-                        for (ln = 0; ln < 32; ++ln) {
-                            float p = 0.0f;
-                            if ((size_t) (ln * J) < hd)
-                                for (j = 0; j < J; ++j) p = fmaf(qh[ln * J + j], krow[ln * J + j], p);
-                            lanes[ln] = p;
+                float m = -INFINITY, l = 0.0f;
+                size_t c0;
+                for (d = 0; d < hd; ++d) acc[d] = 0.0f;
+                for (c0 = t0; c0 < t1; c0 += 32) {
+                    float sc[32], p[32], tmp[32], mx = -INFINITY, mn, alpha, psum;
+                    const float *vrow[32];
+                    int ln;
+                    for (ln = 0; ln < 32; ++ln) {
+                        const size_t t = c0 + (size_t) ln;
+                        vrow[ln] = NULL;
+                        if (t < t1) {
+                            const int cur = t == pos;
+                            const float *krow = cur ? cur_k + kvh * hd : k_cache + (layer * context + t) * kv_dim + kvh * hd;
+                            float dot = 0.0f;
+                            vrow[ln] = cur ? cur_v + kvh * hd : v_cache + (layer * context + t) * kv_dim + kvh * hd;
+                            for (d = 0; d < hd; ++d) dot = fmaf(qh[d], krow[d], dot);
+                            sc[ln] = dot * scale;
+                        } else {
+                            sc[ln] = -INFINITY;
                         }
-                        sc = butterfly(lanes, 32) * scale;
-                        mn = wm[w] > sc ? wm[w] : sc;
-                        alpha = orc_expf_det(wm[w] - mn);
-                        beta = orc_expf_det(sc - mn);
-                        wl[w] = wl[w] * alpha + beta;
-                        wm[w] = mn;
-                        for (d = 0; d < hd; ++d) wacc[w * hd + d] = wacc[w * hd + d] * alpha + beta * vrow[d];
+                        mx = fmaxf(mx, sc[ln]);
                     }
+                    mn = fmaxf(m, mx);
+                    alpha = orc_expf_det(m - mn);
+                    for (ln = 0; ln < 32; ++ln) {
+                        p[ln] = vrow[ln] ? orc_expf_det(sc[ln] - mn) : 0.0f;
+                        tmp[ln] = p[ln];
+                    }
+                    psum = butterfly(tmp, 32);
+                    l = l * alpha + psum;
+                    for (d = 0; d < hd; ++d) {
+                        float a = acc[d] * alpha;
+                        for (ln = 0; ln < 32; ++ln) a = fmaf(p[ln], vrow[ln] ? vrow[ln][d] : 0.0f, a);
+                        acc[d] = a;
+                    }
+                    m = mn;
                 }
-                for (w = 0; w < ATT_WARPS; ++w) M = fmaxf(M, wm[w]);
-                for (w = 0; w < ATT_WARPS; ++w) {
-                    wt[w] = wm[w] == -INFINITY ? 0.0f : orc_expf_det(wm[w] - M);
-                    L = L + wt[w] * wl[w];
-                }
-                for (d = 0; d < hd; ++d) {
-                    float a = 0.0f;
-                    for (w = 0; w < ATT_WARPS; ++w) a = a + wt[w] * wacc[w * hd + d];
-                    pacc[s * hd + d] = a;
-                }
-                pm[s] = M;
-                pl[s] = L;
-                free(wacc);
+                pm[s] = m;
+                pl[s] = l;
+                memcpy(pacc + s * hd, acc, hd * sizeof(float));
             }
             {
-                float M = -INFINITY, L = 0.0f, inv;
-                size_t d;
+                float M = -INFINITY, L = 0.0f, inv, w[64];
                 for (s = 0; s < n_active; ++s) M = fmaxf(M, pm[s]);
-                for (s = 0; s < n_active; ++s)
-                    if (pm[s] != -INFINITY) L = L + orc_expf_det(pm[s] - M) * pl[s];
+                for (s = 0; s < n_active; ++s) w[s] = orc_expf_det(pm[s] - M);
+                for (s = 0; s < n_active; ++s) L = fmaf(w[s], pl[s], L);
                 inv = L > 0.0f ? 1.0f / L : 0.0f;
                 for (d = 0; d < hd; ++d) {
                     float o = 0.0f;
-                    for (s = 0; s < n_active; ++s)
-                        if (pm[s] != -INFINITY) o = o + orc_expf_det(pm[s] - M) * pacc[s * hd + d];
+                    for (s = 0; s < n_active; ++s) o = fmaf(w[s], pacc[s * hd + d], o);
                     out[h * hd + d] = o * inv;
                 }
             }
@@ -834,6 +834,7 @@ int orc_attention_dev(float *out, const float *q, const float *k_cache, const fl
     free(pm);
     free(pl);
     free(pacc);
+    free(acc);
     return 1;
 }
 
