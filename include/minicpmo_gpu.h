@@ -215,6 +215,35 @@ MINICPMO_API int minicpmo_gpu_context_qwen3_step_kernels(void *handle, int with_
 /* Bytes of device memory held by the uploaded copy of a tensor. */
 MINICPMO_API size_t minicpmo_gpu_context_tensor_device_bytes(void *handle, const void *host_ptr);
 
+/* ---- allocation-free decode attention (no reference counterpart) ---- */
+
+/* Limits of the fixed scratch the entry below uses instead of allocating:
+ * at most 1024 KV heads, and head_count x n_split x (head_dim + 2) x 4 bytes
+ * of split-K partial sums at most 2 MiB (n_split = clamp(ceil(256 /
+ * kv_head_count), 1, 64); Qwen3-32B's 64 heads / 8 KV heads / head_dim 128
+ * need 1.02 MiB).  Larger shapes are rejected with an error. */
+#define MINICPMO_NOALLOC_MAX_KV_HEADS 1024
+#define MINICPMO_NOALLOC_PARTIAL_BYTES (2u << 20)
+
+/* The decode attention of minicpmo_gpu_context_attention over caller-owned
+ * DEVICE buffers (q, one layer's K/V cache [context_capacity][kv_heads *
+ * head_dim], f32 or f16 when kv_f16, rows 0..pos filled; dst receives
+ * head_count * head_dim floats), enqueued on `stream` (a cudaStream_t, NULL
+ * for the legacy stream) without waiting for it.  No context, and no device
+ * memory is allocated: for callers that cannot allocate while they run (a
+ * serving loop that has reserved all memory up front, a host whose device
+ * memory belongs to its own pool), because cudaMalloc can synchronise the
+ * device and fail late.  The split-K scratch is one static device array per
+ * device (limits above).  Set-up happens on the first call made with a given
+ * device current (the symbol's address and the kernels' shared-memory
+ * opt-in); make that first call before any stream capture.  Each call clears
+ * the split counters on `stream` before launching.  Calls that overlap on the
+ * GPU (other streams, other host threads) share the scratch and race:
+ * serialise them.  Returns 1, or 0 with a message in `error`. */
+MINICPMO_API int minicpmo_gpu_attention_no_alloc(const float *q, const void *k_cache, const void *v_cache, int kv_f16,
+                                    size_t pos, size_t head_count, size_t kv_head_count, size_t head_dim,
+                                    size_t context_capacity, float *dst, void *stream, char *error, size_t error_cap);
+
 #ifdef __cplusplus
 }
 #endif

@@ -133,6 +133,7 @@ SIGNATURES = {
     "minicpmo_gpu_context_qwen3_time_decode": (i32, [vp, u32, sz, sz, fptr] + E),
     "minicpmo_gpu_context_tensor_device_bytes": (sz, [vp, vp]),
     "minicpmo_gpu_context_qwen3_step_kernels": (i32, [vp, i32]),
+    "minicpmo_gpu_attention_no_alloc": (i32, [vp, vp, vp, i32, sz, sz, sz, sz, sz, vp, vp] + E),
 }
 
 

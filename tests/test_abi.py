@@ -49,3 +49,26 @@ def test_null_handles_are_rejected(pkg):
     assert err.value.startswith(b"error:")
     lib.minicpmo_gpu_context_destroy(None)  # NULL-safe (gpu_shim.c:2349-2352)
     assert lib.minicpmo_gpu_context_create(0, 0, None, err, 512) == 0
+
+
+def test_no_alloc_attention_limits_are_checked_on_the_host(pkg):
+    """Shapes beyond the fixed scratch are refused before any CUDA call."""
+    import ctypes as C
+
+    lib = pkg.lib()
+    buf = (C.c_float * 4)()
+    err = C.create_string_buffer(512)
+    fn = lib.minicpmo_gpu_attention_no_alloc
+    fn.argtypes = [C.c_void_p] * 3 + [C.c_int] + [C.c_size_t] * 5 + [C.c_void_p] * 2 + [C.c_char_p, C.c_size_t]
+    p = C.cast(buf, C.c_void_p)
+    # 1024 heads / 128 kv heads / head_dim 256 -> 2 splits x 258 floats x 1024 heads = 2113536 B > 2 MiB
+    assert fn(p, p, p, 0, 0, 1024, 128, 256, 1, p, None, err, 512) == 0
+    assert b"scratch bytes" in err.value and b"2097152" in err.value
+    assert fn(p, p, p, 0, 0, 2048, 2048, 64, 1, p, None, err, 512) == 0
+    assert b"kv heads exceed" in err.value
+    assert fn(p, p, p, 0, 0, 32, 2, 128, 1, p, None, err, 512) == 0  # group of 16
+    assert b"group" in err.value
+    assert fn(p, p, p, 0, 5, 8, 8, 128, 5, p, None, err, 512) == 0  # pos outside the context
+    assert b"outside context" in err.value
+    assert fn(None, p, p, 0, 0, 8, 8, 128, 1, p, None, err, 512) == 0
+    assert b"null buffer" in err.value
