@@ -68,7 +68,11 @@ def peaks():
 
 
 def model_bytes(tensors, shape, pos_mean):
-    w = sum(int(d.nbytes) for _, _, _, _, d in tensors)
+    """Bytes one decode step must read: every weight once, except the token
+    embedding (one row per step), plus the f32 KV rows attended."""
+    w = 0
+    for name, _, rows, _, d in tensors:
+        w += int(d.nbytes) // rows if name == "token_embd.weight" else int(d.nbytes)
     kv = 2 * shape.layers * shape.kv_dim * 4 * (pos_mean + 1)
     return w, kv
 
@@ -155,11 +159,11 @@ def run_reference(args, shape, mix):
     dev = "cuda" if torch.cuda.is_available() else "cpu"
     tensors = build_weights(shape, mix, dev)
     threads = os.cpu_count() or 1
-    # each step is one decode token of the reference CPU path at position >= PROMPT
+    # each step is one decode token of the reference CPU path at position >= args.prompt
     n = args.steps
     from oracle import oracle as O
 
-    ctx = PROMPT + args.warmup + n + 1
+    ctx = args.prompt + args.warmup + n + 1
     tmap = {nm: (dt, r, c, d) for nm, dt, r, c, d in tensors}
     m = O.OracleModel(shape, tmap, ctx, q8_1=False, pool_threads=threads, use_reference_matvec=True)
     rng = np.random.Generator(np.random.PCG64(5))
@@ -167,7 +171,7 @@ def run_reference(args, shape, mix):
     m.vc[:] = rng.standard_normal(m.vc.size, dtype=np.float32)
     kind = "reference" if m.uses_reference_matvec else "port"
     ids = np.random.Generator(np.random.PCG64(11)).integers(0, shape.vocab, args.warmup + n)
-    pos = PROMPT
+    pos = args.prompt
     for i in range(args.warmup):
         m.forward(int(ids[i]), pos)
         pos += 1
@@ -195,7 +199,7 @@ def run_reference(args, shape, mix):
         "config": {"workload": f"{args.shape}-shape Q4_K_M greedy decode, prompt 512", "layers": shape.layers,
                    "hidden": shape.hidden, "vocab": shape.vocab, "parallelism": "cpu threads"},
         "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": threads, "kind": kind,
-                         "sample": f"{n} decode tokens at positions {PROMPT + args.warmup}..{pos - 1} "
+                         "sample": f"{n} decode tokens at positions {args.prompt + args.warmup}..{pos - 1} "
                                    "(f32 activations, reference cpu_kernels.c AVX2 matvec, pthread row pool)"},
         "e2e": {"value": tps, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -211,6 +215,9 @@ def main() -> int:
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--shape", default="qwen3-8b")
     ap.add_argument("--cpu-sample", type=int, default=4, help="decode tokens for the CPU baseline sample (0: skip)")
+    ap.add_argument("--prompt", type=int, default=PROMPT,
+                    help="prompt length before decode (default: the 512 of the headline config; shorter only for "
+                         "profiler launch lists)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -245,10 +252,10 @@ def main() -> int:
     torch.cuda.empty_cache()
     t_gen = time.perf_counter() - t_gen
     t_load = time.perf_counter()
-    rt = Qwen3Runtime.open(tensors, shape=shape, device_index=local, context=PROMPT + args.warmup + 2 * args.steps + 8)
+    rt = Qwen3Runtime.open(tensors, shape=shape, device_index=local, context=args.prompt + args.warmup + 2 * args.steps + 8)
     t_load = time.perf_counter() - t_load
     g = rt.gpu
-    prompt = gguf.prompt_ids(PROMPT, shape.vocab, seed=7 + rank)
+    prompt = gguf.prompt_ids(args.prompt, shape.vocab, seed=7 + rank)
     t_pf = time.perf_counter()
     nxt, _ = rt.append_prompt_ids(prompt)
     t_pf = time.perf_counter() - t_pf
@@ -327,9 +334,9 @@ def main() -> int:
         "dtype": "q4_k/q6_k x q8_1 (int8 dp4a, f32 accumulate)",
         "data": "synthetic: seeded N(0,0.02) weights quantised Q4_K_M-style, 512 uniform random prompt ids",
         "config": {
-            "workload": f"{args.shape}-shape Q4_K_M greedy decode after a 512-token prompt (BASELINE config 2)",
+            "workload": f"{args.shape}-shape Q4_K_M greedy decode after a {args.prompt}-token prompt (BASELINE config 2)",
             "layers": shape.layers, "hidden": shape.hidden, "heads": shape.heads, "kv_heads": shape.kv_heads,
-            "ffn": shape.ffn, "vocab": shape.vocab, "prompt": PROMPT, "decode_positions": [start_pos, start_pos + args.steps],
+            "ffn": shape.ffn, "vocab": shape.vocab, "prompt": args.prompt, "decode_positions": [start_pos, start_pos + args.steps],
             "kv_cache": "f32", "parallelism": f"replicas x{world}" if world > 1 else "single gpu",
             "l2": "weights 4.9 GB per step >> 126 MB L2 (no flush needed)",
             "weights_bytes": w_bytes,
@@ -347,9 +354,9 @@ def main() -> int:
     }
     if rank == 0 and world == 1 and args.cpu_sample > 0:
         try:
-            cps, kind = cpu_reference(shape, tensors, args.cpu_sample, PROMPT, os.cpu_count() or 1)
+            cps, kind = cpu_reference(shape, tensors, args.cpu_sample, args.prompt, os.cpu_count() or 1)
             line["cpu_baseline"] = {"value": cps, "unit": "tok/s", "cores": os.cpu_count() or 1, "kind": kind,
-                                    "sample": f"{args.cpu_sample} decode tokens after {PROMPT} seeded KV positions, "
+                                    "sample": f"{args.cpu_sample} decode tokens after {args.prompt} seeded KV positions, "
                                               "reference cpu_kernels.c AVX2 matvec in a pthread row pool, f32 activations"}
         except Exception as exc:  # the GPU line must still print
             line["cpu_baseline"] = {"value": None, "error": str(exc)[:200]}

@@ -200,6 +200,14 @@ MINICPMO_API int minicpmo_gpu_context_rms_norm_q8_1(void *handle, const float *x
  * [out_dim][in_dim/32] (Q4_K, Q8_0) or [out_dim][in_dim/16] (Q6_K). */
 MINICPMO_API int minicpmo_gpu_context_matvec_q8_1(void *handle, const void *host_ptr, const void *xq, size_t in_dim, size_t out_dim,
                                      float *y_out, int32_t *dots_out, char *error, size_t error_cap);
+/* GEMV of an uploaded quantised tensor on host f32 activations that the
+ * GEMV kernel quantises to Q8_1 itself (as the decode step's fused down and
+ * o projections do), after RMSNorm with the uploaded weight norm_host_ptr
+ * (eps) when that is not NULL (as the fused q/k/v, gate/up and lm_head
+ * GEMVs do).  Same bits as rms_norm_q8_1 / q8_1_quantize then matvec_q8_1. */
+MINICPMO_API int minicpmo_gpu_context_matvec_f32_input(void *handle, const void *host_ptr, const float *x,
+                                          const void *norm_host_ptr, float eps, size_t in_dim, size_t out_dim,
+                                          float *y_out, char *error, size_t error_cap);
 /* Runs the GEMV of an uploaded tensor `iters` times back to back on
  * device-resident activations and reports the mean kernel time (CUDA
  * events on the context stream). */
@@ -227,7 +235,7 @@ MINICPMO_API size_t minicpmo_gpu_context_tensor_device_bytes(void *handle, const
 
 /* The decode attention of minicpmo_gpu_context_attention over caller-owned
  * DEVICE buffers (q, one layer's K/V cache [context_capacity][kv_heads *
- * head_dim], f32 or f16 when kv_f16, rows 0..pos filled; dst receives
+ * head_dim], f32 or f16 when kv_f16, 16-byte aligned, rows 0..pos filled; dst receives
  * head_count * head_dim floats), enqueued on `stream` (a cudaStream_t, NULL
  * for the legacy stream) without waiting for it.  No context, and no device
  * memory is allocated: for callers that cannot allocate while they run (a

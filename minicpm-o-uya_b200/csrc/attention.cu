@@ -37,6 +37,8 @@ constexpr int kGMax = 8;     // q heads per kv head handled by one CTA (<= 2 per
 constexpr int kSub = 32;     // positions per sub-chunk (one per lane)
 constexpr int kMaxSplit = 64;
 
+// The split merge reuses the K/V tile area: per q head of the group the
+// splits' m, l and weights, 1/L, and the merged output row.
 struct AttnSmem {
   float* q;     // [kGMax][hd]
   float* kpos;  // [hd]
@@ -44,11 +46,21 @@ struct AttnSmem {
   float* sq;    // [kAttnWarps][256]
   float* kt;    // [kSub][hd + 1]
   float* vt;    // [kSub][hd + 1]
-  float* w;     // [kAttnWarps][kMaxSplit] combine weights
+  float* cm;    // [kGMax][kMaxSplit]   (merge, aliases kt/vt)
+  float* cl;    // [kGMax][kMaxSplit]
+  float* cw;    // [kGMax][kMaxSplit]
+  float* cinv;  // [kGMax]
+  float* co;    // [kGMax][hd]
 };
 
+__host__ __device__ inline size_t attn_tile_floats(int hd) {
+  const size_t kv = 2 * (size_t)kSub * (hd + 1);
+  const size_t merge = 3 * (size_t)kGMax * kMaxSplit + kGMax + (size_t)kGMax * hd;
+  return kv > merge ? kv : merge;
+}
+
 __host__ __device__ inline size_t attn_smem_floats(int hd) {
-  return (size_t)kGMax * hd + 2 * hd + kAttnWarps * 256 + 2 * (size_t)kSub * (hd + 1) + kAttnWarps * kMaxSplit;
+  return (size_t)kGMax * hd + 2 * hd + kAttnWarps * 256 + attn_tile_floats(hd);
 }
 
 __device__ __forceinline__ AttnSmem carve(float* base, int hd) {
@@ -59,7 +71,11 @@ __device__ __forceinline__ AttnSmem carve(float* base, int hd) {
   s.sq = s.vpos + hd;
   s.kt = s.sq + kAttnWarps * 256;
   s.vt = s.kt + kSub * (hd + 1);
-  s.w = s.vt + kSub * (hd + 1);
+  s.cm = s.kt;
+  s.cl = s.cm + kGMax * kMaxSplit;
+  s.cw = s.cl + kGMax * kMaxSplit;
+  s.cinv = s.cw + kGMax * kMaxSplit;
+  s.co = s.cinv + kGMax;
   return s;
 }
 
@@ -77,6 +93,96 @@ __device__ __forceinline__ void kv_store(void* p, size_t i, float v) {
     reinterpret_cast<__half*>(p)[i] = __float2half_rn(v);
   else
     reinterpret_cast<float*>(p)[i] = v;
+}
+
+// K/V rows are read once per step: streaming (evict-first) loads.
+template <typename T>
+__device__ __forceinline__ float4 kv_load4(const void* p, size_t i) {
+  if constexpr (sizeof(T) == 2) {
+    const uint2 u = __ldcs(reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(p) + i));
+    const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+    const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+    return make_float4(lo.x, lo.y, hi.x, hi.y);
+  } else {
+    return __ldcs(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + i));
+  }
+}
+
+// K/V rows c0 .. c0+31 (zero past t1) into kt/vt, 4 consecutive values of a
+// row per item (hd % 4 == 0, rows 16-byte aligned), kBatch items per thread
+// per round with every load issued before the stores.
+template <typename T>
+__device__ __forceinline__ void stage_kv(const AttnArgs& a, const AttnSmem& sm, int c0, int t1, int pos, bool fused,
+                                         int kv_dim, size_t kv_off, int hd, int hs) {
+  constexpr int kBatch = 8;
+  const int nt = blockDim.x;
+  if (hd & 3) {  // small odd head sizes: one value per item
+    for (int e0 = threadIdx.x; e0 < kSub * hd; e0 += nt * kBatch) {
+      float kr[kBatch], vr[kBatch];
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const int e = e0 + u * nt;
+        kr[u] = vr[u] = 0.0f;
+        if (e < kSub * hd) {
+          const int r = e / hd, d = e - r * hd, t = c0 + r;
+          if (t < t1) {
+            if (fused && t == pos) {
+              kr[u] = sm.kpos[d];
+              vr[u] = sm.vpos[d];
+            } else {
+              const size_t i = (size_t)t * kv_dim + kv_off + d;
+              kr[u] = kv_load<T>(a.k_cache, i);
+              vr[u] = kv_load<T>(a.v_cache, i);
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const int e = e0 + u * nt;
+        if (e < kSub * hd) {
+          const int r = e / hd, d = e - r * hd;
+          sm.kt[r * hs + d] = kr[u];
+          sm.vt[r * hs + d] = vr[u];
+        }
+      }
+    }
+    return;
+  }
+  const int n4 = kSub * hd / 4;
+  for (int e0 = threadIdx.x; e0 < n4; e0 += nt * kBatch) {
+    float4 kr[kBatch], vr[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int e = e0 + u * nt;
+      kr[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      vr[u] = kr[u];
+      if (e < n4) {
+        const int r = (e * 4) / hd, d = e * 4 - r * hd, t = c0 + r;
+        if (t < t1) {
+          if (fused && t == pos) {
+            kr[u] = make_float4(sm.kpos[d], sm.kpos[d + 1], sm.kpos[d + 2], sm.kpos[d + 3]);
+            vr[u] = make_float4(sm.vpos[d], sm.vpos[d + 1], sm.vpos[d + 2], sm.vpos[d + 3]);
+          } else {
+            const size_t i = (size_t)t * kv_dim + kv_off + d;
+            kr[u] = kv_load4<T>(a.k_cache, i);
+            vr[u] = kv_load4<T>(a.v_cache, i);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int e = e0 + u * nt;
+      if (e < n4) {
+        const int r = (e * 4) / hd, d = e * 4 - r * hd;
+        float* kd = sm.kt + r * hs + d;
+        float* vd = sm.vt + r * hs + d;
+        kd[0] = kr[u].x; kd[1] = kr[u].y; kd[2] = kr[u].z; kd[3] = kr[u].w;
+        vd[0] = vr[u].x; vd[1] = vr[u].y; vd[2] = vr[u].z; vd[3] = vr[u].w;
+      }
+    }
+  }
 }
 
 // J = output elements per lane in the P.V phase (hd = 32*J), or J = 1 with
@@ -116,22 +222,50 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a)
   const int stride_part = hd + 2;
   const bool fused = a.fuse_norm_rope_append != 0;
 
-  // K/V of the current position (fused: normalised/rotated here and appended).
-  if (fused) {
-    if (warp == 0) {
-      for (int d = lane; d < hd; d += 32) sm.kpos[d] = a.k[kv_off + d];
+  const bool active = split < n_active;
+  // K/V of the current position (fused: normalised/rotated here; needed by
+  // split 0, which appends it, and by the split that holds position pos).
+  if (fused && (split == 0 || split == n_active - 1)) {
+    if (warp < 2) {
+      const float* src = (warp == 0 ? a.k : a.v) + kv_off;
+      float* dst = warp == 0 ? sm.kpos : sm.vpos;
+      float r[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) r[k] = lane + 32 * k < hd ? src[lane + 32 * k] : 0.0f;
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (lane + 32 * k < hd) dst[lane + 32 * k] = r[k];
       __syncwarp();
-      norm_rope_row(sm.kpos, sm.sq, hd, a.k_norm, a.k_norm_dtype, true, a.rope_cos, a.rope_sin, a.rope_base,
-                    a.rope_scale, pos, lane);
-    } else if (warp == 1) {
-      for (int d = lane; d < hd; d += 32) sm.vpos[d] = a.v[kv_off + d];
+      if (warp == 0)
+        norm_rope_row(sm.kpos, sm.sq, hd, a.k_norm, a.k_norm_dtype, true, a.rope_cos, a.rope_sin, a.rope_base,
+                      a.rope_scale, pos, lane);
     }
   }
-  // q rows of this kv head's group
-  for (int g = warp; g < G; g += kAttnWarps) {
-    float* row = sm.q + g * hd;
-    for (int d = lane; d < hd; d += 32) row[d] = a.q[(size_t)(hb + g) * hd + d];
+  // q rows of this kv head's group (loads of both rows of a warp first)
+  if (active) {
+    float qv[2][8];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int g = warp + i * kAttnWarps;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int d = lane + 32 * k;
+        qv[i][k] = (g < G && d < hd) ? a.q[(size_t)(hb + g) * hd + d] : 0.0f;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int g = warp + i * kAttnWarps;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int d = lane + 32 * k;
+        if (g < G && d < hd) sm.q[g * hd + d] = qv[i][k];
+      }
+    }
     __syncwarp();
+  }
+  for (int g = warp; active && g < G; g += kAttnWarps) {
+    float* row = sm.q + g * hd;
     if (fused)
       norm_rope_row(row, sm.sq + warp * 256, hd, a.q_norm, a.q_norm_dtype, true, a.rope_cos, a.rope_sin, a.rope_base,
                     a.rope_scale, pos, lane);
@@ -144,7 +278,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a)
     }
   }
 
-  if (split < n_active) {
+  if (active) {
     // up to two heads per warp (G <= 8)
     float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.0f, 0.0f}, acc[2][J];
 #pragma unroll
@@ -153,23 +287,10 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a)
       for (int j = 0; j < J; ++j) acc[i][j] = 0.0f;
     const bool act = lane * J < hd;
     for (int c0 = t0; c0 < t1; c0 += kSub) {
-      // stage K and V rows of this sub-chunk (the current position from smem)
-      for (int e = threadIdx.x; e < kSub * hd; e += blockDim.x) {
-        const int r = e / hd, d = e - r * hd, t = c0 + r;
-        float kv = 0.0f, vv = 0.0f;
-        if (t < t1) {
-          if (fused && t == pos) {
-            kv = sm.kpos[d];
-            vv = sm.vpos[d];
-          } else {
-            const size_t i = (size_t)t * kv_dim + kv_off + d;
-            kv = kv_load<T>(a.k_cache, i);
-            vv = kv_load<T>(a.v_cache, i);
-          }
-        }
-        sm.kt[r * hs + d] = kv;
-        sm.vt[r * hs + d] = vv;
-      }
+      // stage K and V rows of this sub-chunk (the current position from
+      // smem): groups of 4 values, all loads of a batch issued before the
+      // shared-memory stores
+      stage_kv<T>(a, sm, c0, t1, pos, fused, kv_dim, kv_off, hd, hs);
       __syncthreads();
       const int t = c0 + lane;
       const bool valid = t < t1;
@@ -223,40 +344,69 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a)
   if (ticket_s != (unsigned)(a.n_split - 1)) return;
   if (threadIdx.x == 0) atomicExch(&a.counters[kvh], 0u);
   __threadfence();
-  float* wsm = sm.w + warp * kMaxSplit;
-  for (int h = hb + warp; h < he; h += kAttnWarps) {
-    const float* ph = a.partial + (size_t)h * a.n_split * stride_part;
+  // Merge, with every partial load issued in batches: (1) m and l of all
+  // (head, split) pairs into smem; (2) per head M = max m, w_s = exp(m_s - M)
+  // and L = sum_s w_s l_s (fma in split order); (3) o_d = sum_s w_s acc_sd
+  // (fma in split order) * (1/L) by one thread per (head, d); (4) Q8_1 blocks
+  // of the output, one warp per block.
+  const int nt = blockDim.x;
+  for (int i = threadIdx.x; i < G * n_active; i += nt) {
+    const int g = i / n_active, sp = i - g * n_active;
+    const float* ps = a.partial + ((size_t)(hb + g) * a.n_split + sp) * stride_part;
+    sm.cm[g * kMaxSplit + sp] = __ldcg(ps);
+    sm.cl[g * kMaxSplit + sp] = __ldcg(ps + 1);
+  }
+  __syncthreads();
+  for (int g = warp; g < G; g += kAttnWarps) {
+    const float* mg = sm.cm + g * kMaxSplit;
     float M = -INFINITY;
-    for (int s = lane; s < n_active; s += 32) M = fmaxf(M, __ldcg(ph + (size_t)s * stride_part));
+    for (int sp = lane; sp < n_active; sp += 32) M = fmaxf(M, mg[sp]);
     M = warp_max(M);
-    for (int s = lane; s < n_active; s += 32) wsm[s] = expf_det(__fsub_rn(__ldcg(ph + (size_t)s * stride_part), M));
+    for (int sp = lane; sp < n_active; sp += 32) sm.cw[g * kMaxSplit + sp] = expf_det(__fsub_rn(mg[sp], M));
     __syncwarp();
-    float L = 0.0f;
-    for (int s = 0; s < n_active; ++s) L = __fmaf_rn(wsm[s], __ldcg(ph + (size_t)s * stride_part + 1), L);
-    const float invL = L > 0.0f ? __fdiv_rn(1.0f, L) : 0.0f;
-    for (int d0 = 0; d0 < hd; d0 += 32) {
-      const int d = d0 + lane;
-      float o = 0.0f;
-      if (d < hd) {
-        for (int s = 0; s < n_active; ++s) o = __fmaf_rn(wsm[s], __ldcg(ph + (size_t)s * stride_part + 2 + d), o);
-        o = __fmul_rn(o, invL);
-        a.out[(size_t)h * hd + d] = o;
-      }
-      if (a.out_q8 && (hd % 32) == 0) {
-        uint16_t dbits;
-        bool zero;
-        const int q = q8_1_quant_lane(o, &dbits, &zero);
-        const float sum = warp_seq_sum(o);
-        const uint16_t sbits = zero ? (uint16_t)0 : f32_to_f16_ref(sum);
-        uint32_t word = ((uint32_t)(q & 0xff)) << (8 * (lane & 3));
-        word |= __shfl_xor_sync(0xffffffffu, word, 1);
-        word |= __shfl_xor_sync(0xffffffffu, word, 2);
-        uint32_t* ob = reinterpret_cast<uint32_t*>(a.out_q8 + ((size_t)h * hd + d0) / 32 * 36);
-        if (lane == 0) ob[0] = (uint32_t)dbits | ((uint32_t)sbits << 16);
-        if ((lane & 3) == 0) ob[1 + (lane >> 2)] = word;
-      }
+    if (lane == 0) {
+      float L = 0.0f;
+      for (int sp = 0; sp < n_active; ++sp) L = __fmaf_rn(sm.cw[g * kMaxSplit + sp], sm.cl[g * kMaxSplit + sp], L);
+      sm.cinv[g] = L > 0.0f ? __fdiv_rn(1.0f, L) : 0.0f;
     }
-    __syncwarp();
+  }
+  __syncthreads();
+  constexpr int kLd = 16;
+  for (int i = threadIdx.x; i < G * hd; i += nt) {
+    const int g = i / hd, d = i - g * hd;
+    const float* pg = a.partial + (size_t)(hb + g) * a.n_split * stride_part + 2 + d;
+    const float* wg = sm.cw + g * kMaxSplit;
+    float o = 0.0f;
+    for (int s0 = 0; s0 < n_active; s0 += kLd) {
+      float r[kLd];
+#pragma unroll
+      for (int u = 0; u < kLd; ++u) r[u] = s0 + u < n_active ? __ldcg(pg + (size_t)(s0 + u) * stride_part) : 0.0f;
+#pragma unroll
+      for (int u = 0; u < kLd; ++u)
+        if (s0 + u < n_active) o = __fmaf_rn(wg[s0 + u], r[u], o);
+    }
+    o = __fmul_rn(o, sm.cinv[g]);
+    a.out[(size_t)(hb + g) * hd + d] = o;
+    sm.co[i] = o;
+  }
+  if (a.out_q8 && (hd % 32) == 0) {
+    __syncthreads();
+    for (int b = warp; b < G * hd / 32; b += kAttnWarps) {
+      const float o = sm.co[b * 32 + lane];
+      uint16_t dbits;
+      bool zero;
+      const int q = q8_1_quant_lane(o, &dbits, &zero);
+      uint32_t word = ((uint32_t)(q & 0xff)) << (8 * (lane & 3));
+      word |= __shfl_xor_sync(0xffffffffu, word, 1);
+      word |= __shfl_xor_sync(0xffffffffu, word, 2);
+      uint32_t* ob = reinterpret_cast<uint32_t*>(a.out_q8 + ((size_t)hb * hd + (size_t)b * 32) / 32 * 36);
+      if (lane == 0) {
+        float sum = 0.0f;  // the sequential f16 s of the reference block
+        for (int t = 0; t < 32; ++t) sum = __fadd_rn(sum, sm.co[b * 32 + t]);
+        ob[0] = (uint32_t)dbits | ((uint32_t)(zero ? (uint16_t)0 : f32_to_f16_ref(sum)) << 16);
+      }
+      if ((lane & 3) == 0) ob[1 + (lane >> 2)] = word;
+    }
   }
 }
 

@@ -102,15 +102,27 @@ __device__ __forceinline__ float warp_max(float v) {
 // operations so the result is bit-identical to the reference's host
 // quantiser.
 __device__ __forceinline__ int q8_1_quant_lane(float x, uint16_t* d_bits, bool* all_zero) {
-  float amax = warp_max(fabsf(x));
+  // amax: one warp reduction over the bit patterns (order-preserving for
+  // non-negative floats); NaN inputs count as 0, as in the reference's
+  // `fabsf(x) > amax` scan
+  const float ax = fabsf(x);
+  const float amax = __int_as_float((int)__reduce_max_sync(0xffffffffu, ax == ax ? (unsigned)__float_as_int(ax) : 0u));
   *all_zero = amax == 0.0f;
   if (amax == 0.0f) {
     *d_bits = 0;
     return 0;
   }
-  float d = __fdiv_rn(amax, 127.0f);
+  const float d = __fdiv_rn(amax, 127.0f);
   *d_bits = f32_to_f16_ref(d);
-  float v = __fdiv_rn(x, d);
+  // q = trunc(v +- 0.5) with v = x/d correctly rounded.  x * rcp(d) is
+  // within 2.3e-5 of v for |v| <= 128 (two roundings of 2^-24 relative each,
+  // plus half an ulp of v), and trunc(v +- 0.5) only changes where |v| is
+  // within 2^-17 of a half-integer; so away from a 1e-4 window around the
+  // half-integers the product gives the same q, and inside it (or when
+  // rcp(d) overflows) the exact quotient is used.
+  float v = __fmul_rn(x, __frcp_rn(d));
+  const float a = fabsf(v);
+  if (!(fabsf(__fsub_rn(__fsub_rn(a, floorf(a)), 0.5f)) >= 1e-4f)) v = __fdiv_rn(x, d);
   int q = __float2int_rz(v >= 0.0f ? __fadd_rn(v, 0.5f) : __fsub_rn(v, 0.5f));
   q = q > 127 ? 127 : q;
   q = q < -128 ? -128 : q;

@@ -240,9 +240,32 @@ __device__ __forceinline__ const GemvSeg& seg_of(const GemvArgs& a, int wr) {
 
 constexpr int kMaxConsumers = 16;  // consumer warps per CTA (+1 producer warp)
 
+// x region: xs, xd, xds, xs16, then 256 floats + 1 of RMSNorm reduction space.
 __host__ __device__ inline size_t gemv_x_bytes(int cols) {
-  const size_t b = (size_t)cols + (size_t)(cols / 32) * 8 + (size_t)(cols / 16) * 4;
+  const size_t b = (size_t)cols + (size_t)(cols / 32) * 8 + (size_t)(cols / 16) * 4 + 257 * 4;
   return (b + 127) / 128 * 128;
+}
+
+// Writes one Q8_1 block (32 values, one per lane) straight into the
+// transposed shared-memory layout: the quants and d of q8_1_quant_lane (the
+// bits k_quantize_q8_1 stores), and the exact integer sums of each half.
+__device__ __forceinline__ void x_block_from_f32(float v, int b, int nb, int lane, uint4* xs, float* xd, float* xds,
+                                                 int* xs16) {
+  uint16_t dbits;
+  bool zero;
+  const int q = q8_1_quant_lane(v, &dbits, &zero);
+  const int sb = b >> 3, j = b & 7, c = j * 2;
+  // quant byte straight into its 16-byte chunk: chunk c holds values 0..15
+  reinterpret_cast<int8_t*>(xs + (size_t)(c + (lane >> 4)) * nb + sb)[lane & 15] = (int8_t)q;
+  const int s_lo = __reduce_add_sync(0xffffffffu, lane < 16 ? q : 0);
+  const int s_hi = __reduce_add_sync(0xffffffffu, lane < 16 ? 0 : q);
+  if (lane == 0) {
+    const float d8 = f16_to_f32(dbits);
+    xd[j * nb + sb] = d8;
+    xds[j * nb + sb] = __fmul_rn(d8, (float)(s_lo + s_hi));
+    xs16[c * nb + sb] = s_lo;
+    xs16[(c + 1) * nb + sb] = s_hi;
+  }
 }
 
 template <int kClass, bool kDots>
@@ -288,6 +311,7 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1) k_gemv(const Gemv
     const int w = lane;
     if (w >= NC) return;
     const int steps = (nwr > w ? (nwr - w + NC - 1) / NC : 0) * spi;
+    const uint64_t policy = l2_evict_first_policy();
     bool ok = true;
     for (int n = 0; n < steps; ++n) {
       const int sidx = n % S;
@@ -300,7 +324,7 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1) k_gemv(const Gemv
       const GemvSeg& s = seg_of(a, wr);
       const uint8_t* src = (part ? s.w2 : s.w) + (size_t)(wr - s.wr_begin) * s.wr_bytes + (size_t)k * s.step_bytes;
       mbar_arrive_expect_tx(&full[w * S + sidx], (uint32_t)s.step_bytes);
-      bulk_load(ring + (size_t)(w * S + sidx) * slot, src, (uint32_t)s.step_bytes, &full[w * S + sidx]);
+      bulk_load_hint(ring + (size_t)(w * S + sidx) * slot, src, (uint32_t)s.step_bytes, &full[w * S + sidx], policy);
     }
     // Leave only once every copy issued into this CTA's shared memory has
     // landed (the consumers normally see to that; this covers their bail-out).
@@ -311,26 +335,95 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1) k_gemv(const Gemv
   }
 
   // ---- consumers ----
-  pdl_wait();  // xq (and y for the residual add) come from earlier kernels
-  for (int b = threadIdx.x; b < nblk; b += NC * 32) {
-    const uint32_t* src = reinterpret_cast<const uint32_t*>(a.xq + (size_t)b * 36);
-    const uint32_t hdr = src[0];
-    uint32_t q[8];
+  pdl_wait();  // the activations (and y for the residual add) come from earlier kernels
+  const int nthr = NC * 32;
+  if (a.input == kInQ8_1) {
+    for (int b = threadIdx.x; b < nblk; b += nthr) {
+      const uint32_t* src = reinterpret_cast<const uint32_t*>(a.xq + (size_t)b * 36);
+      const uint32_t hdr = src[0];
+      uint32_t q[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) q[i] = src[1 + i];
-    int s_lo = 0, s_hi = 0;
+      for (int i = 0; i < 8; ++i) q[i] = src[1 + i];
+      int s_lo = 0, s_hi = 0;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) s_lo = dp4a((int)q[i], 0x01010101, s_lo);
+      for (int i = 0; i < 4; ++i) s_lo = dp4a((int)q[i], 0x01010101, s_lo);
 #pragma unroll
-    for (int i = 4; i < 8; ++i) s_hi = dp4a((int)q[i], 0x01010101, s_hi);
-    const float d8 = f16_to_f32((uint16_t)(hdr & 0xffffu));
-    const int sb = b >> 3, j = b & 7, c = j * 2;
-    xd[j * nb + sb] = d8;
-    xds[j * nb + sb] = __fmul_rn(d8, (float)(s_lo + s_hi));
-    xs16[c * nb + sb] = s_lo;
-    xs16[(c + 1) * nb + sb] = s_hi;
-    xs[c * nb + sb] = make_uint4(q[0], q[1], q[2], q[3]);
-    xs[(c + 1) * nb + sb] = make_uint4(q[4], q[5], q[6], q[7]);
+      for (int i = 4; i < 8; ++i) s_hi = dp4a((int)q[i], 0x01010101, s_hi);
+      const float d8 = f16_to_f32((uint16_t)(hdr & 0xffffu));
+      const int sb = b >> 3, j = b & 7, c = j * 2;
+      xd[j * nb + sb] = d8;
+      xds[j * nb + sb] = __fmul_rn(d8, (float)(s_lo + s_hi));
+      xs16[c * nb + sb] = s_lo;
+      xs16[(c + 1) * nb + sb] = s_hi;
+      xs[c * nb + sb] = make_uint4(q[0], q[1], q[2], q[3]);
+      xs[(c + 1) * nb + sb] = make_uint4(q[4], q[5], q[6], q[7]);
+    }
+  } else {
+    // f32 input: every load is issued before the arithmetic that needs it
+    // (batches of kXB blocks per warp), so the prologue costs about two L2
+    // round trips instead of one per block.
+    constexpr int kXB = 8;
+    const float* xf = a.xf;
+    const bool norm = a.input == kInRmsNorm;
+    float v[kXB], wv[kXB];
+    auto load_batch = [&](int b0) {
+#pragma unroll
+      for (int u = 0; u < kXB; ++u) {
+        const int b = b0 + u * NC;
+        if (b < nblk) {
+          v[u] = xf[b * 32 + lane];
+          wv[u] = norm ? load_weight(a.norm_w, a.norm_dtype, b * 32 + lane) : 1.0f;
+        }
+      }
+    };
+    load_batch(warp);
+    float inv = 1.0f;
+    if (norm) {
+      // sum of squares in k_rmsnorm_q8_1's order: 256 strided partial sums
+      // (each sequential in i), a halving tree, then a warp tree
+      float* red = reinterpret_cast<float*>(xs16 + cols / 16);
+      const int per = cols / 256;
+      for (int t = threadIdx.x; t < 256; t += nthr) {
+        float p = 0.0f;
+        int k = 0;
+        for (; k + 8 <= per; k += 8) {
+          float r[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) r[u] = xf[t + 256 * (k + u)];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) p = __fadd_rn(p, __fmul_rn(r[u], r[u]));
+        }
+        for (; k < per; ++k) {
+          const float r = xf[t + 256 * k];
+          p = __fadd_rn(p, __fmul_rn(r, r));
+        }
+        red[t] = p;
+      }
+      for (int stride = 128; stride >= 32; stride >>= 1) {
+        asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
+        for (int t = threadIdx.x; t < stride; t += nthr) red[t] = __fadd_rn(red[t], red[t + stride]);
+      }
+      asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
+      if (warp == 0) {
+        float r = red[lane];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) r = __fadd_rn(r, __shfl_down_sync(0xffffffffu, r, o));
+        if (lane == 0) red[256] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(r, (float)cols), a.eps)));
+      }
+      asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
+      inv = red[256];
+    }
+    for (int b0 = warp; b0 < nblk; b0 += NC * kXB) {
+      if (b0 != warp) load_batch(b0);
+#pragma unroll
+      for (int u = 0; u < kXB; ++u) {
+        const int b = b0 + u * NC;
+        if (b < nblk) {
+          const float x = norm ? __fmul_rn(__fmul_rn(v[u], inv), wv[u]) : v[u];
+          x_block_from_f32(x, b, nb, lane, xs, xd, xds, xs16);
+        }
+      }
+    }
   }
   asm volatile("bar.sync 1, %0;" ::"r"(NC * 32) : "memory");
   if (threadIdx.x == 0) pdl_launch_dependents();
@@ -526,6 +619,8 @@ cudaError_t launch_gemv(GemvArgs& a, int grid, cudaStream_t st, bool pdl) {
     if (a.seg[i].ks != a.seg[0].ks || a.seg[i].lpr != a.seg[0].lpr) return cudaErrorInvalidValue;
   }
   if (a.seg[0].epi == kEpiSwiglu && a.nseg != 1) return cudaErrorInvalidValue;
+  if (a.input == kInQ8_1 ? !a.xq : (!a.xf || (a.input == kInRmsNorm && !a.norm_w) || a.input > kInRmsNorm))
+    return cudaErrorInvalidValue;
   if (has8 && (has4 || has6)) return cudaErrorInvalidValue;  // no mixed Q8_0 kernel
   a.total_wr = wr;
   a.slot_bytes = slot;

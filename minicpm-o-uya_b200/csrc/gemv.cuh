@@ -31,6 +31,16 @@ struct GemvSeg {
 
 constexpr int kMaxSegs = 3;
 
+// Where a GEMV's Q8_1 input comes from.  Each CTA builds the shared-memory
+// copy of the activations in its prologue; the f32 modes quantise there with
+// the arithmetic of k_quantize_q8_1 / k_rmsnorm_q8_1, so the quants and
+// scales are bit-identical to feeding those kernels' output through xq.
+enum GemvInput : int {
+  kInQ8_1 = 0,     // xq: Q8_1 blocks in global memory
+  kInF32 = 1,      // xf: f32 values, quantised in the prologue
+  kInRmsNorm = 2,  // xf: f32 values; RMSNorm(xf) * norm_w (eps), then quantised
+};
+
 // All segments of one launch share the input width `cols` (hence lpr/ks);
 // a kEpiSwiglu launch has exactly one segment.
 struct GemvArgs {
@@ -38,11 +48,16 @@ struct GemvArgs {
   int nseg;
   int cols;
   int total_wr;
-  int stages;         // ring slots per consumer warp
-  int slot_bytes;     // max step block bytes over the segments
-  const uint8_t* xq;  // Q8_1 activations, cols/32 blocks of 36 B
-  int* dots;          // optional: per-block integer dots, [row][block] (parity tests)
-  int* err;           // set to 1 when a bounded wait gives up
+  int stages;          // ring slots per consumer warp
+  int slot_bytes;      // max step block bytes over the segments
+  int input;           // GemvInput
+  const uint8_t* xq;   // kInQ8_1: Q8_1 activations, cols/32 blocks of 36 B
+  const float* xf;     // kInF32 / kInRmsNorm: f32 activations [cols]
+  const void* norm_w;  // kInRmsNorm: norm weight [cols] (F32 / F16 / BF16)
+  int norm_dtype;
+  float eps;
+  int* dots;           // optional: per-block integer dots, [row][block] (parity tests)
+  int* err;            // set to 1 when a bounded wait gives up
 };
 
 // Fills seg from a tile geometry.

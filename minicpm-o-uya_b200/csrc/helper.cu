@@ -371,13 +371,16 @@ void free_model(Model* m) {
 
 // y (+)= W.x for one matrix of the model; quantised weights read xq,
 // dense ones the f32 input x.
+// With xq == nullptr a quantised GEMV quantises x itself (kInF32).
 cudaError_t model_mv(Ctx* c, Upload* w, const float* x, const uint8_t* xq, float* y, int epi, float* tmp, int grid,
                      int* err) {
   if (w->tiled) {
     GemvArgs a{};
     a.nseg = 1;
     a.cols = (int)w->cols;
+    a.input = xq ? kInQ8_1 : kInF32;
     a.xq = xq;
+    a.xf = x;
     a.err = err;
     gemv_seg_from_geom(w->geom, w->dev, nullptr, y, epi, &a.seg[0]);
     return launch_gemv(a, grid, c->stream, true);
@@ -388,6 +391,25 @@ cudaError_t model_mv(Ctx* c, Upload* w, const float* x, const uint8_t* xq, float
     return launch_add_inplace(y, tmp, (int)w->rows, c->stream);
   }
   return launch_dense_gemv(w->dev, w->dtype, (int)w->rows, (int)w->cols, x, y, c->stream, true);
+}
+
+// q/k/v share one launch when all are tiled and Q8_0 is not mixed with the
+// k-quants (separate kernel classes).
+bool groupable(Upload* const* u, int n) {
+  bool q80 = false, kq = false;
+  for (int i = 0; i < n; ++i) {
+    if (!u[i]->tiled) return false;
+    (u[i]->dtype == kQ8_0 ? q80 : kq) = true;
+  }
+  return !(q80 && kq);
+}
+
+void norm_input(GemvArgs* a, const float* x, const Upload* norm, float eps) {
+  a->input = kInRmsNorm;
+  a->xf = x;
+  a->norm_w = norm->dev;
+  a->norm_dtype = norm->dtype;
+  a->eps = eps;
 }
 
 #define REC(expr)                            \
@@ -405,19 +427,19 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
   REC(launch_mark_seen(m.seen, m.st, (int)cf.vocab, s, true));
   for (uint32_t li = 0; li < cf.layers; ++li) {
     const LayerW& L = m.layer[li];
-    // attention block
-    REC(launch_rmsnorm_q8_1(m.hidden, L.attn_norm->dev, L.attn_norm->dtype, h, cf.rms_eps, m.normed, m.xq, s, true));
-    if (L.q->tiled && L.k->tiled && L.v->tiled) {
-      Upload* ups[3] = {L.q, L.k, L.v};
+    // attention block: RMSNorm -> Q8_1 inside the q/k/v GEMV's prologue
+    Upload* qkv[3] = {L.q, L.k, L.v};
+    if (groupable(qkv, 3)) {
       GemvArgs a{};
       a.nseg = 3;
       a.cols = h;
-      a.xq = m.xq;
+      norm_input(&a, m.hidden, L.attn_norm, cf.rms_eps);
       a.err = &m.st->err;
       float* ys[3] = {m.q, m.k, m.v};
-      for (int i = 0; i < 3; ++i) gemv_seg_from_geom(ups[i]->geom, ups[i]->dev, nullptr, ys[i], kEpiStore, &a.seg[i]);
+      for (int i = 0; i < 3; ++i) gemv_seg_from_geom(qkv[i]->geom, qkv[i]->dev, nullptr, ys[i], kEpiStore, &a.seg[i]);
       REC(launch_gemv(a, m.grid_h, s, true));
     } else {
+      REC(launch_rmsnorm_q8_1(m.hidden, L.attn_norm->dev, L.attn_norm->dtype, h, cf.rms_eps, m.normed, m.xq, s, true));
       REC(model_mv(c, L.q, m.normed, m.xq, m.q, kEpiStore, m.tmp, m.grid_h, &m.st->err));
       REC(model_mv(c, L.k, m.normed, m.xq, m.k, kEpiStore, m.tmp, m.grid_h, &m.st->err));
       REC(model_mv(c, L.v, m.normed, m.xq, m.v, kEpiStore, m.tmp, m.grid_h, &m.st->err));
@@ -451,29 +473,39 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
     a.out = m.attn;
     a.out_q8 = (L.o->tiled && hd % 32 == 0) ? m.aq : nullptr;
     REC(launch_attention(a, s, true));
-    if (L.o->tiled && hd % 32 != 0) REC(launch_quantize_q8_1(m.attn, (int)m.qd, m.aq, s, true));
-    REC(model_mv(c, L.o, m.attn, m.aq, m.hidden, kEpiAdd, m.tmp, m.grid_q, &m.st->err));
-    // feed-forward block
-    REC(launch_rmsnorm_q8_1(m.hidden, L.ffn_norm->dev, L.ffn_norm->dtype, h, cf.rms_eps, m.normed, m.xq, s, true));
+    // (head_dim % 32 != 0: the o GEMV quantises the f32 attention output itself)
+    REC(model_mv(c, L.o, m.attn, a.out_q8, m.hidden, kEpiAdd, m.tmp, m.grid_q, &m.st->err));
+    // feed-forward block: RMSNorm -> Q8_1 inside the gate/up GEMV, SwiGLU in
+    // its epilogue, f32 -> Q8_1 inside the down GEMV
     if (L.gate->tiled && L.up->tiled && L.gate->dtype == L.up->dtype && L.gate->rows == L.up->rows) {
       GemvArgs g{};
       g.nseg = 1;
       g.cols = h;
-      g.xq = m.xq;
+      norm_input(&g, m.hidden, L.ffn_norm, cf.rms_eps);
       g.err = &m.st->err;
       gemv_seg_from_geom(L.gate->geom, L.gate->dev, L.up->dev, m.fused, kEpiSwiglu, &g.seg[0]);
       REC(launch_gemv(g, m.grid_h, s, true));
     } else {
+      REC(launch_rmsnorm_q8_1(m.hidden, L.ffn_norm->dev, L.ffn_norm->dtype, h, cf.rms_eps, m.normed, m.xq, s, true));
       REC(model_mv(c, L.gate, m.normed, m.xq, m.gate, kEpiStore, m.tmp, m.grid_h, &m.st->err));
       REC(model_mv(c, L.up, m.normed, m.xq, m.up, kEpiStore, m.tmp, m.grid_h, &m.st->err));
       REC(launch_silu_mul(m.fused, m.gate, m.up, f, s));
     }
-    if (L.down->tiled) REC(launch_quantize_q8_1(m.fused, f, m.fq, s, true));
-    REC(model_mv(c, L.down, m.fused, m.fq, m.hidden, kEpiAdd, m.tmp, m.grid_f, &m.st->err));
+    REC(model_mv(c, L.down, m.fused, nullptr, m.hidden, kEpiAdd, m.tmp, m.grid_f, &m.st->err));
   }
   if (logits) {
-    REC(launch_rmsnorm_q8_1(m.hidden, m.out_norm->dev, m.out_norm->dtype, h, cf.rms_eps, m.normed, m.xq, s, true));
-    REC(model_mv(c, m.out, m.normed, m.xq, m.logits, kEpiStore, m.tmp, m.grid_h, &m.st->err));
+    if (m.out->tiled) {
+      GemvArgs o{};
+      o.nseg = 1;
+      o.cols = h;
+      norm_input(&o, m.hidden, m.out_norm, cf.rms_eps);
+      o.err = &m.st->err;
+      gemv_seg_from_geom(m.out->geom, m.out->dev, nullptr, m.logits, kEpiStore, &o.seg[0]);
+      REC(launch_gemv(o, m.grid_h, s, true));
+    } else {
+      REC(launch_rmsnorm_q8_1(m.hidden, m.out_norm->dev, m.out_norm->dtype, h, cf.rms_eps, m.normed, m.xq, s, true));
+      REC(model_mv(c, m.out, m.normed, m.xq, m.logits, kEpiStore, m.tmp, m.grid_h, &m.st->err));
+    }
     REC(launch_argmax(m.logits, (int)cf.vocab, m.seen, m.am_scratch, m.am_counter, m.st, m.history, m.history_cap,
                       m.am_grid, s, true));
   }
@@ -1478,6 +1510,44 @@ int minicpmo_gpu_context_matvec_q8_1(void* handle, const void* host_ptr, const v
     ok = cuda_ok(c, cudaMemcpyAsync(dots_out, c->dots, out_dim * per_row * 4, cudaMemcpyDeviceToHost, c->stream), "mv_d2h",
                  error, error_cap);
   if (ok) ok = cuda_ok(c, cudaStreamSynchronize(c->stream), "mv_sync", error, error_cap);
+  return ok ? 1 : 0;
+}
+
+int minicpmo_gpu_context_matvec_f32_input(void* handle, const void* host_ptr, const float* x, const void* norm_host_ptr,
+                                          float eps, size_t in_dim, size_t out_dim, float* y_out, char* error,
+                                          size_t error_cap) {
+  Ctx* c = (Ctx*)handle;
+  if (!c) return copy_error(error, error_cap, "error: null gpu context"), 0;
+  DeviceGuard g(c);
+  Upload* u = find_upload(c, host_ptr);
+  if (!u || !u->tiled || !x || !y_out)
+    return fail(c, error, error_cap, "error: matvec_f32_input needs an uploaded quantised tensor");
+  if (u->cols != in_dim || u->rows != out_dim) return fail(c, error, error_cap, "error: matvec_f32_input shape mismatch");
+  Upload* nw = nullptr;
+  if (norm_host_ptr) {
+    nw = find_upload(c, norm_host_ptr);
+    if (!nw || nw->tiled || nw->rows * nw->cols != in_dim)
+      return fail(c, error, error_cap, "error: matvec_f32_input norm weight not uploaded or wrong size");
+  }
+  if (!ensure(c, &c->sx, &c->sx_bytes, in_dim * 4, "scratch_x_malloc", error, error_cap) ||
+      !ensure(c, &c->sy, &c->sy_bytes, out_dim * 4, "scratch_y_malloc", error, error_cap))
+    return 0;
+  GemvArgs a{};
+  a.nseg = 1;
+  a.cols = (int)in_dim;
+  a.input = nw ? kInRmsNorm : kInF32;
+  a.xf = c->sx;
+  a.norm_w = nw ? nw->dev : nullptr;
+  a.norm_dtype = nw ? nw->dtype : 0;
+  a.eps = eps;
+  a.err = c->dev_err;
+  gemv_seg_from_geom(u->geom, u->dev, nullptr, c->sy, kEpiStore, &a.seg[0]);
+  bool ok = cuda_ok(c, cudaMemcpyAsync(c->sx, x, in_dim * 4, cudaMemcpyHostToDevice, c->stream), "mvf_h2d", error,
+                    error_cap) &&
+            cuda_ok(c, launch_gemv(a, c->sm_count, c->stream, false), "launch_matvec_f32_input", error, error_cap) &&
+            cuda_ok(c, cudaMemcpyAsync(y_out, c->sy, out_dim * 4, cudaMemcpyDeviceToHost, c->stream), "mvf_d2h", error,
+                    error_cap) &&
+            cuda_ok(c, cudaStreamSynchronize(c->stream), "mvf_sync", error, error_cap);
   return ok ? 1 : 0;
 }
 

@@ -98,6 +98,8 @@ extern "C" int minicpmo_gpu_attention_no_alloc(const float* q, const void* k_cac
                      "error: no_alloc attention: needs %zu scratch bytes (%zu heads x %d splits x %zu), limit %zu", need,
                      head_count, n_split, head_dim + 2, kPartialBytes);
 
+  if (((uintptr_t)k_cache | (uintptr_t)v_cache) & 15)
+    return put_error(error, error_cap, "error: no_alloc attention: K/V caches must be 16-byte aligned");
   unsigned char* scratch = scratch_for_current_device(error, error_cap);
   if (!scratch) return 0;
   cudaStream_t st = static_cast<cudaStream_t>(stream);

@@ -15,6 +15,25 @@ namespace mcpo {
 __device__ inline void norm_rope_row(float* row, float* sq, int hd, const void* w, int w_dtype, bool rope,
                                      const float* cos_t, const float* sin_t, float base, float fscale, int pos,
                                      int lane) {
+  // every global load (weights, rope table) is issued up front: hd <= 256
+  // gives at most 8 weights and 4 (cos, sin) pairs per lane
+  const int half = hd / 2;
+  float wr[8], cr[4], sr[4];
+  if (w) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int d = lane + 32 * k;
+      wr[k] = d < hd ? load_weight(w, w_dtype, d) : 0.0f;
+    }
+  }
+  if (rope && cos_t) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int d = lane + 32 * k;
+      cr[k] = d < half ? cos_t[(size_t)pos * half + d] : 0.0f;
+      sr[k] = d < half ? sin_t[(size_t)pos * half + d] : 0.0f;
+    }
+  }
   if (w) {
     for (int t = lane; t < 256; t += 32) sq[t] = t < hd ? __fmul_rn(row[t], row[t]) : 0.0f;
     __syncwarp();
@@ -24,33 +43,42 @@ __device__ inline void norm_rope_row(float* row, float* sq, int hd, const void* 
     for (int o = 16; o > 0; o >>= 1) c = __fadd_rn(c, __shfl_down_sync(0xffffffffu, c, o));
     c = __shfl_sync(0xffffffffu, c, 0);
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(c, (float)hd), 1e-6f)));
-    for (int d = lane; d < hd; d += 32) row[d] = __fmul_rn(__fmul_rn(row[d], inv), load_weight(w, w_dtype, d));
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int d = lane + 32 * k;
+      if (d < hd) row[d] = __fmul_rn(__fmul_rn(row[d], inv), wr[k]);
+    }
     __syncwarp();
   }
   if (!rope) return;
-  const int half = hd / 2;
   float r0[4], r1[4];
-  int cnt = 0;
-  for (int d = lane; d < half && cnt < 4; d += 32, ++cnt) {
-    float c, s;
-    if (cos_t) {
-      c = cos_t[(size_t)pos * half + d];
-      s = sin_t[(size_t)pos * half + d];
-    } else {
-      // qwen3.uya:1620-1623 without a table
-      const float theta = __fdiv_rn(__fmul_rn((float)pos, fscale), powf(base, __fdiv_rn((float)(2 * d), (float)hd)));
-      c = cosf(theta);
-      s = sinf(theta);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int d = lane + 32 * k;
+    if (d < half) {
+      float c, s;
+      if (cos_t) {
+        c = cr[k];
+        s = sr[k];
+      } else {
+        // qwen3.uya:1620-1623 without a table
+        const float theta = __fdiv_rn(__fmul_rn((float)pos, fscale), powf(base, __fdiv_rn((float)(2 * d), (float)hd)));
+        c = cosf(theta);
+        s = sinf(theta);
+      }
+      const float x0 = row[d], x1 = row[d + half];
+      r0[k] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+      r1[k] = __fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, s));
     }
-    const float x0 = row[d], x1 = row[d + half];
-    r0[cnt] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
-    r1[cnt] = __fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, s));
   }
   __syncwarp();
-  cnt = 0;
-  for (int d = lane; d < half && cnt < 4; d += 32, ++cnt) {
-    row[d] = r0[cnt];
-    row[d + half] = r1[cnt];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int d = lane + 32 * k;
+    if (d < half) {
+      row[d] = r0[k];
+      row[d + half] = r1[k];
+    }
   }
   __syncwarp();
 }

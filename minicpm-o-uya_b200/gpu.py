@@ -129,6 +129,7 @@ SIGNATURES = {
     "minicpmo_gpu_context_q8_1_quantize": (i32, [vp, fptr, sz, vp] + E),
     "minicpmo_gpu_context_rms_norm_q8_1": (i32, [vp, fptr, vp, sz, f32, fptr, vp] + E),
     "minicpmo_gpu_context_matvec_q8_1": (i32, [vp, vp, vp, sz, sz, fptr, i32ptr] + E),
+    "minicpmo_gpu_context_matvec_f32_input": (i32, [vp, vp, fptr, vp, f32, sz, sz, fptr] + E),
     "minicpmo_gpu_context_time_matvec": (i32, [vp, vp, sz, sz, i32, fptr] + E),
     "minicpmo_gpu_context_qwen3_time_decode": (i32, [vp, u32, sz, sz, fptr] + E),
     "minicpmo_gpu_context_tensor_device_bytes": (sz, [vp, vp]),
@@ -358,6 +359,14 @@ class GpuContext:
         self._call("minicpmo_gpu_context_matvec_q8_1", t.ptr, xq.ctypes.data, t.cols, t.rows, _f(y),
                    d.ctypes.data_as(i32ptr) if d is not None else None)
         return (y, d) if dots else y
+
+    def matvec_f32_input(self, t: Tensor, x, norm: Tensor | None = None, eps: float = 1e-6) -> np.ndarray:
+        """GEMV whose kernel quantises x (after RMSNorm with `norm`, if given)."""
+        x = _as_f32(x)
+        y = np.empty(t.rows, np.float32)
+        self._call("minicpmo_gpu_context_matvec_f32_input", t.ptr, _f(x), norm.ptr if norm is not None else None, eps,
+                   t.cols, t.rows, _f(y))
+        return y
 
     def time_matvec(self, t: Tensor, iters: int = 20) -> float:
         us = f32()

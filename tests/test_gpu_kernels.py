@@ -47,6 +47,24 @@ def test_q8_1_bit_exact_random(gpu_ctx, O, scale):
     assert np.array_equal(gpu_ctx.q8_1_quantize(x), O.q8_1_quantize(x))
 
 
+def test_q8_1_bit_exact_near_half_integers(gpu_ctx, O):
+    """Values whose quotient x/d sits on or a few ulp from a rounding boundary
+    k + 0.5 (where the kernels switch from x*rcp(d) to the exact division)."""
+    rng = np.random.Generator(np.random.PCG64(99))
+    blocks = []
+    for amax in [127.0, 100.0, 1.0, 3.3e-3, 7.77e4, 1e-30]:
+        d = np.float32(np.float32(amax) / np.float32(127.0))
+        for _ in range(24):
+            k = rng.integers(-127, 127, 31)
+            x = ((k + 0.5) * np.float64(d)).astype(np.float32)
+            ulps = rng.integers(-3, 4, 31).astype(np.int32)
+            x = (x.view(np.int32) + ulps).view(np.float32)
+            x = np.clip(x, -np.float32(amax), np.float32(amax))
+            blocks.append(np.concatenate([[np.float32(amax)], x]).astype(np.float32))
+    x = np.concatenate(blocks)
+    assert np.array_equal(gpu_ctx.q8_1_quantize(x), O.q8_1_quantize(x))
+
+
 @pytest.mark.parametrize("wdt", [F32, F16, BF16])
 @pytest.mark.parametrize("n", [1024, 4096, 5120, 12288])
 def test_rms_norm_q8_1_bit_exact(pkg, gpu_ctx, O, wdt, n):
@@ -77,6 +95,31 @@ def test_matvec_dots_bit_exact_and_rows_close(pkg, gpu_ctx, O, dt, rows, cols):
     assert np.array_equal(dots, O.block_dots(dt, t.data, rows, cols, xq))
     assert np.array_equal(y, O.matvec_q8_1_dev(dt, t.data, rows, cols, xq))
     assert rel_row_err(y, O.matvec_q8_1(dt, t.data, rows, cols, xq)) < MATVEC_TOL
+
+
+@pytest.mark.parametrize("dt", [Q4_K, Q6_K, Q8_0])
+@pytest.mark.parametrize("rows,cols", [(130, 3072), (64, 4096), (40, 12288), (37, 256)])
+@pytest.mark.parametrize("wdt", [None, F32, F16, BF16])
+def test_matvec_fused_input_matches_two_kernel_path(pkg, gpu_ctx, dt, rows, cols, wdt):
+    """The GEMV prologue's own RMSNorm/quantisation gives the bits of
+    rms_norm_q8_1 (or q8_1_quantize) followed by matvec_q8_1."""
+    from minicpmo_b200 import gguf
+    from minicpmo_b200.gpu import Tensor
+
+    t, _ = make_tensor(pkg, f"fin{dt}_{rows}_{cols}", dt, rows, cols, seed=rows + cols)
+    gpu_ctx.upload_tensor(t)
+    x = rvec(cols, cols + 3, 2.0)
+    x[32:64] = 0.0  # an all-zero Q8_1 block
+    if wdt is None:
+        y = gpu_ctx.matvec_f32_input(t, x)
+        xq = gpu_ctx.q8_1_quantize(x)
+    else:
+        w32 = torch.randn((1, cols), generator=torch.Generator().manual_seed(cols + wdt)) * 0.05 + 1.0
+        w = Tensor(f"finw{cols}_{wdt}", gguf.quantize(w32, wdt).numpy(), wdt, 1, cols)
+        gpu_ctx.upload_tensor(w)
+        y = gpu_ctx.matvec_f32_input(t, x, w, 1e-6)
+        _, xq = gpu_ctx.rms_norm_q8_1(x, w, 1e-6)
+    assert np.array_equal(y, gpu_ctx.matvec_q8_1(t, xq))
 
 
 @pytest.mark.parametrize("dt", [Q4_K, Q6_K])
