@@ -161,7 +161,11 @@ typedef struct minicpmo_qwen3_config {
     const float *rope_sin;  /*   then built as qwen3_precompute_rope (qwen3.uya:1633-1662) */
     int kv_f16;             /* 0: f32 KV cache (reference); 1: f16 */
     int max_batch;          /* sequences for forward_batch (0 -> 1) */
-    int reserved[6];
+    int decode_mode;        /* 0: one persistent kernel per decode step when the
+                               model fits it (all linear weights Q4_K/Q6_K, or all
+                               Q8_0), else one kernel per operation; 1: always one
+                               kernel per operation.  Same results either way. */
+    int reserved[5];
 } minicpmo_qwen3_config;
 
 MINICPMO_API int minicpmo_gpu_context_qwen3_bind(void *handle, const minicpmo_qwen3_config *config, char *error, size_t error_cap);
@@ -220,6 +224,14 @@ MINICPMO_API int minicpmo_gpu_context_qwen3_time_decode(void *handle, uint32_t f
 /* Kernel launches in one decode step's graph (with or without the lm_head
  * and sampler); 0 when no model is bound. */
 MINICPMO_API int minicpmo_gpu_context_qwen3_step_kernels(void *handle, int with_logits);
+/* With MCPO_STEP_TRACE=1 in the environment at bind time, the persistent
+ * step kernel records per stage and CTA the globaltimer (ns) at the start of
+ * the stage, when the activations are ready (GEMV stages) and when all of the
+ * CTA's warps are done; this copies the last step's record,
+ * [stage][cta][start, ready, end], into out (cap entries).  0 when tracing
+ * is off. */
+MINICPMO_API int minicpmo_gpu_context_qwen3_step_trace(void *handle, uint64_t *out, size_t cap, uint32_t *n_stages,
+                                          uint32_t *n_ctas);
 /* Bytes of device memory held by the uploaded copy of a tensor. */
 MINICPMO_API size_t minicpmo_gpu_context_tensor_device_bytes(void *handle, const void *host_ptr);
 

@@ -23,6 +23,7 @@
 #include <cuda_fp16.h>
 #include <math.h>
 
+#include "attn_dev.cuh"
 #include "common.cuh"
 #include "gemv.cuh"
 #include "rowops.cuh"
@@ -34,7 +35,6 @@ namespace {
 
 constexpr int kAttnWarps = 4;
 constexpr int kGMax = 8;     // q heads per kv head handled by one CTA (<= 2 per warp)
-constexpr int kSub = 32;     // positions per sub-chunk (one per lane)
 constexpr int kMaxSplit = 64;
 
 // The split merge reuses the K/V tile area: per q head of the group the
@@ -80,109 +80,10 @@ __device__ __forceinline__ AttnSmem carve(float* base, int hd) {
 }
 
 template <typename T>
-__device__ __forceinline__ float kv_load(const void* p, size_t i) {
-  if constexpr (sizeof(T) == 2)
-    return __half2float(reinterpret_cast<const __half*>(p)[i]);
-  else
-    return reinterpret_cast<const float*>(p)[i];
-}
-
-template <typename T>
-__device__ __forceinline__ void kv_store(void* p, size_t i, float v) {
-  if constexpr (sizeof(T) == 2)
-    reinterpret_cast<__half*>(p)[i] = __float2half_rn(v);
-  else
-    reinterpret_cast<float*>(p)[i] = v;
-}
-
-// K/V rows are read once per step: streaming (evict-first) loads.
-template <typename T>
-__device__ __forceinline__ float4 kv_load4(const void* p, size_t i) {
-  if constexpr (sizeof(T) == 2) {
-    const uint2 u = __ldcs(reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(p) + i));
-    const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
-    const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
-    return make_float4(lo.x, lo.y, hi.x, hi.y);
-  } else {
-    return __ldcs(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + i));
-  }
-}
-
-// K/V rows c0 .. c0+31 (zero past t1) into kt/vt, 4 consecutive values of a
-// row per item (hd % 4 == 0, rows 16-byte aligned), kBatch items per thread
-// per round with every load issued before the stores.
-template <typename T>
 __device__ __forceinline__ void stage_kv(const AttnArgs& a, const AttnSmem& sm, int c0, int t1, int pos, bool fused,
                                          int kv_dim, size_t kv_off, int hd, int hs) {
-  constexpr int kBatch = 8;
-  const int nt = blockDim.x;
-  if (hd & 3) {  // small odd head sizes: one value per item
-    for (int e0 = threadIdx.x; e0 < kSub * hd; e0 += nt * kBatch) {
-      float kr[kBatch], vr[kBatch];
-#pragma unroll
-      for (int u = 0; u < kBatch; ++u) {
-        const int e = e0 + u * nt;
-        kr[u] = vr[u] = 0.0f;
-        if (e < kSub * hd) {
-          const int r = e / hd, d = e - r * hd, t = c0 + r;
-          if (t < t1) {
-            if (fused && t == pos) {
-              kr[u] = sm.kpos[d];
-              vr[u] = sm.vpos[d];
-            } else {
-              const size_t i = (size_t)t * kv_dim + kv_off + d;
-              kr[u] = kv_load<T>(a.k_cache, i);
-              vr[u] = kv_load<T>(a.v_cache, i);
-            }
-          }
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < kBatch; ++u) {
-        const int e = e0 + u * nt;
-        if (e < kSub * hd) {
-          const int r = e / hd, d = e - r * hd;
-          sm.kt[r * hs + d] = kr[u];
-          sm.vt[r * hs + d] = vr[u];
-        }
-      }
-    }
-    return;
-  }
-  const int n4 = kSub * hd / 4;
-  for (int e0 = threadIdx.x; e0 < n4; e0 += nt * kBatch) {
-    float4 kr[kBatch], vr[kBatch];
-#pragma unroll
-    for (int u = 0; u < kBatch; ++u) {
-      const int e = e0 + u * nt;
-      kr[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-      vr[u] = kr[u];
-      if (e < n4) {
-        const int r = (e * 4) / hd, d = e * 4 - r * hd, t = c0 + r;
-        if (t < t1) {
-          if (fused && t == pos) {
-            kr[u] = make_float4(sm.kpos[d], sm.kpos[d + 1], sm.kpos[d + 2], sm.kpos[d + 3]);
-            vr[u] = make_float4(sm.vpos[d], sm.vpos[d + 1], sm.vpos[d + 2], sm.vpos[d + 3]);
-          } else {
-            const size_t i = (size_t)t * kv_dim + kv_off + d;
-            kr[u] = kv_load4<T>(a.k_cache, i);
-            vr[u] = kv_load4<T>(a.v_cache, i);
-          }
-        }
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < kBatch; ++u) {
-      const int e = e0 + u * nt;
-      if (e < n4) {
-        const int r = (e * 4) / hd, d = e * 4 - r * hd;
-        float* kd = sm.kt + r * hs + d;
-        float* vd = sm.vt + r * hs + d;
-        kd[0] = kr[u].x; kd[1] = kr[u].y; kd[2] = kr[u].z; kd[3] = kr[u].w;
-        vd[0] = vr[u].x; vd[1] = vr[u].y; vd[2] = vr[u].z; vd[3] = vr[u].w;
-      }
-    }
-  }
+  stage_kv_tile<T>(a.k_cache, a.v_cache, sm.kpos, sm.vpos, sm.kt, sm.vt, c0, t1, pos, fused, kv_dim, kv_off, hd, hs,
+                   threadIdx.x, blockDim.x);
 }
 
 // J = output elements per lane in the P.V phase (hd = 32*J), or J = 1 with

@@ -80,6 +80,12 @@ inline void gemv_seg_from_geom(const TileGeom& g, const uint8_t* w, const uint8_
 
 // One-time per-device setup (opts the GEMV kernels into large shared memory).
 cudaError_t gemv_init();
+// Bytes of the shared-memory activation region of a GEMV over `cols` inputs.
+size_t gemv_x_bytes_host(int cols);
+// Lays the segments out in one warp-row space (wr_begin, total_wr,
+// slot_bytes) and validates them; *dtypes_mask gets bit 0 Q4_K, 1 Q6_K,
+// 2 Q8_0.
+cudaError_t gemv_prepare(GemvArgs& a, int* dtypes_mask);
 // Launches over `grid` persistent CTAs (one per SM); fills wr_begin, total_wr,
 // stages and slot_bytes.  pdl: allow programmatic dependent launch.
 cudaError_t launch_gemv(GemvArgs& a, int grid, cudaStream_t st, bool pdl);

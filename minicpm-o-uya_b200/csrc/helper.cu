@@ -19,6 +19,7 @@
 #include <vector>
 
 #include "attention.cuh"
+#include "step.cuh"
 #include "gemv.cuh"
 #include "layout.cuh"
 #include "minicpmo_gpu.h"
@@ -76,6 +77,16 @@ struct Model {
   cudaGraphExec_t exec[2] = {nullptr, nullptr};
   int kernels[2] = {0, 0};  // kernel launches recorded in each graph
   int* rec_count = nullptr;
+  // persistent step kernel (decode_mode 0 when the model fits it)
+  bool step_ok = false;
+  bool step_q80 = false;
+  StageDesc* stages = nullptr;  // device copy of the stage list
+  int n_stages = 0;             // with the lm_head stage (the last)
+  StepPlan plan{};
+  size_t step_smem = 0;
+  unsigned* step_scratch = nullptr;  // [barrier, abort, pad, pad, attention counters...]
+  size_t step_scratch_bytes = 0;
+  unsigned long long* step_trace = nullptr;  // MCPO_STEP_TRACE=1: per-stage, per-CTA timestamps
 };
 
 struct Ctx {
@@ -363,7 +374,7 @@ void free_model(Model* m) {
   void* bufs[] = {m->hidden, m->normed, m->q,     m->k,       m->v,         m->attn,       m->gate,     m->up,
                   m->fused,  m->tmp,    m->logits, m->xq,     m->aq,        m->fq,         m->kc,       m->vc,
                   m->rope_cos, m->rope_sin, m->partial, m->counters, m->am_scratch, m->am_counter, m->st, m->seen,
-                  m->history};
+                  m->history, m->stages, m->step_scratch, m->step_trace};
   for (void* p : bufs)
     if (p) cudaFree(p);
   if (m->st_host) cudaFreeHost(m->st_host);
@@ -425,6 +436,18 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
   const cudaStream_t s = c->stream;
   REC(launch_embed(m.tok->dev, m.tok->geom, m.tok->dtype, (int)m.tok->rows, h, &m.st->token, 0, m.hidden, s, true));
   REC(launch_mark_seen(m.seen, m.st, (int)cf.vocab, s, true));
+  if (m.step_ok) {
+    // the whole layer chain (and the lm_head) as one persistent kernel
+    cudaError_t e = cudaMemsetAsync(m.step_scratch, 0, m.step_scratch_bytes, s);
+    if (e != cudaSuccess) return e;
+    StepPlan p = m.plan;
+    p.n_stages = logits ? m.n_stages : m.n_stages - 1;
+    REC(launch_decode_step(p, c->sm_count, m.step_smem, m.step_q80, cf.kv_f16 != 0, s));
+    if (logits)
+      REC(launch_argmax(m.logits, (int)cf.vocab, m.seen, m.am_scratch, m.am_counter, m.st, m.history, m.history_cap,
+                        m.am_grid, s, true));
+    return cudaSuccess;
+  }
   for (uint32_t li = 0; li < cf.layers; ++li) {
     const LayerW& L = m.layer[li];
     // attention block: RMSNorm -> Q8_1 inside the q/k/v GEMV's prologue
@@ -510,6 +533,145 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
                       m.am_grid, s, true));
   }
   return cudaSuccess;
+}
+
+// The stage list of the persistent step kernel, or false when the model
+// does not fit it (then the per-kernel graph runs the same arithmetic).
+bool build_step_plan(Ctx* c, Model& m) {
+  const auto& cf = m.cfg;
+  const int h = (int)cf.hidden, hd = (int)cf.head_dim;
+  if (cf.heads % cf.kv_heads || cf.heads / cf.kv_heads > 8 || m.n_split > 64) return false;
+  if (!(hd == 64 || hd == 128 || hd == 256 || (hd <= 32 && hd % 4 == 0))) return false;
+  int coop = 0;
+  if (cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, c->device) != cudaSuccess || !coop) return false;
+  std::vector<StageDesc> st;
+  int mask_all = 0, slot = 0, max_cols = 0;
+  auto add_gemv = [&](GemvArgs& g) -> bool {
+    int mask = 0;
+    if (gemv_prepare(g, &mask) != cudaSuccess) return false;
+    mask_all |= mask;
+    slot = std::max(slot, g.slot_bytes);
+    max_cols = std::max(max_cols, g.cols);
+    StageDesc d{};
+    d.kind = kStageGemv;
+    d.g = g;
+    st.push_back(d);
+    return true;
+  };
+  for (uint32_t li = 0; li < cf.layers; ++li) {
+    const LayerW& L = m.layer[li];
+    Upload* qkv[3] = {L.q, L.k, L.v};
+    if (!groupable(qkv, 3) || !L.o->tiled || !L.down->tiled || !L.gate->tiled || !L.up->tiled ||
+        L.gate->dtype != L.up->dtype || L.gate->rows != L.up->rows)
+      return false;
+    GemvArgs a{};
+    a.nseg = 3;
+    a.cols = h;
+    norm_input(&a, m.hidden, L.attn_norm, cf.rms_eps);
+    a.err = &m.st->err;
+    float* ys[3] = {m.q, m.k, m.v};
+    for (int i = 0; i < 3; ++i) gemv_seg_from_geom(qkv[i]->geom, qkv[i]->dev, nullptr, ys[i], kEpiStore, &a.seg[i]);
+    if (!add_gemv(a)) return false;
+    StageDesc ad{};
+    ad.kind = kStageAttn;
+    AttnArgs& at = ad.at;
+    at.q = m.q;
+    at.k = m.k;
+    at.v = m.v;
+    at.fuse_norm_rope_append = 1;
+    at.q_norm = L.q_norm ? L.q_norm->dev : nullptr;
+    at.q_norm_dtype = L.q_norm ? L.q_norm->dtype : 0;
+    at.k_norm = L.k_norm ? L.k_norm->dev : nullptr;
+    at.k_norm_dtype = L.k_norm ? L.k_norm->dtype : 0;
+    at.rope_cos = m.rope_cos;
+    at.rope_sin = m.rope_sin;
+    at.rope_base = cf.rope_freq_base;
+    at.rope_scale = cf.rope_freq_scale;
+    const size_t esz = cf.kv_f16 ? 2 : 4;
+    at.k_cache = (uint8_t*)m.kc + li * m.kv_layer_elems * esz;
+    at.v_cache = (uint8_t*)m.vc + li * m.kv_layer_elems * esz;
+    at.kv_f16 = cf.kv_f16;
+    at.pos_ptr = &m.st->pos;
+    at.n_head = (int)cf.heads;
+    at.n_kv = (int)cf.kv_heads;
+    at.head_dim = hd;
+    at.ctx = (int)cf.context;
+    at.n_split = m.n_split;
+    at.scale = 1.0f / sqrtf((float)hd);
+    at.partial = m.partial;
+    at.counters = m.step_scratch + 4;
+    at.out = m.attn;
+    at.out_q8 = hd % 32 == 0 ? m.aq : nullptr;
+    st.push_back(ad);
+    GemvArgs o{};
+    o.nseg = 1;
+    o.cols = (int)m.qd;
+    o.input = hd % 32 == 0 ? kInQ8_1 : kInF32;
+    o.xq = m.aq;
+    o.xf = m.attn;
+    o.err = &m.st->err;
+    gemv_seg_from_geom(L.o->geom, L.o->dev, nullptr, m.hidden, kEpiAdd, &o.seg[0]);
+    if (!add_gemv(o)) return false;
+    GemvArgs g{};
+    g.nseg = 1;
+    g.cols = h;
+    norm_input(&g, m.hidden, L.ffn_norm, cf.rms_eps);
+    g.err = &m.st->err;
+    gemv_seg_from_geom(L.gate->geom, L.gate->dev, L.up->dev, m.fused, kEpiSwiglu, &g.seg[0]);
+    if (!add_gemv(g)) return false;
+    GemvArgs dn{};
+    dn.nseg = 1;
+    dn.cols = (int)cf.ffn;
+    dn.input = kInF32;
+    dn.xf = m.fused;
+    dn.err = &m.st->err;
+    gemv_seg_from_geom(L.down->geom, L.down->dev, nullptr, m.hidden, kEpiAdd, &dn.seg[0]);
+    if (!add_gemv(dn)) return false;
+  }
+  if (!m.out->tiled) return false;
+  GemvArgs lo{};
+  lo.nseg = 1;
+  lo.cols = h;
+  norm_input(&lo, m.hidden, m.out_norm, cf.rms_eps);
+  lo.err = &m.st->err;
+  gemv_seg_from_geom(m.out->geom, m.out->dev, nullptr, m.logits, kEpiStore, &lo.seg[0]);
+  if (!add_gemv(lo)) return false;
+  if ((mask_all & 4) && (mask_all & 3)) return false;  // Q8_0 mixed with K-quants
+  const size_t x_bytes = std::max(gemv_x_bytes_host(max_cols), step_attn_bytes(hd));
+  int nc = 0, S = 0;
+  size_t smem = 0;
+  if (!step_layout(slot, x_bytes, &nc, &S, &smem)) return false;
+  m.step_scratch_bytes = 16 + (size_t)cf.kv_heads * 4;
+  if (cudaMalloc((void**)&m.step_scratch, m.step_scratch_bytes) != cudaSuccess) return false;
+  for (auto& d : st)
+    if (d.kind == kStageAttn) d.at.counters = m.step_scratch + 4;
+  if (cudaMalloc((void**)&m.stages, st.size() * sizeof(StageDesc)) != cudaSuccess ||
+      cudaMemcpy(m.stages, st.data(), st.size() * sizeof(StageDesc), cudaMemcpyHostToDevice) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  m.n_stages = (int)st.size();
+  m.step_q80 = (mask_all & 4) != 0;
+  m.step_smem = smem;
+  m.plan.stages = m.stages;
+  m.plan.n_stages = m.n_stages;
+  m.plan.nc = nc;
+  m.plan.S = S;
+  m.plan.slot = slot;
+  m.plan.x_bytes = (int)x_bytes;
+  m.plan.bar = m.step_scratch;
+  m.plan.abort = reinterpret_cast<int*>(m.step_scratch + 1);
+  m.plan.err = &m.st->err;
+  const char* pre = getenv("MCPO_STEP_PREISSUE");
+  // f32-input stages: no weight copies ahead of the prologue (its
+  // activation loads would queue behind them); tuning override
+  // MCPO_STEP_PREISSUE
+  m.plan.preissue = (pre && *pre) ? atoi(pre) : 0;
+  const char* tr = getenv("MCPO_STEP_TRACE");
+  if (tr && tr[0] == '1' &&
+      cudaMalloc((void**)&m.step_trace, (size_t)m.n_stages * c->sm_count * 3 * 8) == cudaSuccess)
+    m.plan.trace = m.step_trace;
+  return true;
 }
 
 int build_graph(Ctx* c, Model& m, int which, char* err, size_t cap) {
@@ -670,8 +832,20 @@ int bind_model(Ctx* c, const minicpmo_qwen3_config* cfg, char* err, size_t cap) 
   m.grid_h = m.grid_q = m.grid_f = c->sm_count;  // persistent GEMV: one CTA per SM
   c->stats.kv_device_bytes = 2 * cf.layers * m.kv_layer_elems * esz;
   c->stats.host_to_device_bytes += 2 * n_rope * 4;
-  if (!cuda_ok(c, cudaStreamSynchronize(c->stream), "qwen3_bind_sync", err, cap) || !build_graph(c, m, 0, err, cap) ||
-      !build_graph(c, m, 1, err, cap)) {
+  if (!cuda_ok(c, cudaStreamSynchronize(c->stream), "qwen3_bind_sync", err, cap)) {
+    free_model(&m);
+    return 0;
+  }
+  m.step_ok = cf.decode_mode == 0 && build_step_plan(c, m);
+  if (m.step_ok && (!build_graph(c, m, 0, err, cap) || !build_graph(c, m, 1, err, cap))) {
+    // the persistent kernel could not be captured: fall back to the
+    // per-kernel graph (same arithmetic)
+    for (auto& e : m.exec)
+      if (e) cudaGraphExecDestroy(e), e = nullptr;
+    cudaGetLastError();
+    m.step_ok = false;
+  }
+  if (!m.step_ok && (!build_graph(c, m, 0, err, cap) || !build_graph(c, m, 1, err, cap))) {
     free_model(&m);
     return 0;
   }
@@ -734,6 +908,7 @@ int minicpmo_gpu_context_create(unsigned int device_index, int debug, void** out
   c->own_stream = true;
   if (!cuda_ok(c, gemv_init(), "gemv_init", error, error_cap) ||
       !cuda_ok(c, attention_init(), "attention_init", error, error_cap) ||
+      !cuda_ok(c, decode_step_init(), "decode_step_init", error, error_cap) ||
       !cuda_ok(c, cudaMalloc((void**)&c->dev_err, sizeof(int)), "error_word_malloc", error, error_cap) ||
       !cuda_ok(c, cudaMemset(c->dev_err, 0, sizeof(int)), "error_word_memset", error, error_cap)) {
     if (c->dev_err) cudaFree(c->dev_err);
@@ -1354,6 +1529,7 @@ int minicpmo_gpu_context_qwen3_forward(void* handle, uint32_t token, size_t pos,
     c->stats.device_to_host_bytes += (size_t)m.cfg.hidden * 4;
   }
   if (!cuda_ok(c, cudaStreamSynchronize(c->stream), "forward_sync", error, error_cap)) return 0;
+  if (hs->err) return fail(c, error, error_cap, "error: qwen3 forward: a bounded device wait gave up (step aborted)");
   c->stats.attention_kernel_calls += m.cfg.layers;
   if (out_token) *out_token = which == 0 ? (uint32_t)hs->next_token : 0u;
   if (out_top2_gap) *out_top2_gap = which == 0 ? hs->gap : 0.0f;
@@ -1406,7 +1582,10 @@ int decode_loop(Ctx* c, uint32_t first_token, size_t first_pos, size_t n_steps, 
   if (ok && tokens_out)
     ok = cuda_ok(c, cudaMemcpyAsync(tokens_out, m.history, n_steps * 4, cudaMemcpyDeviceToHost, c->stream),
                  "decode_tokens_d2h", error, error_cap);
+  if (ok) ok = cuda_ok(c, cudaMemcpyAsync(hs, m.st, sizeof(StepState), cudaMemcpyDeviceToHost, c->stream),
+                       "decode_state_d2h", error, error_cap);
   if (ok) ok = cuda_ok(c, cudaStreamSynchronize(c->stream), "decode_sync", error, error_cap);
+  if (ok && hs->err) ok = fail(c, error, error_cap, "error: qwen3 decode: a bounded device wait gave up (step aborted)");
   if (ok && total_ms) cudaEventElapsedTime(total_ms, e0, e1);
   if (e0) cudaEventDestroy(e0);
   if (e1) cudaEventDestroy(e1);
@@ -1607,6 +1786,20 @@ int minicpmo_gpu_context_qwen3_step_kernels(void* handle, int with_logits) {
   Ctx* c = (Ctx*)handle;
   if (!c || !c->model) return 0;
   return c->model->kernels[with_logits ? 0 : 1];
+}
+
+int minicpmo_gpu_context_qwen3_step_trace(void* handle, uint64_t* out, size_t cap, uint32_t* n_stages,
+                                          uint32_t* n_ctas) {
+  Ctx* c = (Ctx*)handle;
+  if (!c || !c->model || !c->model->step_trace) return 0;
+  DeviceGuard g(c);
+  Model& m = *c->model;
+  const size_t n = (size_t)m.n_stages * c->sm_count * 3;
+  if (n_stages) *n_stages = (uint32_t)m.n_stages;
+  if (n_ctas) *n_ctas = (uint32_t)c->sm_count;
+  if (!out || cap < n) return 0;
+  if (cudaMemcpy(out, m.step_trace, n * 8, cudaMemcpyDeviceToHost) != cudaSuccess) return 0;
+  return 1;
 }
 
 size_t minicpmo_gpu_context_tensor_device_bytes(void* handle, const void* host_ptr) {

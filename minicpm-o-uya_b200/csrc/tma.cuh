@@ -54,6 +54,17 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   return false;
 }
 
+// Bounded wait that also gives up, without raising *err, once *abort is set
+// (checked every 64 polls): used where another party may abandon the work.
+__device__ __forceinline__ bool mbar_wait_abort(uint64_t* bar, uint32_t parity, int* err, const volatile int* abort) {
+  for (int i = 0; i < kWaitLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (abort && (i & 63) == 63 && *abort) return false;
+  }
+  if (err) atomicExch(err, 1);
+  return false;
+}
+
 // Bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned) from
 // global memory into this CTA's shared memory; completes on `bar`.
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {

@@ -66,7 +66,8 @@ class Qwen3Config(C.Structure):
         ("rope_sin", fptr),
         ("kv_f16", i32),
         ("max_batch", i32),
-        ("reserved", i32 * 6),
+        ("decode_mode", i32),
+        ("reserved", i32 * 5),
     ]
 
 
@@ -134,6 +135,7 @@ SIGNATURES = {
     "minicpmo_gpu_context_qwen3_time_decode": (i32, [vp, u32, sz, sz, fptr] + E),
     "minicpmo_gpu_context_tensor_device_bytes": (sz, [vp, vp]),
     "minicpmo_gpu_context_qwen3_step_kernels": (i32, [vp, i32]),
+    "minicpmo_gpu_context_qwen3_step_trace": (i32, [vp, vp, sz, u32ptr, u32ptr]),
     "minicpmo_gpu_attention_no_alloc": (i32, [vp, vp, vp, i32, sz, sz, sz, sz, sz, vp, vp] + E),
 }
 
@@ -375,6 +377,17 @@ class GpuContext:
 
     def qwen3_step_kernels(self, with_logits: bool = True) -> int:
         return int(self.lib.minicpmo_gpu_context_qwen3_step_kernels(self.handle, int(with_logits)))
+
+    def qwen3_step_trace(self):
+        """[stage][cta][start, ready, end] ns of the last persistent step (MCPO_STEP_TRACE=1 at bind), or None."""
+        ns, nc = u32(), u32()
+        self.lib.minicpmo_gpu_context_qwen3_step_trace(self.handle, None, 0, C.byref(ns), C.byref(nc))
+        if ns.value == 0:
+            return None
+        out = np.empty((ns.value, nc.value, 3), np.uint64)
+        if not self.lib.minicpmo_gpu_context_qwen3_step_trace(self.handle, out.ctypes.data, out.size, None, None):
+            return None
+        return out
 
     def tensor_device_bytes(self, t: Tensor) -> int:
         return int(self.lib.minicpmo_gpu_context_tensor_device_bytes(self.handle, t.ptr))

@@ -49,8 +49,10 @@ class Qwen3Runtime:
 
     @classmethod
     def open(cls, weights, shape: Optional[Qwen3Shape] = None, device_index: int = 0, kv_f16: bool = False,
-             context: Optional[int] = None, debug: bool = False) -> "Qwen3Runtime":
-        """weights: a GGUF path/GgufFile, or a list of (name, dtype, rows, cols, uint8 bytes)."""
+             context: Optional[int] = None, debug: bool = False, decode_mode: int = 0) -> "Qwen3Runtime":
+        """weights: a GGUF path/GgufFile, or a list of (name, dtype, rows, cols, uint8 bytes).
+        decode_mode 0: one persistent kernel per decode step where the model fits it; 1: one
+        kernel per operation (same results)."""
         if isinstance(weights, (str,)) or hasattr(weights, "__fspath__"):
             weights = GgufFile(weights)
         if isinstance(weights, GgufFile):
@@ -75,6 +77,7 @@ class Qwen3Runtime:
         cfg.rope_freq_base = shape.rope_base
         cfg.rope_freq_scale = 1.0
         cfg.kv_f16 = int(kv_f16)
+        cfg.decode_mode = int(decode_mode)
         gpu.qwen3_bind(cfg)
         return cls(shape=shape, gpu=gpu, tensors=tensors, context=ctx)
 

@@ -122,6 +122,34 @@ def test_matvec_fused_input_matches_two_kernel_path(pkg, gpu_ctx, dt, rows, cols
     assert np.array_equal(y, gpu_ctx.matvec_q8_1(t, xq))
 
 
+def _near_half_integer_blocks(n, seed):
+    """n values in 32-value blocks whose quotients x/d sit on or a few ulp from
+    k + 0.5 (the rounding boundaries of the Q8_1 quantiser)."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    out = []
+    amaxes = [127.0, 100.0, 1.0, 3.3e-3, 7.77e4]
+    for i in range(n // 32):
+        amax = amaxes[i % len(amaxes)]
+        d = np.float32(np.float32(amax) / np.float32(127.0))
+        k = rng.integers(-127, 127, 31)
+        x = ((k + 0.5) * np.float64(d)).astype(np.float32)
+        x = (x.view(np.int32) + rng.integers(-3, 4, 31).astype(np.int32)).view(np.float32)
+        x = np.clip(x, -np.float32(amax), np.float32(amax))
+        out.append(np.concatenate([[np.float32(amax)], x]).astype(np.float32))
+    return np.concatenate(out)
+
+
+@pytest.mark.parametrize("dt", [Q4_K, Q6_K])
+@pytest.mark.parametrize("cols", [4096, 12288])
+def test_matvec_fused_input_near_half_integers(pkg, gpu_ctx, dt, cols):
+    """The f32-input prologue (one thread per block, approximate reciprocal
+    with an exact fallback) on values placed at the rounding boundaries."""
+    t, _ = make_tensor(pkg, f"fhb{dt}_{cols}", dt, 64, cols, seed=cols + dt)
+    gpu_ctx.upload_tensor(t)
+    x = _near_half_integer_blocks(cols, cols)
+    assert np.array_equal(gpu_ctx.matvec_f32_input(t, x), gpu_ctx.matvec_q8_1(t, gpu_ctx.q8_1_quantize(x)))
+
+
 @pytest.mark.parametrize("dt", [Q4_K, Q6_K])
 def test_matvec_vs_reference_cuda_kernels(pkg, gpu_ctx, O, dt):
     if O.ref_lib("kernels") is None:

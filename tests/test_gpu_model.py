@@ -168,3 +168,36 @@ def test_slot_api_forward_matches_fused(pkg, O):
     st = g.snapshot()
     assert st["native_quant_matvec_count"] > 0 and st["attention_kernel_calls"] > 0
     rt.close()
+
+
+@pytest.mark.parametrize("kv_f16", [False, True])
+def test_persistent_step_matches_per_kernel_graph(pkg, O, kv_f16):
+    """decode_mode 0 (the whole step in one persistent kernel) and decode_mode
+    1 (one kernel per operation) give identical logits, tokens and gaps, on
+    the 8B attention layout (32 q / 8 kv heads, head_dim 128) far enough into
+    the context that attention merges many splits."""
+    from minicpmo_b200 import gguf
+    from minicpmo_b200.qwen3 import Qwen3Runtime
+
+    shape = small_shape(hidden=512, heads=32, kv_heads=8, head_dim=128, ffn=1024, vocab=1024, context=400)
+    tensors = build(pkg, shape, gguf.Q4_K_M, seed=3)
+    rt0 = Qwen3Runtime.open(tensors, shape=shape, context=shape.context, kv_f16=kv_f16, decode_mode=0)
+    rt1 = Qwen3Runtime.open(tensors, shape=shape, context=shape.context, kv_f16=kv_f16, decode_mode=1)
+    assert rt0.gpu.qwen3_step_kernels(True) == 4  # embed, seen-set, the step, sampler
+    assert rt1.gpu.qwen3_step_kernels(True) > 4 * shape.layers
+    ids = gguf.prompt_ids(330, shape.vocab, seed=9)
+    l0 = np.empty(shape.vocab, np.float32)
+    l1 = np.empty(shape.vocab, np.float32)
+    for pos in range(330):
+        t0, g0 = rt0.forward(int(ids[pos]), pos, logits=pos % 3 == 0 or pos > 300, want_logits=l0)
+        t1, g1 = rt1.forward(int(ids[pos]), pos, logits=pos % 3 == 0 or pos > 300, want_logits=l1)
+        if pos % 3 == 0 or pos > 300:
+            assert np.array_equal(l0, l1), (pos, rel_row_err(l0, l1))
+            assert (t0, g0) == (t1, g1), pos
+    # device-side greedy loop from the same state
+    a = rt0.gpu.qwen3_decode(int(ids[0]), 330, 40)
+    b = rt1.gpu.qwen3_decode(int(ids[0]), 330, 40)
+    assert np.array_equal(a, b)
+    rt0.close()
+    rt1.close()
+
