@@ -215,6 +215,10 @@ def main() -> int:
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--shape", default="qwen3-8b")
     ap.add_argument("--cpu-sample", type=int, default=4, help="decode tokens for the CPU baseline sample (0: skip)")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="override the layer count (smaller cases of the same shape, for profiler captures)")
+    ap.add_argument("--decode-mode", type=int, default=0,
+                    help="0: the library default; 1: one kernel per operation; 2: one persistent kernel per step")
     ap.add_argument("--prompt", type=int, default=PROMPT,
                     help="prompt length before decode (default: the 512 of the headline config; shorter only for "
                          "profiler launch lists)")
@@ -226,6 +230,8 @@ def main() -> int:
     from minicpmo_b200 import gguf
 
     shape = gguf.SHAPES[args.shape]
+    if args.layers > 0:
+        shape = gguf.Qwen3Shape(**{**shape.__dict__, "layers": args.layers})
     mix = gguf.Q4_K_M
     if args.impl == "reference":
         return run_reference(args, shape, mix)
@@ -252,7 +258,8 @@ def main() -> int:
     torch.cuda.empty_cache()
     t_gen = time.perf_counter() - t_gen
     t_load = time.perf_counter()
-    rt = Qwen3Runtime.open(tensors, shape=shape, device_index=local, context=args.prompt + args.warmup + 2 * args.steps + 8)
+    rt = Qwen3Runtime.open(tensors, shape=shape, device_index=local, context=args.prompt + args.warmup + 2 * args.steps + 8,
+                           decode_mode=args.decode_mode)
     t_load = time.perf_counter() - t_load
     g = rt.gpu
     prompt = gguf.prompt_ids(args.prompt, shape.vocab, seed=7 + rank)
@@ -298,9 +305,13 @@ def main() -> int:
     value = tokens_total / step_s
     e2e_v = tokens_total / e2e_s
 
-    # ---- roofline of the dominant kernel: the quantised GEMV on the gate/up shape
+    # ---- roofline.  Persistent mode: the dominant (only large) kernel is the
+    # step kernel itself, one launch per token, so its achieved bandwidth is
+    # the step's algorithmic bytes over the device-timed step.  Per-kernel
+    # mode: the quantised GEMV on the gate/up shape, timed alone.
     hbm, peak_kind = peaks()
     T = rt.tensors
+    persistent = g.qwen3_step_kernels(True) <= 4
     shapes = {}
     for name in ("blk.0.ffn_gate.weight", "blk.0.ffn_down.weight", "blk.0.attn_q.weight", "output.weight"):
         t = T[name]
@@ -308,16 +319,24 @@ def main() -> int:
         alg = t.nbytes + t.cols // 32 * 36 + t.rows * 4
         shapes[name] = {"dtype": {10: "Q4_K", 12: "Q6_K", 6: "Q8_0"}[t.dtype], "rows": t.rows,
                         "cols": t.cols, "us": us, "gbs": alg / us / 1e3, "frac": alg / us / 1e3 / hbm}
-    dom = shapes["blk.0.ffn_gate.weight"]
+    w_bytes, kv_bytes = model_bytes(tensors, shape, start_pos + args.steps // 2)
+    step_bytes = w_bytes + kv_bytes
+    traffic_key = "decode_step_qwen3_8b_bytes" if persistent else "gemv_q4_k_12288x4096_bytes"
     traffic = None
     tf = ROOT / "profiles" / "ncu_traffic.json"
     if tf.exists():
         try:
-            traffic = json.loads(tf.read_text()).get("gemv_q4_k_12288x4096_bytes")
+            traffic = json.loads(tf.read_text()).get(traffic_key)
         except (ValueError, KeyError):
             traffic = None
-    w_bytes, kv_bytes = model_bytes(tensors, shape, start_pos + args.steps // 2)
-    step_bytes = w_bytes + kv_bytes
+    if persistent:
+        gbs = step_bytes / (step_s / args.steps) / 1e9
+        dom = {"gbs": gbs, "frac": gbs / hbm}
+        dom_desc = ("k_decode_step (the whole layer chain + lm_head in one persistent launch per token; "
+                    "timed with CUDA events over the K graph replays, which add 3 small kernels)")
+    else:
+        dom = shapes["blk.0.ffn_gate.weight"]
+        dom_desc = "k_gemv (Q4_K 12288x4096, the ffn_gate/up shape), timed alone, weights rotated > L2"
     kernels = g.qwen3_step_kernels(True)
 
     line = {
@@ -347,9 +366,10 @@ def main() -> int:
         "e2e": {"value": e2e_v, "unit": "tok/s", "h2d_bytes_per_step": STATE_BYTES, "d2h_bytes_per_step": STATE_BYTES},
         "gpu_launches": kernels * args.steps,
         "roofline": {"bound": "hbm", "achieved": dom["gbs"], "peak": hbm, "unit": "GB/s", "frac": dom["frac"],
-                     "traffic": traffic, "peak_kind": peak_kind,
-                     "kernel": "k_gemv (Q4_K 12288x4096, the ffn_gate/up shape), timed alone, weights rotated > L2",
-                     "shapes": shapes},
+                     "traffic": traffic, "peak_kind": peak_kind, "kernel": dom_desc,
+                     "algorithmic_bytes_per_launch": step_bytes if persistent else None,
+                     "gemv_sweep": shapes},
+        "decode_mode": "persistent" if persistent else "per-kernel",
         "clocks": clk,
     }
     if rank == 0 and world == 1 and args.cpu_sample > 0:

@@ -161,10 +161,11 @@ typedef struct minicpmo_qwen3_config {
     const float *rope_sin;  /*   then built as qwen3_precompute_rope (qwen3.uya:1633-1662) */
     int kv_f16;             /* 0: f32 KV cache (reference); 1: f16 */
     int max_batch;          /* sequences for forward_batch (0 -> 1) */
-    int decode_mode;        /* 0: one persistent kernel per decode step when the
-                               model fits it (all linear weights Q4_K/Q6_K, or all
-                               Q8_0), else one kernel per operation; 1: always one
-                               kernel per operation.  Same results either way. */
+    int decode_mode;        /* 0: the default (currently 1, the faster one measured);
+                               1: one kernel per operation (a CUDA graph of ~5 per
+                               layer); 2: one persistent kernel per decode step when
+                               the model fits it (all linear weights Q4_K/Q6_K, or
+                               all Q8_0), else 1.  Same results in every mode. */
     int reserved[5];
 } minicpmo_qwen3_config;
 

@@ -836,7 +836,7 @@ int bind_model(Ctx* c, const minicpmo_qwen3_config* cfg, char* err, size_t cap) 
     free_model(&m);
     return 0;
   }
-  m.step_ok = cf.decode_mode == 0 && build_step_plan(c, m);
+  m.step_ok = cf.decode_mode == 2 && build_step_plan(c, m);
   if (m.step_ok && (!build_graph(c, m, 0, err, cap) || !build_graph(c, m, 1, err, cap))) {
     // the persistent kernel could not be captured: fall back to the
     // per-kernel graph (same arithmetic)

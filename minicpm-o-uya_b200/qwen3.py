@@ -51,8 +51,8 @@ class Qwen3Runtime:
     def open(cls, weights, shape: Optional[Qwen3Shape] = None, device_index: int = 0, kv_f16: bool = False,
              context: Optional[int] = None, debug: bool = False, decode_mode: int = 0) -> "Qwen3Runtime":
         """weights: a GGUF path/GgufFile, or a list of (name, dtype, rows, cols, uint8 bytes).
-        decode_mode 0: one persistent kernel per decode step where the model fits it; 1: one
-        kernel per operation (same results)."""
+        decode_mode 0: the default (one kernel per operation); 1: one kernel per operation; 2: one
+        persistent kernel per decode step where the model fits it (same results in every mode)."""
         if isinstance(weights, (str,)) or hasattr(weights, "__fspath__"):
             weights = GgufFile(weights)
         if isinstance(weights, GgufFile):

@@ -32,12 +32,12 @@ def build(pkg, shape, mix, seed=1):
     return gguf.synth_model(shape, mix, seed_base=seed)
 
 
-def run_parity(pkg, O, shape, mix, steps, kv_f16=False, seed=1, tol=LOGIT_TOL):
+def run_parity(pkg, O, shape, mix, steps, kv_f16=False, seed=1, tol=LOGIT_TOL, decode_mode=0):
     from minicpmo_b200 import gguf
     from minicpmo_b200.qwen3 import Qwen3Runtime
 
     tensors = build(pkg, shape, mix, seed)
-    rt = Qwen3Runtime.open(tensors, shape=shape, context=shape.context, kv_f16=kv_f16)
+    rt = Qwen3Runtime.open(tensors, shape=shape, context=shape.context, kv_f16=kv_f16, decode_mode=decode_mode)
     tmap = {n: (dt, r, c, d) for n, dt, r, c, d in tensors}
     orc = O.OracleModel(shape, tmap, shape.context, q8_1=True, kv_f16=kv_f16)
     nat = O.OracleModel(shape, tmap, shape.context, q8_1=True, device_order=False) if not kv_f16 else None
@@ -172,7 +172,7 @@ def test_slot_api_forward_matches_fused(pkg, O):
 
 @pytest.mark.parametrize("kv_f16", [False, True])
 def test_persistent_step_matches_per_kernel_graph(pkg, O, kv_f16):
-    """decode_mode 0 (the whole step in one persistent kernel) and decode_mode
+    """decode_mode 2 (the whole step in one persistent kernel) and decode_mode
     1 (one kernel per operation) give identical logits, tokens and gaps, on
     the 8B attention layout (32 q / 8 kv heads, head_dim 128) far enough into
     the context that attention merges many splits."""
@@ -181,7 +181,7 @@ def test_persistent_step_matches_per_kernel_graph(pkg, O, kv_f16):
 
     shape = small_shape(hidden=512, heads=32, kv_heads=8, head_dim=128, ffn=1024, vocab=1024, context=400)
     tensors = build(pkg, shape, gguf.Q4_K_M, seed=3)
-    rt0 = Qwen3Runtime.open(tensors, shape=shape, context=shape.context, kv_f16=kv_f16, decode_mode=0)
+    rt0 = Qwen3Runtime.open(tensors, shape=shape, context=shape.context, kv_f16=kv_f16, decode_mode=2)
     rt1 = Qwen3Runtime.open(tensors, shape=shape, context=shape.context, kv_f16=kv_f16, decode_mode=1)
     assert rt0.gpu.qwen3_step_kernels(True) == 4  # embed, seen-set, the step, sampler
     assert rt1.gpu.qwen3_step_kernels(True) > 4 * shape.layers
@@ -201,3 +201,12 @@ def test_persistent_step_matches_per_kernel_graph(pkg, O, kv_f16):
     rt0.close()
     rt1.close()
 
+
+
+@pytest.mark.parametrize("mix", ["Q4_K_M", "ALL_Q8_0"])
+def test_persistent_step_vs_oracle(pkg, O, mix):
+    """The persistent step kernel (both of its weight classes) against the
+    oracle in device order: bit-identical logits."""
+    from minicpmo_b200 import gguf
+
+    run_parity(pkg, O, small_shape(layers=3), getattr(gguf, mix), steps=24, decode_mode=2)
