@@ -38,9 +38,12 @@ constexpr int kGMax = 8;     // q heads per kv head handled by one CTA (<= 2 per
 constexpr int kMaxSplit = 64;
 
 // The split merge reuses the K/V tile area: per q head of the group the
-// splits' m, l and weights, 1/L, and the merged output row.
+// splits' m, l and weights, 1/L, and (when they fit) a copy of every split's
+// partial row; the merged output rows reuse the q area.
+constexpr int kMergeStage = 12288;  // floats of staged partial rows (48 KB)
+
 struct AttnSmem {
-  float* q;     // [kGMax][hd]
+  float* q;     // [kGMax][hd]; the merged rows after the merge
   float* kpos;  // [hd]
   float* vpos;  // [hd]
   float* sq;    // [kAttnWarps][256]
@@ -50,17 +53,17 @@ struct AttnSmem {
   float* cl;    // [kGMax][kMaxSplit]
   float* cw;    // [kGMax][kMaxSplit]
   float* cinv;  // [kGMax]
-  float* co;    // [kGMax][hd]
+  float* mp;    // [G][n_active][attn_part_stride(hd)] staged partials, 16-byte aligned
 };
 
 __host__ __device__ inline size_t attn_tile_floats(int hd) {
   const size_t kv = 2 * (size_t)kSub * (hd + 1);
-  const size_t merge = 3 * (size_t)kGMax * kMaxSplit + kGMax + (size_t)kGMax * hd;
+  const size_t merge = 3 * (size_t)kGMax * kMaxSplit + kGMax + 4 + kMergeStage;
   return kv > merge ? kv : merge;
 }
 
 __host__ __device__ inline size_t attn_smem_floats(int hd) {
-  return (size_t)kGMax * hd + 2 * hd + kAttnWarps * 256 + attn_tile_floats(hd);
+  return (size_t)kGMax * hd + 2 * hd + kAttnWarps * 256 + attn_tile_floats(hd) + 4;
 }
 
 __device__ __forceinline__ AttnSmem carve(float* base, int hd) {
@@ -75,8 +78,13 @@ __device__ __forceinline__ AttnSmem carve(float* base, int hd) {
   s.cl = s.cm + kGMax * kMaxSplit;
   s.cw = s.cl + kGMax * kMaxSplit;
   s.cinv = s.cw + kGMax * kMaxSplit;
-  s.co = s.cinv + kGMax;
+  const uintptr_t m = reinterpret_cast<uintptr_t>(s.cinv + kGMax);
+  s.mp = reinterpret_cast<float*>((m + 15) & ~static_cast<uintptr_t>(15));
   return s;
+}
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
 }
 
 template <typename T>
@@ -106,8 +114,6 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a)
   const AttnSmem sm = carve(smem_f, hd);
   const int kvh = blockIdx.x, split = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  pdl_wait();
-  pdl_launch_dependents();
   const int hb = (kvh * a.n_head + a.n_kv - 1) / a.n_kv;
   const int he = ((kvh + 1) * a.n_head + a.n_kv - 1) / a.n_kv;
   const int G = he - hb;
@@ -120,10 +126,49 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a)
   const int t1 = min(t0 + chunk, n_pos);
   const int kv_dim = a.n_kv * hd;
   const size_t kv_off = (size_t)kvh * hd;
-  const int stride_part = hd + 2;
+  const int stride_part = attn_part_stride(hd);
   const bool fused = a.fuse_norm_rope_append != 0;
-
   const bool active = split < n_active;
+  const int nt = blockDim.x;
+
+  // Before waiting for the previous kernel (programmatic dependent launch):
+  // everything that only depends on earlier steps -- the position, the K/V
+  // rows of earlier positions for the first sub-chunk (into registers; the
+  // current position comes from this kernel's prologue), and the norm weight
+  // and RoPE lines (into L1).
+  const int n4 = kSub * hd / 4;
+  const bool early = active && (hd & 3) == 0 && n4 <= 8 * nt;
+  float4 pk[8], pv[8];
+  if (early) {
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int e = threadIdx.x + u * nt;
+      pk[u] = pv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (e < n4) {
+        const int r = (e * 4) / hd, d = e * 4 - r * hd, t = t0 + r;
+        if (t < t1 && !(fused && t == pos)) {
+          const size_t i = (size_t)t * kv_dim + kv_off + d;
+          pk[u] = kv_load4<T>(a.k_cache, i);
+          pv[u] = kv_load4<T>(a.v_cache, i);
+        }
+      }
+    }
+  }
+  if (fused && active && threadIdx.x < 12) {
+    const uint8_t* line = nullptr;
+    const int qb = a.q_norm_dtype == kF32 ? 4 : 2, kb = a.k_norm_dtype == kF32 ? 4 : 2;
+    const int t = threadIdx.x;
+    if (t < 4 && a.q_norm && t * 128 < hd * qb) line = static_cast<const uint8_t*>(a.q_norm) + t * 128;
+    if (t >= 4 && t < 8 && a.k_norm && (t - 4) * 128 < hd * kb) line = static_cast<const uint8_t*>(a.k_norm) + (t - 4) * 128;
+    if (t >= 8 && a.rope_cos) {
+      const float* tab = (t < 10 ? a.rope_cos : a.rope_sin) + (size_t)pos * (hd / 2);
+      if (((t - 8) & 1) * 128 < hd * 2) line = reinterpret_cast<const uint8_t*>(tab) + ((t - 8) & 1) * 128;
+    }
+    if (line) asm volatile("prefetch.global.L1 [%0];" ::"l"(line));
+  }
+  pdl_wait();
+  pdl_launch_dependents();
+
   // K/V of the current position (fused: normalised/rotated here; needed by
   // split 0, which appends it, and by the split that holds position pos).
   if (fused && (split == 0 || split == n_active - 1)) {
@@ -191,7 +236,26 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a)
       // stage K and V rows of this sub-chunk (the current position from
       // smem): groups of 4 values, all loads of a batch issued before the
       // shared-memory stores
-      stage_kv<T>(a, sm, c0, t1, pos, fused, kv_dim, kv_off, hd, hs);
+      if (early && c0 == t0) {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int e = threadIdx.x + u * nt;
+          if (e < n4) {
+            const int r = (e * 4) / hd, d = e * 4 - r * hd, t = c0 + r;
+            float4 kk = pk[u], vv = pv[u];
+            if (fused && t == pos && t < t1) {
+              kk = make_float4(sm.kpos[d], sm.kpos[d + 1], sm.kpos[d + 2], sm.kpos[d + 3]);
+              vv = make_float4(sm.vpos[d], sm.vpos[d + 1], sm.vpos[d + 2], sm.vpos[d + 3]);
+            }
+            float* kd = sm.kt + r * hs + d;
+            float* vd = sm.vt + r * hs + d;
+            kd[0] = kk.x; kd[1] = kk.y; kd[2] = kk.z; kd[3] = kk.w;
+            vd[0] = vv.x; vd[1] = vv.y; vd[2] = vv.z; vd[3] = vv.w;
+          }
+        }
+      } else {
+        stage_kv<T>(a, sm, c0, t1, pos, fused, kv_dim, kv_off, hd, hs);
+      }
       __syncthreads();
       const int t = c0 + lane;
       const bool valid = t < t1;
@@ -228,7 +292,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a)
       float* dst = a.partial + ((size_t)(hb + g) * a.n_split + split) * stride_part;
       if (act)
 #pragma unroll
-        for (int j = 0; j < J; ++j) dst[2 + lane * J + j] = acc[i][j];
+        for (int j = 0; j < J; ++j) dst[4 + lane * J + j] = acc[i][j];
       if (lane == 0) {
         dst[0] = m[i];
         dst[1] = l[i];
@@ -236,26 +300,47 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a)
     }
   }
 
-  // last CTA of this kv head merges the splits
+  // last CTA of this kv head merges the splits: the CTA barrier orders every
+  // thread's partial stores before thread 0's acquire-release ticket
   __shared__ unsigned ticket_s;
-  __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) ticket_s = atomicAdd(&a.counters[kvh], 1u);
+  if (threadIdx.x == 0) {
+    unsigned t;
+    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(t) : "l"(&a.counters[kvh]) : "memory");
+    ticket_s = t;
+  }
   __syncthreads();
   if (ticket_s != (unsigned)(a.n_split - 1)) return;
   if (threadIdx.x == 0) atomicExch(&a.counters[kvh], 0u);
-  __threadfence();
-  // Merge, with every partial load issued in batches: (1) m and l of all
-  // (head, split) pairs into smem; (2) per head M = max m, w_s = exp(m_s - M)
-  // and L = sum_s w_s l_s (fma in split order); (3) o_d = sum_s w_s acc_sd
-  // (fma in split order) * (1/L) by one thread per (head, d); (4) Q8_1 blocks
-  // of the output, one warp per block.
-  const int nt = blockDim.x;
-  for (int i = threadIdx.x; i < G * n_active; i += nt) {
-    const int g = i / n_active, sp = i - g * n_active;
-    const float* ps = a.partial + ((size_t)(hb + g) * a.n_split + sp) * stride_part;
-    sm.cm[g * kMaxSplit + sp] = __ldcg(ps);
-    sm.cl[g * kMaxSplit + sp] = __ldcg(ps + 1);
+  // Merge: (1) m and l of all (head, split) pairs -- with every split's
+  // partial row copied into shared memory in one round trip when they fit
+  // (L2-only bulk copies); (2) per head M = max m, w_s = exp(m_s - M) and
+  // L = sum_s w_s l_s (fma in split order); (3) o_d = sum_s w_s acc_sd (fma in
+  // split order) * (1/L) by one thread per (head, d); (4) Q8_1 blocks of the
+  // output, one warp per block.
+  const bool staged = (size_t)G * n_active * stride_part <= (size_t)kMergeStage;
+  if (staged) {
+    const int per = stride_part / 4;  // 16-byte pieces per partial row
+    for (int i = threadIdx.x; i < G * n_active * per; i += nt) {
+      const int row = i / per, c = i - row * per;
+      const int g = row / n_active, sp = row - g * n_active;
+      cp_async16(sm.mp + (size_t)row * stride_part + c * 4,
+                 a.partial + ((size_t)(hb + g) * a.n_split + sp) * stride_part + c * 4);
+    }
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
+    for (int i = threadIdx.x; i < G * n_active; i += nt) {
+      const int g = i / n_active, sp = i - g * n_active;
+      sm.cm[g * kMaxSplit + sp] = sm.mp[(size_t)i * stride_part];
+      sm.cl[g * kMaxSplit + sp] = sm.mp[(size_t)i * stride_part + 1];
+    }
+  } else {
+    for (int i = threadIdx.x; i < G * n_active; i += nt) {
+      const int g = i / n_active, sp = i - g * n_active;
+      const float* ps = a.partial + ((size_t)(hb + g) * a.n_split + sp) * stride_part;
+      sm.cm[g * kMaxSplit + sp] = __ldcg(ps);
+      sm.cl[g * kMaxSplit + sp] = __ldcg(ps + 1);
+    }
   }
   __syncthreads();
   for (int g = warp; g < G; g += kAttnWarps) {
@@ -275,25 +360,30 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a)
   constexpr int kLd = 16;
   for (int i = threadIdx.x; i < G * hd; i += nt) {
     const int g = i / hd, d = i - g * hd;
-    const float* pg = a.partial + (size_t)(hb + g) * a.n_split * stride_part + 2 + d;
     const float* wg = sm.cw + g * kMaxSplit;
     float o = 0.0f;
-    for (int s0 = 0; s0 < n_active; s0 += kLd) {
-      float r[kLd];
+    if (staged) {
+      const float* pg = sm.mp + (size_t)g * n_active * stride_part + 4 + d;
+      for (int sp = 0; sp < n_active; ++sp) o = __fmaf_rn(wg[sp], pg[(size_t)sp * stride_part], o);
+    } else {
+      const float* pg = a.partial + (size_t)(hb + g) * a.n_split * stride_part + 4 + d;
+      for (int s0 = 0; s0 < n_active; s0 += kLd) {
+        float r[kLd];
 #pragma unroll
-      for (int u = 0; u < kLd; ++u) r[u] = s0 + u < n_active ? __ldcg(pg + (size_t)(s0 + u) * stride_part) : 0.0f;
+        for (int u = 0; u < kLd; ++u) r[u] = s0 + u < n_active ? __ldcg(pg + (size_t)(s0 + u) * stride_part) : 0.0f;
 #pragma unroll
-      for (int u = 0; u < kLd; ++u)
-        if (s0 + u < n_active) o = __fmaf_rn(wg[s0 + u], r[u], o);
+        for (int u = 0; u < kLd; ++u)
+          if (s0 + u < n_active) o = __fmaf_rn(wg[s0 + u], r[u], o);
+      }
     }
     o = __fmul_rn(o, sm.cinv[g]);
     a.out[(size_t)(hb + g) * hd + d] = o;
-    sm.co[i] = o;
+    sm.q[i] = o;
   }
   if (a.out_q8 && (hd % 32) == 0) {
     __syncthreads();
     for (int b = warp; b < G * hd / 32; b += kAttnWarps) {
-      const float o = sm.co[b * 32 + lane];
+      const float o = sm.q[b * 32 + lane];
       uint16_t dbits;
       bool zero;
       const int q = q8_1_quant_lane(o, &dbits, &zero);
@@ -303,7 +393,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a)
       uint32_t* ob = reinterpret_cast<uint32_t*>(a.out_q8 + ((size_t)hb * hd + (size_t)b * 32) / 32 * 36);
       if (lane == 0) {
         float sum = 0.0f;  // the sequential f16 s of the reference block
-        for (int t = 0; t < 32; ++t) sum = __fadd_rn(sum, sm.co[b * 32 + t]);
+        for (int t = 0; t < 32; ++t) sum = __fadd_rn(sum, sm.q[b * 32 + t]);
         ob[0] = (uint32_t)dbits | ((uint32_t)(zero ? (uint16_t)0 : f32_to_f16_ref(sum)) << 16);
       }
       if ((lane & 3) == 0) ob[1 + (lane >> 2)] = word;
@@ -332,7 +422,7 @@ cudaError_t init_j() {
 }  // namespace
 
 size_t attn_partial_floats(int n_head, int n_split, int head_dim) {
-  return (size_t)n_head * n_split * (head_dim + 2);
+  return (size_t)n_head * n_split * attn_part_stride(head_dim);
 }
 
 cudaError_t attention_init() {

@@ -28,13 +28,16 @@ struct AttnArgs {
   int n_split;
   float scale;
   // scratch
-  float* partial;      // [n_head][n_split][head_dim + 2]
+  float* partial;      // [n_head][n_split][attn_part_stride(head_dim)]: m, l, 2 pad, acc[head_dim]
   unsigned* counters;  // [n_kv], zero at rest
   // outputs
   float* out;          // [n_head*head_dim]
   uint8_t* out_q8;     // optional Q8_1 of out (needs head_dim % 32 == 0)
 };
 
+// Floats per (head, split) partial: m, l, two pad floats, then head_dim
+// accumulators (rows stay 16-byte aligned for bulk copies).
+__host__ __device__ inline int attn_part_stride(int head_dim) { return head_dim + 4; }
 size_t attn_partial_floats(int n_head, int n_split, int head_dim);
 // One-time per-device setup (opts the kernels into their shared memory).
 cudaError_t attention_init();

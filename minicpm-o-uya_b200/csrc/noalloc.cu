@@ -96,7 +96,7 @@ extern "C" int minicpmo_gpu_attention_no_alloc(const float* q, const void* k_cac
   if (need > kPartialBytes)
     return put_error(error, error_cap,
                      "error: no_alloc attention: needs %zu scratch bytes (%zu heads x %d splits x %zu), limit %zu", need,
-                     head_count, n_split, head_dim + 2, kPartialBytes);
+                     head_count, n_split, (size_t)attn_part_stride((int)head_dim), kPartialBytes);
 
   if (((uintptr_t)k_cache | (uintptr_t)v_cache) & 15)
     return put_error(error, error_cap, "error: no_alloc attention: K/V caches must be 16-byte aligned");

@@ -168,7 +168,7 @@ __device__ void attn_item(const AttnArgs& a, const AttnStageSmem& sm, int kvh, i
   const int t1 = min(t0 + chunk, n_pos);
   const int kv_dim = a.n_kv * hd;
   const size_t kv_off = (size_t)kvh * hd;
-  const int stride_part = hd + 2;
+  const int stride_part = attn_part_stride(hd);
   const bool fused = a.fuse_norm_rope_append != 0;
 
   // Everything the item reads that does not depend on its own prologue is
@@ -295,7 +295,7 @@ __device__ void attn_item(const AttnArgs& a, const AttnStageSmem& sm, int kvh, i
     const int i = tid + j * nthr;
     if (i < pairs) {
       const int g = i / hd, d = i - g * hd;
-      a.partial[((size_t)(hb + g) * a.n_split + split) * stride_part + 2 + d] = acc[j];
+      a.partial[((size_t)(hb + g) * a.n_split + split) * stride_part + 4 + d] = acc[j];
     }
   }
   if (warp < G && lane == 0) {
@@ -328,7 +328,7 @@ __device__ void attn_item(const AttnArgs& a, const AttnStageSmem& sm, int kvh, i
 #pragma unroll
       for (int sp = 0; sp < kFastSplits; ++sp)
         pacc[j][sp] = (i < pairs && sp < n_active)
-                          ? __ldcg(a.partial + ((size_t)(hb + g) * a.n_split + sp) * stride_part + 2 + d)
+                          ? __ldcg(a.partial + ((size_t)(hb + g) * a.n_split + sp) * stride_part + 4 + d)
                           : 0.0f;
     }
   }
@@ -373,7 +373,7 @@ __device__ void attn_item(const AttnArgs& a, const AttnStageSmem& sm, int kvh, i
   constexpr int kLd = 8;
   for (int i = fast ? pairs : tid; i < pairs; i += nthr) {
     const int g = i / hd, d = i - g * hd;
-    const float* pg = a.partial + (size_t)(hb + g) * a.n_split * stride_part + 2 + d;
+    const float* pg = a.partial + (size_t)(hb + g) * a.n_split * stride_part + 4 + d;
     const float* wg = sm.cw + g * kMaxSplitS;
     float o = 0.0f;
     for (int s0 = 0; s0 < n_active; s0 += kLd) {
