@@ -516,7 +516,9 @@ __device__ __forceinline__ bool gemv_items(const GemvArgs& a, const XShared& x, 
     for (int part = 0; part < (swiglu ? 2 : 1); ++part) {
       for (int k = 0; k < ks; ++k, ++n) {
         const int sidx = n % S;
-        if (!mbar_wait_abort(&full[warp * S + sidx], (uint32_t)(n / S) & 1u, a.err, abort)) return false;
+        if (abort ? !mbar_wait_abort(&full[warp * S + sidx], (uint32_t)(n / S) & 1u, a.err, abort)
+                  : !mbar_wait_sleep(&full[warp * S + sidx], (uint32_t)(n / S) & 1u, a.err))
+          return false;
         const uint8_t* blk = ring + (size_t)(warp * S + sidx) * slot;
         const float v =
             step_value<kClass, kDots>(s.dtype, blk, lane, x, k * s.lpr + lane_in_row, part == 0 ? dots : nullptr);

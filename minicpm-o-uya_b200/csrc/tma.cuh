@@ -46,6 +46,30 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the warp is parked (no issue slots
+// spent polling) until the phase completes or `ns` nanoseconds pass.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded parked wait for a whole warp waiting on the same barrier (at most
+// kSleepLimit hints of 2 us, about 2 s).
+constexpr int kSleepLimit = 1 << 20;
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, int* err) {
+  for (int i = 0; i < kSleepLimit; ++i)
+    if (mbar_try_wait_sleep(bar, parity, 2000u)) return true;
+  if (err) atomicExch(err, 1);
+  return false;
+}
+
 // Bounded wait: returns false (and raises *err) if the phase never completes.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
   for (int i = 0; i < kWaitLimit; ++i)
