@@ -67,6 +67,11 @@ def peaks():
     return 6650.0, "fallback"
 
 
+def metric_name(shape_key: str) -> str:
+    label = {"qwen3-0.6b": "Qwen3-0.6B", "qwen3-8b": "Qwen3-8B", "qwen3-32b": "Qwen3-32B"}.get(shape_key, shape_key)
+    return f"{label} Q4_K_M decode tok/s"
+
+
 def model_bytes(tensors, shape, pos_mean):
     """Bytes one decode step must read: every weight once, except the token
     embedding (one row per step), plus the f32 KV rows attended."""
@@ -184,7 +189,7 @@ def run_reference(args, shape, mix):
     tps = n / dt
     line = {
         "impl": "reference",
-        "metric": "Qwen3-8B Q4_K_M decode tok/s",
+        "metric": metric_name(args.shape),
         "value": tps,
         "unit": "tok/s",
         "n_gpus": 0,
@@ -207,6 +212,51 @@ def run_reference(args, shape, mix):
     return 0
 
 
+def run_kernel_sweep(args) -> int:
+    """Config 1: y = W.x at the north-star shapes for Q4_K, Q6_K and Q8_0 weights (N(0, 0.02)), x N(0, 1)
+    stand-in (a fixed pattern: the GEMV's time does not depend on the values).  Each GEMV is timed alone
+    with CUDA events over weight copies rotated through more than 2x the L2; the hidden-input shapes are
+    also timed with the fused RMSNorm -> Q8_1 prologue, the down shape with the f32 -> Q8_1 prologue (the
+    SwiGLU output it consumes in the step)."""
+    import torch
+    from minicpmo_b200 import gguf
+    from minicpmo_b200.gpu import GpuContext, Tensor
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if int(os.environ.get("RANK", "0")) != 0:
+        return 0
+    torch.cuda.set_device(local)
+    g = GpuContext(local)
+    hbm, peak_kind = peaks()
+    names = {10: "Q4_K", 12: "Q6_K", 6: "Q8_0"}
+    norms = {}
+    for rows, cols in [(4096, 4096), (12288, 4096), (4096, 12288), (151936, 4096)]:
+        for dt in (10, 12, 6):
+            name = f"sweep.{names[dt]}.{rows}x{cols}"
+            t = Tensor(name, gguf.synth_tensor(name, dt, rows, cols, "weight", device="cuda"), dt, rows, cols)
+            g.upload_tensor(t)
+            w_bytes = t.nbytes
+            modes = [("q8_1", 0, cols // 32 * 36)]
+            if cols == 4096:
+                if cols not in norms:
+                    nt = Tensor(f"sweep.norm{cols}", gguf.synth_tensor(f"sweep.norm{cols}", 0, 1, cols, "norm",
+                                                                        device="cuda"), 0, 1, cols)
+                    g.upload_tensor(nt)
+                    norms[cols] = nt
+                modes.append(("rmsnorm_f32", 2, cols * 8))
+            else:
+                modes.append(("f32", 1, cols * 4))
+            for label, mode, x_bytes in modes:
+                us = g.time_matvec_input(t, mode, norms.get(cols) if mode == 2 else None, iters=20)
+                alg = w_bytes + x_bytes + rows * 4
+                print(json.dumps({"kernel_sweep": {"dtype": names[dt], "rows": rows, "cols": cols, "input": label,
+                                                   "us": us, "bytes": alg, "gbs": alg / us / 1e3,
+                                                   "frac": alg / us / 1e3 / hbm, "peak_gbs": hbm,
+                                                   "peak_kind": peak_kind}}), flush=True)
+    g.close()
+    return 0
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -215,6 +265,9 @@ def main() -> int:
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--shape", default="qwen3-8b")
     ap.add_argument("--cpu-sample", type=int, default=4, help="decode tokens for the CPU baseline sample (0: skip)")
+    ap.add_argument("--kernel-sweep", action="store_true",
+                    help="BASELINE config 1: time the GEMV on each shape x dtype (and its fused prologues); "
+                         "one JSON line per case")
     ap.add_argument("--layers", type=int, default=0,
                     help="override the layer count (smaller cases of the same shape, for profiler captures)")
     ap.add_argument("--decode-mode", type=int, default=0,
@@ -235,6 +288,8 @@ def main() -> int:
     mix = gguf.Q4_K_M
     if args.impl == "reference":
         return run_reference(args, shape, mix)
+    if args.kernel_sweep:
+        return run_kernel_sweep(args)
 
     import torch
 
@@ -313,7 +368,8 @@ def main() -> int:
     T = rt.tensors
     persistent = g.qwen3_step_kernels(True) <= 4
     shapes = {}
-    for name in ("blk.0.ffn_gate.weight", "blk.0.ffn_down.weight", "blk.0.attn_q.weight", "output.weight"):
+    lm_name = "output.weight" if "output.weight" in T else "token_embd.weight"  # tied lm_head (0.6B)
+    for name in ("blk.0.ffn_gate.weight", "blk.0.ffn_down.weight", "blk.0.attn_q.weight", lm_name):
         t = T[name]
         us = g.time_matvec(t, iters=20)
         alg = t.nbytes + t.cols // 32 * 36 + t.rows * 4
@@ -340,7 +396,7 @@ def main() -> int:
     kernels = g.qwen3_step_kernels(True)
 
     line = {
-        "metric": "Qwen3-8B Q4_K_M decode tok/s",
+        "metric": metric_name(args.shape),
         "value": value,
         "unit": "tok/s",
         "n_gpus": world,

@@ -218,6 +218,13 @@ MINICPMO_API int minicpmo_gpu_context_matvec_f32_input(void *handle, const void 
  * events on the context stream). */
 MINICPMO_API int minicpmo_gpu_context_time_matvec(void *handle, const void *host_ptr, size_t in_dim, size_t out_dim, int iters,
                                      float *avg_us, char *error, size_t error_cap);
+/* time_matvec with the GEMV's input mode: 0 Q8_1 activations (as
+ * time_matvec), 1 f32 activations quantised to Q8_1 in the GEMV's prologue,
+ * 2 RMSNorm(f32) with the uploaded weight norm_host_ptr (eps 1e-6), then
+ * quantised in the prologue (the fused producers of the decode step). */
+MINICPMO_API int minicpmo_gpu_context_time_matvec_input(void *handle, const void *host_ptr, size_t in_dim, size_t out_dim,
+                                           int iters, int input, const void *norm_host_ptr, float *avg_us,
+                                           char *error, size_t error_cap);
 /* Device time of n_steps auto-advancing decode steps (graph replays, no host
  * copies); reports the total milliseconds. */
 MINICPMO_API int minicpmo_gpu_context_qwen3_time_decode(void *handle, uint32_t first_token, size_t first_pos, size_t n_steps,

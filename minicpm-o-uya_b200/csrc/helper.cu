@@ -1732,14 +1732,31 @@ int minicpmo_gpu_context_matvec_f32_input(void* handle, const void* host_ptr, co
 
 int minicpmo_gpu_context_time_matvec(void* handle, const void* host_ptr, size_t in_dim, size_t out_dim, int iters,
                                      float* avg_us, char* error, size_t error_cap) {
+  return minicpmo_gpu_context_time_matvec_input(handle, host_ptr, in_dim, out_dim, iters, 0, nullptr, avg_us, error,
+                                                error_cap);
+}
+
+int minicpmo_gpu_context_time_matvec_input(void* handle, const void* host_ptr, size_t in_dim, size_t out_dim, int iters,
+                                           int input, const void* norm_host_ptr, float* avg_us, char* error,
+                                           size_t error_cap) {
   Ctx* c = (Ctx*)handle;
   if (!c) return copy_error(error, error_cap, "error: null gpu context"), 0;
   DeviceGuard g(c);
   Upload* u = find_upload(c, host_ptr);
-  if (!u || !u->tiled || u->cols != in_dim || u->rows != out_dim || iters <= 0)
+  if (!u || !u->tiled || u->cols != in_dim || u->rows != out_dim || iters <= 0 || input < 0 || input > 2)
     return fail(c, error, error_cap, "error: time_matvec needs an uploaded quantised tensor of that shape");
+  Upload* nw = nullptr;
+  if (input == 2) {
+    nw = find_upload(c, norm_host_ptr);
+    if (!nw || nw->tiled || nw->rows * nw->cols != in_dim)
+      return fail(c, error, error_cap, "error: time_matvec: norm weight not uploaded or wrong size");
+  }
   if (!ensure_xq(c, in_dim, error, error_cap) ||
-      !ensure(c, &c->sy, &c->sy_bytes, out_dim * 4, "scratch_y_malloc", error, error_cap))
+      !ensure(c, &c->sy, &c->sy_bytes, out_dim * 4, "scratch_y_malloc", error, error_cap) ||
+      (input != 0 && !ensure(c, &c->sx, &c->sx_bytes, in_dim * 4, "scratch_x_malloc", error, error_cap)))
+    return 0;
+  // f32 input: a fixed nonzero pattern (0x3f3f3f3f = 0.747f per value)
+  if (input != 0 && !cuda_ok(c, cudaMemsetAsync(c->sx, 0x3f, in_dim * 4, c->stream), "time_x_memset", error, error_cap))
     return 0;
   // Rotate over enough copies that every launch streams its weights from
   // HBM (the set is larger than twice the 126 MB L2).
@@ -1762,7 +1779,12 @@ int minicpmo_gpu_context_time_matvec(void* handle, const void* host_ptr, size_t 
     GemvArgs a{};
     a.nseg = 1;
     a.cols = (int)in_dim;
+    a.input = input;
     a.xq = c->xq;
+    a.xf = c->sx;
+    a.norm_w = nw ? nw->dev : nullptr;
+    a.norm_dtype = nw ? nw->dtype : 0;
+    a.eps = 1e-6f;
     a.err = c->dev_err;
     gemv_seg_from_geom(u->geom, bufs[i % copies], nullptr, c->sy, kEpiStore, &a.seg[0]);
     return launch_gemv(a, grid, c->stream, false);

@@ -131,6 +131,7 @@ SIGNATURES = {
     "minicpmo_gpu_context_rms_norm_q8_1": (i32, [vp, fptr, vp, sz, f32, fptr, vp] + E),
     "minicpmo_gpu_context_matvec_q8_1": (i32, [vp, vp, vp, sz, sz, fptr, i32ptr] + E),
     "minicpmo_gpu_context_matvec_f32_input": (i32, [vp, vp, fptr, vp, f32, sz, sz, fptr] + E),
+    "minicpmo_gpu_context_time_matvec_input": (i32, [vp, vp, sz, sz, i32, i32, vp, fptr] + E),
     "minicpmo_gpu_context_time_matvec": (i32, [vp, vp, sz, sz, i32, fptr] + E),
     "minicpmo_gpu_context_qwen3_time_decode": (i32, [vp, u32, sz, sz, fptr] + E),
     "minicpmo_gpu_context_tensor_device_bytes": (sz, [vp, vp]),
@@ -369,6 +370,13 @@ class GpuContext:
         self._call("minicpmo_gpu_context_matvec_f32_input", t.ptr, _f(x), norm.ptr if norm is not None else None, eps,
                    t.cols, t.rows, _f(y))
         return y
+
+    def time_matvec_input(self, t: Tensor, input_mode: int, norm: Optional[Tensor] = None, iters: int = 20) -> float:
+        """Mean device time (us) of the GEMV with input mode 0 (Q8_1), 1 (f32) or 2 (RMSNorm + f32)."""
+        us = f32()
+        self._call("minicpmo_gpu_context_time_matvec_input", t.ptr, t.cols, t.rows, iters, input_mode,
+                   norm.ptr if norm is not None else None, C.byref(us))
+        return float(us.value)
 
     def time_matvec(self, t: Tensor, iters: int = 20) -> float:
         us = f32()
