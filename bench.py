@@ -265,6 +265,9 @@ def main() -> int:
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--shape", default="qwen3-8b")
     ap.add_argument("--cpu-sample", type=int, default=4, help="decode tokens for the CPU baseline sample (0: skip)")
+    ap.add_argument("--tp", action="store_true",
+                    help="under torchrun: tensor parallelism over the N GPUs (one sequence, strong scaling) "
+                         "instead of N independent replicas")
     ap.add_argument("--kernel-sweep", action="store_true",
                     help="BASELINE config 1: time the GEMV on each shape x dtype (and its fused prologues); "
                          "one JSON line per case")
@@ -313,11 +316,16 @@ def main() -> int:
     torch.cuda.empty_cache()
     t_gen = time.perf_counter() - t_gen
     t_load = time.perf_counter()
+    tp = None
+    if args.tp and world > 1:
+        from minicpmo_b200.qwen3 import TensorParallel
+
+        tp = TensorParallel(rank, world)
     rt = Qwen3Runtime.open(tensors, shape=shape, device_index=local, context=args.prompt + args.warmup + 2 * args.steps + 8,
-                           decode_mode=args.decode_mode)
+                           decode_mode=args.decode_mode, tp=tp)
     t_load = time.perf_counter() - t_load
     g = rt.gpu
-    prompt = gguf.prompt_ids(args.prompt, shape.vocab, seed=7 + rank)
+    prompt = gguf.prompt_ids(args.prompt, shape.vocab, seed=7 + (0 if tp is not None else rank))
     t_pf = time.perf_counter()
     nxt, _ = rt.append_prompt_ids(prompt)
     t_pf = time.perf_counter() - t_pf
@@ -356,7 +364,7 @@ def main() -> int:
     if dist is not None:
         dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
     step_s, e2e_s = float(ms_t[0]), float(ms_t[1])
-    tokens_total = args.steps * world
+    tokens_total = args.steps * (1 if tp is not None else world)
     value = tokens_total / step_s
     e2e_v = tokens_total / e2e_s
 
@@ -404,7 +412,7 @@ def main() -> int:
         "warmup": args.warmup,
         "ms_per_step": 1000.0 * step_s / args.steps,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if tp is not None else "weak",
         "vs_baseline": None,
         "dtype": "q4_k/q6_k x q8_1 (int8 dp4a, f32 accumulate)",
         "data": "synthetic: seeded N(0,0.02) weights quantised Q4_K_M-style, 512 uniform random prompt ids",
@@ -412,7 +420,9 @@ def main() -> int:
             "workload": f"{args.shape}-shape Q4_K_M greedy decode after a {args.prompt}-token prompt (BASELINE config 2)",
             "layers": shape.layers, "hidden": shape.hidden, "heads": shape.heads, "kv_heads": shape.kv_heads,
             "ffn": shape.ffn, "vocab": shape.vocab, "prompt": args.prompt, "decode_positions": [start_pos, start_pos + args.steps],
-            "kv_cache": "f32", "parallelism": f"replicas x{world}" if world > 1 else "single gpu",
+            "kv_cache": "f32",
+            "parallelism": (f"tp{world} (heads/FFN/vocab shards, P2P all-reduce over NVLink)" if tp is not None
+                            else f"replicas x{world}" if world > 1 else "single gpu"),
             "l2": "weights 4.9 GB per step >> 126 MB L2 (no flush needed)",
             "weights_bytes": w_bytes,
             "step_bytes_mean": step_bytes,

@@ -171,6 +171,26 @@ typedef struct minicpmo_qwen3_config {
 
 MINICPMO_API int minicpmo_gpu_context_qwen3_bind(void *handle, const minicpmo_qwen3_config *config, char *error, size_t error_cap);
 
+/* ---- tensor parallelism over the GPUs of one node (one process per GPU) ----
+ * 1. every rank: minicpmo_gpu_context_tp_buffer(hidden) allocates this rank's
+ *    exchange buffer and returns its cudaIpcMemHandle_t (64 bytes);
+ * 2. the host all-gathers the handles (rank order) by any means;
+ * 3. every rank uploads the full tensors as for qwen3_bind, then calls
+ *    qwen3_bind_tp(cfg, rank, world, handles): the rank keeps its shards --
+ *    q/k/v by heads, gate/up/down by 256-value FFN blocks, o by its heads'
+ *    input columns, the lm_head by vocab rows -- and its decode graph
+ *    all-reduces the o and down partials (hidden += sum in rank order, peer
+ *    loads over NVLink, bounded waits) and merges the per-rank samplers;
+ * 4. the host barriers the ranks, then drives qwen3_forward / qwen3_decode on
+ *    every rank with the same tokens; every rank returns the same token.
+ * heads, kv_heads must divide by world; ffn by 256.  With tensor parallelism
+ * qwen3_forward's logits_out receives only this rank's vocab slice (at its
+ * offset).  No reference counterpart (the reference is single-GPU). */
+MINICPMO_API int minicpmo_gpu_context_tp_buffer(void *handle, size_t hidden, void *ipc_handle_out, char *error,
+                                   size_t error_cap);
+MINICPMO_API int minicpmo_gpu_context_qwen3_bind_tp(void *handle, const minicpmo_qwen3_config *config, int rank, int world,
+                                       const void *peer_ipc_handles, char *error, size_t error_cap);
+
 /* Forward `token` at `pos` (qwen3_forward_token_runtime, qwen3.uya:1991-1995)
  * and sample greedily on the device.  flags bit 0: skip the lm_head and the
  * sampler (prompt tokens that need no logits).  logits_out (may be NULL)

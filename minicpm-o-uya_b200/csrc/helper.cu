@@ -20,6 +20,7 @@
 
 #include "attention.cuh"
 #include "step.cuh"
+#include "tp.cuh"
 #include "gemv.cuh"
 #include "layout.cuh"
 #include "minicpmo_gpu.h"
@@ -39,6 +40,7 @@ struct Upload {
   uint8_t* dev = nullptr;
   size_t dev_bytes = 0;
   bool tiled = false;
+  bool view = false;  // a row range of another upload's device buffer (not owned)
   TileGeom geom{};
 };
 
@@ -87,6 +89,13 @@ struct Model {
   unsigned* step_scratch = nullptr;  // [barrier, abort, pad, pad, attention counters...]
   size_t step_scratch_bytes = 0;
   unsigned long long* step_trace = nullptr;  // MCPO_STEP_TRACE=1: per-stage, per-CTA timestamps
+  // tensor parallelism (tp_world > 1): this rank's shards, local dims in cfg
+  int tp_world = 1, tp_rank = 0;
+  uint32_t vocab_global = 0, vocab_base = 0;
+  TpPeers peers{};
+  std::vector<void*> peer_maps;  // IPC mappings to close
+  unsigned* tp_epoch = nullptr;
+  std::vector<std::unique_ptr<Upload>> shards;
 };
 
 struct Ctx {
@@ -136,6 +145,8 @@ struct Ctx {
   uint32_t* am_seen = nullptr;
   size_t am_seen_bytes = 0;
   std::unique_ptr<Model> model;
+  uint8_t* tp_buf = nullptr;  // this rank's tensor-parallel exchange buffer (IPC-exported)
+  size_t tp_buf_hidden = 0;
   int* dev_err = nullptr;  // raised by a device-side bounded wait that gave up
   minicpmo_gpu_stats stats{};
   char last_error[512] = {0};
@@ -374,10 +385,15 @@ void free_model(Model* m) {
   void* bufs[] = {m->hidden, m->normed, m->q,     m->k,       m->v,         m->attn,       m->gate,     m->up,
                   m->fused,  m->tmp,    m->logits, m->xq,     m->aq,        m->fq,         m->kc,       m->vc,
                   m->rope_cos, m->rope_sin, m->partial, m->counters, m->am_scratch, m->am_counter, m->st, m->seen,
-                  m->history, m->stages, m->step_scratch, m->step_trace};
+                  m->history, m->stages, m->step_scratch, m->step_trace, m->tp_epoch};
   for (void* p : bufs)
     if (p) cudaFree(p);
   if (m->st_host) cudaFreeHost(m->st_host);
+  for (auto& u : m->shards)
+    if (u->dev && !u->view) cudaFree(u->dev);
+  m->shards.clear();
+  for (void* p : m->peer_maps) cudaIpcCloseMemHandle(p);
+  m->peer_maps.clear();
 }
 
 // y (+)= W.x for one matrix of the model; quantised weights read xq,
@@ -435,7 +451,8 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
   const int h = (int)cf.hidden, f = (int)cf.ffn, hd = (int)cf.head_dim;
   const cudaStream_t s = c->stream;
   REC(launch_embed(m.tok->dev, m.tok->geom, m.tok->dtype, (int)m.tok->rows, h, &m.st->token, 0, m.hidden, s, true));
-  REC(launch_mark_seen(m.seen, m.st, (int)cf.vocab, s, true));
+  REC(launch_mark_seen(m.seen, m.st, (int)(m.tp_world > 1 ? m.vocab_global : cf.vocab), s, true));
+  const bool tp = m.tp_world > 1;
   if (m.step_ok) {
     // the whole layer chain (and the lm_head) as one persistent kernel
     cudaError_t e = cudaMemsetAsync(m.step_scratch, 0, m.step_scratch_bytes, s);
@@ -497,7 +514,12 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
     a.out_q8 = (L.o->tiled && hd % 32 == 0) ? m.aq : nullptr;
     REC(launch_attention(a, s, true));
     // (head_dim % 32 != 0: the o GEMV quantises the f32 attention output itself)
-    REC(model_mv(c, L.o, m.attn, a.out_q8, m.hidden, kEpiAdd, m.tmp, m.grid_q, &m.st->err));
+    if (tp) {  // row-parallel: this rank's partial, then hidden += sum of all ranks' partials
+      REC(model_mv(c, L.o, m.attn, a.out_q8, m.peers.part[m.tp_rank][0], kEpiStore, m.tmp, m.grid_q, &m.st->err));
+      REC(launch_tp_reduce_add(m.peers, 0, m.hidden, h, m.tp_epoch, &m.st->err, s));
+    } else {
+      REC(model_mv(c, L.o, m.attn, a.out_q8, m.hidden, kEpiAdd, m.tmp, m.grid_q, &m.st->err));
+    }
     // feed-forward block: RMSNorm -> Q8_1 inside the gate/up GEMV, SwiGLU in
     // its epilogue, f32 -> Q8_1 inside the down GEMV
     if (L.gate->tiled && L.up->tiled && L.gate->dtype == L.up->dtype && L.gate->rows == L.up->rows) {
@@ -514,7 +536,12 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
       REC(model_mv(c, L.up, m.normed, m.xq, m.up, kEpiStore, m.tmp, m.grid_h, &m.st->err));
       REC(launch_silu_mul(m.fused, m.gate, m.up, f, s));
     }
-    REC(model_mv(c, L.down, m.fused, nullptr, m.hidden, kEpiAdd, m.tmp, m.grid_f, &m.st->err));
+    if (tp) {
+      REC(model_mv(c, L.down, m.fused, nullptr, m.peers.part[m.tp_rank][1], kEpiStore, m.tmp, m.grid_f, &m.st->err));
+      REC(launch_tp_reduce_add(m.peers, 1, m.hidden, h, m.tp_epoch, &m.st->err, s));
+    } else {
+      REC(model_mv(c, L.down, m.fused, nullptr, m.hidden, kEpiAdd, m.tmp, m.grid_f, &m.st->err));
+    }
   }
   if (logits) {
     if (m.out->tiled) {
@@ -529,8 +556,14 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
       REC(launch_rmsnorm_q8_1(m.hidden, m.out_norm->dev, m.out_norm->dtype, h, cf.rms_eps, m.normed, m.xq, s, true));
       REC(model_mv(c, m.out, m.normed, m.xq, m.logits, kEpiStore, m.tmp, m.grid_h, &m.st->err));
     }
-    REC(launch_argmax(m.logits, (int)cf.vocab, m.seen, m.am_scratch, m.am_counter, m.st, m.history, m.history_cap,
-                      m.am_grid, s, true));
+    if (tp) {  // this rank's vocab slice, then the cross-rank merge updates the state
+      REC(launch_argmax(m.logits, (int)cf.vocab, m.seen, m.am_scratch, m.am_counter, m.st, m.history, m.history_cap,
+                        m.am_grid, s, true, (int)m.vocab_base, m.peers.top[m.tp_rank]));
+      REC(launch_tp_sample_merge(m.peers, m.st, m.history, m.history_cap, m.tp_epoch, &m.st->err, s));
+    } else {
+      REC(launch_argmax(m.logits, (int)cf.vocab, m.seen, m.am_scratch, m.am_counter, m.st, m.history, m.history_cap,
+                        m.am_grid, s, true));
+    }
   }
   return cudaSuccess;
 }
@@ -710,7 +743,136 @@ bool check_shape(Ctx* c, Upload* u, size_t rows, size_t cols, char* err, size_t 
   return false;
 }
 
-int bind_model(Ctx* c, const minicpmo_qwen3_config* cfg, char* err, size_t cap) {
+// The model's vocabulary (global under tensor parallelism).
+uint32_t vocab_of(const Model& m) { return m.tp_world > 1 ? m.vocab_global : m.cfg.vocab; }
+
+// ---------------------------------------------------------------------
+// tensor parallelism: shards of the uploaded full tensors
+// ---------------------------------------------------------------------
+// Rows [r0, r1) of a tiled matrix: its warp-rows are contiguous, so with r0
+// on a warp-row boundary the range is a view of the same device buffer.
+Upload* row_view(Model& m, const Upload* u, size_t r0, size_t r1) {
+  if (!u || !u->tiled || r1 <= r0 || r0 % (size_t)u->geom.rpw) return nullptr;
+  std::unique_ptr<Upload> v(new Upload(*u));
+  v->host_ptr = nullptr;
+  v->rows = r1 - r0;
+  v->view = true;
+  if (!make_geom(u->dtype, (int)v->rows, (int)u->cols, &v->geom)) return nullptr;
+  v->dev = u->dev + (r0 / (size_t)u->geom.rpw) * u->geom.wr_bytes;
+  v->dev_bytes = v->geom.total_bytes;
+  m.shards.push_back(std::move(v));
+  return m.shards.back().get();
+}
+
+// Columns [c0, c1) (multiples of 256) of a quantised matrix, rebuilt from the
+// caller's GGUF bytes (still valid: weight pointers are borrowed for the
+// context's lifetime) into a tiled buffer of its own.
+Upload* col_slice(Ctx* c, Model& m, const Upload* u, size_t c0, size_t c1, char* err, size_t cap) {
+  if (!u || !u->tiled || !u->host_ptr || c0 % 256 || c1 % 256 || c1 <= c0 || c1 > u->cols) return nullptr;
+  const size_t rb = gguf_row_bytes(u->dtype, u->cols), sbb = rb / (u->cols / 256);
+  const size_t nrb = (c1 - c0) / 256 * sbb;
+  std::vector<uint8_t> host(u->rows * nrb);
+  const uint8_t* src = static_cast<const uint8_t*>(u->host_ptr);
+  for (size_t r = 0; r < u->rows; ++r) memcpy(host.data() + r * nrb, src + r * rb + c0 / 256 * sbb, nrb);
+  std::unique_ptr<Upload> v(new Upload());
+  v->name = u->name + ".cols";
+  v->rows = u->rows;
+  v->cols = c1 - c0;
+  v->dtype = u->dtype;
+  v->bytes = host.size();
+  if (!make_geom(v->dtype, (int)v->rows, (int)v->cols, &v->geom)) return nullptr;
+  if (!ensure(c, &c->stage, &c->stage_bytes, host.size(), "tp_stage_malloc", err, cap) ||
+      !cuda_ok(c, cudaMalloc((void**)&v->dev, v->geom.total_bytes), "tp_shard_malloc", err, cap))
+    return nullptr;
+  v->dev_bytes = v->geom.total_bytes;
+  v->tiled = true;
+  m.shards.push_back(std::move(v));
+  Upload* w = m.shards.back().get();
+  if (!cuda_ok(c, cudaMemsetAsync(w->dev, 0, w->dev_bytes, c->stream), "tp_shard_memset", err, cap) ||
+      !cuda_ok(c, cudaMemcpyAsync(c->stage, host.data(), host.size(), cudaMemcpyHostToDevice, c->stream), "tp_shard_h2d",
+               err, cap) ||
+      !cuda_ok(c, launch_relayout(c->stage, w->dev, w->geom, nrb, c->stream), "tp_shard_relayout", err, cap) ||
+      !cuda_ok(c, cudaStreamSynchronize(c->stream), "tp_shard_sync", err, cap))
+    return nullptr;
+  return w;
+}
+
+// Replaces the model's global tensors by this rank's shards and its config
+// by the local dims.  Column-parallel (output rows): q/k/v by heads, gate/up
+// by 256-value FFN blocks, the lm_head by vocab rows.  Row-parallel (input
+// columns): o by this rank's heads, down by its FFN blocks.  Norms and the
+// embedding are replicated.  peer_handles: world x cudaIpcMemHandle_t of
+// every rank's exchange buffer (this rank's entry is its own).
+int shard_model(Ctx* c, Model& m, int rank, int world, const uint8_t* peer_handles, char* err, size_t cap) {
+  minicpmo_qwen3_config& cf = m.cfg;
+  if (world > kTpMaxWorld || rank < 0 || rank >= world || !peer_handles)
+    return fail(c, err, cap, "error: qwen3 bind_tp: bad rank=%d world=%d", rank, world);
+  if (!c->tp_buf || c->tp_buf_hidden != cf.hidden)
+    return fail(c, err, cap, "error: qwen3 bind_tp: export the exchange buffer (tp_buffer) for hidden=%u first", cf.hidden);
+  if (cf.heads % world || cf.kv_heads % world || cf.ffn % 256)
+    return fail(c, err, cap, "error: qwen3 bind_tp: heads=%u kv_heads=%u ffn=%u do not split over %d ranks", cf.heads,
+                cf.kv_heads, cf.ffn, world);
+  const size_t hd = cf.head_dim, heads_r = cf.heads / world, kv_r = cf.kv_heads / world;
+  if ((heads_r * hd) % 256)
+    return fail(c, err, cap, "error: qwen3 bind_tp: a rank's q columns (%zu) must be a multiple of 256", heads_r * hd);
+  const size_t nsb = cf.ffn / 256, sb0 = nsb * rank / world, sb1 = nsb * (rank + 1) / world;
+  if (sb1 <= sb0) return fail(c, err, cap, "error: qwen3 bind_tp: ffn too small for %d ranks", world);
+  if (!m.out->tiled) return fail(c, err, cap, "error: qwen3 bind_tp: the lm_head must be quantised");
+  const size_t V = cf.vocab, rpo = (size_t)m.out->geom.rpw;
+  const size_t v0 = V * rank / world / rpo * rpo, v1 = rank + 1 == world ? V : V * (rank + 1) / world / rpo * rpo;
+  for (LayerW& L : m.layer) {
+    Upload* q = row_view(m, L.q, rank * heads_r * hd, (rank + 1) * heads_r * hd);
+    Upload* k = row_view(m, L.k, rank * kv_r * hd, (rank + 1) * kv_r * hd);
+    Upload* v = row_view(m, L.v, rank * kv_r * hd, (rank + 1) * kv_r * hd);
+    Upload* g = row_view(m, L.gate, sb0 * 256, sb1 * 256);
+    Upload* u = row_view(m, L.up, sb0 * 256, sb1 * 256);
+    Upload* o = col_slice(c, m, L.o, rank * heads_r * hd, (rank + 1) * heads_r * hd, err, cap);
+    Upload* d = o ? col_slice(c, m, L.down, sb0 * 256, sb1 * 256, err, cap) : nullptr;
+    if (!q || !k || !v || !g || !u || !o || !d)
+      return fail(c, err, cap, "error: qwen3 bind_tp: cannot shard layer tensors (quantised weights required)");
+    L.q = q, L.k = k, L.v = v, L.gate = g, L.up = u, L.o = o, L.down = d;
+  }
+  m.out = row_view(m, m.out, v0, v1);
+  if (!m.out) return fail(c, err, cap, "error: qwen3 bind_tp: cannot shard the lm_head");
+  // exchange buffers: own and peers' (IPC)
+  TpPeers& p = m.peers;
+  p.rank = rank;
+  p.world = world;
+  for (int r = 0; r < world; ++r) {
+    uint8_t* base = nullptr;
+    if (r == rank) {
+      base = c->tp_buf;
+    } else {
+      cudaIpcMemHandle_t hnd;
+      memcpy(&hnd, peer_handles + (size_t)r * sizeof(cudaIpcMemHandle_t), sizeof(hnd));
+      void* ptr = nullptr;
+      if (!cuda_ok(c, cudaIpcOpenMemHandle(&ptr, hnd, cudaIpcMemLazyEnablePeerAccess), "tp_ipc_open", err, cap)) return 0;
+      m.peer_maps.push_back(ptr);
+      base = static_cast<uint8_t*>(ptr);
+    }
+    p.part[r][0] = reinterpret_cast<float*>(base + TpLayout::part_offset(0, cf.hidden));
+    p.part[r][1] = reinterpret_cast<float*>(base + TpLayout::part_offset(1, cf.hidden));
+    p.top[r] = reinterpret_cast<float*>(base + TpLayout::top_offset(cf.hidden));
+    p.flag[r] = reinterpret_cast<unsigned*>(base + TpLayout::flag_offset(cf.hidden));
+  }
+  if (!cuda_ok(c, cudaMalloc((void**)&m.tp_epoch, sizeof(unsigned)), "tp_epoch_malloc", err, cap) ||
+      !cuda_ok(c, cudaMemsetAsync(m.tp_epoch, 0, sizeof(unsigned), c->stream), "tp_epoch_memset", err, cap))
+    return 0;
+  m.tp_rank = rank;
+  m.tp_world = world;
+  m.vocab_global = cf.vocab;
+  m.vocab_base = (uint32_t)v0;
+  cf.heads = (uint32_t)heads_r;
+  cf.kv_heads = (uint32_t)kv_r;
+  cf.ffn = (uint32_t)((sb1 - sb0) * 256);
+  cf.vocab = (uint32_t)(v1 - v0);
+  m.qd = heads_r * hd;
+  m.kvd = kv_r * hd;
+  return 1;
+}
+
+int bind_model(Ctx* c, const minicpmo_qwen3_config* cfg, char* err, size_t cap, int tp_rank = 0, int tp_world = 1,
+               const uint8_t* peer_handles = nullptr) {
   if (!cfg) return fail(c, err, cap, "error: qwen3 bind: null config");
   const auto& cf = *cfg;
   if (cf.layers == 0 || cf.hidden == 0 || cf.heads == 0 || cf.kv_heads == 0 || cf.head_dim == 0 || cf.ffn == 0 ||
@@ -770,12 +932,18 @@ int bind_model(Ctx* c, const minicpmo_qwen3_config* cfg, char* err, size_t cap) 
       !check_shape(c, m.out_norm, 1, cf.hidden, err, cap))
     return 0;
   if (is_quant(m.out_norm->dtype)) return fail(c, err, cap, "error: qwen3 bind: output_norm must be F32/F16/BF16");
-  // buffers
-  const size_t h = cf.hidden, f = cf.ffn, V = cf.vocab, hd = cf.head_dim;
+  if (tp_world > 1 && !shard_model(c, m, tp_rank, tp_world, peer_handles, err, cap)) {
+    free_model(&m);
+    return 0;
+  }
+  // buffers (this rank's dims under tensor parallelism)
+  const minicpmo_qwen3_config& lc = m.cfg;
+  const size_t h = lc.hidden, f = lc.ffn, V = lc.vocab, hd = lc.head_dim;
+  const size_t Vg = m.tp_world > 1 ? m.vocab_global : V;
   const size_t maxd = std::max(std::max(h, f), m.qd);
   m.kv_layer_elems = (size_t)cf.context * m.kvd;
   const size_t esz = cf.kv_f16 ? 2 : 4;
-  m.n_split = attn_n_split((int)cf.kv_heads);
+  m.n_split = attn_n_split((int)lc.kv_heads);
   m.am_grid = c->sm_count;
   m.history_cap = 1 << 16;
   struct A {
@@ -789,9 +957,9 @@ int bind_model(Ctx* c, const minicpmo_qwen3_config* cfg, char* err, size_t cap) 
       {(void**)&m.aq, (m.qd / 32 + 1) * 36}, {(void**)&m.fq, (f / 32 + 1) * 36},
       {&m.kc, cf.layers * m.kv_layer_elems * esz}, {&m.vc, cf.layers * m.kv_layer_elems * esz},
       {(void**)&m.rope_cos, (size_t)cf.context * (hd / 2) * 4}, {(void**)&m.rope_sin, (size_t)cf.context * (hd / 2) * 4},
-      {(void**)&m.partial, attn_partial_floats((int)cf.heads, m.n_split, (int)hd) * 4},
-      {(void**)&m.counters, cf.kv_heads * 4}, {(void**)&m.am_scratch, (size_t)m.am_grid * 3 * 4},
-      {(void**)&m.am_counter, 4}, {(void**)&m.st, sizeof(StepState)}, {(void**)&m.seen, (V / 32 + 1) * 4},
+      {(void**)&m.partial, attn_partial_floats((int)lc.heads, m.n_split, (int)hd) * 4},
+      {(void**)&m.counters, lc.kv_heads * 4}, {(void**)&m.am_scratch, (size_t)m.am_grid * 3 * 4},
+      {(void**)&m.am_counter, 4}, {(void**)&m.st, sizeof(StepState)}, {(void**)&m.seen, (Vg / 32 + 1) * 4},
       {(void**)&m.history, (size_t)m.history_cap * 4},
   };
   for (auto& a : allocs) {
@@ -836,7 +1004,7 @@ int bind_model(Ctx* c, const minicpmo_qwen3_config* cfg, char* err, size_t cap) 
     free_model(&m);
     return 0;
   }
-  m.step_ok = cf.decode_mode == 2 && build_step_plan(c, m);
+  m.step_ok = cf.decode_mode == 2 && m.tp_world == 1 && build_step_plan(c, m);
   if (m.step_ok && (!build_graph(c, m, 0, err, cap) || !build_graph(c, m, 1, err, cap))) {
     // the persistent kernel could not be captured: fall back to the
     // per-kernel graph (same arithmetic)
@@ -938,7 +1106,8 @@ void minicpmo_gpu_context_destroy(void* handle) {
     for (auto& s : c->slots)
       if (s.ptr) cudaFree(s.ptr);
     void* bufs[] = {c->stage, c->xq, c->sx, c->sy, c->dots, c->k_cache, c->v_cache, c->attn_partial, c->attn_counters,
-                    c->rope_cos, c->rope_sin, c->am_scratch, c->am_counter, c->am_state, c->am_seen, c->dev_err};
+                    c->rope_cos, c->rope_sin, c->am_scratch, c->am_counter, c->am_state, c->am_seen, c->dev_err,
+                    c->tp_buf};
     for (void* p : bufs)
       if (p) cudaFree(p);
     if (c->am_state_host) cudaFreeHost(c->am_state_host);
@@ -1491,6 +1660,39 @@ int minicpmo_gpu_context_qwen3_bind(void* handle, const minicpmo_qwen3_config* c
   return bind_model(c, config, error, error_cap);
 }
 
+int minicpmo_gpu_context_tp_buffer(void* handle, size_t hidden, void* ipc_handle_out, char* error, size_t error_cap) {
+  Ctx* c = (Ctx*)handle;
+  if (!c) return copy_error(error, error_cap, "error: null gpu context"), 0;
+  DeviceGuard g(c);
+  if (hidden == 0 || hidden > (1u << 24) || !ipc_handle_out)
+    return fail(c, error, error_cap, "error: tp_buffer: bad hidden=%zu or null handle output", hidden);
+  if (c->model && c->model->tp_world > 1)
+    return fail(c, error, error_cap, "error: tp_buffer: a tensor-parallel model is bound to this buffer");
+  if (c->tp_buf && c->tp_buf_hidden != hidden) {
+    cudaFree(c->tp_buf);
+    c->tp_buf = nullptr;
+  }
+  const size_t bytes = TpLayout::bytes(hidden);
+  if (!c->tp_buf && !cuda_ok(c, cudaMalloc((void**)&c->tp_buf, bytes), "tp_buffer_malloc", error, error_cap)) return 0;
+  c->tp_buf_hidden = hidden;
+  cudaIpcMemHandle_t h;
+  if (!cuda_ok(c, cudaMemsetAsync(c->tp_buf, 0, bytes, c->stream), "tp_buffer_memset", error, error_cap) ||
+      !cuda_ok(c, cudaStreamSynchronize(c->stream), "tp_buffer_sync", error, error_cap) ||
+      !cuda_ok(c, cudaIpcGetMemHandle(&h, c->tp_buf), "tp_buffer_ipc_handle", error, error_cap))
+    return 0;
+  memcpy(ipc_handle_out, &h, sizeof(h));
+  return 1;
+}
+
+int minicpmo_gpu_context_qwen3_bind_tp(void* handle, const minicpmo_qwen3_config* config, int rank, int world,
+                                       const void* peer_ipc_handles, char* error, size_t error_cap) {
+  Ctx* c = (Ctx*)handle;
+  if (!c) return copy_error(error, error_cap, "error: null gpu context"), 0;
+  DeviceGuard g(c);
+  if (world <= 1) return bind_model(c, config, error, error_cap);
+  return bind_model(c, config, error, error_cap, rank, world, static_cast<const uint8_t*>(peer_ipc_handles));
+}
+
 int minicpmo_gpu_context_qwen3_forward(void* handle, uint32_t token, size_t pos, int flags, float repeat_penalty,
                                        uint32_t* out_token, float* out_top2_gap, float* logits_out, float* hidden_out,
                                        char* error, size_t error_cap) {
@@ -1501,7 +1703,8 @@ int minicpmo_gpu_context_qwen3_forward(void* handle, uint32_t token, size_t pos,
   Model& m = *c->model;
   if (pos >= m.cfg.context)
     return fail(c, error, error_cap, "error: qwen3 forward pos=%zu exceeds runtime_context=%u", pos, m.cfg.context);
-  if (token >= m.cfg.vocab) return fail(c, error, error_cap, "error: qwen3 forward token=%u >= vocab=%u", token, m.cfg.vocab);
+  if (token >= vocab_of(m))
+    return fail(c, error, error_cap, "error: qwen3 forward token=%u >= vocab=%u", token, vocab_of(m));
   const int which = (flags & 1) ? 1 : 0;
   StepState* hs = m.st_host;
   memset(hs, 0, sizeof(StepState));
@@ -1516,8 +1719,9 @@ int minicpmo_gpu_context_qwen3_forward(void* handle, uint32_t token, size_t pos,
     return 0;
   c->stats.host_to_device_bytes += sizeof(StepState);
   c->stats.device_to_host_bytes += sizeof(StepState);
-  if (logits_out && which == 0) {
-    if (!cuda_ok(c, cudaMemcpyAsync(logits_out, m.logits, (size_t)m.cfg.vocab * 4, cudaMemcpyDeviceToHost, c->stream),
+  if (logits_out && which == 0) {  // under tensor parallelism: this rank's slice, at its offset
+    if (!cuda_ok(c, cudaMemcpyAsync(logits_out + m.vocab_base, m.logits, (size_t)m.cfg.vocab * 4, cudaMemcpyDeviceToHost,
+                                    c->stream),
                  "forward_logits_d2h", error, error_cap))
       return 0;
     c->stats.device_to_host_bytes += (size_t)m.cfg.vocab * 4;
@@ -1542,7 +1746,7 @@ int minicpmo_gpu_context_qwen3_reset(void* handle, char* error, size_t error_cap
   DeviceGuard g(c);
   if (!c->model) return fail(c, error, error_cap, "error: qwen3 reset: model not bound");
   Model& m = *c->model;
-  return cuda_ok(c, cudaMemsetAsync(m.seen, 0, ((size_t)m.cfg.vocab / 32 + 1) * 4, c->stream), "reset_memset", error,
+  return cuda_ok(c, cudaMemsetAsync(m.seen, 0, ((size_t)vocab_of(m) / 32 + 1) * 4, c->stream), "reset_memset", error,
                  error_cap) &&
                  cuda_ok(c, cudaStreamSynchronize(c->stream), "reset_sync", error, error_cap)
              ? 1
@@ -1561,7 +1765,7 @@ int decode_loop(Ctx* c, uint32_t first_token, size_t first_pos, size_t n_steps, 
     return fail(c, error, error_cap, "error: qwen3 decode exceeds context pos=%zu steps=%zu context=%u", first_pos, n_steps,
                 m.cfg.context);
   if (n_steps > (size_t)m.history_cap) return fail(c, error, error_cap, "error: qwen3 decode: too many steps");
-  if (first_token >= m.cfg.vocab) return fail(c, error, error_cap, "error: qwen3 decode: token out of range");
+  if (first_token >= vocab_of(m)) return fail(c, error, error_cap, "error: qwen3 decode: token out of range");
   StepState* hs = m.st_host;
   memset(hs, 0, sizeof(StepState));
   hs->token = (int)first_token;

@@ -162,18 +162,19 @@ __device__ __forceinline__ Top2 warp_merge(Top2 t) {
 
 __global__ void __launch_bounds__(256) k_argmax(const float* __restrict__ logits, int n, const uint32_t* seen_bits,
                                                 float* scratch, unsigned* counter, StepState* st, int* history,
-                                                int history_cap) {
+                                                int history_cap, int vocab_base, float* tp_top) {
   pdl_wait();
   pdl_launch_dependents();
   const float penalty = st->penalty;
   Top2 t{-INFINITY, 0x7fffffff, -INFINITY};
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
     float v = logits[i];
-    if (penalty > 1.0f && seen_bits && ((seen_bits[i >> 5] >> (i & 31)) & 1u)) {
+    const int gi = i + vocab_base;  // global vocab index (a tensor-parallel slice starts at vocab_base)
+    if (penalty > 1.0f && seen_bits && ((seen_bits[gi >> 5] >> (gi & 31)) & 1u)) {
       if (v > 0.0f) v = __fdiv_rn(v, penalty);
       if (v < 0.0f) v = __fmul_rn(v, penalty);
     }
-    Top2 u{v, i, -INFINITY};
+    Top2 u{v, gi, -INFINITY};
     t = merge(t, u);
   }
   t = warp_merge(t);
@@ -205,11 +206,17 @@ __global__ void __launch_bounds__(256) k_argmax(const float* __restrict__ logits
   if (threadIdx.x == 0) {
     Top2 f = ws[0];
     for (int w = 1; w < 8; ++w) f = merge(f, ws[w]);
+    *counter = 0u;
+    if (tp_top) {  // a slice of the vocab: the cross-rank merge finishes the step
+      tp_top[0] = f.b;
+      tp_top[1] = __int_as_float(f.i);
+      tp_top[2] = f.s;
+      return;
+    }
     if (f.i < 0 || f.i >= n) {  // every value NaN: report token 0 and flag it
       f.i = 0;
       st->err = 1;
     }
-    *counter = 0u;
     st->next_token = f.i;
     st->best = f.b;
     st->gap = f.b - f.s;
@@ -275,10 +282,11 @@ cudaError_t launch_embed(const uint8_t* w, const TileGeom& g, int dtype, int row
 }
 
 cudaError_t launch_argmax(const float* logits, int n, const uint32_t* seen_bits, float* scratch, unsigned* counter,
-                          StepState* st, int* history, int history_cap, int grid, cudaStream_t s, bool pdl) {
+                          StepState* st, int* history, int history_cap, int grid, cudaStream_t s, bool pdl,
+                          int vocab_base, float* tp_top) {
   if (grid <= 0) grid = 1;
   return launch_k(k_argmax, dim3(grid), dim3(256), 0, s, pdl, logits, n, seen_bits, scratch, counter, st, history,
-                  history_cap);
+                  history_cap, vocab_base, tp_top);
 }
 
 cudaError_t launch_mark_seen(uint32_t* bits, const StepState* st, int vocab, cudaStream_t s, bool pdl) {

@@ -29,8 +29,11 @@ cudaError_t launch_embed(const uint8_t* w, const TileGeom& g, int dtype, int row
                          float* out, cudaStream_t st, bool pdl = false);
 // grid CTAs; scratch holds 3 floats per CTA; counter is zero at rest.
 // history (may be null) receives next_token at history_len when auto-advancing.
+// vocab_base/tp_top: a tensor-parallel vocab slice -- indices are offset by
+// vocab_base and the result (best, index, second) goes to tp_top instead of st.
 cudaError_t launch_argmax(const float* logits, int n, const uint32_t* seen_bits, float* scratch, unsigned* counter,
-                          StepState* st, int* history, int history_cap, int grid, cudaStream_t s, bool pdl = false);
+                          StepState* st, int* history, int history_cap, int grid, cudaStream_t s, bool pdl = false,
+                          int vocab_base = 0, float* tp_top = nullptr);
 cudaError_t launch_mark_seen(uint32_t* bits, const StepState* st, int vocab, cudaStream_t s, bool pdl = false);
 cudaError_t launch_add_inplace(float* dst, const float* src, int n, cudaStream_t st);
 cudaError_t launch_silu_mul(float* dst, const float* gate, const float* up, int n, cudaStream_t st);

@@ -124,6 +124,8 @@ SIGNATURES = {
     "minicpmo_gpu_context_embed_lookup": (i32, [vp, C.c_uint, vp, i32, u32, sz] + E),
     "minicpmo_gpu_context_argmax_penalized": (i32, [vp, C.c_uint, sz, u32ptr, sz, f32, u32ptr, fptr] + E),
     "minicpmo_gpu_context_qwen3_bind": (i32, [vp, C.POINTER(Qwen3Config)] + E),
+    "minicpmo_gpu_context_tp_buffer": (i32, [vp, sz, vp] + E),
+    "minicpmo_gpu_context_qwen3_bind_tp": (i32, [vp, C.POINTER(Qwen3Config), i32, i32, vp] + E),
     "minicpmo_gpu_context_qwen3_forward": (i32, [vp, u32, sz, i32, f32, u32ptr, fptr, fptr, fptr] + E),
     "minicpmo_gpu_context_qwen3_reset": (i32, [vp] + E),
     "minicpmo_gpu_context_qwen3_decode": (i32, [vp, u32, sz, sz, f32, u32ptr] + E),
@@ -315,6 +317,21 @@ class GpuContext:
     def qwen3_bind(self, cfg: Qwen3Config) -> None:
         self._keep["qwen3_cfg"] = cfg
         self._call("minicpmo_gpu_context_qwen3_bind", C.byref(cfg))
+
+    def tp_buffer(self, hidden: int) -> bytes:
+        """Allocate this rank's tensor-parallel exchange buffer; returns its 64-byte CUDA IPC handle."""
+        h = C.create_string_buffer(64)
+        self._call("minicpmo_gpu_context_tp_buffer", hidden, C.cast(h, C.c_void_p))
+        return h.raw
+
+    def qwen3_bind_tp(self, cfg: Qwen3Config, rank: int, world: int, handles: Sequence[bytes]) -> None:
+        blob = b"".join(handles)
+        if len(blob) != 64 * world:
+            raise GpuError("error: qwen3_bind_tp needs one 64-byte handle per rank")
+        buf = C.create_string_buffer(blob, len(blob))
+        self._keep["qwen3_cfg"] = cfg
+        self._keep["tp_handles"] = buf
+        self._call("minicpmo_gpu_context_qwen3_bind_tp", C.byref(cfg), rank, world, C.cast(buf, C.c_void_p))
 
     def qwen3_forward(self, token: int, pos: int, logits: bool = True, penalty: float = 1.0,
                       want_logits: Optional[np.ndarray] = None, want_hidden: Optional[np.ndarray] = None):

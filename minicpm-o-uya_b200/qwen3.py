@@ -49,10 +49,13 @@ class Qwen3Runtime:
 
     @classmethod
     def open(cls, weights, shape: Optional[Qwen3Shape] = None, device_index: int = 0, kv_f16: bool = False,
-             context: Optional[int] = None, debug: bool = False, decode_mode: int = 0) -> "Qwen3Runtime":
+             context: Optional[int] = None, debug: bool = False, decode_mode: int = 0,
+             tp: Optional["TensorParallel"] = None) -> "Qwen3Runtime":
         """weights: a GGUF path/GgufFile, or a list of (name, dtype, rows, cols, uint8 bytes).
         decode_mode 0: the default (one kernel per operation); 1: one kernel per operation; 2: one
-        persistent kernel per decode step where the model fits it (same results in every mode)."""
+        persistent kernel per decode step where the model fits it (same results in every mode).
+        tp: tensor parallelism over the ranks of one node (`TensorParallel`, one process per GPU);
+        every rank opens with the same weights and drives the same tokens."""
         if isinstance(weights, (str,)) or hasattr(weights, "__fspath__"):
             weights = GgufFile(weights)
         if isinstance(weights, GgufFile):
@@ -78,7 +81,12 @@ class Qwen3Runtime:
         cfg.rope_freq_scale = 1.0
         cfg.kv_f16 = int(kv_f16)
         cfg.decode_mode = int(decode_mode)
-        gpu.qwen3_bind(cfg)
+        if tp is not None and tp.world > 1:
+            handles = tp.all_gather(gpu.tp_buffer(shape.hidden))
+            gpu.qwen3_bind_tp(cfg, tp.rank, tp.world, handles)
+            tp.all_gather(b"")  # every rank bound (exchange flags zeroed) before any decodes
+        else:
+            gpu.qwen3_bind(cfg)
         return cls(shape=shape, gpu=gpu, tensors=tensors, context=ctx)
 
     def close(self) -> None:
@@ -184,3 +192,30 @@ def format_bench_lines(r: Dict[str, float], repetitions: int, stats: dict) -> Li
         f"weights_device_bytes={stats['weight_upload_bytes']} kv_device_bytes={stats['kv_device_bytes']}",
         "bench: PASS",
     ]
+
+
+class TensorParallel:
+    """Rank, world size and an all-gather of small byte strings between the ranks of one node.
+
+    The default all-gather uses the initialised ``torch.distributed`` process group (any backend);
+    a host embedding the library can pass its own (``gather(bytes) -> list of bytes in rank order``).
+    """
+
+    def __init__(self, rank: int, world: int, gather=None):
+        self.rank, self.world = int(rank), int(world)
+        self._gather = gather
+
+    def all_gather(self, blob: bytes) -> List[bytes]:
+        if self._gather is not None:
+            return list(self._gather(blob))
+        import torch.distributed as dist
+
+        out: List[object] = [None] * self.world
+        dist.all_gather_object(out, bytes(blob))
+        return [bytes(b) for b in out]
+
+    @classmethod
+    def from_env(cls) -> "TensorParallel":
+        import os
+
+        return cls(int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")))

@@ -1,0 +1,74 @@
+"""Tensor-parallel decode worker, launched by tests/test_gpu_tp.py under
+torch.distributed.run (one process per GPU).  Every rank binds its shards of
+the same seeded model and decodes the same teacher-forced tokens; rank 0 also
+runs the single-GPU runtime and prints one JSON line comparing the two."""
+from __future__ import annotations
+
+import json
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+sys.path.insert(0, str(Path(__file__).resolve().parent))
+from conftest import load_pkg, rel_row_err  # noqa: E402
+
+
+def main() -> int:
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    import datetime
+
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
+    load_pkg()
+    from minicpmo_b200 import gguf
+    from minicpmo_b200.qwen3 import Qwen3Runtime, TensorParallel
+
+    steps = int(os.environ.get("TP_STEPS", "48"))
+    kv = max(2, world)  # every rank keeps >= 1 kv head and 512 q columns
+    shape = gguf.Qwen3Shape(layers=2, hidden=512, heads=4 * kv, kv_heads=kv, head_dim=128, ffn=2048, vocab=2048,
+                            context=96)
+    tensors = gguf.synth_model(shape, gguf.Q4_K_M, seed_base=5)
+    rt = Qwen3Runtime.open(tensors, shape=shape, device_index=local, context=shape.context,
+                           tp=TensorParallel(rank, world))
+    ids = gguf.prompt_ids(steps, shape.vocab, seed=3)
+    lg = np.zeros(shape.vocab, np.float32)
+    toks, gaps, slices = [], [], []
+    for pos in range(steps):
+        t, g = rt.forward(int(ids[pos]), pos, logits=True, want_logits=lg)
+        toks.append(int(t))
+        gaps.append(float(g))
+        slices.append(lg.copy())
+    dec = rt.gpu.qwen3_decode(int(ids[0]), steps, 16).tolist()
+    everyone = [None] * world
+    dist.all_gather_object(everyone, {"toks": toks, "dec": dec})
+    if rank == 0:
+        ref = Qwen3Runtime.open(tensors, shape=shape, device_index=local, context=shape.context)
+        rl = np.zeros(shape.vocab, np.float32)
+        mism, worst = 0, 0.0
+        lo, hi = None, None
+        for pos in range(steps):
+            t, g = ref.forward(int(ids[pos]), pos, logits=True, want_logits=rl)
+            nz = np.nonzero(slices[pos])[0]
+            lo, hi = (nz.min(), nz.max() + 1) if nz.size else (0, 0)
+            worst = max(worst, rel_row_err(slices[pos][lo:hi], rl[lo:hi]))
+            if t != toks[pos] and g > 1e-3:
+                mism += 1
+        ref_dec = ref.gpu.qwen3_decode(int(ids[0]), steps, 16).tolist()
+        agree = all(e["toks"] == toks and e["dec"] == dec for e in everyone)
+        print(json.dumps({"world": world, "ranks_agree": agree, "token_mismatch_large_gap": mism,
+                          "worst_logit_err": worst, "decode_equal": dec == ref_dec, "min_gap": min(gaps)}))
+        ref.close()
+    dist.barrier()  # no rank unmaps its exchange buffer while a peer may still read it
+    rt.close()
+    dist.barrier()
+    dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
