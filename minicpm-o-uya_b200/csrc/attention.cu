@@ -47,8 +47,8 @@ struct AttnSmem {
   float* kpos;  // [hd]
   float* vpos;  // [hd]
   float* sq;    // [kAttnWarps][256]
-  float* kt;    // [kSub][hd + 1]
-  float* vt;    // [kSub][hd + 1]
+  float* kt;    // [kSub][attn_tile_stride(hd)]
+  float* vt;    // [kSub][attn_tile_stride(hd)]
   float* cm;    // [kGMax][kMaxSplit]   (merge, aliases kt/vt)
   float* cl;    // [kGMax][kMaxSplit]
   float* cw;    // [kGMax][kMaxSplit]
@@ -56,8 +56,13 @@ struct AttnSmem {
   float* mp;    // [G][n_active][attn_part_stride(hd)] staged partials, 16-byte aligned
 };
 
+// K/V tile row stride: hd + 4 keeps rows 16-byte aligned (async 16-byte
+// copies, float4 reads) and lanes reading rows lane*hs conflict-free per
+// quarter warp; odd small head sizes use hd + 1 with scalar access.
+__host__ __device__ inline int attn_tile_stride(int hd) { return (hd & 3) ? hd + 1 : hd + 4; }
+
 __host__ __device__ inline size_t attn_tile_floats(int hd) {
-  const size_t kv = 2 * (size_t)kSub * (hd + 1);
+  const size_t kv = 2 * (size_t)kSub * attn_tile_stride(hd);
   const size_t merge = 3 * (size_t)kGMax * kMaxSplit + kGMax + 4 + kMergeStage;
   return kv > merge ? kv : merge;
 }
@@ -73,7 +78,7 @@ __device__ __forceinline__ AttnSmem carve(float* base, int hd) {
   s.vpos = s.kpos + hd;
   s.sq = s.vpos + hd;
   s.kt = s.sq + kAttnWarps * 256;
-  s.vt = s.kt + kSub * (hd + 1);
+  s.vt = s.kt + kSub * attn_tile_stride(hd);
   s.cm = s.kt;
   s.cl = s.cm + kGMax * kMaxSplit;
   s.cw = s.cl + kGMax * kMaxSplit;
@@ -85,6 +90,55 @@ __device__ __forceinline__ AttnSmem carve(float* base, int hd) {
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+
+// f32 cache, hd % 4 == 0: rows [c0, c0 + kSub) of K and V into the tile with
+// L2-only 16-byte async copies (one commit group), rows >= t1 zero-filled.
+// The current position's row (fused mode) is skipped; the caller writes it
+// from kpos/vpos and then waits for the group.  False (nothing issued) when
+// the cache is f16 or the head size is not a multiple of 4.
+template <typename T>
+__device__ __forceinline__ bool stage_tile_async(const AttnArgs& a, const AttnSmem& sm, int c0, int t1, int pos,
+                                                 bool fused, int kv_dim, size_t kv_off, int hd, int hs) {
+  if constexpr (sizeof(T) != 4) {
+    return false;
+  } else {
+    if (hd & 3) return false;
+    const int per = hd >> 2;
+    const float* kc = static_cast<const float*>(a.k_cache);
+    const float* vc = static_cast<const float*>(a.v_cache);
+    for (int e = threadIdx.x; e < kSub * per; e += blockDim.x) {
+      const int r = e / per, d = (e - r * per) * 4, t = c0 + r;
+      float* kd = sm.kt + r * hs + d;
+      float* vd = sm.vt + r * hs + d;
+      if (t < t1) {
+        if (!(fused && t == pos)) {
+          const size_t i = (size_t)t * kv_dim + kv_off + d;
+          cp_async16(kd, kc + i);
+          cp_async16(vd, vc + i);
+        }
+      } else {
+        *reinterpret_cast<float4*>(kd) = make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4*>(vd) = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    return true;
+  }
+}
+
+// The current position's row from kpos/vpos into tile row pos - c0 (when it
+// falls in [c0, t1)), then the wait for the tile's async copies.
+__device__ __forceinline__ void finish_tile_async(const AttnSmem& sm, int c0, int t1, int pos, bool fused, int hd,
+                                                  int hs) {
+  if (fused && pos >= c0 && pos < t1) {
+    const int r = pos - c0;
+    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+      sm.kt[r * hs + d] = sm.kpos[d];
+      sm.vt[r * hs + d] = sm.vpos[d];
+    }
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
 template <typename T>
@@ -110,7 +164,7 @@ template <int J, typename T>
 __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a) {
   extern __shared__ __align__(16) float smem_f[];
   const int hd = a.head_dim;
-  const int hs = hd + 1;  // padded row stride (conflict-free column reads)
+  const int hs = attn_tile_stride(hd);
   const AttnSmem sm = carve(smem_f, hd);
   const int kvh = blockIdx.x, split = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -133,11 +187,13 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a)
 
   // Before waiting for the previous kernel (programmatic dependent launch):
   // everything that only depends on earlier steps -- the position, the K/V
-  // rows of earlier positions for the first sub-chunk (into registers; the
-  // current position comes from this kernel's prologue), and the norm weight
-  // and RoPE lines (into L1).
+  // rows of earlier positions for the first sub-chunk (f32 cache: async
+  // copies straight into the tile; f16: into registers; the current position
+  // comes from this kernel's prologue), and the norm weight and RoPE lines
+  // (into L1).
+  const bool tile_async = active && stage_tile_async<T>(a, sm, t0, t1, pos, fused, kv_dim, kv_off, hd, hs);
   const int n4 = kSub * hd / 4;
-  const bool early = active && (hd & 3) == 0 && n4 <= 8 * nt;
+  const bool early = active && !tile_async && (hd & 3) == 0 && n4 <= 8 * nt;
   float4 pk[8], pv[8];
   if (early) {
 #pragma unroll
@@ -236,7 +292,12 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a)
       // stage K and V rows of this sub-chunk (the current position from
       // smem): groups of 4 values, all loads of a batch issued before the
       // shared-memory stores
-      if (early && c0 == t0) {
+      if (tile_async && c0 == t0) {
+        finish_tile_async(sm, c0, t1, pos, fused, hd, hs);
+      } else if (tile_async && c0 > t0) {
+        stage_tile_async<T>(a, sm, c0, t1, pos, fused, kv_dim, kv_off, hd, hs);
+        finish_tile_async(sm, c0, t1, pos, fused, hd, hs);
+      } else if (early && c0 == t0) {
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
           const int e = threadIdx.x + u * nt;
@@ -265,7 +326,19 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a)
         if (g >= G) break;
         const float* qrow = sm.q + g * hd;
         float sc = 0.0f;
-        for (int d = 0; d < hd; ++d) sc = __fmaf_rn(qrow[d], sm.kt[lane * hs + d], sc);
+        if ((hs & 3) == 0) {  // 16-byte reads, the same sequential order over d
+          const float4* kr = reinterpret_cast<const float4*>(sm.kt + lane * hs);
+          const float4* qr = reinterpret_cast<const float4*>(qrow);
+          for (int d4 = 0; d4 < (hd >> 2); ++d4) {
+            const float4 k4 = kr[d4], q4 = qr[d4];
+            sc = __fmaf_rn(q4.x, k4.x, sc);
+            sc = __fmaf_rn(q4.y, k4.y, sc);
+            sc = __fmaf_rn(q4.z, k4.z, sc);
+            sc = __fmaf_rn(q4.w, k4.w, sc);
+          }
+        } else {
+          for (int d = 0; d < hd; ++d) sc = __fmaf_rn(qrow[d], sm.kt[lane * hs + d], sc);
+        }
         sc = valid ? __fmul_rn(sc, a.scale) : -INFINITY;
         const float mx = warp_max(sc);
         const float mn = fmaxf(m[i], mx);
@@ -278,9 +351,34 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a)
         for (int j = 0; j < J; ++j) acc[i][j] = __fmul_rn(acc[i][j], alpha);
         for (int tt = 0; tt < kSub; ++tt) {
           const float pt = __shfl_sync(0xffffffffu, p, tt);
-          if (act)
+          if (act) {
+            float vv[J];
+            const float* vr = sm.vt + tt * hs + lane * J;
+            if constexpr (J % 4 == 0) {
+              if ((hs & 3) == 0) {
 #pragma unroll
-            for (int j = 0; j < J; ++j) acc[i][j] = __fmaf_rn(pt, sm.vt[tt * hs + lane * J + j], acc[i][j]);
+                for (int j = 0; j < J; j += 4) {
+                  const float4 v4 = *reinterpret_cast<const float4*>(vr + j);
+                  vv[j] = v4.x; vv[j + 1] = v4.y; vv[j + 2] = v4.z; vv[j + 3] = v4.w;
+                }
+              } else {
+#pragma unroll
+                for (int j = 0; j < J; ++j) vv[j] = vr[j];
+              }
+            } else if constexpr (J == 2) {
+              if ((hs & 3) == 0) {
+                const float2 v2 = *reinterpret_cast<const float2*>(vr);
+                vv[0] = v2.x; vv[1] = v2.y;
+              } else {
+                vv[0] = vr[0]; vv[1] = vr[1];
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < J; ++j) vv[j] = vr[j];
+            }
+#pragma unroll
+            for (int j = 0; j < J; ++j) acc[i][j] = __fmaf_rn(pt, vv[j], acc[i][j]);
+          }
         }
       }
       __syncthreads();
