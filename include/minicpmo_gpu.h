@@ -268,8 +268,8 @@ MINICPMO_API size_t minicpmo_gpu_context_tensor_device_bytes(void *handle, const
 /* Limits of the fixed scratch the entry below uses instead of allocating:
  * at most 1024 KV heads, and head_count x n_split x (head_dim + 4) x 4 bytes
  * of split-K partial sums at most 2 MiB (n_split = clamp(ceil(256 /
- * kv_head_count), 1, 64); Qwen3-32B's 64 heads / 8 KV heads / head_dim 128
- * need 1.03 MiB).  Larger shapes are rejected with an error. */
+ * kv_head_count), 1, 8); Qwen3-32B's 64 heads / 8 KV heads / head_dim 128
+ * need 264 KiB).  Larger shapes are rejected with an error. */
 #define MINICPMO_NOALLOC_MAX_KV_HEADS 1024
 #define MINICPMO_NOALLOC_PARTIAL_BYTES (2u << 20)
 

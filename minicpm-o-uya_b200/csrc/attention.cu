@@ -5,23 +5,37 @@
 // softmax over t, out = sum_t p_t v_t.  KV cache layout [layer][pos][kv_dim]
 // as the reference (qwen3.uya:1664-1666), f32 (reference) or f16.
 //
-// B200 design: split-K flash decoding.  grid = (n_kv, n_split); a CTA owns one
-// kv head and a contiguous range of positions, serves every q head of its
-// GQA group from one pass over K and V (each K/V row is read once per
-// token), keeps an online softmax per head in registers and writes one
-// partial (m, l, acc) per head.  The last CTA to finish a kv head (atomic
-// ticket) merges the partials, writes the f32 output and, optionally, its
-// Q8_1 blocks for the o-projection -- no separate combine launch.
+// B200 design: split-K flash decoding.  grid = (n_kv, n_split, batch); a CTA
+// owns one kv head of one sequence and a contiguous range of positions,
+// serves every q head of its GQA group from one pass over K and V (each K/V
+// row is read once per token), keeps an online softmax per head in
+// registers and produces one partial (m, l, acc) per head.  The partials of
+// a kv head are merged either inside a thread-block cluster through
+// distributed shared memory (the default of the decode graph) or by the
+// last-arriving CTA through global memory (atomic ticket); both merge in
+// split order with the same operations, so they give the same bits.  The
+// merge writes the f32 output and, optionally, its Q8_1 blocks for the
+// o-projection -- no separate combine launch.
+//
+// K/V rows reach shared memory by 16-byte asynchronous copies (L2 only) in
+// the cache's own type, into a ring of 32-position tiles: the first tiles
+// are requested before the kernel waits for its predecessor (programmatic
+// dependent launch), and each later tile is requested while the tile before
+// it is being used.
 //
 // Fused mode also performs, for the current position, the per-head
 // QK-RMSNorm (qwen3.uya:1543-1558, eps 1e-6, reduction order of
 // gpu_shim.c:719-745 with an exact 1/sqrtf), NeoX RoPE from the host-built
 // cos/sin table (qwen3.uya:1605-1662) and the KV append
 // (qwen3.uya:1668-1675), so q/k never round-trip through separate kernels.
+// The current position is attended as the cache stores it (f16: rounded).
 #include "attention.cuh"
 
 #include <cuda_fp16.h>
 #include <math.h>
+#include <string.h>
+
+#include <type_traits>
 
 #include "attn_dev.cuh"
 #include "common.cuh"
@@ -34,118 +48,217 @@ namespace mcpo {
 namespace {
 
 constexpr int kAttnWarps = 4;
-constexpr int kGMax = 8;     // q heads per kv head handled by one CTA (<= 2 per warp)
+constexpr int kGMax = 8;  // q heads per kv head handled by one CTA (<= 2 per warp)
 constexpr int kMaxSplit = 64;
 
-// The split merge reuses the K/V tile area: per q head of the group the
+// The global-memory merge reuses the tile area: per q head of the group the
 // splits' m, l and weights, 1/L, and (when they fit) a copy of every split's
-// partial row; the merged output rows reuse the q area.
+// partial row.
 constexpr int kMergeStage = 12288;  // floats of staged partial rows (48 KB)
 
-struct AttnSmem {
-  float* q;     // [kGMax][hd]; the merged rows after the merge
-  float* kpos;  // [hd]
-  float* vpos;  // [hd]
-  float* sq;    // [kAttnWarps][256]
-  float* kt;    // [kSub][attn_tile_stride(hd)]
-  float* vt;    // [kSub][attn_tile_stride(hd)]
-  float* cm;    // [kGMax][kMaxSplit]   (merge, aliases kt/vt)
-  float* cl;    // [kGMax][kMaxSplit]
-  float* cw;    // [kGMax][kMaxSplit]
-  float* cinv;  // [kGMax]
-  float* mp;    // [G][n_active][attn_part_stride(hd)] staged partials, 16-byte aligned
-};
-
-// K/V tile row stride: hd + 4 keeps rows 16-byte aligned (async 16-byte
-// copies, float4 reads) and lanes reading rows lane*hs conflict-free per
-// quarter warp; odd small head sizes use hd + 1 with scalar access.
+// Small odd head sizes (J = 1, head_dim <= 32) stage f32 tiles through
+// registers with this row stride; the async tiles use head_dim + 16 bytes.
 __host__ __device__ inline int attn_tile_stride(int hd) { return (hd & 3) ? hd + 1 : hd + 4; }
 
-__host__ __device__ inline size_t attn_tile_floats(int hd) {
-  const size_t kv = 2 * (size_t)kSub * attn_tile_stride(hd);
-  const size_t merge = 3 * (size_t)kGMax * kMaxSplit + kGMax + 4 + kMergeStage;
-  return kv > merge ? kv : merge;
+// Tile geometry of one instantiation.  J >= 2 (head_dim 64/128/256): tiles
+// in the cache type TT, rows of head_dim + 16 bytes (16-byte aligned, and
+// lanes reading rows lane*stride hit distinct banks per quarter warp), a
+// ring of kRing tiles.  J = 1: one f32 tile staged through registers.
+template <int J, typename T>
+struct TileCfg {
+  static constexpr bool kAsync = J >= 2;
+  using TT = std::conditional_t<kAsync, T, float>;
+  static constexpr int kRing = kAsync ? (J >= 8 ? 2 : 3) : 1;
+  __host__ __device__ static int stride(int hd) { return kAsync ? hd + 16 / (int)sizeof(TT) : attn_tile_stride(hd); }
+  __host__ __device__ static size_t buf_bytes(int hd) { return 2 * (size_t)kSub * stride(hd) * sizeof(TT); }
+};
+
+__host__ __device__ inline size_t round16(size_t b) { return (b + 15) & ~(size_t)15; }
+
+// Shared memory: q [kGMax][hd], kpos [hd], vpos [hd], norm scratch
+// [kAttnWarps][256] (f32), then at tiles_offset the tile ring, which the
+// merge reuses (cluster: this split's partial rows [G][hd + 4]; global:
+// m/l/w [kGMax][kMaxSplit] x3, 1/L [kGMax], staged partial rows).
+__host__ __device__ inline size_t attn_tiles_offset(int hd) {
+  return round16(sizeof(float) * ((size_t)kGMax * hd + 2 * (size_t)hd + kAttnWarps * 256));
 }
 
-__host__ __device__ inline size_t attn_smem_floats(int hd) {
-  return (size_t)kGMax * hd + 2 * hd + kAttnWarps * 256 + attn_tile_floats(hd) + 4;
+__host__ __device__ inline size_t attn_merge_stage_offset() {
+  return round16(sizeof(float) * (3 * (size_t)kGMax * kMaxSplit + kGMax));
 }
 
-__device__ __forceinline__ AttnSmem carve(float* base, int hd) {
-  AttnSmem s;
-  s.q = base;
-  s.kpos = s.q + kGMax * hd;
-  s.vpos = s.kpos + hd;
-  s.sq = s.vpos + hd;
-  s.kt = s.sq + kAttnWarps * 256;
-  s.vt = s.kt + kSub * attn_tile_stride(hd);
-  s.cm = s.kt;
-  s.cl = s.cm + kGMax * kMaxSplit;
-  s.cw = s.cl + kGMax * kMaxSplit;
-  s.cinv = s.cw + kGMax * kMaxSplit;
-  const uintptr_t m = reinterpret_cast<uintptr_t>(s.cinv + kGMax);
-  s.mp = reinterpret_cast<float*>((m + 15) & ~static_cast<uintptr_t>(15));
-  return s;
+template <int J, typename T, bool kCluster>
+__host__ __device__ inline size_t attn_smem_bytes_t(int hd) {
+  using C = TileCfg<J, T>;
+  const size_t tiles = C::kRing * C::buf_bytes(hd);
+  const size_t merge = kCluster ? sizeof(float) * (size_t)kGMax * attn_part_stride(hd)
+                                : attn_merge_stage_offset() + sizeof(float) * (size_t)kMergeStage;
+  return attn_tiles_offset(hd) + (tiles > merge ? tiles : merge);
+}
+
+// Distributed shared memory: the address of `p` in the shared memory of
+// cluster CTA `rank`, a load from it, and a full cluster barrier (release /
+// acquire: shared-memory writes before it are visible to every CTA of the
+// cluster after it).
+__device__ __forceinline__ uint32_t dsmem_addr(const void* p, int rank) {
+  uint32_t a;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_addr(p)), "r"(rank));
+  return a;
+}
+
+__device__ __forceinline__ float dsmem_ld(uint32_t a) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(a) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
 }
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
 }
 
-// f32 cache, hd % 4 == 0: rows [c0, c0 + kSub) of K and V into the tile with
-// L2-only 16-byte async copies (one commit group), rows >= t1 zero-filled.
-// The current position's row (fused mode) is skipped; the caller writes it
-// from kpos/vpos and then waits for the group.  False (nothing issued) when
-// the cache is f16 or the head size is not a multiple of 4.
-template <typename T>
-__device__ __forceinline__ bool stage_tile_async(const AttnArgs& a, const AttnSmem& sm, int c0, int t1, int pos,
-                                                 bool fused, int kv_dim, size_t kv_off, int hd, int hs) {
-  if constexpr (sizeof(T) != 4) {
-    return false;
-  } else {
-    if (hd & 3) return false;
-    const int per = hd >> 2;
-    const float* kc = static_cast<const float*>(a.k_cache);
-    const float* vc = static_cast<const float*>(a.v_cache);
-    for (int e = threadIdx.x; e < kSub * per; e += blockDim.x) {
-      const int r = e / per, d = (e - r * per) * 4, t = c0 + r;
-      float* kd = sm.kt + r * hs + d;
-      float* vd = sm.vt + r * hs + d;
-      if (t < t1) {
-        if (!(fused && t == pos)) {
-          const size_t i = (size_t)t * kv_dim + kv_off + d;
-          cp_async16(kd, kc + i);
-          cp_async16(vd, vc + i);
-        }
-      } else {
-        *reinterpret_cast<float4*>(kd) = make_float4(0.f, 0.f, 0.f, 0.f);
-        *reinterpret_cast<float4*>(vd) = make_float4(0.f, 0.f, 0.f, 0.f);
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+template <typename TT>
+__device__ __forceinline__ TT to_tile(float v) {
+  if constexpr (sizeof(TT) == 2)
+    return __float2half_rn(v);
+  else
+    return v;
+}
+
+__device__ __forceinline__ float2 h2f2(uint32_t u) {
+  __half2 h;
+  memcpy(&h, &u, 4);
+  return __half22float2(h);
+}
+
+// Requests K/V rows [c0, c0 + kSub) of a cache in its own type into tile
+// buffer `buf` ([K rows][V rows], row stride hs elements) with 16-byte
+// asynchronous copies; rows >= t1 are zero-filled, and the current
+// position's row (fused mode) is left for put_pos_row.  No commit.
+template <typename TT>
+__device__ __forceinline__ void issue_tile(uint8_t* buf, const uint8_t* kc, const uint8_t* vc, int c0, int t1,
+                                           int pos, bool fused, int kv_dim, size_t kv_off, int hd, int hs) {
+  const int per = hd * (int)sizeof(TT) / 16;
+  const size_t rowb = (size_t)hs * sizeof(TT);
+  uint8_t* kt = buf;
+  uint8_t* vt = buf + kSub * rowb;
+  for (int e = threadIdx.x; e < kSub * per; e += blockDim.x) {
+    const int r = e / per, p = e - r * per, t = c0 + r;
+    uint8_t* kd = kt + r * rowb + p * 16;
+    uint8_t* vd = vt + r * rowb + p * 16;
+    if (t < t1) {
+      if (!(fused && t == pos)) {
+        const size_t off = ((size_t)t * kv_dim + kv_off) * sizeof(TT) + (size_t)p * 16;
+        cp_async16(kd, kc + off);
+        cp_async16(vd, vc + off);
       }
+    } else {
+      *reinterpret_cast<uint4*>(kd) = make_uint4(0u, 0u, 0u, 0u);
+      *reinterpret_cast<uint4*>(vd) = make_uint4(0u, 0u, 0u, 0u);
     }
-    asm volatile("cp.async.commit_group;" ::: "memory");
-    return true;
   }
 }
 
-// The current position's row from kpos/vpos into tile row pos - c0 (when it
-// falls in [c0, t1)), then the wait for the tile's async copies.
-__device__ __forceinline__ void finish_tile_async(const AttnSmem& sm, int c0, int t1, int pos, bool fused, int hd,
-                                                  int hs) {
-  if (fused && pos >= c0 && pos < t1) {
-    const int r = pos - c0;
+// The current position's row into the tile of sub-chunk [c0, c0 + kSub)
+// when it lies there (rounded to the tile type, as the cache stores it).
+template <typename TT>
+__device__ __forceinline__ void put_pos_row(uint8_t* buf, const float* kpos, const float* vpos, int c0, int t1,
+                                            int pos, bool fused, int hd, int hs) {
+  if (fused && pos >= c0 && pos < min(t1, c0 + kSub)) {
+    TT* kr = reinterpret_cast<TT*>(buf) + (size_t)(pos - c0) * hs;
+    TT* vr = kr + (size_t)kSub * hs;
     for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-      sm.kt[r * hs + d] = sm.kpos[d];
-      sm.vt[r * hs + d] = sm.vpos[d];
+      kr[d] = to_tile<TT>(kpos[d]);
+      vr[d] = to_tile<TT>(vpos[d]);
     }
   }
-  asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
-template <typename T>
-__device__ __forceinline__ void stage_kv(const AttnArgs& a, const AttnSmem& sm, int c0, int t1, int pos, bool fused,
-                                         int kv_dim, size_t kv_off, int hd, int hs) {
-  stage_kv_tile<T>(a.k_cache, a.v_cache, sm.kpos, sm.vpos, sm.kt, sm.vt, c0, t1, pos, fused, kv_dim, kv_off, hd, hs,
-                   threadIdx.x, blockDim.x);
+// s = sum_d q_d k_d as one sequential fma chain over d.
+template <typename TT>
+__device__ __forceinline__ float score_row(const float* q, const TT* k, int hd, int hs) {
+  float sc = 0.0f;
+  if constexpr (sizeof(TT) == 2) {  // hd % 8 == 0, 16-byte aligned rows
+    const uint4* k8 = reinterpret_cast<const uint4*>(k);
+    const float4* q4 = reinterpret_cast<const float4*>(q);
+    for (int i = 0; i < (hd >> 3); ++i) {
+      const uint4 u = k8[i];
+      const float4 qa = q4[2 * i], qb = q4[2 * i + 1];
+      float2 f = h2f2(u.x);
+      sc = __fmaf_rn(qa.x, f.x, sc);
+      sc = __fmaf_rn(qa.y, f.y, sc);
+      f = h2f2(u.y);
+      sc = __fmaf_rn(qa.z, f.x, sc);
+      sc = __fmaf_rn(qa.w, f.y, sc);
+      f = h2f2(u.z);
+      sc = __fmaf_rn(qb.x, f.x, sc);
+      sc = __fmaf_rn(qb.y, f.y, sc);
+      f = h2f2(u.w);
+      sc = __fmaf_rn(qb.z, f.x, sc);
+      sc = __fmaf_rn(qb.w, f.y, sc);
+    }
+  } else {
+    if ((hs & 3) == 0 && (hd & 3) == 0) {
+      const float4* k4 = reinterpret_cast<const float4*>(k);
+      const float4* q4 = reinterpret_cast<const float4*>(q);
+      for (int i = 0; i < (hd >> 2); ++i) {
+        const float4 kv = k4[i], qv = q4[i];
+        sc = __fmaf_rn(qv.x, kv.x, sc);
+        sc = __fmaf_rn(qv.y, kv.y, sc);
+        sc = __fmaf_rn(qv.z, kv.z, sc);
+        sc = __fmaf_rn(qv.w, kv.w, sc);
+      }
+    } else {
+      for (int d = 0; d < hd; ++d) sc = __fmaf_rn(q[d], k[d], sc);
+    }
+  }
+  return sc;
+}
+
+// J consecutive values of a V row (as f32).
+template <int J, typename TT>
+__device__ __forceinline__ void load_v(const TT* vr, float (&v)[J]) {
+  if constexpr (sizeof(TT) == 2) {
+    if constexpr (J == 8) {
+      const uint4 u = *reinterpret_cast<const uint4*>(vr);
+      float2 f = h2f2(u.x); v[0] = f.x; v[1] = f.y;
+      f = h2f2(u.y); v[2] = f.x; v[3] = f.y;
+      f = h2f2(u.z); v[4] = f.x; v[5] = f.y;
+      f = h2f2(u.w); v[6] = f.x; v[7] = f.y;
+    } else if constexpr (J == 4) {
+      const uint2 u = *reinterpret_cast<const uint2*>(vr);
+      float2 f = h2f2(u.x); v[0] = f.x; v[1] = f.y;
+      f = h2f2(u.y); v[2] = f.x; v[3] = f.y;
+    } else {
+      static_assert(J == 2, "f16 tiles serve J >= 2");
+      const float2 f = h2f2(*reinterpret_cast<const uint32_t*>(vr));
+      v[0] = f.x; v[1] = f.y;
+    }
+  } else {
+    if constexpr (J % 4 == 0) {
+#pragma unroll
+      for (int j = 0; j < J; j += 4) {
+        const float4 f = *reinterpret_cast<const float4*>(vr + j);
+        v[j] = f.x; v[j + 1] = f.y; v[j + 2] = f.z; v[j + 3] = f.w;
+      }
+    } else if constexpr (J == 2) {
+      const float2 f = *reinterpret_cast<const float2*>(vr);
+      v[0] = f.x; v[1] = f.y;
+    } else {
+#pragma unroll
+      for (int j = 0; j < J; ++j) v[j] = vr[j];
+    }
+  }
 }
 
 // J = output elements per lane in the P.V phase (hd = 32*J), or J = 1 with
@@ -160,54 +273,64 @@ __device__ __forceinline__ void stage_kv(const AttnArgs& a, const AttnSmem& sm, 
 //   acc_d = acc_d*alpha, then acc_d = fma(p_t, v_td, acc_d) for t in order
 // and the splits are merged as o_d = (sum_s w_s acc_sd) / (sum_s w_s l_s),
 // w_s = exp(m_s - max m), sums in split order with fma.
-template <int J, typename T>
+//
+// kCluster: the a.n_split CTAs of a kv head are one thread-block cluster;
+// each keeps its partial (m, l, acc) in shared memory and, after a cluster
+// barrier, merges 32-value units of the kv head's output (unit u on CTA
+// u mod n_split) reading every split's partial through distributed shared
+// memory -- no global scratch, no atomics, no second pass over global
+// memory.  Every thread of every CTA reaches both cluster barriers.
+template <int J, typename T, bool kCluster>
 __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a) {
-  extern __shared__ __align__(16) float smem_f[];
+  using C = TileCfg<J, T>;
+  using TT = typename C::TT;
+  constexpr int NT = C::kRing;
+  extern __shared__ __align__(16) uint8_t smem_b[];
   const int hd = a.head_dim;
-  const int hs = attn_tile_stride(hd);
-  const AttnSmem sm = carve(smem_f, hd);
-  const int kvh = blockIdx.x, split = blockIdx.y;
+  const int hs = C::stride(hd);
+  float* s_q = reinterpret_cast<float*>(smem_b);  // [kGMax][hd]; the merged rows after the merge
+  float* s_kpos = s_q + kGMax * hd;
+  float* s_vpos = s_kpos + hd;
+  float* s_sq = s_vpos + hd;  // [kAttnWarps][256]
+  uint8_t* s_tiles = smem_b + attn_tiles_offset(hd);
+  const size_t buf_bytes = C::buf_bytes(hd);
+
+  const int kvh = blockIdx.x, split = blockIdx.y, z = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int hb = (kvh * a.n_head + a.n_kv - 1) / a.n_kv;
   const int he = ((kvh + 1) * a.n_head + a.n_kv - 1) / a.n_kv;
   const int G = he - hb;
-  const int pos = a.pos_ptr ? *a.pos_ptr : a.pos_static;
+  const float* qp = a.q + (size_t)z * a.qkv_bstride;
+  const uint8_t* kc = static_cast<const uint8_t*>(a.k_cache) + (size_t)z * a.cache_bstride * sizeof(T);
+  const uint8_t* vc = static_cast<const uint8_t*>(a.v_cache) + (size_t)z * a.cache_bstride * sizeof(T);
+  float* outp = a.out + (size_t)z * a.out_bstride;
+  uint8_t* oq8 = a.out_q8 ? a.out_q8 + (size_t)z * a.outq8_bstride : nullptr;
+  const int pos = a.pos_ptr ? a.pos_ptr[z] : a.pos_static;
   const int n_pos = pos + 1;
   int chunk = (n_pos + a.n_split - 1) / a.n_split;
   if (chunk < 32) chunk = 32;
   const int n_active = (n_pos + chunk - 1) / chunk;
   const int t0 = split * chunk;
   const int t1 = min(t0 + chunk, n_pos);
+  const int nsub = split < n_active ? (t1 - t0 + kSub - 1) / kSub : 0;
   const int kv_dim = a.n_kv * hd;
   const size_t kv_off = (size_t)kvh * hd;
   const int stride_part = attn_part_stride(hd);
   const bool fused = a.fuse_norm_rope_append != 0;
-  const bool active = split < n_active;
+  const bool active = nsub > 0;
   const int nt = blockDim.x;
 
   // Before waiting for the previous kernel (programmatic dependent launch):
   // everything that only depends on earlier steps -- the position, the K/V
-  // rows of earlier positions for the first sub-chunk (f32 cache: async
-  // copies straight into the tile; f16: into registers; the current position
-  // comes from this kernel's prologue), and the norm weight and RoPE lines
-  // (into L1).
-  const bool tile_async = active && stage_tile_async<T>(a, sm, t0, t1, pos, fused, kv_dim, kv_off, hd, hs);
-  const int n4 = kSub * hd / 4;
-  const bool early = active && !tile_async && (hd & 3) == 0 && n4 <= 8 * nt;
-  float4 pk[8], pv[8];
-  if (early) {
+  // rows of earlier positions of the first NT-1 sub-chunks (the current
+  // position comes from this kernel's prologue), and the norm weight and
+  // RoPE lines (into L1).
+  if constexpr (C::kAsync) {
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int e = threadIdx.x + u * nt;
-      pk[u] = pv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (e < n4) {
-        const int r = (e * 4) / hd, d = e * 4 - r * hd, t = t0 + r;
-        if (t < t1 && !(fused && t == pos)) {
-          const size_t i = (size_t)t * kv_dim + kv_off + d;
-          pk[u] = kv_load4<T>(a.k_cache, i);
-          pv[u] = kv_load4<T>(a.v_cache, i);
-        }
-      }
+    for (int i = 0; i < NT - 1; ++i) {
+      if (i < nsub)
+        issue_tile<TT>(s_tiles + i * buf_bytes, kc, vc, t0 + i * kSub, t1, pos, fused, kv_dim, kv_off, hd, hs);
+      cp_async_commit();
     }
   }
   if (fused && active && threadIdx.x < 12) {
@@ -229,8 +352,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a)
   // split 0, which appends it, and by the split that holds position pos).
   if (fused && (split == 0 || split == n_active - 1)) {
     if (warp < 2) {
-      const float* src = (warp == 0 ? a.k : a.v) + kv_off;
-      float* dst = warp == 0 ? sm.kpos : sm.vpos;
+      const float* src = (warp == 0 ? a.k : a.v) + (size_t)z * a.qkv_bstride + kv_off;
+      float* dst = warp == 0 ? s_kpos : s_vpos;
       float r[8];
 #pragma unroll
       for (int k = 0; k < 8; ++k) r[k] = lane + 32 * k < hd ? src[lane + 32 * k] : 0.0f;
@@ -239,7 +362,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a)
         if (lane + 32 * k < hd) dst[lane + 32 * k] = r[k];
       __syncwarp();
       if (warp == 0)
-        norm_rope_row(sm.kpos, sm.sq, hd, a.k_norm, a.k_norm_dtype, true, a.rope_cos, a.rope_sin, a.rope_base,
+        norm_rope_row(s_kpos, s_sq, hd, a.k_norm, a.k_norm_dtype, true, a.rope_cos, a.rope_sin, a.rope_base,
                       a.rope_scale, pos, lane);
     }
   }
@@ -252,7 +375,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a)
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         const int d = lane + 32 * k;
-        qv[i][k] = (g < G && d < hd) ? a.q[(size_t)(hb + g) * hd + d] : 0.0f;
+        qv[i][k] = (g < G && d < hd) ? qp[(size_t)(hb + g) * hd + d] : 0.0f;
       }
     }
 #pragma unroll
@@ -261,22 +384,24 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a)
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         const int d = lane + 32 * k;
-        if (g < G && d < hd) sm.q[g * hd + d] = qv[i][k];
+        if (g < G && d < hd) s_q[g * hd + d] = qv[i][k];
       }
     }
     __syncwarp();
   }
   for (int g = warp; active && g < G; g += kAttnWarps) {
-    float* row = sm.q + g * hd;
+    float* row = s_q + g * hd;
     if (fused)
-      norm_rope_row(row, sm.sq + warp * 256, hd, a.q_norm, a.q_norm_dtype, true, a.rope_cos, a.rope_sin, a.rope_base,
+      norm_rope_row(row, s_sq + warp * 256, hd, a.q_norm, a.q_norm_dtype, true, a.rope_cos, a.rope_sin, a.rope_base,
                     a.rope_scale, pos, lane);
   }
   __syncthreads();
   if (fused && split == 0) {
+    void* kw = const_cast<uint8_t*>(kc);
+    void* vw = const_cast<uint8_t*>(vc);
     for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-      kv_store<T>(a.k_cache, (size_t)pos * kv_dim + kv_off + d, sm.kpos[d]);
-      kv_store<T>(a.v_cache, (size_t)pos * kv_dim + kv_off + d, sm.vpos[d]);
+      kv_store<T>(kw, (size_t)pos * kv_dim + kv_off + d, s_kpos[d]);
+      kv_store<T>(vw, (size_t)pos * kv_dim + kv_off + d, s_vpos[d]);
     }
   }
 
@@ -288,183 +413,206 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a)
 #pragma unroll
       for (int j = 0; j < J; ++j) acc[i][j] = 0.0f;
     const bool act = lane * J < hd;
-    for (int c0 = t0; c0 < t1; c0 += kSub) {
-      // stage K and V rows of this sub-chunk (the current position from
-      // smem): groups of 4 values, all loads of a batch issued before the
-      // shared-memory stores
-      if (tile_async && c0 == t0) {
-        finish_tile_async(sm, c0, t1, pos, fused, hd, hs);
-      } else if (tile_async && c0 > t0) {
-        stage_tile_async<T>(a, sm, c0, t1, pos, fused, kv_dim, kv_off, hd, hs);
-        finish_tile_async(sm, c0, t1, pos, fused, hd, hs);
-      } else if (early && c0 == t0) {
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const int e = threadIdx.x + u * nt;
-          if (e < n4) {
-            const int r = (e * 4) / hd, d = e * 4 - r * hd, t = c0 + r;
-            float4 kk = pk[u], vv = pv[u];
-            if (fused && t == pos && t < t1) {
-              kk = make_float4(sm.kpos[d], sm.kpos[d + 1], sm.kpos[d + 2], sm.kpos[d + 3]);
-              vv = make_float4(sm.vpos[d], sm.vpos[d + 1], sm.vpos[d + 2], sm.vpos[d + 3]);
-            }
-            float* kd = sm.kt + r * hs + d;
-            float* vd = sm.vt + r * hs + d;
-            kd[0] = kk.x; kd[1] = kk.y; kd[2] = kk.z; kd[3] = kk.w;
-            vd[0] = vv.x; vd[1] = vv.y; vd[2] = vv.z; vd[3] = vv.w;
-          }
-        }
+    for (int i = 0; i < nsub; ++i) {
+      const int c0 = t0 + i * kSub;
+      uint8_t* buf = s_tiles + (size_t)(i % NT) * buf_bytes;
+      if constexpr (C::kAsync) {
+        // request the tile NT-1 ahead into the buffer the previous
+        // iteration finished with, then complete this one
+        if (i + NT - 1 < nsub)
+          issue_tile<TT>(s_tiles + (size_t)((i + NT - 1) % NT) * buf_bytes, kc, vc, c0 + (NT - 1) * kSub, t1, pos,
+                         fused, kv_dim, kv_off, hd, hs);
+        cp_async_commit();
+        put_pos_row<TT>(buf, s_kpos, s_vpos, c0, t1, pos, fused, hd, hs);
+        cp_async_wait<NT - 1>();
       } else {
-        stage_kv<T>(a, sm, c0, t1, pos, fused, kv_dim, kv_off, hd, hs);
+        float* kt = reinterpret_cast<float*>(buf);
+        stage_kv_tile<T>(kc, vc, s_kpos, s_vpos, kt, kt + (size_t)kSub * hs, c0, t1, pos, fused, kv_dim, kv_off, hd,
+                         hs, threadIdx.x, nt);
       }
       __syncthreads();
+      const TT* ktile = reinterpret_cast<const TT*>(buf);
+      const TT* vtile = ktile + (size_t)kSub * hs;
       const int t = c0 + lane;
       const bool valid = t < t1;
 #pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        const int g = warp + i * kAttnWarps;
+      for (int hi = 0; hi < 2; ++hi) {
+        const int g = warp + hi * kAttnWarps;
         if (g >= G) break;
-        const float* qrow = sm.q + g * hd;
-        float sc = 0.0f;
-        if ((hs & 3) == 0) {  // 16-byte reads, the same sequential order over d
-          const float4* kr = reinterpret_cast<const float4*>(sm.kt + lane * hs);
-          const float4* qr = reinterpret_cast<const float4*>(qrow);
-          for (int d4 = 0; d4 < (hd >> 2); ++d4) {
-            const float4 k4 = kr[d4], q4 = qr[d4];
-            sc = __fmaf_rn(q4.x, k4.x, sc);
-            sc = __fmaf_rn(q4.y, k4.y, sc);
-            sc = __fmaf_rn(q4.z, k4.z, sc);
-            sc = __fmaf_rn(q4.w, k4.w, sc);
-          }
-        } else {
-          for (int d = 0; d < hd; ++d) sc = __fmaf_rn(qrow[d], sm.kt[lane * hs + d], sc);
-        }
+        float sc = score_row<TT>(s_q + g * hd, ktile + (size_t)lane * hs, hd, hs);
         sc = valid ? __fmul_rn(sc, a.scale) : -INFINITY;
         const float mx = warp_max(sc);
-        const float mn = fmaxf(m[i], mx);
-        const float alpha = expf_det(__fsub_rn(m[i], mn));
+        const float mn = fmaxf(m[hi], mx);
+        const float alpha = expf_det(__fsub_rn(m[hi], mn));
         const float p = valid ? expf_det(__fsub_rn(sc, mn)) : 0.0f;
         const float psum = __shfl_sync(0xffffffffu, warp_sum(p), 0);
-        l[i] = __fadd_rn(__fmul_rn(l[i], alpha), psum);
-        m[i] = mn;
+        l[hi] = __fadd_rn(__fmul_rn(l[hi], alpha), psum);
+        m[hi] = mn;
 #pragma unroll
-        for (int j = 0; j < J; ++j) acc[i][j] = __fmul_rn(acc[i][j], alpha);
+        for (int j = 0; j < J; ++j) acc[hi][j] = __fmul_rn(acc[hi][j], alpha);
         for (int tt = 0; tt < kSub; ++tt) {
           const float pt = __shfl_sync(0xffffffffu, p, tt);
           if (act) {
             float vv[J];
-            const float* vr = sm.vt + tt * hs + lane * J;
-            if constexpr (J % 4 == 0) {
-              if ((hs & 3) == 0) {
+            load_v<J, TT>(vtile + (size_t)tt * hs + lane * J, vv);
 #pragma unroll
-                for (int j = 0; j < J; j += 4) {
-                  const float4 v4 = *reinterpret_cast<const float4*>(vr + j);
-                  vv[j] = v4.x; vv[j + 1] = v4.y; vv[j + 2] = v4.z; vv[j + 3] = v4.w;
-                }
-              } else {
-#pragma unroll
-                for (int j = 0; j < J; ++j) vv[j] = vr[j];
-              }
-            } else if constexpr (J == 2) {
-              if ((hs & 3) == 0) {
-                const float2 v2 = *reinterpret_cast<const float2*>(vr);
-                vv[0] = v2.x; vv[1] = v2.y;
-              } else {
-                vv[0] = vr[0]; vv[1] = vr[1];
-              }
-            } else {
-#pragma unroll
-              for (int j = 0; j < J; ++j) vv[j] = vr[j];
-            }
-#pragma unroll
-            for (int j = 0; j < J; ++j) acc[i][j] = __fmaf_rn(pt, vv[j], acc[i][j]);
+            for (int j = 0; j < J; ++j) acc[hi][j] = __fmaf_rn(pt, vv[j], acc[hi][j]);
           }
         }
       }
       __syncthreads();
     }
+    float* part_base = kCluster ? reinterpret_cast<float*>(s_tiles)
+                                : a.partial + ((size_t)z * a.n_head + hb) * a.n_split * stride_part;
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const int g = warp + i * kAttnWarps;
+    for (int hi = 0; hi < 2; ++hi) {
+      const int g = warp + hi * kAttnWarps;
       if (g >= G) break;
-      float* dst = a.partial + ((size_t)(hb + g) * a.n_split + split) * stride_part;
+      float* dst = kCluster ? part_base + (size_t)g * stride_part
+                            : part_base + ((size_t)g * a.n_split + split) * stride_part;
       if (act)
 #pragma unroll
-        for (int j = 0; j < J; ++j) dst[4 + lane * J + j] = acc[i][j];
+        for (int j = 0; j < J; ++j) dst[4 + lane * J + j] = acc[hi][j];
       if (lane == 0) {
-        dst[0] = m[i];
-        dst[1] = l[i];
+        dst[0] = m[hi];
+        dst[1] = l[hi];
       }
     }
+  }
+
+  if constexpr (kCluster) {
+    // Every split's partial rows are in its shared memory (tile area).  Unit
+    // u (32 consecutive output values of this kv head's G heads) is merged
+    // by warp (u / n_split) mod 4 of CTA u mod n_split, lane = value:
+    // M = max_s m_s, w_s = exp(m_s - M), L = sum_s w_s l_s and
+    // o = sum_s w_s acc_s (fma chains in split order), o * (1/L).
+    cluster_sync_all();
+    const int S = a.n_split;
+    const int n_units = (G * hd + 31) / 32;
+    const float* part_s = reinterpret_cast<const float*>(s_tiles);
+    for (int u = split + S * warp; u < n_units; u += S * kAttnWarps) {
+      const int e = u * 32 + lane;
+      const bool ve = e < G * hd;
+      const int g = ve ? e / hd : 0, d = ve ? e - g * hd : 0;
+      const float* row = part_s + (size_t)g * stride_part;
+      float ms[kAttnMaxCluster], ls[kAttnMaxCluster], av[kAttnMaxCluster];
+#pragma unroll
+      for (int sp = 0; sp < kAttnMaxCluster; ++sp) {
+        ms[sp] = -INFINITY;
+        ls[sp] = av[sp] = 0.0f;
+        if (sp < n_active) {
+          ms[sp] = dsmem_ld(dsmem_addr(row, sp));
+          ls[sp] = dsmem_ld(dsmem_addr(row + 1, sp));
+          av[sp] = dsmem_ld(dsmem_addr(row + 4 + d, sp));
+        }
+      }
+      float M = -INFINITY;
+#pragma unroll
+      for (int sp = 0; sp < kAttnMaxCluster; ++sp)
+        if (sp < n_active) M = fmaxf(M, ms[sp]);
+      float L = 0.0f, o = 0.0f;
+#pragma unroll
+      for (int sp = 0; sp < kAttnMaxCluster; ++sp) {
+        if (sp < n_active) {
+          const float w = expf_det(__fsub_rn(ms[sp], M));
+          L = __fmaf_rn(w, ls[sp], L);
+          o = __fmaf_rn(w, av[sp], o);
+        }
+      }
+      o = __fmul_rn(o, L > 0.0f ? __fdiv_rn(1.0f, L) : 0.0f);
+      if (ve) outp[(size_t)hb * hd + e] = o;
+      if (oq8 && (hd % 32) == 0) {
+        uint16_t dbits;
+        bool zero;
+        const int q = q8_1_quant_lane(o, &dbits, &zero);
+        uint32_t word = ((uint32_t)(q & 0xff)) << (8 * (lane & 3));
+        word |= __shfl_xor_sync(0xffffffffu, word, 1);
+        word |= __shfl_xor_sync(0xffffffffu, word, 2);
+        float sum = 0.0f;  // the sequential f16 s of the reference block
+        for (int t = 0; t < 32; ++t) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, o, t));
+        uint32_t* ob = reinterpret_cast<uint32_t*>(oq8 + ((size_t)hb * hd / 32 + u) * 36);
+        if (lane == 0) ob[0] = (uint32_t)dbits | ((uint32_t)(zero ? (uint16_t)0 : f32_to_f16_ref(sum)) << 16);
+        if ((lane & 3) == 0) ob[1 + (lane >> 2)] = word;
+      }
+    }
+    cluster_sync_all();  // no CTA leaves while another still reads its partials
+    return;
   }
 
   // last CTA of this kv head merges the splits: the CTA barrier orders every
   // thread's partial stores before thread 0's acquire-release ticket
   __shared__ unsigned ticket_s;
+  unsigned* counter = a.counters + (size_t)z * a.n_kv + kvh;
   __syncthreads();
   if (threadIdx.x == 0) {
     unsigned t;
-    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(t) : "l"(&a.counters[kvh]) : "memory");
+    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(t) : "l"(counter) : "memory");
     ticket_s = t;
   }
   __syncthreads();
   if (ticket_s != (unsigned)(a.n_split - 1)) return;
-  if (threadIdx.x == 0) atomicExch(&a.counters[kvh], 0u);
+  if (threadIdx.x == 0) atomicExch(counter, 0u);
   // Merge: (1) m and l of all (head, split) pairs -- with every split's
   // partial row copied into shared memory in one round trip when they fit
-  // (L2-only bulk copies); (2) per head M = max m, w_s = exp(m_s - M) and
+  // (L2-only async copies); (2) per head M = max m, w_s = exp(m_s - M) and
   // L = sum_s w_s l_s (fma in split order); (3) o_d = sum_s w_s acc_sd (fma in
   // split order) * (1/L) by one thread per (head, d); (4) Q8_1 blocks of the
   // output, one warp per block.
+  const float* part_g = a.partial + ((size_t)z * a.n_head + hb) * a.n_split * stride_part;
+  float* cm = reinterpret_cast<float*>(s_tiles);
+  float* cl = cm + kGMax * kMaxSplit;
+  float* cw = cl + kGMax * kMaxSplit;
+  float* cinv = cw + kGMax * kMaxSplit;
+  float* mp = reinterpret_cast<float*>(s_tiles + attn_merge_stage_offset());
   const bool staged = (size_t)G * n_active * stride_part <= (size_t)kMergeStage;
   if (staged) {
     const int per = stride_part / 4;  // 16-byte pieces per partial row
     for (int i = threadIdx.x; i < G * n_active * per; i += nt) {
       const int row = i / per, c = i - row * per;
       const int g = row / n_active, sp = row - g * n_active;
-      cp_async16(sm.mp + (size_t)row * stride_part + c * 4,
-                 a.partial + ((size_t)(hb + g) * a.n_split + sp) * stride_part + c * 4);
+      cp_async16(mp + (size_t)row * stride_part + c * 4, part_g + ((size_t)g * a.n_split + sp) * stride_part + c * 4);
     }
-    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+    cp_async_commit();
+    cp_async_wait<0>();
     __syncthreads();
     for (int i = threadIdx.x; i < G * n_active; i += nt) {
       const int g = i / n_active, sp = i - g * n_active;
-      sm.cm[g * kMaxSplit + sp] = sm.mp[(size_t)i * stride_part];
-      sm.cl[g * kMaxSplit + sp] = sm.mp[(size_t)i * stride_part + 1];
+      cm[g * kMaxSplit + sp] = mp[(size_t)i * stride_part];
+      cl[g * kMaxSplit + sp] = mp[(size_t)i * stride_part + 1];
     }
   } else {
     for (int i = threadIdx.x; i < G * n_active; i += nt) {
       const int g = i / n_active, sp = i - g * n_active;
-      const float* ps = a.partial + ((size_t)(hb + g) * a.n_split + sp) * stride_part;
-      sm.cm[g * kMaxSplit + sp] = __ldcg(ps);
-      sm.cl[g * kMaxSplit + sp] = __ldcg(ps + 1);
+      const float* ps = part_g + ((size_t)g * a.n_split + sp) * stride_part;
+      cm[g * kMaxSplit + sp] = __ldcg(ps);
+      cl[g * kMaxSplit + sp] = __ldcg(ps + 1);
     }
   }
   __syncthreads();
   for (int g = warp; g < G; g += kAttnWarps) {
-    const float* mg = sm.cm + g * kMaxSplit;
+    const float* mg = cm + g * kMaxSplit;
     float M = -INFINITY;
     for (int sp = lane; sp < n_active; sp += 32) M = fmaxf(M, mg[sp]);
     M = warp_max(M);
-    for (int sp = lane; sp < n_active; sp += 32) sm.cw[g * kMaxSplit + sp] = expf_det(__fsub_rn(mg[sp], M));
+    for (int sp = lane; sp < n_active; sp += 32) cw[g * kMaxSplit + sp] = expf_det(__fsub_rn(mg[sp], M));
     __syncwarp();
     if (lane == 0) {
       float L = 0.0f;
-      for (int sp = 0; sp < n_active; ++sp) L = __fmaf_rn(sm.cw[g * kMaxSplit + sp], sm.cl[g * kMaxSplit + sp], L);
-      sm.cinv[g] = L > 0.0f ? __fdiv_rn(1.0f, L) : 0.0f;
+      for (int sp = 0; sp < n_active; ++sp) L = __fmaf_rn(cw[g * kMaxSplit + sp], cl[g * kMaxSplit + sp], L);
+      cinv[g] = L > 0.0f ? __fdiv_rn(1.0f, L) : 0.0f;
     }
   }
   __syncthreads();
   constexpr int kLd = 16;
   for (int i = threadIdx.x; i < G * hd; i += nt) {
     const int g = i / hd, d = i - g * hd;
-    const float* wg = sm.cw + g * kMaxSplit;
+    const float* wg = cw + g * kMaxSplit;
     float o = 0.0f;
     if (staged) {
-      const float* pg = sm.mp + (size_t)g * n_active * stride_part + 4 + d;
+      const float* pg = mp + (size_t)g * n_active * stride_part + 4 + d;
       for (int sp = 0; sp < n_active; ++sp) o = __fmaf_rn(wg[sp], pg[(size_t)sp * stride_part], o);
     } else {
-      const float* pg = a.partial + (size_t)(hb + g) * a.n_split * stride_part + 4 + d;
+      const float* pg = part_g + (size_t)g * a.n_split * stride_part + 4 + d;
       for (int s0 = 0; s0 < n_active; s0 += kLd) {
         float r[kLd];
 #pragma unroll
@@ -474,24 +622,24 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a)
           if (s0 + u < n_active) o = __fmaf_rn(wg[s0 + u], r[u], o);
       }
     }
-    o = __fmul_rn(o, sm.cinv[g]);
-    a.out[(size_t)(hb + g) * hd + d] = o;
-    sm.q[i] = o;
+    o = __fmul_rn(o, cinv[g]);
+    outp[(size_t)(hb + g) * hd + d] = o;
+    s_q[i] = o;
   }
-  if (a.out_q8 && (hd % 32) == 0) {
+  if (oq8 && (hd % 32) == 0) {
     __syncthreads();
     for (int b = warp; b < G * hd / 32; b += kAttnWarps) {
-      const float o = sm.q[b * 32 + lane];
+      const float o = s_q[b * 32 + lane];
       uint16_t dbits;
       bool zero;
       const int q = q8_1_quant_lane(o, &dbits, &zero);
       uint32_t word = ((uint32_t)(q & 0xff)) << (8 * (lane & 3));
       word |= __shfl_xor_sync(0xffffffffu, word, 1);
       word |= __shfl_xor_sync(0xffffffffu, word, 2);
-      uint32_t* ob = reinterpret_cast<uint32_t*>(a.out_q8 + ((size_t)hb * hd + (size_t)b * 32) / 32 * 36);
+      uint32_t* ob = reinterpret_cast<uint32_t*>(oq8 + ((size_t)hb * hd + (size_t)b * 32) / 32 * 36);
       if (lane == 0) {
         float sum = 0.0f;  // the sequential f16 s of the reference block
-        for (int t = 0; t < 32; ++t) sum = __fadd_rn(sum, sm.q[b * 32 + t]);
+        for (int t = 0; t < 32; ++t) sum = __fadd_rn(sum, s_q[b * 32 + t]);
         ob[0] = (uint32_t)dbits | ((uint32_t)(zero ? (uint16_t)0 : f32_to_f16_ref(sum)) << 16);
       }
       if ((lane & 3) == 0) ob[1 + (lane >> 2)] = word;
@@ -499,21 +647,105 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a)
   }
 }
 
-size_t attn_smem_bytes(int hd) { return sizeof(float) * attn_smem_floats(hd); }
+// Cluster launch: grid (n_kv, n_split, batch) in clusters of (1, n_split, 1),
+// with programmatic dependent launch when pdl is set.
+template <typename Kern>
+cudaError_t launch_cluster(Kern kernel, dim3 grid, int cluster_y, size_t smem, cudaStream_t st, bool pdl,
+                           const AttnArgs& a) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kAttnWarps * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = (unsigned)cluster_y;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 2 : 1;
+  return cudaLaunchKernelEx(&cfg, kernel, a);
+}
 
-template <int J>
-cudaError_t launch_j(const AttnArgs& a, cudaStream_t st, bool pdl) {
-  const dim3 grid(a.n_kv, a.n_split);
-  const size_t smem = attn_smem_bytes(a.head_dim);
-  if (a.kv_f16) return launch_k(k_attention<J, __half>, grid, dim3(kAttnWarps * 32), smem, st, pdl, a);
-  return launch_k(k_attention<J, float>, grid, dim3(kAttnWarps * 32), smem, st, pdl, a);
+// Whether clusters of n CTAs of a kernel can be resident, queried once at
+// set-up per device; the cluster merge is launched only where they can
+// (otherwise the global-memory merge, with the same bits, is used).
+constexpr int kMaxDevices = 64;
+bool g_cluster_ok[kMaxDevices][2][4][kAttnMaxCluster + 1];  // [device][f16][J index][cluster size]
+
+int current_device() {
+  int d = 0;
+  if (cudaGetDevice(&d) != cudaSuccess || d < 0 || d >= kMaxDevices) return -1;
+  return d;
+}
+
+template <typename Kern>
+bool query_cluster(Kern kernel, size_t smem, int n) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1, n, 1);
+  cfg.blockDim = dim3(kAttnWarps * 32);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = (unsigned)n;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return false;
+  }
+  return clusters > 0;
+}
+
+constexpr int j_index(int J) { return J == 1 ? 0 : J == 2 ? 1 : J == 4 ? 2 : 3; }
+
+template <int J, typename T>
+cudaError_t init_jt(int dev) {
+  const size_t mx = attn_smem_bytes_t<J, T, false>(32 * J);
+  const size_t mc = attn_smem_bytes_t<J, T, true>(32 * J);
+  cudaError_t e = cudaFuncSetAttribute(k_attention<J, T, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mx);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(k_attention<J, T, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mc);
+  if (e != cudaSuccess) return e;
+  const bool nonportable =
+      cudaFuncSetAttribute(k_attention<J, T, true>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess;
+  if (!nonportable) (void)cudaGetLastError();
+  for (int n = 1; n <= kAttnMaxCluster; ++n)
+    g_cluster_ok[dev][sizeof(T) == 2][j_index(J)][n] =
+        (n <= 8 || nonportable) && query_cluster(k_attention<J, T, true>, mc, n);
+  return cudaSuccess;
 }
 
 template <int J>
-cudaError_t init_j() {
-  const int mx = (int)attn_smem_bytes(256);
-  cudaError_t e = cudaFuncSetAttribute(k_attention<J, __half>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(k_attention<J, float>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
+cudaError_t launch_j(const AttnArgs& a, cudaStream_t st, bool pdl) {
+  const int hd = a.head_dim;
+  const dim3 grid(a.n_kv, a.n_split, a.batch > 0 ? a.batch : 1);
+  const bool f16 = a.kv_f16 != 0;
+  const int dev = a.cluster ? current_device() : -1;
+  if (dev >= 0 && g_cluster_ok[dev][f16][j_index(J)][a.n_split]) {
+    if (f16)
+      return launch_cluster(k_attention<J, __half, true>, grid, a.n_split, attn_smem_bytes_t<J, __half, true>(hd), st,
+                            pdl, a);
+    return launch_cluster(k_attention<J, float, true>, grid, a.n_split, attn_smem_bytes_t<J, float, true>(hd), st, pdl,
+                          a);
+  }
+  if (!a.partial || !a.counters) return cudaErrorInvalidValue;
+  if (f16)
+    return launch_k(k_attention<J, __half, false>, grid, dim3(kAttnWarps * 32), attn_smem_bytes_t<J, __half, false>(hd),
+                    st, pdl, a);
+  return launch_k(k_attention<J, float, false>, grid, dim3(kAttnWarps * 32), attn_smem_bytes_t<J, float, false>(hd), st,
+                  pdl, a);
+}
+
+template <int J>
+cudaError_t init_j(int dev) {
+  cudaError_t e = init_jt<J, float>(dev);
+  if (e == cudaSuccess) e = init_jt<J, __half>(dev);
   return e;
 }
 
@@ -524,15 +756,18 @@ size_t attn_partial_floats(int n_head, int n_split, int head_dim) {
 }
 
 cudaError_t attention_init() {
-  cudaError_t e = init_j<1>();
-  if (e == cudaSuccess) e = init_j<2>();
-  if (e == cudaSuccess) e = init_j<4>();
-  if (e == cudaSuccess) e = init_j<8>();
+  const int dev = current_device();
+  if (dev < 0) return cudaErrorInvalidDevice;
+  cudaError_t e = init_j<1>(dev);
+  if (e == cudaSuccess) e = init_j<2>(dev);
+  if (e == cudaSuccess) e = init_j<4>(dev);
+  if (e == cudaSuccess) e = init_j<8>(dev);
   return e;
 }
 
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st, bool pdl) {
   if (a.n_split > kMaxSplit || a.n_split < 1) return cudaErrorInvalidValue;
+  if (a.cluster && a.n_split > kAttnMaxCluster) return cudaErrorInvalidValue;
   if (a.n_head > kGMax * a.n_kv) return cudaErrorInvalidValue;
   switch (a.head_dim) {
     case 64: return launch_j<2>(a, st, pdl);

@@ -26,14 +26,28 @@ struct AttnArgs {
   int pos_static;
   int n_head, n_kv, head_dim, ctx;
   int n_split;
+  // 1: the splits of a kv head form one thread-block cluster and merge
+  // through distributed shared memory (n_split <= kAttnMaxCluster; partial
+  // and counters unused); 0: split-K partials in global memory, merged by
+  // the last-arriving CTA.  Same arithmetic, same bits.
+  int cluster;
   float scale;
   // scratch
-  float* partial;      // [n_head][n_split][attn_part_stride(head_dim)]: m, l, 2 pad, acc[head_dim]
-  unsigned* counters;  // [n_kv], zero at rest
+  float* partial;      // [batch][n_head][n_split][attn_part_stride(head_dim)]: m, l, 2 pad, acc[head_dim]
+  unsigned* counters;  // [batch][n_kv], zero at rest
   // outputs
   float* out;          // [n_head*head_dim]
   uint8_t* out_q8;     // optional Q8_1 of out (needs head_dim % 32 == 0)
+  // independent sequences (grid z): sequence b reads q/k/v at + b*qkv_bstride
+  // floats, its caches at + b*cache_bstride elements, its position at
+  // pos_ptr[b] (pos_static when pos_ptr is null), and writes out at
+  // + b*out_bstride floats and out_q8 at + b*outq8_bstride bytes.  batch 0
+  // means 1.
+  int batch;
+  size_t qkv_bstride, cache_bstride, out_bstride, outq8_bstride;
 };
+
+constexpr int kAttnMaxCluster = 16;  // cluster size (beyond 8 needs the non-portable opt-in)
 
 // Floats per (head, split) partial: m, l, two pad floats, then head_dim
 // accumulators (rows stay 16-byte aligned for bulk copies).

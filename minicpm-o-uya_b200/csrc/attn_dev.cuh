@@ -24,6 +24,16 @@ __device__ __forceinline__ void kv_store(void* p, size_t i, float v) {
     reinterpret_cast<float*>(p)[i] = v;
 }
 
+// A value of the current position as the cache holds it (f16: rounded to
+// nearest even), so the current position is attended exactly as stored.
+template <typename T>
+__device__ __forceinline__ float kv_round(float v) {
+  if constexpr (sizeof(T) == 2)
+    return __half2float(__float2half_rn(v));
+  else
+    return v;
+}
+
 // K/V rows are read once per step: streaming (evict-first) loads.
 template <typename T>
 __device__ __forceinline__ float4 kv_load4(const void* p, size_t i) {
@@ -55,8 +65,8 @@ __device__ __forceinline__ void stage_kv_tile(const void* k_cache, const void* v
           const int r = e / hd, d = e - r * hd, t = c0 + r;
           if (t < t1) {
             if (fused && t == pos) {
-              kr[u] = kpos[d];
-              vr[u] = vpos[d];
+              kr[u] = kv_round<T>(kpos[d]);
+              vr[u] = kv_round<T>(vpos[d]);
             } else {
               const size_t i = (size_t)t * kv_dim + kv_off + d;
               kr[u] = kv_load<T>(k_cache, i);
@@ -89,8 +99,10 @@ __device__ __forceinline__ void stage_kv_tile(const void* k_cache, const void* v
         const int r = (e * 4) / hd, d = e * 4 - r * hd, t = c0 + r;
         if (t < t1) {
           if (fused && t == pos) {
-            kr[u] = make_float4(kpos[d], kpos[d + 1], kpos[d + 2], kpos[d + 3]);
-            vr[u] = make_float4(vpos[d], vpos[d + 1], vpos[d + 2], vpos[d + 3]);
+            kr[u] = make_float4(kv_round<T>(kpos[d]), kv_round<T>(kpos[d + 1]), kv_round<T>(kpos[d + 2]),
+                                kv_round<T>(kpos[d + 3]));
+            vr[u] = make_float4(kv_round<T>(vpos[d]), kv_round<T>(vpos[d + 1]), kv_round<T>(vpos[d + 2]),
+                                kv_round<T>(vpos[d + 3]));
           } else {
             const size_t i = (size_t)t * kv_dim + kv_off + d;
             kr[u] = kv_load4<T>(k_cache, i);

@@ -81,9 +81,11 @@ __device__ __forceinline__ float warp_sum(float v) {
 
 // Number of KV splits of the decode attention: a function of the kv-head
 // count only, so results do not depend on the GPU's SM count.
+// Splits of the positions per kv head: ceil(256 / n_kv) CTAs' worth of
+// parallelism, at most 16 (one thread-block cluster per kv head).
 __host__ __device__ inline int attn_n_split(int n_kv) {
   int s = (256 + n_kv - 1) / n_kv;
-  return s < 1 ? 1 : (s > 64 ? 64 : s);
+  return s < 1 ? 1 : (s > 16 ? 16 : s);
 }
 
 __device__ __forceinline__ float warp_max(float v) {

@@ -422,6 +422,17 @@ cudaError_t model_mv(Ctx* c, Upload* w, const float* x, const uint8_t* xq, float
 
 // q/k/v share one launch when all are tiled and Q8_0 is not mixed with the
 // k-quants (separate kernel classes).
+// Decode attention of the model graph: split merge inside a thread-block
+// cluster (1, the default) or through global memory (tuning override
+// MCPO_ATTN_CLUSTER=0); the same bits either way.
+int attn_cluster_cfg() {
+  static const int v = [] {
+    const char* e = getenv("MCPO_ATTN_CLUSTER");
+    return (e && *e) ? (atoi(e) != 0 ? 1 : 0) : 1;
+  }();
+  return v;
+}
+
 bool groupable(Upload* const* u, int n) {
   bool q80 = false, kq = false;
   for (int i = 0; i < n; ++i) {
@@ -507,6 +518,7 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
     a.head_dim = hd;
     a.ctx = (int)cf.context;
     a.n_split = m.n_split;
+    a.cluster = attn_cluster_cfg();
     a.scale = 1.0f / sqrtf((float)hd);
     a.partial = m.partial;
     a.counters = m.counters;

@@ -245,8 +245,10 @@ __device__ void attn_item(const AttnArgs& a, const AttnStageSmem& sm, int kvh, i
           const int r = (e * 4) / hd, d = e * 4 - r * hd, t = c0 + r;
           float4 kk = pk[u], vv = pv[u];
           if (fused && t == pos && t < t1) {
-            kk = make_float4(sm.kpos[d], sm.kpos[d + 1], sm.kpos[d + 2], sm.kpos[d + 3]);
-            vv = make_float4(sm.vpos[d], sm.vpos[d + 1], sm.vpos[d + 2], sm.vpos[d + 3]);
+            kk = make_float4(kv_round<T>(sm.kpos[d]), kv_round<T>(sm.kpos[d + 1]), kv_round<T>(sm.kpos[d + 2]),
+                             kv_round<T>(sm.kpos[d + 3]));
+            vv = make_float4(kv_round<T>(sm.vpos[d]), kv_round<T>(sm.vpos[d + 1]), kv_round<T>(sm.vpos[d + 2]),
+                             kv_round<T>(sm.vpos[d + 3]));
           }
           float* kd = sm.kt + r * hs + d;
           float* vd = sm.vt + r * hs + d;

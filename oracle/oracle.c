@@ -582,7 +582,7 @@ float orc_expf_det(float x) {
 
 int orc_attn_n_split(int n_kv) {
     int s = (256 + n_kv - 1) / n_kv;
-    return s < 1 ? 1 : (s > 64 ? 64 : s);
+    return s < 1 ? 1 : (s > 16 ? 16 : s);
 }
 
 uint16_t orc_f32_to_f16_rne(float v) {
@@ -895,6 +895,9 @@ int orc_forward_token(const orc_model *m, orc_state *st, uint32_t token, size_t 
         memcpy(st->k_cache + ((size_t) L * m->context + pos) * kvd, k, kvd * 4);
         memcpy(st->v_cache + ((size_t) L * m->context + pos) * kvd, v, kvd * 4);
         if (st->norm_order == 1) {
+            /* f16 cache: every position, the current one included, is read
+             * back as stored (rounded to nearest even) */
+            const float *cur_k = k, *cur_v = v;
             if (st->kv_f16) {
                 float *kc = st->k_cache + ((size_t) L * m->context + pos) * kvd;
                 float *vc = st->v_cache + ((size_t) L * m->context + pos) * kvd;
@@ -902,9 +905,11 @@ int orc_forward_token(const orc_model *m, orc_state *st, uint32_t token, size_t 
                     kc[i] = orc_f16_to_f32(orc_f32_to_f16_rne(kc[i]));
                     vc[i] = orc_f16_to_f32(orc_f32_to_f16_rne(vc[i]));
                 }
+                cur_k = kc;
+                cur_v = vc;
             }
-            ok = ok && orc_attention_dev(ctx, q, st->k_cache, st->v_cache, k, v, L, pos, m->heads, m->kv_heads,
-                                         m->head_dim, m->context);
+            ok = ok && orc_attention_dev(ctx, q, st->k_cache, st->v_cache, cur_k, cur_v, L, pos, m->heads,
+                                         m->kv_heads, m->head_dim, m->context);
         } else {
             ok = ok && orc_attention(ctx, q, st->k_cache, st->v_cache, L, pos, m->heads, m->kv_heads, m->head_dim,
                                      m->context);
