@@ -225,6 +225,16 @@ MINICPMO_API int minicpmo_gpu_context_rms_norm_q8_1(void *handle, const float *x
  * [out_dim][in_dim/32] (Q4_K, Q8_0) or [out_dim][in_dim/16] (Q6_K). */
 MINICPMO_API int minicpmo_gpu_context_matvec_q8_1(void *handle, const void *host_ptr, const void *xq, size_t in_dim, size_t out_dim,
                                      float *y_out, int32_t *dots_out, char *error, size_t error_cap);
+/* Batched projection on the tensor cores (the decode path of
+ * minicpmo_gpu_context_qwen3_forward_batch): y[n][out_dim] = W . x[n] for
+ * n_seq <= 32 host f32 rows x[n][in_dim], W an uploaded Q8_0 tensor with
+ * out_dim % 128 == 0 and in_dim % 256 == 0.  W and x are rounded to f16
+ * and the products summed in f32.  No reference counterpart (the
+ * reference has no GPU Q8_0 path, gpu.uya:130-132; its CPU path is
+ * qwen3_q8_0_matvec_range, qwen3.uya:1200-1231). */
+MINICPMO_API int minicpmo_gpu_context_matmul_q8_0_batch(void *handle, const void *host_ptr, const float *x, size_t n_seq,
+                                           size_t in_dim, size_t out_dim, float *y_out, char *error,
+                                           size_t error_cap);
 /* GEMV of an uploaded quantised tensor on host f32 activations that the
  * GEMV kernel quantises to Q8_1 itself (as the decode step's fused down and
  * o projections do), after RMSNorm with the uploaded weight norm_host_ptr

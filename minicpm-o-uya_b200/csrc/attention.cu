@@ -305,7 +305,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a)
   const uint8_t* vc = static_cast<const uint8_t*>(a.v_cache) + (size_t)z * a.cache_bstride * sizeof(T);
   float* outp = a.out + (size_t)z * a.out_bstride;
   uint8_t* oq8 = a.out_q8 ? a.out_q8 + (size_t)z * a.outq8_bstride : nullptr;
-  const int pos = a.pos_ptr ? a.pos_ptr[z] : a.pos_static;
+  const int pos = a.pos_ptr ? a.pos_ptr[(size_t)z * (a.pos_stride > 0 ? a.pos_stride : 1)] : a.pos_static;
   const int n_pos = pos + 1;
   int chunk = (n_pos + a.n_split - 1) / a.n_split;
   if (chunk < 32) chunk = 32;

@@ -40,11 +40,12 @@ struct AttnArgs {
   uint8_t* out_q8;     // optional Q8_1 of out (needs head_dim % 32 == 0)
   // independent sequences (grid z): sequence b reads q/k/v at + b*qkv_bstride
   // floats, its caches at + b*cache_bstride elements, its position at
-  // pos_ptr[b] (pos_static when pos_ptr is null), and writes out at
+  // pos_ptr[b * pos_stride] (pos_static when pos_ptr is null), and writes out at
   // + b*out_bstride floats and out_q8 at + b*outq8_bstride bytes.  batch 0
   // means 1.
   int batch;
   size_t qkv_bstride, cache_bstride, out_bstride, outq8_bstride;
+  int pos_stride;  // ints between sequences' positions at pos_ptr (0: 1)
 };
 
 constexpr int kAttnMaxCluster = 16;  // cluster size (beyond 8 needs the non-portable opt-in)

@@ -1,0 +1,529 @@
+// gemm.cu -- batched decode projections (config: all linear weights Q8_0,
+// up to 32 independent sequences) on the sm_100a tensor cores (tcgen05).
+//
+// Batch-1 decode is a weight stream and runs on dp4a (gemv.cu); with 32
+// sequences the same stream carries 32x the arithmetic, which dp4a cannot
+// keep up with, so the weights are dequantised to f16 in shared memory and
+// multiplied on the tensor cores with f32 accumulation in tensor memory:
+//
+//   warp 0      producer: per 256-value K-tile, 128 bulk copies of the tile's
+//               raw Q8_0 row pieces (8 blocks = 272 bytes each, 16-byte
+//               aligned in the GGUF row) and one bulk copy of the f16
+//               activation tile (N x 256, already in the operand layout);
+//   warps 2..5  dequantise: thread = row, q * d in f16 (int8 -> f16 exactly
+//               via the 0x6400 exponent trick, one rounding in the multiply),
+//               written as 8x16-byte core matrices of the K-major operand
+//               layout (no swizzle), in two 128-value halves per K-tile;
+//   warp 1      one elected thread issues tcgen05.mma kind::f16 (M = 128,
+//               N = sequences, K = 16) into a 128 x N f32 accumulator in
+//               tensor memory and releases stages with tcgen05.commit;
+//   epilogue    warps 2..5 read the accumulator with tcgen05.ld (lane = row)
+//               and store / add Y, or, with K split over several CTAs, write
+//               partial sums that the last CTA of the row tile adds in split
+//               order (deterministic).
+//
+// All waits are bounded (mbarrier try_wait with an iteration limit); a wait
+// that gives up raises the error word and a shared abort flag, the other
+// roles stop at their next wait, and the CTA still waits (bounded) for its
+// copies and MMAs in flight before it frees tensor memory and exits.
+//
+// Arithmetic: the result differs from the reference's f32-activation CPU
+// path (qwen3.uya:1200-1231) by the f16 rounding of the dequantised weights
+// and of the activations (relative 2^-11 each), far inside the 1e-3 matvec
+// tolerance.
+#include "gemm.cuh"
+
+#include <cuda_fp16.h>
+#include <math.h>
+#include <string.h>
+
+#include "common.cuh"
+#include "gemv.cuh"
+#include "tma.cuh"
+
+namespace mcpo {
+
+namespace {
+
+constexpr int kRawStages = 3;   // raw Q8_0 + activation tiles in flight
+constexpr int kAStages = 2;     // f16 operand half-tiles (128 rows x 128 K)
+constexpr int kRowPiece = 272;  // bytes of 256 values of one Q8_0 row
+constexpr int kRawBytes = kGemmTileRows * kRowPiece;     // 34816
+constexpr int kABytes = kGemmTileRows * 128 * 2;         // 32768
+constexpr int kThreads = 6 * 32;
+
+__host__ __device__ constexpr size_t act_bytes(int N) { return (size_t)N * kGemmKTile * 2; }
+
+// Shared memory: [A stages][raw stages][activation stages][barriers][tmem addr][abort]
+struct GemmSmem {
+  __host__ __device__ static size_t a_off() { return 0; }
+  __host__ __device__ static size_t raw_off() { return (size_t)kAStages * kABytes; }
+  __host__ __device__ static size_t act_off() { return raw_off() + (size_t)kRawStages * kRawBytes; }
+  __host__ __device__ static size_t bar_off(int N) { return act_off() + (size_t)kRawStages * act_bytes(N); }
+  __host__ __device__ static size_t bytes(int N) { return bar_off(N) + 8 * (2 * kRawStages + 2 * kAStages + 1) + 16 + 1024; }
+};
+
+// ---- tcgen05 primitives ----
+
+// Shared-memory matrix descriptor, K-major, no swizzle: core matrices of 8
+// rows x 16 bytes stored contiguously (128 bytes); lbo = byte distance
+// between the two 16-byte K-chunks of one MMA (K = 16), sbo = byte distance
+// between consecutive 8-row groups.  Version 1 (sm_100), base offset 0.
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((saddr >> 4) & 0x3fffu) | ((uint64_t)((lbo >> 4) & 0x3fffu) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3fffu) << 32) | (1ull << 46);
+}
+
+// Instruction descriptor for kind::f16: f16 A and B (K-major), f32
+// accumulator, M = 128, N = n.
+__host__ __device__ constexpr uint32_t umma_idesc_f16(int n) {
+  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kGemmTileRows >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrives on `bar` once every tcgen05 operation this thread issued before it
+// has completed.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+// Generic-proxy shared-memory writes become visible to the tensor cores.
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(dst_smem)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// 16 consecutive f32 accumulator columns of this thread's lane.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Bounded wait that leaves early once the CTA's abort flag is set.
+__device__ __forceinline__ bool gwait(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_s) {
+  for (int i = 0; i < kWaitLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63) == 63 && *abort_s) return false;
+  }
+  *abort_s = 1;
+  if (err) atomicExch(err, 1);
+  return false;
+}
+
+// Two signed bytes (positions 0,1 or 2,3 of w, already xor 0x80) as f16x2
+// exactly: 0x6400 | u is 1024 + u, minus 1152 gives u - 128 = q.
+__device__ __forceinline__ __half2 q8x2_to_h2(uint32_t wx, uint32_t sel) {
+  const uint32_t b = __byte_perm(wx, 0x64646464u, sel);
+  __half2 h;
+  memcpy(&h, &b, 4);
+  return __hsub2(h, __float2half2_rn(1152.0f));
+}
+
+// Row r's 128 values [128h, 128h + 128) of the raw K-tile (Q8_0 blocks
+// 4h..4h+3, 136 bytes at r*272 + 136h, 8-byte aligned) -> 16 chunks of 8
+// f16 values, chunk c to a_stage + c*2048 + r*16 (core matrix of rows
+// r & ~7, row r & 7).
+__device__ __forceinline__ void dequant_half(const uint8_t* raw, uint8_t* a_stage, int r, int h) {
+  uint32_t w[34];
+  const uint2* src = reinterpret_cast<const uint2*>(raw + (size_t)r * kRowPiece + 136 * h);
+#pragma unroll
+  for (int i = 0; i < 17; ++i) {
+    const uint2 v = src[i];
+    w[2 * i] = v.x;
+    w[2 * i + 1] = v.y;
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    // block j: d at byte 34j, qs at bytes 34j+2 .. 34j+33
+    const int db = 34 * j;
+    const uint32_t dw = w[db >> 2] >> (8 * (db & 3));
+    __half d;
+    const uint16_t dbits = (uint16_t)(dw & 0xffffu);
+    memcpy(&d, &dbits, 2);
+    const __half2 d2 = __half2half2(d);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      uint32_t out[4];
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        const int b = db + 2 + 8 * c + 2 * p;  // first byte of the pair (even, same word as b+1)
+        const uint32_t wx = w[b >> 2] ^ 0x80808080u;
+        const __half2 v = __hmul2(q8x2_to_h2(wx, (b & 3) ? 0x4342u : 0x4140u), d2);
+        memcpy(&out[p], &v, 4);
+      }
+      *reinterpret_cast<uint4*>(a_stage + (size_t)(4 * j + c) * 2048 + (size_t)r * 16) =
+          make_uint4(out[0], out[1], out[2], out[3]);
+    }
+  }
+}
+
+template <int N>
+__global__ void __launch_bounds__(kThreads, 1) k_gemm_q80(const GemmArgs a) {
+  // The tensor-core operand tiles are addressed from a 1024-byte aligned
+  // shared-memory base (the dynamic region itself is only guaranteed 16-byte
+  // alignment when device code is linked separately); the launch reserves
+  // the 1 KB of slack.
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+  uint8_t* a_st = smem + GemmSmem::a_off();
+  uint8_t* raw_st = smem + GemmSmem::raw_off();
+  uint8_t* act_st = smem + GemmSmem::act_off();
+  uint64_t* raw_full = reinterpret_cast<uint64_t*>(smem + GemmSmem::bar_off(N));
+  uint64_t* raw_empty = raw_full + kRawStages;
+  uint64_t* a_full = raw_empty + kRawStages;
+  uint64_t* a_empty = a_full + kAStages;
+  uint64_t* acc_full = a_empty + kAStages;
+  uint32_t* tmem_s = reinterpret_cast<uint32_t*>(acc_full + 1);
+  volatile int* abort_s = reinterpret_cast<volatile int*>(tmem_s + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x, split = blockIdx.y;
+  const int row0 = tile * kGemmTileRows;
+  const int kt_total = a.K / kGemmKTile;
+  const int kt0 = (int)((long long)split * kt_total / a.ksplit);
+  const int kt1 = (int)((long long)(split + 1) * kt_total / a.ksplit);
+  const int nkt = kt1 - kt0;
+  const size_t row_bytes = (size_t)(a.K / 32) * 34;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kRawStages; ++i) {
+      mbar_init(&raw_full[i], 1);
+      mbar_init(&raw_empty[i], 4 + 1);  // four dequantising warps + the MMA commit
+    }
+    for (int i = 0; i < kAStages; ++i) {
+      mbar_init(&a_full[i], 4);
+      mbar_init(&a_empty[i], 1);
+    }
+    mbar_init(acc_full, 1);
+    *abort_s = 0;
+    mbar_fence_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_s, 32);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_s;
+
+  if (warp == 0) {
+    // ---- producer: the weight pieces of the first stages are requested
+    // before waiting for the previous kernel (they do not depend on it); the
+    // activation tiles after.  Waits are made warp-uniform.
+    const uint64_t policy = l2_evict_first_policy();
+    auto issue_weights = [&](int i) {
+      const int s = i % kRawStages, kt = kt0 + i;
+      if (lane == 0) mbar_arrive_expect_tx(&raw_full[s], (uint32_t)(kRawBytes + act_bytes(N)));
+      __syncwarp();
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int r = lane + 32 * q;
+        int R = row0 + r;
+        const uint8_t* wseg = a.seg[0].w;
+        if (a.nseg > 1 && R >= a.seg[0].rows) {
+          R -= a.seg[0].rows;
+          wseg = a.seg[1].w;
+          if (a.nseg > 2 && R >= a.seg[1].rows) {
+            R -= a.seg[1].rows;
+            wseg = a.seg[2].w;
+          }
+        }
+        const uint8_t* src = wseg + (size_t)R * row_bytes + (size_t)kt * kRowPiece;
+        bulk_load_hint(raw_st + (size_t)s * kRawBytes + (size_t)r * kRowPiece, src, kRowPiece, &raw_full[s], policy);
+      }
+    };
+    auto issue_act = [&](int i) {
+      const int s = i % kRawStages, kt = kt0 + i;
+      if (lane == 0)
+        bulk_load(act_st + (size_t)s * act_bytes(N), a.x + (size_t)kt * act_bytes(N), (uint32_t)act_bytes(N),
+                  &raw_full[s]);
+    };
+    const int npre = nkt < kRawStages ? nkt : kRawStages;
+    for (int i = 0; i < npre; ++i) issue_weights(i);
+    pdl_wait();
+    for (int i = 0; i < npre; ++i) issue_act(i);
+    int issued = npre;
+    for (int i = npre; i < nkt; ++i) {
+      const int s = i % kRawStages;
+      if (!__all_sync(0xffffffffu, gwait(&raw_empty[s], (uint32_t)((i / kRawStages) - 1) & 1u, a.err, abort_s))) break;
+      issue_weights(i);
+      issue_act(i);
+      issued = i + 1;
+    }
+    // leave only once this CTA's copies have landed
+    for (int i = issued > kRawStages ? issued - kRawStages : 0; i < issued; ++i)
+      if (!mbar_wait(&raw_full[i % kRawStages], (uint32_t)(i / kRawStages) & 1u, a.err)) break;
+  } else if (warp == 1) {
+    // ---- MMA issuer (one thread) ----
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc_f16(N);
+      const uint32_t lbo_a = 2048, sbo = 128, lbo_b = (N / 8) * 128;
+      bool ok = true;
+      for (int i = 0; i < nkt && ok; ++i) {
+        const int s = i % kRawStages;
+        if (!gwait(&raw_full[s], (uint32_t)(i / kRawStages) & 1u, a.err, abort_s)) break;
+        for (int h = 0; h < 2; ++h) {
+          const int ai = 2 * i + h, sa = ai % kAStages;
+          if (!gwait(&a_full[sa], (uint32_t)(ai / kAStages) & 1u, a.err, abort_s)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_addr(a_st + (size_t)sa * kABytes);
+          const uint32_t b_base = smem_addr(act_st + (size_t)s * act_bytes(N)) + (uint32_t)(h * 16) * lbo_b;
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint64_t ad = umma_desc(a_base + kk * 2 * lbo_a, lbo_a, sbo);
+            const uint64_t bd = umma_desc(b_base + kk * 2 * lbo_b, lbo_b, sbo);
+            umma_f16(tmem, ad, bd, idesc, (i | h | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit(&a_empty[sa]);
+        }
+        if (ok) umma_commit(&raw_empty[s]);
+      }
+      // after every MMA issued, on every path: the epilogue reads the
+      // accumulator (or, on abort, only waits) before tensor memory is freed
+      umma_commit(acc_full);
+    }
+    __syncwarp();
+  } else {
+    // ---- dequantising warps, then the epilogue (waits warp-uniform) ----
+    const int r = ((warp & 3) << 5) | lane;  // = tensor-memory lane of this thread
+    for (int i = 0; i < nkt; ++i) {
+      const int s = i % kRawStages;
+      if (!__all_sync(0xffffffffu, gwait(&raw_full[s], (uint32_t)(i / kRawStages) & 1u, a.err, abort_s))) break;
+      bool ok = true;
+      for (int h = 0; h < 2 && ok; ++h) {
+        const int ai = 2 * i + h, sa = ai % kAStages;
+        if (ai >= kAStages &&
+            !__all_sync(0xffffffffu, gwait(&a_empty[sa], (uint32_t)((ai / kAStages) - 1) & 1u, a.err, abort_s))) {
+          ok = false;
+          break;
+        }
+        dequant_half(raw_st + (size_t)s * kRawBytes, a_st + (size_t)sa * kABytes, r, h);
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&a_full[sa]);
+      }
+      if (!ok) break;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&raw_empty[s]);
+    }
+    const bool go = __all_sync(0xffffffffu, mbar_wait(acc_full, 0u, a.err) && !*abort_s);
+    tc_fence_after();
+    float v[N];
+#pragma unroll
+    for (int c = 0; c < N; ++c) v[c] = 0.0f;
+    if (go) {
+      const uint32_t taddr = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+#pragma unroll
+      for (int c = 0; c < N; c += 16) {
+        float t[16];
+        tmem_ld16(taddr + c, t);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[c + i] = t[i];
+      }
+    }
+    const int row = row0 + r;
+    if (a.ksplit <= 1) {
+      if (go)
+#pragma unroll
+        for (int n = 0; n < N; ++n) {
+          if (n < a.n_valid) {
+            float* y = a.y + (size_t)n * a.ldy + row;
+            *y = a.epi == kGemmAdd ? __fadd_rn(*y, v[n]) : v[n];
+          }
+        }
+    } else {
+      // partial sums, then the last CTA of this row tile adds them in split
+      // order; the named barrier spans the four epilogue warps on every path
+      __shared__ unsigned ticket_s;
+#pragma unroll
+      for (int n = 0; n < N; ++n) a.partial[((size_t)split * N + n) * a.rows_total + row] = v[n];
+      __threadfence();
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (r == 0) ticket_s = atomicAdd(&a.counters[tile], 1u);
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (ticket_s == (unsigned)(a.ksplit - 1)) {
+        __threadfence();
+        for (int n = 0; n < a.n_valid; ++n) {
+          float sum = 0.0f;
+          for (int sp = 0; sp < a.ksplit; ++sp)
+            sum = __fadd_rn(sum, __ldcg(a.partial + ((size_t)sp * N + n) * a.rows_total + row));
+          float* y = a.y + (size_t)n * a.ldy + row;
+          *y = a.epi == kGemmAdd ? __fadd_rn(*y, sum) : sum;
+        }
+        if (r == 0) a.counters[tile] = 0u;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0) pdl_launch_dependents();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 32);
+  }
+}
+
+// ---- activation producers (f16 operand layout) ----
+
+__global__ void k_pack_x16(const float* __restrict__ x, int ld, int n_valid, int K, int N, uint8_t* __restrict__ x16) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int n = blockIdx.y;
+  if (n >= n_valid) return;
+  for (int k = (blockIdx.x * blockDim.x + threadIdx.x) * 8; k < K; k += gridDim.x * blockDim.x * 8) {
+    const float* src = x + (size_t)n * ld + k;
+    uint32_t o[4];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const __half2 h = __floats2half2_rn(src[2 * p], src[2 * p + 1]);
+      memcpy(&o[p], &h, 4);
+    }
+    *reinterpret_cast<uint4*>(x16 + gemm_x_offset(n, k, N)) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// One CTA (256 threads) per sequence: sum of squares in the order of
+// gpu_shim.c:694-718 (256 strided partial sums, halving tree), then
+// x * inv * w into the operand layout.
+__global__ void __launch_bounds__(256) k_rmsnorm_x16(const float* __restrict__ x, int ld, const void* __restrict__ w,
+                                                     int w_dtype, int K, float eps, int N, uint8_t* __restrict__ x16) {
+  __shared__ float part[256];
+  __shared__ float inv_s;
+  pdl_wait();
+  pdl_launch_dependents();
+  const int n = blockIdx.x, t = threadIdx.x;
+  const float* xr = x + (size_t)n * ld;
+  float p = 0.0f;
+  for (int i = t; i < K; i += 256) p = __fadd_rn(p, __fmul_rn(xr[i], xr[i]));
+  part[t] = p;
+  __syncthreads();
+  for (int stride = 128; stride >= 32; stride >>= 1) {
+    if (t < stride) part[t] = __fadd_rn(part[t], part[t + stride]);
+    __syncthreads();
+  }
+  if (t < 32) {
+    float v = part[t];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, o));
+    if (t == 0) inv_s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(v, (float)K), eps)));
+  }
+  __syncthreads();
+  const float inv = inv_s;
+  for (int k = t * 8; k < K; k += 256 * 8) {
+    uint32_t o[4];
+#pragma unroll
+    for (int p2 = 0; p2 < 4; ++p2) {
+      const int i = k + 2 * p2;
+      const float a0 = __fmul_rn(__fmul_rn(xr[i], inv), load_weight(w, w_dtype, i));
+      const float a1 = __fmul_rn(__fmul_rn(xr[i + 1], inv), load_weight(w, w_dtype, i + 1));
+      const __half2 h = __floats2half2_rn(a0, a1);
+      memcpy(&o[p2], &h, 4);
+    }
+    *reinterpret_cast<uint4*>(x16 + gemm_x_offset(n, k, N)) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+__global__ void k_swiglu_x16(const float* __restrict__ gu, int F, int n_valid, int N, uint8_t* __restrict__ x16) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int n = blockIdx.y;
+  if (n >= n_valid) return;
+  const float* g = gu + (size_t)n * 2 * F;
+  const float* u = g + F;
+  for (int k = (blockIdx.x * blockDim.x + threadIdx.x) * 8; k < F; k += gridDim.x * blockDim.x * 8) {
+    uint32_t o[4];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const __half2 h = __floats2half2_rn(silu_mul_det(g[k + 2 * p], u[k + 2 * p]),
+                                          silu_mul_det(g[k + 2 * p + 1], u[k + 2 * p + 1]));
+      memcpy(&o[p], &h, 4);
+    }
+    *reinterpret_cast<uint4*>(x16 + gemm_x_offset(n, k, N)) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+}  // namespace
+
+int gemm_pick_ksplit(int tiles, int ktiles, int sms) {
+  if (tiles >= sms) return 1;
+  int s = (sms + tiles - 1) / tiles;
+  if (s > ktiles) s = ktiles;
+  if (s > 8) s = 8;
+  return s < 1 ? 1 : s;
+}
+
+cudaError_t gemm_init() {
+  cudaError_t e = cudaFuncSetAttribute(k_gemm_q80<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)GemmSmem::bytes(16));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(k_gemm_q80<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GemmSmem::bytes(32));
+  return e;
+}
+
+cudaError_t launch_gemm_q80(const GemmArgs& a, cudaStream_t st, bool pdl) {
+  if (a.N != 16 && a.N != 32) return cudaErrorInvalidValue;
+  if (a.K <= 0 || a.K % kGemmKTile || a.n_valid < 1 || a.n_valid > a.N || a.nseg < 1 || a.nseg > kGemmMaxSegs)
+    return cudaErrorInvalidValue;
+  int rows = 0;
+  for (int i = 0; i < a.nseg; ++i) {
+    if (a.seg[i].rows <= 0 || a.seg[i].rows % kGemmTileRows || !a.seg[i].w) return cudaErrorInvalidValue;
+    rows += a.seg[i].rows;
+  }
+  if (rows != a.rows_total || a.ksplit < 1 || a.ksplit > a.K / kGemmKTile) return cudaErrorInvalidValue;
+  if (a.ksplit > 1 && (!a.partial || !a.counters)) return cudaErrorInvalidValue;
+  const dim3 grid(a.rows_total / kGemmTileRows, a.ksplit);
+  if (a.N == 16) return launch_k(k_gemm_q80<16>, grid, dim3(kThreads), GemmSmem::bytes(16), st, pdl, a);
+  return launch_k(k_gemm_q80<32>, grid, dim3(kThreads), GemmSmem::bytes(32), st, pdl, a);
+}
+
+cudaError_t launch_pack_x16(const float* x, int ld, int n_valid, int K, int N, uint8_t* x16, cudaStream_t st,
+                            bool pdl) {
+  if (K % 8 || n_valid > N) return cudaErrorInvalidValue;
+  const int per = (K / 8 + 127) / 128;
+  return launch_k(k_pack_x16, dim3(per < 1 ? 1 : per, n_valid), dim3(128), 0, st, pdl, x, ld, n_valid, K, N, x16);
+}
+
+cudaError_t launch_rmsnorm_x16(const float* x, int ld, const void* w, int w_dtype, int n_valid, int K, float eps,
+                               int N, uint8_t* x16, cudaStream_t st, bool pdl) {
+  if (K % 8 || n_valid > N) return cudaErrorInvalidValue;
+  return launch_k(k_rmsnorm_x16, dim3(n_valid), dim3(256), 0, st, pdl, x, ld, w, w_dtype, K, eps, N, x16);
+}
+
+cudaError_t launch_swiglu_x16(const float* gu, int F, int n_valid, int N, uint8_t* x16, cudaStream_t st, bool pdl) {
+  if (F % 8 || n_valid > N) return cudaErrorInvalidValue;
+  const int per = (F / 8 + 127) / 128;
+  return launch_k(k_swiglu_x16, dim3(per < 1 ? 1 : per, n_valid), dim3(128), 0, st, pdl, gu, F, n_valid, N, x16);
+}
+
+}  // namespace mcpo

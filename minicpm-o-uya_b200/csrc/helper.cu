@@ -21,6 +21,7 @@
 #include "attention.cuh"
 #include "step.cuh"
 #include "tp.cuh"
+#include "gemm.cuh"
 #include "gemv.cuh"
 #include "layout.cuh"
 #include "minicpmo_gpu.h"
@@ -42,6 +43,8 @@ struct Upload {
   bool tiled = false;
   bool view = false;  // a row range of another upload's device buffer (not owned)
   TileGeom geom{};
+  uint8_t* raw = nullptr;  // Q8_0 only: the GGUF rows as uploaded, for the batched tensor-core path
+  size_t raw_bytes = 0;
 };
 
 struct Slot {
@@ -147,6 +150,13 @@ struct Ctx {
   std::unique_ptr<Model> model;
   uint8_t* tp_buf = nullptr;  // this rank's tensor-parallel exchange buffer (IPC-exported)
   size_t tp_buf_hidden = 0;
+  // batched tensor-core GEMM scratch (matmul_q8_0_batch)
+  uint8_t* bx16 = nullptr;
+  size_t bx16_bytes = 0;
+  float* bpart = nullptr;
+  size_t bpart_bytes = 0;
+  unsigned* bcnt = nullptr;
+  size_t bcnt_bytes = 0;
   int* dev_err = nullptr;  // raised by a device-side bounded wait that gave up
   minicpmo_gpu_stats stats{};
   char last_error[512] = {0};
@@ -264,6 +274,11 @@ int do_upload(Ctx* c, const char* name, const void* host_ptr, size_t bytes, int 
     u->dev = nullptr;
     u->dev_bytes = 0;
   }
+  if (u->raw) {
+    cudaFree(u->raw);
+    u->raw = nullptr;
+    u->raw_bytes = 0;
+  }
   if (name) {
     if (!u->name.empty() && u->name != name) c->by_name.erase(u->name);
     u->name = name;
@@ -304,6 +319,40 @@ int do_upload(Ctx* c, const char* name, const void* host_ptr, size_t bytes, int 
     fprintf(stderr, "minicpmo-gpu: upload tensor=%s bytes=%zu dtype=%d rows=%zu cols=%zu device_bytes=%zu tiled=%d\n",
             name ? name : "(null)", need, dtype, rows, cols, u->dev_bytes, (int)u->tiled);
   return 1;
+}
+
+// Reads and clears the context's device error word (raised by a kernel's
+// bounded wait that gave up); false with a message when it was set.
+bool check_dev_err(Ctx* c, char* err, size_t cap) {
+  int v = 0;
+  if (!cuda_ok(c, cudaMemcpyAsync(&v, c->dev_err, sizeof(int), cudaMemcpyDeviceToHost, c->stream), "error_word_d2h", err,
+               cap) ||
+      !cuda_ok(c, cudaStreamSynchronize(c->stream), "error_word_sync", err, cap))
+    return false;
+  if (v == 0) return true;
+  cudaMemsetAsync(c->dev_err, 0, sizeof(int), c->stream);
+  fail(c, err, cap, "error: a device-side wait gave up (pipeline stalled)");
+  return false;
+}
+
+// The raw GGUF rows of a Q8_0 upload on the device (the batched
+// tensor-core path reads 256-value row pieces), copied once from the
+// borrowed host bytes.
+bool ensure_raw(Ctx* c, Upload* u, char* err, size_t cap) {
+  if (u->raw) return true;
+  if (u->dtype != kQ8_0 || u->cols % 256) {
+    fail(c, err, cap, "error: batched path needs a Q8_0 tensor with cols a multiple of 256 (tensor=%s)", u->name.c_str());
+    return false;
+  }
+  const size_t need = u->rows * gguf_row_bytes(kQ8_0, u->cols);
+  if (!cuda_ok(c, cudaMalloc((void**)&u->raw, need), "weight_raw_malloc", err, cap)) return false;
+  u->raw_bytes = need;
+  if (!cuda_ok(c, cudaMemcpyAsync(u->raw, u->host_ptr, need, cudaMemcpyHostToDevice, c->stream), "weight_raw_h2d", err,
+               cap) ||
+      !cuda_ok(c, cudaStreamSynchronize(c->stream), "weight_raw_sync", err, cap))
+    return false;
+  c->stats.host_to_device_bytes += need;
+  return true;
 }
 
 // One quantised GEMV launch over up to three uploads sharing the input.
@@ -1086,7 +1135,7 @@ int minicpmo_gpu_context_create(unsigned int device_index, int debug, void** out
     return 0;
   }
   c->own_stream = true;
-  if (!cuda_ok(c, gemv_init(), "gemv_init", error, error_cap) ||
+  if (!cuda_ok(c, gemv_init(), "gemv_init", error, error_cap) || !cuda_ok(c, gemm_init(), "gemm_init", error, error_cap) ||
       !cuda_ok(c, attention_init(), "attention_init", error, error_cap) ||
       !cuda_ok(c, decode_step_init(), "decode_step_init", error, error_cap) ||
       !cuda_ok(c, cudaMalloc((void**)&c->dev_err, sizeof(int)), "error_word_malloc", error, error_cap) ||
@@ -1113,13 +1162,15 @@ void minicpmo_gpu_context_destroy(void* handle) {
     if (c->stream) cudaStreamSynchronize(c->stream);
     if (c->model) free_model(c->model.get());
     c->model.reset();
-    for (auto& u : c->uploads)
+    for (auto& u : c->uploads) {
       if (u->dev) cudaFree(u->dev);
+      if (u->raw) cudaFree(u->raw);
+    }
     for (auto& s : c->slots)
       if (s.ptr) cudaFree(s.ptr);
     void* bufs[] = {c->stage, c->xq, c->sx, c->sy, c->dots, c->k_cache, c->v_cache, c->attn_partial, c->attn_counters,
                     c->rope_cos, c->rope_sin, c->am_scratch, c->am_counter, c->am_state, c->am_seen, c->dev_err,
-                    c->tp_buf};
+                    c->tp_buf, c->bx16, c->bpart, c->bcnt};
     for (void* p : bufs)
       if (p) cudaFree(p);
     if (c->am_state_host) cudaFreeHost(c->am_state_host);
@@ -1905,6 +1956,64 @@ int minicpmo_gpu_context_matvec_q8_1(void* handle, const void* host_ptr, const v
     ok = cuda_ok(c, cudaMemcpyAsync(dots_out, c->dots, out_dim * per_row * 4, cudaMemcpyDeviceToHost, c->stream), "mv_d2h",
                  error, error_cap);
   if (ok) ok = cuda_ok(c, cudaStreamSynchronize(c->stream), "mv_sync", error, error_cap);
+  return ok ? 1 : 0;
+}
+
+int minicpmo_gpu_context_matmul_q8_0_batch(void* handle, const void* host_ptr, const float* x, size_t n_seq,
+                                           size_t in_dim, size_t out_dim, float* y_out, char* error, size_t error_cap) {
+  Ctx* c = (Ctx*)handle;
+  if (!c) return copy_error(error, error_cap, "error: null gpu context"), 0;
+  DeviceGuard g(c);
+  Upload* u = find_upload(c, host_ptr);
+  if (!u || !x || !y_out) return fail(c, error, error_cap, "error: matmul_q8_0_batch needs an uploaded Q8_0 tensor");
+  if (u->cols != in_dim || u->rows != out_dim) return fail(c, error, error_cap, "error: matmul_q8_0_batch shape mismatch");
+  if (n_seq < 1 || n_seq > (size_t)kGemmMaxN)
+    return fail(c, error, error_cap, "error: matmul_q8_0_batch n_seq=%zu outside 1..%d", n_seq, kGemmMaxN);
+  if (out_dim % kGemmTileRows || in_dim % kGemmKTile)
+    return fail(c, error, error_cap, "error: matmul_q8_0_batch needs rows %% %d == 0 and cols %% %d == 0", kGemmTileRows,
+                kGemmKTile);
+  if (!ensure_raw(c, u, error, error_cap)) return 0;
+  const int N = n_seq <= 16 ? 16 : 32;
+  const int tiles = (int)(out_dim / kGemmTileRows), ktiles = (int)(in_dim / kGemmKTile);
+  const int ks = gemm_pick_ksplit(tiles, ktiles, c->sm_count);
+  if (!ensure(c, &c->sx, &c->sx_bytes, n_seq * in_dim * 4, "scratch_x_malloc", error, error_cap) ||
+      !ensure(c, &c->sy, &c->sy_bytes, n_seq * out_dim * 4, "scratch_y_malloc", error, error_cap) ||
+      !ensure(c, &c->bx16, &c->bx16_bytes, (size_t)N * in_dim * 2, "batch_x16_malloc", error, error_cap))
+    return 0;
+  if (ks > 1) {
+    const bool grow = c->bcnt_bytes < (size_t)tiles * 4;
+    if (!ensure(c, &c->bpart, &c->bpart_bytes, (size_t)ks * N * out_dim * 4, "batch_partial_malloc", error, error_cap) ||
+        !ensure(c, &c->bcnt, &c->bcnt_bytes, (size_t)tiles * 4, "batch_counter_malloc", error, error_cap))
+      return 0;
+    if (grow && !cuda_ok(c, cudaMemsetAsync(c->bcnt, 0, c->bcnt_bytes, c->stream), "batch_counter_memset", error, error_cap))
+      return 0;
+  }
+  GemmArgs a{};
+  a.seg[0].w = u->raw;
+  a.seg[0].rows = (int)out_dim;
+  a.nseg = 1;
+  a.rows_total = (int)out_dim;
+  a.K = (int)in_dim;
+  a.x = c->bx16;
+  a.N = N;
+  a.n_valid = (int)n_seq;
+  a.y = c->sy;
+  a.ldy = (int)out_dim;
+  a.epi = kGemmStore;
+  a.ksplit = ks;
+  a.partial = c->bpart;
+  a.counters = c->bcnt;
+  a.err = c->dev_err;
+  bool ok = cuda_ok(c, cudaMemsetAsync(c->bx16, 0, (size_t)N * in_dim * 2, c->stream), "mm_x16_memset", error, error_cap) &&
+            cuda_ok(c, cudaMemcpyAsync(c->sx, x, n_seq * in_dim * 4, cudaMemcpyHostToDevice, c->stream), "mm_h2d", error,
+                    error_cap) &&
+            cuda_ok(c, launch_pack_x16(c->sx, (int)in_dim, (int)n_seq, (int)in_dim, N, c->bx16, c->stream), "mm_pack",
+                    error, error_cap) &&
+            cuda_ok(c, launch_gemm_q80(a, c->stream), "mm_gemm", error, error_cap) &&
+            cuda_ok(c, cudaMemcpyAsync(y_out, c->sy, n_seq * out_dim * 4, cudaMemcpyDeviceToHost, c->stream), "mm_d2h",
+                    error, error_cap) &&
+            cuda_ok(c, cudaStreamSynchronize(c->stream), "mm_sync", error, error_cap);
+  if (ok && !check_dev_err(c, error, error_cap)) ok = false;
   return ok ? 1 : 0;
 }
 

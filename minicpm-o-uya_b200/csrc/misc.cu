@@ -68,11 +68,14 @@ __device__ __forceinline__ uint8_t tb(const uint8_t* w, const TileGeom& g, int r
   return w[tiled_byte_offset(g, row, sb, o)];
 }
 
+// Sequence blockIdx.y reads its token at tok_ptr[y * tok_stride] and
+// writes out + y * hidden.
 __global__ void k_embed(const uint8_t* __restrict__ w, TileGeom g, int dtype, int rows, int hidden, const int* tok_ptr,
-                        int tok_static, float* __restrict__ out) {
+                        int tok_static, float* __restrict__ out, int tok_stride) {
   pdl_wait();
   pdl_launch_dependents();
-  const int token = tok_ptr ? *tok_ptr : tok_static;
+  const int token = tok_ptr ? tok_ptr[(size_t)blockIdx.y * tok_stride] : tok_static;
+  out += (size_t)blockIdx.y * hidden;
   if (token < 0 || token >= rows) {  // never index outside the table; the host validates ids
     for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < hidden; e += gridDim.x * blockDim.x) out[e] = 0.0f;
     return;
@@ -165,6 +168,13 @@ __global__ void __launch_bounds__(256) k_argmax(const float* __restrict__ logits
                                                 int history_cap, int vocab_base, float* tp_top) {
   pdl_wait();
   pdl_launch_dependents();
+  // independent sequences along grid y: logits, scratch, counter, state and
+  // history of sequence y
+  logits += (size_t)blockIdx.y * n;
+  scratch += (size_t)blockIdx.y * gridDim.x * 3;
+  counter += blockIdx.y;
+  st += blockIdx.y;
+  if (history) history += (size_t)blockIdx.y * history_cap;
   const float penalty = st->penalty;
   Top2 t{-INFINITY, 0x7fffffff, -INFINITY};
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
@@ -276,17 +286,19 @@ cudaError_t launch_relayout(const uint8_t* src, uint8_t* dst, const TileGeom& g,
 }
 
 cudaError_t launch_embed(const uint8_t* w, const TileGeom& g, int dtype, int rows, int hidden, const int* tok_ptr, int tok,
-                         float* out, cudaStream_t st, bool pdl) {
+                         float* out, cudaStream_t st, bool pdl, int batch, int tok_stride) {
   const int grid = (hidden + 255) / 256;
-  return launch_k(k_embed, dim3(grid), dim3(256), 0, st, pdl, w, g, dtype, rows, hidden, tok_ptr, tok, out);
+  return launch_k(k_embed, dim3(grid, batch < 1 ? 1 : batch), dim3(256), 0, st, pdl, w, g, dtype, rows, hidden, tok_ptr,
+                  tok, out, tok_stride);
 }
 
 cudaError_t launch_argmax(const float* logits, int n, const uint32_t* seen_bits, float* scratch, unsigned* counter,
                           StepState* st, int* history, int history_cap, int grid, cudaStream_t s, bool pdl,
-                          int vocab_base, float* tp_top) {
+                          int vocab_base, float* tp_top, int batch) {
   if (grid <= 0) grid = 1;
-  return launch_k(k_argmax, dim3(grid), dim3(256), 0, s, pdl, logits, n, seen_bits, scratch, counter, st, history,
-                  history_cap, vocab_base, tp_top);
+  if (batch > 1 && (seen_bits || tp_top)) return cudaErrorInvalidValue;
+  return launch_k(k_argmax, dim3(grid, batch < 1 ? 1 : batch), dim3(256), 0, s, pdl, logits, n, seen_bits, scratch,
+                  counter, st, history, history_cap, vocab_base, tp_top);
 }
 
 cudaError_t launch_mark_seen(uint32_t* bits, const StepState* st, int vocab, cudaStream_t s, bool pdl) {

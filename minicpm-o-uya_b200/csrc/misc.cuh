@@ -24,16 +24,21 @@ struct StepState {
 };
 
 cudaError_t launch_relayout(const uint8_t* src, uint8_t* dst, const TileGeom& g, size_t row_bytes, cudaStream_t st);
-// token (from tok_ptr when non-null) outside [0, rows) yields zeros.
+// token (from tok_ptr when non-null) outside [0, rows) yields zeros.  batch
+// sequences: sequence b's token at tok_ptr[b * tok_stride], its row at
+// out + b * hidden.
 cudaError_t launch_embed(const uint8_t* w, const TileGeom& g, int dtype, int rows, int hidden, const int* tok_ptr, int tok,
-                         float* out, cudaStream_t st, bool pdl = false);
+                         float* out, cudaStream_t st, bool pdl = false, int batch = 1, int tok_stride = 0);
 // grid CTAs; scratch holds 3 floats per CTA; counter is zero at rest.
 // history (may be null) receives next_token at history_len when auto-advancing.
 // vocab_base/tp_top: a tensor-parallel vocab slice -- indices are offset by
 // vocab_base and the result (best, index, second) goes to tp_top instead of st.
+// batch > 1: independent sequences -- logits [batch][n], scratch
+// [batch][grid*3], counter [batch], st [batch], history [batch][history_cap];
+// no repeat penalty (seen_bits null) and no vocab slices.
 cudaError_t launch_argmax(const float* logits, int n, const uint32_t* seen_bits, float* scratch, unsigned* counter,
                           StepState* st, int* history, int history_cap, int grid, cudaStream_t s, bool pdl = false,
-                          int vocab_base = 0, float* tp_top = nullptr);
+                          int vocab_base = 0, float* tp_top = nullptr, int batch = 1);
 cudaError_t launch_mark_seen(uint32_t* bits, const StepState* st, int vocab, cudaStream_t s, bool pdl = false);
 cudaError_t launch_add_inplace(float* dst, const float* src, int n, cudaStream_t st);
 cudaError_t launch_silu_mul(float* dst, const float* gate, const float* up, int n, cudaStream_t st);

@@ -134,6 +134,7 @@ SIGNATURES = {
     "minicpmo_gpu_context_matvec_q8_1": (i32, [vp, vp, vp, sz, sz, fptr, i32ptr] + E),
     "minicpmo_gpu_context_matvec_f32_input": (i32, [vp, vp, fptr, vp, f32, sz, sz, fptr] + E),
     "minicpmo_gpu_context_time_matvec_input": (i32, [vp, vp, sz, sz, i32, i32, vp, fptr] + E),
+    "minicpmo_gpu_context_matmul_q8_0_batch": (i32, [vp, vp, fptr, sz, sz, sz, fptr] + E),
     "minicpmo_gpu_context_time_matvec": (i32, [vp, vp, sz, sz, i32, fptr] + E),
     "minicpmo_gpu_context_qwen3_time_decode": (i32, [vp, u32, sz, sz, fptr] + E),
     "minicpmo_gpu_context_tensor_device_bytes": (sz, [vp, vp]),
@@ -386,6 +387,15 @@ class GpuContext:
         y = np.empty(t.rows, np.float32)
         self._call("minicpmo_gpu_context_matvec_f32_input", t.ptr, _f(x), norm.ptr if norm is not None else None, eps,
                    t.cols, t.rows, _f(y))
+        return y
+
+    def matmul_q8_0_batch(self, t: Tensor, x) -> np.ndarray:
+        """Tensor-core batched projection: rows of x [n, cols] -> [n, rows] (f16 operands, f32 sums)."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        if x.ndim != 2 or x.shape[1] != t.cols:
+            raise ValueError("x must be [n_seq, cols]")
+        y = np.empty((x.shape[0], t.rows), np.float32)
+        self._call("minicpmo_gpu_context_matmul_q8_0_batch", t.ptr, _f(x), x.shape[0], t.cols, t.rows, _f(y))
         return y
 
     def time_matvec_input(self, t: Tensor, input_mode: int, norm: Optional[Tensor] = None, iters: int = 20) -> float:
