@@ -160,7 +160,9 @@ typedef struct minicpmo_qwen3_config {
     const float *rope_cos;  /* host tables [context][head_dim/2] or NULL: */
     const float *rope_sin;  /*   then built as qwen3_precompute_rope (qwen3.uya:1633-1662) */
     int kv_f16;             /* 0: f32 KV cache (reference); 1: f16 */
-    int max_batch;          /* sequences for forward_batch (0 -> 1) */
+    int max_batch;          /* sequences of the batched decode (forward_batch,
+                               decode_batch): 0 or 1 -> none; 2..32 needs every
+                               linear weight Q8_0 */
     int decode_mode;        /* 0: the default (currently 1, the faster one measured);
                                1: one kernel per operation (a CUDA graph of ~5 per
                                layer); 2: one persistent kernel per decode step when
@@ -208,6 +210,35 @@ MINICPMO_API int minicpmo_gpu_context_qwen3_reset(void *handle, char *error, siz
  * round trips).  tokens_out[n_steps] receives the sampled ids. */
 MINICPMO_API int minicpmo_gpu_context_qwen3_decode(void *handle, uint32_t first_token, size_t first_pos, size_t n_steps,
                                       float repeat_penalty, uint32_t *tokens_out, char *error, size_t error_cap);
+
+/* ---- batched decode of independent sequences (config: all linear weights
+ * Q8_0; no reference counterpart -- the reference decodes one sequence,
+ * qwen3.uya:2412-2639, and has no GPU Q8_0 path, gpu.uya:130-132) ----
+ * Bound by qwen3_bind with max_batch in 2..32: every linear weight (q, k, v,
+ * o, gate, up, down, lm_head) must be Q8_0 with rows % 128 == 0 and
+ * cols % 256 == 0.  The projections run on the tensor cores (weights and
+ * activations rounded to f16, sums in f32); every sequence has its own KV
+ * cache ([layer][sequence][context][kv_dim]), position and greedy sampler
+ * (no repeat penalty).  n_seq must equal max_batch. */
+/* One step: sequence i forwards tokens[i] at positions[i].  flags bit 0:
+ * skip the lm_head and samplers (prompt positions).  out_tokens /
+ * out_top2_gaps [n_seq] and logits_out [n_seq][vocab] may be NULL. */
+MINICPMO_API int minicpmo_gpu_context_qwen3_forward_batch(void *handle, size_t n_seq, const uint32_t *tokens,
+                                             const uint32_t *positions, int flags, uint32_t *out_tokens,
+                                             float *out_top2_gaps, float *logits_out, char *error,
+                                             size_t error_cap);
+/* Greedy decode of n_steps tokens per sequence on the device, feeding each
+ * sampled token back; tokens_out [n_seq][n_steps] (may be NULL). */
+MINICPMO_API int minicpmo_gpu_context_qwen3_decode_batch(void *handle, size_t n_seq, const uint32_t *first_tokens,
+                                            const uint32_t *first_positions, size_t n_steps, uint32_t *tokens_out,
+                                            char *error, size_t error_cap);
+/* Device time of n_steps batched decode steps (graph replays, CUDA events
+ * on the context stream); total_ms over all steps. */
+MINICPMO_API int minicpmo_gpu_context_qwen3_time_decode_batch(void *handle, size_t n_seq, const uint32_t *first_tokens,
+                                                 const uint32_t *first_positions, size_t n_steps, float *total_ms,
+                                                 char *error, size_t error_cap);
+/* Kernel launches in one batched step's graph; 0 without a batched model. */
+MINICPMO_API int minicpmo_gpu_context_qwen3_batch_kernels(void *handle, int with_logits);
 
 /* ---- parity and measurement helpers (no reference counterpart) ---- */
 

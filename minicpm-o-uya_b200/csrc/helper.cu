@@ -56,8 +56,33 @@ struct LayerW {
   Upload *attn_norm, *q, *k, *v, *q_norm, *k_norm, *o, *ffn_norm, *gate, *up, *down;
 };
 
+// Batched decode of max_batch independent sequences (all linear weights
+// Q8_0): the projections run on the tensor cores over the raw GGUF rows,
+// each sequence has its own KV cache, position and sampler state.
+struct BatchState {
+  int B = 0, N = 0;  // sequences; operand rows of the tensor-core GEMM (16 or 32)
+  size_t ldqkv = 0;  // q | k | v row of one sequence
+  float *hidden = nullptr, *qkv = nullptr, *attn = nullptr, *gu = nullptr, *logits = nullptr;
+  uint8_t* x16 = nullptr;  // f16 operand of the next projection
+  float* part = nullptr;   // split-K partial sums
+  unsigned* cnt = nullptr;
+  void *kc = nullptr, *vc = nullptr;  // [layer][sequence][context][kv_dim]
+  float* attn_partial = nullptr;
+  unsigned* attn_counters = nullptr;
+  StepState* st = nullptr;       // [B]
+  StepState* st_host = nullptr;  // pinned [B]
+  float* am_scratch = nullptr;
+  unsigned* am_counter = nullptr;
+  int* history = nullptr;  // [B][history_cap]
+  int history_cap = 0;
+  int am_grid = 0;
+  cudaGraphExec_t exec[2] = {nullptr, nullptr};
+  int kernels[2] = {0, 0};
+};
+
 struct Model {
   minicpmo_qwen3_config cfg{};
+  std::unique_ptr<BatchState> batch;
   std::vector<LayerW> layer;
   Upload *tok = nullptr, *out_norm = nullptr, *out = nullptr;
   size_t qd = 0, kvd = 0;
@@ -427,8 +452,22 @@ int check_attention_shape(Ctx* c, size_t layer, size_t pos, size_t n_head, size_
 // ---------------------------------------------------------------------
 // Qwen3 decode step as one graph
 // ---------------------------------------------------------------------
+void free_batch(BatchState* b) {
+  if (!b) return;
+  for (auto& e : b->exec)
+    if (e) cudaGraphExecDestroy(e), e = nullptr;
+  void* bufs[] = {b->hidden, b->qkv, b->attn, b->gu, b->logits, b->x16, b->part, b->cnt, b->kc, b->vc,
+                  b->attn_partial, b->attn_counters, b->st, b->am_scratch, b->am_counter, b->history};
+  for (void* p : bufs)
+    if (p) cudaFree(p);
+  if (b->st_host) cudaFreeHost(b->st_host);
+  b->st_host = nullptr;
+}
+
 void free_model(Model* m) {
   if (!m) return;
+  if (m->batch) free_batch(m->batch.get());
+  m->batch.reset();
   for (auto& e : m->exec)
     if (e) cudaGraphExecDestroy(e);
   void* bufs[] = {m->hidden, m->normed, m->q,     m->k,       m->v,         m->attn,       m->gate,     m->up,
@@ -627,6 +666,255 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
     }
   }
   return cudaSuccess;
+}
+
+// One tensor-core projection launch of the batched step over up to three
+// matrices sharing the input operand b.x16.
+cudaError_t batch_gemm(Ctx* c, Model& m, Upload* const* w, int n, int K, float* y, int ldy, int epi) {
+  BatchState& b = *m.batch;
+  GemmArgs g{};
+  g.nseg = n;
+  int rows = 0;
+  for (int i = 0; i < n; ++i) {
+    g.seg[i].w = w[i]->raw;
+    g.seg[i].rows = (int)w[i]->rows;
+    rows += (int)w[i]->rows;
+  }
+  g.rows_total = rows;
+  g.K = K;
+  g.x = b.x16;
+  g.N = b.N;
+  g.n_valid = b.B;
+  g.y = y;
+  g.ldy = ldy;
+  g.epi = epi;
+  g.ksplit = gemm_pick_ksplit(rows / kGemmTileRows, K / kGemmKTile, c->sm_count);
+  g.partial = b.part;
+  g.counters = b.cnt;
+  g.err = &b.st[0].err;
+  return launch_gemm_q80(g, c->stream, true);
+}
+
+// The batched decode step: embed -> per layer [RMSNorm -> q|k|v (tensor
+// cores) -> attention (batch grid, fused QK-norm/RoPE/append) -> o (+=) ->
+// RMSNorm -> gate|up -> SwiGLU -> down (+=)] -> RMSNorm -> lm_head ->
+// per-sequence greedy sampler.  The activations between projections are
+// f16 operands; norms, attention and sampling are f32 as in the
+// single-sequence step.
+cudaError_t record_batch_step(Ctx* c, Model& m, bool logits) {
+  const auto& cf = m.cfg;
+  BatchState& b = *m.batch;
+  cudaStream_t s = c->stream;
+  const int h = (int)cf.hidden, f = (int)cf.ffn, hd = (int)cf.head_dim, B = b.B, N = b.N;
+  const int qd = (int)m.qd, kvd = (int)m.kvd;
+  const int sst = (int)(sizeof(StepState) / sizeof(int));
+  REC(launch_embed(m.tok->dev, m.tok->geom, m.tok->dtype, (int)m.tok->rows, h, &b.st[0].token, 0, b.hidden, s, true, B,
+                   sst));
+  const size_t esz = cf.kv_f16 ? 2 : 4;
+  for (uint32_t li = 0; li < cf.layers; ++li) {
+    LayerW& L = m.layer[li];
+    REC(launch_rmsnorm_x16(b.hidden, h, L.attn_norm->dev, L.attn_norm->dtype, B, h, cf.rms_eps, N, b.x16, s, true));
+    Upload* qkv[3] = {L.q, L.k, L.v};
+    REC(batch_gemm(c, m, qkv, 3, h, b.qkv, (int)b.ldqkv, kGemmStore));
+    AttnArgs a{};
+    a.q = b.qkv;
+    a.k = b.qkv + qd;
+    a.v = b.qkv + qd + kvd;
+    a.fuse_norm_rope_append = 1;
+    a.q_norm = L.q_norm ? L.q_norm->dev : nullptr;
+    a.q_norm_dtype = L.q_norm ? L.q_norm->dtype : 0;
+    a.k_norm = L.k_norm ? L.k_norm->dev : nullptr;
+    a.k_norm_dtype = L.k_norm ? L.k_norm->dtype : 0;
+    a.rope_cos = m.rope_cos;
+    a.rope_sin = m.rope_sin;
+    a.rope_base = cf.rope_freq_base;
+    a.rope_scale = cf.rope_freq_scale;
+    const size_t layer_elems = (size_t)B * cf.context * kvd;
+    a.k_cache = (uint8_t*)b.kc + li * layer_elems * esz;
+    a.v_cache = (uint8_t*)b.vc + li * layer_elems * esz;
+    a.kv_f16 = cf.kv_f16;
+    a.pos_ptr = &b.st[0].pos;
+    a.pos_stride = sst;
+    a.n_head = (int)cf.heads;
+    a.n_kv = (int)cf.kv_heads;
+    a.head_dim = hd;
+    a.ctx = (int)cf.context;
+    a.n_split = m.n_split;
+    a.cluster = attn_cluster_cfg();
+    a.scale = 1.0f / sqrtf((float)hd);
+    a.partial = b.attn_partial;
+    a.counters = b.attn_counters;
+    a.out = b.attn;
+    a.out_q8 = nullptr;
+    a.batch = B;
+    a.qkv_bstride = b.ldqkv;
+    a.cache_bstride = (size_t)cf.context * kvd;
+    a.out_bstride = (size_t)qd;
+    REC(launch_attention(a, s, true));
+    REC(launch_pack_x16(b.attn, qd, B, qd, N, b.x16, s, true));
+    Upload* o[1] = {L.o};
+    REC(batch_gemm(c, m, o, 1, qd, b.hidden, h, kGemmAdd));
+    REC(launch_rmsnorm_x16(b.hidden, h, L.ffn_norm->dev, L.ffn_norm->dtype, B, h, cf.rms_eps, N, b.x16, s, true));
+    Upload* gu[2] = {L.gate, L.up};
+    REC(batch_gemm(c, m, gu, 2, h, b.gu, 2 * f, kGemmStore));
+    REC(launch_swiglu_x16(b.gu, f, B, N, b.x16, s, true));
+    Upload* dn[1] = {L.down};
+    REC(batch_gemm(c, m, dn, 1, f, b.hidden, h, kGemmAdd));
+  }
+  if (logits) {
+    REC(launch_rmsnorm_x16(b.hidden, h, m.out_norm->dev, m.out_norm->dtype, B, h, cf.rms_eps, N, b.x16, s, true));
+    Upload* lm[1] = {m.out};
+    REC(batch_gemm(c, m, lm, 1, h, b.logits, (int)cf.vocab, kGemmStore));
+    REC(launch_argmax(b.logits, (int)cf.vocab, nullptr, b.am_scratch, b.am_counter, b.st, b.history, b.history_cap,
+                      b.am_grid, s, true, 0, nullptr, B));
+  }
+  return cudaSuccess;
+}
+
+int build_batch_graph(Ctx* c, Model& m, int which, char* err, size_t cap) {
+  BatchState& b = *m.batch;
+  cudaGraph_t g = nullptr;
+  if (!cuda_ok(c, cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal), "batch_graph_begin", err, cap))
+    return 0;
+  b.kernels[which] = 0;
+  m.rec_count = &b.kernels[which];
+  cudaError_t rec = record_batch_step(c, m, which == 0);
+  m.rec_count = nullptr;
+  cudaError_t end = cudaStreamEndCapture(c->stream, &g);
+  if (rec != cudaSuccess) {
+    if (g) cudaGraphDestroy(g);
+    cuda_ok(c, rec, "batch_graph_record", err, cap);
+    return 0;
+  }
+  if (!cuda_ok(c, end, "batch_graph_end", err, cap)) return 0;
+  cudaError_t inst = cudaGraphInstantiate(&b.exec[which], g, 0);
+  cudaGraphDestroy(g);
+  return cuda_ok(c, inst, "batch_graph_instantiate", err, cap) ? 1 : 0;
+}
+
+// Batched decode set-up for cfg.max_batch > 1: every linear weight Q8_0
+// (rows a multiple of 128, inputs of 256), a raw-row device copy of each,
+// per-sequence caches and states, and the two step graphs.
+int bind_batch(Ctx* c, Model& m, char* err, size_t cap) {
+  const auto& cf = m.cfg;
+  const int B = cf.max_batch;
+  if (B < 2 || B > kGemmMaxN) return fail(c, err, cap, "error: qwen3 bind: max_batch %d outside 2..%d", B, kGemmMaxN);
+  if (m.tp_world > 1) return fail(c, err, cap, "error: qwen3 bind: batched decode is single-GPU (run one replica per GPU)");
+  std::vector<Upload*> lin;
+  for (auto& L : m.layer) {
+    Upload* u[7] = {L.q, L.k, L.v, L.o, L.gate, L.up, L.down};
+    lin.insert(lin.end(), u, u + 7);
+  }
+  lin.push_back(m.out);
+  for (Upload* u : lin) {
+    if (u->dtype != kQ8_0 || u->rows % kGemmTileRows || u->cols % kGemmKTile)
+      return fail(c, err, cap,
+                  "error: qwen3 bind: batched decode needs every linear weight Q8_0 with rows %% %d == 0 and cols %% %d "
+                  "== 0 (tensor=%s)",
+                  kGemmTileRows, kGemmKTile, u->name.c_str());
+    if (!ensure_raw(c, u, err, cap)) return 0;
+  }
+  m.batch.reset(new BatchState());
+  BatchState& b = *m.batch;
+  b.B = B;
+  b.N = B <= 16 ? 16 : 32;
+  b.ldqkv = m.qd + 2 * m.kvd;
+  const size_t h = cf.hidden, f = cf.ffn, V = cf.vocab, hd = cf.head_dim;
+  const size_t kmax = std::max(std::max(h, f), m.qd);
+  // split-K scratch: the largest launch of the step
+  size_t part = 0, tiles_max = 0;
+  auto acc = [&](size_t rows, size_t K) {
+    const int ks = gemm_pick_ksplit((int)(rows / kGemmTileRows), (int)(K / kGemmKTile), c->sm_count);
+    part = std::max(part, (size_t)ks * b.N * rows * 4);
+    tiles_max = std::max(tiles_max, rows / kGemmTileRows);
+  };
+  acc(b.ldqkv, h);
+  acc(h, m.qd);
+  acc(2 * f, h);
+  acc(h, f);
+  acc(V, h);
+  const size_t esz = cf.kv_f16 ? 2 : 4;
+  const size_t kv_bytes = (size_t)cf.layers * B * cf.context * m.kvd * esz;
+  b.am_grid = c->sm_count;
+  b.history_cap = 1 << 14;
+  struct A {
+    void** p;
+    size_t bytes;
+  } allocs[] = {
+      {(void**)&b.hidden, B * h * 4},
+      {(void**)&b.qkv, B * b.ldqkv * 4},
+      {(void**)&b.attn, B * m.qd * 4},
+      {(void**)&b.gu, B * 2 * f * 4},
+      {(void**)&b.logits, B * V * 4},
+      {(void**)&b.x16, (size_t)b.N * kmax * 2},
+      {(void**)&b.part, part > 0 ? part : 4},
+      {(void**)&b.cnt, tiles_max * 4 + 4},
+      {&b.kc, kv_bytes},
+      {&b.vc, kv_bytes},
+      {(void**)&b.attn_partial, (size_t)B * attn_partial_floats((int)cf.heads, m.n_split, (int)hd) * 4},
+      {(void**)&b.attn_counters, (size_t)B * cf.kv_heads * 4},
+      {(void**)&b.st, B * sizeof(StepState)},
+      {(void**)&b.am_scratch, (size_t)B * b.am_grid * 3 * 4},
+      {(void**)&b.am_counter, (size_t)B * 4},
+      {(void**)&b.history, (size_t)B * b.history_cap * 4},
+  };
+  for (auto& a : allocs) {
+    if (!cuda_ok(c, cudaMalloc(a.p, a.bytes), "qwen3_bind_batch_malloc", err, cap)) return 0;
+    if (!cuda_ok(c, cudaMemsetAsync(*a.p, 0, a.bytes, c->stream), "qwen3_bind_batch_memset", err, cap)) return 0;
+  }
+  if (!cuda_ok(c, cudaMallocHost((void**)&b.st_host, B * sizeof(StepState)), "qwen3_bind_batch_pinned", err, cap))
+    return 0;
+  memset(b.st_host, 0, B * sizeof(StepState));
+  c->stats.kv_device_bytes += 2 * kv_bytes;
+  if (!cuda_ok(c, cudaStreamSynchronize(c->stream), "qwen3_bind_batch_sync", err, cap)) return 0;
+  return build_batch_graph(c, m, 0, err, cap) && build_batch_graph(c, m, 1, err, cap);
+}
+
+// Copies the batch states in, runs `steps` graph replays (which 0: with the
+// lm_head and sampler), optionally times them with events, and copies the
+// states back.  Sequences' token/pos come from tokens/pos (n = B).
+int run_batch(Ctx* c, Model& m, const uint32_t* tokens, const uint32_t* pos, int which, size_t steps, int advance,
+              float* total_ms, char* err, size_t cap) {
+  BatchState& b = *m.batch;
+  for (int i = 0; i < b.B; ++i) {
+    if (tokens[i] >= m.cfg.vocab) return fail(c, err, cap, "error: qwen3 batch: token %u >= vocab", tokens[i]);
+    if ((size_t)pos[i] + (advance ? steps : 1) > m.cfg.context)
+      return fail(c, err, cap, "error: qwen3 batch: sequence %d pos=%u steps=%zu exceeds context %u", i, pos[i], steps,
+                  m.cfg.context);
+    StepState& h = b.st_host[i];
+    memset(&h, 0, sizeof(StepState));
+    h.token = (int)tokens[i];
+    h.pos = (int)pos[i];
+    h.penalty = 1.0f;
+    h.auto_advance = advance;
+  }
+  if (advance && steps > (size_t)b.history_cap) return fail(c, err, cap, "error: qwen3 batch: too many steps");
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  if (total_ms) {
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+  }
+  bool ok = cuda_ok(c, cudaMemcpyAsync(b.st, b.st_host, b.B * sizeof(StepState), cudaMemcpyHostToDevice, c->stream),
+                    "batch_state_h2d", err, cap);
+  if (ok && e0) cudaEventRecord(e0, c->stream);
+  for (size_t i = 0; ok && i < steps; ++i)
+    ok = cuda_ok(c, cudaGraphLaunch(b.exec[which], c->stream), "batch_graph_launch", err, cap);
+  if (ok && e1) cudaEventRecord(e1, c->stream);
+  if (ok)
+    ok = cuda_ok(c, cudaMemcpyAsync(b.st_host, b.st, b.B * sizeof(StepState), cudaMemcpyDeviceToHost, c->stream),
+                 "batch_state_d2h", err, cap);
+  if (ok) ok = cuda_ok(c, cudaStreamSynchronize(c->stream), "batch_sync", err, cap);
+  for (int i = 0; ok && i < b.B; ++i)
+    if (b.st_host[i].err) ok = fail(c, err, cap, "error: qwen3 batch: a bounded device wait gave up (step aborted)");
+  if (ok && total_ms) cudaEventElapsedTime(total_ms, e0, e1);
+  if (e0) cudaEventDestroy(e0);
+  if (e1) cudaEventDestroy(e1);
+  if (ok) {
+    c->stats.host_to_device_bytes += b.B * sizeof(StepState);
+    c->stats.device_to_host_bytes += b.B * sizeof(StepState);
+    c->stats.attention_kernel_calls += steps * m.cfg.layers;
+  }
+  return ok ? 1 : 0;
 }
 
 // The stage list of the persistent step kernel, or false when the model
@@ -1075,6 +1363,10 @@ int bind_model(Ctx* c, const minicpmo_qwen3_config* cfg, char* err, size_t cap, 
     m.step_ok = false;
   }
   if (!m.step_ok && (!build_graph(c, m, 0, err, cap) || !build_graph(c, m, 1, err, cap))) {
+    free_model(&m);
+    return 0;
+  }
+  if (cf.max_batch > 1 && !bind_batch(c, m, err, cap)) {
     free_model(&m);
     return 0;
   }
@@ -1885,6 +2177,78 @@ int minicpmo_gpu_context_qwen3_time_decode(void* handle, uint32_t first_token, s
   const int ok = decode_loop(c, first_token, first_pos, n_steps, 1.0f, nullptr, &ms, error, error_cap);
   if (ok && total_ms) *total_ms = ms;
   return ok;
+}
+
+int minicpmo_gpu_context_qwen3_forward_batch(void* handle, size_t n_seq, const uint32_t* tokens, const uint32_t* positions,
+                                             int flags, uint32_t* out_tokens, float* out_top2_gaps, float* logits_out,
+                                             char* error, size_t error_cap) {
+  Ctx* c = (Ctx*)handle;
+  if (!c) return copy_error(error, error_cap, "error: null gpu context"), 0;
+  DeviceGuard g(c);
+  if (!c->model || !c->model->batch) return fail(c, error, error_cap, "error: qwen3 forward_batch: no batched model bound");
+  Model& m = *c->model;
+  BatchState& b = *m.batch;
+  if (n_seq != (size_t)b.B || !tokens || !positions)
+    return fail(c, error, error_cap, "error: qwen3 forward_batch: n_seq=%zu must equal max_batch=%d", n_seq, b.B);
+  const int which = (flags & 1) ? 1 : 0;
+  if (!run_batch(c, m, tokens, positions, which, 1, 0, nullptr, error, error_cap)) return 0;
+  for (int i = 0; i < b.B; ++i) {
+    if (out_tokens) out_tokens[i] = which == 0 ? (uint32_t)b.st_host[i].next_token : 0u;
+    if (out_top2_gaps) out_top2_gaps[i] = which == 0 ? b.st_host[i].gap : 0.0f;
+  }
+  if (logits_out && which == 0) {
+    const size_t bytes = (size_t)b.B * m.cfg.vocab * 4;
+    if (!cuda_ok(c, cudaMemcpy(logits_out, b.logits, bytes, cudaMemcpyDeviceToHost), "forward_batch_logits_d2h", error,
+                 error_cap))
+      return 0;
+    c->stats.device_to_host_bytes += bytes;
+  }
+  return 1;
+}
+
+int minicpmo_gpu_context_qwen3_decode_batch(void* handle, size_t n_seq, const uint32_t* first_tokens,
+                                            const uint32_t* first_positions, size_t n_steps, uint32_t* tokens_out,
+                                            char* error, size_t error_cap) {
+  Ctx* c = (Ctx*)handle;
+  if (!c) return copy_error(error, error_cap, "error: null gpu context"), 0;
+  DeviceGuard g(c);
+  if (!c->model || !c->model->batch) return fail(c, error, error_cap, "error: qwen3 decode_batch: no batched model bound");
+  Model& m = *c->model;
+  BatchState& b = *m.batch;
+  if (n_seq != (size_t)b.B || !first_tokens || !first_positions)
+    return fail(c, error, error_cap, "error: qwen3 decode_batch: n_seq=%zu must equal max_batch=%d", n_seq, b.B);
+  if (!run_batch(c, m, first_tokens, first_positions, 0, n_steps, 1, nullptr, error, error_cap)) return 0;
+  if (tokens_out) {
+    for (int i = 0; i < b.B; ++i)
+      if (!cuda_ok(c, cudaMemcpy(tokens_out + (size_t)i * n_steps, b.history + (size_t)i * b.history_cap, n_steps * 4,
+                                 cudaMemcpyDeviceToHost),
+                   "decode_batch_tokens_d2h", error, error_cap))
+        return 0;
+    c->stats.device_to_host_bytes += (size_t)b.B * n_steps * 4;
+  }
+  return 1;
+}
+
+int minicpmo_gpu_context_qwen3_time_decode_batch(void* handle, size_t n_seq, const uint32_t* first_tokens,
+                                                 const uint32_t* first_positions, size_t n_steps, float* total_ms,
+                                                 char* error, size_t error_cap) {
+  Ctx* c = (Ctx*)handle;
+  if (!c) return copy_error(error, error_cap, "error: null gpu context"), 0;
+  DeviceGuard g(c);
+  if (!c->model || !c->model->batch) return fail(c, error, error_cap, "error: qwen3 time_decode_batch: no batched model bound");
+  Model& m = *c->model;
+  if (n_seq != (size_t)m.batch->B || !first_tokens || !first_positions)
+    return fail(c, error, error_cap, "error: qwen3 time_decode_batch: n_seq must equal max_batch");
+  float ms = 0.0f;
+  const int ok = run_batch(c, m, first_tokens, first_positions, 0, n_steps, 1, &ms, error, error_cap);
+  if (ok && total_ms) *total_ms = ms;
+  return ok;
+}
+
+int minicpmo_gpu_context_qwen3_batch_kernels(void* handle, int with_logits) {
+  Ctx* c = (Ctx*)handle;
+  if (!c || !c->model || !c->model->batch) return 0;
+  return c->model->batch->kernels[with_logits ? 0 : 1];
 }
 
 int minicpmo_gpu_context_q8_1_quantize(void* handle, const float* x, size_t n, void* xq_out, char* error,

@@ -135,6 +135,10 @@ SIGNATURES = {
     "minicpmo_gpu_context_matvec_f32_input": (i32, [vp, vp, fptr, vp, f32, sz, sz, fptr] + E),
     "minicpmo_gpu_context_time_matvec_input": (i32, [vp, vp, sz, sz, i32, i32, vp, fptr] + E),
     "minicpmo_gpu_context_matmul_q8_0_batch": (i32, [vp, vp, fptr, sz, sz, sz, fptr] + E),
+    "minicpmo_gpu_context_qwen3_forward_batch": (i32, [vp, sz, u32ptr, u32ptr, i32, u32ptr, fptr, fptr] + E),
+    "minicpmo_gpu_context_qwen3_decode_batch": (i32, [vp, sz, u32ptr, u32ptr, sz, u32ptr] + E),
+    "minicpmo_gpu_context_qwen3_time_decode_batch": (i32, [vp, sz, u32ptr, u32ptr, sz, fptr] + E),
+    "minicpmo_gpu_context_qwen3_batch_kernels": (i32, [vp, i32]),
     "minicpmo_gpu_context_time_matvec": (i32, [vp, vp, sz, sz, i32, fptr] + E),
     "minicpmo_gpu_context_qwen3_time_decode": (i32, [vp, u32, sz, sz, fptr] + E),
     "minicpmo_gpu_context_tensor_device_bytes": (sz, [vp, vp]),
@@ -317,6 +321,7 @@ class GpuContext:
 
     def qwen3_bind(self, cfg: Qwen3Config) -> None:
         self._keep["qwen3_cfg"] = cfg
+        self._vocab = int(cfg.vocab)
         self._call("minicpmo_gpu_context_qwen3_bind", C.byref(cfg))
 
     def tp_buffer(self, hidden: int) -> bytes:
@@ -409,6 +414,38 @@ class GpuContext:
         us = f32()
         self._call("minicpmo_gpu_context_time_matvec", t.ptr, t.cols, t.rows, iters, C.byref(us))
         return float(us.value)
+
+    def qwen3_forward_batch(self, tokens, positions, logits: bool = True, want_logits: bool = False):
+        """One batched step: (next tokens, top-2 gaps, logits [n, vocab] or None)."""
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        p = np.ascontiguousarray(positions, dtype=np.uint32)
+        n = t.size
+        out_t = np.zeros(n, np.uint32)
+        gaps = np.zeros(n, np.float32)
+        lg = np.empty((n, self._vocab), np.float32) if (want_logits and logits) else None
+        self._call("minicpmo_gpu_context_qwen3_forward_batch", n, t.ctypes.data_as(u32ptr), p.ctypes.data_as(u32ptr),
+                   0 if logits else 1, out_t.ctypes.data_as(u32ptr), _f(gaps), _f(lg) if lg is not None else None)
+        return out_t, gaps, lg
+
+    def qwen3_decode_batch(self, first_tokens, first_positions, n_steps: int) -> np.ndarray:
+        """Greedy decode on the device: tokens [n_seq, n_steps]."""
+        t = np.ascontiguousarray(first_tokens, dtype=np.uint32)
+        p = np.ascontiguousarray(first_positions, dtype=np.uint32)
+        out = np.zeros((t.size, n_steps), np.uint32)
+        self._call("minicpmo_gpu_context_qwen3_decode_batch", t.size, t.ctypes.data_as(u32ptr), p.ctypes.data_as(u32ptr),
+                   n_steps, out.ctypes.data_as(u32ptr))
+        return out
+
+    def qwen3_time_decode_batch(self, first_tokens, first_positions, n_steps: int) -> float:
+        t = np.ascontiguousarray(first_tokens, dtype=np.uint32)
+        p = np.ascontiguousarray(first_positions, dtype=np.uint32)
+        ms = f32()
+        self._call("minicpmo_gpu_context_qwen3_time_decode_batch", t.size, t.ctypes.data_as(u32ptr),
+                   p.ctypes.data_as(u32ptr), n_steps, C.byref(ms))
+        return float(ms.value)
+
+    def qwen3_batch_kernels(self, with_logits: bool = True) -> int:
+        return int(self.lib.minicpmo_gpu_context_qwen3_batch_kernels(self.handle, int(with_logits)))
 
     def qwen3_step_kernels(self, with_logits: bool = True) -> int:
         return int(self.lib.minicpmo_gpu_context_qwen3_step_kernels(self.handle, int(with_logits)))

@@ -50,12 +50,14 @@ class Qwen3Runtime:
     @classmethod
     def open(cls, weights, shape: Optional[Qwen3Shape] = None, device_index: int = 0, kv_f16: bool = False,
              context: Optional[int] = None, debug: bool = False, decode_mode: int = 0,
-             tp: Optional["TensorParallel"] = None) -> "Qwen3Runtime":
+             tp: Optional["TensorParallel"] = None, max_batch: int = 0) -> "Qwen3Runtime":
         """weights: a GGUF path/GgufFile, or a list of (name, dtype, rows, cols, uint8 bytes).
         decode_mode 0: the default (one kernel per operation); 1: one kernel per operation; 2: one
         persistent kernel per decode step where the model fits it (same results in every mode).
         tp: tensor parallelism over the ranks of one node (`TensorParallel`, one process per GPU);
-        every rank opens with the same weights and drives the same tokens."""
+        every rank opens with the same weights and drives the same tokens.
+        max_batch 2..32: also bind the batched decode of that many independent sequences
+        (every linear weight Q8_0; forward_batch / append_prompt_batch / generate_batch)."""
         if isinstance(weights, (str,)) or hasattr(weights, "__fspath__"):
             weights = GgufFile(weights)
         if isinstance(weights, GgufFile):
@@ -81,6 +83,7 @@ class Qwen3Runtime:
         cfg.rope_freq_scale = 1.0
         cfg.kv_f16 = int(kv_f16)
         cfg.decode_mode = int(decode_mode)
+        cfg.max_batch = int(max_batch)
         if tp is not None and tp.world > 1:
             handles = tp.all_gather(gpu.tp_buffer(shape.hidden))
             gpu.qwen3_bind_tp(cfg, tp.rank, tp.world, handles)
@@ -127,6 +130,43 @@ class Qwen3Runtime:
             self.total_tokens += 1
             tok = nxt
         self.last_token = tok
+        return out
+
+    # -- batched decode (max_batch independent sequences) --------------------
+    def forward_batch(self, tokens, positions, logits: bool = True, want_logits: bool = False):
+        """One step of every sequence: (next tokens, top-2 gaps, logits [n, vocab] or None)."""
+        return self.gpu.qwen3_forward_batch(tokens, positions, logits=logits, want_logits=want_logits)
+
+    def append_prompt_batch(self, prompts) -> Tuple[np.ndarray, np.ndarray]:
+        """Forward equal-length prompts [n_seq][P] position by position (logits only at the last);
+        returns each sequence's next token and top-2 gap."""
+        ids = np.asarray(prompts, dtype=np.uint32)
+        if ids.ndim != 2 or ids.shape[1] == 0:
+            raise ValueError("error: prompts must be [n_seq][P] with P > 0")
+        n, P = ids.shape
+        start = getattr(self, "batch_tokens", 0)
+        if start + P > self.context:
+            raise ValueError(f"error: context overflow total_tokens={start} add_tokens={P} runtime_context={self.context}")
+        nxt, gap = None, None
+        for i in range(P):
+            pos = np.full(n, start + i, np.uint32)
+            nxt, gap, _ = self.gpu.qwen3_forward_batch(ids[:, i], pos, logits=(i + 1 == P))
+        self.batch_tokens = start + P
+        self.batch_last = nxt
+        return nxt, gap
+
+    def generate_batch(self, n_new: int) -> np.ndarray:
+        """Greedy decode of every sequence after append_prompt_batch, the sampled tokens fed back on
+        the device; returns [n_seq][n] (the first column is the token sampled from the prompt)."""
+        start = self.batch_tokens
+        n = min(n_new, self.context - start)
+        if n <= 0:
+            return np.zeros((len(self.batch_last), 0), np.uint32)
+        first = np.asarray(self.batch_last, np.uint32)
+        toks = self.gpu.qwen3_decode_batch(first, np.full(first.size, start, np.uint32), n)
+        out = np.concatenate([first[:, None], toks[:, :-1]], axis=1)
+        self.batch_tokens = start + n
+        self.batch_last = toks[:, -1].copy()
         return out
 
     def generate_device(self, n_new: int, penalty: float = 1.0) -> List[int]:
