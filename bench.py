@@ -257,6 +257,121 @@ def run_kernel_sweep(args) -> int:
     return 0
 
 
+def run_batch_bench(args, shape, world, rank, local, dist, barrier) -> int:
+    """Qwen3-8B shape, every linear weight Q8_0, f16 KV cache at a 4096-token
+    context, B independent sequences each after a prompt of --prompt ids (default 1024), greedy
+    decode; the projections run on the tcgen05 tensor cores.  Under torchrun every rank decodes
+    its own B sequences (replicas, weak scaling)."""
+    import torch
+
+    from minicpmo_b200 import gguf
+    from minicpmo_b200.qwen3 import Qwen3Runtime
+
+    B = args.batch
+    prompt_len = args.prompt if args.prompt != PROMPT else 1024
+    mix = gguf.ALL_Q8_0
+    t_gen = time.perf_counter()
+    tensors = build_weights(shape, mix, f"cuda:{local}")
+    torch.cuda.empty_cache()
+    t_gen = time.perf_counter() - t_gen
+    t_load = time.perf_counter()
+    ctx = max(4096, prompt_len + args.warmup + 2 * args.steps + 8)
+    rt = Qwen3Runtime.open(tensors, shape=shape, device_index=local, context=ctx, kv_f16=True, max_batch=B)
+    t_load = time.perf_counter() - t_load
+    g = rt.gpu
+    prompts = np.stack([gguf.prompt_ids(prompt_len, shape.vocab, seed=7 + 1000 * rank + b) for b in range(B)])
+    t_pf = time.perf_counter()
+    nxt, _ = rt.append_prompt_batch(prompts)
+    t_pf = time.perf_counter() - t_pf
+    rt.generate_batch(args.warmup)  # untimed warm-up steps
+    cur = np.asarray(rt.batch_last, np.uint32)
+    pos0 = rt.batch_tokens
+
+    clocks = ClockSampler(local, ROOT / "gpurun_out" / f"clocks_rank{rank}.csv"
+                          if (ROOT / "gpurun_out").exists() else Path(f"/tmp/clocks_rank{rank}.csv"))
+    barrier()
+    wall0 = time.perf_counter()
+    ms = g.qwen3_time_decode_batch(cur, np.full(B, pos0, np.uint32), args.steps)
+    barrier()
+    wall = time.perf_counter() - wall0
+    clk = clocks.stop()
+    start_pos = pos0
+    pos1 = pos0 + args.steps
+    # e2e: the public per-step batch call with host buffers (states in, tokens out)
+    barrier()
+    e0 = time.perf_counter()
+    tok = cur
+    for i in range(args.steps):
+        tok, _, _ = g.qwen3_forward_batch(tok, np.full(B, pos1 + i, np.uint32))
+    barrier()
+    e2e_s = time.perf_counter() - e0
+
+    ms_t = torch.tensor([ms / 1000.0, e2e_s], dtype=torch.float64, device=f"cuda:{local}")
+    if dist is not None:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    step_s, e2e_s = float(ms_t[0]), float(ms_t[1])
+    tokens_total = args.steps * B * world
+    value = tokens_total / step_s
+    e2e_v = tokens_total / e2e_s
+
+    # roofline: the dominant kernel is the tensor-core projection; the gate
+    # shape (12288 x 4096 Q8_0, one of the two matrices of the gate|up launch)
+    # timed alone with the L2 flushed before each launch
+    hbm, peak_kind = peaks()
+    T = rt.tensors
+    gate = T["blk.0.ffn_gate.weight"]
+    us = g.time_matmul_q8_0_batch(gate, B, iters=10)
+    alg = gate.nbytes + B * gate.cols * 2 + B * gate.rows * 4
+    gemm_gbs = alg / us / 1e3
+    flops = 2.0 * gate.rows * gate.cols * B
+    w_bytes = 0
+    for name, _, rows, _, d in tensors:
+        w_bytes += int(d.nbytes) // rows if name == "token_embd.weight" else int(d.nbytes)
+    kv_bytes = 2 * shape.layers * shape.kv_dim * 2 * (start_pos + args.steps // 2 + 1) * B
+    step_bytes = w_bytes + kv_bytes
+    kernels = g.qwen3_batch_kernels(True)
+    line = {
+        "metric": f"Qwen3-8B Q8_0 batched decode (B={B}) tok/s",
+        "value": value,
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": 1000.0 * step_s / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "q8_0 weights and activations as f16 on tcgen05 (f32 accumulate); f16 KV",
+        "data": f"synthetic: seeded N(0,0.02) weights quantised Q8_0, {B} x {prompt_len} uniform random prompt ids",
+        "config": {
+            "workload": f"qwen3-8b-shape all-Q8_0 batched greedy decode, B={B}, prompt {prompt_len}, f16 KV at "
+                        f"{ctx}-token context (BASELINE config 3)",
+            "batch": B, "layers": shape.layers, "hidden": shape.hidden, "ffn": shape.ffn, "vocab": shape.vocab,
+            "prompt": prompt_len, "context": ctx, "decode_positions": [start_pos, start_pos + args.steps],
+            "kv_cache": "f16",
+            "parallelism": f"replicas x{world} ({B} sequences per GPU)" if world > 1 else "single gpu",
+            "l2": "weights 8.0 GB per step >> 126 MB L2 (no flush needed)",
+            "weights_bytes": w_bytes, "step_bytes_mean": step_bytes,
+            "step_hbm_frac": step_bytes / step_s * args.steps / 1e9 / hbm,
+            "prefill_s": t_pf, "load_s": t_load, "synth_s": t_gen, "wall_timed_s": wall,
+        },
+        "e2e": {"value": e2e_v, "unit": "tok/s", "h2d_bytes_per_step": STATE_BYTES * B,
+                "d2h_bytes_per_step": STATE_BYTES * B},
+        "gpu_launches": kernels * args.steps,
+        "roofline": {"bound": "hbm", "achieved": gemm_gbs, "peak": hbm, "unit": "GB/s", "frac": gemm_gbs / hbm,
+                     "traffic": None, "peak_kind": peak_kind,
+                     "kernel": f"k_gemm_q80<{16 if B <= 16 else 32}> (tcgen05, Q8_0 12288x4096 x {B} sequences), "
+                               "timed alone with the L2 flushed before each launch",
+                     "algorithmic_bytes_per_launch": alg, "us_per_launch": us,
+                     "tensor_tflops": flops / us / 1e6},
+        "clocks": clk,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    rt.close()
+    return 0
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -275,6 +390,9 @@ def main() -> int:
                     help="override the layer count (smaller cases of the same shape, for profiler captures)")
     ap.add_argument("--decode-mode", type=int, default=0,
                     help="0: the library default; 1: one kernel per operation; 2: one persistent kernel per step")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="BASELINE config 3: batched decode of this many sequences (2..32), all-Q8_0 weights on the "
+                         "tensor cores, f16 KV, prompt 1024 unless --prompt is given")
     ap.add_argument("--prompt", type=int, default=PROMPT,
                     help="prompt length before decode (default: the 512 of the headline config; shorter only for "
                          "profiler launch lists)")
@@ -310,6 +428,18 @@ def main() -> int:
 
     from minicpmo_b200.gpu import Tensor
     from minicpmo_b200.qwen3 import Qwen3Runtime
+
+    if args.batch > 1:
+        def barrier_b():
+            if dist is not None:
+                dist.barrier()
+            torch.cuda.synchronize()
+
+        rc = run_batch_bench(args, shape, world, rank, local, dist, barrier_b)
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+        return rc
 
     t_gen = time.perf_counter()
     tensors = build_weights(shape, mix, f"cuda:{local}")

@@ -266,6 +266,11 @@ MINICPMO_API int minicpmo_gpu_context_matvec_q8_1(void *handle, const void *host
 MINICPMO_API int minicpmo_gpu_context_matmul_q8_0_batch(void *handle, const void *host_ptr, const float *x, size_t n_seq,
                                            size_t in_dim, size_t out_dim, float *y_out, char *error,
                                            size_t error_cap);
+/* Mean device time (us) of the tensor-core projection of an uploaded Q8_0
+ * tensor for n_seq sequences, over `iters` launches with the L2 flushed
+ * (a 256 MB write) before each, so every launch streams W from HBM. */
+MINICPMO_API int minicpmo_gpu_context_time_matmul_q8_0_batch(void *handle, const void *host_ptr, size_t n_seq, int iters,
+                                                float *avg_us, char *error, size_t error_cap);
 /* GEMV of an uploaded quantised tensor on host f32 activations that the
  * GEMV kernel quantises to Q8_1 itself (as the decode step's fused down and
  * o projections do), after RMSNorm with the uploaded weight norm_host_ptr

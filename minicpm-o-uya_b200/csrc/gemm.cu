@@ -6,18 +6,20 @@
 // keep up with, so the weights are dequantised to f16 in shared memory and
 // multiplied on the tensor cores with f32 accumulation in tensor memory:
 //
-//   warp 0      producer: per 256-value K-tile, 128 bulk copies of the tile's
-//               raw Q8_0 row pieces (8 blocks = 272 bytes each, 16-byte
-//               aligned in the GGUF row) and one bulk copy of the f16
-//               activation tile (N x 256, already in the operand layout);
-//   warps 2..5  dequantise: thread = row, q * d in f16 (int8 -> f16 exactly
-//               via the 0x6400 exponent trick, one rounding in the multiply),
-//               written as 8x16-byte core matrices of the K-major operand
-//               layout (no swizzle), in two 128-value halves per K-tile;
+//   warp 0      producer: per 256-value K-tile, one bulk copy of the tile's
+//               Q8_0 bytes (the weights are re-tiled at upload so that the
+//               128 rows x 8 blocks of a (row tile, K-tile) pair are one
+//               34816-byte block) and one bulk copy of the f16 activation
+//               tile (N x 256, already in the operand layout);
+//   warps 2..9  dequantise: thread = (row, half of the K-tile), q * d in f16
+//               (int8 -> f16 exactly via the 0x6400 exponent trick, one
+//               rounding in the multiply), written as 8x16-byte core matrices
+//               of the K-major operand layout (no swizzle);
 //   warp 1      one elected thread issues tcgen05.mma kind::f16 (M = 128,
 //               N = sequences, K = 16) into a 128 x N f32 accumulator in
 //               tensor memory and releases stages with tcgen05.commit;
-//   epilogue    warps 2..5 read the accumulator with tcgen05.ld (lane = row)
+//   epilogue    warps 2..9 read the accumulator with tcgen05.ld (lane = row,
+//               each warp half of the sequence columns)
 //               and store / add Y, or, with K split over several CTAs, write
 //               partial sums that the last CTA of the row tile adds in split
 //               order (deterministic).
@@ -45,12 +47,14 @@ namespace mcpo {
 
 namespace {
 
-constexpr int kRawStages = 3;   // raw Q8_0 + activation tiles in flight
-constexpr int kAStages = 2;     // f16 operand half-tiles (128 rows x 128 K)
+constexpr int kRawStages = 3;   // Q8_0 weight tiles in flight
+constexpr int kActStages = 2;   // f16 activation tiles in flight
+constexpr int kAStages = 4;     // f16 operand quarter-tiles (128 rows x 64 K): two per dequantising group
 constexpr int kRowPiece = 272;  // bytes of 256 values of one Q8_0 row
 constexpr int kRawBytes = kGemmTileRows * kRowPiece;     // 34816
-constexpr int kABytes = kGemmTileRows * 128 * 2;         // 32768
-constexpr int kThreads = 6 * 32;
+constexpr int kABytes = kGemmTileRows * 64 * 2;          // 16384
+constexpr int kDqWarps = 8;  // dequantising / epilogue warps: 4 per 128-value half of a K-tile
+constexpr int kThreads = (2 + kDqWarps) * 32;
 
 __host__ __device__ constexpr size_t act_bytes(int N) { return (size_t)N * kGemmKTile * 2; }
 
@@ -59,8 +63,10 @@ struct GemmSmem {
   __host__ __device__ static size_t a_off() { return 0; }
   __host__ __device__ static size_t raw_off() { return (size_t)kAStages * kABytes; }
   __host__ __device__ static size_t act_off() { return raw_off() + (size_t)kRawStages * kRawBytes; }
-  __host__ __device__ static size_t bar_off(int N) { return act_off() + (size_t)kRawStages * act_bytes(N); }
-  __host__ __device__ static size_t bytes(int N) { return bar_off(N) + 8 * (2 * kRawStages + 2 * kAStages + 1) + 16 + 1024; }
+  __host__ __device__ static size_t bar_off(int N) { return act_off() + (size_t)kActStages * act_bytes(N); }
+  __host__ __device__ static size_t bytes(int N) {
+    return bar_off(N) + 8 * (2 * kRawStages + 2 * kActStages + 2 * kAStages + 1) + 16 + 1024;
+  }
 };
 
 // ---- tcgen05 primitives ----
@@ -129,6 +135,17 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
+  uint32_t r[8];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr)
+               : "memory");
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 // Bounded wait that leaves early once the CTA's abort flag is set.
 __device__ __forceinline__ bool gwait(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_s) {
   for (int i = 0; i < kWaitLimit; ++i) {
@@ -149,36 +166,36 @@ __device__ __forceinline__ __half2 q8x2_to_h2(uint32_t wx, uint32_t sel) {
   return __hsub2(h, __float2half2_rn(1152.0f));
 }
 
-// Row r's 128 values [128h, 128h + 128) of the raw K-tile (Q8_0 blocks
-// 4h..4h+3, 136 bytes at r*272 + 136h, 8-byte aligned) -> 16 chunks of 8
-// f16 values, chunk c to a_stage + c*2048 + r*16 (core matrix of rows
-// r & ~7, row r & 7).
-__device__ __forceinline__ void dequant_half(const uint8_t* raw, uint8_t* a_stage, int r, int h) {
-  uint32_t w[34];
-  const uint2* src = reinterpret_cast<const uint2*>(raw + (size_t)r * kRowPiece + 136 * h);
+// Row r's 64 values [64qt, 64qt + 64) of the staged K-tile (Q8_0 blocks
+// 2qt, 2qt+1: 17 words at [qt][i][r]) -> 8 chunks of 8 f16 values, chunk c
+// to a_stage + c*2048 + r*16 (core matrix of rows r & ~7, row r & 7).
+__device__ __forceinline__ void dequant_quarter(const uint8_t* raw, uint8_t* a_stage, int r, int qt) {
+  uint32_t w[17];
+  const uint32_t* src = reinterpret_cast<const uint32_t*>(raw) + (size_t)qt * 17 * kGemmTileRows + r;
 #pragma unroll
-  for (int i = 0; i < 17; ++i) {
-    const uint2 v = src[i];
-    w[2 * i] = v.x;
-    w[2 * i + 1] = v.y;
+  for (int i = 0; i < 17; ++i) w[i] = src[(size_t)i * kGemmTileRows];
+  // block scales (bytes 0-1 and 34-35) before the sign flip of the quants
+  __half2 d2[2];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int db = 34 * j;
+    const uint16_t dbits = (uint16_t)((w[db >> 2] >> (8 * (db & 3))) & 0xffffu);
+    __half d;
+    memcpy(&d, &dbits, 2);
+    d2[j] = __half2half2(d);
   }
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    // block j: d at byte 34j, qs at bytes 34j+2 .. 34j+33
+  for (int i = 0; i < 17; ++i) w[i] ^= 0x80808080u;
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
     const int db = 34 * j;
-    const uint32_t dw = w[db >> 2] >> (8 * (db & 3));
-    __half d;
-    const uint16_t dbits = (uint16_t)(dw & 0xffffu);
-    memcpy(&d, &dbits, 2);
-    const __half2 d2 = __half2half2(d);
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       uint32_t out[4];
 #pragma unroll
       for (int p = 0; p < 4; ++p) {
         const int b = db + 2 + 8 * c + 2 * p;  // first byte of the pair (even, same word as b+1)
-        const uint32_t wx = w[b >> 2] ^ 0x80808080u;
-        const __half2 v = __hmul2(q8x2_to_h2(wx, (b & 3) ? 0x4342u : 0x4140u), d2);
+        const __half2 v = __hmul2(q8x2_to_h2(w[b >> 2], (b & 3) ? 0x4342u : 0x4140u), d2[j]);
         memcpy(&out[p], &v, 4);
       }
       *reinterpret_cast<uint4*>(a_stage + (size_t)(4 * j + c) * 2048 + (size_t)r * 16) =
@@ -200,7 +217,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_q80(const GemmArgs a) {
   uint8_t* act_st = smem + GemmSmem::act_off();
   uint64_t* raw_full = reinterpret_cast<uint64_t*>(smem + GemmSmem::bar_off(N));
   uint64_t* raw_empty = raw_full + kRawStages;
-  uint64_t* a_full = raw_empty + kRawStages;
+  uint64_t* x_full = raw_empty + kRawStages;
+  uint64_t* x_empty = x_full + kActStages;
+  uint64_t* a_full = x_empty + kActStages;
   uint64_t* a_empty = a_full + kAStages;
   uint64_t* acc_full = a_empty + kAStages;
   uint32_t* tmem_s = reinterpret_cast<uint32_t*>(acc_full + 1);
@@ -213,15 +232,18 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_q80(const GemmArgs a) {
   const int kt0 = (int)((long long)split * kt_total / a.ksplit);
   const int kt1 = (int)((long long)(split + 1) * kt_total / a.ksplit);
   const int nkt = kt1 - kt0;
-  const size_t row_bytes = (size_t)(a.K / 32) * 34;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kRawStages; ++i) {
       mbar_init(&raw_full[i], 1);
-      mbar_init(&raw_empty[i], 4 + 1);  // four dequantising warps + the MMA commit
+      mbar_init(&raw_empty[i], kDqWarps);  // released by the dequantising warps
+    }
+    for (int i = 0; i < kActStages; ++i) {
+      mbar_init(&x_full[i], 1);
+      mbar_init(&x_empty[i], 1);  // released by the MMA commit
     }
     for (int i = 0; i < kAStages; ++i) {
-      mbar_init(&a_full[i], 4);
+      mbar_init(&a_full[i], kDqWarps / 2);  // the four warps of one group
       mbar_init(&a_empty[i], 1);
     }
     mbar_init(acc_full, 1);
@@ -235,52 +257,50 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_q80(const GemmArgs a) {
   const uint32_t tmem = *tmem_s;
 
   if (warp == 0) {
-    // ---- producer: the weight pieces of the first stages are requested
-    // before waiting for the previous kernel (they do not depend on it); the
-    // activation tiles after.  Waits are made warp-uniform.
-    const uint64_t policy = l2_evict_first_policy();
-    auto issue_weights = [&](int i) {
-      const int s = i % kRawStages, kt = kt0 + i;
-      if (lane == 0) mbar_arrive_expect_tx(&raw_full[s], (uint32_t)(kRawBytes + act_bytes(N)));
-      __syncwarp();
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int r = lane + 32 * q;
-        int R = row0 + r;
-        const uint8_t* wseg = a.seg[0].w;
-        if (a.nseg > 1 && R >= a.seg[0].rows) {
-          R -= a.seg[0].rows;
-          wseg = a.seg[1].w;
-          if (a.nseg > 2 && R >= a.seg[1].rows) {
-            R -= a.seg[1].rows;
-            wseg = a.seg[2].w;
-          }
+    // ---- producer: lane 0 streams the weight tiles (they do not depend on
+    // the previous kernel, so it starts at once), lane 1 the activation
+    // tiles (after the dependency wait); independent rings, so weights run
+    // ahead as far as their ring allows.
+    if (lane == 0) {
+      // this row tile's block list in its segment
+      int R = row0;
+      const uint8_t* wseg = a.seg[0].w;
+      if (a.nseg > 1 && R >= a.seg[0].rows) {
+        R -= a.seg[0].rows;
+        wseg = a.seg[1].w;
+        if (a.nseg > 2 && R >= a.seg[1].rows) {
+          R -= a.seg[1].rows;
+          wseg = a.seg[2].w;
         }
-        const uint8_t* src = wseg + (size_t)R * row_bytes + (size_t)kt * kRowPiece;
-        bulk_load_hint(raw_st + (size_t)s * kRawBytes + (size_t)r * kRowPiece, src, kRowPiece, &raw_full[s], policy);
       }
-    };
-    auto issue_act = [&](int i) {
-      const int s = i % kRawStages, kt = kt0 + i;
-      if (lane == 0)
-        bulk_load(act_st + (size_t)s * act_bytes(N), a.x + (size_t)kt * act_bytes(N), (uint32_t)act_bytes(N),
-                  &raw_full[s]);
-    };
-    const int npre = nkt < kRawStages ? nkt : kRawStages;
-    for (int i = 0; i < npre; ++i) issue_weights(i);
-    pdl_wait();
-    for (int i = 0; i < npre; ++i) issue_act(i);
-    int issued = npre;
-    for (int i = npre; i < nkt; ++i) {
-      const int s = i % kRawStages;
-      if (!__all_sync(0xffffffffu, gwait(&raw_empty[s], (uint32_t)((i / kRawStages) - 1) & 1u, a.err, abort_s))) break;
-      issue_weights(i);
-      issue_act(i);
-      issued = i + 1;
+      const uint8_t* wtile = wseg + (size_t)(R / kGemmTileRows) * kt_total * kRawBytes;
+      const uint64_t policy = l2_evict_first_policy();
+      int issued = 0;
+      for (int i = 0; i < nkt; ++i) {
+        const int s = i % kRawStages;
+        if (i >= kRawStages && !gwait(&raw_empty[s], (uint32_t)((i / kRawStages) - 1) & 1u, a.err, abort_s)) break;
+        mbar_arrive_expect_tx(&raw_full[s], (uint32_t)kRawBytes);
+        bulk_load_hint(raw_st + (size_t)s * kRawBytes, wtile + (size_t)(kt0 + i) * kRawBytes, kRawBytes, &raw_full[s],
+                       policy);
+        issued = i + 1;
+      }
+      for (int i = issued > kRawStages ? issued - kRawStages : 0; i < issued; ++i)
+        if (!mbar_wait(&raw_full[i % kRawStages], (uint32_t)(i / kRawStages) & 1u, a.err)) break;
+    } else if (lane == 1) {
+      pdl_wait();
+      int issued = 0;
+      for (int i = 0; i < nkt; ++i) {
+        const int s = i % kActStages;
+        if (i >= kActStages && !gwait(&x_empty[s], (uint32_t)((i / kActStages) - 1) & 1u, a.err, abort_s)) break;
+        mbar_arrive_expect_tx(&x_full[s], (uint32_t)act_bytes(N));
+        bulk_load(act_st + (size_t)s * act_bytes(N), a.x + (size_t)(kt0 + i) * act_bytes(N), (uint32_t)act_bytes(N),
+                  &x_full[s]);
+        issued = i + 1;
+      }
+      for (int i = issued > kActStages ? issued - kActStages : 0; i < issued; ++i)
+        if (!mbar_wait(&x_full[i % kActStages], (uint32_t)(i / kActStages) & 1u, a.err)) break;
     }
-    // leave only once this CTA's copies have landed
-    for (int i = issued > kRawStages ? issued - kRawStages : 0; i < issued; ++i)
-      if (!mbar_wait(&raw_full[i % kRawStages], (uint32_t)(i / kRawStages) & 1u, a.err)) break;
+    __syncwarp();
   } else if (warp == 1) {
     // ---- MMA issuer (one thread) ----
     if (lane == 0) {
@@ -288,26 +308,26 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_q80(const GemmArgs a) {
       const uint32_t lbo_a = 2048, sbo = 128, lbo_b = (N / 8) * 128;
       bool ok = true;
       for (int i = 0; i < nkt && ok; ++i) {
-        const int s = i % kRawStages;
-        if (!gwait(&raw_full[s], (uint32_t)(i / kRawStages) & 1u, a.err, abort_s)) break;
-        for (int h = 0; h < 2; ++h) {
-          const int ai = 2 * i + h, sa = ai % kAStages;
-          if (!gwait(&a_full[sa], (uint32_t)(ai / kAStages) & 1u, a.err, abort_s)) {
+        const int s = i % kActStages;
+        if (!gwait(&x_full[s], (uint32_t)(i / kActStages) & 1u, a.err, abort_s)) break;
+        for (int qt = 0; qt < 4; ++qt) {
+          const int sa = qt;  // A stage qt holds quarter qt of every K-tile
+          if (!gwait(&a_full[sa], (uint32_t)i & 1u, a.err, abort_s)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t a_base = smem_addr(a_st + (size_t)sa * kABytes);
-          const uint32_t b_base = smem_addr(act_st + (size_t)s * act_bytes(N)) + (uint32_t)(h * 16) * lbo_b;
+          const uint32_t b_base = smem_addr(act_st + (size_t)s * act_bytes(N)) + (uint32_t)(qt * 8) * lbo_b;
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
+          for (int kk = 0; kk < 4; ++kk) {
             const uint64_t ad = umma_desc(a_base + kk * 2 * lbo_a, lbo_a, sbo);
             const uint64_t bd = umma_desc(b_base + kk * 2 * lbo_b, lbo_b, sbo);
-            umma_f16(tmem, ad, bd, idesc, (i | h | kk) != 0 ? 1u : 0u);
+            umma_f16(tmem, ad, bd, idesc, (i | qt | kk) != 0 ? 1u : 0u);
           }
           umma_commit(&a_empty[sa]);
         }
-        if (ok) umma_commit(&raw_empty[s]);
+        if (ok) umma_commit(&x_empty[s]);
       }
       // after every MMA issued, on every path: the epilogue reads the
       // accumulator (or, on abort, only waits) before tensor memory is freed
@@ -315,23 +335,28 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_q80(const GemmArgs a) {
     }
     __syncwarp();
   } else {
-    // ---- dequantising warps, then the epilogue (waits warp-uniform) ----
-    const int r = ((warp & 3) << 5) | lane;  // = tensor-memory lane of this thread
+    // ---- dequantising warps, then the epilogue (waits warp-uniform).  Warp
+    // w belongs to group h = (w-2)/4, which converts quarters h and h+2 of
+    // every K-tile (A stages h and h+2: while the tensor cores read one, the
+    // group fills the other) for rows 32*(w%4) .. +31 (= its tensor-memory
+    // lane quarter); in the epilogue it takes sequence columns
+    // [h*N/2, h*N/2 + N/2).
+    const int h = (warp - 2) >> 2;
+    const int r = ((warp & 3) << 5) | lane;
     for (int i = 0; i < nkt; ++i) {
       const int s = i % kRawStages;
       if (!__all_sync(0xffffffffu, gwait(&raw_full[s], (uint32_t)(i / kRawStages) & 1u, a.err, abort_s))) break;
       bool ok = true;
-      for (int h = 0; h < 2 && ok; ++h) {
-        const int ai = 2 * i + h, sa = ai % kAStages;
-        if (ai >= kAStages &&
-            !__all_sync(0xffffffffu, gwait(&a_empty[sa], (uint32_t)((ai / kAStages) - 1) & 1u, a.err, abort_s))) {
+      for (int t = 0; t < 2 && ok; ++t) {
+        const int qt = h + 2 * t;
+        if (i > 0 && !__all_sync(0xffffffffu, gwait(&a_empty[qt], (uint32_t)((i - 1) & 1), a.err, abort_s))) {
           ok = false;
           break;
         }
-        dequant_half(raw_st + (size_t)s * kRawBytes, a_st + (size_t)sa * kABytes, r, h);
+        dequant_quarter(raw_st + (size_t)s * kRawBytes, a_st + (size_t)qt * kABytes, r, qt);
         fence_proxy_async();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&a_full[sa]);
+        if (lane == 0) mbar_arrive(&a_full[qt]);
       }
       if (!ok) break;
       __syncwarp();
@@ -339,49 +364,60 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_q80(const GemmArgs a) {
     }
     const bool go = __all_sync(0xffffffffu, mbar_wait(acc_full, 0u, a.err) && !*abort_s);
     tc_fence_after();
-    float v[N];
+    constexpr int NH = N / 2;
+    const int c0 = h * NH;
+    float v[NH];
 #pragma unroll
-    for (int c = 0; c < N; ++c) v[c] = 0.0f;
+    for (int c = 0; c < NH; ++c) v[c] = 0.0f;
     if (go) {
-      const uint32_t taddr = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-#pragma unroll
-      for (int c = 0; c < N; c += 16) {
-        float t[16];
-        tmem_ld16(taddr + c, t);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) v[c + i] = t[i];
+      const uint32_t taddr = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)c0;
+      if constexpr (NH == 16) {
+        tmem_ld16(taddr, v);
+      } else {
+        tmem_ld8(taddr, v);
       }
     }
     const int row = row0 + r;
     if (a.ksplit <= 1) {
       if (go)
 #pragma unroll
-        for (int n = 0; n < N; ++n) {
-          if (n < a.n_valid) {
-            float* y = a.y + (size_t)n * a.ldy + row;
+        for (int n = 0; n < NH; ++n) {
+          if (c0 + n < a.n_valid) {
+            float* y = a.y + (size_t)(c0 + n) * a.ldy + row;
             *y = a.epi == kGemmAdd ? __fadd_rn(*y, v[n]) : v[n];
           }
         }
     } else {
       // partial sums, then the last CTA of this row tile adds them in split
-      // order; the named barrier spans the four epilogue warps on every path
+      // order; the named barrier spans the epilogue warps on every path
       __shared__ unsigned ticket_s;
 #pragma unroll
-      for (int n = 0; n < N; ++n) a.partial[((size_t)split * N + n) * a.rows_total + row] = v[n];
+      for (int n = 0; n < NH; ++n) a.partial[((size_t)split * N + c0 + n) * a.rows_total + row] = v[n];
       __threadfence();
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (r == 0) ticket_s = atomicAdd(&a.counters[tile], 1u);
-      asm volatile("bar.sync 1, 128;" ::: "memory");
+      asm volatile("bar.sync 1, %0;" ::"n"(kDqWarps * 32) : "memory");
+      if (warp == 2 && lane == 0) ticket_s = atomicAdd(&a.counters[tile], 1u);
+      asm volatile("bar.sync 1, %0;" ::"n"(kDqWarps * 32) : "memory");
       if (ticket_s == (unsigned)(a.ksplit - 1)) {
         __threadfence();
-        for (int n = 0; n < a.n_valid; ++n) {
-          float sum = 0.0f;
-          for (int sp = 0; sp < a.ksplit; ++sp)
-            sum = __fadd_rn(sum, __ldcg(a.partial + ((size_t)sp * N + n) * a.rows_total + row));
-          float* y = a.y + (size_t)n * a.ldy + row;
-          *y = a.epi == kGemmAdd ? __fadd_rn(*y, sum) : sum;
+        // sums in split order; every split's values are loaded before the adds
+        float sum[NH];
+#pragma unroll
+        for (int n = 0; n < NH; ++n) sum[n] = 0.0f;
+        for (int sp = 0; sp < a.ksplit; ++sp) {
+          float pv[NH];
+#pragma unroll
+          for (int n = 0; n < NH; ++n) pv[n] = __ldcg(a.partial + ((size_t)sp * N + c0 + n) * a.rows_total + row);
+#pragma unroll
+          for (int n = 0; n < NH; ++n) sum[n] = __fadd_rn(sum[n], pv[n]);
         }
-        if (r == 0) a.counters[tile] = 0u;
+#pragma unroll
+        for (int n = 0; n < NH; ++n) {
+          if (c0 + n < a.n_valid) {
+            float* y = a.y + (size_t)(c0 + n) * a.ldy + row;
+            *y = a.epi == kGemmAdd ? __fadd_rn(*y, sum[n]) : sum[n];
+          }
+        }
+        if (warp == 2 && lane == 0) a.counters[tile] = 0u;
       }
     }
   }
@@ -473,14 +509,51 @@ __global__ void k_swiglu_x16(const float* __restrict__ gu, int F, int n_valid, i
   }
 }
 
+// GGUF Q8_0 rows [rows][K/32 * 34 bytes] -> one contiguous 34816-byte block
+// per (row tile, K-tile), laid out [quarter 4][word 17][row 128] in 32-bit
+// words: quarter qt of row r is the 68 bytes of Q8_0 blocks 2qt, 2qt+1 of
+// that row's 256 values, and the 32 rows a warp converts together read
+// consecutive words (no shared-memory bank conflicts).  One thread per word.
+__global__ void k_gemm_tile_weights(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, int rows, int K) {
+  const int kt_total = K / kGemmKTile;
+  const size_t row_bytes = (size_t)(K / 32) * 34;
+  const size_t nwords = (size_t)rows * row_bytes / 4;
+  constexpr int kBlockWords = kRawBytes / 4;  // 8704
+  for (size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x; e < nwords; e += (size_t)gridDim.x * blockDim.x) {
+    const size_t blk = e / kBlockWords;
+    const int within = (int)(e % kBlockWords);
+    const int qt = within / (17 * kGemmTileRows);
+    const int i = (within / kGemmTileRows) % 17;
+    const int r = within % kGemmTileRows;
+    const size_t tile = blk / kt_total, kt = blk % kt_total;
+    const uint8_t* p = src + (tile * kGemmTileRows + r) * row_bytes + kt * kRowPiece + (size_t)qt * 68 + (size_t)i * 4;
+    uint32_t w;
+    memcpy(&w, p, 4);  // 4-byte aligned: row_bytes, 272 and 68 are multiples of 4
+    reinterpret_cast<uint32_t*>(dst)[e] = w;
+  }
+}
+
 }  // namespace
 
+cudaError_t launch_gemm_tile_weights(const uint8_t* src, uint8_t* dst, int rows, int K, cudaStream_t st) {
+  if (rows <= 0 || rows % kGemmTileRows || K <= 0 || K % kGemmKTile) return cudaErrorInvalidValue;
+  k_gemm_tile_weights<<<148 * 16, 256, 0, st>>>(src, dst, rows, K);
+  return cudaGetLastError();
+}
+
 int gemm_pick_ksplit(int tiles, int ktiles, int sms) {
-  if (tiles >= sms) return 1;
-  int s = (sms + tiles - 1) / tiles;
-  if (s > ktiles) s = ktiles;
-  if (s > 8) s = 8;
-  return s < 1 ? 1 : s;
+  // one CTA per SM: minimise waves x K-tiles per CTA (the critical path);
+  // matrices with a wave of row tiles or more are not split (partial sums
+  // would add traffic for nothing)
+  if (tiles >= sms || sms <= 0) return 1;
+  int best = 1;
+  long long best_cost = -1;
+  for (int s = 1; s <= 8 && s <= ktiles; ++s) {
+    const long long waves = ((long long)tiles * s + sms - 1) / sms;
+    const long long cost = waves * ((ktiles + s - 1) / s);
+    if (best_cost < 0 || cost < best_cost) best_cost = cost, best = s;
+  }
+  return best;
 }
 
 cudaError_t gemm_init() {

@@ -16,7 +16,8 @@ constexpr int kGemmMaxSegs = 3;
 
 enum GemmEpi : int { kGemmStore = 0, kGemmAdd = 1 };
 
-// One matrix of a launch: raw Q8_0 rows [rows][cols/32 * 34 bytes].
+// One matrix of a launch: Q8_0 bytes re-tiled by launch_gemm_tile_weights
+// (one 34816-byte block per 128 rows x 256 values, [rows/128][cols/256]).
 struct GemmSeg {
   const uint8_t* w;
   int rows;  // multiple of kGemmTileRows
@@ -56,6 +57,9 @@ __host__ __device__ inline size_t gemm_x_offset(int n, int k, int N) {
 int gemm_pick_ksplit(int tiles, int ktiles, int sms);
 
 cudaError_t gemm_init();
+// GGUF Q8_0 rows [rows][K/32 * 34 bytes] (device) -> the GemmSeg tiling
+// (same size); rows % 128 == 0, K % 256 == 0.
+cudaError_t launch_gemm_tile_weights(const uint8_t* src, uint8_t* dst, int rows, int K, cudaStream_t st);
 cudaError_t launch_gemm_q80(const GemmArgs& a, cudaStream_t st, bool pdl = false);
 
 // f32 rows x[n][ld] (n < n_valid, k < K) -> the f16 operand layout; rows

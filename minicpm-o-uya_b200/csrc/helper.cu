@@ -360,20 +360,24 @@ bool check_dev_err(Ctx* c, char* err, size_t cap) {
   return false;
 }
 
-// The raw GGUF rows of a Q8_0 upload on the device (the batched
-// tensor-core path reads 256-value row pieces), copied once from the
-// borrowed host bytes.
+// The Q8_0 bytes of an upload re-tiled for the batched tensor-core path
+// (128-row x 256-value blocks contiguous, launch_gemm_tile_weights), made
+// once from the borrowed host bytes through the staging buffer.
 bool ensure_raw(Ctx* c, Upload* u, char* err, size_t cap) {
   if (u->raw) return true;
-  if (u->dtype != kQ8_0 || u->cols % 256) {
-    fail(c, err, cap, "error: batched path needs a Q8_0 tensor with cols a multiple of 256 (tensor=%s)", u->name.c_str());
+  if (u->dtype != kQ8_0 || u->cols % kGemmKTile || u->rows % kGemmTileRows) {
+    fail(c, err, cap, "error: batched path needs a Q8_0 tensor with rows %% %d == 0 and cols %% %d == 0 (tensor=%s)",
+         kGemmTileRows, kGemmKTile, u->name.c_str());
     return false;
   }
   const size_t need = u->rows * gguf_row_bytes(kQ8_0, u->cols);
+  if (!ensure(c, &c->stage, &c->stage_bytes, need, "weight_stage_malloc", err, cap)) return false;
   if (!cuda_ok(c, cudaMalloc((void**)&u->raw, need), "weight_raw_malloc", err, cap)) return false;
   u->raw_bytes = need;
-  if (!cuda_ok(c, cudaMemcpyAsync(u->raw, u->host_ptr, need, cudaMemcpyHostToDevice, c->stream), "weight_raw_h2d", err,
+  if (!cuda_ok(c, cudaMemcpyAsync(c->stage, u->host_ptr, need, cudaMemcpyHostToDevice, c->stream), "weight_raw_h2d", err,
                cap) ||
+      !cuda_ok(c, launch_gemm_tile_weights(c->stage, u->raw, (int)u->rows, (int)u->cols, c->stream), "weight_raw_tile",
+               err, cap) ||
       !cuda_ok(c, cudaStreamSynchronize(c->stream), "weight_raw_sync", err, cap))
     return false;
   c->stats.host_to_device_bytes += need;
@@ -2378,6 +2382,69 @@ int minicpmo_gpu_context_matmul_q8_0_batch(void* handle, const void* host_ptr, c
                     error, error_cap) &&
             cuda_ok(c, cudaStreamSynchronize(c->stream), "mm_sync", error, error_cap);
   if (ok && !check_dev_err(c, error, error_cap)) ok = false;
+  return ok ? 1 : 0;
+}
+
+int minicpmo_gpu_context_time_matmul_q8_0_batch(void* handle, const void* host_ptr, size_t n_seq, int iters,
+                                                float* avg_us, char* error, size_t error_cap) {
+  Ctx* c = (Ctx*)handle;
+  if (!c) return copy_error(error, error_cap, "error: null gpu context"), 0;
+  DeviceGuard g(c);
+  Upload* u = find_upload(c, host_ptr);
+  if (!u || iters <= 0 || n_seq < 1 || n_seq > (size_t)kGemmMaxN || u->rows % kGemmTileRows || u->cols % kGemmKTile)
+    return fail(c, error, error_cap, "error: time_matmul_q8_0_batch needs an uploaded Q8_0 tensor and 1..32 sequences");
+  if (!ensure_raw(c, u, error, error_cap)) return 0;
+  const int N = n_seq <= 16 ? 16 : 32;
+  const size_t in_dim = u->cols, out_dim = u->rows;
+  const int tiles = (int)(out_dim / kGemmTileRows), ktiles = (int)(in_dim / kGemmKTile);
+  const int ks = gemm_pick_ksplit(tiles, ktiles, c->sm_count);
+  const size_t flush_bytes = (size_t)256 << 20;  // > the 126 MB L2: every timed launch streams W from HBM
+  if (!ensure(c, &c->sy, &c->sy_bytes, n_seq * out_dim * 4, "scratch_y_malloc", error, error_cap) ||
+      !ensure(c, &c->bx16, &c->bx16_bytes, (size_t)N * in_dim * 2, "batch_x16_malloc", error, error_cap) ||
+      !ensure(c, &c->stage, &c->stage_bytes, flush_bytes, "l2_flush_malloc", error, error_cap))
+    return 0;
+  if (ks > 1) {
+    const bool grow = c->bcnt_bytes < (size_t)tiles * 4;
+    if (!ensure(c, &c->bpart, &c->bpart_bytes, (size_t)ks * N * out_dim * 4, "batch_partial_malloc", error, error_cap) ||
+        !ensure(c, &c->bcnt, &c->bcnt_bytes, (size_t)tiles * 4, "batch_counter_malloc", error, error_cap))
+      return 0;
+    if (grow && !cuda_ok(c, cudaMemsetAsync(c->bcnt, 0, c->bcnt_bytes, c->stream), "batch_counter_memset", error, error_cap))
+      return 0;
+  }
+  GemmArgs a{};
+  a.seg[0].w = u->raw;
+  a.seg[0].rows = (int)out_dim;
+  a.nseg = 1;
+  a.rows_total = (int)out_dim;
+  a.K = (int)in_dim;
+  a.x = c->bx16;
+  a.N = N;
+  a.n_valid = (int)n_seq;
+  a.y = c->sy;
+  a.ldy = (int)out_dim;
+  a.epi = kGemmStore;
+  a.ksplit = ks;
+  a.partial = c->bpart;
+  a.counters = c->bcnt;
+  a.err = c->dev_err;
+  cudaEvent_t e0, e1;
+  cudaEventCreate(&e0);
+  cudaEventCreate(&e1);
+  float total = 0.0f;
+  bool ok = cuda_ok(c, cudaMemsetAsync(c->bx16, 0, (size_t)N * in_dim * 2, c->stream), "tm_x16_memset", error, error_cap);
+  for (int i = 0; ok && i <= iters; ++i) {  // iteration 0 warms up
+    ok = cuda_ok(c, cudaMemsetAsync(c->stage, i & 0xff, flush_bytes, c->stream), "tm_l2_flush", error, error_cap);
+    if (ok) cudaEventRecord(e0, c->stream);
+    if (ok) ok = cuda_ok(c, launch_gemm_q80(a, c->stream), "tm_gemm", error, error_cap);
+    if (ok) cudaEventRecord(e1, c->stream);
+    if (ok) ok = cuda_ok(c, cudaEventSynchronize(e1), "tm_sync", error, error_cap);
+    float ms = 0.0f;
+    if (ok && i > 0) cudaEventElapsedTime(&ms, e0, e1), total += ms;
+  }
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  if (ok && !check_dev_err(c, error, error_cap)) ok = false;
+  if (ok && avg_us) *avg_us = total * 1000.0f / (float)iters;
   return ok ? 1 : 0;
 }
 

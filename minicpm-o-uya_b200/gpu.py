@@ -135,6 +135,7 @@ SIGNATURES = {
     "minicpmo_gpu_context_matvec_f32_input": (i32, [vp, vp, fptr, vp, f32, sz, sz, fptr] + E),
     "minicpmo_gpu_context_time_matvec_input": (i32, [vp, vp, sz, sz, i32, i32, vp, fptr] + E),
     "minicpmo_gpu_context_matmul_q8_0_batch": (i32, [vp, vp, fptr, sz, sz, sz, fptr] + E),
+    "minicpmo_gpu_context_time_matmul_q8_0_batch": (i32, [vp, vp, sz, i32, fptr] + E),
     "minicpmo_gpu_context_qwen3_forward_batch": (i32, [vp, sz, u32ptr, u32ptr, i32, u32ptr, fptr, fptr] + E),
     "minicpmo_gpu_context_qwen3_decode_batch": (i32, [vp, sz, u32ptr, u32ptr, sz, u32ptr] + E),
     "minicpmo_gpu_context_qwen3_time_decode_batch": (i32, [vp, sz, u32ptr, u32ptr, sz, fptr] + E),
@@ -413,6 +414,12 @@ class GpuContext:
     def time_matvec(self, t: Tensor, iters: int = 20) -> float:
         us = f32()
         self._call("minicpmo_gpu_context_time_matvec", t.ptr, t.cols, t.rows, iters, C.byref(us))
+        return float(us.value)
+
+    def time_matmul_q8_0_batch(self, t: Tensor, n_seq: int, iters: int = 10) -> float:
+        """Mean device time (us) of the tensor-core projection, L2 flushed before each launch."""
+        us = f32()
+        self._call("minicpmo_gpu_context_time_matmul_q8_0_batch", t.ptr, n_seq, iters, C.byref(us))
         return float(us.value)
 
     def qwen3_forward_batch(self, tokens, positions, logits: bool = True, want_logits: bool = False):
