@@ -87,13 +87,19 @@ __host__ __device__ inline size_t attn_merge_stage_offset() {
   return round16(sizeof(float) * (3 * (size_t)kGMax * kMaxSplit + kGMax));
 }
 
+// The tile ring's mbarriers (one per buffer) follow the tile / merge area.
 template <int J, typename T, bool kCluster>
-__host__ __device__ inline size_t attn_smem_bytes_t(int hd) {
+__host__ __device__ inline size_t attn_bars_offset(int hd) {
   using C = TileCfg<J, T>;
   const size_t tiles = C::kRing * C::buf_bytes(hd);
   const size_t merge = kCluster ? sizeof(float) * (size_t)kGMax * attn_part_stride(hd)
                                 : attn_merge_stage_offset() + sizeof(float) * (size_t)kMergeStage;
-  return attn_tiles_offset(hd) + (tiles > merge ? tiles : merge);
+  return round16(attn_tiles_offset(hd) + (tiles > merge ? tiles : merge));
+}
+
+template <int J, typename T, bool kCluster>
+__host__ __device__ inline size_t attn_smem_bytes_t(int hd) {
+  return attn_bars_offset<J, T, kCluster>(hd) + 8 * TileCfg<J, T>::kRing;
 }
 
 // Distributed shared memory: the address of `p` in the shared memory of
@@ -142,30 +148,40 @@ __device__ __forceinline__ float2 h2f2(uint32_t u) {
 }
 
 // Requests K/V rows [c0, c0 + kSub) of a cache in its own type into tile
-// buffer `buf` ([K rows][V rows], row stride hs elements) with 16-byte
-// asynchronous copies; rows >= t1 are zero-filled, and the current
-// position's row (fused mode) is left for put_pos_row.  No commit.
+// buffer `buf` ([K rows][V rows], row stride hs elements): warp 0, one bulk
+// copy per row and matrix (lane = row), completing on `bar`.  Rows >= t1
+// and the current position's row (fused mode) are not copied (zero_rows /
+// put_pos_row fill them).
 template <typename TT>
-__device__ __forceinline__ void issue_tile(uint8_t* buf, const uint8_t* kc, const uint8_t* vc, int c0, int t1,
-                                           int pos, bool fused, int kv_dim, size_t kv_off, int hd, int hs) {
+__device__ __forceinline__ void issue_tile(uint8_t* buf, uint64_t* bar, const uint8_t* kc, const uint8_t* vc, int c0,
+                                           int t1, int pos, bool fused, int kv_dim, size_t kv_off, int hd, int hs,
+                                           int lane) {
+  const size_t rowb = (size_t)hs * sizeof(TT);
+  const uint32_t bytes = (uint32_t)(hd * sizeof(TT));
+  const int t = c0 + lane;
+  const bool cp = t < t1 && !(fused && t == pos);
+  const unsigned rows = __popc(__ballot_sync(0xffffffffu, cp));
+  if (lane == 0) mbar_arrive_expect_tx(bar, rows * 2u * bytes);
+  __syncwarp();
+  if (cp) {
+    const size_t off = ((size_t)t * kv_dim + kv_off) * sizeof(TT);
+    bulk_load(buf + (size_t)lane * rowb, kc + off, bytes, bar);
+    bulk_load(buf + (size_t)(kSub + lane) * rowb, vc + off, bytes, bar);
+  }
+}
+
+// Zeroes tile rows [t1 - c0, kSub) (positions past the chunk: their scores
+// are masked, but P.V reads them).
+template <typename TT>
+__device__ __forceinline__ void zero_rows(uint8_t* buf, int c0, int t1, int hd, int hs) {
+  const int r0 = t1 - c0;
+  if (r0 >= kSub) return;
   const int per = hd * (int)sizeof(TT) / 16;
   const size_t rowb = (size_t)hs * sizeof(TT);
-  uint8_t* kt = buf;
-  uint8_t* vt = buf + kSub * rowb;
-  for (int e = threadIdx.x; e < kSub * per; e += blockDim.x) {
-    const int r = e / per, p = e - r * per, t = c0 + r;
-    uint8_t* kd = kt + r * rowb + p * 16;
-    uint8_t* vd = vt + r * rowb + p * 16;
-    if (t < t1) {
-      if (!(fused && t == pos)) {
-        const size_t off = ((size_t)t * kv_dim + kv_off) * sizeof(TT) + (size_t)p * 16;
-        cp_async16(kd, kc + off);
-        cp_async16(vd, vc + off);
-      }
-    } else {
-      *reinterpret_cast<uint4*>(kd) = make_uint4(0u, 0u, 0u, 0u);
-      *reinterpret_cast<uint4*>(vd) = make_uint4(0u, 0u, 0u, 0u);
-    }
+  for (int e = threadIdx.x; e < (kSub - r0) * per; e += blockDim.x) {
+    const int r = r0 + e / per, p = e % per;
+    *reinterpret_cast<uint4*>(buf + (size_t)r * rowb + p * 16) = make_uint4(0u, 0u, 0u, 0u);
+    *reinterpret_cast<uint4*>(buf + (size_t)(kSub + r) * rowb + p * 16) = make_uint4(0u, 0u, 0u, 0u);
   }
 }
 
@@ -293,6 +309,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a)
   float* s_vpos = s_kpos + hd;
   float* s_sq = s_vpos + hd;  // [kAttnWarps][256]
   uint8_t* s_tiles = smem_b + attn_tiles_offset(hd);
+  uint64_t* s_bar = reinterpret_cast<uint64_t*>(smem_b + attn_bars_offset<J, T, kCluster>(hd));
   const size_t buf_bytes = C::buf_bytes(hd);
 
   const int kvh = blockIdx.x, split = blockIdx.y, z = blockIdx.z;
@@ -326,11 +343,18 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a)
   // position comes from this kernel's prologue), and the norm weight and
   // RoPE lines (into L1).
   if constexpr (C::kAsync) {
+    if (warp == 0) {
+      if (lane == 0) {
 #pragma unroll
-    for (int i = 0; i < NT - 1; ++i) {
-      if (i < nsub)
-        issue_tile<TT>(s_tiles + i * buf_bytes, kc, vc, t0 + i * kSub, t1, pos, fused, kv_dim, kv_off, hd, hs);
-      cp_async_commit();
+        for (int b = 0; b < NT; ++b) mbar_init(&s_bar[b], 1);
+        mbar_fence_init();
+      }
+      __syncwarp();
+#pragma unroll
+      for (int i = 0; i < NT - 1; ++i)
+        if (i < nsub)
+          issue_tile<TT>(s_tiles + i * buf_bytes, &s_bar[i], kc, vc, t0 + i * kSub, t1, pos, fused, kv_dim, kv_off, hd,
+                         hs, lane);
     }
   }
   if (fused && active && threadIdx.x < 12) {
@@ -348,27 +372,19 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a)
   pdl_wait();
   pdl_launch_dependents();
 
-  // K/V of the current position (fused: normalised/rotated here; needed by
-  // split 0, which appends it, and by the split that holds position pos).
-  if (fused && (split == 0 || split == n_active - 1)) {
-    if (warp < 2) {
-      const float* src = (warp == 0 ? a.k : a.v) + (size_t)z * a.qkv_bstride + kv_off;
-      float* dst = warp == 0 ? s_kpos : s_vpos;
-      float r[8];
+  // Every global load of the prologue first: K/V of the current position
+  // (fused: normalised/rotated here; needed by split 0, which appends it,
+  // and by the split that holds position pos) on warps 0/1, and each warp's
+  // q rows of this kv head's group; then the stores and the norms.
+  const bool kv_split = fused && (split == 0 || split == n_active - 1) && warp < 2;
+  float kvr[8];
+  float qv[2][8];
+  if (kv_split) {
+    const float* src = (warp == 0 ? a.k : a.v) + (size_t)z * a.qkv_bstride + kv_off;
 #pragma unroll
-      for (int k = 0; k < 8; ++k) r[k] = lane + 32 * k < hd ? src[lane + 32 * k] : 0.0f;
-#pragma unroll
-      for (int k = 0; k < 8; ++k)
-        if (lane + 32 * k < hd) dst[lane + 32 * k] = r[k];
-      __syncwarp();
-      if (warp == 0)
-        norm_rope_row(s_kpos, s_sq, hd, a.k_norm, a.k_norm_dtype, true, a.rope_cos, a.rope_sin, a.rope_base,
-                      a.rope_scale, pos, lane);
-    }
+    for (int k = 0; k < 8; ++k) kvr[k] = lane + 32 * k < hd ? src[lane + 32 * k] : 0.0f;
   }
-  // q rows of this kv head's group (loads of both rows of a warp first)
   if (active) {
-    float qv[2][8];
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
       const int g = warp + i * kAttnWarps;
@@ -378,6 +394,14 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a)
         qv[i][k] = (g < G && d < hd) ? qp[(size_t)(hb + g) * hd + d] : 0.0f;
       }
     }
+  }
+  if (kv_split) {
+    float* dst = warp == 0 ? s_kpos : s_vpos;
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (lane + 32 * k < hd) dst[lane + 32 * k] = kvr[k];
+  }
+  if (active) {
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
       const int g = warp + i * kAttnWarps;
@@ -387,8 +411,11 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a)
         if (g < G && d < hd) s_q[g * hd + d] = qv[i][k];
       }
     }
-    __syncwarp();
   }
+  __syncwarp();
+  if (kv_split && warp == 0)
+    norm_rope_row(s_kpos, s_sq, hd, a.k_norm, a.k_norm_dtype, true, a.rope_cos, a.rope_sin, a.rope_base, a.rope_scale,
+                  pos, lane);
   for (int g = warp; active && g < G; g += kAttnWarps) {
     float* row = s_q + g * hd;
     if (fused)
@@ -419,12 +446,12 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a)
       if constexpr (C::kAsync) {
         // request the tile NT-1 ahead into the buffer the previous
         // iteration finished with, then complete this one
-        if (i + NT - 1 < nsub)
-          issue_tile<TT>(s_tiles + (size_t)((i + NT - 1) % NT) * buf_bytes, kc, vc, c0 + (NT - 1) * kSub, t1, pos,
-                         fused, kv_dim, kv_off, hd, hs);
-        cp_async_commit();
+        if (warp == 0 && i + NT - 1 < nsub)
+          issue_tile<TT>(s_tiles + (size_t)((i + NT - 1) % NT) * buf_bytes, &s_bar[(i + NT - 1) % NT], kc, vc,
+                         c0 + (NT - 1) * kSub, t1, pos, fused, kv_dim, kv_off, hd, hs, lane);
         put_pos_row<TT>(buf, s_kpos, s_vpos, c0, t1, pos, fused, hd, hs);
-        cp_async_wait<NT - 1>();
+        zero_rows<TT>(buf, c0, t1, hd, hs);
+        mbar_wait(&s_bar[i % NT], (uint32_t)(i / NT) & 1u, a.err);
       } else {
         float* kt = reinterpret_cast<float*>(buf);
         stage_kv_tile<T>(kc, vc, s_kpos, s_vpos, kt, kt + (size_t)kSub * hs, c0, t1, pos, fused, kv_dim, kv_off, hd,
@@ -495,28 +522,45 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a)
       const bool ve = e < G * hd;
       const int g = ve ? e / hd : 0, d = ve ? e - g * hd : 0;
       const float* row = part_s + (size_t)g * stride_part;
-      float ms[kAttnMaxCluster], ls[kAttnMaxCluster], av[kAttnMaxCluster];
+      float av[kAttnMaxCluster];
 #pragma unroll
-      for (int sp = 0; sp < kAttnMaxCluster; ++sp) {
-        ms[sp] = -INFINITY;
-        ls[sp] = av[sp] = 0.0f;
-        if (sp < n_active) {
-          ms[sp] = dsmem_ld(dsmem_addr(row, sp));
-          ls[sp] = dsmem_ld(dsmem_addr(row + 1, sp));
-          av[sp] = dsmem_ld(dsmem_addr(row + 4 + d, sp));
-        }
-      }
-      float M = -INFINITY;
-#pragma unroll
-      for (int sp = 0; sp < kAttnMaxCluster; ++sp)
-        if (sp < n_active) M = fmaxf(M, ms[sp]);
+      for (int sp = 0; sp < kAttnMaxCluster; ++sp) av[sp] = sp < n_active ? dsmem_ld(dsmem_addr(row + 4 + d, sp)) : 0.0f;
       float L = 0.0f, o = 0.0f;
+      if ((hd & 31) == 0) {
+        // one head per unit: lane sp holds split sp's (m, l) and weight
+        // w_sp = exp(m_sp - M); the sums run in split order via shuffles
+        const float* hrow = part_s + (size_t)(u * 32 / hd) * stride_part;
+        const float msp = lane < n_active ? dsmem_ld(dsmem_addr(hrow, lane)) : -INFINITY;
+        const float lsp = lane < n_active ? dsmem_ld(dsmem_addr(hrow + 1, lane)) : 0.0f;
+        const float M = warp_max(msp);
+        const float wsp = lane < n_active ? expf_det(__fsub_rn(msp, M)) : 0.0f;
 #pragma unroll
-      for (int sp = 0; sp < kAttnMaxCluster; ++sp) {
-        if (sp < n_active) {
-          const float w = expf_det(__fsub_rn(ms[sp], M));
-          L = __fmaf_rn(w, ls[sp], L);
-          o = __fmaf_rn(w, av[sp], o);
+        for (int sp = 0; sp < kAttnMaxCluster; ++sp) {
+          const float w = __shfl_sync(0xffffffffu, wsp, sp);
+          const float ls = __shfl_sync(0xffffffffu, lsp, sp);
+          if (sp < n_active) {
+            L = __fmaf_rn(w, ls, L);
+            o = __fmaf_rn(w, av[sp], o);
+          }
+        }
+      } else {  // small heads: a unit spans several heads, each lane its own
+        float ms[kAttnMaxCluster], ls[kAttnMaxCluster];
+#pragma unroll
+        for (int sp = 0; sp < kAttnMaxCluster; ++sp) {
+          ms[sp] = sp < n_active ? dsmem_ld(dsmem_addr(row, sp)) : -INFINITY;
+          ls[sp] = sp < n_active ? dsmem_ld(dsmem_addr(row + 1, sp)) : 0.0f;
+        }
+        float M = -INFINITY;
+#pragma unroll
+        for (int sp = 0; sp < kAttnMaxCluster; ++sp)
+          if (sp < n_active) M = fmaxf(M, ms[sp]);
+#pragma unroll
+        for (int sp = 0; sp < kAttnMaxCluster; ++sp) {
+          if (sp < n_active) {
+            const float w = expf_det(__fsub_rn(ms[sp], M));
+            L = __fmaf_rn(w, ls[sp], L);
+            o = __fmaf_rn(w, av[sp], o);
+          }
         }
       }
       o = __fmul_rn(o, L > 0.0f ? __fdiv_rn(1.0f, L) : 0.0f);

@@ -46,6 +46,7 @@ struct AttnArgs {
   int batch;
   size_t qkv_bstride, cache_bstride, out_bstride, outq8_bstride;
   int pos_stride;  // ints between sequences' positions at pos_ptr (0: 1)
+  int* err;        // raised by a bounded wait that gave up (may be null)
 };
 
 constexpr int kAttnMaxCluster = 16;  // cluster size (beyond 8 needs the non-portable opt-in)

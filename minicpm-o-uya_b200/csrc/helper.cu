@@ -616,6 +616,7 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
     a.counters = m.counters;
     a.out = m.attn;
     a.out_q8 = (L.o->tiled && hd % 32 == 0) ? m.aq : nullptr;
+    a.err = &m.st->err;
     REC(launch_attention(a, s, true));
     // (head_dim % 32 != 0: the o GEMV quantises the f32 attention output itself)
     if (tp) {  // row-parallel: this rank's partial, then hidden += sum of all ranks' partials
@@ -754,6 +755,7 @@ cudaError_t record_batch_step(Ctx* c, Model& m, bool logits) {
     a.qkv_bstride = b.ldqkv;
     a.cache_bstride = (size_t)cf.context * kvd;
     a.out_bstride = (size_t)qd;
+    a.err = &b.st[0].err;
     REC(launch_attention(a, s, true));
     REC(launch_pack_x16(b.attn, qd, B, qd, N, b.x16, s, true));
     Upload* o[1] = {L.o};
