@@ -312,10 +312,10 @@ MINICPMO_API size_t minicpmo_gpu_context_tensor_device_bytes(void *handle, const
 /* ---- allocation-free decode attention (no reference counterpart) ---- */
 
 /* Limits of the fixed scratch the entry below uses instead of allocating:
- * at most 1024 KV heads, and head_count x n_split x (head_dim + 4) x 4 bytes
- * of split-K partial sums at most 2 MiB (n_split = clamp(ceil(256 /
- * kv_head_count), 1, 8); Qwen3-32B's 64 heads / 8 KV heads / head_dim 128
- * need 264 KiB).  Larger shapes are rejected with an error. */
+ * at most 1024 KV heads, and head_count x ceil(context_capacity / 32) x
+ * (head_dim + 4) x 4 bytes of per-block partial sums at most 2 MiB (Qwen3-8B's
+ * 32 heads with head_dim 128 fit a 3968-position cache; Qwen3-32B's 64 heads
+ * a 1984-position one).  Larger shapes are rejected with an error. */
 #define MINICPMO_NOALLOC_MAX_KV_HEADS 1024
 #define MINICPMO_NOALLOC_PARTIAL_BYTES (2u << 20)
 

@@ -5,23 +5,30 @@
 // softmax over t, out = sum_t p_t v_t.  KV cache layout [layer][pos][kv_dim]
 // as the reference (qwen3.uya:1664-1666), f32 (reference) or f16.
 //
-// B200 design: split-K flash decoding.  grid = (n_kv, n_split, batch); a CTA
-// owns one kv head of one sequence and a contiguous range of positions,
-// serves every q head of its GQA group from one pass over K and V (each K/V
-// row is read once per token), keeps an online softmax per head in
-// registers and produces one partial (m, l, acc) per head.  The partials of
-// a kv head are merged either inside a thread-block cluster through
-// distributed shared memory (the default of the decode graph) or by the
-// last-arriving CTA through global memory (atomic ticket); both merge in
-// split order with the same operations, so they give the same bits.  The
-// merge writes the f32 output and, optionally, its Q8_1 blocks for the
-// o-projection -- no separate combine launch.
+// Arithmetic (the device order, restated by the oracle): positions are cut
+// into blocks of 32.  For every q head and block c, with lane = position:
+//   s_t = scale * sum_d q_d k_td          (one sequential fma chain over d)
+//   m_c = max_t s_t,  p_t = exp(s_t - m_c) (0 past the last position)
+//   l_c = butterfly_sum(p),  acc_c,d = sum_t p_t v_td  (fma in t order)
+// and the blocks merge in block order:
+//   M = max_c m_c,  w_c = exp(m_c - M),  L = sum_c w_c l_c,
+//   o_d = (sum_c w_c acc_c,d) * (1/L)      (fma chains in c order).
 //
-// K/V rows reach shared memory by 16-byte asynchronous copies (L2 only) in
-// the cache's own type, into a ring of 32-position tiles: the first tiles
+// B200 design: grid = (n_kv, n_split, batch); the n_split CTAs of a kv head
+// take its blocks round-robin, and inside a CTA eight warps work on (head,
+// block) pairs side by side, so a 600-position context is one round of
+// work.  K/V rows reach shared memory in the cache's own type by 16-byte
+// asynchronous copies from every thread (L2 only), a ring of 32-position
+// tiles whose mbarriers count the copies' arrivals; the first round's tiles
 // are requested before the kernel waits for its predecessor (programmatic
-// dependent launch), and each later tile is requested while the tile before
-// it is being used.
+// dependent launch).  The block partials merge either inside a thread-block
+// cluster -- each warp stores its block's values straight into the shared
+// memory of the CTA that merges each 32-value output unit, so the merge
+// reads only local shared memory (the default of the single-sequence
+// decode graph) -- or through global memory by the last-arriving CTA
+// (atomic ticket; the batched decode); both give the same bits.  The merge
+// writes the f32 output and, optionally, its Q8_1 blocks for the
+// o-projection.
 //
 // Fused mode also performs, for the current position, the per-head
 // QK-RMSNorm (qwen3.uya:1543-1558, eps 1e-6, reduction order of
@@ -47,14 +54,10 @@ namespace mcpo {
 
 namespace {
 
-constexpr int kAttnWarps = 4;
-constexpr int kGMax = 8;  // q heads per kv head handled by one CTA (<= 2 per warp)
+constexpr int kAttnWarps = 8;
+constexpr int kGMax = 8;  // q heads per kv head handled by one CTA
 constexpr int kMaxSplit = 64;
-
-// The global-memory merge reuses the tile area: per q head of the group the
-// splits' m, l and weights, 1/L, and (when they fit) a copy of every split's
-// partial row.
-constexpr int kMergeStage = 12288;  // floats of staged partial rows (48 KB)
+constexpr int kMaxBlocks = 4096;  // blocks per sequence (131072 positions)
 
 // Small odd head sizes (J = 1, head_dim <= 32) stage f32 tiles through
 // registers with this row stride; the async tiles use head_dim + 16 bytes.
@@ -68,42 +71,80 @@ template <int J, typename T>
 struct TileCfg {
   static constexpr bool kAsync = J >= 2;
   using TT = std::conditional_t<kAsync, T, float>;
-  static constexpr int kRing = kAsync ? (J >= 8 ? 2 : 3) : 1;
+  static constexpr int kRing = (kAsync && (sizeof(T) == 2 || J < 8)) ? 4 : 2;
   __host__ __device__ static int stride(int hd) { return kAsync ? hd + 16 / (int)sizeof(TT) : attn_tile_stride(hd); }
   __host__ __device__ static size_t buf_bytes(int hd) { return 2 * (size_t)kSub * stride(hd) * sizeof(TT); }
 };
 
 __host__ __device__ inline size_t round16(size_t b) { return (b + 15) & ~(size_t)15; }
 
+// Blocks a CTA computes per round: one warp per (head, block), at most
+// half the tile ring (the next round's tiles load meanwhile).
+template <int J, typename T>
+__host__ __device__ inline int attn_bpr(int G) {
+  const int b = kAttnWarps / G, h = TileCfg<J, T>::kRing / 2;
+  return b < 1 ? 1 : (b < h ? b : h);
+}
+
+// Tile buffers a CTA uses when the CTAs of a kv head hold at most nb_cta
+// blocks each: every block its own buffer when two rounds cover them, else
+// two rounds' worth in turn.  The shared-memory carve-up uses the group
+// size g_min = n_head / n_kv (the most blocks per round of any kv head).
+template <int J, typename T>
+__host__ __device__ inline int attn_ring(int g, int nb_cta) {
+  const int r = 2 * attn_bpr<J, T>(g);
+  return nb_cta < 1 ? 1 : (nb_cta < r ? nb_cta : r);
+}
+
+// Cluster merge: the CTA that merges a 32-value output unit receives, for
+// every block c of the context, that unit's 32 accumulator values and the
+// block's (m, l) in one row of kMergeRow floats (16-byte rows).
+constexpr int kMergeRow = 36;
+
 // Shared memory: q [kGMax][hd], kpos [hd], vpos [hd], norm scratch
-// [kAttnWarps][256] (f32), then at tiles_offset the tile ring, which the
-// merge reuses (cluster: this split's partial rows [G][hd + 4]; global:
-// m/l/w [kGMax][kMaxSplit] x3, 1/L [kGMax], staged partial rows).
+// [kAttnWarps][256] (f32), `ring` tile buffers, the cluster path's merge
+// rows [slots][attn_n_blocks(ctx)][kMergeRow] (f32), one mbarrier per tile
+// buffer.
 __host__ __device__ inline size_t attn_tiles_offset(int hd) {
   return round16(sizeof(float) * ((size_t)kGMax * hd + 2 * (size_t)hd + kAttnWarps * 256));
 }
 
-__host__ __device__ inline size_t attn_merge_stage_offset() {
-  return round16(sizeof(float) * (3 * (size_t)kGMax * kMaxSplit + kGMax));
+template <int J, typename T>
+__host__ __device__ inline size_t attn_parts_offset(int hd, int ring) {
+  return attn_tiles_offset(hd) + (size_t)ring * TileCfg<J, T>::buf_bytes(hd);
 }
 
-// The tile ring's mbarriers (one per buffer) follow the tile / merge area.
-template <int J, typename T, bool kCluster>
-__host__ __device__ inline size_t attn_bars_offset(int hd) {
-  using C = TileCfg<J, T>;
-  const size_t tiles = C::kRing * C::buf_bytes(hd);
-  const size_t merge = kCluster ? sizeof(float) * (size_t)kGMax * attn_part_stride(hd)
-                                : attn_merge_stage_offset() + sizeof(float) * (size_t)kMergeStage;
-  return round16(attn_tiles_offset(hd) + (tiles > merge ? tiles : merge));
+template <int J, typename T>
+__host__ __device__ inline size_t attn_bars_offset(int hd, int ring, int merge_rows) {
+  return round16(attn_parts_offset<J, T>(hd, ring) + sizeof(float) * (size_t)merge_rows * kMergeRow);
 }
 
-template <int J, typename T, bool kCluster>
-__host__ __device__ inline size_t attn_smem_bytes_t(int hd) {
-  return attn_bars_offset<J, T, kCluster>(hd) + 8 * TileCfg<J, T>::kRing;
+template <int J, typename T>
+__host__ __device__ inline size_t attn_smem_bytes_t(int hd, int ring, int merge_rows) {
+  return attn_bars_offset<J, T>(hd, ring, merge_rows) + 8 * (size_t)ring;
+}
+
+// The layout of one launch (kernel and host compute it alike): a unit u of
+// a kv head's G * hd / 32 is merged by CTA u mod n_split in its slot
+// u / n_split.
+struct AttnLayout {
+  int ring, merge_rows;
+};
+
+template <int J, typename T>
+__host__ __device__ inline AttnLayout attn_layout(int hd, int n_head, int n_kv, int ctx, int n_split, bool cluster) {
+  const int nb_cta = (attn_n_blocks(ctx) + n_split - 1) / n_split;
+  const int g_min = n_head / n_kv > 0 ? n_head / n_kv : 1;
+  const int g_max = (n_head + n_kv - 1) / n_kv;
+  const int slots = (g_max * (hd / 32) + n_split - 1) / n_split;
+  AttnLayout l;
+  l.ring = attn_ring<J, T>(g_min, nb_cta);
+  l.merge_rows = cluster ? slots * attn_n_blocks(ctx) : 0;
+  return l;
 }
 
 // Distributed shared memory: the address of `p` in the shared memory of
-// cluster CTA `rank`, a load from it, and a full cluster barrier (release /
+// cluster CTA `rank`, stores to it, and a full cluster barrier (release /
 // acquire: shared-memory writes before it are visible to every CTA of the
 // cluster after it).
 __device__ __forceinline__ uint32_t dsmem_addr(const void* p, int rank) {
@@ -112,25 +153,16 @@ __device__ __forceinline__ uint32_t dsmem_addr(const void* p, int rank) {
   return a;
 }
 
-__device__ __forceinline__ float dsmem_ld(uint32_t a) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(a) : "memory");
-  return v;
+__device__ __forceinline__ void dsmem_st4(uint32_t a, float x, float y, float z, float w) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(a), "f"(x), "f"(y), "f"(z), "f"(w) : "memory");
+}
+
+__device__ __forceinline__ void dsmem_st2(uint32_t a, float x, float y) {
+  asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(a), "f"(x), "f"(y) : "memory");
 }
 
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
-}
-
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
-}
-
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 template <typename TT>
@@ -148,26 +180,29 @@ __device__ __forceinline__ float2 h2f2(uint32_t u) {
 }
 
 // Requests K/V rows [c0, c0 + kSub) of a cache in its own type into tile
-// buffer `buf` ([K rows][V rows], row stride hs elements): warp 0, one bulk
-// copy per row and matrix (lane = row), completing on `bar`.  Rows >= t1
-// and the current position's row (fused mode) are not copied (zero_rows /
-// put_pos_row fill them).
+// buffer `buf` ([K rows][V rows], row stride hs elements): every thread of
+// the CTA copies its share of the 16-byte pieces (cp.async, L2 only) and
+// arrives on `bar` once they have landed (the barrier counts one arrival
+// per thread).  Rows >= t1 and the current position's row (fused mode) are
+// not copied (zero_rows / put_pos_row fill them).
 template <typename TT>
 __device__ __forceinline__ void issue_tile(uint8_t* buf, uint64_t* bar, const uint8_t* kc, const uint8_t* vc, int c0,
-                                           int t1, int pos, bool fused, int kv_dim, size_t kv_off, int hd, int hs,
-                                           int lane) {
+                                           int t1, int pos, bool fused, int kv_dim, size_t kv_off, int hd, int hs) {
+  const int cpr = hd * (int)sizeof(TT) / 16;  // pieces per row
   const size_t rowb = (size_t)hs * sizeof(TT);
-  const uint32_t bytes = (uint32_t)(hd * sizeof(TT));
-  const int t = c0 + lane;
-  const bool cp = t < t1 && !(fused && t == pos);
-  const unsigned rows = __popc(__ballot_sync(0xffffffffu, cp));
-  if (lane == 0) mbar_arrive_expect_tx(bar, rows * 2u * bytes);
-  __syncwarp();
-  if (cp) {
-    const size_t off = ((size_t)t * kv_dim + kv_off) * sizeof(TT);
-    bulk_load(buf + (size_t)lane * rowb, kc + off, bytes, bar);
-    bulk_load(buf + (size_t)(kSub + lane) * rowb, vc + off, bytes, bar);
+  const int n = 2 * kSub * cpr;
+  for (int e = threadIdx.x; e < n; e += blockDim.x) {
+    const int m = e / (kSub * cpr), rem = e - m * (kSub * cpr);
+    const int r = rem / cpr, pc = rem - r * cpr, t = c0 + r;
+    if (t < t1 && !(fused && t == pos)) {
+      const uint8_t* src = (m ? vc : kc) + ((size_t)t * kv_dim + kv_off) * sizeof(TT) + (size_t)pc * 16;
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(buf + (size_t)(m * kSub + r) * rowb +
+                                                                             (size_t)pc * 16)),
+                   "l"(src)
+                   : "memory");
+    }
   }
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
 // Zeroes tile rows [t1 - c0, kSub) (positions past the chunk: their scores
@@ -277,39 +312,152 @@ __device__ __forceinline__ void load_v(const TT* vr, float (&v)[J]) {
   }
 }
 
+// One output value merged over the blocks of a context in block order, the
+// accessors giving block c's m, l and this lane's accumulator value (one
+// head for the whole warp):
+//   M = max_c m_c,  w_c = exp(m_c - M),  L = sum_c w_c l_c,
+//   o = (sum_c w_c acc_c) * (1/L)        (fma chains in c order).
+// Lane k holds blocks k, k+32, ...: their (m, l) and weights; the sums run
+// via shuffles.  Up to 128 blocks every value is requested in one round.
+template <typename FM, typename FL, typename FA>
+__device__ __forceinline__ float merge_blocks(int nblk, int lane, FM mf, FL lf, FA af) {
+  float L = 0.0f, o = 0.0f;
+  if (nblk <= 4 * 32) {
+    float mr[4], lr[4], av[32];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int c = 32 * q + lane;
+      mr[q] = c < nblk ? mf(c) : -INFINITY;
+      lr[q] = c < nblk ? lf(c) : 0.0f;
+    }
+#pragma unroll
+    for (int k = 0; k < 32; ++k) av[k] = k < nblk ? af(k) : 0.0f;
+    const float M = warp_max(fmaxf(fmaxf(mr[0], mr[1]), fmaxf(mr[2], mr[3])));
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int c0 = 32 * q;
+      if (c0 < nblk) {
+        if (q > 0) {
+#pragma unroll
+          for (int k = 0; k < 32; ++k) av[k] = c0 + k < nblk ? af(c0 + k) : 0.0f;
+        }
+        const float wc = c0 + lane < nblk ? expf_det(__fsub_rn(mr[q], M)) : 0.0f;
+#pragma unroll
+        for (int k = 0; k < 32; ++k) {
+          const float w = __shfl_sync(0xffffffffu, wc, k);
+          const float ls = __shfl_sync(0xffffffffu, lr[q], k);
+          if (c0 + k < nblk) {
+            L = __fmaf_rn(w, ls, L);
+            o = __fmaf_rn(w, av[k], o);
+          }
+        }
+      }
+    }
+  } else {  // longer contexts: the maximum first, then 32 blocks at a time
+    float M = -INFINITY;
+    for (int c0 = 0; c0 < nblk; c0 += 4 * 32) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        if (c0 + 32 * q + lane < nblk) M = fmaxf(M, mf(c0 + 32 * q + lane));
+    }
+    M = warp_max(M);
+    for (int c0 = 0; c0 < nblk; c0 += 32) {
+      const int c = c0 + lane;
+      const float mc = c < nblk ? mf(c) : -INFINITY;
+      const float lc = c < nblk ? lf(c) : 0.0f;
+      float av[32];
+#pragma unroll
+      for (int k = 0; k < 32; ++k) av[k] = c0 + k < nblk ? af(c0 + k) : 0.0f;
+      const float wc = c < nblk ? expf_det(__fsub_rn(mc, M)) : 0.0f;
+#pragma unroll
+      for (int k = 0; k < 32; ++k) {
+        const float w = __shfl_sync(0xffffffffu, wc, k);
+        const float ls = __shfl_sync(0xffffffffu, lc, k);
+        if (c0 + k < nblk) {
+          L = __fmaf_rn(w, ls, L);
+          o = __fmaf_rn(w, av[k], o);
+        }
+      }
+    }
+  }
+  return __fmul_rn(o, L > 0.0f ? __fdiv_rn(1.0f, L) : 0.0f);
+}
+
+// Writes merged unit u (lane = value) of the kv head whose first q head is
+// hb: the f32 output and, when requested (head_dim % 32 == 0), its Q8_1
+// block for the o-projection.
+__device__ __forceinline__ void write_unit(float o, int u, int lane, int hb, int hd, bool ve, float* outp,
+                                           uint8_t* oq8) {
+  if (ve) outp[(size_t)hb * hd + u * 32 + lane] = o;
+  if (oq8 && (hd % 32) == 0) {
+    uint16_t dbits;
+    bool zero;
+    const int q = q8_1_quant_lane(o, &dbits, &zero);
+    uint32_t word = ((uint32_t)(q & 0xff)) << (8 * (lane & 3));
+    word |= __shfl_xor_sync(0xffffffffu, word, 1);
+    word |= __shfl_xor_sync(0xffffffffu, word, 2);
+    float sum = 0.0f;  // the sequential f16 s of the reference block
+    for (int t = 0; t < 32; ++t) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, o, t));
+    uint32_t* ob = reinterpret_cast<uint32_t*>(oq8 + ((size_t)hb * hd / 32 + u) * 36);
+    if (lane == 0) ob[0] = (uint32_t)dbits | ((uint32_t)(zero ? (uint16_t)0 : f32_to_f16_ref(sum)) << 16);
+    if ((lane & 3) == 0) ob[1 + (lane >> 2)] = word;
+  }
+}
+
+// Per-head RMSNorm + RoPE of a row held in registers, v[k] = row[lane + 32k]
+// (head_dim = 32*J, J >= 2, so the rotation pairs k with k + J/2 in the
+// same lane), with the weights and the position's (cos, sin) already
+// loaded: the operations and their order are those of norm_rope_row with a
+// RoPE table.
+template <int J>
+__device__ __forceinline__ void norm_rope_regs(float (&v)[8], const float (&wr)[8], const float (&cr)[4],
+                                               const float (&sr)[4], bool has_w, int hd) {
+  static_assert(J >= 2 && J <= 8 && J % 2 == 0, "head_dim 64, 128 or 256");
+  if (has_w) {
+    float q[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) q[k] = k < J ? __fmul_rn(v[k], v[k]) : 0.0f;
+    float c = __fadd_rn(__fadd_rn(__fadd_rn(q[0], q[4]), __fadd_rn(q[2], q[6])),
+                        __fadd_rn(__fadd_rn(q[1], q[5]), __fadd_rn(q[3], q[7])));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) c = __fadd_rn(c, __shfl_down_sync(0xffffffffu, c, o));
+    c = __shfl_sync(0xffffffffu, c, 0);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(c, (float)hd), 1e-6f)));
+#pragma unroll
+    for (int k = 0; k < J; ++k) v[k] = __fmul_rn(__fmul_rn(v[k], inv), wr[k]);
+  }
+  constexpr int H = J / 2;
+#pragma unroll
+  for (int k = 0; k < H; ++k) {
+    const float x0 = v[k], x1 = v[k + H];
+    v[k] = __fsub_rn(__fmul_rn(x0, cr[k]), __fmul_rn(x1, sr[k]));
+    v[k + H] = __fadd_rn(__fmul_rn(x1, cr[k]), __fmul_rn(x0, sr[k]));
+  }
+}
+
 // J = output elements per lane in the P.V phase (hd = 32*J), or J = 1 with
-// hd <= 32 (masked lanes).
-//
-// Per q head and KV chunk, in order over sub-chunks of 32 positions
-// (lane = position):
-//   s_t   = scale * sum_d q_d k_td            (sequential fma over d)
-//   m'    = max(m, max_t s_t)
-//   alpha = exp(m - m'),  p_t = exp(s_t - m')  (0 beyond the chunk)
-//   l     = l*alpha + butterfly_sum(p)
-//   acc_d = acc_d*alpha, then acc_d = fma(p_t, v_td, acc_d) for t in order
-// and the splits are merged as o_d = (sum_s w_s acc_sd) / (sum_s w_s l_s),
-// w_s = exp(m_s - max m), sums in split order with fma.
-//
-// kCluster: the a.n_split CTAs of a kv head are one thread-block cluster;
-// each keeps its partial (m, l, acc) in shared memory and, after a cluster
-// barrier, merges 32-value units of the kv head's output (unit u on CTA
-// u mod n_split) reading every split's partial through distributed shared
-// memory -- no global scratch, no atomics, no second pass over global
-// memory.  Every thread of every CTA reaches both cluster barriers.
+// hd <= 32 (masked lanes).  kCluster: the a.n_split CTAs of a kv head are
+// one thread-block cluster; block partials stay in shared memory and, after
+// a cluster barrier, 32-value units of the kv head's output are merged
+// (unit u on CTA u mod n_split) reading the partials through distributed
+// shared memory.  Every thread of every CTA reaches both cluster barriers.
 template <int J, typename T, bool kCluster>
-__global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a) {
+__global__ void __launch_bounds__(kAttnWarps * 32, 2) k_attention(const AttnArgs a) {
   using C = TileCfg<J, T>;
   using TT = typename C::TT;
-  constexpr int NT = C::kRing;
   extern __shared__ __align__(16) uint8_t smem_b[];
   const int hd = a.head_dim;
   const int hs = C::stride(hd);
+  const int S = a.n_split;
+  const int nbmax_cta = (attn_n_blocks(a.ctx) + S - 1) / S;
+  const AttnLayout lay = attn_layout<J, T>(hd, a.n_head, a.n_kv, a.ctx, S, kCluster);
   float* s_q = reinterpret_cast<float*>(smem_b);  // [kGMax][hd]; the merged rows after the merge
   float* s_kpos = s_q + kGMax * hd;
   float* s_vpos = s_kpos + hd;
   float* s_sq = s_vpos + hd;  // [kAttnWarps][256]
   uint8_t* s_tiles = smem_b + attn_tiles_offset(hd);
-  uint64_t* s_bar = reinterpret_cast<uint64_t*>(smem_b + attn_bars_offset<J, T, kCluster>(hd));
+  float* s_merge = reinterpret_cast<float*>(smem_b + attn_parts_offset<J, T>(hd, lay.ring));
+  uint64_t* s_bar = reinterpret_cast<uint64_t*>(smem_b + attn_bars_offset<J, T>(hd, lay.ring, lay.merge_rows));
   const size_t buf_bytes = C::buf_bytes(hd);
 
   const int kvh = blockIdx.x, split = blockIdx.y, z = blockIdx.z;
@@ -323,41 +471,41 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a)
   float* outp = a.out + (size_t)z * a.out_bstride;
   uint8_t* oq8 = a.out_q8 ? a.out_q8 + (size_t)z * a.outq8_bstride : nullptr;
   const int pos = a.pos_ptr ? a.pos_ptr[(size_t)z * (a.pos_stride > 0 ? a.pos_stride : 1)] : a.pos_static;
+  if (pos < 0 || pos >= a.ctx) {  // every CTA of the sequence (and cluster) leaves here
+    if (threadIdx.x == 0 && a.err) atomicExch(a.err, 2);
+    return;
+  }
+  // cluster: shared memory of another CTA is written only once every CTA
+  // of the cluster has started (this arrival, the wait before the rounds)
+  if constexpr (kCluster) asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
   const int n_pos = pos + 1;
-  int chunk = (n_pos + a.n_split - 1) / a.n_split;
-  if (chunk < 32) chunk = 32;
-  const int n_active = (n_pos + chunk - 1) / chunk;
-  const int t0 = split * chunk;
-  const int t1 = min(t0 + chunk, n_pos);
-  const int nsub = split < n_active ? (t1 - t0 + kSub - 1) / kSub : 0;
+  const int nblk = attn_n_blocks(n_pos);
+  const int nb = split < nblk ? (nblk - 1 - split) / S + 1 : 0;  // this CTA's blocks: split + S*i, i < nb
+  const int bpr = attn_bpr<J, T>(G);
+  const int NT = attn_ring<J, T>(G, nbmax_cta);  // <= lay.ring (G >= g_min)
   const int kv_dim = a.n_kv * hd;
   const size_t kv_off = (size_t)kvh * hd;
   const int stride_part = attn_part_stride(hd);
   const bool fused = a.fuse_norm_rope_append != 0;
-  const bool active = nsub > 0;
+  const int pos_cta = (nblk - 1) % S;  // the CTA holding the current position's block
   const int nt = blockDim.x;
 
   // Before waiting for the previous kernel (programmatic dependent launch):
-  // everything that only depends on earlier steps -- the position, the K/V
-  // rows of earlier positions of the first NT-1 sub-chunks (the current
-  // position comes from this kernel's prologue), and the norm weight and
-  // RoPE lines (into L1).
+  // the position, the K/V rows of earlier positions for the first round's
+  // blocks (the current position comes from this kernel's prologue), and
+  // the norm weights and RoPE row (into registers, or into L1 for the
+  // shared-memory norm).
   if constexpr (C::kAsync) {
-    if (warp == 0) {
-      if (lane == 0) {
-#pragma unroll
-        for (int b = 0; b < NT; ++b) mbar_init(&s_bar[b], 1);
-        mbar_fence_init();
-      }
-      __syncwarp();
-#pragma unroll
-      for (int i = 0; i < NT - 1; ++i)
-        if (i < nsub)
-          issue_tile<TT>(s_tiles + i * buf_bytes, &s_bar[i], kc, vc, t0 + i * kSub, t1, pos, fused, kv_dim, kv_off, hd,
-                         hs, lane);
+    if (threadIdx.x == 0) {
+      for (int b = 0; b < NT; ++b) mbar_init(&s_bar[b], nt);
+      mbar_fence_init();
     }
+    __syncthreads();
+    for (int i = 0; i < bpr && i < nb; ++i)
+      issue_tile<TT>(s_tiles + (size_t)(i % NT) * buf_bytes, &s_bar[i % NT], kc, vc, (split + S * i) * kSub, n_pos,
+                     pos, fused, kv_dim, kv_off, hd, hs);
   }
-  if (fused && active && threadIdx.x < 12) {
+  if (fused && nb > 0 && threadIdx.x < 12 && !(J >= 2 && a.rope_cos && a.rope_sin)) {
     const uint8_t* line = nullptr;
     const int qb = a.q_norm_dtype == kF32 ? 4 : 2, kb = a.k_norm_dtype == kF32 ? 4 : 2;
     const int t = threadIdx.x;
@@ -369,324 +517,225 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(const AttnArgs a)
     }
     if (line) asm volatile("prefetch.global.L1 [%0];" ::"l"(line));
   }
+  // Prologue roles: warp g < G takes q row g; K/V of the current position
+  // (fused: normalised/rotated here; needed by split 0, which appends it,
+  // and by the CTA holding the current position's block) the next two
+  // warps.  With a RoPE table and head_dim 64/128/256 the norm and rotation
+  // run in registers, their weights and table row loaded before the wait.
+  const bool kv_cta = fused && (split == 0 || split == pos_cta);
+  const int kw = G < kAttnWarps ? G : 0, vw = G + 1 < kAttnWarps ? G + 1 : 1;
+  const bool has_q = nb > 0 && warp < G;
+  const bool has_kv = kv_cta && (warp == kw || warp == vw);
+  const bool reg_norm = J >= 2 && fused && a.rope_cos != nullptr && a.rope_sin != nullptr;
+  float wq[8], wk[8], cr[4], sr[4];
+  if (reg_norm) {
+    const int half = hd / 2;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int d = lane + 32 * k;
+      wq[k] = has_q && a.q_norm && d < hd ? load_weight(a.q_norm, a.q_norm_dtype, d) : 0.0f;
+      wk[k] = has_kv && warp == kw && a.k_norm && d < hd ? load_weight(a.k_norm, a.k_norm_dtype, d) : 0.0f;
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int d = lane + 32 * k;
+      const bool need = (has_q || (has_kv && warp == kw)) && d < half;
+      cr[k] = need ? a.rope_cos[(size_t)pos * half + d] : 0.0f;
+      sr[k] = need ? a.rope_sin[(size_t)pos * half + d] : 0.0f;
+    }
+  }
   pdl_wait();
   pdl_launch_dependents();
 
-  // Every global load of the prologue first: K/V of the current position
-  // (fused: normalised/rotated here; needed by split 0, which appends it,
-  // and by the split that holds position pos) on warps 0/1, and each warp's
-  // q rows of this kv head's group; then the stores and the norms.
-  const bool kv_split = fused && (split == 0 || split == n_active - 1) && warp < 2;
-  float kvr[8];
-  float qv[2][8];
-  if (kv_split) {
-    const float* src = (warp == 0 ? a.k : a.v) + (size_t)z * a.qkv_bstride + kv_off;
+  // every global load first, then the norms, then the stores
+  float qv[8], kvr[8];
+  if (has_q) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int d = lane + 32 * k;
+      qv[k] = d < hd ? qp[(size_t)(hb + warp) * hd + d] : 0.0f;
+    }
+  }
+  if (has_kv) {
+    const float* src = (warp == kw ? a.k : a.v) + (size_t)z * a.qkv_bstride + kv_off;
 #pragma unroll
     for (int k = 0; k < 8; ++k) kvr[k] = lane + 32 * k < hd ? src[lane + 32 * k] : 0.0f;
   }
-  if (active) {
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const int g = warp + i * kAttnWarps;
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int d = lane + 32 * k;
-        qv[i][k] = (g < G && d < hd) ? qp[(size_t)(hb + g) * hd + d] : 0.0f;
-      }
+  if constexpr (J >= 2) {
+    if (reg_norm) {
+      if (has_q) norm_rope_regs<J>(qv, wq, cr, sr, a.q_norm != nullptr, hd);
+      if (has_kv && warp == kw) norm_rope_regs<J>(kvr, wk, cr, sr, a.k_norm != nullptr, hd);
     }
   }
-  if (kv_split) {
-    float* dst = warp == 0 ? s_kpos : s_vpos;
+  if (has_q) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (lane + 32 * k < hd) s_q[warp * hd + lane + 32 * k] = qv[k];
+  }
+  if (has_kv) {
+    float* dst = warp == kw ? s_kpos : s_vpos;
 #pragma unroll
     for (int k = 0; k < 8; ++k)
       if (lane + 32 * k < hd) dst[lane + 32 * k] = kvr[k];
   }
-  if (active) {
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const int g = warp + i * kAttnWarps;
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int d = lane + 32 * k;
-        if (g < G && d < hd) s_q[g * hd + d] = qv[i][k];
-      }
-    }
-  }
   __syncwarp();
-  if (kv_split && warp == 0)
-    norm_rope_row(s_kpos, s_sq, hd, a.k_norm, a.k_norm_dtype, true, a.rope_cos, a.rope_sin, a.rope_base, a.rope_scale,
-                  pos, lane);
-  for (int g = warp; active && g < G; g += kAttnWarps) {
-    float* row = s_q + g * hd;
-    if (fused)
-      norm_rope_row(row, s_sq + warp * 256, hd, a.q_norm, a.q_norm_dtype, true, a.rope_cos, a.rope_sin, a.rope_base,
-                    a.rope_scale, pos, lane);
-  }
+  if (fused && !reg_norm && has_q)
+    norm_rope_row(s_q + warp * hd, s_sq + warp * 256, hd, a.q_norm, a.q_norm_dtype, true, a.rope_cos, a.rope_sin,
+                  a.rope_base, a.rope_scale, pos, lane);
+  if (!reg_norm && has_kv && warp == kw)
+    norm_rope_row(s_kpos, s_sq + warp * 256, hd, a.k_norm, a.k_norm_dtype, true, a.rope_cos, a.rope_sin, a.rope_base,
+                  a.rope_scale, pos, lane);
   __syncthreads();
   if (fused && split == 0) {
-    void* kw = const_cast<uint8_t*>(kc);
-    void* vw = const_cast<uint8_t*>(vc);
+    void* kwp = const_cast<uint8_t*>(kc);
+    void* vwp = const_cast<uint8_t*>(vc);
     for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-      kv_store<T>(kw, (size_t)pos * kv_dim + kv_off + d, s_kpos[d]);
-      kv_store<T>(vw, (size_t)pos * kv_dim + kv_off + d, s_vpos[d]);
+      kv_store<T>(kwp, (size_t)pos * kv_dim + kv_off + d, s_kpos[d]);
+      kv_store<T>(vwp, (size_t)pos * kv_dim + kv_off + d, s_vpos[d]);
     }
   }
 
-  if (active) {
-    // up to two heads per warp (G <= 8)
-    float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.0f, 0.0f}, acc[2][J];
-#pragma unroll
-    for (int i = 0; i < 2; ++i)
-#pragma unroll
-      for (int j = 0; j < J; ++j) acc[i][j] = 0.0f;
-    const bool act = lane * J < hd;
-    for (int i = 0; i < nsub; ++i) {
-      const int c0 = t0 + i * kSub;
-      uint8_t* buf = s_tiles + (size_t)(i % NT) * buf_bytes;
-      if constexpr (C::kAsync) {
-        // request the tile NT-1 ahead into the buffer the previous
-        // iteration finished with, then complete this one
-        if (warp == 0 && i + NT - 1 < nsub)
-          issue_tile<TT>(s_tiles + (size_t)((i + NT - 1) % NT) * buf_bytes, &s_bar[(i + NT - 1) % NT], kc, vc,
-                         c0 + (NT - 1) * kSub, t1, pos, fused, kv_dim, kv_off, hd, hs, lane);
-        put_pos_row<TT>(buf, s_kpos, s_vpos, c0, t1, pos, fused, hd, hs);
-        zero_rows<TT>(buf, c0, t1, hd, hs);
-        mbar_wait(&s_bar[i % NT], (uint32_t)(i / NT) & 1u, a.err);
-      } else {
-        float* kt = reinterpret_cast<float*>(buf);
-        stage_kv_tile<T>(kc, vc, s_kpos, s_vpos, kt, kt + (size_t)kSub * hs, c0, t1, pos, fused, kv_dim, kv_off, hd,
-                         hs, threadIdx.x, nt);
+  if constexpr (kCluster) asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+
+  // Rounds of bpr blocks; warp w takes (head w % G, block r*bpr + w / G).
+  const int nblk_max = attn_n_blocks(a.ctx);
+  const bool act = lane * J < hd;
+  for (int r = 0; r * bpr < nb; ++r) {
+    if constexpr (C::kAsync) {
+      // next round's tiles into the buffers the round before finished with
+      for (int j = 0; j < bpr; ++j) {
+        const int i = (r + 1) * bpr + j;
+        if (i < nb)
+          issue_tile<TT>(s_tiles + (size_t)(i % NT) * buf_bytes, &s_bar[i % NT], kc, vc, (split + S * i) * kSub, n_pos,
+                         pos, fused, kv_dim, kv_off, hd, hs);
       }
-      __syncthreads();
-      const TT* ktile = reinterpret_cast<const TT*>(buf);
+      for (int j = 0; j < bpr; ++j) {
+        const int i = r * bpr + j;
+        if (i >= nb) break;
+        uint8_t* buf = s_tiles + (size_t)(i % NT) * buf_bytes;
+        put_pos_row<TT>(buf, s_kpos, s_vpos, (split + S * i) * kSub, n_pos, pos, fused, hd, hs);
+        zero_rows<TT>(buf, (split + S * i) * kSub, n_pos, hd, hs);
+      }
+      for (int j = 0; j < bpr; ++j) {
+        const int i = r * bpr + j;
+        if (i >= nb) break;
+        mbar_wait(&s_bar[i % NT], (uint32_t)(i / NT) & 1u, a.err);
+      }
+    } else {
+      for (int j = 0; j < bpr; ++j) {
+        const int i = r * bpr + j;
+        if (i >= nb) break;
+        float* kt = reinterpret_cast<float*>(s_tiles + (size_t)(i % NT) * buf_bytes);
+        stage_kv_tile<T>(kc, vc, s_kpos, s_vpos, kt, kt + (size_t)kSub * hs, (split + S * i) * kSub, n_pos, pos, fused,
+                         kv_dim, kv_off, hd, hs, threadIdx.x, nt);
+      }
+    }
+    __syncthreads();
+    const int g = warp % G, j = warp / G, i = r * bpr + j;
+    if (j < bpr && i < nb) {
+      const int c = split + S * i;
+      const TT* ktile = reinterpret_cast<const TT*>(s_tiles + (size_t)(i % NT) * buf_bytes);
       const TT* vtile = ktile + (size_t)kSub * hs;
-      const int t = c0 + lane;
-      const bool valid = t < t1;
+      const bool valid = c * kSub + lane < n_pos;
+      float sc = score_row<TT>(s_q + g * hd, ktile + (size_t)lane * hs, hd, hs);
+      sc = valid ? __fmul_rn(sc, a.scale) : -INFINITY;
+      const float m = warp_max(sc);
+      const float p = valid ? expf_det(__fsub_rn(sc, m)) : 0.0f;
+      const float l = __shfl_sync(0xffffffffu, warp_sum(p), 0);
+      float acc[J];
 #pragma unroll
-      for (int hi = 0; hi < 2; ++hi) {
-        const int g = warp + hi * kAttnWarps;
-        if (g >= G) break;
-        float sc = score_row<TT>(s_q + g * hd, ktile + (size_t)lane * hs, hd, hs);
-        sc = valid ? __fmul_rn(sc, a.scale) : -INFINITY;
-        const float mx = warp_max(sc);
-        const float mn = fmaxf(m[hi], mx);
-        const float alpha = expf_det(__fsub_rn(m[hi], mn));
-        const float p = valid ? expf_det(__fsub_rn(sc, mn)) : 0.0f;
-        const float psum = __shfl_sync(0xffffffffu, warp_sum(p), 0);
-        l[hi] = __fadd_rn(__fmul_rn(l[hi], alpha), psum);
-        m[hi] = mn;
+      for (int jj = 0; jj < J; ++jj) acc[jj] = 0.0f;
+#pragma unroll 8
+      for (int tt = 0; tt < kSub; ++tt) {
+        const float pt = __shfl_sync(0xffffffffu, p, tt);
+        if (act) {
+          float vv[J];
+          load_v<J, TT>(vtile + (size_t)tt * hs + lane * J, vv);
 #pragma unroll
-        for (int j = 0; j < J; ++j) acc[hi][j] = __fmul_rn(acc[hi][j], alpha);
-        for (int tt = 0; tt < kSub; ++tt) {
-          const float pt = __shfl_sync(0xffffffffu, p, tt);
-          if (act) {
-            float vv[J];
-            load_v<J, TT>(vtile + (size_t)tt * hs + lane * J, vv);
-#pragma unroll
-            for (int j = 0; j < J; ++j) acc[hi][j] = __fmaf_rn(pt, vv[j], acc[hi][j]);
-          }
+          for (int jj = 0; jj < J; ++jj) acc[jj] = __fmaf_rn(pt, vv[jj], acc[jj]);
         }
       }
-      __syncthreads();
-    }
-    float* part_base = kCluster ? reinterpret_cast<float*>(s_tiles)
-                                : a.partial + ((size_t)z * a.n_head + hb) * a.n_split * stride_part;
+      if constexpr (kCluster) {
+        // into the merge row of block c at the CTA merging each unit: this
+        // lane's J values lie in unit g * hd/32 + lane*J/32; lane k < hd/32
+        // sends (m, l) for unit g * hd/32 + k
+        static_assert(!kCluster || J >= 2, "the cluster merge serves head_dim 64/128/256");
+        const int upw = hd / 32;
+        const int U = g * upw + (lane * J) / 32;
+        const uint32_t ra = dsmem_addr(s_merge + ((size_t)(U / S) * nblk_max + c) * kMergeRow + (lane * J) % 32, U % S);
+        if constexpr (J == 2) {
+          dsmem_st2(ra, acc[0], acc[1]);
+        } else {
 #pragma unroll
-    for (int hi = 0; hi < 2; ++hi) {
-      const int g = warp + hi * kAttnWarps;
-      if (g >= G) break;
-      float* dst = kCluster ? part_base + (size_t)g * stride_part
-                            : part_base + ((size_t)g * a.n_split + split) * stride_part;
-      if (act)
+          for (int jj = 0; jj < J; jj += 4) dsmem_st4(ra + 4 * jj, acc[jj], acc[jj + 1], acc[jj + 2], acc[jj + 3]);
+        }
+        if (lane < upw) {
+          const int U2 = g * upw + lane;
+          dsmem_st2(dsmem_addr(s_merge + ((size_t)(U2 / S) * nblk_max + c) * kMergeRow + 32, U2 % S), m, l);
+        }
+      } else {
+        float* dst = a.partial + (((size_t)z * a.n_head + hb + g) * nblk_max + c) * stride_part;
+        if (act)
 #pragma unroll
-        for (int j = 0; j < J; ++j) dst[4 + lane * J + j] = acc[hi][j];
-      if (lane == 0) {
-        dst[0] = m[hi];
-        dst[1] = l[hi];
+          for (int jj = 0; jj < J; ++jj) dst[4 + lane * J + jj] = acc[jj];
+        if (lane == 0) {
+          dst[0] = m;
+          dst[1] = l;
+        }
       }
     }
+    __syncthreads();
   }
 
+  // ---- merge over blocks in block order.  Unit u = 32 consecutive output
+  // values of this kv head's G heads, lane = value.
+  const int n_units = (G * hd + 31) / 32;
   if constexpr (kCluster) {
-    // Every split's partial rows are in its shared memory (tile area).  Unit
-    // u (32 consecutive output values of this kv head's G heads) is merged
-    // by warp (u / n_split) mod 4 of CTA u mod n_split, lane = value:
-    // M = max_s m_s, w_s = exp(m_s - M), L = sum_s w_s l_s and
-    // o = sum_s w_s acc_s (fma chains in split order), o * (1/L).
-    cluster_sync_all();
-    const int S = a.n_split;
-    const int n_units = (G * hd + 31) / 32;
-    const float* part_s = reinterpret_cast<const float*>(s_tiles);
-    for (int u = split + S * warp; u < n_units; u += S * kAttnWarps) {
+    cluster_sync_all();  // every merge row of this CTA's units has arrived
+    for (int slot = warp; split + slot * S < n_units; slot += kAttnWarps) {
+      const int u = split + slot * S;
+      const float* rows = s_merge + (size_t)slot * nblk_max * kMergeRow;
+      const float o = merge_blocks(
+          nblk, lane, [&](int c) { return rows[(size_t)c * kMergeRow + 32]; },
+          [&](int c) { return rows[(size_t)c * kMergeRow + 33]; },
+          [&](int c) { return rows[(size_t)c * kMergeRow + lane]; });
+      write_unit(o, u, lane, hb, hd, true, outp, oq8);
+    }
+  } else {
+    __shared__ unsigned ticket_s;
+    unsigned* counter = a.counters + (size_t)z * a.n_kv + kvh;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      unsigned t;
+      asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(t) : "l"(counter) : "memory");
+      ticket_s = t;
+    }
+    __syncthreads();
+    if (ticket_s != (unsigned)(S - 1)) return;
+    if (threadIdx.x == 0) atomicExch(counter, 0u);
+    const float* part = a.partial + ((size_t)z * a.n_head + hb) * nblk_max * stride_part;
+    for (int u = warp; u < n_units; u += kAttnWarps) {
       const int e = u * 32 + lane;
       const bool ve = e < G * hd;
       const int g = ve ? e / hd : 0, d = ve ? e - g * hd : 0;
-      const float* row = part_s + (size_t)g * stride_part;
-      float av[kAttnMaxCluster];
-#pragma unroll
-      for (int sp = 0; sp < kAttnMaxCluster; ++sp) av[sp] = sp < n_active ? dsmem_ld(dsmem_addr(row + 4 + d, sp)) : 0.0f;
-      float L = 0.0f, o = 0.0f;
-      if ((hd & 31) == 0) {
-        // one head per unit: lane sp holds split sp's (m, l) and weight
-        // w_sp = exp(m_sp - M); the sums run in split order via shuffles
-        const float* hrow = part_s + (size_t)(u * 32 / hd) * stride_part;
-        const float msp = lane < n_active ? dsmem_ld(dsmem_addr(hrow, lane)) : -INFINITY;
-        const float lsp = lane < n_active ? dsmem_ld(dsmem_addr(hrow + 1, lane)) : 0.0f;
-        const float M = warp_max(msp);
-        const float wsp = lane < n_active ? expf_det(__fsub_rn(msp, M)) : 0.0f;
-#pragma unroll
-        for (int sp = 0; sp < kAttnMaxCluster; ++sp) {
-          const float w = __shfl_sync(0xffffffffu, wsp, sp);
-          const float ls = __shfl_sync(0xffffffffu, lsp, sp);
-          if (sp < n_active) {
-            L = __fmaf_rn(w, ls, L);
-            o = __fmaf_rn(w, av[sp], o);
-          }
-        }
+      const float* hp = part + (size_t)g * nblk_max * stride_part;
+      float o;
+      if ((hd & 31) == 0) {  // one head per unit
+        o = merge_blocks(
+            nblk, lane, [&](int c) { return __ldcg(hp + (size_t)c * stride_part); },
+            [&](int c) { return __ldcg(hp + (size_t)c * stride_part + 1); },
+            [&](int c) { return __ldcg(hp + (size_t)c * stride_part + 4 + d); });
       } else {  // small heads: a unit spans several heads, each lane its own
-        float ms[kAttnMaxCluster], ls[kAttnMaxCluster];
-#pragma unroll
-        for (int sp = 0; sp < kAttnMaxCluster; ++sp) {
-          ms[sp] = sp < n_active ? dsmem_ld(dsmem_addr(row, sp)) : -INFINITY;
-          ls[sp] = sp < n_active ? dsmem_ld(dsmem_addr(row + 1, sp)) : 0.0f;
+        float M = -INFINITY, L = 0.0f, acc = 0.0f;
+        for (int c = 0; c < nblk; ++c) M = fmaxf(M, __ldcg(hp + (size_t)c * stride_part));
+        for (int c = 0; c < nblk; ++c) {
+          const float w = expf_det(__fsub_rn(__ldcg(hp + (size_t)c * stride_part), M));
+          L = __fmaf_rn(w, __ldcg(hp + (size_t)c * stride_part + 1), L);
+          acc = __fmaf_rn(w, __ldcg(hp + (size_t)c * stride_part + 4 + d), acc);
         }
-        float M = -INFINITY;
-#pragma unroll
-        for (int sp = 0; sp < kAttnMaxCluster; ++sp)
-          if (sp < n_active) M = fmaxf(M, ms[sp]);
-#pragma unroll
-        for (int sp = 0; sp < kAttnMaxCluster; ++sp) {
-          if (sp < n_active) {
-            const float w = expf_det(__fsub_rn(ms[sp], M));
-            L = __fmaf_rn(w, ls[sp], L);
-            o = __fmaf_rn(w, av[sp], o);
-          }
-        }
+        o = __fmul_rn(acc, L > 0.0f ? __fdiv_rn(1.0f, L) : 0.0f);
       }
-      o = __fmul_rn(o, L > 0.0f ? __fdiv_rn(1.0f, L) : 0.0f);
-      if (ve) outp[(size_t)hb * hd + e] = o;
-      if (oq8 && (hd % 32) == 0) {
-        uint16_t dbits;
-        bool zero;
-        const int q = q8_1_quant_lane(o, &dbits, &zero);
-        uint32_t word = ((uint32_t)(q & 0xff)) << (8 * (lane & 3));
-        word |= __shfl_xor_sync(0xffffffffu, word, 1);
-        word |= __shfl_xor_sync(0xffffffffu, word, 2);
-        float sum = 0.0f;  // the sequential f16 s of the reference block
-        for (int t = 0; t < 32; ++t) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, o, t));
-        uint32_t* ob = reinterpret_cast<uint32_t*>(oq8 + ((size_t)hb * hd / 32 + u) * 36);
-        if (lane == 0) ob[0] = (uint32_t)dbits | ((uint32_t)(zero ? (uint16_t)0 : f32_to_f16_ref(sum)) << 16);
-        if ((lane & 3) == 0) ob[1 + (lane >> 2)] = word;
-      }
-    }
-    cluster_sync_all();  // no CTA leaves while another still reads its partials
-    return;
-  }
-
-  // last CTA of this kv head merges the splits: the CTA barrier orders every
-  // thread's partial stores before thread 0's acquire-release ticket
-  __shared__ unsigned ticket_s;
-  unsigned* counter = a.counters + (size_t)z * a.n_kv + kvh;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    unsigned t;
-    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(t) : "l"(counter) : "memory");
-    ticket_s = t;
-  }
-  __syncthreads();
-  if (ticket_s != (unsigned)(a.n_split - 1)) return;
-  if (threadIdx.x == 0) atomicExch(counter, 0u);
-  // Merge: (1) m and l of all (head, split) pairs -- with every split's
-  // partial row copied into shared memory in one round trip when they fit
-  // (L2-only async copies); (2) per head M = max m, w_s = exp(m_s - M) and
-  // L = sum_s w_s l_s (fma in split order); (3) o_d = sum_s w_s acc_sd (fma in
-  // split order) * (1/L) by one thread per (head, d); (4) Q8_1 blocks of the
-  // output, one warp per block.
-  const float* part_g = a.partial + ((size_t)z * a.n_head + hb) * a.n_split * stride_part;
-  float* cm = reinterpret_cast<float*>(s_tiles);
-  float* cl = cm + kGMax * kMaxSplit;
-  float* cw = cl + kGMax * kMaxSplit;
-  float* cinv = cw + kGMax * kMaxSplit;
-  float* mp = reinterpret_cast<float*>(s_tiles + attn_merge_stage_offset());
-  const bool staged = (size_t)G * n_active * stride_part <= (size_t)kMergeStage;
-  if (staged) {
-    const int per = stride_part / 4;  // 16-byte pieces per partial row
-    for (int i = threadIdx.x; i < G * n_active * per; i += nt) {
-      const int row = i / per, c = i - row * per;
-      const int g = row / n_active, sp = row - g * n_active;
-      cp_async16(mp + (size_t)row * stride_part + c * 4, part_g + ((size_t)g * a.n_split + sp) * stride_part + c * 4);
-    }
-    cp_async_commit();
-    cp_async_wait<0>();
-    __syncthreads();
-    for (int i = threadIdx.x; i < G * n_active; i += nt) {
-      const int g = i / n_active, sp = i - g * n_active;
-      cm[g * kMaxSplit + sp] = mp[(size_t)i * stride_part];
-      cl[g * kMaxSplit + sp] = mp[(size_t)i * stride_part + 1];
-    }
-  } else {
-    for (int i = threadIdx.x; i < G * n_active; i += nt) {
-      const int g = i / n_active, sp = i - g * n_active;
-      const float* ps = part_g + ((size_t)g * a.n_split + sp) * stride_part;
-      cm[g * kMaxSplit + sp] = __ldcg(ps);
-      cl[g * kMaxSplit + sp] = __ldcg(ps + 1);
-    }
-  }
-  __syncthreads();
-  for (int g = warp; g < G; g += kAttnWarps) {
-    const float* mg = cm + g * kMaxSplit;
-    float M = -INFINITY;
-    for (int sp = lane; sp < n_active; sp += 32) M = fmaxf(M, mg[sp]);
-    M = warp_max(M);
-    for (int sp = lane; sp < n_active; sp += 32) cw[g * kMaxSplit + sp] = expf_det(__fsub_rn(mg[sp], M));
-    __syncwarp();
-    if (lane == 0) {
-      float L = 0.0f;
-      for (int sp = 0; sp < n_active; ++sp) L = __fmaf_rn(cw[g * kMaxSplit + sp], cl[g * kMaxSplit + sp], L);
-      cinv[g] = L > 0.0f ? __fdiv_rn(1.0f, L) : 0.0f;
-    }
-  }
-  __syncthreads();
-  constexpr int kLd = 16;
-  for (int i = threadIdx.x; i < G * hd; i += nt) {
-    const int g = i / hd, d = i - g * hd;
-    const float* wg = cw + g * kMaxSplit;
-    float o = 0.0f;
-    if (staged) {
-      const float* pg = mp + (size_t)g * n_active * stride_part + 4 + d;
-      for (int sp = 0; sp < n_active; ++sp) o = __fmaf_rn(wg[sp], pg[(size_t)sp * stride_part], o);
-    } else {
-      const float* pg = part_g + (size_t)g * a.n_split * stride_part + 4 + d;
-      for (int s0 = 0; s0 < n_active; s0 += kLd) {
-        float r[kLd];
-#pragma unroll
-        for (int u = 0; u < kLd; ++u) r[u] = s0 + u < n_active ? __ldcg(pg + (size_t)(s0 + u) * stride_part) : 0.0f;
-#pragma unroll
-        for (int u = 0; u < kLd; ++u)
-          if (s0 + u < n_active) o = __fmaf_rn(wg[s0 + u], r[u], o);
-      }
-    }
-    o = __fmul_rn(o, cinv[g]);
-    outp[(size_t)(hb + g) * hd + d] = o;
-    s_q[i] = o;
-  }
-  if (oq8 && (hd % 32) == 0) {
-    __syncthreads();
-    for (int b = warp; b < G * hd / 32; b += kAttnWarps) {
-      const float o = s_q[b * 32 + lane];
-      uint16_t dbits;
-      bool zero;
-      const int q = q8_1_quant_lane(o, &dbits, &zero);
-      uint32_t word = ((uint32_t)(q & 0xff)) << (8 * (lane & 3));
-      word |= __shfl_xor_sync(0xffffffffu, word, 1);
-      word |= __shfl_xor_sync(0xffffffffu, word, 2);
-      uint32_t* ob = reinterpret_cast<uint32_t*>(oq8 + ((size_t)hb * hd + (size_t)b * 32) / 32 * 36);
-      if (lane == 0) {
-        float sum = 0.0f;  // the sequential f16 s of the reference block
-        for (int t = 0; t < 32; ++t) sum = __fadd_rn(sum, s_q[b * 32 + t]);
-        ob[0] = (uint32_t)dbits | ((uint32_t)(zero ? (uint16_t)0 : f32_to_f16_ref(sum)) << 16);
-      }
-      if ((lane & 3) == 0) ob[1 + (lane >> 2)] = word;
+      write_unit(o, u, lane, hb, hd, ve, outp, oq8);
     }
   }
 }
@@ -714,8 +763,9 @@ cudaError_t launch_cluster(Kern kernel, dim3 grid, int cluster_y, size_t smem, c
 }
 
 // Whether clusters of n CTAs of a kernel can be resident, queried once at
-// set-up per device; the cluster merge is launched only where they can
-// (otherwise the global-memory merge, with the same bits, is used).
+// set-up per device (with the largest cluster-path shared memory); the
+// cluster merge is launched only where they can (otherwise the
+// global-memory merge, with the same bits, is used).
 constexpr int kMaxDevices = 64;
 bool g_cluster_ok[kMaxDevices][2][4][kAttnMaxCluster + 1];  // [device][f16][J index][cluster size]
 
@@ -747,21 +797,28 @@ bool query_cluster(Kern kernel, size_t smem, int n) {
 }
 
 constexpr int j_index(int J) { return J == 1 ? 0 : J == 2 ? 1 : J == 4 ? 2 : 3; }
+// dynamic shared memory the cluster kernels are set up for (the sm_100
+// opt-in maximum per CTA, 232448 bytes, less a margin for static data)
+constexpr int kDynSmemMax = 232448 - 256;
 
 template <int J, typename T>
 cudaError_t init_jt(int dev) {
-  const size_t mx = attn_smem_bytes_t<J, T, false>(32 * J);
-  const size_t mc = attn_smem_bytes_t<J, T, true>(32 * J);
+  const size_t mx = attn_smem_bytes_t<J, T>(32 * J, TileCfg<J, T>::kRing, 0);  // a full ring
   cudaError_t e = cudaFuncSetAttribute(k_attention<J, T, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mx);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(k_attention<J, T, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mc);
   if (e != cudaSuccess) return e;
-  const bool nonportable =
-      cudaFuncSetAttribute(k_attention<J, T, true>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess;
-  if (!nonportable) (void)cudaGetLastError();
-  for (int n = 1; n <= kAttnMaxCluster; ++n)
-    g_cluster_ok[dev][sizeof(T) == 2][j_index(J)][n] =
-        (n <= 8 || nonportable) && query_cluster(k_attention<J, T, true>, mc, n);
+  if constexpr (J >= 2) {
+    e = cudaFuncSetAttribute(k_attention<J, T, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kDynSmemMax);
+    if (e != cudaSuccess) return e;
+    const bool nonportable =
+        cudaFuncSetAttribute(k_attention<J, T, true>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==
+        cudaSuccess;
+    if (!nonportable) (void)cudaGetLastError();
+    // queried at the largest shared memory (one CTA per SM): a cluster that
+    // is resident then is resident with any smaller carve-up
+    for (int n = 1; n <= kAttnMaxCluster; ++n)
+      g_cluster_ok[dev][sizeof(T) == 2][j_index(J)][n] =
+          (n <= 8 || nonportable) && query_cluster(k_attention<J, T, true>, kDynSmemMax, n);
+  }
   return cudaSuccess;
 }
 
@@ -770,20 +827,26 @@ cudaError_t launch_j(const AttnArgs& a, cudaStream_t st, bool pdl) {
   const int hd = a.head_dim;
   const dim3 grid(a.n_kv, a.n_split, a.batch > 0 ? a.batch : 1);
   const bool f16 = a.kv_f16 != 0;
-  const int dev = a.cluster ? current_device() : -1;
-  if (dev >= 0 && g_cluster_ok[dev][f16][j_index(J)][a.n_split]) {
-    if (f16)
-      return launch_cluster(k_attention<J, __half, true>, grid, a.n_split, attn_smem_bytes_t<J, __half, true>(hd), st,
-                            pdl, a);
-    return launch_cluster(k_attention<J, float, true>, grid, a.n_split, attn_smem_bytes_t<J, float, true>(hd), st, pdl,
-                          a);
+  auto bytes = [&](auto t, bool cl) {
+    using TE = decltype(t);
+    const AttnLayout l = attn_layout<J, TE>(hd, a.n_head, a.n_kv, a.ctx, a.n_split, cl);
+    return attn_smem_bytes_t<J, TE>(hd, l.ring, l.merge_rows);
+  };
+  if constexpr (J >= 2) {
+    const int nb_cta = (attn_n_blocks(a.ctx) + a.n_split - 1) / a.n_split;
+    const int dev = a.cluster ? current_device() : -1;
+    if (dev >= 0 && nb_cta <= kAttnMaxBlocksCta && g_cluster_ok[dev][f16][j_index(J)][a.n_split]) {
+      const size_t b = f16 ? bytes(__half(), true) : bytes(0.0f, true);
+      if (b <= (size_t)kDynSmemMax) {
+        if (f16) return launch_cluster(k_attention<J, __half, true>, grid, a.n_split, b, st, pdl, a);
+        return launch_cluster(k_attention<J, float, true>, grid, a.n_split, b, st, pdl, a);
+      }
+    }
   }
   if (!a.partial || !a.counters) return cudaErrorInvalidValue;
   if (f16)
-    return launch_k(k_attention<J, __half, false>, grid, dim3(kAttnWarps * 32), attn_smem_bytes_t<J, __half, false>(hd),
-                    st, pdl, a);
-  return launch_k(k_attention<J, float, false>, grid, dim3(kAttnWarps * 32), attn_smem_bytes_t<J, float, false>(hd), st,
-                  pdl, a);
+    return launch_k(k_attention<J, __half, false>, grid, dim3(kAttnWarps * 32), bytes(__half(), false), st, pdl, a);
+  return launch_k(k_attention<J, float, false>, grid, dim3(kAttnWarps * 32), bytes(0.0f, false), st, pdl, a);
 }
 
 template <int J>
@@ -795,8 +858,8 @@ cudaError_t init_j(int dev) {
 
 }  // namespace
 
-size_t attn_partial_floats(int n_head, int n_split, int head_dim) {
-  return (size_t)n_head * n_split * attn_part_stride(head_dim);
+size_t attn_partial_floats(int n_head, int n_blocks, int head_dim) {
+  return (size_t)n_head * n_blocks * attn_part_stride(head_dim);
 }
 
 cudaError_t attention_init() {
@@ -812,7 +875,7 @@ cudaError_t attention_init() {
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st, bool pdl) {
   if (a.n_split > kMaxSplit || a.n_split < 1) return cudaErrorInvalidValue;
   if (a.cluster && a.n_split > kAttnMaxCluster) return cudaErrorInvalidValue;
-  if (a.n_head > kGMax * a.n_kv) return cudaErrorInvalidValue;
+  if (a.n_kv < 1 || a.n_head < a.n_kv || a.n_head > kGMax * a.n_kv || a.ctx < 1 || attn_n_blocks(a.ctx) > kMaxBlocks) return cudaErrorInvalidValue;
   switch (a.head_dim) {
     case 64: return launch_j<2>(a, st, pdl);
     case 128: return launch_j<4>(a, st, pdl);

@@ -25,15 +25,16 @@ struct AttnArgs {
   const int* pos_ptr;  // device position (graph replay) or null
   int pos_static;
   int n_head, n_kv, head_dim, ctx;
-  int n_split;
-  // 1: the splits of a kv head form one thread-block cluster and merge
-  // through distributed shared memory (n_split <= kAttnMaxCluster; partial
-  // and counters unused); 0: split-K partials in global memory, merged by
-  // the last-arriving CTA.  Same arithmetic, same bits.
+  int n_split;  // CTAs per kv head (and sequence); CTA s takes blocks s, s + n_split, ...
+  // 1: the CTAs of a kv head form one thread-block cluster and merge through
+  // distributed shared memory (n_split <= kAttnMaxCluster, at most
+  // kAttnMaxBlocksCta blocks per CTA; partial and counters unused); 0:
+  // block partials in global memory, merged by the last-arriving CTA.  Same
+  // arithmetic, same bits.
   int cluster;
   float scale;
   // scratch
-  float* partial;      // [batch][n_head][n_split][attn_part_stride(head_dim)]: m, l, 2 pad, acc[head_dim]
+  float* partial;      // [batch][n_head][attn_n_blocks(ctx)][attn_part_stride(head_dim)]: m, l, 2 pad, acc[head_dim]
   unsigned* counters;  // [batch][n_kv], zero at rest
   // outputs
   float* out;          // [n_head*head_dim]
@@ -49,12 +50,15 @@ struct AttnArgs {
   int* err;        // raised by a bounded wait that gave up (may be null)
 };
 
-constexpr int kAttnMaxCluster = 16;  // cluster size (beyond 8 needs the non-portable opt-in)
+constexpr int kAttnMaxCluster = 16;    // cluster size (beyond 8 needs the non-portable opt-in)
+constexpr int kAttnMaxBlocksCta = 8;   // cluster path: blocks per CTA (partials kept in shared memory)
 
-// Floats per (head, split) partial: m, l, two pad floats, then head_dim
+// Positions are attended in blocks of 32 (lane = position).
+__host__ __device__ inline int attn_n_blocks(int ctx) { return (ctx + 31) / 32; }
+// Floats per (head, block) partial: m, l, two pad floats, then head_dim
 // accumulators (rows stay 16-byte aligned for bulk copies).
 __host__ __device__ inline int attn_part_stride(int head_dim) { return head_dim + 4; }
-size_t attn_partial_floats(int n_head, int n_split, int head_dim);
+size_t attn_partial_floats(int n_head, int n_blocks, int head_dim);
 // One-time per-device setup (opts the kernels into their shared memory).
 cudaError_t attention_init();
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st, bool pdl = false);

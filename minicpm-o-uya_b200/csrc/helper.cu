@@ -356,7 +356,7 @@ bool check_dev_err(Ctx* c, char* err, size_t cap) {
     return false;
   if (v == 0) return true;
   cudaMemsetAsync(c->dev_err, 0, sizeof(int), c->stream);
-  fail(c, err, cap, "error: a device-side wait gave up (pipeline stalled)");
+  fail(c, err, cap, "error: a device-side check failed (a bounded wait gave up, or a position outside the cache)");
   return false;
 }
 
@@ -408,7 +408,8 @@ bool ensure_xq(Ctx* c, size_t cols, char* err, size_t cap) {
 int run_attention(Ctx* c, const float* q, float* dst, size_t layer, size_t pos, size_t n_head, size_t n_kv, size_t hd,
                   char* err, size_t cap) {
   const int n_split = attn_n_split((int)n_kv);
-  if (!ensure(c, &c->attn_partial, &c->attn_partial_bytes, attn_partial_floats((int)n_head, n_split, (int)hd) * 4,
+  if (!ensure(c, &c->attn_partial, &c->attn_partial_bytes,
+              attn_partial_floats((int)n_head, attn_n_blocks((int)c->kv_ctx), (int)hd) * 4,
               "attention_partial_malloc", err, cap))
     return 0;
   if (c->attn_counters_bytes < n_kv * 4) {
@@ -523,6 +524,21 @@ int attn_cluster_cfg() {
     return (e && *e) ? (atoi(e) != 0 ? 1 : 0) : 1;
   }();
   return v;
+}
+
+// CTAs per kv head and sequence of the batched attention: about eight CTAs
+// per SM over the whole batch (B = 32, 8 kv heads: 4), at most the
+// single-sequence count; MCPO_ATTN_BATCH_SPLIT overrides.  The batched
+// attention merges through global memory (16-CTA clusters of many
+// sequences schedule poorly).
+int attn_batch_split_cfg(int single, int batch, int n_kv, int sms) {
+  static const int v = [] {
+    const char* e = getenv("MCPO_ATTN_BATCH_SPLIT");
+    return (e && *e) ? atoi(e) : 0;
+  }();
+  if (v >= 1 && v <= kAttnMaxCluster) return v;
+  const int per = batch * n_kv > 0 ? 8 * sms / (batch * n_kv) : single;
+  return per < 1 ? 1 : (per < single ? per : single);
 }
 
 bool groupable(Upload* const* u, int n) {
@@ -744,8 +760,8 @@ cudaError_t record_batch_step(Ctx* c, Model& m, bool logits) {
     a.n_kv = (int)cf.kv_heads;
     a.head_dim = hd;
     a.ctx = (int)cf.context;
-    a.n_split = m.n_split;
-    a.cluster = attn_cluster_cfg();
+    a.n_split = attn_batch_split_cfg(m.n_split, B, (int)cf.kv_heads, c->sm_count);
+    a.cluster = 0;
     a.scale = 1.0f / sqrtf((float)hd);
     a.partial = b.attn_partial;
     a.counters = b.attn_counters;
@@ -857,7 +873,7 @@ int bind_batch(Ctx* c, Model& m, char* err, size_t cap) {
       {(void**)&b.cnt, tiles_max * 4 + 4},
       {&b.kc, kv_bytes},
       {&b.vc, kv_bytes},
-      {(void**)&b.attn_partial, (size_t)B * attn_partial_floats((int)cf.heads, m.n_split, (int)hd) * 4},
+      {(void**)&b.attn_partial, (size_t)B * attn_partial_floats((int)cf.heads, attn_n_blocks((int)cf.context), (int)hd) * 4},
       {(void**)&b.attn_counters, (size_t)B * cf.kv_heads * 4},
       {(void**)&b.st, B * sizeof(StepState)},
       {(void**)&b.am_scratch, (size_t)B * b.am_grid * 3 * 4},
@@ -911,7 +927,7 @@ int run_batch(Ctx* c, Model& m, const uint32_t* tokens, const uint32_t* pos, int
                  "batch_state_d2h", err, cap);
   if (ok) ok = cuda_ok(c, cudaStreamSynchronize(c->stream), "batch_sync", err, cap);
   for (int i = 0; ok && i < b.B; ++i)
-    if (b.st_host[i].err) ok = fail(c, err, cap, "error: qwen3 batch: a bounded device wait gave up (step aborted)");
+    if (b.st_host[i].err) ok = fail(c, err, cap, "error: qwen3 batch: a device-side check failed (a bounded wait gave up, or a position outside the cache)");
   if (ok && total_ms) cudaEventElapsedTime(total_ms, e0, e1);
   if (e0) cudaEventDestroy(e0);
   if (e1) cudaEventDestroy(e1);
@@ -928,7 +944,9 @@ int run_batch(Ctx* c, Model& m, const uint32_t* tokens, const uint32_t* pos, int
 bool build_step_plan(Ctx* c, Model& m) {
   const auto& cf = m.cfg;
   const int h = (int)cf.hidden, hd = (int)cf.head_dim;
-  if (cf.heads % cf.kv_heads || cf.heads / cf.kv_heads > 8 || m.n_split > 64) return false;
+  // the stage attends in blocks of 32 positions (one split per block, as
+  // k_attention): at most 64 blocks, a 2048-position context
+  if (cf.heads % cf.kv_heads || cf.heads / cf.kv_heads > 8 || attn_n_blocks((int)cf.context) > 64) return false;
   if (!(hd == 64 || hd == 128 || hd == 256 || (hd <= 32 && hd % 4 == 0))) return false;
   int coop = 0;
   if (cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, c->device) != cudaSuccess || !coop) return false;
@@ -984,7 +1002,7 @@ bool build_step_plan(Ctx* c, Model& m) {
     at.n_kv = (int)cf.kv_heads;
     at.head_dim = hd;
     at.ctx = (int)cf.context;
-    at.n_split = m.n_split;
+    at.n_split = attn_n_blocks((int)cf.context);
     at.scale = 1.0f / sqrtf((float)hd);
     at.partial = m.partial;
     at.counters = m.step_scratch + 4;
@@ -1312,7 +1330,7 @@ int bind_model(Ctx* c, const minicpmo_qwen3_config* cfg, char* err, size_t cap, 
       {(void**)&m.aq, (m.qd / 32 + 1) * 36}, {(void**)&m.fq, (f / 32 + 1) * 36},
       {&m.kc, cf.layers * m.kv_layer_elems * esz}, {&m.vc, cf.layers * m.kv_layer_elems * esz},
       {(void**)&m.rope_cos, (size_t)cf.context * (hd / 2) * 4}, {(void**)&m.rope_sin, (size_t)cf.context * (hd / 2) * 4},
-      {(void**)&m.partial, attn_partial_floats((int)lc.heads, m.n_split, (int)hd) * 4},
+      {(void**)&m.partial, attn_partial_floats((int)lc.heads, attn_n_blocks((int)cf.context), (int)hd) * 4},
       {(void**)&m.counters, lc.kv_heads * 4}, {(void**)&m.am_scratch, (size_t)m.am_grid * 3 * 4},
       {(void**)&m.am_counter, 4}, {(void**)&m.st, sizeof(StepState)}, {(void**)&m.seen, (Vg / 32 + 1) * 4},
       {(void**)&m.history, (size_t)m.history_cap * 4},
@@ -2094,7 +2112,7 @@ int minicpmo_gpu_context_qwen3_forward(void* handle, uint32_t token, size_t pos,
     c->stats.device_to_host_bytes += (size_t)m.cfg.hidden * 4;
   }
   if (!cuda_ok(c, cudaStreamSynchronize(c->stream), "forward_sync", error, error_cap)) return 0;
-  if (hs->err) return fail(c, error, error_cap, "error: qwen3 forward: a bounded device wait gave up (step aborted)");
+  if (hs->err) return fail(c, error, error_cap, "error: qwen3 forward: a device-side check failed (a bounded wait gave up, or a position outside the cache)");
   c->stats.attention_kernel_calls += m.cfg.layers;
   if (out_token) *out_token = which == 0 ? (uint32_t)hs->next_token : 0u;
   if (out_top2_gap) *out_top2_gap = which == 0 ? hs->gap : 0.0f;
@@ -2150,7 +2168,7 @@ int decode_loop(Ctx* c, uint32_t first_token, size_t first_pos, size_t n_steps, 
   if (ok) ok = cuda_ok(c, cudaMemcpyAsync(hs, m.st, sizeof(StepState), cudaMemcpyDeviceToHost, c->stream),
                        "decode_state_d2h", error, error_cap);
   if (ok) ok = cuda_ok(c, cudaStreamSynchronize(c->stream), "decode_sync", error, error_cap);
-  if (ok && hs->err) ok = fail(c, error, error_cap, "error: qwen3 decode: a bounded device wait gave up (step aborted)");
+  if (ok && hs->err) ok = fail(c, error, error_cap, "error: qwen3 decode: a device-side check failed (a bounded wait gave up, or a position outside the cache)");
   if (ok && total_ms) cudaEventElapsedTime(total_ms, e0, e1);
   if (e0) cudaEventDestroy(e0);
   if (e1) cudaEventDestroy(e1);

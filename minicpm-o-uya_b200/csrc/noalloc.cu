@@ -92,11 +92,13 @@ extern "C" int minicpmo_gpu_attention_no_alloc(const float* q, const void* k_cac
     return put_error(error, error_cap, "error: no_alloc attention: %zu kv heads exceed the limit of %d", kv_head_count,
                      MINICPMO_NOALLOC_MAX_KV_HEADS);
   const int n_split = attn_n_split((int)kv_head_count);
-  const size_t need = attn_partial_floats((int)head_count, n_split, (int)head_dim) * 4;
+  const int n_blocks = attn_n_blocks((int)context_capacity);
+  const size_t need = attn_partial_floats((int)head_count, n_blocks, (int)head_dim) * 4;
   if (need > kPartialBytes)
     return put_error(error, error_cap,
-                     "error: no_alloc attention: needs %zu scratch bytes (%zu heads x %d splits x %zu), limit %zu", need,
-                     head_count, n_split, (size_t)attn_part_stride((int)head_dim), kPartialBytes);
+                     "error: no_alloc attention: needs %zu scratch bytes (%zu heads x %d blocks of 32 positions x %zu), "
+                     "limit %zu",
+                     need, head_count, n_blocks, (size_t)attn_part_stride((int)head_dim) * 4, kPartialBytes);
 
   if (((uintptr_t)k_cache | (uintptr_t)v_cache) & 15)
     return put_error(error, error_cap, "error: no_alloc attention: K/V caches must be 16-byte aligned");

@@ -754,17 +754,17 @@ int orc_attention_dev(float *out, const float *q, const float *k_cache, const fl
                       const float *cur_v, size_t layer, size_t pos, size_t head_count, size_t kv_head_count,
                       size_t head_dim, size_t context) {
     const size_t hd = head_dim, kv_dim = kv_head_count * hd;
-    const int n_split = orc_attn_n_split((int) kv_head_count);
     const float scale = 1.0f / sqrtf((float) hd);
     const size_t n_pos = pos + 1;
-    size_t chunk = (n_pos + (size_t) n_split - 1) / (size_t) n_split;
+    /* blocks of 32 positions, each a partial (m, l, acc) of its own, merged
+     * in block order */
+    const size_t chunk = 32;
     size_t n_active, kvh;
     float *pm, *pl, *pacc, *acc;
     if (!(hd == 64 || hd == 128 || hd == 256 || hd <= 32)) return 0;
-    if (chunk < 32) chunk = 32;
     n_active = (n_pos + chunk - 1) / chunk;
     pm = (float *) malloc(n_active * sizeof(float));
-    pl = (float *) malloc(n_active * sizeof(float));
+    pl = (float *) malloc(2 * n_active * sizeof(float)); /* l, then the merge weights */
     pacc = (float *) malloc(n_active * hd * sizeof(float));
     acc = (float *) malloc(hd * sizeof(float));
     if (!pm || !pl || !pacc || !acc) { free(pm); free(pl); free(pacc); free(acc); return 0; }
@@ -818,7 +818,7 @@ int orc_attention_dev(float *out, const float *q, const float *k_cache, const fl
                 memcpy(pacc + s * hd, acc, hd * sizeof(float));
             }
             {
-                float M = -INFINITY, L = 0.0f, inv, w[64];
+                float M = -INFINITY, L = 0.0f, inv, *w = pl + n_active;
                 for (s = 0; s < n_active; ++s) M = fmaxf(M, pm[s]);
                 for (s = 0; s < n_active; ++s) w[s] = orc_expf_det(pm[s] - M);
                 for (s = 0; s < n_active; ++s) L = fmaf(w[s], pl[s], L);

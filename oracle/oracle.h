@@ -89,9 +89,9 @@ uint32_t orc_argmax_penalized(const float *values, size_t n, const uint32_t *see
  *  - matvec: per row, LPR lanes (largest power of two <= 32 dividing
  *    cols/256); lane l sums super-blocks l, l+LPR, ... in order; the lanes
  *    are combined by an xor butterfly (LPR/2 .. 1) and lane 0 is the row;
- *  - attention: split-K over attn_n_split(n_kv) position chunks of
- *    max(32, ceil((pos+1)/splits)) positions, 4 interleaved warps per chunk,
- *    online softmax per warp, merged warp by warp then split by split;
+ *  - attention: positions in blocks of 32; per block and head a partial
+ *    (m = max score, l = butterfly sum of exp(s - m), acc = sum p v in
+ *    position order), the blocks merged in block order;
  *  - exp: orc_expf_det (Cody-Waite reduction + degree-7 Taylor/Horner).
  */
 float orc_expf_det(float x);

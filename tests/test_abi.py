@@ -61,8 +61,8 @@ def test_no_alloc_attention_limits_are_checked_on_the_host(pkg):
     fn = lib.minicpmo_gpu_attention_no_alloc
     fn.argtypes = [C.c_void_p] * 3 + [C.c_int] + [C.c_size_t] * 5 + [C.c_void_p] * 2 + [C.c_char_p, C.c_size_t]
     p = C.cast(buf, C.c_void_p)
-    # 1024 heads / 128 kv heads / head_dim 256 -> 2 splits x 258 floats x 1024 heads = 2113536 B > 2 MiB
-    assert fn(p, p, p, 0, 0, 1024, 128, 256, 1, p, None, err, 512) == 0
+    # 32 heads, head_dim 128, a 4096-position cache -> 128 blocks x 132 floats x 32 heads = 2162688 B > 2 MiB
+    assert fn(p, p, p, 0, 0, 32, 8, 128, 4096, p, None, err, 512) == 0
     assert b"scratch bytes" in err.value and b"2097152" in err.value
     assert fn(p, p, p, 0, 0, 2048, 2048, 64, 1, p, None, err, 512) == 0
     assert b"kv heads exceed" in err.value
