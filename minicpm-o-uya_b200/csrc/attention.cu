@@ -17,11 +17,12 @@
 // B200 design: grid = (n_kv, n_split, batch); the n_split CTAs of a kv head
 // take its blocks round-robin, and inside a CTA eight warps work on (head,
 // block) pairs side by side, so a 600-position context is one round of
-// work.  K/V rows reach shared memory in the cache's own type by 16-byte
-// asynchronous copies from every thread (L2 only), a ring of 32-position
-// tiles whose mbarriers count the copies' arrivals; the first round's tiles
-// are requested before the kernel waits for its predecessor (programmatic
-// dependent launch).  The block partials merge either inside a thread-block
+// work.  K/V tiles reach shared memory in the cache's own type by 2-D TMA
+// tensor copies issued by one thread (a layer's cache is a [rows][kv_dim]
+// tensor map, boxes of 32 positions x 128 bytes in the 128-byte swizzle), a
+// ring of 32-position tiles on mbarriers; the first round's tiles are
+// requested before the kernel waits for its predecessor (programmatic
+// dependent launch), and no other thread spends issue slots on copies.  The block partials merge either inside a thread-block
 // cluster -- each warp stores its block's values straight into the shared
 // memory of the CTA that merges each 32-value output unit, so the merge
 // reads only local shared memory (the default of the single-sequence
@@ -38,6 +39,7 @@
 // The current position is attended as the cache stores it (f16: rounded).
 #include "attention.cuh"
 
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <math.h>
 #include <string.h>
@@ -60,20 +62,24 @@ constexpr int kMaxSplit = 64;
 constexpr int kMaxBlocks = 4096;  // blocks per sequence (131072 positions)
 
 // Small odd head sizes (J = 1, head_dim <= 32) stage f32 tiles through
-// registers with this row stride; the async tiles use head_dim + 16 bytes.
+// registers with this row stride.
 __host__ __device__ inline int attn_tile_stride(int hd) { return (hd & 3) ? hd + 1 : hd + 4; }
 
 // Tile geometry of one instantiation.  J >= 2 (head_dim 64/128/256): tiles
-// in the cache type TT, rows of head_dim + 16 bytes (16-byte aligned, and
-// lanes reading rows lane*stride hit distinct banks per quarter warp), a
-// ring of kRing tiles.  J = 1: one f32 tile staged through registers.
+// in the cache type TT brought in by TMA tensor copies, each 32-position K
+// (or V) tile head_dim*sizeof(TT)/128 boxes of 32 rows x 128 bytes in the
+// 128-byte swizzle (16-byte chunk c of row r stored at chunk c ^ (r & 7),
+// so lanes reading rows lane hit distinct banks per quarter warp), a ring
+// of kRing tiles.  J = 1: one f32 tile staged through registers.
 template <int J, typename T>
 struct TileCfg {
   static constexpr bool kAsync = J >= 2;
   using TT = std::conditional_t<kAsync, T, float>;
   static constexpr int kRing = (kAsync && (sizeof(T) == 2 || J < 8)) ? 4 : 2;
-  __host__ __device__ static int stride(int hd) { return kAsync ? hd + 16 / (int)sizeof(TT) : attn_tile_stride(hd); }
-  __host__ __device__ static size_t buf_bytes(int hd) { return 2 * (size_t)kSub * stride(hd) * sizeof(TT); }
+  __host__ __device__ static int stride(int hd) { return attn_tile_stride(hd); }  // J = 1
+  __host__ __device__ static size_t buf_bytes(int hd) {
+    return kAsync ? 2 * (size_t)kSub * hd * sizeof(TT) : 2 * (size_t)kSub * attn_tile_stride(hd) * sizeof(float);
+  }
 };
 
 __host__ __device__ inline size_t round16(size_t b) { return (b + 15) & ~(size_t)15; }
@@ -105,8 +111,8 @@ constexpr int kMergeRow = 36;
 // [kAttnWarps][256] (f32), `ring` tile buffers, the cluster path's merge
 // rows [slots][attn_n_blocks(ctx)][kMergeRow] (f32), one mbarrier per tile
 // buffer.
-__host__ __device__ inline size_t attn_tiles_offset(int hd) {
-  return round16(sizeof(float) * ((size_t)kGMax * hd + 2 * (size_t)hd + kAttnWarps * 256));
+__host__ __device__ inline size_t attn_tiles_offset(int hd) {  // 1024-aligned (swizzle atoms)
+  return (sizeof(float) * ((size_t)kGMax * hd + 2 * (size_t)hd + kAttnWarps * 256) + 1023) & ~(size_t)1023;
 }
 
 template <int J, typename T>
@@ -121,7 +127,8 @@ __host__ __device__ inline size_t attn_bars_offset(int hd, int ring, int merge_r
 
 template <int J, typename T>
 __host__ __device__ inline size_t attn_smem_bytes_t(int hd, int ring, int merge_rows) {
-  return attn_bars_offset<J, T>(hd, ring, merge_rows) + 8 * (size_t)ring;
+  // + 1024: the kernel aligns its base to 1024 bytes
+  return attn_bars_offset<J, T>(hd, ring, merge_rows) + 8 * (size_t)ring + 1024;
 }
 
 // The layout of one launch (kernel and host compute it alike): a unit u of
@@ -179,60 +186,99 @@ __device__ __forceinline__ float2 h2f2(uint32_t u) {
   return __half22float2(h);
 }
 
-// Requests K/V rows [c0, c0 + kSub) of a cache in its own type into tile
-// buffer `buf` ([K rows][V rows], row stride hs elements): every thread of
-// the CTA copies its share of the 16-byte pieces (cp.async, L2 only) and
-// arrives on `bar` once they have landed (the barrier counts one arrival
-// per thread).  Rows >= t1 and the current position's row (fused mode) are
-// not copied (zero_rows / put_pos_row fill them).
-template <typename TT>
-__device__ __forceinline__ void issue_tile(uint8_t* buf, uint64_t* bar, const uint8_t* kc, const uint8_t* vc, int c0,
-                                           int t1, int pos, bool fused, int kv_dim, size_t kv_off, int hd, int hs) {
-  const int cpr = hd * (int)sizeof(TT) / 16;  // pieces per row
-  const size_t rowb = (size_t)hs * sizeof(TT);
-  const int n = 2 * kSub * cpr;
-  for (int e = threadIdx.x; e < n; e += blockDim.x) {
-    const int m = e / (kSub * cpr), rem = e - m * (kSub * cpr);
-    const int r = rem / cpr, pc = rem - r * cpr, t = c0 + r;
-    if (t < t1 && !(fused && t == pos)) {
-      const uint8_t* src = (m ? vc : kc) + ((size_t)t * kv_dim + kv_off) * sizeof(TT) + (size_t)pc * 16;
-      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(buf + (size_t)(m * kSub + r) * rowb +
-                                                                             (size_t)pc * 16)),
-                   "l"(src)
-                   : "memory");
-    }
-  }
-  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
+// Byte offset of byte `byte` of row r (0..31) in a swizzled K or V tile.
+__device__ __forceinline__ uint32_t sw_off(int r, int byte) {
+  return (uint32_t)((byte >> 7) * 4096 + r * 128 + ((((byte >> 4) & 7) ^ (r & 7)) << 4) + (byte & 15));
 }
 
-// Zeroes tile rows [t1 - c0, kSub) (positions past the chunk: their scores
-// are masked, but P.V reads them).
+// One 2-D TMA tensor copy (no multicast) of the box at element (x, y) of
+// `map` into this CTA's shared memory, completing on `bar`.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Requests the K and V tiles of positions [y, y + 32) of the maps' rows,
+// columns [x0, x0 + head_dim), into tile buffer `buf` ([K boxes][V boxes]):
+// one thread, 2 * head_dim*sizeof(TT)/128 copies completing on `bar`.  Rows
+// past the map read as zero; rows past the current position and the current
+// position's row (fused mode) are rewritten after the wait.
 template <typename TT>
-__device__ __forceinline__ void zero_rows(uint8_t* buf, int c0, int t1, int hd, int hs) {
+__device__ __forceinline__ void issue_tile(uint8_t* buf, uint64_t* bar, const CUtensorMap* km, const CUtensorMap* vm,
+                                           int x0, int y, int hd) {
+  const int nbox = hd * (int)sizeof(TT) / 128, per = 128 / (int)sizeof(TT);
+  mbar_arrive_expect_tx(bar, (uint32_t)(2 * nbox * 4096));
+  for (int j = 0; j < nbox; ++j) {
+    tma_load_2d(buf + j * 4096, km, x0 + j * per, y, bar);
+    tma_load_2d(buf + (nbox + j) * 4096, vm, x0 + j * per, y, bar);
+  }
+}
+
+// Zeroes rows [t1 - c0, kSub) of a landed tile (positions past the current
+// one: their scores are masked, but P.V reads them).
+template <typename TT>
+__device__ __forceinline__ void zero_rows(uint8_t* buf, int c0, int t1, int hd) {
   const int r0 = t1 - c0;
   if (r0 >= kSub) return;
-  const int per = hd * (int)sizeof(TT) / 16;
-  const size_t rowb = (size_t)hs * sizeof(TT);
-  for (int e = threadIdx.x; e < (kSub - r0) * per; e += blockDim.x) {
-    const int r = r0 + e / per, p = e % per;
-    *reinterpret_cast<uint4*>(buf + (size_t)r * rowb + p * 16) = make_uint4(0u, 0u, 0u, 0u);
-    *reinterpret_cast<uint4*>(buf + (size_t)(kSub + r) * rowb + p * 16) = make_uint4(0u, 0u, 0u, 0u);
+  const int nr = kSub - r0, nbox2 = 2 * hd * (int)sizeof(TT) / 128;
+  for (int e = threadIdx.x; e < nbox2 * nr * 8; e += blockDim.x) {
+    const int box = e / (nr * 8), rem = e - box * (nr * 8), r = r0 + (rem >> 3), ch = rem & 7;
+    *reinterpret_cast<uint4*>(buf + box * 4096 + r * 128 + ch * 16) = make_uint4(0u, 0u, 0u, 0u);
   }
 }
 
-// The current position's row into the tile of sub-chunk [c0, c0 + kSub)
-// when it lies there (rounded to the tile type, as the cache stores it).
+// The current position's row into a landed tile of [c0, c0 + kSub) when it
+// lies there (rounded to the tile type, as the cache stores it).
 template <typename TT>
-__device__ __forceinline__ void put_pos_row(uint8_t* buf, const float* kpos, const float* vpos, int c0, int t1,
-                                            int pos, bool fused, int hd, int hs) {
-  if (fused && pos >= c0 && pos < min(t1, c0 + kSub)) {
-    TT* kr = reinterpret_cast<TT*>(buf) + (size_t)(pos - c0) * hs;
-    TT* vr = kr + (size_t)kSub * hs;
+__device__ __forceinline__ void put_pos_row(uint8_t* buf, const float* kpos, const float* vpos, int c0, int pos,
+                                            bool fused, int hd) {
+  if (fused && pos >= c0 && pos < c0 + kSub) {
+    const int r = pos - c0;
+    uint8_t* vb = buf + (size_t)kSub * hd * sizeof(TT);
     for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-      kr[d] = to_tile<TT>(kpos[d]);
-      vr[d] = to_tile<TT>(vpos[d]);
+      const uint32_t o = sw_off(r, d * (int)sizeof(TT));
+      *reinterpret_cast<TT*>(buf + o) = to_tile<TT>(kpos[d]);
+      *reinterpret_cast<TT*>(vb + o) = to_tile<TT>(vpos[d]);
     }
   }
+}
+
+// s = sum_d q_d k_d over row r of a swizzled K tile, one sequential fma
+// chain over d.
+template <typename TT>
+__device__ __forceinline__ float score_row_sw(const float* q, const uint8_t* kt, int r, int hd) {
+  float sc = 0.0f;
+  const int nch = hd * (int)sizeof(TT) / 16;
+  for (int i = 0; i < nch; ++i) {
+    const uint4 u = *reinterpret_cast<const uint4*>(kt + sw_off(r, i * 16));
+    if constexpr (sizeof(TT) == 2) {
+      const float4 qa = reinterpret_cast<const float4*>(q)[2 * i], qb = reinterpret_cast<const float4*>(q)[2 * i + 1];
+      float2 f = h2f2(u.x);
+      sc = __fmaf_rn(qa.x, f.x, sc);
+      sc = __fmaf_rn(qa.y, f.y, sc);
+      f = h2f2(u.y);
+      sc = __fmaf_rn(qa.z, f.x, sc);
+      sc = __fmaf_rn(qa.w, f.y, sc);
+      f = h2f2(u.z);
+      sc = __fmaf_rn(qb.x, f.x, sc);
+      sc = __fmaf_rn(qb.y, f.y, sc);
+      f = h2f2(u.w);
+      sc = __fmaf_rn(qb.z, f.x, sc);
+      sc = __fmaf_rn(qb.w, f.y, sc);
+    } else {
+      const float4 qv = reinterpret_cast<const float4*>(q)[i];
+      sc = __fmaf_rn(qv.x, __uint_as_float(u.x), sc);
+      sc = __fmaf_rn(qv.y, __uint_as_float(u.y), sc);
+      sc = __fmaf_rn(qv.z, __uint_as_float(u.z), sc);
+      sc = __fmaf_rn(qv.w, __uint_as_float(u.w), sc);
+    }
+  }
+  return sc;
 }
 
 // s = sum_d q_d k_d as one sequential fma chain over d.
@@ -309,6 +355,21 @@ __device__ __forceinline__ void load_v(const TT* vr, float (&v)[J]) {
 #pragma unroll
       for (int j = 0; j < J; ++j) v[j] = vr[j];
     }
+  }
+}
+
+// J consecutive values (as f32) of row r of a swizzled V tile, starting at
+// value lane*J.
+template <int J, typename TT>
+__device__ __forceinline__ void load_v_sw(const uint8_t* vt, int r, int lane, float (&v)[J]) {
+  const int byte = lane * J * (int)sizeof(TT);
+  if constexpr (J * sizeof(TT) == 32) {  // f32, J = 8: two chunks
+    const float4 a = *reinterpret_cast<const float4*>(vt + sw_off(r, byte));
+    const float4 b = *reinterpret_cast<const float4*>(vt + sw_off(r, byte + 16));
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+    load_v<J, TT>(reinterpret_cast<const TT*>(vt + sw_off(r, byte)), v);
   }
 }
 
@@ -442,12 +503,15 @@ __device__ __forceinline__ void norm_rope_regs(float (&v)[8], const float (&wr)[
 // (unit u on CTA u mod n_split) reading the partials through distributed
 // shared memory.  Every thread of every CTA reaches both cluster barriers.
 template <int J, typename T, bool kCluster>
-__global__ void __launch_bounds__(kAttnWarps * 32, 2) k_attention(const AttnArgs a) {
+__global__ void __launch_bounds__(kAttnWarps * 32, 2)
+    k_attention(const AttnArgs a, const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap) {
   using C = TileCfg<J, T>;
   using TT = typename C::TT;
-  extern __shared__ __align__(16) uint8_t smem_b[];
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  // the swizzled tiles need 1024-byte alignment (the launch adds the slack)
+  uint8_t* smem_b = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
   const int hd = a.head_dim;
-  const int hs = C::stride(hd);
+  const int hs = C::stride(hd);  // J = 1 tiles
   const int S = a.n_split;
   const int nbmax_cta = (attn_n_blocks(a.ctx) + S - 1) / S;
   const AttnLayout lay = attn_layout<J, T>(hd, a.n_head, a.n_kv, a.ctx, S, kCluster);
@@ -495,15 +559,16 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) k_attention(const AttnArgs
   // blocks (the current position comes from this kernel's prologue), and
   // the norm weights and RoPE row (into registers, or into L1 for the
   // shared-memory norm).
+  const int row0 = z * a.ctx;  // this sequence's first row in the maps
   if constexpr (C::kAsync) {
     if (threadIdx.x == 0) {
-      for (int b = 0; b < NT; ++b) mbar_init(&s_bar[b], nt);
+      for (int b = 0; b < NT; ++b) mbar_init(&s_bar[b], 1);
       mbar_fence_init();
+      for (int i = 0; i < bpr && i < nb; ++i)
+        issue_tile<TT>(s_tiles + (size_t)(i % NT) * buf_bytes, &s_bar[i % NT], &kmap, &vmap, (int)kv_off,
+                       row0 + (split + S * i) * kSub, hd);
     }
     __syncthreads();
-    for (int i = 0; i < bpr && i < nb; ++i)
-      issue_tile<TT>(s_tiles + (size_t)(i % NT) * buf_bytes, &s_bar[i % NT], kc, vc, (split + S * i) * kSub, n_pos,
-                     pos, fused, kv_dim, kv_off, hd, hs);
   }
   if (fused && nb > 0 && threadIdx.x < 12 && !(J >= 2 && a.rope_cos && a.rope_sin)) {
     const uint8_t* line = nullptr;
@@ -603,23 +668,27 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) k_attention(const AttnArgs
   for (int r = 0; r * bpr < nb; ++r) {
     if constexpr (C::kAsync) {
       // next round's tiles into the buffers the round before finished with
-      for (int j = 0; j < bpr; ++j) {
-        const int i = (r + 1) * bpr + j;
-        if (i < nb)
-          issue_tile<TT>(s_tiles + (size_t)(i % NT) * buf_bytes, &s_bar[i % NT], kc, vc, (split + S * i) * kSub, n_pos,
-                         pos, fused, kv_dim, kv_off, hd, hs);
-      }
-      for (int j = 0; j < bpr; ++j) {
-        const int i = r * bpr + j;
-        if (i >= nb) break;
-        uint8_t* buf = s_tiles + (size_t)(i % NT) * buf_bytes;
-        put_pos_row<TT>(buf, s_kpos, s_vpos, (split + S * i) * kSub, n_pos, pos, fused, hd, hs);
-        zero_rows<TT>(buf, (split + S * i) * kSub, n_pos, hd, hs);
+      // (their generic reads and writes ordered before the copies)
+      if (threadIdx.x == 0) {
+        fence_proxy_async();
+        for (int j = 0; j < bpr; ++j) {
+          const int i = (r + 1) * bpr + j;
+          if (i < nb)
+            issue_tile<TT>(s_tiles + (size_t)(i % NT) * buf_bytes, &s_bar[i % NT], &kmap, &vmap, (int)kv_off,
+                           row0 + (split + S * i) * kSub, hd);
+        }
       }
       for (int j = 0; j < bpr; ++j) {
         const int i = r * bpr + j;
         if (i >= nb) break;
         mbar_wait(&s_bar[i % NT], (uint32_t)(i / NT) & 1u, a.err);
+      }
+      for (int j = 0; j < bpr; ++j) {
+        const int i = r * bpr + j;
+        if (i >= nb) break;
+        uint8_t* buf = s_tiles + (size_t)(i % NT) * buf_bytes;
+        put_pos_row<TT>(buf, s_kpos, s_vpos, (split + S * i) * kSub, pos, fused, hd);
+        zero_rows<TT>(buf, (split + S * i) * kSub, n_pos, hd);
       }
     } else {
       for (int j = 0; j < bpr; ++j) {
@@ -634,10 +703,13 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) k_attention(const AttnArgs
     const int g = warp % G, j = warp / G, i = r * bpr + j;
     if (j < bpr && i < nb) {
       const int c = split + S * i;
-      const TT* ktile = reinterpret_cast<const TT*>(s_tiles + (size_t)(i % NT) * buf_bytes);
-      const TT* vtile = ktile + (size_t)kSub * hs;
+      const uint8_t* tile = s_tiles + (size_t)(i % NT) * buf_bytes;
       const bool valid = c * kSub + lane < n_pos;
-      float sc = score_row<TT>(s_q + g * hd, ktile + (size_t)lane * hs, hd, hs);
+      float sc;
+      if constexpr (C::kAsync)
+        sc = score_row_sw<TT>(s_q + g * hd, tile, lane, hd);
+      else
+        sc = score_row<TT>(s_q + g * hd, reinterpret_cast<const TT*>(tile) + (size_t)lane * hs, hd, hs);
       sc = valid ? __fmul_rn(sc, a.scale) : -INFINITY;
       const float m = warp_max(sc);
       const float p = valid ? expf_det(__fsub_rn(sc, m)) : 0.0f;
@@ -650,7 +722,10 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) k_attention(const AttnArgs
         const float pt = __shfl_sync(0xffffffffu, p, tt);
         if (act) {
           float vv[J];
-          load_v<J, TT>(vtile + (size_t)tt * hs + lane * J, vv);
+          if constexpr (C::kAsync)
+            load_v_sw<J, TT>(tile + (size_t)kSub * hd * sizeof(TT), tt, lane, vv);
+          else
+            load_v<J, TT>(reinterpret_cast<const TT*>(tile) + (size_t)(kSub + tt) * hs + lane * J, vv);
 #pragma unroll
           for (int jj = 0; jj < J; ++jj) acc[jj] = __fmaf_rn(pt, vv[jj], acc[jj]);
         }
@@ -744,7 +819,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) k_attention(const AttnArgs
 // with programmatic dependent launch when pdl is set.
 template <typename Kern>
 cudaError_t launch_cluster(Kern kernel, dim3 grid, int cluster_y, size_t smem, cudaStream_t st, bool pdl,
-                           const AttnArgs& a) {
+                           const AttnArgs& a, const CUtensorMap& km, const CUtensorMap& vm) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(kAttnWarps * 32);
@@ -759,7 +834,29 @@ cudaError_t launch_cluster(Kern kernel, dim3 grid, int cluster_y, size_t smem, c
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 2 : 1;
-  return cudaLaunchKernelEx(&cfg, kernel, a);
+  return cudaLaunchKernelEx(&cfg, kernel, a, km, vm);
+}
+
+// cuTensorMapEncodeTiled, from the driver (resolved once at set-up).
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn g_encode = nullptr;
+
+// The K or V cache of one layer as a 2-D tensor [rows][kv_dim] in its own
+// type (rows = sequences x context), read in boxes of 32 rows x 128 bytes
+// with the 128-byte swizzle; rows past the end read as zero.
+bool encode_kv_map(CUtensorMap* m, const void* base, bool f16, int kv_dim, unsigned long long rows) {
+  const int esz = f16 ? 2 : 4;
+  if (!g_encode || !base || (reinterpret_cast<uintptr_t>(base) & 15) || ((size_t)kv_dim * esz) % 16) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)kv_dim, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)kv_dim * esz};
+  const cuuint32_t box[2] = {(cuuint32_t)(128 / esz), (cuuint32_t)kSub};
+  const cuuint32_t estr[2] = {1, 1};
+  return g_encode(m, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 // Whether clusters of n CTAs of a kernel can be resident, queried once at
@@ -827,6 +924,19 @@ cudaError_t launch_j(const AttnArgs& a, cudaStream_t st, bool pdl) {
   const int hd = a.head_dim;
   const dim3 grid(a.n_kv, a.n_split, a.batch > 0 ? a.batch : 1);
   const bool f16 = a.kv_f16 != 0;
+  CUtensorMap km, vm;
+  memset(&km, 0, sizeof(km));
+  memset(&vm, 0, sizeof(vm));
+  if constexpr (J >= 2) {
+    // the sequences' caches must be consecutive [batch][ctx][kv_dim] blocks
+    const int B = a.batch > 1 ? a.batch : 1;
+    const int kv_dim = a.n_kv * hd;
+    if (B > 1 && a.cache_bstride != (size_t)a.ctx * kv_dim) return cudaErrorInvalidValue;
+    const unsigned long long rows = (unsigned long long)B * a.ctx;
+    if (rows > 0x7fffffffull || !encode_kv_map(&km, a.k_cache, f16, kv_dim, rows) ||
+        !encode_kv_map(&vm, a.v_cache, f16, kv_dim, rows))
+      return cudaErrorInvalidValue;
+  }
   auto bytes = [&](auto t, bool cl) {
     using TE = decltype(t);
     const AttnLayout l = attn_layout<J, TE>(hd, a.n_head, a.n_kv, a.ctx, a.n_split, cl);
@@ -838,15 +948,16 @@ cudaError_t launch_j(const AttnArgs& a, cudaStream_t st, bool pdl) {
     if (dev >= 0 && nb_cta <= kAttnMaxBlocksCta && g_cluster_ok[dev][f16][j_index(J)][a.n_split]) {
       const size_t b = f16 ? bytes(__half(), true) : bytes(0.0f, true);
       if (b <= (size_t)kDynSmemMax) {
-        if (f16) return launch_cluster(k_attention<J, __half, true>, grid, a.n_split, b, st, pdl, a);
-        return launch_cluster(k_attention<J, float, true>, grid, a.n_split, b, st, pdl, a);
+        if (f16) return launch_cluster(k_attention<J, __half, true>, grid, a.n_split, b, st, pdl, a, km, vm);
+        return launch_cluster(k_attention<J, float, true>, grid, a.n_split, b, st, pdl, a, km, vm);
       }
     }
   }
   if (!a.partial || !a.counters) return cudaErrorInvalidValue;
   if (f16)
-    return launch_k(k_attention<J, __half, false>, grid, dim3(kAttnWarps * 32), bytes(__half(), false), st, pdl, a);
-  return launch_k(k_attention<J, float, false>, grid, dim3(kAttnWarps * 32), bytes(0.0f, false), st, pdl, a);
+    return launch_k(k_attention<J, __half, false>, grid, dim3(kAttnWarps * 32), bytes(__half(), false), st, pdl, a, km,
+                    vm);
+  return launch_k(k_attention<J, float, false>, grid, dim3(kAttnWarps * 32), bytes(0.0f, false), st, pdl, a, km, vm);
 }
 
 template <int J>
@@ -865,6 +976,14 @@ size_t attn_partial_floats(int n_head, int n_blocks, int head_dim) {
 cudaError_t attention_init() {
   const int dev = current_device();
   if (dev < 0) return cudaErrorInvalidDevice;
+  if (!g_encode) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn)
+      return cudaErrorNotSupported;
+    g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+  }
   cudaError_t e = init_j<1>(dev);
   if (e == cudaSuccess) e = init_j<2>(dev);
   if (e == cudaSuccess) e = init_j<4>(dev);
