@@ -254,6 +254,7 @@ template <typename TT>
 __device__ __forceinline__ float score_row_sw(const float* q, const uint8_t* kt, int r, int hd) {
   float sc = 0.0f;
   const int nch = hd * (int)sizeof(TT) / 16;
+#pragma unroll 4
   for (int i = 0; i < nch; ++i) {
     const uint4 u = *reinterpret_cast<const uint4*>(kt + sw_off(r, i * 16));
     if constexpr (sizeof(TT) == 2) {
@@ -439,6 +440,30 @@ __device__ __forceinline__ float merge_blocks(int nblk, int lane, FM mf, FL lf, 
           o = __fmaf_rn(w, av[k], o);
         }
       }
+    }
+  }
+  return __fmul_rn(o, L > 0.0f ? __fdiv_rn(1.0f, L) : 0.0f);
+}
+
+// merge_blocks for accessors that read this CTA's shared memory (cheap
+// loads): the same operations in the same order, as short loops (the
+// kernel runs once per CTA, so its code is fetched cold).
+template <typename FM, typename FL, typename FA>
+__device__ __forceinline__ float merge_blocks_local(int nblk, int lane, FM mf, FL lf, FA af) {
+  float M = -INFINITY;
+  for (int c = lane; c < nblk; c += 32) M = fmaxf(M, mf(c));
+  M = warp_max(M);
+  float L = 0.0f, o = 0.0f;
+  for (int c0 = 0; c0 < nblk; c0 += 32) {
+    const int c = c0 + lane;
+    const float lc = c < nblk ? lf(c) : 0.0f;
+    const float wc = c < nblk ? expf_det(__fsub_rn(mf(c), M)) : 0.0f;
+    const int nc = nblk - c0 < 32 ? nblk - c0 : 32;
+#pragma unroll 4
+    for (int k = 0; k < nc; ++k) {
+      const float w = __shfl_sync(0xffffffffu, wc, k);
+      L = __fmaf_rn(w, __shfl_sync(0xffffffffu, lc, k), L);
+      o = __fmaf_rn(w, af(c0 + k), o);
     }
   }
   return __fmul_rn(o, L > 0.0f ? __fdiv_rn(1.0f, L) : 0.0f);
@@ -707,7 +732,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2)
       const bool valid = c * kSub + lane < n_pos;
       float sc;
       if constexpr (C::kAsync)
-        sc = score_row_sw<TT>(s_q + g * hd, tile, lane, hd);
+        sc = score_row_sw<TT>(s_q + g * hd, tile, lane, 32 * J);  // head_dim = 32 * J
       else
         sc = score_row<TT>(s_q + g * hd, reinterpret_cast<const TT*>(tile) + (size_t)lane * hs, hd, hs);
       sc = valid ? __fmul_rn(sc, a.scale) : -INFINITY;
@@ -723,7 +748,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2)
         if (act) {
           float vv[J];
           if constexpr (C::kAsync)
-            load_v_sw<J, TT>(tile + (size_t)kSub * hd * sizeof(TT), tt, lane, vv);
+            load_v_sw<J, TT>(tile + (size_t)kSub * 32 * J * sizeof(TT), tt, lane, vv);
           else
             load_v<J, TT>(reinterpret_cast<const TT*>(tile) + (size_t)(kSub + tt) * hs + lane * J, vv);
 #pragma unroll
@@ -770,7 +795,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2)
     for (int slot = warp; split + slot * S < n_units; slot += kAttnWarps) {
       const int u = split + slot * S;
       const float* rows = s_merge + (size_t)slot * nblk_max * kMergeRow;
-      const float o = merge_blocks(
+      const float o = merge_blocks_local(
           nblk, lane, [&](int c) { return rows[(size_t)c * kMergeRow + 32]; },
           [&](int c) { return rows[(size_t)c * kMergeRow + 33]; },
           [&](int c) { return rows[(size_t)c * kMergeRow + lane]; });
