@@ -406,39 +406,50 @@ __device__ __forceinline__ void gemv_build_x(const GemvArgs& a, uint8_t* xbase, 
     }
   } else {
     // f32 input: four lanes per 32-value block, eight values each (a warp
-    // covers 8 consecutive blocks, 1 KB of coalesced loads).  Every load of a
-    // tile is issued before it is needed (the first tile's before the
-    // RMSNorm reduction, the next tile's before the current one is
-    // quantised).  Arithmetic per element as q8_1_quant_lane.
+    // covers 8 consecutive blocks, 1 KB of coalesced loads).  A warp's tiles
+    // (up to three; with RMSNorm one) are all requested at once, before the
+    // RMSNorm reduction; larger inputs request each tile while the one
+    // before it is quantised.  Arithmetic per element as q8_1_quant_lane.
     const float* xf = a.xf;
     const bool norm = a.input == kInRmsNorm;
     const void* nw = a.norm_w;
     const int ndt = a.norm_dtype;
     const float eps = a.eps;
     const int part = lane & 3;
-    float xv[8], wv[8];
-    auto load_tile = [&](int tile) {
+    const int ntile = (nblk + 7) / 8;
+    const bool at_once = norm ? ntile <= NC : ntile <= 3 * NC;
+    float xv[3][8], wv[8];
+    auto load_x = [&](int tile, float (&dst)[8]) {
       const int b = tile * 8 + (lane >> 2);
       if (b < nblk) {
         const float4* src = reinterpret_cast<const float4*>(xf + (size_t)b * 32 + part * 8);
         const float4 t0 = src[0], t1 = src[1];
-        xv[0] = t0.x; xv[1] = t0.y; xv[2] = t0.z; xv[3] = t0.w;
-        xv[4] = t1.x; xv[5] = t1.y; xv[6] = t1.z; xv[7] = t1.w;
-        if (norm) {
-#pragma unroll
-          for (int i = 0; i < 8; ++i) wv[i] = load_weight(nw, ndt, b * 32 + part * 8 + i);
-        }
+        dst[0] = t0.x; dst[1] = t0.y; dst[2] = t0.z; dst[3] = t0.w;
+        dst[4] = t1.x; dst[5] = t1.y; dst[6] = t1.z; dst[7] = t1.w;
       } else {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) xv[i] = wv[i] = 0.0f;
+        for (int i = 0; i < 8; ++i) dst[i] = 0.0f;
       }
     };
-    const int ntile = (nblk + 7) / 8;
-    if (warp < ntile) load_tile(warp);
+    auto load_w = [&](int tile) {
+      const int b = tile * 8 + (lane >> 2);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) wv[i] = b < nblk ? load_weight(nw, ndt, b * 32 + part * 8 + i) : 0.0f;
+    };
+    if (at_once) {
+#pragma unroll
+      for (int u = 0; u < 3; ++u)
+        if (warp + u * NC < ntile) load_x(warp + u * NC, xv[u]);
+    } else if (warp < ntile) {
+      load_x(warp, xv[0]);
+    }
+    if (norm && warp < ntile) load_w(warp);
     float inv = 1.0f;
     if (norm) {
       // sum of squares in k_rmsnorm_q8_1's order: 256 strided partial sums
-      // (each sequential in i), a halving tree, then a warp tree
+      // (each sequential in i), a halving tree (strides 128, 64, 32), then a
+      // warp tree -- the trees computed by every warp from the partials in
+      // registers (lane l adds partials l + 32k in the halving order)
       float* red = reinterpret_cast<float*>(xs16 + cols / 16);
       const int per = cols / 256;
       for (int t = tid; t < 256; t += nthr) {
@@ -457,26 +468,39 @@ __device__ __forceinline__ void gemv_build_x(const GemvArgs& a, uint8_t* xbase, 
         }
         red[t] = p;
       }
-      for (int stride = 128; stride >= 32; stride >>= 1) {
-        asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
-        for (int t = tid; t < stride; t += nthr) red[t] = __fadd_rn(red[t], red[t + stride]);
-      }
       asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
-      if (warp == 0) {
-        float r = red[lane];
+      float q[8];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) r = __fadd_rn(r, __shfl_down_sync(0xffffffffu, r, o));
-        if (lane == 0) red[256] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(r, (float)cols), eps)));
-      }
-      asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
-      inv = red[256];
+      for (int k = 0; k < 8; ++k) q[k] = red[lane + 32 * k];
+      float r = __fadd_rn(__fadd_rn(__fadd_rn(q[0], q[4]), __fadd_rn(q[2], q[6])),
+                          __fadd_rn(__fadd_rn(q[1], q[5]), __fadd_rn(q[3], q[7])));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) r = __fadd_rn(r, __shfl_down_sync(0xffffffffu, r, o));
+      r = __shfl_sync(0xffffffffu, r, 0);
+      inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(r, (float)cols), eps)));
     }
-    for (int tile = warp; tile < ntile; tile += NC) {
-      float x[8];
+    if (at_once) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) x[i] = norm ? __fmul_rn(__fmul_rn(xv[i], inv), wv[i]) : xv[i];
-      if (tile + NC < ntile) load_tile(tile + NC);
-      x_block_quarter(x, tile * 8 + (lane >> 2), nblk, part, nb, xs, xd, xds, xs16);
+      for (int u = 0; u < 3; ++u) {
+        const int tile = warp + u * NC;
+        if (tile < ntile) {
+          float x[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) x[i] = norm ? __fmul_rn(__fmul_rn(xv[u][i], inv), wv[i]) : xv[u][i];
+          x_block_quarter(x, tile * 8 + (lane >> 2), nblk, part, nb, xs, xd, xds, xs16);
+        }
+      }
+    } else {
+      for (int tile = warp; tile < ntile; tile += NC) {
+        float x[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) x[i] = norm ? __fmul_rn(__fmul_rn(xv[0][i], inv), wv[i]) : xv[0][i];
+        if (tile + NC < ntile) {
+          load_x(tile + NC, xv[0]);
+          if (norm) load_w(tile + NC);
+        }
+        x_block_quarter(x, tile * 8 + (lane >> 2), nblk, part, nb, xs, xd, xds, xs16);
+      }
     }
   }
 }
