@@ -248,35 +248,63 @@ __device__ __forceinline__ void put_pos_row(uint8_t* buf, const float* kpos, con
   }
 }
 
-// s = sum_d q_d k_d over row r of a swizzled K tile, one sequential fma
-// chain over d.
-template <typename TT>
-__device__ __forceinline__ float score_row_sw(const float* q, const uint8_t* kt, int r, int hd) {
+// s = sum_d q_d k_d over row r of a swizzled K tile (head_dim HD), one
+// sequential fma chain over d; the loads run two 16-byte chunks ahead of
+// the chain.
+template <typename TT, int HD>
+__device__ __forceinline__ float score_row_sw(const float* q, const uint8_t* kt, int r) {
+  constexpr int nch = HD * (int)sizeof(TT) / 16;  // 16-byte chunks of the row
+  constexpr int QPC = sizeof(TT) == 2 ? 2 : 1;    // q float4s per chunk
+  constexpr int GRP = 2;
+  static_assert(nch % GRP == 0, "whole chunk groups");
+  const float4* q4 = reinterpret_cast<const float4*>(q);
+  uint4 kc[GRP];
+  float4 qc[GRP * QPC];
+#pragma unroll
+  for (int u = 0; u < GRP; ++u) kc[u] = *reinterpret_cast<const uint4*>(kt + sw_off(r, u * 16));
+#pragma unroll
+  for (int u = 0; u < GRP * QPC; ++u) qc[u] = q4[u];
   float sc = 0.0f;
-  const int nch = hd * (int)sizeof(TT) / 16;
-#pragma unroll 4
-  for (int i = 0; i < nch; ++i) {
-    const uint4 u = *reinterpret_cast<const uint4*>(kt + sw_off(r, i * 16));
-    if constexpr (sizeof(TT) == 2) {
-      const float4 qa = reinterpret_cast<const float4*>(q)[2 * i], qb = reinterpret_cast<const float4*>(q)[2 * i + 1];
-      float2 f = h2f2(u.x);
-      sc = __fmaf_rn(qa.x, f.x, sc);
-      sc = __fmaf_rn(qa.y, f.y, sc);
-      f = h2f2(u.y);
-      sc = __fmaf_rn(qa.z, f.x, sc);
-      sc = __fmaf_rn(qa.w, f.y, sc);
-      f = h2f2(u.z);
-      sc = __fmaf_rn(qb.x, f.x, sc);
-      sc = __fmaf_rn(qb.y, f.y, sc);
-      f = h2f2(u.w);
-      sc = __fmaf_rn(qb.z, f.x, sc);
-      sc = __fmaf_rn(qb.w, f.y, sc);
-    } else {
-      const float4 qv = reinterpret_cast<const float4*>(q)[i];
-      sc = __fmaf_rn(qv.x, __uint_as_float(u.x), sc);
-      sc = __fmaf_rn(qv.y, __uint_as_float(u.y), sc);
-      sc = __fmaf_rn(qv.z, __uint_as_float(u.z), sc);
-      sc = __fmaf_rn(qv.w, __uint_as_float(u.w), sc);
+#pragma unroll
+  for (int g = 0; g < nch / GRP; ++g) {
+    uint4 kn[GRP];
+    float4 qn[GRP * QPC];
+    if (g + 1 < nch / GRP) {
+#pragma unroll
+      for (int u = 0; u < GRP; ++u) kn[u] = *reinterpret_cast<const uint4*>(kt + sw_off(r, ((g + 1) * GRP + u) * 16));
+#pragma unroll
+      for (int u = 0; u < GRP * QPC; ++u) qn[u] = q4[(g + 1) * GRP * QPC + u];
+    }
+#pragma unroll
+    for (int u = 0; u < GRP; ++u) {
+      const uint4 k = kc[u];
+      if constexpr (sizeof(TT) == 2) {
+        const float4 qa = qc[2 * u], qb = qc[2 * u + 1];
+        float2 f = h2f2(k.x);
+        sc = __fmaf_rn(qa.x, f.x, sc);
+        sc = __fmaf_rn(qa.y, f.y, sc);
+        f = h2f2(k.y);
+        sc = __fmaf_rn(qa.z, f.x, sc);
+        sc = __fmaf_rn(qa.w, f.y, sc);
+        f = h2f2(k.z);
+        sc = __fmaf_rn(qb.x, f.x, sc);
+        sc = __fmaf_rn(qb.y, f.y, sc);
+        f = h2f2(k.w);
+        sc = __fmaf_rn(qb.z, f.x, sc);
+        sc = __fmaf_rn(qb.w, f.y, sc);
+      } else {
+        const float4 qv = qc[u];
+        sc = __fmaf_rn(qv.x, __uint_as_float(k.x), sc);
+        sc = __fmaf_rn(qv.y, __uint_as_float(k.y), sc);
+        sc = __fmaf_rn(qv.z, __uint_as_float(k.z), sc);
+        sc = __fmaf_rn(qv.w, __uint_as_float(k.w), sc);
+      }
+    }
+    if (g + 1 < nch / GRP) {
+#pragma unroll
+      for (int u = 0; u < GRP; ++u) kc[u] = kn[u];
+#pragma unroll
+      for (int u = 0; u < GRP * QPC; ++u) qc[u] = qn[u];
     }
   }
   return sc;
@@ -732,7 +760,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2)
       const bool valid = c * kSub + lane < n_pos;
       float sc;
       if constexpr (C::kAsync)
-        sc = score_row_sw<TT>(s_q + g * hd, tile, lane, 32 * J);  // head_dim = 32 * J
+        sc = score_row_sw<TT, 32 * J>(s_q + g * hd, tile, lane);  // head_dim = 32 * J
       else
         sc = score_row<TT>(s_q + g * hd, reinterpret_cast<const TT*>(tile) + (size_t)lane * hs, hd, hs);
       sc = valid ? __fmul_rn(sc, a.scale) : -INFINITY;
@@ -742,17 +770,38 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2)
       float acc[J];
 #pragma unroll
       for (int jj = 0; jj < J; ++jj) acc[jj] = 0.0f;
+      if constexpr (C::kAsync) {
+        // P.V: the probabilities through this warp's shared scratch (free
+        // after the prologue) as broadcasts, V rows in groups whose loads
+        // are all issued before their fma chains
+        float* pw = s_sq + warp * 256;
+        pw[lane] = p;
+        __syncwarp();
+        const uint8_t* vt = tile + (size_t)kSub * 32 * J * sizeof(TT);
+        constexpr int PG = J * sizeof(TT) > 16 ? 4 : 8;  // positions per group
+#pragma unroll
+        for (int t0 = 0; t0 < kSub; t0 += PG) {
+          float pt[PG], vv[PG][J];
+#pragma unroll
+          for (int u = 0; u < PG; ++u) pt[u] = pw[t0 + u];
+#pragma unroll
+          for (int u = 0; u < PG; ++u) load_v_sw<J, TT>(vt, t0 + u, lane, vv[u]);
+#pragma unroll
+          for (int u = 0; u < PG; ++u)
+#pragma unroll
+            for (int jj = 0; jj < J; ++jj) acc[jj] = __fmaf_rn(pt[u], vv[u][jj], acc[jj]);
+        }
+        __syncwarp();
+      } else {
 #pragma unroll 8
-      for (int tt = 0; tt < kSub; ++tt) {
-        const float pt = __shfl_sync(0xffffffffu, p, tt);
-        if (act) {
-          float vv[J];
-          if constexpr (C::kAsync)
-            load_v_sw<J, TT>(tile + (size_t)kSub * 32 * J * sizeof(TT), tt, lane, vv);
-          else
+        for (int tt = 0; tt < kSub; ++tt) {
+          const float pt = __shfl_sync(0xffffffffu, p, tt);
+          if (act) {
+            float vv[J];
             load_v<J, TT>(reinterpret_cast<const TT*>(tile) + (size_t)(kSub + tt) * hs + lane * J, vv);
 #pragma unroll
-          for (int jj = 0; jj < J; ++jj) acc[jj] = __fmaf_rn(pt, vv[jj], acc[jj]);
+            for (int jj = 0; jj < J; ++jj) acc[jj] = __fmaf_rn(pt, vv[jj], acc[jj]);
+          }
         }
       }
       if constexpr (kCluster) {
