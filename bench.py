@@ -257,6 +257,17 @@ def run_kernel_sweep(args) -> int:
     return 0
 
 
+def _ncu_traffic(key):
+    """Per-launch DRAM bytes of the roofline kernel from the committed ncu summary (or None)."""
+    tf = ROOT / "profiles" / "ncu_traffic.json"
+    if not tf.exists():
+        return None
+    try:
+        return json.loads(tf.read_text()).get(key)
+    except (ValueError, KeyError):
+        return None
+
+
 def run_batch_bench(args, shape, world, rank, local, dist, barrier) -> int:
     """Qwen3-8B shape, every linear weight Q8_0, f16 KV cache at a 4096-token
     context, B independent sequences each after a prompt of --prompt ids (default 1024), greedy
@@ -359,7 +370,8 @@ def run_batch_bench(args, shape, world, rank, local, dist, barrier) -> int:
                 "d2h_bytes_per_step": STATE_BYTES * B},
         "gpu_launches": kernels * args.steps,
         "roofline": {"bound": "hbm", "achieved": gemm_gbs, "peak": hbm, "unit": "GB/s", "frac": gemm_gbs / hbm,
-                     "traffic": None, "peak_kind": peak_kind,
+                     "traffic": _ncu_traffic("gemm_q80_12288x4096_x32_bytes") if B == 32 else None,
+                     "peak_kind": peak_kind,
                      "kernel": f"k_gemm_q80<{16 if B <= 16 else 32}> (tcgen05, Q8_0 12288x4096 x {B} sequences), "
                                "timed alone with the L2 flushed before each launch",
                      "algorithmic_bytes_per_launch": alg, "us_per_launch": us,
@@ -516,13 +528,7 @@ def main() -> int:
     w_bytes, kv_bytes = model_bytes(tensors, shape, start_pos + args.steps // 2)
     step_bytes = w_bytes + kv_bytes
     traffic_key = "decode_step_qwen3_8b_bytes" if persistent else "gemv_q4_k_12288x4096_bytes"
-    traffic = None
-    tf = ROOT / "profiles" / "ncu_traffic.json"
-    if tf.exists():
-        try:
-            traffic = json.loads(tf.read_text()).get(traffic_key)
-        except (ValueError, KeyError):
-            traffic = None
+    traffic = _ncu_traffic(traffic_key)
     if persistent:
         gbs = step_bytes / (step_s / args.steps) / 1e9
         dom = {"gbs": gbs, "frac": gbs / hbm}
