@@ -102,8 +102,10 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1) k_gemv(const Gemv
   }
 
   // ---- consumers ----
+  float wpre[8];
+  gemv_norm_weights(a, warp, lane, wpre);
   pdl_wait();  // the activations (and y for the residual add) come from earlier kernels
-  gemv_build_x(a, smem, NC, warp, lane);
+  gemv_build_x(a, smem, NC, warp, lane, wpre);
   asm volatile("bar.sync 1, %0;" ::"r"(NC * 32) : "memory");
   if (threadIdx.x == 0) pdl_launch_dependents();
   const XShared x = gemv_x_view(smem, cols);

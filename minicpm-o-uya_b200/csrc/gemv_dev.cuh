@@ -373,7 +373,20 @@ __device__ __forceinline__ void x_block_quarter(const float (&v)[8], int b, int 
 // quantised here, optionally after RMSNorm.  Called by the NC consumer warps
 // (thread tid = warp*32 + lane); uses named barrier 1 for those NC*32
 // threads and ends without a barrier (the caller synchronises).
-__device__ __forceinline__ void gemv_build_x(const GemvArgs& a, uint8_t* xbase, int NC, int warp, int lane) {
+// The RMSNorm weights of this thread's first activation tile (the weights
+// do not depend on earlier kernels, so they can be requested before the
+// wait for them); zeros for other inputs.
+__device__ __forceinline__ void gemv_norm_weights(const GemvArgs& a, int warp, int lane, float (&wv)[8]) {
+  const int nblk = a.cols / 32;
+  const int b = warp * 8 + (lane >> 2);
+  const bool on = a.input == kInRmsNorm && b < nblk;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) wv[i] = on ? load_weight(a.norm_w, a.norm_dtype, b * 32 + (lane & 3) * 8 + i) : 0.0f;
+}
+
+// wpre: the weights gemv_norm_weights gave (null: loaded here).
+__device__ __forceinline__ void gemv_build_x(const GemvArgs& a, uint8_t* xbase, int NC, int warp, int lane,
+                                             const float* wpre = nullptr) {
   const int cols = a.cols;
   const int nb = cols / 256;
   const int nblk = cols / 32;
@@ -443,7 +456,14 @@ __device__ __forceinline__ void gemv_build_x(const GemvArgs& a, uint8_t* xbase, 
     } else if (warp < ntile) {
       load_x(warp, xv[0]);
     }
-    if (norm && warp < ntile) load_w(warp);
+    if (norm && warp < ntile) {
+      if (wpre) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) wv[i] = wpre[i];
+      } else {
+        load_w(warp);
+      }
+    }
     float inv = 1.0f;
     if (norm) {
       // sum of squares in k_rmsnorm_q8_1's order: 256 strided partial sums
