@@ -3,7 +3,7 @@
 //
 // Batch-1 decode is a weight stream and runs on dp4a (gemv.cu); with 32
 // sequences the same stream carries 32x the arithmetic, which dp4a cannot
-// keep up with, so the weights are dequantised to f16 in shared memory and
+// keep up with, so the weights are dequantised to f16 into tensor memory and
 // multiplied on the tensor cores with f32 accumulation in tensor memory:
 //
 //   warp 0      producer: per 256-value K-tile, one bulk copy of the tile's
@@ -11,13 +11,14 @@
 //               128 rows x 8 blocks of a (row tile, K-tile) pair are one
 //               34816-byte block) and one bulk copy of the f16 activation
 //               tile (N x 256, already in the operand layout);
-//   warps 2..9  dequantise: thread = (row, half of the K-tile), q * d in f16
-//               (int8 -> f16 exactly via the 0x6400 exponent trick, one
-//               rounding in the multiply), written as 8x16-byte core matrices
-//               of the K-major operand layout (no swizzle);
+//   warps 2..9  dequantise: thread = (row, quarter of the K-tile), q * d in
+//               f16 (int8 -> f16 exactly via the 0x6400 exponent trick, one
+//               rounding in the multiply), stored into the A stage in tensor
+//               memory (lane = row, tcgen05.st) -- no shared-memory operand;
 //   warp 1      one elected thread issues tcgen05.mma kind::f16 (M = 128,
-//               N = sequences, K = 16) into a 128 x N f32 accumulator in
-//               tensor memory and releases stages with tcgen05.commit;
+//               N = sequences, K = 16) with A read from tensor memory, into
+//               a 128 x N f32 accumulator in tensor memory, and releases
+//               stages with tcgen05.commit;
 //   epilogue    warps 2..9 read the accumulator with tcgen05.ld (lane = row,
 //               each warp half of the sequence columns)
 //               and store / add Y, or, with K split over several CTAs, write
@@ -47,21 +48,25 @@ namespace mcpo {
 
 namespace {
 
-constexpr int kRawStages = 3;   // Q8_0 weight tiles in flight
-constexpr int kActStages = 2;   // f16 activation tiles in flight
-constexpr int kAStages = 4;     // f16 operand quarter-tiles (128 rows x 64 K): two per dequantising group
+constexpr int kRawStages = 4;   // Q8_0 weight tiles in flight
+constexpr int kActStages = 4;   // f16 activation tiles in flight
+constexpr int kAStages = 8;     // f16 operand quarter-tiles (128 rows x 64 K) in tensor memory: two K-tiles
 constexpr int kRowPiece = 272;  // bytes of 256 values of one Q8_0 row
 constexpr int kRawBytes = kGemmTileRows * kRowPiece;     // 34816
-constexpr int kABytes = kGemmTileRows * 64 * 2;          // 16384
 constexpr int kDqWarps = 8;  // dequantising / epilogue warps: 4 per 128-value half of a K-tile
 constexpr int kThreads = (2 + kDqWarps) * 32;
+// Tensor memory: the 128 x N f32 accumulator in columns [0, 32); A stage s
+// (128 rows x 64 f16, two per 32-bit column) in columns [32 + 32s, 64 + 32s)
+// -- quarter q of K-tile i in stage q + 4 (i & 1), so the dequantising warps
+// run a K-tile ahead of the MMAs.
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTmemA = 32;
 
 __host__ __device__ constexpr size_t act_bytes(int N) { return (size_t)N * kGemmKTile * 2; }
 
-// Shared memory: [A stages][raw stages][activation stages][barriers][tmem addr][abort]
+// Shared memory: [raw stages][activation stages][barriers][tmem addr][abort]
 struct GemmSmem {
-  __host__ __device__ static size_t a_off() { return 0; }
-  __host__ __device__ static size_t raw_off() { return (size_t)kAStages * kABytes; }
+  __host__ __device__ static size_t raw_off() { return 0; }
   __host__ __device__ static size_t act_off() { return raw_off() + (size_t)kRawStages * kRawBytes; }
   __host__ __device__ static size_t bar_off(int N) { return act_off() + (size_t)kActStages * act_bytes(N); }
   __host__ __device__ static size_t bytes(int N) {
@@ -95,6 +100,31 @@ __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+
+// D (+)= A * B with A (128 x 16 f16, lane = row) in tensor memory at tmem_a.
+__device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// 32 consecutive 32-bit tensor-memory columns of this thread's lane.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+      "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+      "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // Arrives on `bar` once every tcgen05 operation this thread issued before it
 // has completed.
@@ -167,9 +197,9 @@ __device__ __forceinline__ __half2 q8x2_to_h2(uint32_t wx, uint32_t sel) {
 }
 
 // Row r's 64 values [64qt, 64qt + 64) of the staged K-tile (Q8_0 blocks
-// 2qt, 2qt+1: 17 words at [qt][i][r]) -> 8 chunks of 8 f16 values, chunk c
-// to a_stage + c*2048 + r*16 (core matrix of rows r & ~7, row r & 7).
-__device__ __forceinline__ void dequant_quarter(const uint8_t* raw, uint8_t* a_stage, int r, int qt) {
+// 2qt, 2qt+1: 17 words at [qt][i][r]) -> 32 words of two f16 values in K
+// order (word c holds values 2c, 2c+1).
+__device__ __forceinline__ void dequant_quarter(const uint8_t* raw, uint32_t (&outw)[32], int r, int qt) {
   uint32_t w[17];
   const uint32_t* src = reinterpret_cast<const uint32_t*>(raw) + (size_t)qt * 17 * kGemmTileRows + r;
 #pragma unroll
@@ -191,15 +221,12 @@ __device__ __forceinline__ void dequant_quarter(const uint8_t* raw, uint8_t* a_s
     const int db = 34 * j;
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
-      uint32_t out[4];
 #pragma unroll
       for (int p = 0; p < 4; ++p) {
         const int b = db + 2 + 8 * c + 2 * p;  // first byte of the pair (even, same word as b+1)
         const __half2 v = __hmul2(q8x2_to_h2(w[b >> 2], (b & 3) ? 0x4342u : 0x4140u), d2[j]);
-        memcpy(&out[p], &v, 4);
+        memcpy(&outw[(4 * j + c) * 4 + p], &v, 4);
       }
-      *reinterpret_cast<uint4*>(a_stage + (size_t)(4 * j + c) * 2048 + (size_t)r * 16) =
-          make_uint4(out[0], out[1], out[2], out[3]);
     }
   }
 }
@@ -212,7 +239,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_q80(const GemmArgs a) {
   // the 1 KB of slack.
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
-  uint8_t* a_st = smem + GemmSmem::a_off();
   uint8_t* raw_st = smem + GemmSmem::raw_off();
   uint8_t* act_st = smem + GemmSmem::act_off();
   uint64_t* raw_full = reinterpret_cast<uint64_t*>(smem + GemmSmem::bar_off(N));
@@ -250,7 +276,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_q80(const GemmArgs a) {
     *abort_s = 0;
     mbar_fence_init();
   }
-  if (warp == 1) tmem_alloc(tmem_s, 32);
+  if (warp == 1) tmem_alloc(tmem_s, kTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -305,25 +331,24 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_q80(const GemmArgs a) {
     // ---- MMA issuer (one thread) ----
     if (lane == 0) {
       const uint32_t idesc = umma_idesc_f16(N);
-      const uint32_t lbo_a = 2048, sbo = 128, lbo_b = (N / 8) * 128;
+      const uint32_t sbo = 128, lbo_b = (N / 8) * 128;
       bool ok = true;
       for (int i = 0; i < nkt && ok; ++i) {
         const int s = i % kActStages;
         if (!gwait(&x_full[s], (uint32_t)(i / kActStages) & 1u, a.err, abort_s)) break;
         for (int qt = 0; qt < 4; ++qt) {
-          const int sa = qt;  // A stage qt holds quarter qt of every K-tile
-          if (!gwait(&a_full[sa], (uint32_t)i & 1u, a.err, abort_s)) {
+          const int sa = qt + 4 * (i & 1);
+          if (!gwait(&a_full[sa], (uint32_t)(i >> 1) & 1u, a.err, abort_s)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_base = smem_addr(a_st + (size_t)sa * kABytes);
+          const uint32_t a_tm = tmem + kTmemA + (uint32_t)sa * 32;  // 4 columns of K per 8 values
           const uint32_t b_base = smem_addr(act_st + (size_t)s * act_bytes(N)) + (uint32_t)(qt * 8) * lbo_b;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t ad = umma_desc(a_base + kk * 2 * lbo_a, lbo_a, sbo);
             const uint64_t bd = umma_desc(b_base + kk * 2 * lbo_b, lbo_b, sbo);
-            umma_f16(tmem, ad, bd, idesc, (i | qt | kk) != 0 ? 1u : 0u);
+            umma_f16_ts(tmem, a_tm + (uint32_t)kk * 8, bd, idesc, (i | qt | kk) != 0 ? 1u : 0u);
           }
           umma_commit(&a_empty[sa]);
         }
@@ -348,15 +373,19 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_q80(const GemmArgs a) {
       if (!__all_sync(0xffffffffu, gwait(&raw_full[s], (uint32_t)(i / kRawStages) & 1u, a.err, abort_s))) break;
       bool ok = true;
       for (int t = 0; t < 2 && ok; ++t) {
-        const int qt = h + 2 * t;
-        if (i > 0 && !__all_sync(0xffffffffu, gwait(&a_empty[qt], (uint32_t)((i - 1) & 1), a.err, abort_s))) {
+        const int qt = h + 2 * t, sa = qt + 4 * (i & 1);
+        if (i > 1 && !__all_sync(0xffffffffu, gwait(&a_empty[sa], (uint32_t)(((i >> 1) - 1) & 1), a.err, abort_s))) {
           ok = false;
           break;
         }
-        dequant_quarter(raw_st + (size_t)s * kRawBytes, a_st + (size_t)qt * kABytes, r, qt);
-        fence_proxy_async();
+        uint32_t aw[32];
+        dequant_quarter(raw_st + (size_t)s * kRawBytes, aw, r, qt);
+        tc_fence_after();  // after the MMAs that read this stage before (a_empty)
+        tmem_st32(tmem + ((uint32_t)((warp & 3) * 32) << 16) + kTmemA + (uint32_t)sa * 32, aw);
+        tmem_wait_st();
+        tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&a_full[qt]);
+        if (lane == 0) mbar_arrive(&a_full[sa]);
       }
       if (!ok) break;
       __syncwarp();
@@ -426,7 +455,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_q80(const GemmArgs a) {
   if (threadIdx.x == 0) pdl_launch_dependents();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 32);
+    tmem_dealloc(tmem, kTmemCols);
   }
 }
 
