@@ -526,10 +526,11 @@ int attn_cluster_cfg() {
   return v;
 }
 
-// CTAs per kv head and sequence of the batched attention: about eight CTAs
-// per SM over the whole batch (B = 32, 8 kv heads: 4), at most the
-// single-sequence count; MCPO_ATTN_BATCH_SPLIT overrides.  The batched
-// attention merges through global memory (16-CTA clusters of many
+// CTAs per kv head and sequence of the batched attention: 4 once the batch
+// supplies 64 or more (sequence, kv head) pairs (measured best at B = 8 and
+// B = 32 with 8 kv heads), else about four CTAs per SM over the batch, at
+// most the single-sequence count; MCPO_ATTN_BATCH_SPLIT overrides.  The
+// batched attention merges through global memory (16-CTA clusters of many
 // sequences schedule poorly).
 int attn_batch_split_cfg(int single, int batch, int n_kv, int sms) {
   static const int v = [] {
@@ -537,7 +538,8 @@ int attn_batch_split_cfg(int single, int batch, int n_kv, int sms) {
     return (e && *e) ? atoi(e) : 0;
   }();
   if (v >= 1 && v <= kAttnMaxCluster) return v;
-  const int per = batch * n_kv > 0 ? 8 * sms / (batch * n_kv) : single;
+  const int pairs = batch * n_kv;
+  const int per = pairs >= 64 ? 4 : (pairs > 0 ? (4 * sms + pairs - 1) / pairs : single);
   return per < 1 ? 1 : (per < single ? per : single);
 }
 
