@@ -202,6 +202,17 @@ MINICPMO_API int minicpmo_gpu_context_qwen3_bind_tp(void *handle, const minicpmo
 MINICPMO_API int minicpmo_gpu_context_qwen3_forward(void *handle, uint32_t token, size_t pos, int flags, float repeat_penalty,
                                        uint32_t *out_token, float *out_top2_gap, float *logits_out, float *hidden_out,
                                        char *error, size_t error_cap);
+/* Forward one caller-given f32 input row (`n` = hidden values, host memory)
+ * at `pos` in place of a token's embedding row, with `placeholder_id` as the
+ * token recorded for it (it joins the repeat penalty's seen set): one step of
+ * qwen3_append_prompt_embeddings (qwen3.uya:2534-2557, which forwards each
+ * span row through qwen3_forward_embedding_runtime and records the
+ * placeholder in prompt_ids).  flags, outputs and errors as
+ * minicpmo_gpu_context_qwen3_forward. */
+MINICPMO_API int minicpmo_gpu_context_qwen3_forward_embedding(void *handle, const float *embedding, size_t n,
+                                                 uint32_t placeholder_id, size_t pos, int flags, float repeat_penalty,
+                                                 uint32_t *out_token, float *out_top2_gap, float *logits_out,
+                                                 float *hidden_out, char *error, size_t error_cap);
 /* Clears the sampler's seen set (a new session, qwen3.uya:2999-3007). */
 MINICPMO_API int minicpmo_gpu_context_qwen3_reset(void *handle, char *error, size_t error_cap);
 

@@ -92,6 +92,7 @@ struct Model {
   void *kc = nullptr, *vc = nullptr;
   size_t kv_layer_elems = 0;
   float *rope_cos = nullptr, *rope_sin = nullptr;
+  float* embed_in = nullptr;  // the caller's input row (qwen3_forward_embedding)
   float* partial = nullptr;
   unsigned* counters = nullptr;
   int n_split = 1;
@@ -478,7 +479,7 @@ void free_model(Model* m) {
   void* bufs[] = {m->hidden, m->normed, m->q,     m->k,       m->v,         m->attn,       m->gate,     m->up,
                   m->fused,  m->tmp,    m->logits, m->xq,     m->aq,        m->fq,         m->kc,       m->vc,
                   m->rope_cos, m->rope_sin, m->partial, m->counters, m->am_scratch, m->am_counter, m->st, m->seen,
-                  m->history, m->stages, m->step_scratch, m->step_trace, m->tp_epoch};
+                  m->history, m->stages, m->step_scratch, m->step_trace, m->tp_epoch, m->embed_in};
   for (void* p : bufs)
     if (p) cudaFree(p);
   if (m->st_host) cudaFreeHost(m->st_host);
@@ -571,7 +572,8 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
   const auto& cf = m.cfg;
   const int h = (int)cf.hidden, f = (int)cf.ffn, hd = (int)cf.head_dim;
   const cudaStream_t s = c->stream;
-  REC(launch_embed(m.tok->dev, m.tok->geom, m.tok->dtype, (int)m.tok->rows, h, &m.st->token, 0, m.hidden, s, true));
+  REC(launch_embed(m.tok->dev, m.tok->geom, m.tok->dtype, (int)m.tok->rows, h, &m.st->token, 0, m.hidden, s, true, 1, 0,
+                   m.embed_in, &m.st->embed_input));
   REC(launch_mark_seen(m.seen, m.st, (int)(m.tp_world > 1 ? m.vocab_global : cf.vocab), s, true));
   const bool tp = m.tp_world > 1;
   if (m.step_ok) {
@@ -1335,7 +1337,7 @@ int bind_model(Ctx* c, const minicpmo_qwen3_config* cfg, char* err, size_t cap, 
       {(void**)&m.partial, attn_partial_floats((int)lc.heads, attn_n_blocks((int)cf.context), (int)hd) * 4},
       {(void**)&m.counters, lc.kv_heads * 4}, {(void**)&m.am_scratch, (size_t)m.am_grid * 3 * 4},
       {(void**)&m.am_counter, 4}, {(void**)&m.st, sizeof(StepState)}, {(void**)&m.seen, (Vg / 32 + 1) * 4},
-      {(void**)&m.history, (size_t)m.history_cap * 4},
+      {(void**)&m.history, (size_t)m.history_cap * 4}, {(void**)&m.embed_in, h * 4},
   };
   for (auto& a : allocs) {
     if (!cuda_ok(c, cudaMalloc(a.p, a.bytes), "qwen3_bind_malloc", err, cap)) {
@@ -2074,24 +2076,37 @@ int minicpmo_gpu_context_qwen3_bind_tp(void* handle, const minicpmo_qwen3_config
   return bind_model(c, config, error, error_cap, rank, world, static_cast<const uint8_t*>(peer_ipc_handles));
 }
 
-int minicpmo_gpu_context_qwen3_forward(void* handle, uint32_t token, size_t pos, int flags, float repeat_penalty,
-                                       uint32_t* out_token, float* out_top2_gap, float* logits_out, float* hidden_out,
-                                       char* error, size_t error_cap) {
-  Ctx* c = (Ctx*)handle;
-  if (!c) return copy_error(error, error_cap, "error: null gpu context"), 0;
-  DeviceGuard g(c);
+}  // extern "C"
+
+namespace {
+
+// One decode step of token `token` at `pos` (qwen3_forward) or, with emb,
+// of the caller's input row with `token` as its placeholder id
+// (qwen3_forward_embedding).
+int forward_impl(Ctx* c, uint32_t token, const float* emb, size_t emb_n, size_t pos, int flags, float repeat_penalty,
+                 uint32_t* out_token, float* out_top2_gap, float* logits_out, float* hidden_out, char* error,
+                 size_t error_cap) {
   if (!c->model) return fail(c, error, error_cap, "error: qwen3 forward: model not bound");
   Model& m = *c->model;
   if (pos >= m.cfg.context)
     return fail(c, error, error_cap, "error: qwen3 forward pos=%zu exceeds runtime_context=%u", pos, m.cfg.context);
   if (token >= vocab_of(m))
     return fail(c, error, error_cap, "error: qwen3 forward token=%u >= vocab=%u", token, vocab_of(m));
+  if (emb && emb_n != m.cfg.hidden)
+    return fail(c, error, error_cap, "error: qwen3 forward_embedding: %zu values, hidden=%u", emb_n, m.cfg.hidden);
   const int which = (flags & 1) ? 1 : 0;
   StepState* hs = m.st_host;
   memset(hs, 0, sizeof(StepState));
   hs->token = (int)token;
   hs->pos = (int)pos;
   hs->penalty = repeat_penalty;
+  hs->embed_input = emb ? 1 : 0;
+  if (emb) {
+    if (!cuda_ok(c, cudaMemcpyAsync(m.embed_in, emb, emb_n * 4, cudaMemcpyHostToDevice, c->stream), "forward_embedding_h2d",
+                 error, error_cap))
+      return 0;
+    c->stats.host_to_device_bytes += emb_n * 4;
+  }
   if (!cuda_ok(c, cudaMemcpyAsync(m.st, hs, sizeof(StepState), cudaMemcpyHostToDevice, c->stream), "forward_state_h2d",
                error, error_cap) ||
       !cuda_ok(c, cudaGraphLaunch(m.exec[which], c->stream), "forward_graph_launch", error, error_cap) ||
@@ -2119,6 +2134,32 @@ int minicpmo_gpu_context_qwen3_forward(void* handle, uint32_t token, size_t pos,
   if (out_token) *out_token = which == 0 ? (uint32_t)hs->next_token : 0u;
   if (out_top2_gap) *out_top2_gap = which == 0 ? hs->gap : 0.0f;
   return 1;
+}
+
+}  // namespace
+
+extern "C" {
+
+int minicpmo_gpu_context_qwen3_forward(void* handle, uint32_t token, size_t pos, int flags, float repeat_penalty,
+                                       uint32_t* out_token, float* out_top2_gap, float* logits_out, float* hidden_out,
+                                       char* error, size_t error_cap) {
+  Ctx* c = (Ctx*)handle;
+  if (!c) return copy_error(error, error_cap, "error: null gpu context"), 0;
+  DeviceGuard g(c);
+  return forward_impl(c, token, nullptr, 0, pos, flags, repeat_penalty, out_token, out_top2_gap, logits_out, hidden_out,
+                      error, error_cap);
+}
+
+int minicpmo_gpu_context_qwen3_forward_embedding(void* handle, const float* embedding, size_t n, uint32_t placeholder_id,
+                                                 size_t pos, int flags, float repeat_penalty, uint32_t* out_token,
+                                                 float* out_top2_gap, float* logits_out, float* hidden_out, char* error,
+                                                 size_t error_cap) {
+  Ctx* c = (Ctx*)handle;
+  if (!c) return copy_error(error, error_cap, "error: null gpu context"), 0;
+  if (!embedding) return fail(c, error, error_cap, "error: qwen3 forward_embedding: null embedding");
+  DeviceGuard g(c);
+  return forward_impl(c, placeholder_id, embedding, n, pos, flags, repeat_penalty, out_token, out_top2_gap, logits_out,
+                      hidden_out, error, error_cap);
 }
 
 int minicpmo_gpu_context_qwen3_reset(void* handle, char* error, size_t error_cap) {

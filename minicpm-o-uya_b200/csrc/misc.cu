@@ -71,9 +71,14 @@ __device__ __forceinline__ uint8_t tb(const uint8_t* w, const TileGeom& g, int r
 // Sequence blockIdx.y reads its token at tok_ptr[y * tok_stride] and
 // writes out + y * hidden.
 __global__ void k_embed(const uint8_t* __restrict__ w, TileGeom g, int dtype, int rows, int hidden, const int* tok_ptr,
-                        int tok_static, float* __restrict__ out, int tok_stride) {
+                        int tok_static, float* __restrict__ out, int tok_stride, const float* __restrict__ in_row,
+                        const int* in_flag) {
   pdl_wait();
   pdl_launch_dependents();
+  if (in_flag && *in_flag) {  // the caller's input row (qwen3_append_prompt_embeddings)
+    for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < hidden; e += gridDim.x * blockDim.x) out[e] = in_row[e];
+    return;
+  }
   const int token = tok_ptr ? tok_ptr[(size_t)blockIdx.y * tok_stride] : tok_static;
   out += (size_t)blockIdx.y * hidden;
   if (token < 0 || token >= rows) {  // never index outside the table; the host validates ids
@@ -286,10 +291,12 @@ cudaError_t launch_relayout(const uint8_t* src, uint8_t* dst, const TileGeom& g,
 }
 
 cudaError_t launch_embed(const uint8_t* w, const TileGeom& g, int dtype, int rows, int hidden, const int* tok_ptr, int tok,
-                         float* out, cudaStream_t st, bool pdl, int batch, int tok_stride) {
+                         float* out, cudaStream_t st, bool pdl, int batch, int tok_stride, const float* in_row,
+                         const int* in_flag) {
   const int grid = (hidden + 255) / 256;
+  if (in_flag && (!in_row || batch > 1)) return cudaErrorInvalidValue;
   return launch_k(k_embed, dim3(grid, batch < 1 ? 1 : batch), dim3(256), 0, st, pdl, w, g, dtype, rows, hidden, tok_ptr,
-                  tok, out, tok_stride);
+                  tok, out, tok_stride, in_row, in_flag);
 }
 
 cudaError_t launch_argmax(const float* logits, int n, const uint32_t* seen_bits, float* scratch, unsigned* counter,

@@ -21,14 +21,17 @@ struct StepState {
   float penalty;    // repeat penalty (<= 1: off)
   int history_len;  // tokens appended to the history buffer while auto-advancing
   int err;
+  int embed_input;  // 1: this step's input row is the caller's embedding (k_embed copies it)
 };
 
 cudaError_t launch_relayout(const uint8_t* src, uint8_t* dst, const TileGeom& g, size_t row_bytes, cudaStream_t st);
 // token (from tok_ptr when non-null) outside [0, rows) yields zeros.  batch
 // sequences: sequence b's token at tok_ptr[b * tok_stride], its row at
-// out + b * hidden.
+// out + b * hidden.  in_flag (optional, single sequence): when *in_flag is
+// nonzero the row is copied from in_row (hidden f32 values) instead.
 cudaError_t launch_embed(const uint8_t* w, const TileGeom& g, int dtype, int rows, int hidden, const int* tok_ptr, int tok,
-                         float* out, cudaStream_t st, bool pdl = false, int batch = 1, int tok_stride = 0);
+                         float* out, cudaStream_t st, bool pdl = false, int batch = 1, int tok_stride = 0,
+                         const float* in_row = nullptr, const int* in_flag = nullptr);
 // grid CTAs; scratch holds 3 floats per CTA; counter is zero at rest.
 // history (may be null) receives next_token at history_len when auto-advancing.
 // vocab_base/tp_top: a tensor-parallel vocab slice -- indices are offset by

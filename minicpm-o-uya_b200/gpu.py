@@ -127,6 +127,7 @@ SIGNATURES = {
     "minicpmo_gpu_context_tp_buffer": (i32, [vp, sz, vp] + E),
     "minicpmo_gpu_context_qwen3_bind_tp": (i32, [vp, C.POINTER(Qwen3Config), i32, i32, vp] + E),
     "minicpmo_gpu_context_qwen3_forward": (i32, [vp, u32, sz, i32, f32, u32ptr, fptr, fptr, fptr] + E),
+    "minicpmo_gpu_context_qwen3_forward_embedding": (i32, [vp, fptr, sz, u32, sz, i32, f32, u32ptr, fptr, fptr, fptr] + E),
     "minicpmo_gpu_context_qwen3_reset": (i32, [vp] + E),
     "minicpmo_gpu_context_qwen3_decode": (i32, [vp, u32, sz, sz, f32, u32ptr] + E),
     "minicpmo_gpu_context_q8_1_quantize": (i32, [vp, fptr, sz, vp] + E),
@@ -346,6 +347,23 @@ class GpuContext:
         gap = f32()
         self._call(
             "minicpmo_gpu_context_qwen3_forward", token, pos, 0 if logits else 1, penalty, C.byref(out), C.byref(gap),
+            _f(want_logits) if want_logits is not None else None,
+            _f(want_hidden) if want_hidden is not None else None,
+        )
+        return int(out.value), float(gap.value)
+
+    def qwen3_forward_embedding(self, embedding, placeholder_id: int, pos: int, logits: bool = True,
+                                penalty: float = 1.0, want_logits: Optional[np.ndarray] = None,
+                                want_hidden: Optional[np.ndarray] = None):
+        """One step on a given f32 input row instead of a token's embedding
+        (qwen3_append_prompt_embeddings, qwen3.uya:2534-2557); the
+        placeholder id joins the repeat penalty's seen set."""
+        e = _as_f32(embedding)
+        out = u32()
+        gap = f32()
+        self._call(
+            "minicpmo_gpu_context_qwen3_forward_embedding", _f(e), e.size, placeholder_id, pos, 0 if logits else 1,
+            penalty, C.byref(out), C.byref(gap),
             _f(want_logits) if want_logits is not None else None,
             _f(want_hidden) if want_hidden is not None else None,
         )

@@ -115,6 +115,29 @@ class Qwen3Runtime:
         self.last_token = nxt
         return nxt, gap
 
+    def append_prompt_embeddings(self, placeholder_id: int, embeddings, penalty: float = 1.0,
+                                 want_logits: Optional[np.ndarray] = None) -> Tuple[int, float]:
+        """qwen3_append_prompt_embeddings (qwen3.uya:2534-2557): each row of
+        embeddings [n][hidden] (f32) is forwarded in place of a token's
+        embedding at the next position, recorded as placeholder_id; logits
+        (and the greedy next token) only for the last row."""
+        e = np.ascontiguousarray(embeddings, np.float32).reshape(-1, self.shape.hidden)
+        n = e.shape[0]
+        if n == 0:
+            return self.last_token, 0.0
+        if self.total_tokens + n > self.context:
+            raise ValueError(f"error: context overflow total_tokens={self.total_tokens} add_embeddings={n} "
+                             f"runtime_context={self.context}")
+        nxt, gap = 0, 0.0
+        for i in range(n):
+            last = i + 1 == n
+            nxt, gap = self.gpu.qwen3_forward_embedding(e[i], placeholder_id, self.total_tokens, logits=last,
+                                                        penalty=penalty, want_logits=want_logits if last else None)
+            self.seen.append(int(placeholder_id))
+            self.total_tokens += 1
+        self.last_token = nxt
+        return nxt, gap
+
     def generate(self, n_new: int, penalty: float = 1.0, stop_token: Optional[int] = None) -> List[int]:
         """Greedy decode after append_prompt_ids; host loop, one forward per token."""
         out = []

@@ -859,7 +859,23 @@ static int mv(const orc_state *st, int dtype, const uint8_t *w, size_t rows, siz
     return orc_matvec_f32(dtype, w, rows, cols, x, y);
 }
 
+static int forward_impl(const orc_model *m, orc_state *st, uint32_t token, const float *emb, size_t pos, float *logits,
+                        float *hidden_out);
+
 int orc_forward_token(const orc_model *m, orc_state *st, uint32_t token, size_t pos, float *logits, float *hidden_out) {
+    return forward_impl(m, st, token, NULL, pos, logits, hidden_out);
+}
+
+/* qwen3.uya:2534-2557 (qwen3_append_prompt_embeddings -> qwen3_forward_embedding_runtime):
+ * the layer stack on a caller-given f32 input row instead of a token's embedding row. */
+int orc_forward_embedding(const orc_model *m, orc_state *st, const float *emb, size_t pos, float *logits,
+                          float *hidden_out) {
+    if (!emb) return 0;
+    return forward_impl(m, st, 0u, emb, pos, logits, hidden_out);
+}
+
+static int forward_impl(const orc_model *m, orc_state *st, uint32_t token, const float *emb, size_t pos, float *logits,
+                        float *hidden_out) {
     size_t h = m->hidden, qd = (size_t) m->heads * m->head_dim, kvd = (size_t) m->kv_heads * m->head_dim;
     size_t f = m->ffn, maxd = h, L;
     size_t emb_rb = orc_row_bytes(m->token_embd_dtype, h);
@@ -876,8 +892,9 @@ int orc_forward_token(const orc_model *m, orc_state *st, uint32_t token, size_t 
     xq = (uint8_t *) calloc(maxd / 32 + 1, 36);
     if (!hid || !nrm || !q || !k || !v || !ctx || !ao || !g || !u || !fu || !dn || !xq) { ok = 0; goto done; }
 
-    /* qwen3.uya:1164-1174: token embedding row */
-    if (!orc_dequant_row(m->token_embd_dtype, m->token_embd + (size_t) token * emb_rb, h, hid)) { ok = 0; goto done; }
+    /* qwen3.uya:1164-1174: token embedding row (or the given input row) */
+    if (emb) memcpy(hid, emb, h * sizeof(float));
+    else if (!orc_dequant_row(m->token_embd_dtype, m->token_embd + (size_t) token * emb_rb, h, hid)) { ok = 0; goto done; }
 
     for (L = 0; L < m->layers && ok; ++L) {
         const orc_layer *lw = &m->layer[L];

@@ -152,6 +152,9 @@ typedef struct orc_state {
 size_t orc_state_kv_floats(const orc_model *m);
 /* logits may be NULL (no lm_head); hidden_out may be NULL. */
 int orc_forward_token(const orc_model *m, orc_state *st, uint32_t token, size_t pos, float *logits, float *hidden_out);
+/* The same on a caller-given f32 input row (qwen3_append_prompt_embeddings, qwen3.uya:2534-2557). */
+int orc_forward_embedding(const orc_model *m, orc_state *st, const float *emb, size_t pos, float *logits,
+                          float *hidden_out);
 
 #ifdef __cplusplus
 }

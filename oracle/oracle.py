@@ -60,6 +60,7 @@ def orc() -> C.CDLL:
             "orc_argmax_penalized": (C.c_uint32, [fp, sz, u32p, sz, C.c_float, fp]),
             "orc_state_kv_floats": (sz, [C.c_void_p]),
             "orc_forward_token": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32, sz, fp, fp]),
+            "orc_forward_embedding": (C.c_int, [C.c_void_p, C.c_void_p, fp, sz, fp, fp]),
             "orc_pool_create": (C.c_void_p, [C.c_int, C.c_char_p]),
             "orc_pool_destroy": (None, [C.c_void_p]),
             "orc_pool_is_reference": (C.c_int, [C.c_void_p]),
@@ -347,6 +348,19 @@ class OracleModel:
                                      _f(lg) if lg is not None else None, _f(hid))
         if not ok:
             raise RuntimeError("oracle forward failed")
+        return lg, hid
+
+    def forward_embedding(self, emb, pos: int, logits: bool = True):
+        """The layer stack on a given f32 input row (qwen3_append_prompt_embeddings, qwen3.uya:2534-2557)."""
+        e = np.ascontiguousarray(emb, np.float32)
+        if e.size != self.shape.hidden:
+            raise ValueError("embedding size != hidden")
+        lg = np.empty(self.shape.vocab, np.float32) if logits else None
+        hid = np.empty(self.shape.hidden, np.float32)
+        ok = orc().orc_forward_embedding(C.byref(self.model), C.byref(self.state), _f(e), pos,
+                                         _f(lg) if lg is not None else None, _f(hid))
+        if not ok:
+            raise RuntimeError("oracle forward_embedding failed")
         return lg, hid
 
     def close(self):

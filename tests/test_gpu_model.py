@@ -210,3 +210,65 @@ def test_persistent_step_vs_oracle(pkg, O, mix):
     from minicpmo_b200 import gguf
 
     run_parity(pkg, O, small_shape(layers=3), getattr(gguf, mix), steps=24, decode_mode=2)
+
+
+@pytest.mark.parametrize("decode_mode", [1, 2])
+def test_prompt_embeddings_match_oracle(pkg, O, decode_mode):
+    """qwen3_append_prompt_embeddings (qwen3.uya:2534-2557): caller-given f32
+    rows forwarded in place of token embeddings, interleaved with tokens, give
+    logits bit-identical to the oracle's device-order forward on the same
+    rows, in the per-operation graph and in the persistent step kernel."""
+    from minicpmo_b200 import gguf
+    from minicpmo_b200.qwen3 import Qwen3Runtime
+
+    shape = small_shape()
+    tensors = build(pkg, shape, gguf.Q4_K_M)
+    rt = Qwen3Runtime.open(tensors, shape=shape, context=shape.context, decode_mode=decode_mode)
+    tmap = {n: (dt, r, c, d) for n, dt, r, c, d in tensors}
+    orc = O.OracleModel(shape, tmap, shape.context, q8_1=True)
+    rng = np.random.default_rng(5)
+    ids = gguf.prompt_ids(10, shape.vocab, seed=9)
+    lg = np.empty(shape.vocab, np.float32)
+    for pos in range(10):
+        if pos in (1, 2, 5, 9):
+            emb = (rng.standard_normal(shape.hidden) * 0.5).astype(np.float32)
+            tok, gap = rt.gpu.qwen3_forward_embedding(emb, 3, pos, want_logits=lg)
+            ref, _ = orc.forward_embedding(emb, pos)
+        else:
+            tok, gap = rt.forward(int(ids[pos]), pos, want_logits=lg)
+            ref, _ = orc.forward(int(ids[pos]), pos)
+        assert np.array_equal(lg, ref), (pos, rel_row_err(lg, ref))
+        tok_ref, gap_ref = O.argmax_penalized(ref)
+        assert tok == tok_ref and gap == gap_ref, pos
+    rt.close()
+    orc.close()
+
+
+def test_runtime_append_prompt_embeddings(pkg, O):
+    """The runtime loop: a span of embedding rows after a token prompt takes
+    one position per row, and its last row's logits and greedy token equal
+    the oracle's; a wrong row length is refused."""
+    from minicpmo_b200 import gguf
+    from minicpmo_b200.qwen3 import Qwen3Runtime
+
+    shape = small_shape()
+    tensors = build(pkg, shape, gguf.Q4_K_M, seed=2)
+    rt = Qwen3Runtime.open(tensors, shape=shape, context=shape.context)
+    tmap = {n: (dt, r, c, d) for n, dt, r, c, d in tensors}
+    orc = O.OracleModel(shape, tmap, shape.context, q8_1=True)
+    ids = [int(t) for t in gguf.prompt_ids(4, shape.vocab, seed=3)]
+    rt.append_prompt_ids(ids)
+    for pos, t in enumerate(ids):
+        orc.forward(t, pos, logits=False)
+    span = (np.random.default_rng(8).standard_normal((3, shape.hidden)) * 0.3).astype(np.float32)
+    lg = np.empty(shape.vocab, np.float32)
+    nxt, _ = rt.append_prompt_embeddings(7, span, want_logits=lg)
+    assert rt.total_tokens == len(ids) + 3
+    for i in range(3):
+        ref, _ = orc.forward_embedding(span[i], len(ids) + i, logits=i == 2)
+    assert np.array_equal(lg, ref)
+    assert nxt == O.argmax_penalized(ref)[0]
+    with pytest.raises(RuntimeError):
+        rt.gpu.qwen3_forward_embedding(np.zeros(shape.hidden - 1, np.float32), 7, rt.total_tokens)
+    rt.close()
+    orc.close()
