@@ -213,6 +213,18 @@ MINICPMO_API int minicpmo_gpu_context_qwen3_forward_embedding(void *handle, cons
                                                  uint32_t placeholder_id, size_t pos, int flags, float repeat_penalty,
                                                  uint32_t *out_token, float *out_top2_gap, float *logits_out,
                                                  float *hidden_out, char *error, size_t error_cap);
+/* qwen3_sample (qwen3.uya:2073-2138) on the logits of the last forward that
+ * computed them: seen[seen_count] is the token history (prompt_ids, with
+ * repeats), *seed_state the xorshift32 state (advanced when a draw is made).
+ * As in the reference, vocabularies above 256 tokens, temperature <= 1e-6
+ * or top_k <= 1 sample greedily (the penalty once per seen token); else the
+ * penalty per history entry, temperature, softmax, top-k, top-p, min-p and
+ * one draw.  Not available under tensor parallelism.  Returns 1, or 0 with
+ * a message in `error`. */
+MINICPMO_API int minicpmo_gpu_context_qwen3_sample(void *handle, const uint32_t *seen, size_t seen_count,
+                                      float temperature, uint32_t top_k, float top_p, float min_p,
+                                      float repeat_penalty, uint32_t *seed_state, uint32_t *out_token, char *error,
+                                      size_t error_cap);
 /* Clears the sampler's seen set (a new session, qwen3.uya:2999-3007). */
 MINICPMO_API int minicpmo_gpu_context_qwen3_reset(void *handle, char *error, size_t error_cap);
 

@@ -93,6 +93,10 @@ struct Model {
   size_t kv_layer_elems = 0;
   float *rope_cos = nullptr, *rope_sin = nullptr;
   float* embed_in = nullptr;  // the caller's input row (qwen3_forward_embedding)
+  // qwen3_sample: the caller's seen list, [seed, token], seen bits, a state
+  uint32_t *smp_seen = nullptr, *smp_io = nullptr, *smp_bits = nullptr;
+  size_t smp_seen_cap = 0;
+  StepState* smp_st = nullptr;
   float* partial = nullptr;
   unsigned* counters = nullptr;
   int n_split = 1;
@@ -479,7 +483,8 @@ void free_model(Model* m) {
   void* bufs[] = {m->hidden, m->normed, m->q,     m->k,       m->v,         m->attn,       m->gate,     m->up,
                   m->fused,  m->tmp,    m->logits, m->xq,     m->aq,        m->fq,         m->kc,       m->vc,
                   m->rope_cos, m->rope_sin, m->partial, m->counters, m->am_scratch, m->am_counter, m->st, m->seen,
-                  m->history, m->stages, m->step_scratch, m->step_trace, m->tp_epoch, m->embed_in};
+                  m->history, m->stages, m->step_scratch, m->step_trace, m->tp_epoch, m->embed_in,
+                  m->smp_seen, m->smp_io, m->smp_bits, m->smp_st};
   for (void* p : bufs)
     if (p) cudaFree(p);
   if (m->st_host) cudaFreeHost(m->st_host);
@@ -2160,6 +2165,70 @@ int minicpmo_gpu_context_qwen3_forward_embedding(void* handle, const float* embe
   DeviceGuard g(c);
   return forward_impl(c, placeholder_id, embedding, n, pos, flags, repeat_penalty, out_token, out_top2_gap, logits_out,
                       hidden_out, error, error_cap);
+}
+
+int minicpmo_gpu_context_qwen3_sample(void* handle, const uint32_t* seen, size_t seen_count, float temperature,
+                                      uint32_t top_k, float top_p, float min_p, float repeat_penalty,
+                                      uint32_t* seed_state, uint32_t* out_token, char* error, size_t error_cap) {
+  Ctx* c = (Ctx*)handle;
+  if (!c) return copy_error(error, error_cap, "error: null gpu context"), 0;
+  DeviceGuard g(c);
+  if (!c->model) return fail(c, error, error_cap, "error: qwen3 sample: model not bound");
+  Model& m = *c->model;
+  if (m.tp_world > 1) return fail(c, error, error_cap, "error: qwen3 sample: not available with tensor parallelism");
+  if (!seed_state || !out_token || (seen_count && !seen))
+    return fail(c, error, error_cap, "error: qwen3 sample: null argument");
+  const int vocab = (int)m.cfg.vocab;
+  if (!m.smp_io) {
+    if (!cuda_ok(c, cudaMalloc((void**)&m.smp_io, 2 * sizeof(uint32_t)), "sample_malloc", error, error_cap) ||
+        !cuda_ok(c, cudaMalloc((void**)&m.smp_bits, ((size_t)vocab / 32 + 1) * 4), "sample_malloc", error, error_cap) ||
+        !cuda_ok(c, cudaMalloc((void**)&m.smp_st, sizeof(StepState)), "sample_malloc", error, error_cap))
+      return 0;
+  }
+  if (seen_count > m.smp_seen_cap) {
+    if (m.smp_seen) cudaFree(m.smp_seen);
+    m.smp_seen = nullptr;
+    m.smp_seen_cap = 0;
+    if (!cuda_ok(c, cudaMalloc((void**)&m.smp_seen, seen_count * 4), "sample_malloc", error, error_cap)) return 0;
+    m.smp_seen_cap = seen_count;
+  }
+  if (seen_count && !cuda_ok(c, cudaMemcpyAsync(m.smp_seen, seen, seen_count * 4, cudaMemcpyHostToDevice, c->stream),
+                             "sample_seen_h2d", error, error_cap))
+    return 0;
+  uint32_t io[2] = {*seed_state, 0u};
+  if (vocab <= 256) {
+    // the reference's whole sampler (greedy or stochastic) on the device
+    if (!cuda_ok(c, cudaMemcpyAsync(m.smp_io, io, sizeof(io), cudaMemcpyHostToDevice, c->stream), "sample_io_h2d", error,
+                 error_cap) ||
+        !cuda_ok(c, launch_sample_small(m.logits, vocab, m.smp_seen, (int)seen_count, temperature, top_k, top_p, min_p,
+                                        repeat_penalty, m.smp_io, c->stream),
+                 "launch_sample", error, error_cap) ||
+        !cuda_ok(c, cudaMemcpyAsync(io, m.smp_io, sizeof(io), cudaMemcpyDeviceToHost, c->stream), "sample_io_d2h", error,
+                 error_cap) ||
+        !cuda_ok(c, cudaStreamSynchronize(c->stream), "sample_sync", error, error_cap))
+      return 0;
+  } else {
+    // above 256 tokens the reference samples greedily (penalty once per seen token)
+    StepState st{};
+    st.penalty = repeat_penalty;
+    if (!cuda_ok(c, cudaMemsetAsync(m.smp_bits, 0, ((size_t)vocab / 32 + 1) * 4, c->stream), "sample_bits_memset",
+                 error, error_cap) ||
+        !cuda_ok(c, launch_seen_bits(m.smp_bits, m.smp_seen, (int)seen_count, vocab, c->stream), "launch_seen_bits",
+                 error, error_cap) ||
+        !cuda_ok(c, cudaMemcpyAsync(m.smp_st, &st, sizeof(st), cudaMemcpyHostToDevice, c->stream), "sample_state_h2d",
+                 error, error_cap) ||
+        !cuda_ok(c, launch_argmax(m.logits, vocab, m.smp_bits, m.am_scratch, m.am_counter, m.smp_st, nullptr, 0, m.am_grid,
+                                  c->stream),
+                 "launch_argmax", error, error_cap) ||
+        !cuda_ok(c, cudaMemcpyAsync(&st, m.smp_st, sizeof(st), cudaMemcpyDeviceToHost, c->stream), "sample_state_d2h",
+                 error, error_cap) ||
+        !cuda_ok(c, cudaStreamSynchronize(c->stream), "sample_sync", error, error_cap))
+      return 0;
+    io[1] = (uint32_t)st.next_token;
+  }
+  *seed_state = io[0];
+  *out_token = io[1];
+  return 1;
 }
 
 int minicpmo_gpu_context_qwen3_reset(void* handle, char* error, size_t error_cap) {

@@ -251,6 +251,139 @@ __global__ void k_mark_seen(uint32_t* bits, const StepState* st, int vocab) {
   if (t >= 0 && t < vocab) atomicOr(&bits[t >> 5], 1u << (t & 31));
 }
 
+// qwen3_sample (qwen3.uya:2073-2138) for vocab <= 256, one CTA of 256
+// threads: greedy (argmax, the penalty once per seen token) unless
+// temperature > 1e-6 and top_k > 1; then the penalty per seen-list entry in
+// list order, logits / temperature, softmax (kernels.uya:149-160: max
+// scan, expf, sequential sum, divisions), the reference's swap selection
+// sort (descending, not stable), top-k, top-p, min-p, renormalisation and
+// one xorshift32 draw (qwen3.uya:2046-2057).  The steps the reference runs
+// in sequence run on one thread, in the same order; the element-wise ones
+// on all.  io[0] = xorshift32 state (in/out), io[1] = the token.
+__global__ void __launch_bounds__(256) k_sample_small(const float* __restrict__ logits, int vocab,
+                                                      const uint32_t* __restrict__ seen, int seen_count, float temp,
+                                                      uint32_t top_k, float top_p, float min_p, float penalty,
+                                                      uint32_t* io) {
+  __shared__ float local[256], probs[256];
+  __shared__ uint32_t order[256];
+  __shared__ unsigned char flag[256];
+  __shared__ float s_max, s_sum;
+  const int t = threadIdx.x;
+  if (t < vocab) {
+    local[t] = logits[t];
+    order[t] = (uint32_t)t;
+    flag[t] = 0;
+  }
+  __syncthreads();
+  if (temp <= 0.000001f || top_k <= 1) {
+    for (int i = t; i < seen_count; i += blockDim.x)
+      if (seen[i] < (uint32_t)vocab) flag[seen[i]] = 1;
+    __syncthreads();
+    if (t == 0) {
+      int best = 0;
+      float bv = local[0];
+      if (penalty > 1.0f && flag[0]) {
+        if (bv > 0.0f) bv = __fdiv_rn(bv, penalty);
+        if (bv < 0.0f) bv = __fmul_rn(bv, penalty);
+      }
+      for (int i = 1; i < vocab; ++i) {
+        float v = local[i];
+        if (penalty > 1.0f && flag[i]) {
+          if (v > 0.0f) v = __fdiv_rn(v, penalty);
+          if (v < 0.0f) v = __fmul_rn(v, penalty);
+        }
+        if (v > bv) {
+          best = i;
+          bv = v;
+        }
+      }
+      io[1] = (uint32_t)best;
+    }
+    return;
+  }
+  if (t == 0 && penalty > 1.0f) {
+    for (int i = 0; i < seen_count; ++i) {
+      const uint32_t s = seen[i];
+      if (s < (uint32_t)vocab) {
+        if (local[s] > 0.0f) local[s] = __fdiv_rn(local[s], penalty);
+        if (local[s] < 0.0f) local[s] = __fmul_rn(local[s], penalty);
+      }
+    }
+  }
+  __syncthreads();
+  if (t < vocab) local[t] = __fdiv_rn(local[t], temp);
+  __syncthreads();
+  if (t == 0) {
+    float m = local[0];
+    for (int i = 1; i < vocab; ++i)
+      if (local[i] > m) m = local[i];
+    s_max = m;
+  }
+  __syncthreads();
+  if (t < vocab) probs[t] = expf(__fsub_rn(local[t], s_max));
+  __syncthreads();
+  if (t == 0) {
+    float sum = 0.0f;
+    for (int i = 0; i < vocab; ++i) sum = __fadd_rn(sum, probs[i]);
+    s_sum = sum;
+  }
+  __syncthreads();
+  if (t < vocab && s_sum != 0.0f) probs[t] = __fdiv_rn(probs[t], s_sum);
+  __syncthreads();
+  if (t != 0) return;
+  for (int a = 0; a < vocab; ++a)
+    for (int b = a + 1; b < vocab; ++b)
+      if (probs[b] > probs[a]) {
+        const float tp = probs[a];
+        const uint32_t ti = order[a];
+        probs[a] = probs[b];
+        probs[b] = tp;
+        order[a] = order[b];
+        order[b] = ti;
+      }
+  int limit = vocab;
+  if (top_k > 0 && top_k < (uint32_t)limit) limit = (int)top_k;
+  float cumulative = 0.0f;
+  int kept = 0;
+  while (kept < limit) {
+    if (kept >= vocab || kept >= 256) break;
+    cumulative = __fadd_rn(cumulative, probs[kept]);
+    kept = kept + 1;
+    if (cumulative >= top_p && top_p < 0.999999f) break;
+  }
+  const float max_prob = probs[0];
+  if (min_p > 0.0f)
+    while (kept > 1) {
+      const int tail = kept - 1;
+      if (tail >= 256 || probs[tail] >= __fmul_rn(max_prob, min_p)) break;
+      kept = kept - 1;
+    }
+  float norm = 0.0f;
+  for (int i = 0; i < kept; ++i) norm = __fadd_rn(norm, probs[i]);
+  uint32_t x = io[0];
+  x ^= x << 13;
+  x ^= x >> 17;
+  x ^= x << 5;
+  io[0] = x;
+  const float r = __fdiv_rn(__uint2float_rn(x), 4294967295.0f);
+  float acc = 0.0f;
+  uint32_t pick = order[0];
+  for (int i = 0; i < kept; ++i) {
+    acc = __fadd_rn(acc, __fdiv_rn(probs[i], norm));
+    if (r <= acc || i + 1 == kept) {
+      pick = order[i];
+      break;
+    }
+  }
+  io[1] = pick;
+}
+
+// Seen bits of a token list (tokens >= vocab ignored).
+__global__ void k_seen_bits(uint32_t* bits, const uint32_t* list, int n, int vocab) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+    if (list[i] < (uint32_t)vocab) atomicOr(&bits[list[i] >> 5], 1u << (list[i] & 31));
+}
+
 // ---------------------------------------------------------------------
 // elementwise slot kernels (gpu_shim.c:649-745)
 // ---------------------------------------------------------------------
@@ -306,6 +439,19 @@ cudaError_t launch_argmax(const float* logits, int n, const uint32_t* seen_bits,
   if (batch > 1 && (seen_bits || tp_top)) return cudaErrorInvalidValue;
   return launch_k(k_argmax, dim3(grid, batch < 1 ? 1 : batch), dim3(256), 0, s, pdl, logits, n, seen_bits, scratch,
                   counter, st, history, history_cap, vocab_base, tp_top);
+}
+
+cudaError_t launch_sample_small(const float* logits, int vocab, const uint32_t* seen, int seen_count, float temp,
+                                uint32_t top_k, float top_p, float min_p, float penalty, uint32_t* io, cudaStream_t st) {
+  if (vocab < 1 || vocab > 256) return cudaErrorInvalidValue;
+  k_sample_small<<<1, 256, 0, st>>>(logits, vocab, seen, seen_count, temp, top_k, top_p, min_p, penalty, io);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_seen_bits(uint32_t* bits, const uint32_t* list, int n, int vocab, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  k_seen_bits<<<(n + 255) / 256, 256, 0, st>>>(bits, list, n, vocab);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_mark_seen(uint32_t* bits, const StepState* st, int vocab, cudaStream_t s, bool pdl) {

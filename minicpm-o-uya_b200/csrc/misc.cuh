@@ -43,6 +43,12 @@ cudaError_t launch_argmax(const float* logits, int n, const uint32_t* seen_bits,
                           StepState* st, int* history, int history_cap, int grid, cudaStream_t s, bool pdl = false,
                           int vocab_base = 0, float* tp_top = nullptr, int batch = 1);
 cudaError_t launch_mark_seen(uint32_t* bits, const StepState* st, int vocab, cudaStream_t s, bool pdl = false);
+// qwen3_sample (qwen3.uya:2073-2138) over vocab <= 256 logits; io[0] the
+// xorshift32 state (in/out), io[1] the token.
+cudaError_t launch_sample_small(const float* logits, int vocab, const uint32_t* seen, int seen_count, float temp,
+                                uint32_t top_k, float top_p, float min_p, float penalty, uint32_t* io, cudaStream_t st);
+// bits |= the tokens of list (those < vocab).
+cudaError_t launch_seen_bits(uint32_t* bits, const uint32_t* list, int n, int vocab, cudaStream_t st);
 cudaError_t launch_add_inplace(float* dst, const float* src, int n, cudaStream_t st);
 cudaError_t launch_silu_mul(float* dst, const float* gate, const float* up, int n, cudaStream_t st);
 cudaError_t launch_head_norm_rope(float* vec, int n_head, int hd, const void* w, int w_dtype, int do_rope,

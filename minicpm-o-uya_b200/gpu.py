@@ -9,7 +9,7 @@ from __future__ import annotations
 
 import ctypes as C
 from dataclasses import dataclass
-from typing import Optional, Sequence
+from typing import Optional, Sequence, Tuple
 
 import numpy as np
 
@@ -128,6 +128,7 @@ SIGNATURES = {
     "minicpmo_gpu_context_qwen3_bind_tp": (i32, [vp, C.POINTER(Qwen3Config), i32, i32, vp] + E),
     "minicpmo_gpu_context_qwen3_forward": (i32, [vp, u32, sz, i32, f32, u32ptr, fptr, fptr, fptr] + E),
     "minicpmo_gpu_context_qwen3_forward_embedding": (i32, [vp, fptr, sz, u32, sz, i32, f32, u32ptr, fptr, fptr, fptr] + E),
+    "minicpmo_gpu_context_qwen3_sample": (i32, [vp, u32ptr, sz, f32, u32, f32, f32, f32, u32ptr, u32ptr] + E),
     "minicpmo_gpu_context_qwen3_reset": (i32, [vp] + E),
     "minicpmo_gpu_context_qwen3_decode": (i32, [vp, u32, sz, sz, f32, u32ptr] + E),
     "minicpmo_gpu_context_q8_1_quantize": (i32, [vp, fptr, sz, vp] + E),
@@ -368,6 +369,16 @@ class GpuContext:
             _f(want_hidden) if want_hidden is not None else None,
         )
         return int(out.value), float(gap.value)
+
+    def qwen3_sample(self, seen, temperature: float, top_k: int, top_p: float, min_p: float, penalty: float,
+                     seed: int) -> Tuple[int, int]:
+        """qwen3_sample (qwen3.uya:2073-2138) on the last forward's logits -> (token, next seed state)."""
+        s = np.ascontiguousarray(np.asarray(seen, dtype=np.uint32))
+        st = u32(seed)
+        out = u32()
+        self._call("minicpmo_gpu_context_qwen3_sample", s.ctypes.data_as(u32ptr), s.size, temperature, top_k, top_p,
+                   min_p, penalty, C.byref(st), C.byref(out))
+        return int(out.value), int(st.value)
 
     def qwen3_reset(self) -> None:
         self._call("minicpmo_gpu_context_qwen3_reset")

@@ -547,6 +547,87 @@ uint32_t orc_argmax_penalized(const float *values, size_t n, const uint32_t *see
 }
 
 
+/* qwen3.uya:2046-2057: xorshift32, and its unit draw value / 4294967295 */
+static uint32_t xorshift32(uint32_t *state) {
+    uint32_t x = *state;
+    x ^= x << 13;
+    x ^= x >> 17;
+    x ^= x << 5;
+    *state = x;
+    return x;
+}
+
+/* qwen3_sample (qwen3.uya:2073-2138): greedy (argmax with the penalty once
+ * per seen token) unless temperature > 1e-6, top_k > 1 and vocab <= 256;
+ * then the penalty per seen-list entry, logits / temperature, softmax
+ * (kernels.uya:149-160), the reference's swap selection sort (descending,
+ * not stable), top-k, top-p, min-p, renormalisation and one xorshift32
+ * draw.  *margin (may be NULL): the smallest |r - running sum| met while
+ * choosing (0 on the greedy path), so callers can tell draws that sit on a
+ * cumulative boundary. */
+uint32_t orc_sample(const float *logits, size_t vocab, const uint32_t *seen, size_t seen_count, float temp,
+                    uint32_t top_k, float top_p, float min_p, float penalty, uint32_t *seed, float *margin) {
+    float local[256], probs[256], maxv, sum, cumulative, max_prob, norm, r, acc, mg = INFINITY;
+    uint32_t order[256];
+    size_t i, a, b, limit, kept;
+    if (margin) *margin = 0.0f;
+    if (temp <= 0.000001f || top_k <= 1 || vocab > 256 || vocab == 0)
+        return orc_argmax_penalized(logits, vocab, seen, seen_count, penalty, NULL);
+    for (i = 0; i < vocab; ++i) { local[i] = logits[i]; order[i] = (uint32_t) i; }
+    if (penalty > 1.0f)
+        for (i = 0; i < seen_count; ++i) {
+            size_t t = seen[i];
+            if (t < vocab) {
+                if (local[t] > 0.0f) local[t] = local[t] / penalty;
+                if (local[t] < 0.0f) local[t] = local[t] * penalty;
+            }
+        }
+    for (i = 0; i < vocab; ++i) local[i] = local[i] / temp;
+    maxv = local[0];
+    for (i = 1; i < vocab; ++i) if (local[i] > maxv) maxv = local[i];
+    sum = 0.0f;
+    for (i = 0; i < vocab; ++i) { probs[i] = expf(local[i] - maxv); sum = sum + probs[i]; }
+    if (sum != 0.0f) for (i = 0; i < vocab; ++i) probs[i] = probs[i] / sum;
+    for (a = 0; a < vocab; ++a)
+        for (b = a + 1; b < vocab; ++b)
+            if (probs[b] > probs[a]) {
+                float tp = probs[a]; uint32_t ti = order[a];
+                probs[a] = probs[b]; probs[b] = tp;
+                order[a] = order[b]; order[b] = ti;
+            }
+    limit = vocab;
+    if (top_k > 0 && top_k < limit) limit = top_k;
+    cumulative = 0.0f;
+    kept = 0;
+    while (kept < limit) {
+        if (kept >= vocab || kept >= 256) break;
+        cumulative = cumulative + probs[kept];
+        kept = kept + 1;
+        if (cumulative >= top_p && top_p < 0.999999f) break;
+    }
+    max_prob = probs[0];
+    if (min_p > 0.0f)
+        while (kept > 1) {
+            size_t tail = kept - 1;
+            if (tail >= 256 || probs[tail] >= max_prob * min_p) break;
+            kept = kept - 1;
+        }
+    norm = 0.0f;
+    for (i = 0; i < kept; ++i) norm = norm + probs[i];
+    r = (float) xorshift32(seed) / 4294967295.0f;
+    acc = 0.0f;
+    for (i = 0; i < kept; ++i) {
+        acc = acc + probs[i] / norm;
+        if (fabsf(r - acc) < mg) mg = fabsf(r - acc);
+        if (r <= acc || i + 1 == kept) {
+            if (margin) *margin = mg;
+            return order[i];
+        }
+    }
+    if (margin) *margin = mg;
+    return order[0];
+}
+
 /* ------------------------------------------------------------------ */
 /* device evaluation order (bit-exact contract with the B200 kernels)  */
 /* ------------------------------------------------------------------ */

@@ -79,6 +79,9 @@ void orc_silu_mul(float *dst, const float *gate, const float *up, size_t n);
  * (penalised) values; gap is +inf when n == 1. */
 uint32_t orc_argmax_penalized(const float *values, size_t n, const uint32_t *seen, size_t seen_count, float penalty,
                               float *top2_gap);
+/* qwen3_sample (qwen3.uya:2073-2138), see oracle.c; *seed is the xorshift32 state. */
+uint32_t orc_sample(const float *logits, size_t vocab, const uint32_t *seen, size_t seen_count, float temp,
+                    uint32_t top_k, float top_p, float min_p, float penalty, uint32_t *seed, float *margin);
 
 /* ---- device evaluation order --------------------------------------------
  * The reference fixes each operation's formula but not the order of float

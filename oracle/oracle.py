@@ -58,6 +58,8 @@ def orc() -> C.CDLL:
             "orc_attention": (C.c_int, [fp, fp, fp, fp, sz, sz, sz, sz, sz, sz]),
             "orc_silu_mul": (None, [fp, fp, fp, sz]),
             "orc_argmax_penalized": (C.c_uint32, [fp, sz, u32p, sz, C.c_float, fp]),
+            "orc_sample": (C.c_uint32, [fp, sz, u32p, sz, C.c_float, C.c_uint32, C.c_float, C.c_float, C.c_float,
+                                        u32p, fp]),
             "orc_state_kv_floats": (sz, [C.c_void_p]),
             "orc_forward_token": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32, sz, fp, fp]),
             "orc_forward_embedding": (C.c_int, [C.c_void_p, C.c_void_p, fp, sz, fp, fp]),
@@ -236,6 +238,18 @@ def argmax_penalized(values: np.ndarray, seen: Sequence[int] = (), penalty: floa
     gap = C.c_float()
     tok = orc().orc_argmax_penalized(_f(v), v.size, s.ctypes.data_as(u32p), s.size, penalty, C.byref(gap))
     return int(tok), float(gap.value)
+
+
+def sample(values: np.ndarray, seen: Sequence[int], temp: float, top_k: int, top_p: float, min_p: float,
+           penalty: float, seed: int):
+    """qwen3_sample (qwen3.uya:2073-2138) -> (token, next seed state, margin of the draw)."""
+    v = np.ascontiguousarray(values, dtype=np.float32)
+    s = np.ascontiguousarray(np.asarray(seen, dtype=np.uint32))
+    st = C.c_uint32(seed)
+    mg = C.c_float()
+    tok = orc().orc_sample(_f(v), v.size, s.ctypes.data_as(u32p), s.size, temp, top_k, top_p, min_p, penalty,
+                           C.byref(st), C.byref(mg))
+    return int(tok), int(st.value), float(mg.value)
 
 
 # ---------------------------------------------------------------------------

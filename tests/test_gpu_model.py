@@ -272,3 +272,55 @@ def test_runtime_append_prompt_embeddings(pkg, O):
         rt.gpu.qwen3_forward_embedding(np.zeros(shape.hidden - 1, np.float32), 7, rt.total_tokens)
     rt.close()
     orc.close()
+
+
+def _sampler_model(pkg, vocab):
+    from minicpmo_b200 import gguf
+    from minicpmo_b200.qwen3 import Qwen3Runtime
+
+    shape = small_shape(vocab=vocab)
+    tensors = build(pkg, shape, gguf.Q4_K_M, seed=4)
+    return shape, Qwen3Runtime.open(tensors, shape=shape, context=shape.context)
+
+
+@pytest.mark.parametrize("vocab", [256, 200])
+def test_device_sampler_matches_reference_restatement(pkg, O, vocab):
+    """qwen3_sample (qwen3.uya:2073-2138) on the device against the oracle's
+    restatement, for vocabularies where the reference samples: penalty per
+    history entry, temperature, softmax, top-k / top-p / min-p and the
+    xorshift32 draw.  Tokens and seed states must agree; the only allowed
+    difference is a draw within 1e-5 of a cumulative boundary (CUDA's expf
+    and libm's may differ in the last bit)."""
+    shape, rt = _sampler_model(pkg, vocab)
+    lg = np.empty(shape.vocab, np.float32)
+    history = [int(t) for t in np.random.default_rng(3).integers(0, shape.vocab, 12)]
+    history += history[:4]  # repeats: the penalty applies once per entry
+    settings = [(0.7, 40, 0.9, 0.05, 1.3), (1.0, 0, 1.0, 0.0, 1.0), (1.5, 8, 0.5, 0.0, 1.1), (0.3, 256, 0.95, 0.2, 1.5),
+                (0.0, 40, 0.9, 0.0, 1.3), (0.8, 1, 0.9, 0.0, 1.2)]
+    seed_gpu = seed_ref = 2463534242
+    near = 0
+    for pos in range(8):
+        rt.forward(int(history[pos]), pos, logits=True, want_logits=lg)
+        for temp, k, p, mp, pen in settings:
+            tok, seed_gpu = rt.gpu.qwen3_sample(history, temp, k, p, mp, pen, seed_gpu)
+            ref, seed_ref, margin = O.sample(lg, history, temp, k, p, mp, pen, seed_ref)
+            assert seed_gpu == seed_ref, (pos, temp, k)
+            if tok != ref:
+                assert margin < 1e-5, (pos, temp, k, tok, ref, margin)
+                near += 1
+    assert near <= 2
+    rt.close()
+
+
+def test_device_sampler_large_vocab_is_greedy(pkg, O):
+    """Above 256 tokens the reference samples greedily whatever the settings:
+    the penalised argmax of the last logits, the seed untouched."""
+    shape, rt = _sampler_model(pkg, 2048)
+    lg = np.empty(shape.vocab, np.float32)
+    history = [5, 9, 9, 700]
+    for pos, t in enumerate(history):
+        rt.forward(t, pos, logits=True, want_logits=lg)
+    tok, seed = rt.gpu.qwen3_sample(history, 0.8, 40, 0.9, 0.05, 1.3, 777)
+    assert seed == 777
+    assert tok == O.argmax_penalized(lg, history, 1.3)[0]
+    rt.close()
