@@ -185,6 +185,26 @@ Q4_K_M = {"attn_q": Q4_K, "attn_k": Q4_K, "attn_v": Q6_K, "attn_output": Q4_K, "
           "ffn_down": Q6_K, "token_embd": Q6_K, "output": Q6_K}
 ALL_Q8_0 = {k: Q8_0 for k in Q4_K_M}
 
+# The per-layer pattern of real llama.cpp Q4_K_M files: attn_v and ffn_down
+# take the higher-precision Q6_K only in the "more bits" layers -- the first
+# and last eighth of the stack and every third layer in between -- and Q4_K
+# elsewhere; token_embd keeps the base Q4_K, the output Q6_K.  (The mixed
+# classes this gives per layer -- q/k/v all Q4_K, or Q4_K with a Q6_K v --
+# are what a loaded real file hands the decode step.)
+Q4_K_M_LAYERED = {**Q4_K_M, "token_embd": Q4_K, "_more_bits": True}
+
+
+def _more_bits(layer: int, n_layers: int) -> bool:
+    return layer < n_layers // 8 or layer >= 7 * n_layers // 8 or (layer - n_layers // 8) % 3 == 2
+
+
+def layer_mix(mix: Dict[str, int], layer: int, n_layers: int) -> Dict[str, int]:
+    """The dtypes of one layer under `mix` (per-layer only for Q4_K_M_LAYERED-style mixes)."""
+    if not mix.get("_more_bits"):
+        return mix
+    hi = _more_bits(layer, n_layers)
+    return {**mix, "attn_v": Q6_K if hi else Q4_K, "ffn_down": Q6_K if hi else Q4_K}
+
 
 def tensor_specs(shape: Qwen3Shape, mix: Dict[str, int]) -> List[Tuple[str, int, int, int, str]]:
     """(name, dtype, rows, cols, kind) in GGUF order; kind 'w' (N(0,0.02)) or 'norm' (1+N(0,0.02))."""
@@ -192,18 +212,19 @@ def tensor_specs(shape: Qwen3Shape, mix: Dict[str, int]) -> List[Tuple[str, int,
     out = [("token_embd.weight", mix["token_embd"], V, h, "w")]
     for l in range(shape.layers):
         p = f"blk.{l}."
+        lm = layer_mix(mix, l, shape.layers)
         out += [
             (p + "attn_norm.weight", F32, 1, h, "norm"),
-            (p + "attn_q.weight", mix["attn_q"], q, h, "w"),
-            (p + "attn_k.weight", mix["attn_k"], kv, h, "w"),
-            (p + "attn_v.weight", mix["attn_v"], kv, h, "w"),
+            (p + "attn_q.weight", lm["attn_q"], q, h, "w"),
+            (p + "attn_k.weight", lm["attn_k"], kv, h, "w"),
+            (p + "attn_v.weight", lm["attn_v"], kv, h, "w"),
             (p + "attn_q_norm.weight", F32, 1, shape.head_dim, "norm"),
             (p + "attn_k_norm.weight", F32, 1, shape.head_dim, "norm"),
-            (p + "attn_output.weight", mix["attn_output"], h, q, "w"),
+            (p + "attn_output.weight", lm["attn_output"], h, q, "w"),
             (p + "ffn_norm.weight", F32, 1, h, "norm"),
-            (p + "ffn_gate.weight", mix["ffn_gate"], f, h, "w"),
-            (p + "ffn_up.weight", mix["ffn_up"], f, h, "w"),
-            (p + "ffn_down.weight", mix["ffn_down"], h, f, "w"),
+            (p + "ffn_gate.weight", lm["ffn_gate"], f, h, "w"),
+            (p + "ffn_up.weight", lm["ffn_up"], f, h, "w"),
+            (p + "ffn_down.weight", lm["ffn_down"], h, f, "w"),
         ]
     out.append(("output_norm.weight", F32, 1, h, "norm"))
     if not shape.tied:

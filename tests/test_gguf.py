@@ -42,3 +42,17 @@ def test_synthetic_seeds_are_stable(pkg):
     b = gguf.synth_tensor("blk.0.attn_q.weight", gguf.Q4_K, 4, 256, "w")
     c = gguf.synth_tensor("blk.1.attn_q.weight", gguf.Q4_K, 4, 256, "w")
     assert np.array_equal(a, b) and not np.array_equal(a, c)
+
+
+def test_layered_q4_k_m_pattern(pkg):
+    """Q4_K_M_LAYERED: attn_v / ffn_down are Q6_K in the first and last
+    eighth of the layers and every third layer between, Q4_K elsewhere."""
+    from minicpmo_b200 import gguf
+
+    shape = gguf.Qwen3Shape(layers=16, hidden=256, heads=4, kv_heads=2, head_dim=64, ffn=512, vocab=300, context=64)
+    specs = {n: dt for n, dt, _, _, _ in gguf.tensor_specs(shape, gguf.Q4_K_M_LAYERED)}
+    hi = [l for l in range(16) if specs[f"blk.{l}.attn_v.weight"] == gguf.Q6_K]
+    assert hi == [0, 1, 4, 7, 10, 13, 14, 15]
+    assert all(specs[f"blk.{l}.ffn_down.weight"] == (gguf.Q6_K if l in hi else gguf.Q4_K) for l in range(16))
+    assert specs["token_embd.weight"] == gguf.Q4_K and specs["output.weight"] == gguf.Q6_K
+    assert all(specs[f"blk.{l}.attn_q.weight"] == gguf.Q4_K for l in range(16))

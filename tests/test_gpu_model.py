@@ -324,3 +324,30 @@ def test_device_sampler_large_vocab_is_greedy(pkg, O):
     assert seed == 777
     assert tok == O.argmax_penalized(lg, history, 1.3)[0]
     rt.close()
+
+
+@pytest.mark.parametrize("decode_mode", [1, 2])
+def test_layered_q4_k_m_file_matches_oracle(pkg, O, tmp_path, decode_mode):
+    """A model with the per-layer dtype pattern of real llama.cpp Q4_K_M files
+    (attn_v / ffn_down Q6_K in some layers, Q4_K in the rest; Q4_K token
+    embeddings), written to a GGUF file and loaded from it, decodes with
+    logits bit-identical to the oracle in both decode modes."""
+    from minicpmo_b200 import gguf
+    from minicpmo_b200.qwen3 import Qwen3Runtime
+
+    shape = small_shape(layers=8)
+    tensors = gguf.synth_model(shape, gguf.Q4_K_M_LAYERED, seed_base=11)
+    path = tmp_path / "layered.gguf"
+    gguf.write_gguf(path, gguf.qwen3_metadata(shape), tensors)
+    rt = Qwen3Runtime.open(str(path), context=shape.context, decode_mode=decode_mode)
+    tmap = {n: (dt, r, c, d) for n, dt, r, c, d in tensors}
+    orc = O.OracleModel(shape, tmap, shape.context, q8_1=True)
+    ids = gguf.prompt_ids(10, shape.vocab, seed=4)
+    lg = np.empty(shape.vocab, np.float32)
+    for pos in range(10):
+        tok, gap = rt.forward(int(ids[pos]), pos, want_logits=lg)
+        ref, _ = orc.forward(int(ids[pos]), pos)
+        assert np.array_equal(lg, ref), (pos, rel_row_err(lg, ref))
+        assert (tok, gap) == O.argmax_penalized(ref), pos
+    rt.close()
+    orc.close()
