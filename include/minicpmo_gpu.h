@@ -225,6 +225,17 @@ MINICPMO_API int minicpmo_gpu_context_qwen3_sample(void *handle, const uint32_t 
                                       float temperature, uint32_t top_k, float top_p, float min_p,
                                       float repeat_penalty, uint32_t *seed_state, uint32_t *out_token, char *error,
                                       size_t error_cap);
+/* Forward the n prompt tokens tokens[0..n) at positions first_pos.. in
+ * passes of up to 4 tokens that stream the weights once per pass (the
+ * reference prefills token by token, qwen3.uya:2485-2506): every token's
+ * arithmetic is that of qwen3_forward, so the KV cache and the last token's
+ * logits and greedy sample (flags bit 0 clear) equal those of n forwards.
+ * The tokens join the penalty's seen set.  Models whose weights are not all
+ * in the tiled GEMV layouts (or under tensor parallelism) are refused with
+ * an error; use qwen3_forward for them. */
+MINICPMO_API int minicpmo_gpu_context_qwen3_prefill(void *handle, const uint32_t *tokens, size_t n, size_t first_pos,
+                                       int flags, float repeat_penalty, uint32_t *out_token,
+                                       float *out_top2_gap, float *logits_out, char *error, size_t error_cap);
 /* Clears the sampler's seen set (a new session, qwen3.uya:2999-3007). */
 MINICPMO_API int minicpmo_gpu_context_qwen3_reset(void *handle, char *error, size_t error_cap);
 

@@ -612,7 +612,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2)
   // blocks (the current position comes from this kernel's prologue), and
   // the norm weights and RoPE row (into registers, or into L1 for the
   // shared-memory norm).
-  const int row0 = z * a.ctx;  // this sequence's first row in the maps
+  const int row0 = a.cache_bstride ? z * a.ctx : 0;  // this sequence's first row in the maps (0: one shared cache)
   if constexpr (C::kAsync) {
     if (threadIdx.x == 0) {
       for (int b = 0; b < NT; ++b) mbar_init(&s_bar[b], 1);
@@ -1002,8 +1002,9 @@ cudaError_t launch_j(const AttnArgs& a, cudaStream_t st, bool pdl) {
   memset(&km, 0, sizeof(km));
   memset(&vm, 0, sizeof(vm));
   if constexpr (J >= 2) {
-    // the sequences' caches must be consecutive [batch][ctx][kv_dim] blocks
-    const int B = a.batch > 1 ? a.batch : 1;
+    // the sequences' caches must be consecutive [batch][ctx][kv_dim] blocks,
+    // or one cache they all read (cache_bstride 0: the tokens of one prompt)
+    const int B = a.batch > 1 && a.cache_bstride ? a.batch : 1;
     const int kv_dim = a.n_kv * hd;
     if (B > 1 && a.cache_bstride != (size_t)a.ctx * kv_dim) return cudaErrorInvalidValue;
     const unsigned long long rows = (unsigned long long)B * a.ctx;

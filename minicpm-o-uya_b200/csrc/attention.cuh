@@ -40,7 +40,8 @@ struct AttnArgs {
   float* out;          // [n_head*head_dim]
   uint8_t* out_q8;     // optional Q8_1 of out (needs head_dim % 32 == 0)
   // independent sequences (grid z): sequence b reads q/k/v at + b*qkv_bstride
-  // floats, its caches at + b*cache_bstride elements, its position at
+  // floats, its caches at + b*cache_bstride elements (0: every z reads the
+  // same cache -- the tokens of one prompt, non-fused mode), its position at
   // pos_ptr[b * pos_stride] (pos_static when pos_ptr is null), and writes out at
   // + b*out_bstride floats and out_q8 at + b*outq8_bstride bytes.  batch 0
   // means 1.

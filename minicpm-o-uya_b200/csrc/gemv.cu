@@ -113,6 +113,68 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1) k_gemv(const Gemv
   gemv_items<kClass, kDots>(a, x, ring, full, empty, S, slot, wr0, nwr, NC, warp, lane, n, nullptr);
 }
 
+// The same GEMV over a.nvec (2..kGemvMaxVec) input vectors: one x region per
+// vector (built with the one-vector prologue), the weights streamed once.
+template <int kClass>
+__global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1) k_gemv_multi(const GemvArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int cols = a.cols;
+  const int S = a.stages;
+  const int slot = a.slot_bytes;
+  const int nvec = a.nvec;
+  const size_t xb = gemv_x_bytes(cols);
+  const int NC = (int)(blockDim.x >> 5) - 1;
+  uint8_t* ring = smem + (size_t)nvec * xb;
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + (size_t)NC * S * slot);
+  uint64_t* empty = full + NC * S;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int T = a.total_wr, G = gridDim.x;
+  const int wr0 = (int)((long long)blockIdx.x * T / G);
+  const int wr1 = (int)((long long)(blockIdx.x + 1) * T / G);
+  const int nwr = wr1 - wr0;
+  const int spi = a.seg[0].ks * (a.seg[0].epi == kEpiSwiglu ? 2 : 1);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NC * S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
+  if (warp == NC) {  // producer, as k_gemv
+    const int w = lane;
+    if (w >= NC) return;
+    const int steps = (nwr > w ? (nwr - w + NC - 1) / NC : 0) * spi;
+    const uint64_t policy = l2_evict_first_policy();
+    for (int n = 0; n < steps; ++n) {
+      const int sidx = n % S;
+      if (n >= S && !mbar_wait(&empty[w * S + sidx], (uint32_t)((n / S) - 1) & 1u, a.err)) break;
+      const int item = n / spi, rem = n % spi, part = rem / a.seg[0].ks, k = rem % a.seg[0].ks;
+      const int wr = wr0 + w + NC * item;
+      const GemvSeg& sg = seg_of(a, wr);
+      const uint8_t* src = (part ? sg.w2 : sg.w) + (size_t)(wr - sg.wr_begin) * sg.wr_bytes + (size_t)k * sg.step_bytes;
+      mbar_arrive_expect_tx(&full[w * S + sidx], (uint32_t)sg.step_bytes);
+      bulk_load_hint(ring + (size_t)(w * S + sidx) * slot, src, (uint32_t)sg.step_bytes, &full[w * S + sidx], policy);
+    }
+    for (int n = steps - S > 0 ? steps - S : 0; n < steps; ++n)
+      if (!mbar_wait(&full[w * S + n % S], (uint32_t)(n / S) & 1u, a.err)) return;
+    return;
+  }
+  pdl_wait();
+  XShared xv[kGemvMaxVec];
+  for (int v = 0; v < nvec; ++v) {
+    GemvArgs av = a;
+    av.xf = a.xf ? a.xf + (size_t)v * a.x_stride : nullptr;
+    av.xq = a.xq ? a.xq + (size_t)v * a.xq_stride : nullptr;
+    gemv_build_x(av, smem + (size_t)v * xb, NC, warp, lane);
+    asm volatile("bar.sync 1, %0;" ::"r"(NC * 32) : "memory");
+  }
+  for (int v = 0; v < kGemvMaxVec; ++v) xv[v] = gemv_x_view(smem + (size_t)(v < nvec ? v : 0) * xb, cols);
+  if (threadIdx.x == 0) pdl_launch_dependents();
+  gemv_items_multi<kClass>(a, xv, nvec, ring, full, empty, S, slot, wr0, nwr, NC, warp, lane);
+}
+
 // ---------------------------------------------------------------------
 // Q8_1 producers
 // ---------------------------------------------------------------------
@@ -232,12 +294,16 @@ int consumers_cfg() {
 
 template <int kClass, bool kDots>
 cudaError_t set_smem_attr() {
-  return cudaFuncSetAttribute(k_gemv<kClass, kDots>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  cudaError_t e = cudaFuncSetAttribute(k_gemv<kClass, kDots>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  if (e == cudaSuccess && !kDots)
+    e = cudaFuncSetAttribute(k_gemv_multi<kClass>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  return e;
 }
 
 template <int kClass>
 cudaError_t launch_class(const GemvArgs& a, int grid, int nc, size_t smem, cudaStream_t st, bool pdl) {
   const dim3 block((nc + 1) * 32);
+  if (a.nvec > 1) return launch_k(k_gemv_multi<kClass>, dim3(grid), block, smem, st, pdl, a);
   if (a.dots) return launch_k(k_gemv<kClass, true>, dim3(grid), block, smem, st, pdl, a);
   return launch_k(k_gemv<kClass, false>, dim3(grid), block, smem, st, pdl, a);
 }
@@ -285,7 +351,8 @@ cudaError_t launch_gemv(GemvArgs& a, int grid, cudaStream_t st, bool pdl) {
   const int stages = stages_cfg() < 1 ? 1 : stages_cfg();
   a.stages = stages;
   if (wr == 0) return cudaSuccess;
-  const size_t xb = gemv_x_bytes(a.cols);
+  if (a.nvec > kGemvMaxVec || (a.nvec > 1 && a.dots)) return cudaErrorInvalidValue;
+  const size_t xb = gemv_x_bytes(a.cols) * (size_t)(a.nvec > 1 ? a.nvec : 1);
   const size_t per_warp = (size_t)stages * (slot + 16);
   int nc = kGemvSmemBudget > xb ? (int)((kGemvSmemBudget - xb) / per_warp) : 0;
   const int want = consumers_cfg() > kMaxConsumers ? kMaxConsumers : consumers_cfg();

@@ -58,7 +58,15 @@ struct GemvArgs {
   float eps;
   int* dots;           // optional: per-block integer dots, [row][block] (parity tests)
   int* err;            // set to 1 when a bounded wait gives up
+  // several input vectors against one pass over the weights (prompt
+  // prefill): vector n reads xf + n*x_stride (floats) or xq + n*xq_stride
+  // (bytes) and writes y + n*y_stride (floats) of each segment; nvec <= 1:
+  // one vector
+  int nvec;
+  int x_stride, xq_stride, y_stride;
 };
+
+constexpr int kGemvMaxVec = 4;  // input vectors per multi-vector launch
 
 // Fills seg from a tile geometry.
 inline void gemv_seg_from_geom(const TileGeom& g, const uint8_t* w, const uint8_t* w2, float* y, int epi,

@@ -582,4 +582,59 @@ __device__ __forceinline__ bool gemv_items(const GemvArgs& a, const XShared& x, 
   return true;
 }
 
+// gemv_items over nvec (<= kGemvMaxVec) input vectors: each step block is
+// dotted with every vector (the same step_value per vector as the one-vector
+// loop, so every vector's rows get the bits a one-vector launch gives).
+template <int kClass>
+__device__ __forceinline__ bool gemv_items_multi(const GemvArgs& a, const XShared* xv, int nvec, uint8_t* ring,
+                                                 uint64_t* full, uint64_t* empty, int S, int slot, int wr0, int nwr,
+                                                 int NC, int warp, int lane) {
+  const bool swiglu = a.seg[0].epi == kEpiSwiglu;
+  const int ks = a.seg[0].ks;
+  const int items = nwr > warp ? (nwr - warp + NC - 1) / NC : 0;
+  int n = 0;
+  for (int item = 0; item < items; ++item) {
+    const int wr = wr0 + warp + NC * item;
+    const GemvSeg s = seg_of(a, wr);
+    const int local = wr - s.wr_begin;
+    const int row_in_warp = lane / s.lpr, lane_in_row = lane % s.lpr;
+    const int row = local * s.rpw + row_in_warp;
+    const bool add = !swiglu && s.epi == kEpiAdd && lane_in_row == 0 && row < s.rows;
+    float yold[kGemvMaxVec];
+#pragma unroll
+    for (int v = 0; v < kGemvMaxVec; ++v) yold[v] = add && v < nvec ? s.y[(size_t)v * a.y_stride + row] : 0.0f;
+    float acc[kGemvMaxVec][2];
+#pragma unroll
+    for (int v = 0; v < kGemvMaxVec; ++v) acc[v][0] = acc[v][1] = 0.0f;
+    for (int part = 0; part < (swiglu ? 2 : 1); ++part) {
+      for (int k = 0; k < ks; ++k, ++n) {
+        const int sidx = n % S;
+        if (!mbar_wait_sleep(&full[warp * S + sidx], (uint32_t)(n / S) & 1u, a.err)) return false;
+        const uint8_t* blk = ring + (size_t)(warp * S + sidx) * slot;
+#pragma unroll
+        for (int v = 0; v < kGemvMaxVec; ++v)
+          if (v < nvec)
+            acc[v][part] = __fadd_rn(acc[v][part],
+                                     step_value<kClass, false>(s.dtype, blk, lane, xv[v], k * s.lpr + lane_in_row, nullptr));
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[warp * S + sidx]);
+      }
+    }
+#pragma unroll
+    for (int v = 0; v < kGemvMaxVec; ++v) {
+      if (v < nvec) {
+        float* y = s.y + (size_t)v * a.y_stride;
+        const float g = reduce_row(acc[v][0], s.lpr);
+        if (swiglu) {
+          const float u = reduce_row(acc[v][1], s.lpr);
+          if (lane_in_row == 0 && row < s.rows) y[row] = silu_mul_det(g, u);
+        } else if (lane_in_row == 0 && row < s.rows) {
+          y[row] = add ? __fadd_rn(yold[v], g) : g;
+        }
+      }
+    }
+  }
+  return true;
+}
+
 }  // namespace mcpo

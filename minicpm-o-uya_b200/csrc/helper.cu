@@ -97,6 +97,11 @@ struct Model {
   uint32_t *smp_seen = nullptr, *smp_io = nullptr, *smp_bits = nullptr;
   size_t smp_seen_cap = 0;
   StepState* smp_st = nullptr;
+  // prompt prefill (qwen3_prefill): up to kGemvMaxVec tokens per pass
+  float *pf_hidden = nullptr, *pf_q = nullptr, *pf_k = nullptr, *pf_v = nullptr, *pf_attn = nullptr,
+        *pf_fused = nullptr, *pf_partial = nullptr;
+  int *pf_tok = nullptr, *pf_pos = nullptr, *pf_err = nullptr;
+  unsigned* pf_counters = nullptr;
   float* partial = nullptr;
   unsigned* counters = nullptr;
   int n_split = 1;
@@ -484,7 +489,9 @@ void free_model(Model* m) {
                   m->fused,  m->tmp,    m->logits, m->xq,     m->aq,        m->fq,         m->kc,       m->vc,
                   m->rope_cos, m->rope_sin, m->partial, m->counters, m->am_scratch, m->am_counter, m->st, m->seen,
                   m->history, m->stages, m->step_scratch, m->step_trace, m->tp_epoch, m->embed_in,
-                  m->smp_seen, m->smp_io, m->smp_bits, m->smp_st};
+                  m->smp_seen, m->smp_io, m->smp_bits, m->smp_st, m->pf_hidden, m->pf_q, m->pf_k, m->pf_v,
+                  m->pf_attn, m->pf_fused, m->pf_partial, m->pf_tok, m->pf_pos, m->pf_counters,
+                  m->pf_err};
   for (void* p : bufs)
     if (p) cudaFree(p);
   if (m->st_host) cudaFreeHost(m->st_host);
@@ -2228,6 +2235,221 @@ int minicpmo_gpu_context_qwen3_sample(void* handle, const uint32_t* seen, size_t
   }
   *seed_state = io[0];
   *out_token = io[1];
+  return 1;
+}
+
+}  // extern "C"
+
+namespace {
+
+// Whether a bound model can prefill with multi-token GEMVs: every linear
+// weight in the tiled GEMV layouts (q/k/v groupable, gate/up alike), head
+// size a multiple of 32 up to 256 (TMA-tiled attention), no tensor
+// parallelism.
+bool prefill_ok(const Model& m) {
+  const auto& cf = m.cfg;
+  if (m.tp_world > 1 || cf.head_dim % 32 || cf.head_dim > 256 || !m.out || !m.out->tiled) return false;
+  for (const LayerW& L : m.layer) {
+    Upload* qkv[3] = {L.q, L.k, L.v};
+    if (!groupable(qkv, 3) || !L.o->tiled || !L.down->tiled || !L.gate->tiled || !L.up->tiled ||
+        L.gate->dtype != L.up->dtype || L.gate->rows != L.up->rows)
+      return false;
+  }
+  return true;
+}
+
+bool prefill_alloc(Ctx* c, Model& m, char* err, size_t cap) {
+  if (m.pf_hidden) return true;
+  const auto& cf = m.cfg;
+  const size_t N = kGemvMaxVec, h = cf.hidden, qd = m.qd, f = cf.ffn, hd = cf.head_dim;
+  struct {
+    void** p;
+    size_t bytes;
+  } allocs[] = {
+      {(void**)&m.pf_hidden, N * h * 4}, {(void**)&m.pf_q, N * qd * 4},   {(void**)&m.pf_k, N * qd * 4},
+      {(void**)&m.pf_v, N * qd * 4},     {(void**)&m.pf_attn, N * qd * 4}, {(void**)&m.pf_fused, N * f * 4},
+      {(void**)&m.pf_tok, N * 4},        {(void**)&m.pf_pos, N * 4},
+      {(void**)&m.pf_partial, N * attn_partial_floats((int)cf.heads, attn_n_blocks((int)cf.context), (int)hd) * 4},
+      {(void**)&m.pf_counters, N * cf.kv_heads * 4}, {(void**)&m.pf_err, 4},
+  };
+  for (auto& a : allocs)
+    if (!cuda_ok(c, cudaMalloc(a.p, a.bytes), "prefill_malloc", err, cap)) return false;
+  return cuda_ok(c, cudaMemsetAsync(m.pf_counters, 0, N * cf.kv_heads * 4, c->stream), "prefill_memset", err, cap);
+}
+
+// n (<= kGemvMaxVec) prompt tokens at positions p0.. in one pass over the
+// weights: each token's arithmetic is that of a decode step (same Q8_1
+// activations and dot orders, same attention and norms), so the cache and
+// the last token's logits equal those of token-by-token forwards.
+int prefill_chunk(Ctx* c, Model& m, const uint32_t* toks, int n, size_t p0, bool logits, float penalty, char* err,
+                  size_t cap) {
+  const auto& cf = m.cfg;
+  const int h = (int)cf.hidden, qd = (int)m.qd, f = (int)cf.ffn, hd = (int)cf.head_dim;
+  const size_t esz = cf.kv_f16 ? 2 : 4;
+  const cudaStream_t s = c->stream;
+  int ht[kGemvMaxVec], hp[kGemvMaxVec];
+  for (int i = 0; i < n; ++i) {
+    ht[i] = (int)toks[i];
+    hp[i] = (int)(p0 + i);
+  }
+  auto ok = [&](cudaError_t e, const char* what) { return cuda_ok(c, e, what, err, cap); };
+  if (!ok(cudaMemcpyAsync(m.pf_tok, ht, n * 4, cudaMemcpyHostToDevice, s), "prefill_tok_h2d") ||
+      !ok(cudaMemcpyAsync(m.pf_pos, hp, n * 4, cudaMemcpyHostToDevice, s), "prefill_pos_h2d") ||
+      !ok(launch_embed(m.tok->dev, m.tok->geom, m.tok->dtype, (int)m.tok->rows, h, m.pf_tok, 0, m.pf_hidden, s, false, n,
+                       1),
+          "prefill_embed") ||
+      !ok(launch_seen_bits(m.seen, reinterpret_cast<const uint32_t*>(m.pf_tok), n, (int)cf.vocab, s), "prefill_seen"))
+    return 0;
+  c->stats.host_to_device_bytes += (size_t)n * 8;
+  for (uint32_t li = 0; li < cf.layers; ++li) {
+    const LayerW& L = m.layer[li];
+    GemvArgs a{};
+    a.nseg = 3;
+    a.cols = h;
+    norm_input(&a, m.pf_hidden, L.attn_norm, cf.rms_eps);
+    a.err = m.pf_err;
+    a.nvec = n;
+    a.x_stride = h;
+    a.y_stride = qd;
+    Upload* qkv[3] = {L.q, L.k, L.v};
+    float* ys[3] = {m.pf_q, m.pf_k, m.pf_v};
+    for (int i = 0; i < 3; ++i) gemv_seg_from_geom(qkv[i]->geom, qkv[i]->dev, nullptr, ys[i], kEpiStore, &a.seg[i]);
+    if (!ok(launch_gemv(a, m.grid_h, s, false), "prefill_qkv")) return 0;
+    uint8_t* kc = (uint8_t*)m.kc + li * m.kv_layer_elems * esz;
+    uint8_t* vc = (uint8_t*)m.vc + li * m.kv_layer_elems * esz;
+    if (!ok(launch_prompt_qk(m.pf_q, m.pf_k, m.pf_v, qd, n, (int)cf.heads, (int)cf.kv_heads, hd,
+                             L.q_norm ? L.q_norm->dev : nullptr, L.q_norm ? L.q_norm->dtype : 0,
+                             L.k_norm ? L.k_norm->dev : nullptr, L.k_norm ? L.k_norm->dtype : 0, m.rope_cos,
+                             m.rope_sin, cf.rope_freq_base, cf.rope_freq_scale, m.pf_pos, kc, vc, cf.kv_f16, s),
+            "prefill_qk"))
+      return 0;
+    AttnArgs at{};
+    at.q = m.pf_q;
+    at.fuse_norm_rope_append = 0;
+    at.k_cache = kc;
+    at.v_cache = vc;
+    at.kv_f16 = cf.kv_f16;
+    at.pos_ptr = m.pf_pos;
+    at.pos_stride = 1;
+    at.n_head = (int)cf.heads;
+    at.n_kv = (int)cf.kv_heads;
+    at.head_dim = hd;
+    at.ctx = (int)cf.context;
+    at.n_split = m.n_split;
+    at.cluster = 0;
+    at.scale = 1.0f / sqrtf((float)hd);
+    at.partial = m.pf_partial;
+    at.counters = m.pf_counters;
+    at.out = m.pf_attn;
+    at.batch = n;
+    at.qkv_bstride = (size_t)qd;
+    at.cache_bstride = 0;
+    at.out_bstride = (size_t)qd;
+    at.err = m.pf_err;
+    if (!ok(launch_attention(at, s, false), "prefill_attention")) return 0;
+    GemvArgs o{};
+    o.nseg = 1;
+    o.cols = qd;
+    o.input = kInF32;
+    o.xf = m.pf_attn;
+    o.err = m.pf_err;
+    o.nvec = n;
+    o.x_stride = qd;
+    o.y_stride = h;
+    gemv_seg_from_geom(L.o->geom, L.o->dev, nullptr, m.pf_hidden, kEpiAdd, &o.seg[0]);
+    if (!ok(launch_gemv(o, m.grid_q, s, false), "prefill_o")) return 0;
+    GemvArgs g{};
+    g.nseg = 1;
+    g.cols = h;
+    norm_input(&g, m.pf_hidden, L.ffn_norm, cf.rms_eps);
+    g.err = m.pf_err;
+    g.nvec = n;
+    g.x_stride = h;
+    g.y_stride = f;
+    gemv_seg_from_geom(L.gate->geom, L.gate->dev, L.up->dev, m.pf_fused, kEpiSwiglu, &g.seg[0]);
+    if (!ok(launch_gemv(g, m.grid_h, s, false), "prefill_gateup")) return 0;
+    GemvArgs d{};
+    d.nseg = 1;
+    d.cols = f;
+    d.input = kInF32;
+    d.xf = m.pf_fused;
+    d.err = m.pf_err;
+    d.nvec = n;
+    d.x_stride = f;
+    d.y_stride = h;
+    gemv_seg_from_geom(L.down->geom, L.down->dev, nullptr, m.pf_hidden, kEpiAdd, &d.seg[0]);
+    if (!ok(launch_gemv(d, m.grid_f, s, false), "prefill_down")) return 0;
+  }
+  if (logits) {
+    GemvArgs o{};
+    o.nseg = 1;
+    o.cols = h;
+    norm_input(&o, m.pf_hidden + (size_t)(n - 1) * h, m.out_norm, cf.rms_eps);
+    o.err = m.pf_err;
+    gemv_seg_from_geom(m.out->geom, m.out->dev, nullptr, m.logits, kEpiStore, &o.seg[0]);
+    StepState* hs = m.st_host;
+    memset(hs, 0, sizeof(StepState));
+    hs->token = ht[n - 1];
+    hs->pos = hp[n - 1];
+    hs->penalty = penalty;
+    if (!ok(launch_gemv(o, m.grid_h, s, false), "prefill_lm_head") ||
+        !ok(cudaMemcpyAsync(m.st, hs, sizeof(StepState), cudaMemcpyHostToDevice, s), "prefill_state_h2d") ||
+        !ok(launch_argmax(m.logits, (int)cf.vocab, m.seen, m.am_scratch, m.am_counter, m.st, m.history, m.history_cap,
+                          m.am_grid, s, false),
+            "prefill_argmax"))
+      return 0;
+  }
+  return 1;
+}
+
+}  // namespace
+
+extern "C" {
+
+int minicpmo_gpu_context_qwen3_prefill(void* handle, const uint32_t* tokens, size_t n, size_t first_pos, int flags,
+                                       float repeat_penalty, uint32_t* out_token, float* out_top2_gap,
+                                       float* logits_out, char* error, size_t error_cap) {
+  Ctx* c = (Ctx*)handle;
+  if (!c) return copy_error(error, error_cap, "error: null gpu context"), 0;
+  DeviceGuard g(c);
+  if (!c->model) return fail(c, error, error_cap, "error: qwen3 prefill: model not bound");
+  Model& m = *c->model;
+  if (!tokens || n == 0) return fail(c, error, error_cap, "error: qwen3 prefill: empty prompt");
+  if (first_pos + n > m.cfg.context)
+    return fail(c, error, error_cap, "error: qwen3 prefill exceeds context pos=%zu n=%zu context=%u", first_pos, n,
+                m.cfg.context);
+  for (size_t i = 0; i < n; ++i)
+    if (tokens[i] >= m.cfg.vocab)
+      return fail(c, error, error_cap, "error: qwen3 prefill token=%u >= vocab=%u", tokens[i], m.cfg.vocab);
+  if (!prefill_ok(m))
+    return fail(c, error, error_cap, "error: qwen3 prefill: this model needs token-by-token forwards");
+  if (!prefill_alloc(c, m, error, error_cap)) return 0;
+  if (!cuda_ok(c, cudaMemsetAsync(m.pf_err, 0, sizeof(int), c->stream), "prefill_err_clear", error, error_cap))
+    return 0;
+  const bool want = !(flags & 1);
+  for (size_t i0 = 0; i0 < n; i0 += kGemvMaxVec) {
+    const int cn = (int)(n - i0 < (size_t)kGemvMaxVec ? n - i0 : kGemvMaxVec);
+    if (!prefill_chunk(c, m, tokens + i0, cn, first_pos + i0, want && i0 + cn == n, repeat_penalty, error, error_cap))
+      return 0;
+  }
+  StepState* hs = m.st_host;
+  if (!cuda_ok(c, cudaMemcpyAsync(hs, m.st, sizeof(StepState), cudaMemcpyDeviceToHost, c->stream), "prefill_state_d2h",
+               error, error_cap))
+    return 0;
+  if (want && logits_out &&
+      !cuda_ok(c, cudaMemcpyAsync(logits_out, m.logits, (size_t)m.cfg.vocab * 4, cudaMemcpyDeviceToHost, c->stream),
+               "prefill_logits_d2h", error, error_cap))
+    return 0;
+  int perr = 0;
+  if (!cuda_ok(c, cudaMemcpyAsync(&perr, m.pf_err, sizeof(int), cudaMemcpyDeviceToHost, c->stream), "prefill_err_d2h",
+               error, error_cap))
+    return 0;
+  if (!cuda_ok(c, cudaStreamSynchronize(c->stream), "prefill_sync", error, error_cap)) return 0;
+  if (perr || (want && hs->err))
+    return fail(c, error, error_cap, "error: qwen3 prefill: a device-side check failed (a bounded wait gave up, or a position outside the cache)");
+  c->stats.attention_kernel_calls += m.cfg.layers * ((n + kGemvMaxVec - 1) / kGemvMaxVec);
+  if (out_token) *out_token = want ? (uint32_t)hs->next_token : 0u;
+  if (out_top2_gap) *out_top2_gap = want ? hs->gap : 0.0f;
   return 1;
 }
 

@@ -5,6 +5,7 @@
 
 #include <math.h>
 
+#include "attn_dev.cuh"
 #include "gemv.cuh"
 #include "rowops.cuh"
 #include "tma.cuh"
@@ -412,7 +413,55 @@ __global__ void k_head_norm_rope(float* vec, int n_head, int hd, const void* w, 
   for (int d = lane; d < hd; d += 32) vec[(size_t)h * hd + d] = row[d];
 }
 
+// Prompt prefill: for token t of a chunk (position pos[t]), the per-head
+// QK-RMSNorm + RoPE of its q and k heads in place (norm_rope_row, as the
+// decode step's attention prologue) and the append of its k and v rows to
+// the cache (the value the cache stores: f16-rounded for an f16 cache).
+// One warp per head, q heads first; rows of q/k/v `stride` floats apart.
+template <typename T>
+__global__ void k_prompt_qk(float* q, float* k, const float* v, int stride, int n_head, int n_kv, int hd,
+                            const void* qn, int qndt, const void* kn, int kndt, const float* cos_t,
+                            const float* sin_t, float base, float fscale, const int* pos, void* kc, void* vc) {
+  __shared__ float row_s[4][256];
+  __shared__ float sq_s[4][256];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x, hh = blockIdx.y * 4 + warp;
+  if (hh >= n_head + n_kv) return;
+  const int p = pos[t];
+  const bool isq = hh < n_head;
+  const int h = isq ? hh : hh - n_head;
+  float* vec = (isq ? q : k) + (size_t)t * stride + (size_t)h * hd;
+  float* row = row_s[warp];
+  for (int d = lane; d < hd; d += 32) row[d] = vec[d];
+  __syncwarp();
+  norm_rope_row(row, sq_s[warp], hd, isq ? qn : kn, isq ? qndt : kndt, true, cos_t, sin_t, base, fscale, p, lane);
+  for (int d = lane; d < hd; d += 32) vec[d] = row[d];
+  if (!isq) {
+    const size_t at = (size_t)p * n_kv * hd + (size_t)h * hd;
+    const float* vr = v + (size_t)t * stride + (size_t)h * hd;
+    for (int d = lane; d < hd; d += 32) {
+      kv_store<T>(kc, at + d, row[d]);
+      kv_store<T>(vc, at + d, vr[d]);
+    }
+  }
+}
+
 }  // namespace
+
+cudaError_t launch_prompt_qk(float* q, float* k, const float* v, int stride, int n_tok, int n_head, int n_kv, int hd,
+                             const void* qn, int qndt, const void* kn, int kndt, const float* cos_t, const float* sin_t,
+                             float base, float fscale, const int* pos, void* kc, void* vc, int kv_f16,
+                             cudaStream_t st) {
+  if (hd > 256 || n_tok < 1) return cudaErrorInvalidValue;
+  const dim3 grid(n_tok, (n_head + n_kv + 3) / 4);
+  if (kv_f16)
+    k_prompt_qk<__half><<<grid, 128, 0, st>>>(q, k, v, stride, n_head, n_kv, hd, qn, qndt, kn, kndt, cos_t, sin_t,
+                                               base, fscale, pos, kc, vc);
+  else
+    k_prompt_qk<float><<<grid, 128, 0, st>>>(q, k, v, stride, n_head, n_kv, hd, qn, qndt, kn, kndt, cos_t, sin_t,
+                                              base, fscale, pos, kc, vc);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_relayout(const uint8_t* src, uint8_t* dst, const TileGeom& g, size_t row_bytes, cudaStream_t st) {
   const int per_sb = g.chunks + (g.dtype == kQ6_K ? 1 : 0);

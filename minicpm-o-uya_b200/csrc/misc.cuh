@@ -47,6 +47,12 @@ cudaError_t launch_mark_seen(uint32_t* bits, const StepState* st, int vocab, cud
 // xorshift32 state (in/out), io[1] the token.
 cudaError_t launch_sample_small(const float* logits, int vocab, const uint32_t* seen, int seen_count, float temp,
                                 uint32_t top_k, float top_p, float min_p, float penalty, uint32_t* io, cudaStream_t st);
+// Prompt prefill: QK-RMSNorm + RoPE of n_tok tokens' q/k heads in place and
+// the append of their k/v rows at positions pos[0..n_tok) of one layer's cache.
+cudaError_t launch_prompt_qk(float* q, float* k, const float* v, int stride, int n_tok, int n_head, int n_kv, int hd,
+                             const void* qn, int qndt, const void* kn, int kndt, const float* cos_t, const float* sin_t,
+                             float base, float fscale, const int* pos, void* kc, void* vc, int kv_f16,
+                             cudaStream_t st);
 // bits |= the tokens of list (those < vocab).
 cudaError_t launch_seen_bits(uint32_t* bits, const uint32_t* list, int n, int vocab, cudaStream_t st);
 cudaError_t launch_add_inplace(float* dst, const float* src, int n, cudaStream_t st);

@@ -129,6 +129,7 @@ SIGNATURES = {
     "minicpmo_gpu_context_qwen3_forward": (i32, [vp, u32, sz, i32, f32, u32ptr, fptr, fptr, fptr] + E),
     "minicpmo_gpu_context_qwen3_forward_embedding": (i32, [vp, fptr, sz, u32, sz, i32, f32, u32ptr, fptr, fptr, fptr] + E),
     "minicpmo_gpu_context_qwen3_sample": (i32, [vp, u32ptr, sz, f32, u32, f32, f32, f32, u32ptr, u32ptr] + E),
+    "minicpmo_gpu_context_qwen3_prefill": (i32, [vp, u32ptr, sz, sz, i32, f32, u32ptr, fptr, fptr] + E),
     "minicpmo_gpu_context_qwen3_reset": (i32, [vp] + E),
     "minicpmo_gpu_context_qwen3_decode": (i32, [vp, u32, sz, sz, f32, u32ptr] + E),
     "minicpmo_gpu_context_q8_1_quantize": (i32, [vp, fptr, sz, vp] + E),
@@ -379,6 +380,17 @@ class GpuContext:
         self._call("minicpmo_gpu_context_qwen3_sample", s.ctypes.data_as(u32ptr), s.size, temperature, top_k, top_p,
                    min_p, penalty, C.byref(st), C.byref(out))
         return int(out.value), int(st.value)
+
+    def qwen3_prefill(self, tokens, first_pos: int, logits: bool = True, penalty: float = 1.0,
+                      want_logits: Optional[np.ndarray] = None):
+        """Prompt tokens in passes of up to 4 (qwen3_prefill); the same bits as token-by-token forwards."""
+        t = np.ascontiguousarray(np.asarray(tokens, dtype=np.uint32))
+        out = u32()
+        gap = f32()
+        self._call("minicpmo_gpu_context_qwen3_prefill", t.ctypes.data_as(u32ptr), t.size, first_pos,
+                   0 if logits else 1, penalty, C.byref(out), C.byref(gap),
+                   _f(want_logits) if want_logits is not None else None)
+        return int(out.value), float(gap.value)
 
     def qwen3_reset(self) -> None:
         self._call("minicpmo_gpu_context_qwen3_reset")

@@ -115,6 +115,22 @@ class Qwen3Runtime:
         self.last_token = nxt
         return nxt, gap
 
+    def prefill_prompt_ids(self, ids: Sequence[int], penalty: float = 1.0,
+                           want_logits: Optional[np.ndarray] = None) -> Tuple[int, float]:
+        """append_prompt_ids through the multi-token prefill (weights streamed once per 4 tokens);
+        the same cache, logits and next token as the token-by-token loop."""
+        if len(ids) == 0:
+            raise ValueError("error: empty prompt")
+        if self.total_tokens + len(ids) > self.context:
+            raise ValueError(f"error: context overflow total_tokens={self.total_tokens} add_tokens={len(ids)} "
+                             f"runtime_context={self.context}")
+        nxt, gap = self.gpu.qwen3_prefill([int(t) for t in ids], self.total_tokens, logits=True, penalty=penalty,
+                                          want_logits=want_logits)
+        self.seen.extend(int(t) for t in ids)
+        self.total_tokens += len(ids)
+        self.last_token = nxt
+        return nxt, gap
+
     def append_prompt_embeddings(self, placeholder_id: int, embeddings, penalty: float = 1.0,
                                  want_logits: Optional[np.ndarray] = None) -> Tuple[int, float]:
         """qwen3_append_prompt_embeddings (qwen3.uya:2534-2557): each row of

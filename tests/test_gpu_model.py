@@ -351,3 +351,57 @@ def test_layered_q4_k_m_file_matches_oracle(pkg, O, tmp_path, decode_mode):
         assert (tok, gap) == O.argmax_penalized(ref), pos
     rt.close()
     orc.close()
+
+
+@pytest.mark.parametrize(
+    "mix,kv_f16,shape_kw,n_prompt",
+    [("Q4_K_M", False, {}, 10), ("Q4_K_M", True, {}, 7), ("ALL_Q8_0", False, {}, 4), ("Q4_K_M", False, {"head_dim": 64}, 9),
+     ("Q4_K_M_LAYERED", False, {"layers": 4}, 13), ("Q4_K_M", False, {}, 1)],
+)
+def test_prefill_matches_token_by_token(pkg, O, mix, kv_f16, shape_kw, n_prompt):
+    """qwen3_prefill (prompt tokens in passes of up to 4 over the weights)
+    against the reference's token-by-token prefill (qwen3.uya:2485-2506,
+    which the forward reproduces bit-exactly): the last token's logits and
+    greedy token are bit-identical, and so is every decode step after it
+    (the KV caches agree)."""
+    from minicpmo_b200 import gguf
+    from minicpmo_b200.qwen3 import Qwen3Runtime
+
+    shape = small_shape(**shape_kw)
+    tensors = build(pkg, shape, getattr(gguf, mix), seed=6)
+    a = Qwen3Runtime.open(tensors, shape=shape, context=shape.context, kv_f16=kv_f16)
+    b = Qwen3Runtime.open(tensors, shape=shape, context=shape.context, kv_f16=kv_f16)
+    ids = [int(t) for t in gguf.prompt_ids(n_prompt, shape.vocab, seed=12)]
+    la, lb = np.empty(shape.vocab, np.float32), np.empty(shape.vocab, np.float32)
+    for pos, t in enumerate(ids):
+        ta, ga = a.forward(t, pos, logits=pos == len(ids) - 1, penalty=1.2, want_logits=la if pos == len(ids) - 1 else None)
+    tb, gb = b.gpu.qwen3_prefill(ids, 0, penalty=1.2, want_logits=lb)
+    assert np.array_equal(la, lb), rel_row_err(la, lb)
+    assert (ta, ga) == (tb, gb)
+    for step in range(5):
+        pos = len(ids) + step
+        ta, ga = a.forward(ta, pos, penalty=1.2, want_logits=la)
+        tb, gb = b.forward(tb, pos, penalty=1.2, want_logits=lb)
+        assert np.array_equal(la, lb), (step, rel_row_err(la, lb))
+        assert (ta, ga) == (tb, gb), step
+    a.close()
+    b.close()
+
+
+def test_runtime_prefill_prompt_ids(pkg, O):
+    """The runtime wrapper: positions advance by the prompt length and the
+    next token equals the token-by-token loop's."""
+    from minicpmo_b200 import gguf
+    from minicpmo_b200.qwen3 import Qwen3Runtime
+
+    shape = small_shape()
+    tensors = build(pkg, shape, gguf.Q4_K_M, seed=8)
+    a = Qwen3Runtime.open(tensors, shape=shape, context=shape.context)
+    b = Qwen3Runtime.open(tensors, shape=shape, context=shape.context)
+    ids = [int(t) for t in gguf.prompt_ids(11, shape.vocab, seed=2)]
+    na, _ = a.append_prompt_ids(ids)
+    nb, _ = b.prefill_prompt_ids(ids)
+    assert (na, a.total_tokens) == (nb, b.total_tokens)
+    assert a.generate(6) == b.generate(6)
+    a.close()
+    b.close()
