@@ -41,6 +41,24 @@
 namespace mcpo {
 
 namespace {
+// One warp per 32-value block; writes the reference's 36-byte block with the
+// sequential f16 sum s (gpu_shim.c:343-378).
+__device__ __forceinline__ void quant_block_warp(float v, uint8_t* dst, int lane) {
+  uint16_t dbits;
+  bool zero;
+  const int q = q8_1_quant_lane(v, &dbits, &zero);
+  const float s = warp_seq_sum(v);
+  const uint16_t sbits = zero ? (uint16_t)0 : f32_to_f16_ref(s);
+  // pack 4 quants per lane group into words
+  const uint32_t qb = (uint32_t)(q & 0xff);
+  uint32_t word = qb << (8 * (lane & 3));
+  word |= __shfl_xor_sync(0xffffffffu, word, 1);
+  word |= __shfl_xor_sync(0xffffffffu, word, 2);
+  uint32_t* o = reinterpret_cast<uint32_t*>(dst);
+  if (lane == 0) o[0] = (uint32_t)dbits | ((uint32_t)sbits << 16);
+  if ((lane & 3) == 0) o[1 + (lane >> 2)] = word;
+}
+
 template <int kClass, bool kDots>
 __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1) k_gemv(const GemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -54,8 +72,19 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1) k_gemv(const Gemv
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int T = a.total_wr, G = gridDim.x;
-  const int wr0 = (int)((long long)blockIdx.x * T / G);
-  const int wr1 = (int)((long long)(blockIdx.x + 1) * T / G);
+  int wr0, wr1, blk0 = 0, nblk = 0;
+  if (a.q8_out) {
+    // Q8_1 output: whole 32-row blocks per CTA, so each CTA quantises the
+    // blocks of its own rows
+    const int NB = (a.seg[0].rows + 31) / 32, wpb = 32 / a.seg[0].rpw;
+    blk0 = (int)((long long)blockIdx.x * NB / G);
+    nblk = (int)((long long)(blockIdx.x + 1) * NB / G) - blk0;
+    wr0 = min(blk0 * wpb, T);
+    wr1 = min((blk0 + nblk) * wpb, T);
+  } else {
+    wr0 = (int)((long long)blockIdx.x * T / G);
+    wr1 = (int)((long long)(blockIdx.x + 1) * T / G);
+  }
   const int nwr = wr1 - wr0;
   const bool swiglu = a.seg[0].epi == kEpiSwiglu;
   const int ks = a.seg[0].ks;
@@ -110,7 +139,17 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1) k_gemv(const Gemv
   if (threadIdx.x == 0) pdl_launch_dependents();
   const XShared x = gemv_x_view(smem, cols);
   int n = 0;
-  gemv_items<kClass, kDots>(a, x, ring, full, empty, S, slot, wr0, nwr, NC, warp, lane, n, nullptr);
+  float* stage = a.q8_out ? reinterpret_cast<float*>(empty + NC * S) : nullptr;
+  gemv_items<kClass, kDots>(a, x, ring, full, empty, S, slot, wr0, nwr, NC, warp, lane, n, nullptr, stage, blk0 * 32);
+  if (a.q8_out) {
+    // every consumer warp arrives here once (also after a wait gave up)
+    asm volatile("bar.sync 1, %0;" ::"r"(NC * 32) : "memory");
+    const int rows = a.seg[0].rows;
+    for (int b = warp; b < nblk; b += NC) {
+      const int r = (blk0 + b) * 32 + lane;
+      quant_block_warp(r < rows ? stage[b * 32 + lane] : 0.0f, a.q8_out + (size_t)(blk0 + b) * 36, lane);
+    }
+  }
 }
 
 // The same GEMV over a.nvec (2..kGemvMaxVec) input vectors: one x region per
@@ -179,23 +218,6 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1) k_gemv_multi(cons
 // Q8_1 producers
 // ---------------------------------------------------------------------
 
-// One warp per 32-value block; writes the reference's 36-byte block with the
-// sequential f16 sum s (gpu_shim.c:343-378).
-__device__ __forceinline__ void quant_block_warp(float v, uint8_t* dst, int lane) {
-  uint16_t dbits;
-  bool zero;
-  const int q = q8_1_quant_lane(v, &dbits, &zero);
-  const float s = warp_seq_sum(v);
-  const uint16_t sbits = zero ? (uint16_t)0 : f32_to_f16_ref(s);
-  // pack 4 quants per lane group into words
-  const uint32_t qb = (uint32_t)(q & 0xff);
-  uint32_t word = qb << (8 * (lane & 3));
-  word |= __shfl_xor_sync(0xffffffffu, word, 1);
-  word |= __shfl_xor_sync(0xffffffffu, word, 2);
-  uint32_t* o = reinterpret_cast<uint32_t*>(dst);
-  if (lane == 0) o[0] = (uint32_t)dbits | ((uint32_t)sbits << 16);
-  if ((lane & 3) == 0) o[1 + (lane >> 2)] = word;
-}
 
 __global__ void k_quantize_q8_1(const float* __restrict__ x, int n, uint8_t* __restrict__ xq) {
   pdl_wait();
@@ -358,8 +380,19 @@ cudaError_t launch_gemv(GemvArgs& a, int grid, cudaStream_t st, bool pdl) {
   const int want = consumers_cfg() > kMaxConsumers ? kMaxConsumers : consumers_cfg();
   nc = nc > want ? want : nc;
   if (nc < 1) return cudaErrorInvalidValue;
-  const size_t smem = xb + (size_t)nc * stages * slot + (size_t)2 * nc * stages * 8;
+  size_t smem = xb + (size_t)nc * stages * slot + (size_t)2 * nc * stages * 8;
   if (grid <= 0 || grid > wr) grid = wr;
+  if (a.q8_out) {
+    // whole 32-row blocks per CTA: as few CTAs as give every CTA the same
+    // largest block count
+    const GemvSeg& s0 = a.seg[0];
+    if (a.nseg != 1 || a.nvec > 1 || a.dots || s0.rpw < 1 || 32 % s0.rpw != 0) return cudaErrorInvalidValue;
+    const int nb = (s0.rows + 31) / 32;
+    const int per = (nb + grid - 1) / grid;
+    grid = (nb + per - 1) / per;
+    smem += (size_t)per * 32 * 4;
+    if (smem > (size_t)227 * 1024) return cudaErrorInvalidValue;
+  }
   if (has4 && has6) return launch_class<kClassQ4K6K>(a, grid, nc, smem, st, pdl);
   if (has6) return launch_class<kClassQ6K>(a, grid, nc, smem, st, pdl);
   if (has8) return launch_class<kClassQ80>(a, grid, nc, smem, st, pdl);

@@ -64,6 +64,10 @@ struct GemvArgs {
   // one vector
   int nvec;
   int x_stride, xq_stride, y_stride;
+  // optional (one segment, one vector): the outputs also as Q8_1 blocks
+  // (36 B per 32 rows, the bits k_quantize_q8_1 gives for y), each CTA
+  // taking whole 32-row blocks; a following GEMV reads them as kInQ8_1
+  uint8_t* q8_out;
 };
 
 constexpr int kGemvMaxVec = 4;  // input vectors per multi-vector launch

@@ -23,12 +23,12 @@ struct XShared {
   int nb;
 };
 
+// Integer dot products are exact, so the four dp4a run as two independent
+// pairs (shorter dependency chains) and are added at the end.
 __device__ __forceinline__ int dot4(uint4 w, uint4 x, int acc) {
-  acc = dp4a((int)w.x, (int)x.x, acc);
-  acc = dp4a((int)w.y, (int)x.y, acc);
-  acc = dp4a((int)w.z, (int)x.z, acc);
-  acc = dp4a((int)w.w, (int)x.w, acc);
-  return acc;
+  const int a0 = dp4a((int)w.y, (int)x.y, dp4a((int)w.x, (int)x.x, 0));
+  const int a1 = dp4a((int)w.w, (int)x.w, dp4a((int)w.z, (int)x.z, 0));
+  return acc + a0 + a1;
 }
 
 
@@ -41,11 +41,9 @@ __device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
 }
 
 __device__ __forceinline__ int dot4_mask(uint4 w, uint4 x, uint32_t m, int acc) {
-  acc = dp4a_us(w.x & m, x.x, acc);
-  acc = dp4a_us(w.y & m, x.y, acc);
-  acc = dp4a_us(w.z & m, x.z, acc);
-  acc = dp4a_us(w.w & m, x.w, acc);
-  return acc;
+  const int a0 = dp4a_us(w.y & m, x.y, dp4a_us(w.x & m, x.x, 0));
+  const int a1 = dp4a_us(w.w & m, x.w, dp4a_us(w.z & m, x.z, 0));
+  return acc + a0 + a1;
 }
 
 // ---- Q4_K super-block: c[0] = {d, dmin, scales}, c[1..8] = qs ----
@@ -70,8 +68,8 @@ __device__ __forceinline__ float sb_dot_q4k(const uint4* c, const XShared& x, in
     const uint4 x1 = x.xs[(4 * g + 1) * x.nb + sb];
     const uint4 x2 = x.xs[(4 * g + 2) * x.nb + sb];
     const uint4 x3 = x.xs[(4 * g + 3) * x.nb + sb];
-    const int dlo = dot4_mask(q1, x1, 0x0f0f0f0fu, dot4_mask(q0, x0, 0x0f0f0f0fu, 0));
-    const int dhi = dot4_mask(q1, x3, 0xf0f0f0f0u, dot4_mask(q0, x2, 0xf0f0f0f0u, 0)) >> 4;
+    const int dlo = dot4_mask(q0, x0, 0x0f0f0f0fu, 0) + dot4_mask(q1, x1, 0x0f0f0f0fu, 0);
+    const int dhi = (dot4_mask(q0, x2, 0xf0f0f0f0u, 0) + dot4_mask(q1, x3, 0xf0f0f0f0u, 0)) >> 4;
     const int j0 = 2 * g, j1 = 2 * g + 1;
     const uint32_t scw = j0 < 4 ? sc_lo : sc_hi, mnw = j0 < 4 ? mn_lo : mn_hi;
     const int s0 = (scw >> (8 * (j0 & 3))) & 0xff, s1 = (scw >> (8 * (j1 & 3))) & 0xff;
@@ -143,8 +141,7 @@ __device__ __forceinline__ float sb_dot_q80(const uint4* c, const XShared& x, in
   float sum = 0.0f;
 #pragma unroll
   for (int b = 0; b < 8; ++b) {
-    int acc = dot4(c[1 + 2 * b], x.xs[(2 * b) * x.nb + sb], 0);
-    acc = dot4(c[2 + 2 * b], x.xs[(2 * b + 1) * x.nb + sb], acc);
+    const int acc = dot4(c[1 + 2 * b], x.xs[(2 * b) * x.nb + sb], 0) + dot4(c[2 + 2 * b], x.xs[(2 * b + 1) * x.nb + sb], 0);
     const float dwf = f16_to_f32((uint16_t)((dw[b >> 1] >> (16 * (b & 1))) & 0xffffu));
     sum = __fmaf_rn(__fmul_rn(dwf, x.xd[b * x.nb + sb]), (float)acc, sum);
     if (kDots && dots) dots[sb * 8 + b] = acc;
@@ -540,7 +537,8 @@ __device__ __forceinline__ XShared gemv_x_view(uint8_t* xbase, int cols) {
 template <int kClass, bool kDots>
 __device__ __forceinline__ bool gemv_items(const GemvArgs& a, const XShared& x, uint8_t* ring, uint64_t* full,
                                            uint64_t* empty, int S, int slot, int wr0, int nwr, int NC, int warp,
-                                           int lane, int& n, const volatile int* abort) {
+                                           int lane, int& n, const volatile int* abort, float* stage = nullptr,
+                                           int stage_r0 = 0) {
   const int cols = a.cols;
   const bool swiglu = a.seg[0].epi == kEpiSwiglu;
   const int ks = a.seg[0].ks;
@@ -572,11 +570,12 @@ __device__ __forceinline__ bool gemv_items(const GemvArgs& a, const XShared& x, 
       }
     }
     const float g = reduce_row(acc[0], s.lpr);
-    if (swiglu) {
-      const float u = reduce_row(acc[1], s.lpr);
-      if (lane_in_row == 0 && row < s.rows) s.y[row] = silu_mul_det(g, u);
-    } else if (lane_in_row == 0 && row < s.rows) {
-      s.y[row] = add ? __fadd_rn(yold, g) : g;
+    // (every lane takes part in both butterflies)
+    const float u = swiglu ? reduce_row(acc[1], s.lpr) : 0.0f;
+    if (lane_in_row == 0 && row < s.rows) {
+      const float out = swiglu ? silu_mul_det(g, u) : add ? __fadd_rn(yold, g) : g;
+      s.y[row] = out;
+      if (stage) stage[row - stage_r0] = out;
     }
   }
   return true;

@@ -531,6 +531,16 @@ cudaError_t model_mv(Ctx* c, Upload* w, const float* x, const uint8_t* xq, float
 // Decode attention of the model graph: split merge inside a thread-block
 // cluster (1, the default) or through global memory (tuning override
 // MCPO_ATTN_CLUSTER=0); the same bits either way.
+// The gate/up GEMV hands the down GEMV Q8_1 blocks (1, the default) or f32
+// values (tuning override MCPO_FFN_Q8=0); the same bits either way.
+int ffn_q8_cfg() {
+  static const int v = [] {
+    const char* e = getenv("MCPO_FFN_Q8");
+    return (e && *e) ? (atoi(e) != 0 ? 1 : 0) : 1;
+  }();
+  return v;
+}
+
 int attn_cluster_cfg() {
   static const int v = [] {
     const char* e = getenv("MCPO_ATTN_CLUSTER");
@@ -658,7 +668,9 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
       REC(model_mv(c, L.o, m.attn, a.out_q8, m.hidden, kEpiAdd, m.tmp, m.grid_q, &m.st->err));
     }
     // feed-forward block: RMSNorm -> Q8_1 inside the gate/up GEMV, SwiGLU in
-    // its epilogue, f32 -> Q8_1 inside the down GEMV
+    // its epilogue, which also writes the Q8_1 blocks the down GEMV reads
+    // (f32 -> Q8_1 inside the down GEMV otherwise)
+    const uint8_t* down_q8 = nullptr;
     if (L.gate->tiled && L.up->tiled && L.gate->dtype == L.up->dtype && L.gate->rows == L.up->rows) {
       GemvArgs g{};
       g.nseg = 1;
@@ -666,6 +678,8 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
       norm_input(&g, m.hidden, L.ffn_norm, cf.rms_eps);
       g.err = &m.st->err;
       gemv_seg_from_geom(L.gate->geom, L.gate->dev, L.up->dev, m.fused, kEpiSwiglu, &g.seg[0]);
+      if (!tp && L.down->tiled && ffn_q8_cfg()) g.q8_out = m.fq;
+      down_q8 = g.q8_out;
       REC(launch_gemv(g, m.grid_h, s, true));
     } else {
       REC(launch_rmsnorm_q8_1(m.hidden, L.ffn_norm->dev, L.ffn_norm->dtype, h, cf.rms_eps, m.normed, m.xq, s, true));
@@ -677,7 +691,7 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
       REC(model_mv(c, L.down, m.fused, nullptr, m.peers.part[m.tp_rank][1], kEpiStore, m.tmp, m.grid_f, &m.st->err));
       REC(launch_tp_reduce_add(m.peers, 1, m.hidden, h, m.tp_epoch, &m.st->err, s));
     } else {
-      REC(model_mv(c, L.down, m.fused, nullptr, m.hidden, kEpiAdd, m.tmp, m.grid_f, &m.st->err));
+      REC(model_mv(c, L.down, m.fused, down_q8, m.hidden, kEpiAdd, m.tmp, m.grid_f, &m.st->err));
     }
   }
   if (logits) {
