@@ -540,7 +540,7 @@ def main() -> int:
                         "cols": t.cols, "us": us, "gbs": alg / us / 1e3, "frac": alg / us / 1e3 / hbm}
     w_bytes, kv_bytes = model_bytes(tensors, shape, start_pos + args.steps // 2)
     step_bytes = w_bytes + kv_bytes
-    traffic_key = "decode_step_qwen3_8b_bytes" if persistent else "gemv_q4_k_12288x4096_bytes"
+    traffic_key = "decode_step_qwen3_8b_bytes" if persistent else "gemv_q4_k_gateup_2x12288x4096_bytes"
     traffic = _ncu_traffic(traffic_key)
     if persistent:
         gbs = step_bytes / (step_s / args.steps) / 1e9
@@ -548,8 +548,16 @@ def main() -> int:
         dom_desc = ("k_decode_step (the whole layer chain + lm_head in one persistent launch per token; "
                     "timed with CUDA events over the K graph replays, which add 3 small kernels)")
     else:
-        dom = shapes["blk.0.ffn_gate.weight"]
-        dom_desc = "k_gemv (Q4_K 12288x4096, the ffn_gate/up shape), timed alone, weights rotated > L2"
+        # the fused gate/up launch (two Q4_K 12288x4096 matrices, RMSNorm
+        # prologue, SwiGLU + Q8_1 epilogue), launched as the decode step
+        # launches it, back to back over the layers (each launch streams its
+        # own layer's weights from HBM)
+        ffn_us, ffn_bytes = g.qwen3_time_ffn(iters=2 * shape.layers)
+        dom = {"us": ffn_us, "gbs": ffn_bytes / ffn_us / 1e3, "frac": ffn_bytes / ffn_us / 1e3 / hbm,
+               "bytes": ffn_bytes}
+        dom_desc = (f"k_gemv<Q4_K> fused ffn gate/up (2 x {shape.ffn}x{shape.hidden} Q4_K + RMSNorm, SwiGLU, Q8_1 "
+                    f"out) as the decode step launches it, CUDA events over {2 * shape.layers} back-to-back launches "
+                    f"rotating the {shape.layers} layers")
     kernels = g.qwen3_step_kernels(True)
 
     line = {
@@ -583,7 +591,7 @@ def main() -> int:
         "gpu_launches": kernels * args.steps,
         "roofline": {"bound": "hbm", "achieved": dom["gbs"], "peak": hbm, "unit": "GB/s", "frac": dom["frac"],
                      "traffic": traffic, "peak_kind": peak_kind, "kernel": dom_desc,
-                     "algorithmic_bytes_per_launch": step_bytes if persistent else None,
+                     "algorithmic_bytes_per_launch": step_bytes if persistent else dom["bytes"],
                      "gemv_sweep": shapes},
         "decode_mode": "persistent" if persistent else "per-kernel",
         "clocks": clk,

@@ -325,6 +325,14 @@ MINICPMO_API int minicpmo_gpu_context_time_matvec(void *handle, const void *host
 MINICPMO_API int minicpmo_gpu_context_time_matvec_input(void *handle, const void *host_ptr, size_t in_dim, size_t out_dim,
                                            int iters, int input, const void *norm_host_ptr, float *avg_us,
                                            char *error, size_t error_cap);
+/* Device time of the bound model's fused ffn gate/up GEMV exactly as the
+ * decode step launches it (RMSNorm prologue from the current hidden state,
+ * SwiGLU epilogue, Q8_1 output for the down GEMV; programmatic dependent
+ * launch), back to back over the layers in turn (every launch streams its
+ * weights from HBM): the average microseconds per launch and the
+ * algorithmic bytes of one launch.  Overwrites only scratch activations. */
+MINICPMO_API int minicpmo_gpu_context_qwen3_time_ffn(void *handle, int iters, float *avg_us, double *bytes_per_launch,
+                                                     char *error, size_t error_cap);
 /* Device time of n_steps auto-advancing decode steps (graph replays, no host
  * copies); reports the total milliseconds. */
 MINICPMO_API int minicpmo_gpu_context_qwen3_time_decode(void *handle, uint32_t first_token, size_t first_pos, size_t n_steps,

@@ -2928,6 +2928,62 @@ int minicpmo_gpu_context_time_matvec_input(void* handle, const void* host_ptr, s
   return ok ? 1 : 0;
 }
 
+int minicpmo_gpu_context_qwen3_time_ffn(void* handle, int iters, float* avg_us, double* bytes_per_launch, char* error,
+                                        size_t error_cap) {
+  Ctx* c = (Ctx*)handle;
+  if (!c) return copy_error(error, error_cap, "error: null gpu context"), 0;
+  DeviceGuard g(c);
+  if (!c->model) return fail(c, error, error_cap, "error: qwen3 time_ffn: model not bound");
+  Model& m = *c->model;
+  const auto& cf = m.cfg;
+  if (iters <= 0) return fail(c, error, error_cap, "error: qwen3 time_ffn: iters must be positive");
+  for (uint32_t li = 0; li < cf.layers; ++li) {
+    const LayerW& L = m.layer[li];
+    if (!(L.gate->tiled && L.up->tiled && L.gate->dtype == L.up->dtype && L.gate->rows == L.up->rows))
+      return fail(c, error, error_cap, "error: qwen3 time_ffn: layer %u has no fused gate/up GEMV", li);
+  }
+  const bool q8 = m.tp_world <= 1 && ffn_q8_cfg();
+  auto args = [&](uint32_t li) {
+    const LayerW& L = m.layer[li];
+    GemvArgs a{};
+    a.nseg = 1;
+    a.cols = (int)cf.hidden;
+    norm_input(&a, m.hidden, L.ffn_norm, cf.rms_eps);
+    a.err = &m.st->err;
+    gemv_seg_from_geom(L.gate->geom, L.gate->dev, L.up->dev, m.fused, kEpiSwiglu, &a.seg[0]);
+    if (q8 && L.down->tiled) a.q8_out = m.fq;
+    return a;
+  };
+  {
+    const GemvArgs a0 = args(0);
+    const double f = (double)cf.ffn, h = (double)cf.hidden;
+    if (bytes_per_launch)
+      *bytes_per_launch = (double)m.layer[0].gate->bytes + (double)m.layer[0].up->bytes + h * 4 +
+                          (double)m.layer[0].ffn_norm->bytes + f * 4 + (a0.q8_out ? f / 32 * 36 : 0.0);
+  }
+  cudaEvent_t e0, e1;
+  cudaEventCreate(&e0);
+  cudaEventCreate(&e1);
+  bool ok = true;
+  for (int i = 0; ok && i < 3; ++i) {
+    GemvArgs a = args((uint32_t)i % cf.layers);
+    ok = cuda_ok(c, launch_gemv(a, m.grid_h, c->stream, true), "time_ffn_warmup", error, error_cap);
+  }
+  if (ok) cudaEventRecord(e0, c->stream);
+  for (int i = 0; ok && i < iters; ++i) {
+    GemvArgs a = args((uint32_t)(i + 3) % cf.layers);
+    ok = cuda_ok(c, launch_gemv(a, m.grid_h, c->stream, true), "time_ffn_launch", error, error_cap);
+  }
+  if (ok) cudaEventRecord(e1, c->stream);
+  if (ok) ok = cuda_ok(c, cudaStreamSynchronize(c->stream), "time_ffn_sync", error, error_cap);
+  float ms = 0.0f;
+  if (ok) cudaEventElapsedTime(&ms, e0, e1);
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  if (ok && avg_us) *avg_us = ms * 1000.0f / (float)iters;
+  return ok ? 1 : 0;
+}
+
 int minicpmo_gpu_context_qwen3_step_kernels(void* handle, int with_logits) {
   Ctx* c = (Ctx*)handle;
   if (!c || !c->model) return 0;

@@ -144,6 +144,7 @@ SIGNATURES = {
     "minicpmo_gpu_context_qwen3_time_decode_batch": (i32, [vp, sz, u32ptr, u32ptr, sz, fptr] + E),
     "minicpmo_gpu_context_qwen3_batch_kernels": (i32, [vp, i32]),
     "minicpmo_gpu_context_time_matvec": (i32, [vp, vp, sz, sz, i32, fptr] + E),
+    "minicpmo_gpu_context_qwen3_time_ffn": (i32, [vp, i32, fptr, C.POINTER(C.c_double)] + E),
     "minicpmo_gpu_context_qwen3_time_decode": (i32, [vp, u32, sz, sz, fptr] + E),
     "minicpmo_gpu_context_tensor_device_bytes": (sz, [vp, vp]),
     "minicpmo_gpu_context_qwen3_step_kernels": (i32, [vp, i32]),
@@ -451,6 +452,14 @@ class GpuContext:
         self._call("minicpmo_gpu_context_time_matvec_input", t.ptr, t.cols, t.rows, iters, input_mode,
                    norm.ptr if norm is not None else None, C.byref(us))
         return float(us.value)
+
+    def qwen3_time_ffn(self, iters: int = 72) -> Tuple[float, float]:
+        """Mean device time (us) of the bound model's fused gate/up GEMV as the
+        decode step launches it, over the layers in turn, and its algorithmic
+        bytes per launch."""
+        us, nbytes = f32(), C.c_double()
+        self._call("minicpmo_gpu_context_qwen3_time_ffn", iters, C.byref(us), C.byref(nbytes))
+        return float(us.value), float(nbytes.value)
 
     def time_matvec(self, t: Tensor, iters: int = 20) -> float:
         us = f32()
