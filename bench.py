@@ -268,6 +268,52 @@ def _ncu_traffic(key):
         return None
 
 
+def run_prefill_bench(args, shape, mix) -> int:
+    """Prompt prefill on 1 GPU: --prompt seeded ids through qwen3_prefill
+    (passes of up to 4 tokens) and, over the same positions of a reset
+    cache, through one qwen3_forward per id (the reference's
+    qwen3_append_prompt_ids loop).  Host wall time around each call, which
+    synchronises; max(1, --steps // 64) repetitions after one untimed."""
+    import torch
+
+    from minicpmo_b200.qwen3 import Qwen3Runtime
+    from minicpmo_b200 import gguf
+
+    torch.cuda.set_device(0)
+    tensors = build_weights(shape, mix, "cuda:0")
+    torch.cuda.empty_cache()
+    rt = Qwen3Runtime.open(tensors, shape=shape, device_index=0, context=args.prompt + 8)
+    prompt = gguf.prompt_ids(args.prompt, shape.vocab, seed=7)
+    reps = max(1, args.steps // 64)
+
+    def timed(fn):
+        rt.reset()
+        torch.cuda.synchronize()
+        t = time.perf_counter()
+        out = fn(prompt)
+        torch.cuda.synchronize()
+        return time.perf_counter() - t, out
+
+    timed(rt.prefill_prompt_ids)
+    pf = [timed(rt.prefill_prompt_ids) for _ in range(reps)]
+    tw = [timed(rt.append_prompt_ids) for _ in range(reps)]
+    assert all(p[1][0] == tw[0][1][0] for p in pf + tw), "prefill and token-by-token next tokens differ"
+    t_pf = min(p[0] for p in pf)
+    t_tw = min(p[0] for p in tw)
+    print(json.dumps({
+        "metric": f"{metric_name(args.shape).replace('decode', 'prefill')}",
+        "value": args.prompt / t_pf, "unit": "tok/s", "n_gpus": 1, "steps": reps, "warmup": 1,
+        "higher_is_better": True, "dtype": "q4_k/q6_k x q8_1 (int8 dp4a, f32 accumulate)",
+        "data": f"synthetic: seeded N(0,0.02) weights quantised Q4_K_M-style, {args.prompt} uniform random prompt ids",
+        "config": {"workload": f"{args.shape}-shape Q4_K_M prompt prefill, {args.prompt} ids from position 0",
+                   "layers": shape.layers, "passes": (args.prompt + 3) // 4},
+        "prefill_s": t_pf, "tokenwise_s": t_tw, "tokenwise_tok_s": args.prompt / t_tw,
+        "speedup_vs_tokenwise": t_tw / t_pf, "next_token": int(pf[0][1][0]),
+    }), flush=True)
+    rt.close()
+    return 0
+
+
 def run_batch_bench(args, shape, world, rank, local, dist, barrier) -> int:
     """Qwen3-8B shape, every linear weight Q8_0, f16 KV cache at a 4096-token
     context, B independent sequences each after a prompt of --prompt ids (default 1024), greedy
@@ -405,6 +451,9 @@ def main() -> int:
     ap.add_argument("--batch", type=int, default=0,
                     help="BASELINE config 3: batched decode of this many sequences (2..32), all-Q8_0 weights on the "
                          "tensor cores, f16 KV, prompt 1024 unless --prompt is given")
+    ap.add_argument("--prefill", action="store_true",
+                    help="time the multi-token prompt prefill (qwen3_prefill) of --prompt ids on 1 GPU against "
+                         "the token-by-token forwards over the same positions; one JSON line")
     ap.add_argument("--prompt", type=int, default=PROMPT,
                     help="prompt length before decode (default: the 512 of the headline config; shorter only for "
                          "profiler launch lists)")
@@ -423,6 +472,8 @@ def main() -> int:
         return run_reference(args, shape, mix)
     if args.kernel_sweep:
         return run_kernel_sweep(args)
+    if args.prefill:
+        return run_prefill_bench(args, shape, mix)
 
     import torch
 

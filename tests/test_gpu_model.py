@@ -405,3 +405,26 @@ def test_runtime_prefill_prompt_ids(pkg, O):
     assert a.generate(6) == b.generate(6)
     a.close()
     b.close()
+
+
+def test_time_ffn_leaves_decode_unchanged(pkg, O):
+    """qwen3_time_ffn reports a positive launch time and the launch's bytes,
+    and touches only scratch activations: decoding afterwards gives the same
+    tokens as a runtime that never timed."""
+    from minicpmo_b200 import gguf
+    from minicpmo_b200.qwen3 import Qwen3Runtime
+
+    shape = small_shape()
+    tensors = build(pkg, shape, gguf.Q4_K_M, seed=9)
+    a = Qwen3Runtime.open(tensors, shape=shape, context=shape.context)
+    b = Qwen3Runtime.open(tensors, shape=shape, context=shape.context)
+    ids = [int(t) for t in gguf.prompt_ids(7, shape.vocab, seed=3)]
+    a.append_prompt_ids(ids)
+    b.append_prompt_ids(ids)
+    us, nbytes = b.gpu.qwen3_time_ffn(iters=2 * shape.layers)
+    assert us > 0.0
+    gate, up = b.tensors["blk.0.ffn_gate.weight"], b.tensors["blk.0.ffn_up.weight"]
+    assert nbytes >= gate.nbytes + up.nbytes
+    assert a.generate(5) == b.generate(5)
+    a.close()
+    b.close()
