@@ -2291,6 +2291,11 @@ bool prefill_alloc(Ctx* c, Model& m, char* err, size_t cap) {
   return cuda_ok(c, cudaMemsetAsync(m.pf_counters, 0, N * cf.kv_heads * 4, c->stream), "prefill_memset", err, cap);
 }
 
+// The four GEMVs of a layer are launched with programmatic dependent launch
+// (their weight streams start before the previous kernel ends; every read of
+// its results waits for it).  The other kernels of the pass are plain
+// launches: the attention requests cache rows before its wait, and rows of
+// this pass come from k_prompt_qk.
 // n (<= kGemvMaxVec) prompt tokens at positions p0.. in one pass over the
 // weights: each token's arithmetic is that of a decode step (same Q8_1
 // activations and dot orders, same attention and norms), so the cache and
@@ -2328,7 +2333,7 @@ int prefill_chunk(Ctx* c, Model& m, const uint32_t* toks, int n, size_t p0, bool
     Upload* qkv[3] = {L.q, L.k, L.v};
     float* ys[3] = {m.pf_q, m.pf_k, m.pf_v};
     for (int i = 0; i < 3; ++i) gemv_seg_from_geom(qkv[i]->geom, qkv[i]->dev, nullptr, ys[i], kEpiStore, &a.seg[i]);
-    if (!ok(launch_gemv(a, m.grid_h, s, false), "prefill_qkv")) return 0;
+    if (!ok(launch_gemv(a, m.grid_h, s, true), "prefill_qkv")) return 0;
     uint8_t* kc = (uint8_t*)m.kc + li * m.kv_layer_elems * esz;
     uint8_t* vc = (uint8_t*)m.vc + li * m.kv_layer_elems * esz;
     if (!ok(launch_prompt_qk(m.pf_q, m.pf_k, m.pf_v, qd, n, (int)cf.heads, (int)cf.kv_heads, hd,
@@ -2371,7 +2376,7 @@ int prefill_chunk(Ctx* c, Model& m, const uint32_t* toks, int n, size_t p0, bool
     o.x_stride = qd;
     o.y_stride = h;
     gemv_seg_from_geom(L.o->geom, L.o->dev, nullptr, m.pf_hidden, kEpiAdd, &o.seg[0]);
-    if (!ok(launch_gemv(o, m.grid_q, s, false), "prefill_o")) return 0;
+    if (!ok(launch_gemv(o, m.grid_q, s, true), "prefill_o")) return 0;
     GemvArgs g{};
     g.nseg = 1;
     g.cols = h;
@@ -2381,7 +2386,7 @@ int prefill_chunk(Ctx* c, Model& m, const uint32_t* toks, int n, size_t p0, bool
     g.x_stride = h;
     g.y_stride = f;
     gemv_seg_from_geom(L.gate->geom, L.gate->dev, L.up->dev, m.pf_fused, kEpiSwiglu, &g.seg[0]);
-    if (!ok(launch_gemv(g, m.grid_h, s, false), "prefill_gateup")) return 0;
+    if (!ok(launch_gemv(g, m.grid_h, s, true), "prefill_gateup")) return 0;
     GemvArgs d{};
     d.nseg = 1;
     d.cols = f;
@@ -2392,7 +2397,7 @@ int prefill_chunk(Ctx* c, Model& m, const uint32_t* toks, int n, size_t p0, bool
     d.x_stride = f;
     d.y_stride = h;
     gemv_seg_from_geom(L.down->geom, L.down->dev, nullptr, m.pf_hidden, kEpiAdd, &d.seg[0]);
-    if (!ok(launch_gemv(d, m.grid_f, s, false), "prefill_down")) return 0;
+    if (!ok(launch_gemv(d, m.grid_f, s, true), "prefill_down")) return 0;
   }
   if (logits) {
     GemvArgs o{};
