@@ -2291,11 +2291,11 @@ bool prefill_alloc(Ctx* c, Model& m, char* err, size_t cap) {
   return cuda_ok(c, cudaMemsetAsync(m.pf_counters, 0, N * cf.kv_heads * 4, c->stream), "prefill_memset", err, cap);
 }
 
-// The four GEMVs of a layer are launched with programmatic dependent launch
-// (their weight streams start before the previous kernel ends; every read of
-// its results waits for it).  The other kernels of the pass are plain
-// launches: the attention requests cache rows before its wait, and rows of
-// this pass come from k_prompt_qk.
+// The four GEMVs of a layer and k_prompt_qk are launched with programmatic
+// dependent launch (the GEMVs' weight streams start before the previous
+// kernel ends; every read of its results waits for it).  The attention is a
+// plain launch: it requests cache rows before its wait, and rows of this
+// pass come from k_prompt_qk.
 // n (<= kGemvMaxVec) prompt tokens at positions p0.. in one pass over the
 // weights: each token's arithmetic is that of a decode step (same Q8_1
 // activations and dot orders, same attention and norms), so the cache and

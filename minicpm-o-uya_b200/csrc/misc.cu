@@ -424,6 +424,7 @@ __global__ void k_prompt_qk(float* q, float* k, const float* v, int stride, int 
                             const float* sin_t, float base, float fscale, const int* pos, void* kc, void* vc) {
   __shared__ float row_s[4][256];
   __shared__ float sq_s[4][256];
+  pdl_wait();  // q/k/v come from the q/k/v GEMV
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x, hh = blockIdx.y * 4 + warp;
   if (hh >= n_head + n_kv) return;
@@ -454,13 +455,13 @@ cudaError_t launch_prompt_qk(float* q, float* k, const float* v, int stride, int
                              cudaStream_t st) {
   if (hd > 256 || n_tok < 1) return cudaErrorInvalidValue;
   const dim3 grid(n_tok, (n_head + n_kv + 3) / 4);
+  // programmatic dependent launch: the CTAs wait for the q/k/v GEMV in the
+  // kernel (the kernel never triggers its dependents early)
   if (kv_f16)
-    k_prompt_qk<__half><<<grid, 128, 0, st>>>(q, k, v, stride, n_head, n_kv, hd, qn, qndt, kn, kndt, cos_t, sin_t,
-                                               base, fscale, pos, kc, vc);
-  else
-    k_prompt_qk<float><<<grid, 128, 0, st>>>(q, k, v, stride, n_head, n_kv, hd, qn, qndt, kn, kndt, cos_t, sin_t,
-                                              base, fscale, pos, kc, vc);
-  return cudaGetLastError();
+    return launch_k(k_prompt_qk<__half>, grid, dim3(128), 0, st, true, q, k, v, stride, n_head, n_kv, hd, qn, qndt, kn,
+                    kndt, cos_t, sin_t, base, fscale, pos, kc, vc);
+  return launch_k(k_prompt_qk<float>, grid, dim3(128), 0, st, true, q, k, v, stride, n_head, n_kv, hd, qn, qndt, kn,
+                  kndt, cos_t, sin_t, base, fscale, pos, kc, vc);
 }
 
 cudaError_t launch_relayout(const uint8_t* src, uint8_t* dst, const TileGeom& g, size_t row_bytes, cudaStream_t st) {
