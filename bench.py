@@ -82,6 +82,15 @@ def model_bytes(tensors, shape, pos_mean):
     return w, kv
 
 
+def clock_csv(rank: int) -> Path:
+    """A private temporary file for one rank's nvidia-smi samples."""
+    import tempfile
+
+    fd, name = tempfile.mkstemp(prefix=f"mcpo_clocks_rank{rank}_", suffix=".csv")
+    os.close(fd)
+    return Path(name)
+
+
 class ClockSampler:
     """nvidia-smi clocks during the timed region (the recipe's clocks line)."""
 
@@ -121,6 +130,10 @@ class ClockSampler:
             for n, v in zip(names, f[5:9]):
                 if v.lower() == "active":
                     reasons.add(n)
+        try:
+            self.path.unlink()
+        except OSError:
+            pass
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
                 "reasons": sorted(reasons), "samples": len(sm)}
 
@@ -138,21 +151,25 @@ def cpu_reference(shape, tensors, n_tokens, start_pos, threads):
     timed token attends over start_pos+1.. positions as in the GPU run."""
     from oracle import oracle as O
 
-    ctx = start_pos + n_tokens + 1
+    ctx = start_pos + 3 * n_tokens + 1
     tmap = {n: (dt, r, c, d) for n, dt, r, c, d in tensors}
     m = O.OracleModel(shape, tmap, ctx, q8_1=False, pool_threads=threads, use_reference_matvec=True)
     rng = np.random.Generator(np.random.PCG64(5))
     m.kc[:] = rng.standard_normal(m.kc.size, dtype=np.float32)
     m.vc[:] = rng.standard_normal(m.vc.size, dtype=np.float32)
     kind = "reference" if m.uses_reference_matvec else "port"
-    ids = np.random.Generator(np.random.PCG64(11)).integers(0, shape.vocab, n_tokens + 1)
+    ids = np.random.Generator(np.random.PCG64(11)).integers(0, shape.vocab, 3 * n_tokens + 1)
     m.forward(int(ids[0]), start_pos)  # untimed warm-up token (page in the weights)
-    t0 = time.perf_counter()
-    for i in range(n_tokens):
-        m.forward(int(ids[i + 1]), start_pos + 1 + i)
-    dt = time.perf_counter() - t0
+    rates = []
+    pos = start_pos + 1
+    for rep in range(3):  # median of 3 timed windows of n_tokens each
+        t0 = time.perf_counter()
+        for i in range(n_tokens):
+            m.forward(int(ids[1 + rep * n_tokens + i]), pos)
+            pos += 1
+        rates.append(n_tokens / (time.perf_counter() - t0))
     m.close()
-    return n_tokens / dt, kind
+    return statistics.median(rates), kind
 
 
 def run_reference(args, shape, mix):
@@ -344,8 +361,7 @@ def run_batch_bench(args, shape, world, rank, local, dist, barrier) -> int:
     cur = np.asarray(rt.batch_last, np.uint32)
     pos0 = rt.batch_tokens
 
-    clocks = ClockSampler(local, ROOT / "gpurun_out" / f"clocks_rank{rank}.csv"
-                          if (ROOT / "gpurun_out").exists() else Path(f"/tmp/clocks_rank{rank}.csv"))
+    clocks = ClockSampler(local, clock_csv(rank))
     barrier()
     wall0 = time.perf_counter()
     ms = g.qwen3_time_decode_batch(cur, np.full(B, pos0, np.uint32), args.steps)
@@ -546,8 +562,7 @@ def main() -> int:
         torch.cuda.synchronize()
 
     # ---- value: device-timed K decode steps (graph replays, token fed back on device)
-    clocks = ClockSampler(local, ROOT / "gpurun_out" / f"clocks_rank{rank}.csv"
-                          if (ROOT / "gpurun_out").exists() else Path(f"/tmp/clocks_rank{rank}.csv"))
+    clocks = ClockSampler(local, clock_csv(rank))
     barrier()
     wall0 = time.perf_counter()
     ms = g.qwen3_time_decode(cur, rt.total_tokens, args.steps)
@@ -651,8 +666,9 @@ def main() -> int:
         try:
             cps, kind = cpu_reference(shape, tensors, args.cpu_sample, args.prompt, os.cpu_count() or 1)
             line["cpu_baseline"] = {"value": cps, "unit": "tok/s", "cores": os.cpu_count() or 1, "kind": kind,
-                                    "sample": f"{args.cpu_sample} decode tokens after {args.prompt} seeded KV positions, "
-                                              "reference cpu_kernels.c AVX2 matvec in a pthread row pool, f32 activations"}
+                                    "sample": f"median of 3 windows of {args.cpu_sample} decode tokens (after one warm-up token) "
+                                              f"following {args.prompt} seeded KV positions, reference cpu_kernels.c "
+                                              "AVX2 matvec in a pthread row pool, f32 activations"}
         except Exception as exc:  # the GPU line must still print
             line["cpu_baseline"] = {"value": None, "error": str(exc)[:200]}
     if rank == 0:

@@ -373,9 +373,15 @@ MINICPMO_API size_t minicpmo_gpu_context_tensor_device_bytes(void *handle, const
  * device (limits above).  Set-up happens on the first call made with a given
  * device current (the symbol's address and the kernels' shared-memory
  * opt-in); make that first call before any stream capture.  Each call clears
- * the split counters on `stream` before launching.  Calls that overlap on the
- * GPU (other streams, other host threads) share the scratch and race:
- * serialise them.  Returns 1, or 0 with a message in `error`. */
+ * the split counters and an error word on `stream` before launching.  Calls
+ * that overlap on the GPU (other streams, other host threads) share the
+ * scratch and race: serialise them.  head_count must be a multiple of
+ * kv_head_count (at most 8 heads per kv head).  Returns 1, or 0 with a
+ * message in `error`; the checks are on the host, before any CUDA call.  The
+ * call is asynchronous: a bounded wait inside the kernel that gives up (only
+ * a fault elsewhere on the device makes one) is recorded in the scratch's
+ * error word but not reported back, and the output of that call is then
+ * undefined. */
 MINICPMO_API int minicpmo_gpu_attention_no_alloc(const float *q, const void *k_cache, const void *v_cache, int kv_f16,
                                     size_t pos, size_t head_count, size_t kv_head_count, size_t head_dim,
                                     size_t context_capacity, float *dst, void *stream, char *error, size_t error_cap);

@@ -11,7 +11,11 @@
 // device: cudaGetSymbolAddress for that device's copy of the scratch array
 // and the kernels' shared-memory opt-in.  Make that first call before any
 // stream capture.  Every call clears the split counters (they must start at
-// zero) with an asynchronous memset on the caller's stream, then launches.
+// zero) and the error word with one asynchronous memset on the caller's
+// stream, then launches.  A bounded wait inside the kernel that gives up
+// (only a fault elsewhere on the device makes one) raises that error word;
+// the call has returned by then, so it is not reported to the caller, and
+// the output of such a call is undefined.
 // The scratch is one array per device, so calls that overlap on the GPU
 // (two streams, or two host threads) race on it; serialise them.
 #include <cuda_runtime.h>
@@ -29,11 +33,12 @@ namespace mcpo {
 namespace {
 
 constexpr size_t kCounterBytes = (size_t)MINICPMO_NOALLOC_MAX_KV_HEADS * 4;
+constexpr size_t kErrBytes = 256;  // the kernel's error word, padded to keep the partials 256-byte aligned
 constexpr size_t kPartialBytes = (size_t)MINICPMO_NOALLOC_PARTIAL_BYTES;
 constexpr int kMaxDevices = 64;
 
-// [counters: MAX_KV_HEADS x u32][partial sums: PARTIAL_BYTES]
-static __device__ __align__(256) unsigned char g_attn_scratch[kCounterBytes + kPartialBytes];
+// [counters: MAX_KV_HEADS x u32][error word, padded][partial sums: PARTIAL_BYTES]
+static __device__ __align__(256) unsigned char g_attn_scratch[kCounterBytes + kErrBytes + kPartialBytes];
 
 std::mutex g_setup_mu;
 unsigned char* g_scratch_ptr[kMaxDevices] = {};
@@ -83,6 +88,9 @@ extern "C" int minicpmo_gpu_attention_no_alloc(const float* q, const void* k_cac
   if (!(head_dim == 64 || head_dim == 128 || head_dim == 256 || head_dim <= 32))
     return put_error(error, error_cap, "error: no_alloc attention: head_dim must be 64, 128, 256 or <= 32 (got %zu)",
                      head_dim);
+  if (head_count < kv_head_count)
+    return put_error(error, error_cap, "error: no_alloc attention: %zu heads fewer than %zu kv heads", head_count,
+                     kv_head_count);
   if (head_count % kv_head_count != 0 || head_count / kv_head_count > 8)
     return put_error(error, error_cap, "error: no_alloc attention: %zu heads over %zu kv heads (need a group of <= 8)",
                      head_count, kv_head_count);
@@ -106,7 +114,8 @@ extern "C" int minicpmo_gpu_attention_no_alloc(const float* q, const void* k_cac
   if (!scratch) return 0;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   unsigned* counters = reinterpret_cast<unsigned*>(scratch);
-  cudaError_t e = cudaMemsetAsync(counters, 0, kv_head_count * 4, st);
+  int* err_word = reinterpret_cast<int*>(scratch + kCounterBytes);
+  cudaError_t e = cudaMemsetAsync(counters, 0, kCounterBytes + sizeof(int), st);
   if (e != cudaSuccess) return put_error(error, error_cap, "error: no_alloc attention: counter clear: %s", cudaGetErrorString(e));
 
   AttnArgs a{};
@@ -123,10 +132,11 @@ extern "C" int minicpmo_gpu_attention_no_alloc(const float* q, const void* k_cac
   a.ctx = (int)context_capacity;
   a.n_split = n_split;
   a.scale = 1.0f / sqrtf((float)head_dim);
-  a.partial = reinterpret_cast<float*>(scratch + kCounterBytes);
+  a.partial = reinterpret_cast<float*>(scratch + kCounterBytes + kErrBytes);
   a.counters = counters;
   a.out = dst;
   a.out_q8 = nullptr;
+  a.err = err_word;
   e = launch_attention(a, st);
   if (e != cudaSuccess) return put_error(error, error_cap, "error: no_alloc attention: launch: %s", cudaGetErrorString(e));
   return 1;

@@ -147,7 +147,7 @@ def quantize(x, dtype: int):
 
 
 # ---------------------------------------------------------------------------
-# synthetic Qwen3 models (SURVEY-style seeded configs)
+# synthetic Qwen3 models (seeded configs of the benchmark shapes)
 # ---------------------------------------------------------------------------
 
 @dataclass

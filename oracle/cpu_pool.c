@@ -112,7 +112,8 @@ void orc_pool_destroy(void *pool) {
     if (!p) return;
     p->stop = 1;
     for (i = 1; i < p->threads; ++i) pthread_join(p->tids[i], NULL);
-    if (p->ref_lib) dlclose(p->ref_lib);
+    /* the reference library stays mapped until the process exits: a later
+     * pool reuses it, and the mapping shows which native code ran */
     free(p->tids);
     free(p);
 }

@@ -1,7 +1,7 @@
 #!/usr/bin/env python3
 """Generates tests/golden/reference_vectors.npz from the reference's own code.
 
-Run where the reference tree is available (``make -C oracle`` builds
+Run where the reference tree is available (``make -C oracle REF=<tree>`` builds
 oracle/_ref/ from it first).  Every output array is computed by reference
 code compiled from its sources, not by this repository:
 

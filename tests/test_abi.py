@@ -68,6 +68,8 @@ def test_no_alloc_attention_limits_are_checked_on_the_host(pkg):
     assert b"kv heads exceed" in err.value
     assert fn(p, p, p, 0, 0, 32, 2, 128, 1, p, None, err, 512) == 0  # group of 16
     assert b"group" in err.value
+    assert fn(p, p, p, 0, 0, 4, 8, 128, 1, p, None, err, 512) == 0  # 4 heads over 8 kv heads
+    assert b"fewer than 8 kv heads" in err.value
     assert fn(p, p, p, 0, 5, 8, 8, 128, 5, p, None, err, 512) == 0  # pos outside the context
     assert b"outside context" in err.value
     assert fn(None, p, p, 0, 0, 8, 8, 128, 1, p, None, err, 512) == 0
