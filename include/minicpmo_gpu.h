@@ -238,6 +238,17 @@ MINICPMO_API int minicpmo_gpu_context_qwen3_prefill(void *handle, const uint32_t
                                        float *out_top2_gap, float *logits_out, char *error, size_t error_cap);
 /* Clears the sampler's seen set (a new session, qwen3.uya:2999-3007). */
 MINICPMO_API int minicpmo_gpu_context_qwen3_reset(void *handle, char *error, size_t error_cap);
+/* Save and restore a session's KV prefix: copy rows [first_pos, first_pos +
+ * n_pos) of layer `layer`'s K and V caches from host memory (kv_write) or
+ * to it (kv_read).  A row is kv_heads * head_dim values (under tensor
+ * parallelism this rank's heads) in the cache's element type: f32, or f16
+ * when the model was bound with kv_f16.  Synchronous.  Not available for a
+ * batched model.  No reference counterpart (the reference keeps its cache in
+ * the helper, gpu_shim.c:1385-1454, and never exposes it). */
+MINICPMO_API int minicpmo_gpu_context_qwen3_kv_write(void *handle, size_t layer, size_t first_pos, size_t n_pos,
+                                        const void *k_rows, const void *v_rows, char *error, size_t error_cap);
+MINICPMO_API int minicpmo_gpu_context_qwen3_kv_read(void *handle, size_t layer, size_t first_pos, size_t n_pos,
+                                       void *k_rows, void *v_rows, char *error, size_t error_cap);
 
 /* Greedy decode of n_steps tokens entirely on the device, feeding each
  * sampled token back (the generate loop, qwen3.uya:2559-2639, without host

@@ -2485,6 +2485,48 @@ int minicpmo_gpu_context_qwen3_reset(void* handle, char* error, size_t error_cap
              : 0;
 }
 
+// Rows [first_pos, first_pos + n_pos) of one layer's K and V caches from or
+// to host memory (write != 0: host -> device).  Rows are kv_heads*head_dim
+// values in the cache's element type.
+int kv_rows_impl(Ctx* c, size_t layer, size_t first_pos, size_t n_pos, void* k_rows, void* v_rows, int write,
+                 char* error, size_t error_cap) {
+  if (!c) return copy_error(error, error_cap, "error: null gpu context"), 0;
+  DeviceGuard g(c);
+  const char* what = write ? "qwen3 kv write" : "qwen3 kv read";
+  if (!c->model) return fail(c, error, error_cap, "error: %s: model not bound", what);
+  Model& m = *c->model;
+  const minicpmo_qwen3_config& cf = m.cfg;
+  if (m.batch) return fail(c, error, error_cap, "error: %s: not available for a batched model", what);
+  if (layer >= cf.layers) return fail(c, error, error_cap, "error: %s: layer %zu of %u", what, layer, cf.layers);
+  if (first_pos > cf.context || n_pos > cf.context - first_pos)
+    return fail(c, error, error_cap, "error: %s: positions %zu..%zu outside context %u", what, first_pos,
+                first_pos + n_pos, cf.context);
+  if (n_pos == 0) return 1;
+  if (!k_rows || !v_rows) return fail(c, error, error_cap, "error: %s: null rows", what);
+  const size_t esz = cf.kv_f16 ? 2 : 4;
+  const size_t off = (layer * m.kv_layer_elems + first_pos * m.kvd) * esz, bytes = n_pos * m.kvd * esz;
+  uint8_t* kd = (uint8_t*)m.kc + off;
+  uint8_t* vd = (uint8_t*)m.vc + off;
+  cudaError_t e = write ? cudaMemcpyAsync(kd, k_rows, bytes, cudaMemcpyHostToDevice, c->stream)
+                        : cudaMemcpyAsync(k_rows, kd, bytes, cudaMemcpyDeviceToHost, c->stream);
+  if (e == cudaSuccess)
+    e = write ? cudaMemcpyAsync(vd, v_rows, bytes, cudaMemcpyHostToDevice, c->stream)
+              : cudaMemcpyAsync(v_rows, vd, bytes, cudaMemcpyDeviceToHost, c->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+  return cuda_ok(c, e, write ? "kv_write" : "kv_read", error, error_cap) ? 1 : 0;
+}
+
+int minicpmo_gpu_context_qwen3_kv_write(void* handle, size_t layer, size_t first_pos, size_t n_pos, const void* k_rows,
+                                        const void* v_rows, char* error, size_t error_cap) {
+  return kv_rows_impl((Ctx*)handle, layer, first_pos, n_pos, const_cast<void*>(k_rows), const_cast<void*>(v_rows), 1,
+                      error, error_cap);
+}
+
+int minicpmo_gpu_context_qwen3_kv_read(void* handle, size_t layer, size_t first_pos, size_t n_pos, void* k_rows,
+                                       void* v_rows, char* error, size_t error_cap) {
+  return kv_rows_impl((Ctx*)handle, layer, first_pos, n_pos, k_rows, v_rows, 0, error, error_cap);
+}
+
 }  // extern "C"
 
 namespace {

@@ -131,6 +131,8 @@ SIGNATURES = {
     "minicpmo_gpu_context_qwen3_sample": (i32, [vp, u32ptr, sz, f32, u32, f32, f32, f32, u32ptr, u32ptr] + E),
     "minicpmo_gpu_context_qwen3_prefill": (i32, [vp, u32ptr, sz, sz, i32, f32, u32ptr, fptr, fptr] + E),
     "minicpmo_gpu_context_qwen3_reset": (i32, [vp] + E),
+    "minicpmo_gpu_context_qwen3_kv_write": (i32, [vp, sz, sz, sz, vp, vp] + E),
+    "minicpmo_gpu_context_qwen3_kv_read": (i32, [vp, sz, sz, sz, vp, vp] + E),
     "minicpmo_gpu_context_qwen3_decode": (i32, [vp, u32, sz, sz, f32, u32ptr] + E),
     "minicpmo_gpu_context_q8_1_quantize": (i32, [vp, fptr, sz, vp] + E),
     "minicpmo_gpu_context_rms_norm_q8_1": (i32, [vp, fptr, vp, sz, f32, fptr, vp] + E),
@@ -395,6 +397,21 @@ class GpuContext:
 
     def qwen3_reset(self) -> None:
         self._call("minicpmo_gpu_context_qwen3_reset")
+
+    def qwen3_kv_write(self, layer: int, first_pos: int, k_rows: np.ndarray, v_rows: np.ndarray) -> None:
+        """Rows [first_pos, first_pos + len) of one layer's K/V cache from host arrays (f32, or f16 for an
+        f16 cache), each row kv_heads * head_dim values."""
+        k = np.ascontiguousarray(k_rows)
+        v = np.ascontiguousarray(v_rows)
+        if k.shape != v.shape or k.ndim != 2:
+            raise ValueError("k_rows and v_rows must be [n_pos][kv_dim] arrays of one shape")
+        self._call("minicpmo_gpu_context_qwen3_kv_write", layer, first_pos, k.shape[0], k.ctypes.data, v.ctypes.data)
+
+    def qwen3_kv_read(self, layer: int, first_pos: int, n_pos: int, kv_dim: int, dtype=np.float32):
+        k = np.empty((n_pos, kv_dim), dtype)
+        v = np.empty((n_pos, kv_dim), dtype)
+        self._call("minicpmo_gpu_context_qwen3_kv_read", layer, first_pos, n_pos, k.ctypes.data, v.ctypes.data)
+        return k, v
 
     def qwen3_decode(self, first_token: int, first_pos: int, steps: int, penalty: float = 1.0) -> np.ndarray:
         toks = np.empty(steps, np.uint32)

@@ -34,6 +34,8 @@ typedef struct orc_pool {
     const uint8_t *w;
     size_t rows, cols, row_bytes;
     const float *x;
+    const uint8_t *xq;  /* Q8_1 task: the quantised activations */
+    int q8_1_order;     /* Q8_1 task: 1 device order, 0 natural order; -1 an f32 task */
     float *y;
     volatile int failed;
 } orc_pool;
@@ -44,7 +46,14 @@ static void do_part(orc_pool *p, int part) {
     size_t start = p->rows * (size_t) part / (size_t) p->threads;
     size_t end = p->rows * (size_t) (part + 1) / (size_t) p->threads;
     if (end <= start) return;
-    if (p->ref_range) {
+    if (p->q8_1_order >= 0) {
+        /* every row is computed on its own, so a row range gives the rows'
+         * bits of the whole-matrix call */
+        const uint8_t *w = p->w + start * p->row_bytes;
+        if (!(p->q8_1_order ? orc_matvec_q8_1_dev(p->dtype, w, end - start, p->cols, p->xq, p->y + start)
+                            : orc_matvec_q8_1(p->dtype, w, end - start, p->cols, p->xq, p->y + start)))
+            p->failed = 1;
+    } else if (p->ref_range) {
         if (!p->ref_range(p->y, p->w, p->dtype, p->x, p->cols, start, end)) p->failed = 1;
     } else {
         if (!orc_matvec_f32(p->dtype, p->w + start * p->row_bytes, end - start, p->cols, p->x, p->y + start)) p->failed = 1;
@@ -90,11 +99,26 @@ void *orc_pool_create(int threads, const char *ref_cpu_so) {
 
 int orc_pool_is_reference(void *pool) { return pool && ((orc_pool *) pool)->ref_range != NULL; }
 
+static int run_task(orc_pool *p);
+
 int orc_pool_matvec(void *user, int dtype, const uint8_t *w, size_t rows, size_t cols, const float *x, float *y) {
     orc_pool *p = (orc_pool *) user;
-    unsigned long target;
     p->dtype = dtype; p->w = w; p->rows = rows; p->cols = cols; p->x = x; p->y = y;
-    p->row_bytes = orc_row_bytes(dtype, cols);
+    p->xq = NULL; p->q8_1_order = -1;
+    return run_task(p);
+}
+
+int orc_pool_matvec_q8_1(void *user, int order, int dtype, const uint8_t *w, size_t rows, size_t cols,
+                         const uint8_t *xq, float *y) {
+    orc_pool *p = (orc_pool *) user;
+    p->dtype = dtype; p->w = w; p->rows = rows; p->cols = cols; p->x = NULL; p->y = y;
+    p->xq = xq; p->q8_1_order = order ? 1 : 0;
+    return run_task(p);
+}
+
+static int run_task(orc_pool *p) {
+    unsigned long target;
+    p->row_bytes = orc_row_bytes(p->dtype, p->cols);
     p->failed = 0;
     if (p->row_bytes == 0) return 0;
     if (p->threads == 1) { do_part(p, 0); return !p->failed; }

@@ -931,6 +931,8 @@ static int mv(const orc_state *st, int dtype, const uint8_t *w, size_t rows, siz
               uint8_t *xq_scratch) {
     if (st->q8_1_activations && (dtype == ORC_Q4_K || dtype == ORC_Q6_K || dtype == ORC_Q8_0)) {
         if (!orc_q8_1_quantize(x, cols, xq_scratch)) return 0;
+        if (st->matvec_user) /* threaded over rows; the same bits */
+            return orc_pool_matvec_q8_1(st->matvec_user, st->norm_order == 1, dtype, w, rows, cols, xq_scratch, y);
         if (st->norm_order == 1) return orc_matvec_q8_1_dev(dtype, w, rows, cols, xq_scratch, y);
         return orc_matvec_q8_1(dtype, w, rows, cols, xq_scratch, y);
     }

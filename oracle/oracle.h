@@ -149,8 +149,20 @@ typedef struct orc_state {
      * 1: the device evaluation order above (bit-exact contract) */
     int norm_order;
     int kv_f16; /* order 1 only: the KV cache stores f16 (RNE) values */
-    orc_matvec_fn matvec; void *matvec_user; /* optional, mode 0 only */
+    /* optional row pool (cpu_pool.c): mode 0 through matvec, mode 1 through
+     * orc_pool_matvec_q8_1 on matvec_user */
+    orc_matvec_fn matvec; void *matvec_user;
 } orc_state;
+
+/* cpu_pool.c: a row-partitioned thread pool (threads >= 1; ref_cpu_so names
+ * the reference's cpu_kernels.c build for mode 0, or NULL) */
+void *orc_pool_create(int threads, const char *ref_cpu_so);
+void orc_pool_destroy(void *pool);
+void orc_state_attach_pool(orc_state *st, void *pool);
+/* Q8_1 matvec over the pool's threads: order 1 device order, 0 natural
+ * order; every row's bits equal the single-threaded call's */
+int orc_pool_matvec_q8_1(void *pool, int order, int dtype, const uint8_t *w, size_t rows, size_t cols,
+                         const uint8_t *xq, float *y);
 
 size_t orc_state_kv_floats(const orc_model *m);
 /* logits may be NULL (no lm_head); hidden_out may be NULL. */

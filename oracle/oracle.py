@@ -346,8 +346,9 @@ class OracleModel:
         st.kv_f16 = int(kv_f16)
         self.state = st
         self.pool = None
-        if pool_threads and not q8_1:
-            ref = str(REF_DIR / "libref_cpu.so") if use_reference_matvec and (REF_DIR / "libref_cpu.so").exists() else None
+        if pool_threads:
+            ref = (str(REF_DIR / "libref_cpu.so")
+                   if use_reference_matvec and not q8_1 and (REF_DIR / "libref_cpu.so").exists() else None)
             self.pool = orc().orc_pool_create(pool_threads, ref.encode() if ref else None)
             orc().orc_state_attach_pool(C.byref(self.state), self.pool)
 

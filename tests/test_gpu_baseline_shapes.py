@@ -1,0 +1,235 @@
+"""Parity at the benchmark shapes themselves (1, 2 and the
+per-layer shapes of config 4), through the C ABI on the B200.
+
+Config 1 (the isolated GEMV sweep): y = W.x at 4096x4096, 12288x4096,
+4096x12288 and 151936x4096 for Q4_K, Q6_K and Q8_0 weights (N(0, 0.02)),
+x N(0, 1):
+  * Q8_1 activations (matvec_q8_1 and the reference-facing host entry
+    minicpmo_gpu_context_matvec): per-block int32 dots and rows bit-exact
+    against the oracle's device order; <= 1e-5 per-row/||y|| against the
+    natural order (the reference's CUDA arithmetic, gpu_shim.c:746-925);
+    <= 1e-3 against the reference's own f32-activation CPU matvec
+    (cpu_kernels.c:791-851, built from the reference tree into oracle/_ref)
+    and its restatement -- the north star's matvec tolerance;
+  * the fused prologues: RMSNorm(eps 1e-6) -> Q8_1 for the 4096-wide inputs,
+    SwiGLU (slot silu_mul) -> Q8_1 for the 12288-wide down input: bit-exact
+    against the oracle chain, <= 1e-3 against the f32 CPU chain.
+
+Configs 0, 2 and 4 (whole decode steps, teacher-forced):
+  * logits bit-identical at every step to the oracle restating the
+    reference's CUDA arithmetic in device order (so greedy tokens and top-2
+    gaps are identical too);
+  * against the reference's CPU path (f32 activations, cpu_kernels.c
+    matvec in a row pool): logits within LOGIT_TOL_F32 of their L2 norm, and
+    the greedy token identical wherever that path's top-2 gap exceeds twice
+    the step's largest logit difference (a smaller gap can flip on the
+    activation quantisation alone: the reference's own CUDA arithmetic, which
+    the GPU reproduces bit for bit, flips there too).  The flips and the worst
+    logit error are printed.
+"""
+from __future__ import annotations
+
+import os
+
+import numpy as np
+import pytest
+
+from conftest import rel_row_err
+
+pytestmark = pytest.mark.gpu
+
+Q4_K, Q6_K, Q8_0, F32 = 10, 12, 6, 0
+NAMES = {Q4_K: "Q4_K", Q6_K: "Q6_K", Q8_0: "Q8_0"}
+MATVEC_TOL = 1e-5       # vs the oracle on identical Q8_1 activations (summation order only)
+NORTH_STAR_TOL = 1e-3   # per-row error / ||y||_2 vs the f32-activation CPU path
+LOGIT_TOL_F32 = 1e-3    # whole-step logits vs the f32-activation CPU path
+THREADS = max(1, min(32, os.cpu_count() or 1))
+
+SWEEP = [(4096, 4096), (12288, 4096), (4096, 12288), (151936, 4096)]
+
+
+def rvec(n, seed, scale=1.0):
+    return (np.random.Generator(np.random.PCG64(seed)).standard_normal(n) * scale).astype(np.float32)
+
+
+def sweep_tensor(dt, rows, cols):
+    from minicpmo_b200 import gguf
+    from minicpmo_b200.gpu import Tensor
+
+    name = f"sweep.{NAMES[dt]}.{rows}x{cols}"
+    return Tensor(name, gguf.synth_tensor(name, dt, rows, cols, "w", device="cuda"), dt, rows, cols)
+
+
+def f32_reference_matvec(O, dt, t, x):
+    """The reference's own cpu_kernels.c matvec when oracle/_ref is built, else its restatement."""
+    if O.ref_lib("cpu") is not None:
+        return O.ref_cpu_matvec(dt, t.data, t.rows, t.cols, x)
+    return O.matvec_f32(dt, t.data, t.rows, t.cols, x)
+
+
+@pytest.mark.parametrize("dt", [Q4_K, Q6_K, Q8_0])
+@pytest.mark.parametrize("rows,cols", SWEEP)
+def test_config1_matvec(pkg, gpu_ctx, O, dt, rows, cols):
+    t = sweep_tensor(dt, rows, cols)
+    gpu_ctx.upload_tensor(t)
+    x = rvec(cols, rows + cols + dt)
+    xq = O.q8_1_quantize(x)
+    assert np.array_equal(gpu_ctx.q8_1_quantize(x), xq)
+    want_dots = rows <= 12288
+    y, dots = gpu_ctx.matvec_q8_1(t, xq, dots=want_dots)
+    if want_dots:
+        assert np.array_equal(dots, O.block_dots(dt, t.data, rows, cols, xq))
+    assert np.array_equal(y, O.matvec_q8_1_dev(dt, t.data, rows, cols, xq))
+    assert rel_row_err(y, O.matvec_q8_1(dt, t.data, rows, cols, xq)) < MATVEC_TOL
+    if dt in (Q4_K, Q6_K) and O.ref_lib("kernels") is not None and rows <= 12288:
+        assert rel_row_err(y, O.ref_kernel_matvec(dt, t.data, rows, cols, xq)) < MATVEC_TOL
+    # the reference-facing entry (host x in, host y out, gpu_shim.c:2529-2719)
+    assert np.array_equal(gpu_ctx.matvec(t, x), y)
+    err_cpu = rel_row_err(y, f32_reference_matvec(O, dt, t, x))
+    err_port = rel_row_err(y, O.matvec_f32(dt, t.data, rows, cols, x))
+    print(f"[config1] {NAMES[dt]} {rows}x{cols}: vs f32 CPU path {err_cpu:.2e} (restatement {err_port:.2e})")
+    assert err_cpu < NORTH_STAR_TOL and err_port < NORTH_STAR_TOL
+
+
+@pytest.mark.parametrize("dt", [Q4_K, Q6_K, Q8_0])
+@pytest.mark.parametrize("rows", [4096, 12288, 151936])
+def test_config1_rmsnorm_prologue(pkg, gpu_ctx, O, dt, rows):
+    """The fused RMSNorm(eps 1e-6) -> Q8_1 prologue of the 4096-wide GEMVs."""
+    from minicpmo_b200 import gguf
+    from minicpmo_b200.gpu import Tensor
+
+    cols = 4096
+    t = sweep_tensor(dt, rows, cols)
+    gpu_ctx.upload_tensor(t)
+    nw = Tensor("sweep.norm4096", gguf.synth_tensor("sweep.norm4096", F32, 1, cols, "norm"), F32, 1, cols)
+    gpu_ctx.upload_tensor(nw)
+    wf = nw.data.view(np.float32).reshape(-1)
+    x = rvec(cols, rows + 17)
+    y = gpu_ctx.matvec_f32_input(t, x, nw, 1e-6)
+    normed = O.rms_norm(x, wf, F32, 1e-6, order=1)
+    assert np.array_equal(y, O.matvec_q8_1_dev(dt, t.data, rows, cols, O.q8_1_quantize(normed)))
+    ref = f32_reference_matvec(O, dt, t, O.rms_norm(x, wf, F32, 1e-6, order=0))
+    assert rel_row_err(y, ref) < NORTH_STAR_TOL
+
+
+@pytest.mark.parametrize("dt", [Q4_K, Q6_K, Q8_0])
+def test_config1_swiglu_prologue(pkg, gpu_ctx, O, dt):
+    """The down projection (4096x12288) on SwiGLU(gate, up) of N(0, 1) gate/up values."""
+    rows, cols = 4096, 12288
+    t = sweep_tensor(dt, rows, cols)
+    gpu_ctx.upload_tensor(t)
+    g, u = rvec(cols, 31), rvec(cols, 32)
+    gpu_ctx.slot_upload(10, g)
+    gpu_ctx.slot_upload(11, u)
+    gpu_ctx.slot_silu_mul(12, 10, 11, cols)
+    fused = gpu_ctx.slot_download(12, cols)
+    assert np.array_equal(fused, O.silu_mul_dev(g, u))
+    y = gpu_ctx.matvec_f32_input(t, fused)
+    assert np.array_equal(y, O.matvec_q8_1_dev(dt, t.data, rows, cols, O.q8_1_quantize(fused)))
+    assert rel_row_err(y, f32_reference_matvec(O, dt, t, O.silu_mul(g, u))) < NORTH_STAR_TOL
+
+
+# --------------------------------------------------------------- whole steps
+def _models(pkg, O, shape, mix, context):
+    from minicpmo_b200 import gguf
+    from minicpmo_b200.qwen3 import Qwen3Runtime
+
+    tensors = gguf.synth_model(shape, mix, device="cuda")
+    rt = Qwen3Runtime.open(tensors, shape=shape, context=context)
+    tmap = {n: (dt, r, c, d) for n, dt, r, c, d in tensors}
+    dev = O.OracleModel(shape, tmap, context, q8_1=True, pool_threads=THREADS)
+    cpu = O.OracleModel(shape, tmap, context, q8_1=False, pool_threads=THREADS, use_reference_matvec=True)
+    return rt, dev, cpu
+
+
+def _step(O, rt, dev, cpu, token, pos, stats):
+    lg = np.empty(rt.shape.vocab, np.float32)
+    tok_gpu, gap_gpu = rt.forward(token, pos, logits=True, want_logits=lg)
+    ref, _ = dev.forward(token, pos)
+    assert np.array_equal(lg, ref), (pos, rel_row_err(lg, ref))
+    tok_dev, gap_dev = O.argmax_penalized(ref)
+    assert (tok_gpu, gap_gpu) == (tok_dev, gap_dev), pos
+    f32, _ = cpu.forward(token, pos)
+    tok_cpu, gap_cpu = O.argmax_penalized(f32)
+    err = rel_row_err(lg, f32)
+    dmax = float(np.max(np.abs(lg.astype(np.float64) - f32)))
+    stats["worst"] = max(stats["worst"], err)
+    stats["dmax"] = max(stats["dmax"], dmax)
+    stats["steps"] += 1
+    assert err < LOGIT_TOL_F32, (pos, err)
+    if tok_gpu != tok_cpu:
+        stats["flips"].append((pos, tok_gpu, tok_cpu, gap_cpu, dmax))
+        assert gap_cpu <= 2 * dmax, (pos, gap_cpu, dmax)
+    return tok_gpu
+
+
+def _report(label, stats):
+    flips = stats["flips"]
+    print(f"[{label}] {stats['steps']} steps bit-identical to the device-order oracle; vs the f32 CPU path: "
+          f"worst logit err {stats['worst']:.3e} of ||logits||, max |dlogit| {stats['dmax']:.3e}, "
+          f"{len(flips)} greedy flips" + (f" (gap <= 2 max|dlogit| each: {flips})" if flips else ""))
+
+
+def test_config0_full_shape_decode(pkg, O):
+    """Qwen3-0.6B shape (28 layers, vocab 151936, tied Q6_K lm_head): the
+    64-id prompt of config 0, then 16 greedy steps, every step checked."""
+    from minicpmo_b200 import gguf
+
+    shape = gguf.Qwen3Shape(**{**gguf.SHAPES["qwen3-0.6b"].__dict__, "context": 96})
+    rt, dev, cpu = _models(pkg, O, shape, gguf.Q4_K_M, 96)
+    ids = gguf.prompt_ids(64, shape.vocab, seed=7)
+    stats = {"worst": 0.0, "dmax": 0.0, "steps": 0, "flips": []}
+    tok = None
+    for pos in range(80):
+        tok = _step(O, rt, dev, cpu, int(ids[pos]) if pos < 64 else tok, pos, stats)
+    _report("config0 qwen3-0.6b", stats)
+    rt.close()
+    dev.close()
+    cpu.close()
+
+
+def _seeded_prefix_decode(pkg, O, shape, prefix, steps, label):
+    from minicpmo_b200 import gguf
+
+    ctx = prefix + steps + 8
+    rt, dev, cpu = _models(pkg, O, shape, gguf.Q4_K_M, ctx)
+    kvd = shape.kv_dim
+    rng = np.random.Generator(np.random.PCG64(prefix))
+    for m in (dev, cpu):
+        assert m.kc.size == shape.layers * ctx * kvd
+    for layer in range(shape.layers):
+        k = rng.standard_normal((prefix, kvd), dtype=np.float32)
+        v = rng.standard_normal((prefix, kvd), dtype=np.float32)
+        rt.gpu.qwen3_kv_write(layer, 0, k, v)
+        for m in (dev, cpu):
+            m.kc.reshape(shape.layers, ctx, kvd)[layer, :prefix] = k
+            m.vc.reshape(shape.layers, ctx, kvd)[layer, :prefix] = v
+    kb, vb = rt.gpu.qwen3_kv_read(shape.layers - 1, prefix - 3, 3, kvd)
+    assert np.array_equal(kb, k[-3:]) and np.array_equal(vb, v[-3:])
+    ids = gguf.prompt_ids(steps, shape.vocab, seed=prefix + 1)
+    stats = {"worst": 0.0, "dmax": 0.0, "steps": 0, "flips": []}
+    for i in range(steps):
+        _step(O, rt, dev, cpu, int(ids[i]), prefix + i, stats)
+    _report(label, stats)
+    rt.close()
+    dev.close()
+    cpu.close()
+
+
+def test_config2_shape_decode_past_512(pkg, O):
+    """Qwen3-8B shape (36 layers, untied Q6_K lm_head of 151936 x 4096): a
+    seeded 512-position KV prefix (the 512-id prompt of config 2, as cache
+    contents identical on both sides), then 4 decode steps at 512..515."""
+    from minicpmo_b200 import gguf
+
+    _seeded_prefix_decode(pkg, O, gguf.SHAPES["qwen3-8b"], 512, 4, "config2 qwen3-8b")
+
+
+def test_config4_layer_shape_decode_past_256(pkg, O):
+    """The per-layer shapes of config 4 (Qwen3-32B: hidden 5120, 64 q / 8 kv
+    heads, FFN 25600, vocab 151936) on 4 layers, after a seeded 256-position
+    prefix (the prompt length of config 4)."""
+    from minicpmo_b200 import gguf
+
+    shape = gguf.Qwen3Shape(**{**gguf.SHAPES["qwen3-32b"].__dict__, "layers": 4})
+    _seeded_prefix_decode(pkg, O, shape, 256, 3, "config4 qwen3-32b shape, 4 layers")

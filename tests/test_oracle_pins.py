@@ -192,3 +192,25 @@ def test_expf_det_accuracy(O):
     ulp = np.spacing(ref[ok].astype(np.float32)).astype(np.float64)
     assert np.max(np.abs(got[ok] - ref[ok]) / ulp) <= 2.0
     assert O.expf_det(np.array([-np.inf]))[0] == 0.0 and np.isinf(O.expf_det(np.array([np.inf]))[0])
+
+
+def test_pooled_q8_1_oracle_matches_single_thread(O):
+    """The row pool used for the full-shape parity tests gives the bits of the
+    single-threaded oracle in both evaluation orders."""
+    from conftest import load_pkg
+
+    load_pkg()
+    from minicpmo_b200 import gguf
+
+    shape = gguf.Qwen3Shape(layers=2, hidden=512, heads=8, kv_heads=2, head_dim=64, ffn=1536, vocab=2048, context=16)
+    tensors = gguf.synth_model(shape, gguf.Q4_K_M)
+    tmap = {n: (dt, r, c, d) for n, dt, r, c, d in tensors}
+    for order in (True, False):
+        one = O.OracleModel(shape, tmap, 16, q8_1=True, device_order=order)
+        many = O.OracleModel(shape, tmap, 16, q8_1=True, device_order=order, pool_threads=3)
+        for pos, tok in enumerate((3, 1000, 77)):
+            a, _ = one.forward(tok, pos)
+            b, _ = many.forward(tok, pos)
+            assert np.array_equal(a, b), (order, pos)
+        one.close()
+        many.close()
