@@ -662,6 +662,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2)
       sr[k] = need ? a.rope_sin[(size_t)pos * half + d] : 0.0f;
     }
   }
+  if (a.pf.n > 0 && warp == kAttnWarps - 1)  // later kernels' weights into L2
+    l2_prefetch_share(a.pf, (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x,
+                      gridDim.x * gridDim.y * gridDim.z, lane, 32);
   pdl_wait();
   pdl_launch_dependents();
 

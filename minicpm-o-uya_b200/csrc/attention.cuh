@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "prefetch.cuh"
+
 namespace mcpo {
 
 struct AttnArgs {
@@ -49,6 +51,7 @@ struct AttnArgs {
   size_t qkv_bstride, cache_bstride, out_bstride, outq8_bstride;
   int pos_stride;  // ints between sequences' positions at pos_ptr (0: 1)
   int* err;        // raised by a bounded wait that gave up (may be null)
+  PfList pf;       // weight bytes of later kernels to prefetch into L2 before the wait (n = 0: none)
 };
 
 constexpr int kAttnMaxCluster = 16;    // cluster size (beyond 8 needs the non-portable opt-in)

@@ -105,7 +105,10 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1) k_gemv(const Gemv
     // up the copies of another).  Needs nothing from the previous kernel, so
     // it does not wait for it.
     const int w = lane;
-    if (w >= NC) return;
+    if (w >= NC) {  // idle lanes: the later kernels' weights into L2
+      if (a.pf.n > 0) l2_prefetch_share(a.pf, blockIdx.x, gridDim.x, w - NC, 32 - NC);
+      return;
+    }
     const int steps = (nwr > w ? (nwr - w + NC - 1) / NC : 0) * spi;
     const uint64_t policy = l2_evict_first_policy();
     bool ok = true;
@@ -183,7 +186,10 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1) k_gemv_multi(cons
   __syncthreads();
   if (warp == NC) {  // producer, as k_gemv
     const int w = lane;
-    if (w >= NC) return;
+    if (w >= NC) {
+      if (a.pf.n > 0) l2_prefetch_share(a.pf, blockIdx.x, gridDim.x, w - NC, 32 - NC);
+      return;
+    }
     const int steps = (nwr > w ? (nwr - w + NC - 1) / NC : 0) * spi;
     const uint64_t policy = l2_evict_first_policy();
     for (int n = 0; n < steps; ++n) {

@@ -6,6 +6,7 @@
 #include <stdint.h>
 
 #include "layout.cuh"
+#include "prefetch.cuh"
 
 namespace mcpo {
 
@@ -68,6 +69,9 @@ struct GemvArgs {
   // (36 B per 32 rows, the bits k_quantize_q8_1 gives for y), each CTA
   // taking whole 32-row blocks; a following GEMV reads them as kInQ8_1
   uint8_t* q8_out;
+  // weight bytes of later kernels to prefetch into L2 (idle producer lanes
+  // issue them at the start; n = 0: none)
+  PfList pf;
 };
 
 constexpr int kGemvMaxVec = 4;  // input vectors per multi-vector launch

@@ -506,9 +506,10 @@ void free_model(Model* m) {
 // dense ones the f32 input x.
 // With xq == nullptr a quantised GEMV quantises x itself (kInF32).
 cudaError_t model_mv(Ctx* c, Upload* w, const float* x, const uint8_t* xq, float* y, int epi, float* tmp, int grid,
-                     int* err) {
+                     int* err, const PfList* pf = nullptr) {
   if (w->tiled) {
     GemvArgs a{};
+    if (pf) a.pf = *pf;
     a.nseg = 1;
     a.cols = (int)w->cols;
     a.input = xq ? kInQ8_1 : kInF32;
@@ -583,6 +584,60 @@ void norm_input(GemvArgs* a, const float* x, const Upload* norm, float eps) {
   a->eps = eps;
 }
 
+// Bytes a GEMV streams from a weight upload.
+size_t stream_bytes(const Upload* u) { return u->tiled ? (size_t)u->geom.n_wr * u->geom.wr_bytes : u->dev_bytes; }
+
+// L2 prefetch window of the decode step (MCPO_PF_MB megabytes ahead of each
+// kernel's own weights; 0 turns prefetching off).
+size_t pf_window_cfg() {
+  static const size_t v = [] {
+    const char* e = getenv("MCPO_PF_MB");
+    return (size_t)((e && *e) ? atoi(e) : 0) << 20;
+  }();
+  return v;
+}
+
+// Plans the L2 prefetches of one decode step.  The step's weights in the
+// order the kernels stream them (per layer q, k, v, o, gate, up, down; then
+// the lm_head) form one byte stream; a kernel whose own weights end at
+// stream offset `end` prefetches the bytes from the frontier (where earlier
+// kernels' windows stopped) up to end + window, so HBM keeps streaming up
+// to `window` bytes ahead of consumption while the dependency chain runs.
+struct PfPlanner {
+  std::vector<PfRange> stream;
+  std::vector<unsigned long long> start;
+  unsigned long long total = 0, frontier = 0, window = 0;
+  void add(const Upload* u) {
+    if (!u || !u->dev) return;
+    const unsigned long long b = stream_bytes(u) & ~15ull;
+    if (b == 0 || (reinterpret_cast<uintptr_t>(u->dev) & 15)) return;
+    stream.push_back(PfRange{u->dev, b});
+    start.push_back(total);
+    total += b;
+  }
+  // the stream offset just after upload u (0 when u is not in the stream)
+  unsigned long long end_of(const Upload* u) const {
+    for (size_t i = 0; i < stream.size(); ++i)
+      if (stream[i].p == u->dev) return start[i] + stream[i].bytes;
+    return 0;
+  }
+  PfList next(unsigned long long end) {
+    PfList l{};
+    if (window == 0) return l;
+    const unsigned long long lo = frontier > end ? frontier : end;
+    const unsigned long long hi = end + window < total ? end + window : total;
+    for (size_t i = 0; i < stream.size() && lo < hi; ++i) {
+      const unsigned long long a = start[i], b = start[i] + stream[i].bytes;
+      const unsigned long long x = lo > a ? lo : a, y = hi < b ? hi : b;
+      if (x >= y) continue;
+      if (l.n == kMaxPf) break;
+      l.r[l.n++] = PfRange{stream[i].p + (x - a), y - x};
+      frontier = y;
+    }
+    return l;
+  }
+};
+
 #define REC(expr)                            \
   do {                                       \
     cudaError_t e_ = (expr);                 \
@@ -610,10 +665,20 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
                         m.am_grid, s, true));
     return cudaSuccess;
   }
+  PfPlanner pf;
+  pf.window = pf_window_cfg();
+  if (pf.window) {
+    for (uint32_t li = 0; li < cf.layers; ++li) {
+      const LayerW& L = m.layer[li];
+      for (const Upload* u : {L.q, L.k, L.v, L.o, L.gate, L.up, L.down}) pf.add(u);
+    }
+    if (logits) pf.add(m.out);
+  }
   for (uint32_t li = 0; li < cf.layers; ++li) {
     const LayerW& L = m.layer[li];
     // attention block: RMSNorm -> Q8_1 inside the q/k/v GEMV's prologue
     Upload* qkv[3] = {L.q, L.k, L.v};
+    const unsigned long long qkv_end = pf.window ? pf.end_of(L.v) : 0;
     if (groupable(qkv, 3)) {
       GemvArgs a{};
       a.nseg = 3;
@@ -622,6 +687,7 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
       a.err = &m.st->err;
       float* ys[3] = {m.q, m.k, m.v};
       for (int i = 0; i < 3; ++i) gemv_seg_from_geom(qkv[i]->geom, qkv[i]->dev, nullptr, ys[i], kEpiStore, &a.seg[i]);
+      a.pf = pf.next(qkv_end);
       REC(launch_gemv(a, m.grid_h, s, true));
     } else {
       REC(launch_rmsnorm_q8_1(m.hidden, L.attn_norm->dev, L.attn_norm->dtype, h, cf.rms_eps, m.normed, m.xq, s, true));
@@ -659,13 +725,15 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
     a.out = m.attn;
     a.out_q8 = (L.o->tiled && hd % 32 == 0) ? m.aq : nullptr;
     a.err = &m.st->err;
+    if (pf.window) a.pf = pf.next(qkv_end);
     REC(launch_attention(a, s, true));
     // (head_dim % 32 != 0: the o GEMV quantises the f32 attention output itself)
     if (tp) {  // row-parallel: this rank's partial, then hidden += sum of all ranks' partials
       REC(model_mv(c, L.o, m.attn, a.out_q8, m.peers.part[m.tp_rank][0], kEpiStore, m.tmp, m.grid_q, &m.st->err));
       REC(launch_tp_reduce_add(m.peers, 0, m.hidden, h, m.tp_epoch, &m.st->err, s));
     } else {
-      REC(model_mv(c, L.o, m.attn, a.out_q8, m.hidden, kEpiAdd, m.tmp, m.grid_q, &m.st->err));
+      const PfList opf = pf.next(pf.window ? pf.end_of(L.o) : 0);
+      REC(model_mv(c, L.o, m.attn, a.out_q8, m.hidden, kEpiAdd, m.tmp, m.grid_q, &m.st->err, &opf));
     }
     // feed-forward block: RMSNorm -> Q8_1 inside the gate/up GEMV, SwiGLU in
     // its epilogue, which also writes the Q8_1 blocks the down GEMV reads
@@ -680,6 +748,7 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
       gemv_seg_from_geom(L.gate->geom, L.gate->dev, L.up->dev, m.fused, kEpiSwiglu, &g.seg[0]);
       if (!tp && L.down->tiled && ffn_q8_cfg()) g.q8_out = m.fq;
       down_q8 = g.q8_out;
+      g.pf = pf.next(pf.window ? pf.end_of(L.up) : 0);
       REC(launch_gemv(g, m.grid_h, s, true));
     } else {
       REC(launch_rmsnorm_q8_1(m.hidden, L.ffn_norm->dev, L.ffn_norm->dtype, h, cf.rms_eps, m.normed, m.xq, s, true));
@@ -691,7 +760,8 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
       REC(model_mv(c, L.down, m.fused, nullptr, m.peers.part[m.tp_rank][1], kEpiStore, m.tmp, m.grid_f, &m.st->err));
       REC(launch_tp_reduce_add(m.peers, 1, m.hidden, h, m.tp_epoch, &m.st->err, s));
     } else {
-      REC(model_mv(c, L.down, m.fused, down_q8, m.hidden, kEpiAdd, m.tmp, m.grid_f, &m.st->err));
+      const PfList dpf = pf.next(pf.window ? pf.end_of(L.down) : 0);
+      REC(model_mv(c, L.down, m.fused, down_q8, m.hidden, kEpiAdd, m.tmp, m.grid_f, &m.st->err, &dpf));
     }
   }
   if (logits) {

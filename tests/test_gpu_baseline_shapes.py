@@ -76,9 +76,11 @@ def test_config1_matvec(pkg, gpu_ctx, O, dt, rows, cols):
     xq = O.q8_1_quantize(x)
     assert np.array_equal(gpu_ctx.q8_1_quantize(x), xq)
     want_dots = rows <= 12288
-    y, dots = gpu_ctx.matvec_q8_1(t, xq, dots=want_dots)
     if want_dots:
+        y, dots = gpu_ctx.matvec_q8_1(t, xq, dots=True)
         assert np.array_equal(dots, O.block_dots(dt, t.data, rows, cols, xq))
+    else:
+        y = gpu_ctx.matvec_q8_1(t, xq)
     assert np.array_equal(y, O.matvec_q8_1_dev(dt, t.data, rows, cols, xq))
     assert rel_row_err(y, O.matvec_q8_1(dt, t.data, rows, cols, xq)) < MATVEC_TOL
     if dt in (Q4_K, Q6_K) and O.ref_lib("kernels") is not None and rows <= 12288:
