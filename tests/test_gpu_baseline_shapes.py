@@ -42,7 +42,13 @@ Q4_K, Q6_K, Q8_0, F32 = 10, 12, 6, 0
 NAMES = {Q4_K: "Q4_K", Q6_K: "Q6_K", Q8_0: "Q8_0"}
 MATVEC_TOL = 1e-5       # vs the oracle on identical Q8_1 activations (summation order only)
 NORTH_STAR_TOL = 1e-3   # per-row error / ||y||_2 vs the f32-activation CPU path
-LOGIT_TOL_F32 = 1e-3    # whole-step logits vs the f32-activation CPU path
+# Whole-step logits vs the f32-activation CPU path: every layer's GEMVs carry
+# the Q8_1 activation rounding of the reference's CUDA arithmetic (each within
+# the 1e-3 matvec bound), and the distance compounds with depth.  The
+# device-order oracle (that arithmetic restated on the CPU, bit-identical to
+# the GPU) sits at the same distance: measured 2.4e-4 (0.6B shape, 28 layers),
+# 3.6e-4 (32B shape, 4 layers), 1.0e-3..1.2e-3 (8B shape, 36 layers).
+LOGIT_TOL_F32 = 2e-3
 THREADS = max(1, min(32, os.cpu_count() or 1))
 
 SWEEP = [(4096, 4096), (12288, 4096), (4096, 12288), (151936, 4096)]
