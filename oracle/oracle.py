@@ -414,6 +414,8 @@ def ref_lib(name: str) -> Optional[C.CDLL]:
             lib.minicpmo_gpu_q8_1_quantize_row.argtypes = [u8p, fp, sz]
             lib.minicpmo_gpu_f32_to_f16.restype = C.c_uint16
             lib.minicpmo_gpu_f32_to_f16.argtypes = [C.c_float]
+            lib.minicpmo_gpu_sqrtf_positive.restype = C.c_float
+            lib.minicpmo_gpu_sqrtf_positive.argtypes = [C.c_float]
         if lib is not None and name == "kernels":
             for fn in ("refk_q4_k_matvec", "refk_q6_k_matvec"):
                 getattr(lib, fn).restype = None
@@ -424,6 +426,12 @@ def ref_lib(name: str) -> Optional[C.CDLL]:
             lib.refk_apply_rope.argtypes = [fp, C.c_int, C.c_int, C.c_int, fp, fp]
             lib.refk_silu_mul.restype = None
             lib.refk_silu_mul.argtypes = [fp, fp, fp, C.c_int]
+            lib.refk_rms_norm.restype = None
+            lib.refk_rms_norm.argtypes = [fp, fp, u8p, C.c_int, C.c_int, C.c_float]
+            lib.refk_head_norm.restype = None
+            lib.refk_head_norm.argtypes = [fp, u8p, C.c_int, C.c_int, C.c_int]
+            lib.refk_attention_decode.restype = None
+            lib.refk_attention_decode.argtypes = [fp, fp, fp, fp] + [C.c_int] * 6 + [C.c_float]
         _ref[name] = lib
     return _ref[name]
 

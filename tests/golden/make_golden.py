@@ -12,6 +12,10 @@ code compiled from its sources, not by this repository:
 * cpu_y_<dt>     -- cpu_kernels.c:791-851 f32-activation matvec
 * rope_out       -- gpu_shim.c:665-693 rope kernel body
 * silu_out       -- gpu_shim.c:659-664
+* rms_out        -- gpu_shim.c:694-718 RMSNorm kernel (one block of 256)
+* hn_out         -- gpu_shim.c:719-745 head-norm kernel (a block per head)
+* att_out        -- gpu_shim.c:926-979 decode-attention kernel (a block
+                    per head), scale 1/minicpmo_gpu_sqrtf_positive(head_dim)
 
 Inputs are seeded (numpy PCG64) and stored alongside.  Usage:
     python tests/golden/make_golden.py
@@ -107,6 +111,35 @@ def main() -> None:
     s = np.empty_like(g)
     O.ref_lib("kernels").refk_silu_mul(s.ctypes.data_as(O.fp), g.ctypes.data_as(O.fp), u.ctypes.data_as(O.fp), g.size)
     out["silu_g"], out["silu_u"], out["silu_out"] = g, u, s
+
+    # RMSNorm, head-norm and decode-attention kernel bodies (gpu_shim.c:694-745,
+    # 926-979), one host thread per CUDA thread, phases split at __syncthreads
+    K = O.ref_lib("kernels")
+    n = 4096
+    xr = (rng.standard_normal(n) * 3).astype(np.float32)
+    wr = (1.0 + rng.standard_normal(n) * 0.02).astype(np.float32)
+    ro = np.empty(n, np.float32)
+    K.refk_rms_norm(ro.ctypes.data_as(O.fp), xr.ctypes.data_as(O.fp), wr.view(np.uint8).ctypes.data_as(O.u8p), 0, n,
+                    1e-6)
+    out["rms_x"], out["rms_w"], out["rms_out"] = xr, wr, ro
+    heads, hd = 6, 128
+    hv = (rng.standard_normal(heads * hd) * 2).astype(np.float32)
+    hw = (1.0 + rng.standard_normal(hd) * 0.02).astype(np.float32)
+    ho = hv.copy()
+    K.refk_head_norm(ho.ctypes.data_as(O.fp), hw.view(np.uint8).ctypes.data_as(O.u8p), 0, heads, hd)
+    out["hn_in"], out["hn_w"], out["hn_out"] = hv, hw, ho
+    layers, ctx, ah, akv, ahd, apos = 2, 80, 8, 2, 128, 70
+    aq = rng.standard_normal(ah * ahd).astype(np.float32)
+    ak = rng.standard_normal((layers, ctx, akv * ahd)).astype(np.float32)
+    av = rng.standard_normal((layers, ctx, akv * ahd)).astype(np.float32)
+    scale = O.ref_lib("shim").minicpmo_gpu_sqrtf_positive(float(ahd))
+    scale = np.float32(1.0) / np.float32(scale)
+    ao = np.empty(ah * ahd, np.float32)
+    K.refk_attention_decode(aq.ctypes.data_as(O.fp), ak.ctypes.data_as(O.fp), av.ctypes.data_as(O.fp),
+                            ao.ctypes.data_as(O.fp), 1, apos, ah, akv, ahd, ctx, float(scale))
+    out["att_q"], out["att_k"], out["att_v"], out["att_out"] = aq, ak, av, ao
+    out["att_shape"] = np.array([layers, ctx, ah, akv, ahd, apos], np.int32)
+    out["att_scale"] = np.array([scale], np.float32)
 
     path = Path(__file__).resolve().parent / "reference_vectors.npz"
     np.savez_compressed(path, **out)

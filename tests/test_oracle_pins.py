@@ -214,3 +214,59 @@ def test_pooled_q8_1_oracle_matches_single_thread(O):
             assert np.array_equal(a, b), (order, pos)
         one.close()
         many.close()
+
+
+# ------------------------------------- 2b. norm and attention kernel bodies
+def test_rms_norm_pinned_to_reference_kernel(O, golden):
+    """gpu_shim.c:694-718 run on the host (256 threads, phases at __syncthreads):
+    the device-order RMSNorm restatement gives its bits (rsqrtf taken as 1/sqrtf)."""
+    y = O.rms_norm(golden["rms_x"], golden["rms_w"], 0, 1e-6, order=1)
+    assert np.array_equal(y, golden["rms_out"])
+    # the reference CPU order (sequential sum) within a few ulp
+    assert rel_row_err(O.rms_norm(golden["rms_x"], golden["rms_w"], 0, 1e-6, order=0), golden["rms_out"]) < 1e-6
+
+
+def test_head_norm_pinned_to_reference_kernel(O, golden):
+    """gpu_shim.c:719-745, one 256-thread block per head."""
+    heads, hd = 6, 128
+    y = O.head_norm(golden["hn_in"], golden["hn_w"], heads, hd, 0, order=1)
+    assert np.array_equal(y, golden["hn_out"])
+    assert rel_row_err(O.head_norm(golden["hn_in"], golden["hn_w"], heads, hd, 0, order=0), golden["hn_out"]) < 1e-6
+
+
+def test_attention_pinned_to_reference_kernel(O, golden):
+    """gpu_shim.c:926-979 (online softmax per position, 256-thread dot trees):
+    the natural-order and device-order attention restatements within 1e-5."""
+    layers, ctx, heads, kv, hd, pos = (int(v) for v in golden["att_shape"])
+    assert golden["att_scale"][0] == np.float32(1.0) / np.float32(np.sqrt(np.float32(hd)))
+    kc, vc = golden["att_k"], golden["att_v"]
+    ref = golden["att_out"]
+    nat = O.attention(golden["att_q"], kc, vc, 1, pos, heads, kv, hd, ctx)
+    dev = O.attention_dev(golden["att_q"], kc, vc, kc[1, pos], vc[1, pos], 1, pos, heads, kv, hd, ctx)
+    assert rel_row_err(nat, ref) < 1e-5
+    assert rel_row_err(dev, ref) < 1e-5
+
+
+def test_norm_and_attention_kernels_live(O):
+    """The same pins on fresh inputs when oracle/_ref is built here."""
+    K = O.ref_lib("kernels")
+    if K is None:
+        pytest.skip("oracle/_ref not built")
+    rng = np.random.Generator(np.random.PCG64(4242))
+    for n in (1024, 5120, 12288):
+        x = (rng.standard_normal(n) * 2).astype(np.float32)
+        w = (1 + rng.standard_normal(n) * 0.02).astype(np.float32)
+        out = np.empty(n, np.float32)
+        K.refk_rms_norm(out.ctypes.data_as(O.fp), x.ctypes.data_as(O.fp), w.view(np.uint8).ctypes.data_as(O.u8p), 0,
+                        n, 1e-6)
+        assert np.array_equal(O.rms_norm(x, w, 0, 1e-6, order=1), out), n
+    layers, ctx, heads, kv, hd = 1, 40, 4, 1, 64
+    q = rng.standard_normal(heads * hd).astype(np.float32)
+    kc = rng.standard_normal((layers, ctx, kv * hd)).astype(np.float32)
+    vc = rng.standard_normal((layers, ctx, kv * hd)).astype(np.float32)
+    for pos in (0, 31, 39):
+        out = np.empty(heads * hd, np.float32)
+        scale = float(np.float32(1.0) / np.float32(np.sqrt(np.float32(hd))))
+        K.refk_attention_decode(q.ctypes.data_as(O.fp), kc.ctypes.data_as(O.fp), vc.ctypes.data_as(O.fp),
+                                out.ctypes.data_as(O.fp), 0, pos, heads, kv, hd, ctx, scale)
+        assert rel_row_err(O.attention(q, kc, vc, 0, pos, heads, kv, hd, ctx), out) < 1e-5
