@@ -22,8 +22,11 @@ as one CUDA-graph replay.
             bounded sample of the same workload.
 
 --impl reference runs only that CPU reference arm.  Under torchrun with N > 1
-each rank decodes an independent sequence on its own GPU (replicas; the
-tensor-parallel path is separate).  Weights are seeded synthetic N(0, 0.02)
+the N GPUs decode one sequence with tensor parallelism (q/k/v and gate/up
+column-parallel, o and down row-parallel with the hidden-vector exchange
+fused into those GEMVs over NVLink, the lm_head vocab-parallel; strong
+scaling); --replicas runs N independent sequences instead (weak scaling).
+Weights are seeded synthetic N(0, 0.02)
 quantised Q4_K_M-style (no real checkpoint exists here).
 """
 from __future__ import annotations
@@ -454,9 +457,10 @@ def main() -> int:
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--shape", default="qwen3-8b")
     ap.add_argument("--cpu-sample", type=int, default=4, help="decode tokens for the CPU baseline sample (0: skip)")
-    ap.add_argument("--tp", action="store_true",
-                    help="under torchrun: tensor parallelism over the N GPUs (one sequence, strong scaling) "
-                         "instead of N independent replicas")
+    ap.add_argument("--replicas", action="store_true",
+                    help="under torchrun: N independent replicas (one sequence each, weak scaling) instead of the "
+                         "default tensor parallelism over the N GPUs (one sequence, strong scaling)")
+    ap.add_argument("--tp", action="store_true", help="(the default under torchrun; kept for old command lines)")
     ap.add_argument("--kernel-sweep", action="store_true",
                     help="BASELINE config 1: time the GEMV on each shape x dtype (and its fused prologues); "
                          "one JSON line per case")
@@ -526,7 +530,7 @@ def main() -> int:
     t_gen = time.perf_counter() - t_gen
     t_load = time.perf_counter()
     tp = None
-    if args.tp and world > 1:
+    if world > 1 and not args.replicas:
         from minicpmo_b200.qwen3 import TensorParallel
 
         tp = TensorParallel(rank, world)

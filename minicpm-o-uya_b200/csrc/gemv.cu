@@ -66,7 +66,7 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1) k_gemv(const Gemv
   const int S = a.stages;
   const int slot = a.slot_bytes;
   const int NC = (int)(blockDim.x >> 5) - 1;  // consumer warps; the last warp produces
-  uint8_t* ring = smem + gemv_x_bytes(cols);
+  uint8_t* ring = smem + gemv_x_region(cols, a.input);
   uint64_t* full = reinterpret_cast<uint64_t*>(ring + (size_t)NC * S * slot);
   uint64_t* empty = full + NC * S;
 
@@ -144,6 +144,18 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1) k_gemv(const Gemv
   int n = 0;
   float* stage = a.q8_out ? reinterpret_cast<float*>(empty + NC * S) : nullptr;
   gemv_items<kClass, kDots>(a, x, ring, full, empty, S, slot, wr0, nwr, NC, warp, lane, n, nullptr, stage, blk0 * 32);
+  if (a.seg[0].epi == kEpiTpPush) {
+    // every consumer's remote stores are visible system-wide before the
+    // arrival counts say so (tp_proto.h)
+    __threadfence_system();
+    asm volatile("bar.sync 1, %0;" ::"r"(NC * 32) : "memory");
+    const GemvSeg& s0 = a.seg[0];
+    const int r0 = wr0 * s0.rpw, r1 = min((wr0 + nwr) * s0.rpw, s0.rows);
+    if (threadIdx.x == 0 && r1 > r0)
+      for (int d = 0; d < a.tp.world; ++d)
+        asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(a.tp.dst_arrive[d]), "r"((unsigned)(r1 - r0))
+                     : "memory");
+  }
   if (a.q8_out) {
     // every consumer warp arrives here once (also after a wait gave up)
     asm volatile("bar.sync 1, %0;" ::"r"(NC * 32) : "memory");
@@ -361,7 +373,16 @@ cudaError_t gemv_prepare(GemvArgs& a, int* dtypes_mask) {
     if (a.seg[i].ks != a.seg[0].ks || a.seg[i].lpr != a.seg[0].lpr) return cudaErrorInvalidValue;
   }
   if (a.seg[0].epi == kEpiSwiglu && a.nseg != 1) return cudaErrorInvalidValue;
-  if (a.input == kInQ8_1 ? !a.xq : (!a.xf || (a.input == kInRmsNorm && !a.norm_w) || a.input > kInRmsNorm))
+  const bool norm = a.input == kInRmsNorm || a.input == kInRmsNormTp;
+  if (a.input == kInQ8_1 ? !a.xq : (!a.xf || (norm && !a.norm_w) || a.input > kInRmsNormTp))
+    return cudaErrorInvalidValue;
+  const bool push = a.seg[0].epi == kEpiTpPush;
+  for (int i = 1; i < a.nseg; ++i)
+    if (a.seg[i].epi == kEpiTpPush) return cudaErrorInvalidValue;
+  if ((push || a.input == kInRmsNormTp) && (a.tp.world < 1 || a.tp.world > kTpMaxWorld || a.nvec > 1 || a.dots))
+    return cudaErrorInvalidValue;
+  if (push && (a.nseg != 1 || a.q8_out)) return cudaErrorInvalidValue;
+  if (a.input == kInRmsNormTp && (!a.tp.step || !a.tp.arrive || !a.tp.sum_out || a.tp.rows != a.cols || a.tp.nx < 1))
     return cudaErrorInvalidValue;
   if ((mask & 8) || ((mask & 4) && (mask & 3))) return cudaErrorInvalidValue;  // no mixed Q8_0 kernel
   a.total_wr = wr;
@@ -380,7 +401,7 @@ cudaError_t launch_gemv(GemvArgs& a, int grid, cudaStream_t st, bool pdl) {
   a.stages = stages;
   if (wr == 0) return cudaSuccess;
   if (a.nvec > kGemvMaxVec || (a.nvec > 1 && a.dots)) return cudaErrorInvalidValue;
-  const size_t xb = gemv_x_bytes(a.cols) * (size_t)(a.nvec > 1 ? a.nvec : 1);
+  const size_t xb = a.nvec > 1 ? gemv_x_bytes(a.cols) * (size_t)a.nvec : gemv_x_region(a.cols, a.input);
   const size_t per_warp = (size_t)stages * (slot + 16);
   int nc = kGemvSmemBudget > xb ? (int)((kGemvSmemBudget - xb) / per_warp) : 0;
   const int want = consumers_cfg() > kMaxConsumers ? kMaxConsumers : consumers_cfg();

@@ -7,6 +7,7 @@
 
 #include "layout.cuh"
 #include "prefetch.cuh"
+#include "tp.cuh"
 
 namespace mcpo {
 
@@ -14,6 +15,7 @@ enum GemvEpilogue : int {
   kEpiStore = 0,   // y[row] = W.x
   kEpiAdd = 1,     // y[row] = y[row] + W.x   (residual add, qwen3.uya:1964-1973)
   kEpiSwiglu = 2,  // y[row] = silu(Wg.x) * (Wu.x)   (kernels.uya:198, qwen3.uya:1970)
+  kEpiTpPush = 3,  // tensor parallelism: W.x of row r to tp.dst[d][r] on every rank d, then the arrival counts
 };
 
 struct GemvSeg {
@@ -40,6 +42,10 @@ enum GemvInput : int {
   kInQ8_1 = 0,     // xq: Q8_1 blocks in global memory
   kInF32 = 1,      // xf: f32 values, quantised in the prologue
   kInRmsNorm = 2,  // xf: f32 values; RMSNorm(xf) * norm_w (eps), then quantised
+  // tensor parallelism: x = xf + (sum of the ranks' partials of exchange
+  // tp, rank order) once they have all arrived; x also goes to tp.sum_out
+  // (each CTA its share); then as kInRmsNorm on x
+  kInRmsNormTp = 3,
 };
 
 // All segments of one launch share the input width `cols` (hence lpr/ks);
@@ -72,6 +78,8 @@ struct GemvArgs {
   // weight bytes of later kernels to prefetch into L2 (idle producer lanes
   // issue them at the start; n = 0: none)
   PfList pf;
+  // kEpiTpPush / kInRmsNormTp: the exchange produced or consumed
+  TpXchg tp;
 };
 
 constexpr int kGemvMaxVec = 4;  // input vectors per multi-vector launch

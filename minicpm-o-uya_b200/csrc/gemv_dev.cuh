@@ -10,6 +10,7 @@
 #include "common.cuh"
 #include "gemv.cuh"
 #include "tma.cuh"
+#include "tp_proto.h"
 
 namespace mcpo {
 
@@ -215,6 +216,47 @@ __host__ __device__ inline size_t gemv_x_bytes(int cols) {
   return (b + 127) / 128 * 128;
 }
 
+// The activation region of one launch: the x region, plus the summed input
+// vector (f32) of a tensor-parallel summing prologue.
+__host__ __device__ inline size_t gemv_x_region(int cols, int input) {
+  return gemv_x_bytes(cols) + (input == kInRmsNormTp ? ((size_t)cols * 4 + 127) / 128 * 128 : 0);
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ uint64_t gemv_globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// The tensor-parallel summing prologue: thread 0 waits (bounded, 1 s) for
+// every rank's partial of the exchange, then the NC*32 consumer threads
+// write sx[i] = xf[i] + rank-order sum of the partials and this CTA's share
+// of sx to tp.sum_out.  Ends with the consumers synchronised.
+__device__ __forceinline__ void gemv_tp_sum(const GemvArgs& a, float* sx, int tid, int nthr) {
+  const TpXchg& t = a.tp;
+  if (tid == 0) {
+    const uint32_t target = tp_target(tp_exchange_index(*t.step, (uint32_t)t.nx, (uint32_t)t.x), (uint32_t)t.rows);
+    const bool ok = tp_wait_all(
+        t.arrive, t.world, target, [](const uint32_t* p) { return ld_acquire_sys_u32(p); },
+        [] { return gemv_globaltimer(); }, 1000000000ull);
+    if (!ok && a.err) atomicExch(a.err, 1);
+  }
+  asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
+  const int cols = a.cols;
+  for (int i = tid; i < cols; i += nthr)
+    sx[i] = tp_rank_sum(a.xf[i], t.world, [&](int r) { return __ldcv(t.src[r] + i); });
+  asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
+  const int G = gridDim.x, b = blockIdx.x;
+  const int lo = (int)((long long)cols * b / G), hi = (int)((long long)cols * (b + 1) / G);
+  for (int i = lo + tid; i < hi; i += nthr) t.sum_out[i] = sx[i];
+}
+
 // Writes one Q8_1 block (32 values, one per lane) straight into the
 // transposed shared-memory layout: the quants and d of q8_1_quant_lane (the
 // bits k_quantize_q8_1 stores), and the exact integer sums of each half.
@@ -376,7 +418,7 @@ __device__ __forceinline__ void x_block_quarter(const float (&v)[8], int b, int 
 __device__ __forceinline__ void gemv_norm_weights(const GemvArgs& a, int warp, int lane, float (&wv)[8]) {
   const int nblk = a.cols / 32;
   const int b = warp * 8 + (lane >> 2);
-  const bool on = a.input == kInRmsNorm && b < nblk;
+  const bool on = (a.input == kInRmsNorm || a.input == kInRmsNormTp) && b < nblk;
 #pragma unroll
   for (int i = 0; i < 8; ++i) wv[i] = on ? load_weight(a.norm_w, a.norm_dtype, b * 32 + (lane & 3) * 8 + i) : 0.0f;
 }
@@ -420,8 +462,14 @@ __device__ __forceinline__ void gemv_build_x(const GemvArgs& a, uint8_t* xbase, 
     // (up to three; with RMSNorm one) are all requested at once, before the
     // RMSNorm reduction; larger inputs request each tile while the one
     // before it is quantised.  Arithmetic per element as q8_1_quant_lane.
+    // The tensor-parallel input is first summed into shared memory.
     const float* xf = a.xf;
-    const bool norm = a.input == kInRmsNorm;
+    if (a.input == kInRmsNormTp) {
+      float* sx = reinterpret_cast<float*>(xbase + gemv_x_bytes(cols));
+      gemv_tp_sum(a, sx, tid, NC * 32);
+      xf = sx;
+    }
+    const bool norm = a.input == kInRmsNorm || a.input == kInRmsNormTp;
     const void* nw = a.norm_w;
     const int ndt = a.norm_dtype;
     const float eps = a.eps;
@@ -574,8 +622,12 @@ __device__ __forceinline__ bool gemv_items(const GemvArgs& a, const XShared& x, 
     const float u = swiglu ? reduce_row(acc[1], s.lpr) : 0.0f;
     if (lane_in_row == 0 && row < s.rows) {
       const float out = swiglu ? silu_mul_det(g, u) : add ? __fadd_rn(yold, g) : g;
-      s.y[row] = out;
-      if (stage) stage[row - stage_r0] = out;
+      if (s.epi == kEpiTpPush) {
+        for (int d = 0; d < a.tp.world; ++d) a.tp.dst[d][row] = out;  // this rank's slot on every rank
+      } else {
+        s.y[row] = out;
+        if (stage) stage[row - stage_r0] = out;
+      }
     }
   }
   return true;

@@ -132,7 +132,9 @@ struct Model {
   uint32_t vocab_global = 0, vocab_base = 0;
   TpPeers peers{};
   std::vector<void*> peer_maps;  // IPC mappings to close
-  unsigned* tp_epoch = nullptr;
+  unsigned* tp_epoch = nullptr;  // sampler-merge epochs
+  unsigned* tp_step = nullptr;   // step counter of the fused hidden exchanges (tp_proto.h)
+  float* hidden2 = nullptr;      // the second residual buffer of the tensor-parallel step
   std::vector<std::unique_ptr<Upload>> shards;
 };
 
@@ -488,7 +490,7 @@ void free_model(Model* m) {
   void* bufs[] = {m->hidden, m->normed, m->q,     m->k,       m->v,         m->attn,       m->gate,     m->up,
                   m->fused,  m->tmp,    m->logits, m->xq,     m->aq,        m->fq,         m->kc,       m->vc,
                   m->rope_cos, m->rope_sin, m->partial, m->counters, m->am_scratch, m->am_counter, m->st, m->seen,
-                  m->history, m->stages, m->step_scratch, m->step_trace, m->tp_epoch, m->embed_in,
+                  m->history, m->stages, m->step_scratch, m->step_trace, m->tp_epoch, m->tp_step, m->hidden2, m->embed_in,
                   m->smp_seen, m->smp_io, m->smp_bits, m->smp_st, m->pf_hidden, m->pf_q, m->pf_k, m->pf_v,
                   m->pf_attn, m->pf_fused, m->pf_partial, m->pf_tok, m->pf_pos, m->pf_counters,
                   m->pf_err};
@@ -653,6 +655,18 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
                    m.embed_in, &m.st->embed_input));
   REC(launch_mark_seen(m.seen, m.st, (int)(m.tp_world > 1 ? m.vocab_global : cf.vocab), s, true));
   const bool tp = m.tp_world > 1;
+  // tensor parallelism: the residual stream alternates between m.hidden (A)
+  // and m.hidden2 (B); exchange 2l follows layer l's o GEMV, 2l+1 its down
+  // GEMV, and each is summed in the prologue of the GEMV that consumes it
+  // (layer l's gate/up: A + o partials -> B; layer l+1's q/k/v and the
+  // lm_head: B + down partials -> A)
+  const int nx = 2 * (int)cf.layers;
+  auto xchg = [&](int x, float* sum_out) {
+    TpXchg t{};
+    tp_xchg(m.peers, nx, x, h, m.tp_step, sum_out, &t);
+    return t;
+  };
+  if (tp) REC(launch_tp_step(m.tp_step, s));
   if (m.step_ok) {
     // the whole layer chain (and the lm_head) as one persistent kernel
     cudaError_t e = cudaMemsetAsync(m.step_scratch, 0, m.step_scratch_bytes, s);
@@ -683,7 +697,11 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
       GemvArgs a{};
       a.nseg = 3;
       a.cols = h;
-      norm_input(&a, m.hidden, L.attn_norm, cf.rms_eps);
+      norm_input(&a, tp && li > 0 ? m.hidden2 : m.hidden, L.attn_norm, cf.rms_eps);
+      if (tp && li > 0) {
+        a.input = kInRmsNormTp;
+        a.tp = xchg(2 * (int)li - 1, m.hidden);
+      }
       a.err = &m.st->err;
       float* ys[3] = {m.q, m.k, m.v};
       for (int i = 0; i < 3; ++i) gemv_seg_from_geom(qkv[i]->geom, qkv[i]->dev, nullptr, ys[i], kEpiStore, &a.seg[i]);
@@ -728,9 +746,17 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
     if (pf.window) a.pf = pf.next(qkv_end);
     REC(launch_attention(a, s, true));
     // (head_dim % 32 != 0: the o GEMV quantises the f32 attention output itself)
-    if (tp) {  // row-parallel: this rank's partial, then hidden += sum of all ranks' partials
-      REC(model_mv(c, L.o, m.attn, a.out_q8, m.peers.part[m.tp_rank][0], kEpiStore, m.tmp, m.grid_q, &m.st->err));
-      REC(launch_tp_reduce_add(m.peers, 0, m.hidden, h, m.tp_epoch, &m.st->err, s));
+    if (tp) {  // row-parallel: this rank's partial pushed to every rank (exchange 2l)
+      GemvArgs o{};
+      o.nseg = 1;
+      o.cols = (int)L.o->cols;
+      o.input = a.out_q8 ? kInQ8_1 : kInF32;
+      o.xq = a.out_q8;
+      o.xf = m.attn;
+      o.err = &m.st->err;
+      gemv_seg_from_geom(L.o->geom, L.o->dev, nullptr, nullptr, kEpiTpPush, &o.seg[0]);
+      o.tp = xchg(2 * (int)li, nullptr);
+      REC(launch_gemv(o, m.grid_q, s, true));
     } else {
       const PfList opf = pf.next(pf.window ? pf.end_of(L.o) : 0);
       REC(model_mv(c, L.o, m.attn, a.out_q8, m.hidden, kEpiAdd, m.tmp, m.grid_q, &m.st->err, &opf));
@@ -744,6 +770,10 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
       g.nseg = 1;
       g.cols = h;
       norm_input(&g, m.hidden, L.ffn_norm, cf.rms_eps);
+      if (tp) {
+        g.input = kInRmsNormTp;
+        g.tp = xchg(2 * (int)li, m.hidden2);
+      }
       g.err = &m.st->err;
       gemv_seg_from_geom(L.gate->geom, L.gate->dev, L.up->dev, m.fused, kEpiSwiglu, &g.seg[0]);
       if (!tp && L.down->tiled && ffn_q8_cfg()) g.q8_out = m.fq;
@@ -756,20 +786,33 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
       REC(model_mv(c, L.up, m.normed, m.xq, m.up, kEpiStore, m.tmp, m.grid_h, &m.st->err));
       REC(launch_silu_mul(m.fused, m.gate, m.up, f, s));
     }
-    if (tp) {
-      REC(model_mv(c, L.down, m.fused, nullptr, m.peers.part[m.tp_rank][1], kEpiStore, m.tmp, m.grid_f, &m.st->err));
-      REC(launch_tp_reduce_add(m.peers, 1, m.hidden, h, m.tp_epoch, &m.st->err, s));
+    if (tp) {  // row-parallel: this rank's partial pushed to every rank (exchange 2l+1)
+      GemvArgs d{};
+      d.nseg = 1;
+      d.cols = (int)L.down->cols;
+      d.input = kInF32;
+      d.xf = m.fused;
+      d.err = &m.st->err;
+      gemv_seg_from_geom(L.down->geom, L.down->dev, nullptr, nullptr, kEpiTpPush, &d.seg[0]);
+      d.tp = xchg(2 * (int)li + 1, nullptr);
+      REC(launch_gemv(d, m.grid_f, s, true));
     } else {
       const PfList dpf = pf.next(pf.window ? pf.end_of(L.down) : 0);
       REC(model_mv(c, L.down, m.fused, down_q8, m.hidden, kEpiAdd, m.tmp, m.grid_f, &m.st->err, &dpf));
     }
   }
+  if (tp && !logits)  // the last exchange still completes the residual stream (hidden_out)
+    REC(launch_tp_finalize(xchg(nx - 1, m.hidden), m.hidden2, &m.st->err, s));
   if (logits) {
     if (m.out->tiled) {
       GemvArgs o{};
       o.nseg = 1;
       o.cols = h;
-      norm_input(&o, m.hidden, m.out_norm, cf.rms_eps);
+      norm_input(&o, tp ? m.hidden2 : m.hidden, m.out_norm, cf.rms_eps);
+      if (tp) {
+        o.input = kInRmsNormTp;
+        o.tp = xchg(nx - 1, m.hidden);
+      }
       o.err = &m.st->err;
       gemv_seg_from_geom(m.out->geom, m.out->dev, nullptr, m.logits, kEpiStore, &o.seg[0]);
       REC(launch_gemv(o, m.grid_h, s, true));
@@ -1229,6 +1272,7 @@ Upload* row_view(Model& m, const Upload* u, size_t r0, size_t r1) {
   std::unique_ptr<Upload> v(new Upload(*u));
   v->host_ptr = nullptr;
   v->rows = r1 - r0;
+  v->bytes = (r1 - r0) * gguf_row_bytes(u->dtype, u->cols);
   v->view = true;
   if (!make_geom(u->dtype, (int)v->rows, (int)u->cols, &v->geom)) return nullptr;
   v->dev = u->dev + (r0 / (size_t)u->geom.rpw) * u->geom.wr_bytes;
@@ -1303,6 +1347,10 @@ int shard_model(Ctx* c, Model& m, int rank, int world, const uint8_t* peer_handl
     Upload* d = o ? col_slice(c, m, L.down, sb0 * 256, sb1 * 256, err, cap) : nullptr;
     if (!q || !k || !v || !g || !u || !o || !d)
       return fail(c, err, cap, "error: qwen3 bind_tp: cannot shard layer tensors (quantised weights required)");
+    Upload* qkv[3] = {q, k, v};
+    if (!groupable(qkv, 3) || g->dtype != u->dtype)
+      return fail(c, err, cap,
+                  "error: qwen3 bind_tp: q/k/v must not mix Q8_0 with K-quants and gate/up must share a dtype");
     L.q = q, L.k = k, L.v = v, L.gate = g, L.up = u, L.o = o, L.down = d;
   }
   m.out = row_view(m, m.out, v0, v1);
@@ -1323,13 +1371,16 @@ int shard_model(Ctx* c, Model& m, int rank, int world, const uint8_t* peer_handl
       m.peer_maps.push_back(ptr);
       base = static_cast<uint8_t*>(ptr);
     }
-    p.part[r][0] = reinterpret_cast<float*>(base + TpLayout::part_offset(0, cf.hidden));
-    p.part[r][1] = reinterpret_cast<float*>(base + TpLayout::part_offset(1, cf.hidden));
+    p.base[r] = base;
     p.top[r] = reinterpret_cast<float*>(base + TpLayout::top_offset(cf.hidden));
     p.flag[r] = reinterpret_cast<unsigned*>(base + TpLayout::flag_offset(cf.hidden));
   }
   if (!cuda_ok(c, cudaMalloc((void**)&m.tp_epoch, sizeof(unsigned)), "tp_epoch_malloc", err, cap) ||
-      !cuda_ok(c, cudaMemsetAsync(m.tp_epoch, 0, sizeof(unsigned), c->stream), "tp_epoch_memset", err, cap))
+      !cuda_ok(c, cudaMemsetAsync(m.tp_epoch, 0, sizeof(unsigned), c->stream), "tp_epoch_memset", err, cap) ||
+      !cuda_ok(c, cudaMalloc((void**)&m.tp_step, sizeof(unsigned)), "tp_step_malloc", err, cap) ||
+      !cuda_ok(c, cudaMemsetAsync(m.tp_step, 0, sizeof(unsigned), c->stream), "tp_step_memset", err, cap) ||
+      !cuda_ok(c, cudaMalloc((void**)&m.hidden2, (size_t)cf.hidden * 4), "tp_hidden2_malloc", err, cap) ||
+      !cuda_ok(c, cudaMemsetAsync(m.hidden2, 0, (size_t)cf.hidden * 4, c->stream), "tp_hidden2_memset", err, cap))
     return 0;
   m.tp_rank = rank;
   m.tp_world = world;

@@ -1,14 +1,12 @@
-// tp.cu -- tensor-parallel exchange kernels (see tp.cuh).
+// tp.cu -- tensor-parallel exchange kernels and descriptors (see tp.cuh).
 //
-// Protocol per exchange: every rank runs the same sequence of exchanges, so
-// a per-rank epoch counter (advanced by each exchange kernel) names the
-// exchange.  A kernel first publishes its epoch with a system-scope release
-// store to its own flag (the partials it publishes were written by earlier
-// kernels of the same stream), then acquires every peer's flag, bounded by
-// 1 s of globaltimer; peer data is read with uncached loads.  Two partial
-// buffers alternate per exchange: a rank writes buffer b for exchange e+2
-// only after exchange e+1, which every peer entered after finishing its reads
-// of exchange e.
+// The hidden-vector exchanges after the row-parallel o and down GEMVs are
+// fused into those GEMVs (push epilogue) and the GEMV that consumes them
+// (summing prologue); the protocol is in tp_proto.h.  What remains here:
+// the step counter and the sampler merge.  The merge uses a flag per rank:
+// a kernel publishes its epoch with a system-scope release store to its own
+// flag, then acquires every peer's flag, bounded by 1 s of globaltimer; peer
+// data is read with uncached loads.
 #include "tp.cuh"
 
 #include <math.h>
@@ -52,27 +50,27 @@ __device__ bool publish_and_wait(const TpPeers& p, unsigned e) {
   return true;
 }
 
-__global__ void __launch_bounds__(1024) k_tp_reduce_add(const TpPeers p, int buf, float* hidden, int n,
-                                                        unsigned* epoch, int* err) {
-  __shared__ unsigned e_s;
+// The consumer half of an exchange on its own (the step without an lm_head):
+// thread 0 waits for every rank's partial, then out = base + rank-order sum.
+__global__ void __launch_bounds__(1024) k_tp_finalize(const TpXchg t, const float* base, int* err) {
   __shared__ int ok_s;
   pdl_wait();
   if (threadIdx.x == 0) {
-    const unsigned e = *epoch + 1u;
-    ok_s = publish_and_wait(p, e) ? 1 : 0;
-    e_s = e;
-    if (!ok_s) atomicExch(err, 1);
+    const uint32_t target = tp_target(tp_exchange_index(*t.step, (uint32_t)t.nx, (uint32_t)t.x), (uint32_t)t.rows);
+    ok_s = tp_wait_all(
+        t.arrive, t.world, target, [](const uint32_t* p) { return ld_acquire_sys(p); }, [] { return gtimer(); },
+        1000000000ull);
+    if (!ok_s && err) atomicExch(err, 1);
   }
   __syncthreads();
-  if (ok_s) {
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-      float t = __ldcv(p.part[0][buf] + i);
-      for (int r = 1; r < p.world; ++r) t = __fadd_rn(t, __ldcv(p.part[r][buf] + i));
-      hidden[i] = __fadd_rn(hidden[i], t);
-    }
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) *epoch = e_s;  // advanced even on a timeout: the error word ends the run
+  for (int i = threadIdx.x; i < t.rows; i += blockDim.x)
+    t.sum_out[i] = tp_rank_sum(base[i], t.world, [&](int r) { return __ldcv(t.src[r] + i); });
+  pdl_launch_dependents();
+}
+
+__global__ void k_tp_step(unsigned* step) {
+  pdl_wait();
+  if (threadIdx.x == 0) *step = *step + 1u;
   pdl_launch_dependents();
 }
 
@@ -120,10 +118,33 @@ __global__ void k_tp_sample_merge(const TpPeers p, StepState* st, int* history, 
 
 }  // namespace
 
-cudaError_t launch_tp_reduce_add(const TpPeers& p, int buf, float* hidden, int n, unsigned* epoch, int* err,
-                                 cudaStream_t st) {
-  if (p.world < 1 || p.world > kTpMaxWorld || buf < 0 || buf > 1) return cudaErrorInvalidValue;
-  return launch_k(k_tp_reduce_add, dim3(1), dim3(1024), 0, st, true, p, buf, hidden, n, epoch, err);
+void tp_xchg(const TpPeers& p, int nx, int x, int rows, const unsigned* step, float* sum_out, TpXchg* out) {
+  TpXchg t{};
+  const int par = x & 1;
+  for (int d = 0; d < p.world; ++d) {
+    t.dst[d] = reinterpret_cast<float*>(p.base[d] + TpLayout::part_offset(par, p.rank, (size_t)rows));
+    t.dst_arrive[d] = reinterpret_cast<unsigned*>(p.base[d] + TpLayout::arrive_offset((size_t)rows)) + p.rank;
+  }
+  uint8_t* own = p.base[p.rank];
+  for (int r = 0; r < p.world; ++r)
+    t.src[r] = reinterpret_cast<const float*>(own + TpLayout::part_offset(par, r, (size_t)rows));
+  t.arrive = reinterpret_cast<const unsigned*>(own + TpLayout::arrive_offset((size_t)rows));
+  t.sum_out = sum_out;
+  t.step = step;
+  t.world = p.world;
+  t.nx = nx;
+  t.x = x;
+  t.rows = rows;
+  *out = t;
+}
+
+cudaError_t launch_tp_finalize(const TpXchg& t, const float* base, int* err, cudaStream_t st) {
+  if (t.world < 1 || t.world > kTpMaxWorld || !t.sum_out || !t.step || !t.arrive) return cudaErrorInvalidValue;
+  return launch_k(k_tp_finalize, dim3(1), dim3(1024), 0, st, true, t, base, err);
+}
+
+cudaError_t launch_tp_step(unsigned* step, cudaStream_t st) {
+  return launch_k(k_tp_step, dim3(1), dim3(32), 0, st, true, step);
 }
 
 cudaError_t launch_tp_sample_merge(const TpPeers& p, StepState* st, int* history, int history_cap, unsigned* epoch,

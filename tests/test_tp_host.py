@@ -48,3 +48,68 @@ def test_tensor_parallel_all_gather_two_ranks():
     for rank in range(2):
         firsts, lens, barrier = out[rank]
         assert firsts == [0, 1] and lens == [64, 64] and barrier == [b"", b""]
+
+
+# --------------------------------------------------------------------------
+# The fused exchange protocol (minicpm-o-uya_b200/csrc/tp_proto.h) on host
+# threads: every rank's partial summed in rank order, no slot overwritten
+# while a slower rank still reads it, and a rank that leaves between steps
+# makes the others time out with an error instead of hanging.
+# --------------------------------------------------------------------------
+import ctypes
+import subprocess
+from pathlib import Path
+
+import pytest
+
+HERE = Path(__file__).resolve().parent
+
+
+@pytest.fixture(scope="module")
+def harness(tmp_path_factory):
+    out = tmp_path_factory.mktemp("tp") / "libtp_harness.so"
+    cmd = ["g++", "-std=c++17", "-O2", "-fPIC", "-shared", "-pthread", "-I",
+           str(HERE.parent / "minicpm-o-uya_b200" / "csrc"), "-o", str(out), str(HERE / "tp_protocol_harness.cpp")]
+    subprocess.run(cmd, check=True, capture_output=True)
+    lib = ctypes.CDLL(str(out))
+    lib.tp_harness_run.restype = ctypes.c_int
+    lib.tp_harness_run.argtypes = ([ctypes.c_int, ctypes.c_uint] + [ctypes.c_int] * 5 +
+                                   [ctypes.c_ulonglong, ctypes.c_int, ctypes.c_uint, ctypes.POINTER(ctypes.c_int),
+                                    ctypes.POINTER(ctypes.c_int)])
+    return lib
+
+
+def _run(lib, world, steps, nx=8, rows=96, kill_rank=-1, kill_step=0, limit_ms=300, skew_us=50, seed=1, first_step=1):
+    status = (ctypes.c_int * world)()
+    bad = (ctypes.c_int * world)()
+    assert lib.tp_harness_run(world, first_step, steps, nx, rows, kill_rank, kill_step, limit_ms * 1_000_000, skew_us,
+                              seed, status, bad) == 1
+    return list(status), list(bad)
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_exchange_protocol_sums_in_rank_order(harness, world):
+    status, bad = _run(harness, world, steps=40, skew_us=30, seed=world)
+    assert status == [0] * world and bad == [0] * world
+
+
+def test_exchange_protocol_counters_wrap(harness):
+    """Monotonic 32-bit counters compare with wraparound arithmetic: steps
+    whose arrival counts cross 2^32 run without a reset."""
+    nx, rows = 8, 96
+    first = (1 << 32) // (nx * rows) - 5  # the counters wrap a few steps in
+    status, bad = _run(harness, 4, steps=12, nx=nx, rows=rows, first_step=first)
+    assert status == [0] * 4 and bad == [0] * 4
+
+
+@pytest.mark.parametrize("world,kill_rank,kill_step", [(2, 1, 3), (4, 2, 5), (8, 0, 2)])
+def test_killed_rank_makes_the_others_time_out(harness, world, kill_rank, kill_step):
+    import time
+
+    t0 = time.perf_counter()
+    status, bad = _run(harness, world, steps=10, kill_rank=kill_rank, kill_step=kill_step, limit_ms=200)
+    elapsed = time.perf_counter() - t0
+    assert status[kill_rank] == 2
+    assert all(s == 1 for r, s in enumerate(status) if r != kill_rank), status  # timed out with an error
+    assert bad == [0] * world  # every exchange before the kill summed correctly
+    assert elapsed < 5.0

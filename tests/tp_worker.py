@@ -29,10 +29,14 @@ def main() -> int:
     from minicpmo_b200.qwen3 import Qwen3Runtime, TensorParallel
 
     steps = int(os.environ.get("TP_STEPS", "48"))
-    kv = max(2, world)  # every rank keeps >= 1 kv head and 512 q columns
-    shape = gguf.Qwen3Shape(layers=2, hidden=512, heads=4 * kv, kv_heads=kv, head_dim=128, ffn=2048, vocab=2048,
-                            context=96)
-    tensors = gguf.synth_model(shape, gguf.Q4_K_M, seed_base=5)
+    if os.environ.get("TP_SHAPE", "small") == "qwen3-8b-4l":
+        shape = gguf.Qwen3Shape(**{**gguf.SHAPES["qwen3-8b"].__dict__, "layers": 4, "context": 64})
+        tensors = gguf.synth_model(shape, gguf.Q4_K_M, device=f"cuda:{local}", seed_base=5)
+    else:
+        kv = max(2, world)  # every rank keeps >= 1 kv head and 512 q columns
+        shape = gguf.Qwen3Shape(layers=2, hidden=512, heads=4 * kv, kv_heads=kv, head_dim=128, ffn=2048, vocab=2048,
+                                context=96)
+        tensors = gguf.synth_model(shape, gguf.Q4_K_M, seed_base=5)
     rt = Qwen3Runtime.open(tensors, shape=shape, device_index=local, context=shape.context,
                            tp=TensorParallel(rank, world))
     ids = gguf.prompt_ids(steps, shape.vocab, seed=3)
@@ -44,8 +48,12 @@ def main() -> int:
         gaps.append(float(g))
         slices.append(lg.copy())
     dec = rt.gpu.qwen3_decode(int(ids[0]), steps, 16).tolist()
+    # prompt tokens without logits (the graph that ends with the finalising exchange), then one more step
+    for pos in range(steps + 16, steps + 20):
+        rt.forward(int(ids[pos % steps]), pos, logits=False)
+    t_last, _ = rt.forward(int(ids[0]), steps + 20, logits=True, want_logits=lg)
     everyone = [None] * world
-    dist.all_gather_object(everyone, {"toks": toks, "dec": dec})
+    dist.all_gather_object(everyone, {"toks": toks, "dec": dec, "last": int(t_last)})
     if rank == 0:
         ref = Qwen3Runtime.open(tensors, shape=shape, device_index=local, context=shape.context)
         rl = np.zeros(shape.vocab, np.float32)
@@ -59,7 +67,12 @@ def main() -> int:
             if t != toks[pos] and g > 1e-3:
                 mism += 1
         ref_dec = ref.gpu.qwen3_decode(int(ids[0]), steps, 16).tolist()
-        agree = all(e["toks"] == toks and e["dec"] == dec for e in everyone)
+        for pos in range(steps + 16, steps + 20):
+            ref.forward(int(ids[pos % steps]), pos, logits=False)
+        ref_last, ref_gap = ref.forward(int(ids[0]), steps + 20, logits=True, want_logits=rl)
+        if ref_last != t_last and ref_gap > 1e-3:
+            mism += 1
+        agree = all(e["toks"] == toks and e["dec"] == dec and e["last"] == int(t_last) for e in everyone)
         print(json.dumps({"world": world, "ranks_agree": agree, "token_mismatch_large_gap": mism,
                           "worst_logit_err": worst, "decode_equal": dec == ref_dec, "min_gap": min(gaps)}))
         ref.close()
