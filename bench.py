@@ -602,7 +602,8 @@ def main() -> int:
     persistent = g.qwen3_step_kernels(True) <= 4
     shapes = {}
     lm_name = "output.weight" if "output.weight" in T else "token_embd.weight"  # tied lm_head (0.6B)
-    for name in ("blk.0.ffn_gate.weight", "blk.0.ffn_down.weight", "blk.0.attn_q.weight", lm_name):
+    for name in (("blk.0.ffn_gate.weight", "blk.0.ffn_down.weight", "blk.0.attn_q.weight", lm_name)
+                 if tp is None else ()):  # (under TP only the shards are resident)
         t = T[name]
         us = g.time_matvec(t, iters=20)
         alg = t.nbytes + t.cols // 32 * 36 + t.rows * 4

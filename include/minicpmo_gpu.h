@@ -180,9 +180,13 @@ MINICPMO_API int minicpmo_gpu_context_qwen3_bind(void *handle, const minicpmo_qw
  * 3. every rank uploads the full tensors as for qwen3_bind, then calls
  *    qwen3_bind_tp(cfg, rank, world, handles): the rank keeps its shards --
  *    q/k/v by heads, gate/up/down by 256-value FFN blocks, o by its heads'
- *    input columns, the lm_head by vocab rows -- and its decode graph
- *    all-reduces the o and down partials (hidden += sum in rank order, peer
- *    loads over NVLink, bounded waits) and merges the per-rank samplers;
+ *    input columns, the lm_head by vocab rows -- in buffers of their own and
+ *    releases the full copies of those tensors (they leave the upload
+ *    registry; re-upload them to bind again).  Its decode graph sums the o
+ *    and down partials of all ranks inside the GEMVs around them: the o and
+ *    down GEMVs store their partial rows into every rank's exchange buffer
+ *    over NVLink, and the next GEMV's prologue waits (bounded) for all of
+ *    them and adds them in rank order.  The per-rank samplers are merged;
  * 4. the host barriers the ranks, then drives qwen3_forward / qwen3_decode on
  *    every rank with the same tokens; every rank returns the same token.
  * heads, kv_heads must divide by world; ffn by 256.  With tensor parallelism

@@ -136,6 +136,7 @@ struct Model {
   unsigned* tp_step = nullptr;   // step counter of the fused hidden exchanges (tp_proto.h)
   float* hidden2 = nullptr;      // the second residual buffer of the tensor-parallel step
   std::vector<std::unique_ptr<Upload>> shards;
+  std::vector<LayerW> layer_full;  // the full uploads the shards came from (released after sharding)
 };
 
 struct Ctx {
@@ -1314,6 +1315,44 @@ Upload* col_slice(Ctx* c, Model& m, const Upload* u, size_t c0, size_t c1, char*
   return w;
 }
 
+// Each rank keeps only its shards resident: row views move into buffers of
+// their own, then the full uploads they came from (and those the column
+// slices were rebuilt from) are freed and leave the registry, so later calls
+// naming those tensors get "not uploaded".  The token embedding stays (it is
+// replicated, and a tied lm_head is sharded from it).
+int keep_shards_only(Ctx* c, Model& m, Upload* out_full, char* err, size_t cap) {
+  std::vector<Upload*> parents;
+  for (auto& sh : m.shards) {
+    Upload* v = sh.get();
+    if (!v->view) continue;
+    uint8_t* d = nullptr;
+    if (!cuda_ok(c, cudaMalloc((void**)&d, v->dev_bytes), "tp_shard_malloc", err, cap) ||
+        !cuda_ok(c, cudaMemcpyAsync(d, v->dev, v->dev_bytes, cudaMemcpyDeviceToDevice, c->stream), "tp_shard_copy", err,
+                 cap)) {
+      if (d) cudaFree(d);
+      return 0;
+    }
+    v->dev = d;
+    v->view = false;
+  }
+  if (!cuda_ok(c, cudaStreamSynchronize(c->stream), "tp_shard_sync", err, cap)) return 0;
+  for (const auto& up : c->uploads) {
+    Upload* u = up.get();
+    bool sharded = u == out_full && u != m.tok;
+    for (const LayerW& L : m.layer_full)
+      sharded = sharded || u == L.q || u == L.k || u == L.v || u == L.o || u == L.gate || u == L.up || u == L.down;
+    if (!sharded || !u->dev) continue;
+    cudaFree(u->dev);
+    u->dev = nullptr;
+    u->dev_bytes = 0;
+    if (u->raw) cudaFree(u->raw);
+    u->raw = nullptr;
+    c->by_ptr.erase(u->host_ptr);
+    if (!u->name.empty()) c->by_name.erase(u->name);
+  }
+  return 1;
+}
+
 // Replaces the model's global tensors by this rank's shards and its config
 // by the local dims.  Column-parallel (output rows): q/k/v by heads, gate/up
 // by 256-value FFN blocks, the lm_head by vocab rows.  Row-parallel (input
@@ -1337,6 +1376,7 @@ int shard_model(Ctx* c, Model& m, int rank, int world, const uint8_t* peer_handl
   if (!m.out->tiled) return fail(c, err, cap, "error: qwen3 bind_tp: the lm_head must be quantised");
   const size_t V = cf.vocab, rpo = (size_t)m.out->geom.rpw;
   const size_t v0 = V * rank / world / rpo * rpo, v1 = rank + 1 == world ? V : V * (rank + 1) / world / rpo * rpo;
+  m.layer_full = m.layer;
   for (LayerW& L : m.layer) {
     Upload* q = row_view(m, L.q, rank * heads_r * hd, (rank + 1) * heads_r * hd);
     Upload* k = row_view(m, L.k, rank * kv_r * hd, (rank + 1) * kv_r * hd);
@@ -1353,8 +1393,10 @@ int shard_model(Ctx* c, Model& m, int rank, int world, const uint8_t* peer_handl
                   "error: qwen3 bind_tp: q/k/v must not mix Q8_0 with K-quants and gate/up must share a dtype");
     L.q = q, L.k = k, L.v = v, L.gate = g, L.up = u, L.o = o, L.down = d;
   }
+  Upload* const out_full = m.out;
   m.out = row_view(m, m.out, v0, v1);
   if (!m.out) return fail(c, err, cap, "error: qwen3 bind_tp: cannot shard the lm_head");
+  if (!keep_shards_only(c, m, out_full, err, cap)) return 0;
   // exchange buffers: own and peers' (IPC)
   TpPeers& p = m.peers;
   p.rank = rank;
