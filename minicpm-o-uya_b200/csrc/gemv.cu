@@ -71,6 +71,7 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1) k_gemv(const Gemv
   uint64_t* empty = full + NC * S;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (a.pdl_early && threadIdx.x == 0) pdl_launch_dependents();
   const int T = a.total_wr, G = gridDim.x;
   int wr0, wr1, blk0 = 0, nblk = 0;
   if (a.q8_out) {
@@ -139,7 +140,7 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1) k_gemv(const Gemv
   pdl_wait();  // the activations (and y for the residual add) come from earlier kernels
   gemv_build_x(a, smem, NC, warp, lane, wpre);
   asm volatile("bar.sync 1, %0;" ::"r"(NC * 32) : "memory");
-  if (threadIdx.x == 0) pdl_launch_dependents();
+  if (!a.pdl_early && threadIdx.x == 0) pdl_launch_dependents();
   const XShared x = gemv_x_view(smem, cols);
   int n = 0;
   float* stage = a.q8_out ? reinterpret_cast<float*>(empty + NC * S) : nullptr;
@@ -331,6 +332,10 @@ int consumers_cfg() {
   static const int v = env_int("MCPO_GEMV_CONSUMERS", 16);
   return v;
 }
+int early_cfg() {
+  static const int v = env_int("MCPO_GEMV_EARLY", 0);
+  return v;
+}
 
 template <int kClass, bool kDots>
 cudaError_t set_smem_attr() {
@@ -399,6 +404,7 @@ cudaError_t launch_gemv(GemvArgs& a, int grid, cudaStream_t st, bool pdl) {
   const int wr = a.total_wr, slot = a.slot_bytes;
   const int stages = stages_cfg() < 1 ? 1 : stages_cfg();
   a.stages = stages;
+  a.pdl_early = pdl && early_cfg() ? 1 : 0;
   if (wr == 0) return cudaSuccess;
   if (a.nvec > kGemvMaxVec || (a.nvec > 1 && a.dots)) return cudaErrorInvalidValue;
   const size_t xb = a.nvec > 1 ? gemv_x_bytes(a.cols) * (size_t)a.nvec : gemv_x_region(a.cols, a.input);

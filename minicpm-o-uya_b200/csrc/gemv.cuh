@@ -80,6 +80,9 @@ struct GemvArgs {
   PfList pf;
   // kEpiTpPush / kInRmsNormTp: the exchange produced or consumed
   TpXchg tp;
+  // 1: allow the next kernel to launch as soon as this one starts (its CTAs
+  // then stream their weights while this kernel runs, where both fit an SM)
+  int pdl_early;
 };
 
 constexpr int kGemvMaxVec = 4;  // input vectors per multi-vector launch
