@@ -106,10 +106,7 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1) k_gemv(const Gemv
     // up the copies of another).  Needs nothing from the previous kernel, so
     // it does not wait for it.
     const int w = lane;
-    if (w >= NC) {  // idle lanes: the later kernels' weights into L2
-      if (a.pf.n > 0) l2_prefetch_share(a.pf, blockIdx.x, gridDim.x, w - NC, 32 - NC);
-      return;
-    }
+    if (w >= NC) return;
     const int steps = (nwr > w ? (nwr - w + NC - 1) / NC : 0) * spi;
     const uint64_t policy = l2_evict_first_policy();
     bool ok = true;
@@ -126,9 +123,11 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1) k_gemv(const Gemv
       mbar_arrive_expect_tx(&full[w * S + sidx], (uint32_t)s.step_bytes);
       bulk_load_hint(ring + (size_t)(w * S + sidx) * slot, src, (uint32_t)s.step_bytes, &full[w * S + sidx], policy);
     }
+    // The lane's own copies are all issued: now the later kernels' weights
+    // into L2 (after, not before: they must not delay this kernel's stream).
+    if (ok && a.pf.n > 0) l2_prefetch_share(a.pf, blockIdx.x, gridDim.x, w, NC);
     // Leave only once every copy issued into this CTA's shared memory has
     // landed (the consumers normally see to that; this covers their bail-out).
-    (void)ok;
     for (int n = steps - S > 0 ? steps - S : 0; n < steps; ++n)
       if (!mbar_wait(&full[w * S + n % S], (uint32_t)(n / S) & 1u, a.err)) return;
     return;
@@ -199,10 +198,7 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1) k_gemv_multi(cons
   __syncthreads();
   if (warp == NC) {  // producer, as k_gemv
     const int w = lane;
-    if (w >= NC) {
-      if (a.pf.n > 0) l2_prefetch_share(a.pf, blockIdx.x, gridDim.x, w - NC, 32 - NC);
-      return;
-    }
+    if (w >= NC) return;
     const int steps = (nwr > w ? (nwr - w + NC - 1) / NC : 0) * spi;
     const uint64_t policy = l2_evict_first_policy();
     for (int n = 0; n < steps; ++n) {

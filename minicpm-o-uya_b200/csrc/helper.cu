@@ -590,11 +590,19 @@ void norm_input(GemvArgs* a, const float* x, const Upload* norm, float eps) {
 // Bytes a GEMV streams from a weight upload.
 size_t stream_bytes(const Upload* u) { return u->tiled ? (size_t)u->geom.n_wr * u->geom.wr_bytes : u->dev_bytes; }
 
-// L2 prefetch window of the decode step (MCPO_PF_MB megabytes ahead of each
-// kernel's own weights; 0 turns prefetching off).
+// L2 prefetch windows of the decode step: MCPO_PF_MB megabytes ahead of a
+// GEMV's own weights (issued once its own copies are), MCPO_PF_ATTN_MB ahead
+// of the attention (which streams no weights); 0 turns prefetching off.
 size_t pf_window_cfg() {
   static const size_t v = [] {
     const char* e = getenv("MCPO_PF_MB");
+    return (size_t)((e && *e) ? atoi(e) : 0) << 20;
+  }();
+  return v;
+}
+size_t pf_attn_window_cfg() {
+  static const size_t v = [] {
+    const char* e = getenv("MCPO_PF_ATTN_MB");
     return (size_t)((e && *e) ? atoi(e) : 0) << 20;
   }();
   return v;
@@ -624,11 +632,12 @@ struct PfPlanner {
       if (stream[i].p == u->dev) return start[i] + stream[i].bytes;
     return 0;
   }
-  PfList next(unsigned long long end) {
+  PfList next(unsigned long long end) { return next(end, window); }
+  PfList next(unsigned long long end, unsigned long long win) {
     PfList l{};
-    if (window == 0) return l;
+    if (win == 0 || stream.empty()) return l;
     const unsigned long long lo = frontier > end ? frontier : end;
-    const unsigned long long hi = end + window < total ? end + window : total;
+    const unsigned long long hi = end + win < total ? end + win : total;
     for (size_t i = 0; i < stream.size() && lo < hi; ++i) {
       const unsigned long long a = start[i], b = start[i] + stream[i].bytes;
       const unsigned long long x = lo > a ? lo : a, y = hi < b ? hi : b;
@@ -682,7 +691,8 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
   }
   PfPlanner pf;
   pf.window = pf_window_cfg();
-  if (pf.window) {
+  const unsigned long long pf_attn = pf_attn_window_cfg();
+  if (pf.window || pf_attn) {
     for (uint32_t li = 0; li < cf.layers; ++li) {
       const LayerW& L = m.layer[li];
       for (const Upload* u : {L.q, L.k, L.v, L.o, L.gate, L.up, L.down}) pf.add(u);
@@ -693,7 +703,7 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
     const LayerW& L = m.layer[li];
     // attention block: RMSNorm -> Q8_1 inside the q/k/v GEMV's prologue
     Upload* qkv[3] = {L.q, L.k, L.v};
-    const unsigned long long qkv_end = pf.window ? pf.end_of(L.v) : 0;
+    const unsigned long long qkv_end = pf.stream.empty() ? 0 : pf.end_of(L.v);
     if (groupable(qkv, 3)) {
       GemvArgs a{};
       a.nseg = 3;
@@ -744,7 +754,7 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
     a.out = m.attn;
     a.out_q8 = (L.o->tiled && hd % 32 == 0) ? m.aq : nullptr;
     a.err = &m.st->err;
-    if (pf.window) a.pf = pf.next(qkv_end);
+    a.pf = pf.next(qkv_end, pf_attn);
     REC(launch_attention(a, s, true));
     // (head_dim % 32 != 0: the o GEMV quantises the f32 attention output itself)
     if (tp) {  // row-parallel: this rank's partial pushed to every rank (exchange 2l)
@@ -759,7 +769,7 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
       o.tp = xchg(2 * (int)li, nullptr);
       REC(launch_gemv(o, m.grid_q, s, true));
     } else {
-      const PfList opf = pf.next(pf.window ? pf.end_of(L.o) : 0);
+      const PfList opf = pf.next(pf.stream.empty() ? 0 : pf.end_of(L.o));
       REC(model_mv(c, L.o, m.attn, a.out_q8, m.hidden, kEpiAdd, m.tmp, m.grid_q, &m.st->err, &opf));
     }
     // feed-forward block: RMSNorm -> Q8_1 inside the gate/up GEMV, SwiGLU in
@@ -779,7 +789,7 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
       gemv_seg_from_geom(L.gate->geom, L.gate->dev, L.up->dev, m.fused, kEpiSwiglu, &g.seg[0]);
       if (!tp && L.down->tiled && ffn_q8_cfg()) g.q8_out = m.fq;
       down_q8 = g.q8_out;
-      g.pf = pf.next(pf.window ? pf.end_of(L.up) : 0);
+      g.pf = pf.next(pf.stream.empty() ? 0 : pf.end_of(L.up));
       REC(launch_gemv(g, m.grid_h, s, true));
     } else {
       REC(launch_rmsnorm_q8_1(m.hidden, L.ffn_norm->dev, L.ffn_norm->dtype, h, cf.rms_eps, m.normed, m.xq, s, true));
@@ -798,7 +808,7 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
       d.tp = xchg(2 * (int)li + 1, nullptr);
       REC(launch_gemv(d, m.grid_f, s, true));
     } else {
-      const PfList dpf = pf.next(pf.window ? pf.end_of(L.down) : 0);
+      const PfList dpf = pf.next(pf.stream.empty() ? 0 : pf.end_of(L.down));
       REC(model_mv(c, L.down, m.fused, down_q8, m.hidden, kEpiAdd, m.tmp, m.grid_f, &m.st->err, &dpf));
     }
   }
