@@ -363,6 +363,16 @@ MINICPMO_API int minicpmo_gpu_context_qwen3_step_kernels(void *handle, int with_
  * is off. */
 MINICPMO_API int minicpmo_gpu_context_qwen3_step_trace(void *handle, uint64_t *out, size_t cap, uint32_t *n_stages,
                                           uint32_t *n_ctas);
+/* With MCPO_GRAPH_TRACE=1 in the environment at bind time, the
+ * per-operation decode step records per launch and CTA the globaltimer (ns)
+ * at the CTA's start, past its wait for the previous kernel, when its
+ * activations are ready (attention: when its round of blocks begins) and
+ * when it is done; launches in order q/k/v, attention, o, gate/up, down per
+ * layer, then the lm_head.  This copies the last step's record,
+ * [launch][cta][4] (zeros for CTAs a launch does not have), into out (cap
+ * entries).  0 when tracing is off. */
+MINICPMO_API int minicpmo_gpu_context_qwen3_graph_trace(void *handle, uint64_t *out, size_t cap, uint32_t *n_launches,
+                                           uint32_t *n_ctas);
 /* Bytes of device memory held by the uploaded copy of a tensor. */
 MINICPMO_API size_t minicpmo_gpu_context_tensor_device_bytes(void *handle, const void *host_ptr);
 

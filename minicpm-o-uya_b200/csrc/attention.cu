@@ -579,6 +579,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2)
 
   const int kvh = blockIdx.x, split = blockIdx.y, z = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  unsigned long long* tr =
+      a.trace ? a.trace + ((size_t)(blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x) * 4 : nullptr;
+  if (threadIdx.x == 0) trace_stamp(tr, 0);
   const int hb = (kvh * a.n_head + a.n_kv - 1) / a.n_kv;
   const int he = ((kvh + 1) * a.n_head + a.n_kv - 1) / a.n_kv;
   const int G = he - hb;
@@ -667,6 +670,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2)
                       gridDim.x * gridDim.y * gridDim.z, lane, 32);
   pdl_wait();
   pdl_launch_dependents();
+  if (threadIdx.x == 0) trace_stamp(tr, 1);
 
   // every global load first, then the norms, then the stores
   float qv[8], kvr[8];
@@ -717,6 +721,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2)
   }
 
   if constexpr (kCluster) asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+  if (threadIdx.x == 0) trace_stamp(tr, 2);
 
   // Rounds of bpr blocks; warp w takes (head w % G, block r*bpr + w / G).
   const int nblk_max = attn_n_blocks(a.ctx);
@@ -853,6 +858,10 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2)
           [&](int c) { return rows[(size_t)c * kMergeRow + lane]; });
       write_unit(o, u, lane, hb, hd, true, outp, oq8);
     }
+    if (tr) {
+      __syncthreads();
+      if (threadIdx.x == 0) trace_stamp(tr, 3);
+    }
   } else {
     __shared__ unsigned ticket_s;
     unsigned* counter = a.counters + (size_t)z * a.n_kv + kvh;
@@ -863,6 +872,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2)
       ticket_s = t;
     }
     __syncthreads();
+    if (threadIdx.x == 0) trace_stamp(tr, 3);
     if (ticket_s != (unsigned)(S - 1)) return;
     if (threadIdx.x == 0) atomicExch(counter, 0u);
     const float* part = a.partial + ((size_t)z * a.n_head + hb) * nblk_max * stride_part;

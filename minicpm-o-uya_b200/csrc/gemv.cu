@@ -71,6 +71,8 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1) k_gemv(const Gemv
   uint64_t* empty = full + NC * S;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  unsigned long long* tr = a.trace ? a.trace + (size_t)blockIdx.x * 4 : nullptr;
+  if (threadIdx.x == 0) trace_stamp(tr, 0);
   if (a.pdl_early && threadIdx.x == 0) pdl_launch_dependents();
   const int T = a.total_wr, G = gridDim.x;
   int wr0, wr1, blk0 = 0, nblk = 0;
@@ -137,8 +139,10 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1) k_gemv(const Gemv
   float wpre[8];
   gemv_norm_weights(a, warp, lane, wpre);
   pdl_wait();  // the activations (and y for the residual add) come from earlier kernels
+  if (threadIdx.x == 0) trace_stamp(tr, 1);
   gemv_build_x(a, smem, NC, warp, lane, wpre);
   asm volatile("bar.sync 1, %0;" ::"r"(NC * 32) : "memory");
+  if (threadIdx.x == 0) trace_stamp(tr, 2);
   if (!a.pdl_early && threadIdx.x == 0) pdl_launch_dependents();
   const XShared x = gemv_x_view(smem, cols);
   int n = 0;
@@ -164,6 +168,10 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1) k_gemv(const Gemv
       const int r = (blk0 + b) * 32 + lane;
       quant_block_warp(r < rows ? stage[b * 32 + lane] : 0.0f, a.q8_out + (size_t)(blk0 + b) * 36, lane);
     }
+  }
+  if (tr) {
+    asm volatile("bar.sync 1, %0;" ::"r"(NC * 32) : "memory");
+    if (threadIdx.x == 0) trace_stamp(tr, 3);
   }
 }
 

@@ -127,6 +127,11 @@ struct Model {
   unsigned* step_scratch = nullptr;  // [barrier, abort, pad, pad, attention counters...]
   size_t step_scratch_bytes = 0;
   unsigned long long* step_trace = nullptr;  // MCPO_STEP_TRACE=1: per-stage, per-CTA timestamps
+  // MCPO_GRAPH_TRACE=1: per-launch, per-CTA timestamps of the per-operation
+  // step ([launch][trace_ctas][4]: q/k/v, attention, o, gate/up, down per
+  // layer, then the lm_head)
+  unsigned long long* graph_trace = nullptr;
+  int trace_launches = 0, trace_ctas = 0;
   // tensor parallelism (tp_world > 1): this rank's shards, local dims in cfg
   int tp_world = 1, tp_rank = 0;
   uint32_t vocab_global = 0, vocab_base = 0;
@@ -491,7 +496,7 @@ void free_model(Model* m) {
   void* bufs[] = {m->hidden, m->normed, m->q,     m->k,       m->v,         m->attn,       m->gate,     m->up,
                   m->fused,  m->tmp,    m->logits, m->xq,     m->aq,        m->fq,         m->kc,       m->vc,
                   m->rope_cos, m->rope_sin, m->partial, m->counters, m->am_scratch, m->am_counter, m->st, m->seen,
-                  m->history, m->stages, m->step_scratch, m->step_trace, m->tp_epoch, m->tp_step, m->hidden2, m->embed_in,
+                  m->history, m->stages, m->step_scratch, m->step_trace, m->graph_trace, m->tp_epoch, m->tp_step, m->hidden2, m->embed_in,
                   m->smp_seen, m->smp_io, m->smp_bits, m->smp_st, m->pf_hidden, m->pf_q, m->pf_k, m->pf_v,
                   m->pf_attn, m->pf_fused, m->pf_partial, m->pf_tok, m->pf_pos, m->pf_counters,
                   m->pf_err};
@@ -509,10 +514,11 @@ void free_model(Model* m) {
 // dense ones the f32 input x.
 // With xq == nullptr a quantised GEMV quantises x itself (kInF32).
 cudaError_t model_mv(Ctx* c, Upload* w, const float* x, const uint8_t* xq, float* y, int epi, float* tmp, int grid,
-                     int* err, const PfList* pf = nullptr) {
+                     int* err, const PfList* pf = nullptr, unsigned long long* trace = nullptr) {
   if (w->tiled) {
     GemvArgs a{};
     if (pf) a.pf = *pf;
+    a.trace = trace;
     a.nseg = 1;
     a.cols = (int)w->cols;
     a.input = xq ? kInQ8_1 : kInF32;
@@ -677,6 +683,11 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
     return t;
   };
   if (tp) REC(launch_tp_step(m.tp_step, s));
+  int traced = 0;
+  auto trace_next = [&]() -> unsigned long long* {
+    if (!m.graph_trace || traced >= m.trace_launches) return nullptr;
+    return m.graph_trace + (size_t)(traced++) * m.trace_ctas * 4;
+  };
   if (m.step_ok) {
     // the whole layer chain (and the lm_head) as one persistent kernel
     cudaError_t e = cudaMemsetAsync(m.step_scratch, 0, m.step_scratch_bytes, s);
@@ -717,6 +728,7 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
       float* ys[3] = {m.q, m.k, m.v};
       for (int i = 0; i < 3; ++i) gemv_seg_from_geom(qkv[i]->geom, qkv[i]->dev, nullptr, ys[i], kEpiStore, &a.seg[i]);
       a.pf = pf.next(qkv_end);
+      a.trace = trace_next();
       REC(launch_gemv(a, m.grid_h, s, true));
     } else {
       REC(launch_rmsnorm_q8_1(m.hidden, L.attn_norm->dev, L.attn_norm->dtype, h, cf.rms_eps, m.normed, m.xq, s, true));
@@ -755,6 +767,7 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
     a.out_q8 = (L.o->tiled && hd % 32 == 0) ? m.aq : nullptr;
     a.err = &m.st->err;
     a.pf = pf.next(qkv_end, pf_attn);
+    a.trace = trace_next();
     REC(launch_attention(a, s, true));
     // (head_dim % 32 != 0: the o GEMV quantises the f32 attention output itself)
     if (tp) {  // row-parallel: this rank's partial pushed to every rank (exchange 2l)
@@ -767,10 +780,11 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
       o.err = &m.st->err;
       gemv_seg_from_geom(L.o->geom, L.o->dev, nullptr, nullptr, kEpiTpPush, &o.seg[0]);
       o.tp = xchg(2 * (int)li, nullptr);
+      o.trace = trace_next();
       REC(launch_gemv(o, m.grid_q, s, true));
     } else {
       const PfList opf = pf.next(pf.stream.empty() ? 0 : pf.end_of(L.o));
-      REC(model_mv(c, L.o, m.attn, a.out_q8, m.hidden, kEpiAdd, m.tmp, m.grid_q, &m.st->err, &opf));
+      REC(model_mv(c, L.o, m.attn, a.out_q8, m.hidden, kEpiAdd, m.tmp, m.grid_q, &m.st->err, &opf, trace_next()));
     }
     // feed-forward block: RMSNorm -> Q8_1 inside the gate/up GEMV, SwiGLU in
     // its epilogue, which also writes the Q8_1 blocks the down GEMV reads
@@ -790,6 +804,7 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
       if (!tp && L.down->tiled && ffn_q8_cfg()) g.q8_out = m.fq;
       down_q8 = g.q8_out;
       g.pf = pf.next(pf.stream.empty() ? 0 : pf.end_of(L.up));
+      g.trace = trace_next();
       REC(launch_gemv(g, m.grid_h, s, true));
     } else {
       REC(launch_rmsnorm_q8_1(m.hidden, L.ffn_norm->dev, L.ffn_norm->dtype, h, cf.rms_eps, m.normed, m.xq, s, true));
@@ -806,10 +821,11 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
       d.err = &m.st->err;
       gemv_seg_from_geom(L.down->geom, L.down->dev, nullptr, nullptr, kEpiTpPush, &d.seg[0]);
       d.tp = xchg(2 * (int)li + 1, nullptr);
+      d.trace = trace_next();
       REC(launch_gemv(d, m.grid_f, s, true));
     } else {
       const PfList dpf = pf.next(pf.stream.empty() ? 0 : pf.end_of(L.down));
-      REC(model_mv(c, L.down, m.fused, down_q8, m.hidden, kEpiAdd, m.tmp, m.grid_f, &m.st->err, &dpf));
+      REC(model_mv(c, L.down, m.fused, down_q8, m.hidden, kEpiAdd, m.tmp, m.grid_f, &m.st->err, &dpf, trace_next()));
     }
   }
   if (tp && !logits)  // the last exchange still completes the residual stream (hidden_out)
@@ -826,6 +842,7 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
       }
       o.err = &m.st->err;
       gemv_seg_from_geom(m.out->geom, m.out->dev, nullptr, m.logits, kEpiStore, &o.seg[0]);
+      o.trace = trace_next();
       REC(launch_gemv(o, m.grid_h, s, true));
     } else {
       REC(launch_rmsnorm_q8_1(m.hidden, m.out_norm->dev, m.out_norm->dtype, h, cf.rms_eps, m.normed, m.xq, s, true));
@@ -1520,6 +1537,18 @@ int bind_model(Ctx* c, const minicpmo_qwen3_config* cfg, char* err, size_t cap, 
   m.kv_layer_elems = (size_t)cf.context * m.kvd;
   const size_t esz = cf.kv_f16 ? 2 : 4;
   m.n_split = attn_n_split((int)lc.kv_heads);
+  {
+    const char* gt = getenv("MCPO_GRAPH_TRACE");
+    if (gt && gt[0] == '1') {
+      m.trace_launches = 5 * (int)lc.layers + 1;
+      m.trace_ctas = std::max(c->sm_count, (int)lc.kv_heads * m.n_split);
+      const size_t tb = (size_t)m.trace_launches * m.trace_ctas * 4 * 8;
+      if (cudaMalloc((void**)&m.graph_trace, tb) != cudaSuccess || cudaMemset(m.graph_trace, 0, tb) != cudaSuccess) {
+        cudaGetLastError();
+        m.graph_trace = nullptr;
+      }
+    }
+  }
   m.am_grid = c->sm_count;
   m.history_cap = 1 << 16;
   struct A {
@@ -3221,6 +3250,20 @@ int minicpmo_gpu_context_qwen3_step_trace(void* handle, uint64_t* out, size_t ca
   if (n_ctas) *n_ctas = (uint32_t)c->sm_count;
   if (!out || cap < n) return 0;
   if (cudaMemcpy(out, m.step_trace, n * 8, cudaMemcpyDeviceToHost) != cudaSuccess) return 0;
+  return 1;
+}
+
+int minicpmo_gpu_context_qwen3_graph_trace(void* handle, uint64_t* out, size_t cap, uint32_t* n_launches,
+                                           uint32_t* n_ctas) {
+  Ctx* c = (Ctx*)handle;
+  if (!c || !c->model || !c->model->graph_trace) return 0;
+  DeviceGuard g(c);
+  Model& m = *c->model;
+  const size_t n = (size_t)m.trace_launches * m.trace_ctas * 4;
+  if (n_launches) *n_launches = (uint32_t)m.trace_launches;
+  if (n_ctas) *n_ctas = (uint32_t)m.trace_ctas;
+  if (!out || cap < n) return 0;
+  if (cudaMemcpy(out, m.graph_trace, n * 8, cudaMemcpyDeviceToHost) != cudaSuccess) return 0;
   return 1;
 }
 

@@ -118,6 +118,15 @@ __device__ __forceinline__ void bulk_load_hint(void* dst, const void* src, uint3
 }
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// globaltimer (ns) into t[i] when a timeline is being recorded.
+__device__ __forceinline__ void trace_stamp(unsigned long long* t, int i) {
+  if (t) {
+    unsigned long long v;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(v));
+    t[i] = v;
+  }
+}
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 }  // namespace mcpo

@@ -151,6 +151,7 @@ SIGNATURES = {
     "minicpmo_gpu_context_tensor_device_bytes": (sz, [vp, vp]),
     "minicpmo_gpu_context_qwen3_step_kernels": (i32, [vp, i32]),
     "minicpmo_gpu_context_qwen3_step_trace": (i32, [vp, vp, sz, u32ptr, u32ptr]),
+    "minicpmo_gpu_context_qwen3_graph_trace": (i32, [vp, vp, sz, u32ptr, u32ptr]),
     "minicpmo_gpu_attention_no_alloc": (i32, [vp, vp, vp, i32, sz, sz, sz, sz, sz, vp, vp] + E),
 }
 
@@ -532,6 +533,18 @@ class GpuContext:
             return None
         out = np.empty((ns.value, nc.value, 3), np.uint64)
         if not self.lib.minicpmo_gpu_context_qwen3_step_trace(self.handle, out.ctypes.data, out.size, None, None):
+            return None
+        return out
+
+    def qwen3_graph_trace(self):
+        """[launch][cta][start, past wait, ready, done] ns of the last per-operation step (MCPO_GRAPH_TRACE=1 at
+        bind), or None."""
+        nl, nc = u32(), u32()
+        self.lib.minicpmo_gpu_context_qwen3_graph_trace(self.handle, None, 0, C.byref(nl), C.byref(nc))
+        if nl.value == 0:
+            return None
+        out = np.empty((nl.value, nc.value, 4), np.uint64)
+        if not self.lib.minicpmo_gpu_context_qwen3_graph_trace(self.handle, out.ctypes.data, out.size, None, None):
             return None
         return out
 
