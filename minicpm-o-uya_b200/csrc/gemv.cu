@@ -108,7 +108,7 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1) k_gemv(const Gemv
     // up the copies of another).  Needs nothing from the previous kernel, so
     // it does not wait for it.
     const int w = lane;
-    if (w >= NC) return;
+    if (w >= NC || a.self_issue) return;
     const int steps = (nwr > w ? (nwr - w + NC - 1) / NC : 0) * spi;
     const uint64_t policy = l2_evict_first_policy();
     bool ok = true;
@@ -136,6 +136,12 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1) k_gemv(const Gemv
   }
 
   // ---- consumers ----
+  int issued = 0;
+  if (a.self_issue && lane == 0) {  // the first S blocks, before the wait for the previous kernel
+    const uint64_t policy = l2_evict_first_policy();
+    for (int m = 0; m < S; ++m)
+      if (gemv_issue_step(a, ring, full, S, slot, wr0, nwr, NC, warp, m, policy)) issued = m + 1;
+  }
   float wpre[8];
   gemv_norm_weights(a, warp, lane, wpre);
   pdl_wait();  // the activations (and y for the residual add) come from earlier kernels
@@ -147,7 +153,14 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1) k_gemv(const Gemv
   const XShared x = gemv_x_view(smem, cols);
   int n = 0;
   float* stage = a.q8_out ? reinterpret_cast<float*>(empty + NC * S) : nullptr;
-  gemv_items<kClass, kDots>(a, x, ring, full, empty, S, slot, wr0, nwr, NC, warp, lane, n, nullptr, stage, blk0 * 32);
+  gemv_items<kClass, kDots>(a, x, ring, full, empty, S, slot, wr0, nwr, NC, warp, lane, n, nullptr, stage, blk0 * 32,
+                            a.self_issue ? &issued : nullptr);
+  if (a.self_issue && lane == 0) {
+    // copies issued but not consumed (a wait gave up) land before the CTA
+    // leaves; each wait is bounded
+    for (int m = n; m < issued; ++m)
+      if (!mbar_wait(&full[warp * S + m % S], (uint32_t)(m / S) & 1u, a.err)) break;
+  }
   if (a.seg[0].epi == kEpiTpPush) {
     // every consumer's remote stores are visible system-wide before the
     // arrival counts say so (tp_proto.h)
@@ -340,6 +353,10 @@ int early_cfg() {
   static const int v = env_int("MCPO_GEMV_EARLY", 0);
   return v;
 }
+int self_issue_cfg() {
+  static const int v = env_int("MCPO_GEMV_SELF", 0);
+  return v;
+}
 
 template <int kClass, bool kDots>
 cudaError_t set_smem_attr() {
@@ -409,6 +426,7 @@ cudaError_t launch_gemv(GemvArgs& a, int grid, cudaStream_t st, bool pdl) {
   const int stages = stages_cfg() < 1 ? 1 : stages_cfg();
   a.stages = stages;
   a.pdl_early = pdl && early_cfg() ? 1 : 0;
+  a.self_issue = self_issue_cfg() && a.nvec <= 1 ? 1 : 0;
   if (wr == 0) return cudaSuccess;
   if (a.nvec > kGemvMaxVec || (a.nvec > 1 && a.dots)) return cudaErrorInvalidValue;
   const size_t xb = a.nvec > 1 ? gemv_x_bytes(a.cols) * (size_t)a.nvec : gemv_x_region(a.cols, a.input);

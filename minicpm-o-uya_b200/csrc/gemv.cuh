@@ -83,6 +83,8 @@ struct GemvArgs {
   // 1: allow the next kernel to launch as soon as this one starts (its CTAs
   // then stream their weights while this kernel runs, where both fit an SM)
   int pdl_early;
+  // 1: each consumer warp issues its own ring copies (the producer warp idles)
+  int self_issue;
   // optional timeline, [CTA][4] globaltimer ns: start, past the wait for the
   // previous kernel, activations ready, all consumer warps done
   unsigned long long* trace;

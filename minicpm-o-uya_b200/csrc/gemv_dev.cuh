@@ -577,16 +577,42 @@ __device__ __forceinline__ XShared gemv_x_view(uint8_t* xbase, int cols) {
                  cols / 256};
 }
 
+// Self-issued rings: consumer warp `warp` (lane 0) issues its own step
+// block n into slot n % S -- the copy the producer warp would issue -- once
+// the warp has finished with the block that slot held.
+__device__ __forceinline__ void fence_proxy_async_cta() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Copies step block n of this warp's sequence into its ring; false when the
+// warp has fewer than n + 1 step blocks.
+__device__ __forceinline__ bool gemv_issue_step(const GemvArgs& a, uint8_t* ring, uint64_t* full, int S, int slot,
+                                                int wr0, int nwr, int NC, int warp, int n, uint64_t policy) {
+  const int ks = a.seg[0].ks;
+  const int spi = ks * (a.seg[0].epi == kEpiSwiglu ? 2 : 1);
+  const int items = nwr > warp ? (nwr - warp + NC - 1) / NC : 0;
+  if (n >= items * spi) return false;
+  const int item = n / spi, rem = n % spi, part = rem / ks, k = rem % ks;
+  const int wr = wr0 + warp + NC * item;
+  const GemvSeg& sg = seg_of(a, wr);
+  const uint8_t* src = (part ? sg.w2 : sg.w) + (size_t)(wr - sg.wr_begin) * sg.wr_bytes + (size_t)k * sg.step_bytes;
+  const int sidx = n % S;
+  mbar_arrive_expect_tx(&full[warp * S + sidx], (uint32_t)sg.step_bytes);
+  bulk_load_hint(ring + (size_t)(warp * S + sidx) * slot, src, (uint32_t)sg.step_bytes, &full[warp * S + sidx], policy);
+  return true;
+}
+
 // The consumer loop of one GEMV over warp-rows [wr0, wr0 + nwr) of a CTA:
 // warp `warp` of NC takes items warp, warp + NC, ...; its step blocks arrive
 // in order in its ring (S slots of `slot` bytes; full/empty mbarriers), n
 // counting the blocks this warp has consumed so far.  Returns false when a
 // wait gave up (error raised) or *abort was set.
+// With self_issue the warp refills its own ring (no producer warp, empty
+// barriers unused): *issued counts the copies it has issued so far.
 template <int kClass, bool kDots>
 __device__ __forceinline__ bool gemv_items(const GemvArgs& a, const XShared& x, uint8_t* ring, uint64_t* full,
                                            uint64_t* empty, int S, int slot, int wr0, int nwr, int NC, int warp,
                                            int lane, int& n, const volatile int* abort, float* stage = nullptr,
-                                           int stage_r0 = 0) {
+                                           int stage_r0 = 0, int* issued = nullptr) {
+  const uint64_t policy = issued ? l2_evict_first_policy() : 0;
   const int cols = a.cols;
   const bool swiglu = a.seg[0].epi == kEpiSwiglu;
   const int ks = a.seg[0].ks;
@@ -614,7 +640,15 @@ __device__ __forceinline__ bool gemv_items(const GemvArgs& a, const XShared& x, 
             step_value<kClass, kDots>(s.dtype, blk, lane, x, k * s.lpr + lane_in_row, part == 0 ? dots : nullptr);
         acc[part] = __fadd_rn(acc[part], v);
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[warp * S + sidx]);
+        if (issued) {
+          // the slot's reads are done: its next block (n + S) goes in
+          if (lane == 0) {
+            fence_proxy_async_cta();
+            if (gemv_issue_step(a, ring, full, S, slot, wr0, nwr, NC, warp, n + S, policy)) *issued = n + S + 1;
+          }
+        } else if (lane == 0) {
+          mbar_arrive(&empty[warp * S + sidx]);
+        }
       }
     }
     const float g = reduce_row(acc[0], s.lpr);
