@@ -249,6 +249,23 @@ def run_kernel_sweep(args) -> int:
     g = GpuContext(local)
     hbm, peak_kind = peaks()
     names = {10: "Q4_K", 12: "Q6_K", 6: "Q8_0"}
+    if args.sweep_launches > 0:
+        # for a profiler's launch list: each case's Q8_1-input GEMV launched a few times on its own, one
+        # tensor resident at a time (no timing, no rotated copies)
+        for rows, cols in [(4096, 4096), (12288, 4096), (4096, 12288), (151936, 4096)]:
+            for dt in (10, 12, 6):
+                name = f"sweep.{names[dt]}.{rows}x{cols}"
+                t = Tensor(name, gguf.synth_tensor(name, dt, rows, cols, "weight", device="cuda"), dt, rows, cols)
+                g.upload_tensor(t)
+                xq = g.q8_1_quantize(np.ones(cols, np.float32))
+                for _ in range(args.sweep_launches):
+                    g.matvec_q8_1(t, xq)
+                print(json.dumps({"kernel_sweep_launches": {"dtype": names[dt], "rows": rows, "cols": cols,
+                                                            "launches": args.sweep_launches}}), flush=True)
+                g.close()
+                g = GpuContext(local)
+        g.close()
+        return 0
     norms = {}
     for rows, cols in [(4096, 4096), (12288, 4096), (4096, 12288), (151936, 4096)]:
         for dt in (10, 12, 6):
@@ -461,6 +478,9 @@ def main() -> int:
                     help="under torchrun: N independent replicas (one sequence each, weak scaling) instead of the "
                          "default tensor parallelism over the N GPUs (one sequence, strong scaling)")
     ap.add_argument("--tp", action="store_true", help="(the default under torchrun; kept for old command lines)")
+    ap.add_argument("--sweep-launches", type=int, default=0,
+                    help="with --kernel-sweep: launch each case's Q8_1-input GEMV this many times without timing "
+                         "(a launch list for a profiler), one weight tensor resident at a time")
     ap.add_argument("--kernel-sweep", action="store_true",
                     help="BASELINE config 1: time the GEMV on each shape x dtype (and its fused prologues); "
                          "one JSON line per case")

@@ -367,10 +367,11 @@ MINICPMO_API int minicpmo_gpu_context_qwen3_step_trace(void *handle, uint64_t *o
  * per-operation decode step records per launch and CTA the globaltimer (ns)
  * at the CTA's start, past its wait for the previous kernel, when its
  * activations are ready (attention: when its round of blocks begins) and
- * when it is done; launches in order q/k/v, attention, o, gate/up, down per
- * layer, then the lm_head.  This copies the last step's record,
- * [launch][cta][4] (zeros for CTAs a launch does not have), into out (cap
- * entries).  0 when tracing is off. */
+ * when it is done (attention also: its blocks done, past its cluster
+ * barrier); launches in order q/k/v, attention, o, gate/up, down per layer,
+ * then the lm_head.  This copies the last step's record, [launch][cta][8]
+ * (zeros where nothing was recorded), into out (cap entries).  0 when
+ * tracing is off. */
 MINICPMO_API int minicpmo_gpu_context_qwen3_graph_trace(void *handle, uint64_t *out, size_t cap, uint32_t *n_launches,
                                            uint32_t *n_ctas);
 /* Bytes of device memory held by the uploaded copy of a tensor. */

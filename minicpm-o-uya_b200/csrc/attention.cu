@@ -580,7 +580,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2)
   const int kvh = blockIdx.x, split = blockIdx.y, z = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   unsigned long long* tr =
-      a.trace ? a.trace + ((size_t)(blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x) * 4 : nullptr;
+      a.trace ? a.trace + ((size_t)(blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x) * 8 : nullptr;
   if (threadIdx.x == 0) trace_stamp(tr, 0);
   const int hb = (kvh * a.n_head + a.n_kv - 1) / a.n_kv;
   const int he = ((kvh + 1) * a.n_head + a.n_kv - 1) / a.n_kv;
@@ -847,8 +847,10 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2)
   // ---- merge over blocks in block order.  Unit u = 32 consecutive output
   // values of this kv head's G heads, lane = value.
   const int n_units = (G * hd + 31) / 32;
+  if (threadIdx.x == 0) trace_stamp(tr, 4);
   if constexpr (kCluster) {
     cluster_sync_all();  // every merge row of this CTA's units has arrived
+    if (threadIdx.x == 0) trace_stamp(tr, 5);
     for (int slot = warp; split + slot * S < n_units; slot += kAttnWarps) {
       const int u = split + slot * S;
       const float* rows = s_merge + (size_t)slot * nblk_max * kMergeRow;

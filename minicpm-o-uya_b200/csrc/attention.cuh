@@ -52,8 +52,9 @@ struct AttnArgs {
   int pos_stride;  // ints between sequences' positions at pos_ptr (0: 1)
   int* err;        // raised by a bounded wait that gave up (may be null)
   PfList pf;       // weight bytes of later kernels to prefetch into L2 before the wait (n = 0: none)
-  // optional timeline, [CTA (x fastest, then y, z)][4] globaltimer ns: start,
-  // past the wait for the previous kernel, the round of blocks begun, done
+  // optional timeline, [CTA (x fastest, then y, z)][8] globaltimer ns: start,
+  // past the wait for the previous kernel, the round of blocks begun, done,
+  // blocks done, past the cluster barrier (3 unused)
   unsigned long long* trace;
 };
 

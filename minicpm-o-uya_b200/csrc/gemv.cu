@@ -71,7 +71,7 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1) k_gemv(const Gemv
   uint64_t* empty = full + NC * S;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  unsigned long long* tr = a.trace ? a.trace + (size_t)blockIdx.x * 4 : nullptr;
+  unsigned long long* tr = a.trace ? a.trace + (size_t)blockIdx.x * 8 : nullptr;
   if (threadIdx.x == 0) trace_stamp(tr, 0);
   if (a.pdl_early && threadIdx.x == 0) pdl_launch_dependents();
   const int T = a.total_wr, G = gridDim.x;

@@ -85,8 +85,8 @@ struct GemvArgs {
   int pdl_early;
   // 1: each consumer warp issues its own ring copies (the producer warp idles)
   int self_issue;
-  // optional timeline, [CTA][4] globaltimer ns: start, past the wait for the
-  // previous kernel, activations ready, all consumer warps done
+  // optional timeline, [CTA][8] globaltimer ns: start, past the wait for the
+  // previous kernel, activations ready, all consumer warps done (4 unused)
   unsigned long long* trace;
 };
 

@@ -128,7 +128,7 @@ struct Model {
   size_t step_scratch_bytes = 0;
   unsigned long long* step_trace = nullptr;  // MCPO_STEP_TRACE=1: per-stage, per-CTA timestamps
   // MCPO_GRAPH_TRACE=1: per-launch, per-CTA timestamps of the per-operation
-  // step ([launch][trace_ctas][4]: q/k/v, attention, o, gate/up, down per
+  // step ([launch][trace_ctas][8]: q/k/v, attention, o, gate/up, down per
   // layer, then the lm_head)
   unsigned long long* graph_trace = nullptr;
   int trace_launches = 0, trace_ctas = 0;
@@ -686,7 +686,7 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
   int traced = 0;
   auto trace_next = [&]() -> unsigned long long* {
     if (!m.graph_trace || traced >= m.trace_launches) return nullptr;
-    return m.graph_trace + (size_t)(traced++) * m.trace_ctas * 4;
+    return m.graph_trace + (size_t)(traced++) * m.trace_ctas * 8;
   };
   if (m.step_ok) {
     // the whole layer chain (and the lm_head) as one persistent kernel
@@ -1542,7 +1542,7 @@ int bind_model(Ctx* c, const minicpmo_qwen3_config* cfg, char* err, size_t cap, 
     if (gt && gt[0] == '1') {
       m.trace_launches = 5 * (int)lc.layers + 1;
       m.trace_ctas = std::max(c->sm_count, (int)lc.kv_heads * m.n_split);
-      const size_t tb = (size_t)m.trace_launches * m.trace_ctas * 4 * 8;
+      const size_t tb = (size_t)m.trace_launches * m.trace_ctas * 8 * 8;
       if (cudaMalloc((void**)&m.graph_trace, tb) != cudaSuccess || cudaMemset(m.graph_trace, 0, tb) != cudaSuccess) {
         cudaGetLastError();
         m.graph_trace = nullptr;
@@ -3259,7 +3259,7 @@ int minicpmo_gpu_context_qwen3_graph_trace(void* handle, uint64_t* out, size_t c
   if (!c || !c->model || !c->model->graph_trace) return 0;
   DeviceGuard g(c);
   Model& m = *c->model;
-  const size_t n = (size_t)m.trace_launches * m.trace_ctas * 4;
+  const size_t n = (size_t)m.trace_launches * m.trace_ctas * 8;
   if (n_launches) *n_launches = (uint32_t)m.trace_launches;
   if (n_ctas) *n_ctas = (uint32_t)m.trace_ctas;
   if (!out || cap < n) return 0;

@@ -537,13 +537,13 @@ class GpuContext:
         return out
 
     def qwen3_graph_trace(self):
-        """[launch][cta][start, past wait, ready, done] ns of the last per-operation step (MCPO_GRAPH_TRACE=1 at
-        bind), or None."""
+        """[launch][cta][8] ns of the last per-operation step (MCPO_GRAPH_TRACE=1 at bind): start, past wait,
+        ready, done (attention also blocks done, past the cluster barrier), or None."""
         nl, nc = u32(), u32()
         self.lib.minicpmo_gpu_context_qwen3_graph_trace(self.handle, None, 0, C.byref(nl), C.byref(nc))
         if nl.value == 0:
             return None
-        out = np.empty((nl.value, nc.value, 4), np.uint64)
+        out = np.empty((nl.value, nc.value, 8), np.uint64)
         if not self.lib.minicpmo_gpu_context_qwen3_graph_trace(self.handle, out.ctypes.data, out.size, None, None):
             return None
         return out

@@ -15,12 +15,15 @@
  * [context][head_dim/2], cos then sin) and one f32 embedding row per token.
  * The driver runs the reference host's per-operation decode
  * (qwen3_forward_embedding_runtime_cuda, qwen3.uya:1865-1918): every call is
- * one of the 19 bridge forwarders, and writes each token's logits.
+ * one of the 19 bridge forwarders, and writes each token's logits.  It prints
+ * one JSON line with the helper's stats and the decode rate of the tokens
+ * after the first (host clock, every token's logits downloaded).
  */
 #include <stdint.h>
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
+#include <time.h>
 
 typedef struct minicpmo_gpu_stats {
     uint64_t v[13];
@@ -119,7 +122,9 @@ int main(int argc, char **argv) {
                                                  sizeof(err)));
     }
     CHECK(minicpmo_gpu_context_prepare_attention(h, layers, context, (size_t) kvh * hd, err, sizeof(err)));
+    struct timespec t0, t1;
     for (t = 0; t < ntok; ++t) {
+        if (t == 1) clock_gettime(CLOCK_MONOTONIC, &t0);
         CHECK(minicpmo_gpu_context_slot_upload_f32(h, HID, emb + (size_t) t * hidden, hidden, err, sizeof(err)));
         for (l = 0; l < layers; ++l) {
             char n[16][96];
@@ -161,9 +166,13 @@ int main(int argc, char **argv) {
         CHECK(minicpmo_gpu_context_slot_download_f32(h, LOG, logits, vocab, err, sizeof(err)));
         if (fwrite(logits, 4, vocab, out) != vocab) return 2;
     }
+    clock_gettime(CLOCK_MONOTONIC, &t1);
     minicpmo_gpu_context_snapshot(h, &st);
-    printf("{\"native_quant_matvec_count\": %llu, \"attention_kernel_calls\": %llu}\n",
-           (unsigned long long) st.v[7], (unsigned long long) st.v[10]);
+    {
+        const double s = (double) (t1.tv_sec - t0.tv_sec) + 1e-9 * (double) (t1.tv_nsec - t0.tv_nsec);
+        printf("{\"native_quant_matvec_count\": %llu, \"attention_kernel_calls\": %llu, \"tok_per_s\": %.3f}\n",
+               (unsigned long long) st.v[7], (unsigned long long) st.v[10], ntok > 1 && s > 0 ? (ntok - 1) / s : 0.0);
+    }
     minicpmo_gpu_context_destroy(h);
     fclose(out);
     return 0;
