@@ -108,6 +108,19 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1) k_gemv(const Gemv
     // up the copies of another).  Needs nothing from the previous kernel, so
     // it does not wait for it.
     const int w = lane;
+    if (w >= NC && a.kv_pos) {
+      // idle lanes: this layer's K/V rows into L2 for the attention after this
+      // kernel (the position was written before this step's graph started)
+      const int pos = *a.kv_pos;
+      PfList kl{};
+      const unsigned long long bytes = (unsigned long long)(pos + 1) * (unsigned long long)a.kv_row_bytes;
+      if (pos >= 0 && pos < a.kv_ctx && (bytes & 15ull) == 0) {
+        kl.r[0] = PfRange{a.kv_k, bytes};
+        kl.r[1] = PfRange{a.kv_v, bytes};
+        kl.n = 2;
+        l2_prefetch_share(kl, blockIdx.x, gridDim.x, w - NC, 32 - NC);
+      }
+    }
     if (w >= NC || a.self_issue) return;
     const int steps = (nwr > w ? (nwr - w + NC - 1) / NC : 0) * spi;
     const uint64_t policy = l2_evict_first_policy();

@@ -85,6 +85,13 @@ struct GemvArgs {
   int pdl_early;
   // 1: each consumer warp issues its own ring copies (the producer warp idles)
   int self_issue;
+  // optional: a layer's K and V cache rows [0, *kv_pos] prefetched into L2 at
+  // the start (for the attention that follows); row_bytes per position
+  const uint8_t* kv_k;
+  const uint8_t* kv_v;
+  const int* kv_pos;
+  int kv_row_bytes;
+  int kv_ctx;  // positions in the cache (a position outside [0, kv_ctx) prefetches nothing)
   // optional timeline, [CTA][8] globaltimer ns: start, past the wait for the
   // previous kernel, activations ready, all consumer warps done (4 unused)
   unsigned long long* trace;

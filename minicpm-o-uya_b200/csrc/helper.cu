@@ -606,6 +606,15 @@ size_t pf_window_cfg() {
   }();
   return v;
 }
+// 1 (MCPO_KV_PF=1): the q/k/v GEMV prefetches its layer's K/V rows into L2.
+int kv_prefetch_cfg() {
+  static const int v = [] {
+    const char* e = getenv("MCPO_KV_PF");
+    return (e && *e) ? atoi(e) : 0;
+  }();
+  return v;
+}
+
 size_t pf_attn_window_cfg() {
   static const size_t v = [] {
     const char* e = getenv("MCPO_PF_ATTN_MB");
@@ -729,6 +738,14 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
       for (int i = 0; i < 3; ++i) gemv_seg_from_geom(qkv[i]->geom, qkv[i]->dev, nullptr, ys[i], kEpiStore, &a.seg[i]);
       a.pf = pf.next(qkv_end);
       a.trace = trace_next();
+      if (kv_prefetch_cfg()) {
+        const size_t esz = cf.kv_f16 ? 2 : 4;
+        a.kv_k = (const uint8_t*)m.kc + li * m.kv_layer_elems * esz;
+        a.kv_v = (const uint8_t*)m.vc + li * m.kv_layer_elems * esz;
+        a.kv_pos = &m.st->pos;
+        a.kv_row_bytes = (int)(m.kvd * esz);
+        a.kv_ctx = (int)cf.context;
+      }
       REC(launch_gemv(a, m.grid_h, s, true));
     } else {
       REC(launch_rmsnorm_q8_1(m.hidden, L.attn_norm->dev, L.attn_norm->dtype, h, cf.rms_eps, m.normed, m.xq, s, true));
