@@ -363,8 +363,10 @@ MINICPMO_API int minicpmo_gpu_context_qwen3_step_kernels(void *handle, int with_
  * is off. */
 MINICPMO_API int minicpmo_gpu_context_qwen3_step_trace(void *handle, uint64_t *out, size_t cap, uint32_t *n_stages,
                                           uint32_t *n_ctas);
-/* With MCPO_GRAPH_TRACE=1 in the environment at bind time, the
- * per-operation decode step records per launch and CTA the globaltimer (ns)
+/* In a library built with TRACE=1 (make -C minicpm-o-uya_b200/csrc TRACE=1;
+ * the default build compiles the timeline out), with MCPO_GRAPH_TRACE=1 in
+ * the environment at bind time, the per-operation decode step records per
+ * launch and CTA the globaltimer (ns)
  * at the CTA's start, past its wait for the previous kernel, when its
  * activations are ready (attention: when its round of blocks begins) and
  * when it is done (attention also: its blocks done, past its cluster

@@ -579,9 +579,11 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2)
 
   const int kvh = blockIdx.x, split = blockIdx.y, z = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#if MCPO_TRACE
   unsigned long long* tr =
       a.trace ? a.trace + ((size_t)(blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x) * 8 : nullptr;
   if (threadIdx.x == 0) trace_stamp(tr, 0);
+#endif
   const int hb = (kvh * a.n_head + a.n_kv - 1) / a.n_kv;
   const int he = ((kvh + 1) * a.n_head + a.n_kv - 1) / a.n_kv;
   const int G = he - hb;
@@ -665,12 +667,11 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2)
       sr[k] = need ? a.rope_sin[(size_t)pos * half + d] : 0.0f;
     }
   }
-  if (a.pf.n > 0 && warp == kAttnWarps - 1)  // later kernels' weights into L2
-    l2_prefetch_share(a.pf, (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x,
-                      gridDim.x * gridDim.y * gridDim.z, lane, 32);
   pdl_wait();
   pdl_launch_dependents();
+#if MCPO_TRACE
   if (threadIdx.x == 0) trace_stamp(tr, 1);
+#endif
 
   // every global load first, then the norms, then the stores
   float qv[8], kvr[8];
@@ -721,7 +722,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2)
   }
 
   if constexpr (kCluster) asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+#if MCPO_TRACE
   if (threadIdx.x == 0) trace_stamp(tr, 2);
+#endif
 
   // Rounds of bpr blocks; warp w takes (head w % G, block r*bpr + w / G).
   const int nblk_max = attn_n_blocks(a.ctx);
@@ -847,10 +850,14 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2)
   // ---- merge over blocks in block order.  Unit u = 32 consecutive output
   // values of this kv head's G heads, lane = value.
   const int n_units = (G * hd + 31) / 32;
+#if MCPO_TRACE
   if (threadIdx.x == 0) trace_stamp(tr, 4);
+#endif
   if constexpr (kCluster) {
     cluster_sync_all();  // every merge row of this CTA's units has arrived
+#if MCPO_TRACE
     if (threadIdx.x == 0) trace_stamp(tr, 5);
+#endif
     for (int slot = warp; split + slot * S < n_units; slot += kAttnWarps) {
       const int u = split + slot * S;
       const float* rows = s_merge + (size_t)slot * nblk_max * kMergeRow;
@@ -860,10 +867,12 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2)
           [&](int c) { return rows[(size_t)c * kMergeRow + lane]; });
       write_unit(o, u, lane, hb, hd, true, outp, oq8);
     }
+#if MCPO_TRACE
     if (tr) {
       __syncthreads();
       if (threadIdx.x == 0) trace_stamp(tr, 3);
     }
+#endif
   } else {
     __shared__ unsigned ticket_s;
     unsigned* counter = a.counters + (size_t)z * a.n_kv + kvh;
@@ -874,7 +883,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2)
       ticket_s = t;
     }
     __syncthreads();
+#if MCPO_TRACE
     if (threadIdx.x == 0) trace_stamp(tr, 3);
+#endif
     if (ticket_s != (unsigned)(S - 1)) return;
     if (threadIdx.x == 0) atomicExch(counter, 0u);
     const float* part = a.partial + ((size_t)z * a.n_head + hb) * nblk_max * stride_part;

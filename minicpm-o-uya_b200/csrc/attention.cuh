@@ -4,7 +4,6 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#include "prefetch.cuh"
 
 namespace mcpo {
 
@@ -51,8 +50,8 @@ struct AttnArgs {
   size_t qkv_bstride, cache_bstride, out_bstride, outq8_bstride;
   int pos_stride;  // ints between sequences' positions at pos_ptr (0: 1)
   int* err;        // raised by a bounded wait that gave up (may be null)
-  PfList pf;       // weight bytes of later kernels to prefetch into L2 before the wait (n = 0: none)
-  // optional timeline, [CTA (x fastest, then y, z)][8] globaltimer ns: start,
+  // optional timeline (builds with MCPO_TRACE=1), [CTA (x fastest, then y,
+  // z)][8] globaltimer ns: start,
   // past the wait for the previous kernel, the round of blocks begun, done,
   // blocks done, past the cluster barrier (3 unused)
   unsigned long long* trace;

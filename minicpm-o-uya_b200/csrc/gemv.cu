@@ -59,7 +59,9 @@ __device__ __forceinline__ void quant_block_warp(float v, uint8_t* dst, int lane
   if ((lane & 3) == 0) o[1 + (lane >> 2)] = word;
 }
 
-template <int kClass, bool kDots>
+// kTp: the tensor-parallel variant (summing prologue and/or push epilogue);
+// the single-GPU kernel compiles none of that code.
+template <int kClass, bool kDots, bool kTp>
 __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1) k_gemv(const GemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int cols = a.cols;
@@ -71,9 +73,10 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1) k_gemv(const Gemv
   uint64_t* empty = full + NC * S;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#if MCPO_TRACE
   unsigned long long* tr = a.trace ? a.trace + (size_t)blockIdx.x * 8 : nullptr;
   if (threadIdx.x == 0) trace_stamp(tr, 0);
-  if (a.pdl_early && threadIdx.x == 0) pdl_launch_dependents();
+#endif
   const int T = a.total_wr, G = gridDim.x;
   int wr0, wr1, blk0 = 0, nblk = 0;
   if (a.q8_out) {
@@ -108,20 +111,7 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1) k_gemv(const Gemv
     // up the copies of another).  Needs nothing from the previous kernel, so
     // it does not wait for it.
     const int w = lane;
-    if (w >= NC && a.kv_pos) {
-      // idle lanes: this layer's K/V rows into L2 for the attention after this
-      // kernel (the position was written before this step's graph started)
-      const int pos = *a.kv_pos;
-      PfList kl{};
-      const unsigned long long bytes = (unsigned long long)(pos + 1) * (unsigned long long)a.kv_row_bytes;
-      if (pos >= 0 && pos < a.kv_ctx && (bytes & 15ull) == 0) {
-        kl.r[0] = PfRange{a.kv_k, bytes};
-        kl.r[1] = PfRange{a.kv_v, bytes};
-        kl.n = 2;
-        l2_prefetch_share(kl, blockIdx.x, gridDim.x, w - NC, 32 - NC);
-      }
-    }
-    if (w >= NC || a.self_issue) return;
+    if (w >= NC) return;
     const int steps = (nwr > w ? (nwr - w + NC - 1) / NC : 0) * spi;
     const uint64_t policy = l2_evict_first_policy();
     bool ok = true;
@@ -138,53 +128,46 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1) k_gemv(const Gemv
       mbar_arrive_expect_tx(&full[w * S + sidx], (uint32_t)s.step_bytes);
       bulk_load_hint(ring + (size_t)(w * S + sidx) * slot, src, (uint32_t)s.step_bytes, &full[w * S + sidx], policy);
     }
-    // The lane's own copies are all issued: now the later kernels' weights
-    // into L2 (after, not before: they must not delay this kernel's stream).
-    if (ok && a.pf.n > 0) l2_prefetch_share(a.pf, blockIdx.x, gridDim.x, w, NC);
     // Leave only once every copy issued into this CTA's shared memory has
     // landed (the consumers normally see to that; this covers their bail-out).
+    (void)ok;
     for (int n = steps - S > 0 ? steps - S : 0; n < steps; ++n)
       if (!mbar_wait(&full[w * S + n % S], (uint32_t)(n / S) & 1u, a.err)) return;
     return;
   }
 
   // ---- consumers ----
-  int issued = 0;
-  if (a.self_issue && lane == 0) {  // the first S blocks, before the wait for the previous kernel
-    const uint64_t policy = l2_evict_first_policy();
-    for (int m = 0; m < S; ++m)
-      if (gemv_issue_step(a, ring, full, S, slot, wr0, nwr, NC, warp, m, policy)) issued = m + 1;
-  }
   float wpre[8];
   gemv_norm_weights(a, warp, lane, wpre);
   pdl_wait();  // the activations (and y for the residual add) come from earlier kernels
+#if MCPO_TRACE
   if (threadIdx.x == 0) trace_stamp(tr, 1);
-  gemv_build_x(a, smem, NC, warp, lane, wpre);
+#endif
+  gemv_build_x<kTp>(a, smem, NC, warp, lane, wpre);
   asm volatile("bar.sync 1, %0;" ::"r"(NC * 32) : "memory");
+#if MCPO_TRACE
   if (threadIdx.x == 0) trace_stamp(tr, 2);
-  if (!a.pdl_early && threadIdx.x == 0) pdl_launch_dependents();
+#endif
+  if (threadIdx.x == 0) pdl_launch_dependents();
   const XShared x = gemv_x_view(smem, cols);
   int n = 0;
   float* stage = a.q8_out ? reinterpret_cast<float*>(empty + NC * S) : nullptr;
-  gemv_items<kClass, kDots>(a, x, ring, full, empty, S, slot, wr0, nwr, NC, warp, lane, n, nullptr, stage, blk0 * 32,
-                            a.self_issue ? &issued : nullptr);
-  if (a.self_issue && lane == 0) {
-    // copies issued but not consumed (a wait gave up) land before the CTA
-    // leaves; each wait is bounded
-    for (int m = n; m < issued; ++m)
-      if (!mbar_wait(&full[warp * S + m % S], (uint32_t)(m / S) & 1u, a.err)) break;
-  }
-  if (a.seg[0].epi == kEpiTpPush) {
-    // every consumer's remote stores are visible system-wide before the
-    // arrival counts say so (tp_proto.h)
-    __threadfence_system();
-    asm volatile("bar.sync 1, %0;" ::"r"(NC * 32) : "memory");
-    const GemvSeg& s0 = a.seg[0];
-    const int r0 = wr0 * s0.rpw, r1 = min((wr0 + nwr) * s0.rpw, s0.rows);
-    if (threadIdx.x == 0 && r1 > r0)
-      for (int d = 0; d < a.tp.world; ++d)
-        asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(a.tp.dst_arrive[d]), "r"((unsigned)(r1 - r0))
-                     : "memory");
+  gemv_items<kClass, kDots, kTp>(a, x, ring, full, empty, S, slot, wr0, nwr, NC, warp, lane, n, nullptr, stage,
+                                 blk0 * 32);
+  if constexpr (kTp) {
+    if (a.seg[0].epi == kEpiTpPush) {
+      // every consumer's remote stores are visible system-wide before the
+      // arrival counts say so (tp_proto.h)
+      __threadfence_system();
+      asm volatile("bar.sync 1, %0;" ::"r"(NC * 32) : "memory");
+      const GemvSeg& s0 = a.seg[0];
+      const int r0 = wr0 * s0.rpw, r1 = min((wr0 + nwr) * s0.rpw, s0.rows);
+      if (threadIdx.x == 0 && r1 > r0)
+        for (int d = 0; d < a.tp.world; ++d)
+          asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(a.tp.dst_arrive[d]),
+                       "r"((unsigned)(r1 - r0))
+                       : "memory");
+    }
   }
   if (a.q8_out) {
     // every consumer warp arrives here once (also after a wait gave up)
@@ -195,10 +178,12 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1) k_gemv(const Gemv
       quant_block_warp(r < rows ? stage[b * 32 + lane] : 0.0f, a.q8_out + (size_t)(blk0 + b) * 36, lane);
     }
   }
+#if MCPO_TRACE
   if (tr) {
     asm volatile("bar.sync 1, %0;" ::"r"(NC * 32) : "memory");
     if (threadIdx.x == 0) trace_stamp(tr, 3);
   }
+#endif
 }
 
 // The same GEMV over a.nvec (2..kGemvMaxVec) input vectors: one x region per
@@ -255,7 +240,7 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1) k_gemv_multi(cons
     GemvArgs av = a;
     av.xf = a.xf ? a.xf + (size_t)v * a.x_stride : nullptr;
     av.xq = a.xq ? a.xq + (size_t)v * a.xq_stride : nullptr;
-    gemv_build_x(av, smem + (size_t)v * xb, NC, warp, lane);
+    gemv_build_x<false>(av, smem + (size_t)v * xb, NC, warp, lane);
     asm volatile("bar.sync 1, %0;" ::"r"(NC * 32) : "memory");
   }
   for (int v = 0; v < kGemvMaxVec; ++v) xv[v] = gemv_x_view(smem + (size_t)(v < nvec ? v : 0) * xb, cols);
@@ -362,18 +347,14 @@ int consumers_cfg() {
   static const int v = env_int("MCPO_GEMV_CONSUMERS", 16);
   return v;
 }
-int early_cfg() {
-  static const int v = env_int("MCPO_GEMV_EARLY", 0);
-  return v;
-}
-int self_issue_cfg() {
-  static const int v = env_int("MCPO_GEMV_SELF", 0);
-  return v;
-}
+
 
 template <int kClass, bool kDots>
 cudaError_t set_smem_attr() {
-  cudaError_t e = cudaFuncSetAttribute(k_gemv<kClass, kDots>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  cudaError_t e = cudaFuncSetAttribute(k_gemv<kClass, kDots, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       227 * 1024);
+  if (e == cudaSuccess && !kDots)
+    e = cudaFuncSetAttribute(k_gemv<kClass, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
   if (e == cudaSuccess && !kDots)
     e = cudaFuncSetAttribute(k_gemv_multi<kClass>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
   return e;
@@ -383,8 +364,10 @@ template <int kClass>
 cudaError_t launch_class(const GemvArgs& a, int grid, int nc, size_t smem, cudaStream_t st, bool pdl) {
   const dim3 block((nc + 1) * 32);
   if (a.nvec > 1) return launch_k(k_gemv_multi<kClass>, dim3(grid), block, smem, st, pdl, a);
-  if (a.dots) return launch_k(k_gemv<kClass, true>, dim3(grid), block, smem, st, pdl, a);
-  return launch_k(k_gemv<kClass, false>, dim3(grid), block, smem, st, pdl, a);
+  if (a.dots) return launch_k(k_gemv<kClass, true, false>, dim3(grid), block, smem, st, pdl, a);
+  if (a.input == kInRmsNormTp || a.seg[0].epi == kEpiTpPush)
+    return launch_k(k_gemv<kClass, false, true>, dim3(grid), block, smem, st, pdl, a);
+  return launch_k(k_gemv<kClass, false, false>, dim3(grid), block, smem, st, pdl, a);
 }
 }  // namespace
 
@@ -438,8 +421,7 @@ cudaError_t launch_gemv(GemvArgs& a, int grid, cudaStream_t st, bool pdl) {
   const int wr = a.total_wr, slot = a.slot_bytes;
   const int stages = stages_cfg() < 1 ? 1 : stages_cfg();
   a.stages = stages;
-  a.pdl_early = pdl && early_cfg() ? 1 : 0;
-  a.self_issue = self_issue_cfg() && a.nvec <= 1 ? 1 : 0;
+
   if (wr == 0) return cudaSuccess;
   if (a.nvec > kGemvMaxVec || (a.nvec > 1 && a.dots)) return cudaErrorInvalidValue;
   const size_t xb = a.nvec > 1 ? gemv_x_bytes(a.cols) * (size_t)a.nvec : gemv_x_region(a.cols, a.input);

@@ -6,8 +6,13 @@
 #include <stdint.h>
 
 #include "layout.cuh"
-#include "prefetch.cuh"
 #include "tp.cuh"
+
+// Kernel timelines (trace fields below) are compiled in only when the
+// library is built with MCPO_TRACE=1 (make TRACE=1).
+#ifndef MCPO_TRACE
+#define MCPO_TRACE 0
+#endif
 
 namespace mcpo {
 
@@ -75,25 +80,11 @@ struct GemvArgs {
   // (36 B per 32 rows, the bits k_quantize_q8_1 gives for y), each CTA
   // taking whole 32-row blocks; a following GEMV reads them as kInQ8_1
   uint8_t* q8_out;
-  // weight bytes of later kernels to prefetch into L2 (idle producer lanes
-  // issue them at the start; n = 0: none)
-  PfList pf;
   // kEpiTpPush / kInRmsNormTp: the exchange produced or consumed
   TpXchg tp;
-  // 1: allow the next kernel to launch as soon as this one starts (its CTAs
-  // then stream their weights while this kernel runs, where both fit an SM)
-  int pdl_early;
-  // 1: each consumer warp issues its own ring copies (the producer warp idles)
-  int self_issue;
-  // optional: a layer's K and V cache rows [0, *kv_pos] prefetched into L2 at
-  // the start (for the attention that follows); row_bytes per position
-  const uint8_t* kv_k;
-  const uint8_t* kv_v;
-  const int* kv_pos;
-  int kv_row_bytes;
-  int kv_ctx;  // positions in the cache (a position outside [0, kv_ctx) prefetches nothing)
-  // optional timeline, [CTA][8] globaltimer ns: start, past the wait for the
-  // previous kernel, activations ready, all consumer warps done (4 unused)
+  // optional timeline (builds with MCPO_TRACE=1), [CTA][8] globaltimer ns:
+  // start, past the wait for the previous kernel, activations ready, all
+  // consumer warps done (4 unused)
   unsigned long long* trace;
 };
 

@@ -423,7 +423,9 @@ __device__ __forceinline__ void gemv_norm_weights(const GemvArgs& a, int warp, i
   for (int i = 0; i < 8; ++i) wv[i] = on ? load_weight(a.norm_w, a.norm_dtype, b * 32 + (lane & 3) * 8 + i) : 0.0f;
 }
 
-// wpre: the weights gemv_norm_weights gave (null: loaded here).
+// wpre: the weights gemv_norm_weights gave (null: loaded here).  kTp: the
+// input may be the tensor-parallel sum (kInRmsNormTp).
+template <bool kTp = false>
 __device__ __forceinline__ void gemv_build_x(const GemvArgs& a, uint8_t* xbase, int NC, int warp, int lane,
                                              const float* wpre = nullptr) {
   const int cols = a.cols;
@@ -464,12 +466,14 @@ __device__ __forceinline__ void gemv_build_x(const GemvArgs& a, uint8_t* xbase, 
     // before it is quantised.  Arithmetic per element as q8_1_quant_lane.
     // The tensor-parallel input is first summed into shared memory.
     const float* xf = a.xf;
-    if (a.input == kInRmsNormTp) {
-      float* sx = reinterpret_cast<float*>(xbase + gemv_x_bytes(cols));
-      gemv_tp_sum(a, sx, tid, NC * 32);
-      xf = sx;
+    if constexpr (kTp) {
+      if (a.input == kInRmsNormTp) {
+        float* sx = reinterpret_cast<float*>(xbase + gemv_x_bytes(cols));
+        gemv_tp_sum(a, sx, tid, NC * 32);
+        xf = sx;
+      }
     }
-    const bool norm = a.input == kInRmsNorm || a.input == kInRmsNormTp;
+    const bool norm = a.input == kInRmsNorm || (kTp && a.input == kInRmsNormTp);
     const void* nw = a.norm_w;
     const int ndt = a.norm_dtype;
     const float eps = a.eps;
@@ -577,42 +581,18 @@ __device__ __forceinline__ XShared gemv_x_view(uint8_t* xbase, int cols) {
                  cols / 256};
 }
 
-// Self-issued rings: consumer warp `warp` (lane 0) issues its own step
-// block n into slot n % S -- the copy the producer warp would issue -- once
-// the warp has finished with the block that slot held.
-__device__ __forceinline__ void fence_proxy_async_cta() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-
-// Copies step block n of this warp's sequence into its ring; false when the
-// warp has fewer than n + 1 step blocks.
-__device__ __forceinline__ bool gemv_issue_step(const GemvArgs& a, uint8_t* ring, uint64_t* full, int S, int slot,
-                                                int wr0, int nwr, int NC, int warp, int n, uint64_t policy) {
-  const int ks = a.seg[0].ks;
-  const int spi = ks * (a.seg[0].epi == kEpiSwiglu ? 2 : 1);
-  const int items = nwr > warp ? (nwr - warp + NC - 1) / NC : 0;
-  if (n >= items * spi) return false;
-  const int item = n / spi, rem = n % spi, part = rem / ks, k = rem % ks;
-  const int wr = wr0 + warp + NC * item;
-  const GemvSeg& sg = seg_of(a, wr);
-  const uint8_t* src = (part ? sg.w2 : sg.w) + (size_t)(wr - sg.wr_begin) * sg.wr_bytes + (size_t)k * sg.step_bytes;
-  const int sidx = n % S;
-  mbar_arrive_expect_tx(&full[warp * S + sidx], (uint32_t)sg.step_bytes);
-  bulk_load_hint(ring + (size_t)(warp * S + sidx) * slot, src, (uint32_t)sg.step_bytes, &full[warp * S + sidx], policy);
-  return true;
-}
-
 // The consumer loop of one GEMV over warp-rows [wr0, wr0 + nwr) of a CTA:
 // warp `warp` of NC takes items warp, warp + NC, ...; its step blocks arrive
 // in order in its ring (S slots of `slot` bytes; full/empty mbarriers), n
 // counting the blocks this warp has consumed so far.  Returns false when a
 // wait gave up (error raised) or *abort was set.
-// With self_issue the warp refills its own ring (no producer warp, empty
-// barriers unused): *issued counts the copies it has issued so far.
-template <int kClass, bool kDots>
+// kTp: outputs of a push epilogue (kEpiTpPush) go to every rank's exchange
+// slot instead of y.
+template <int kClass, bool kDots, bool kTp = false>
 __device__ __forceinline__ bool gemv_items(const GemvArgs& a, const XShared& x, uint8_t* ring, uint64_t* full,
                                            uint64_t* empty, int S, int slot, int wr0, int nwr, int NC, int warp,
                                            int lane, int& n, const volatile int* abort, float* stage = nullptr,
-                                           int stage_r0 = 0, int* issued = nullptr) {
-  const uint64_t policy = issued ? l2_evict_first_policy() : 0;
+                                           int stage_r0 = 0) {
   const int cols = a.cols;
   const bool swiglu = a.seg[0].epi == kEpiSwiglu;
   const int ks = a.seg[0].ks;
@@ -640,15 +620,7 @@ __device__ __forceinline__ bool gemv_items(const GemvArgs& a, const XShared& x, 
             step_value<kClass, kDots>(s.dtype, blk, lane, x, k * s.lpr + lane_in_row, part == 0 ? dots : nullptr);
         acc[part] = __fadd_rn(acc[part], v);
         __syncwarp();
-        if (issued) {
-          // the slot's reads are done: its next block (n + S) goes in
-          if (lane == 0) {
-            fence_proxy_async_cta();
-            if (gemv_issue_step(a, ring, full, S, slot, wr0, nwr, NC, warp, n + S, policy)) *issued = n + S + 1;
-          }
-        } else if (lane == 0) {
-          mbar_arrive(&empty[warp * S + sidx]);
-        }
+        if (lane == 0) mbar_arrive(&empty[warp * S + sidx]);
       }
     }
     const float g = reduce_row(acc[0], s.lpr);
@@ -656,8 +628,13 @@ __device__ __forceinline__ bool gemv_items(const GemvArgs& a, const XShared& x, 
     const float u = swiglu ? reduce_row(acc[1], s.lpr) : 0.0f;
     if (lane_in_row == 0 && row < s.rows) {
       const float out = swiglu ? silu_mul_det(g, u) : add ? __fadd_rn(yold, g) : g;
-      if (s.epi == kEpiTpPush) {
-        for (int d = 0; d < a.tp.world; ++d) a.tp.dst[d][row] = out;  // this rank's slot on every rank
+      if constexpr (kTp) {
+        if (s.epi == kEpiTpPush) {
+          for (int d = 0; d < a.tp.world; ++d) a.tp.dst[d][row] = out;  // this rank's slot on every rank
+        } else {
+          s.y[row] = out;
+          if (stage) stage[row - stage_r0] = out;
+        }
       } else {
         s.y[row] = out;
         if (stage) stage[row - stage_r0] = out;

@@ -514,10 +514,9 @@ void free_model(Model* m) {
 // dense ones the f32 input x.
 // With xq == nullptr a quantised GEMV quantises x itself (kInF32).
 cudaError_t model_mv(Ctx* c, Upload* w, const float* x, const uint8_t* xq, float* y, int epi, float* tmp, int grid,
-                     int* err, const PfList* pf = nullptr, unsigned long long* trace = nullptr) {
+                     int* err, unsigned long long* trace = nullptr) {
   if (w->tiled) {
     GemvArgs a{};
-    if (pf) a.pf = *pf;
     a.trace = trace;
     a.nseg = 1;
     a.cols = (int)w->cols;
@@ -593,78 +592,6 @@ void norm_input(GemvArgs* a, const float* x, const Upload* norm, float eps) {
   a->eps = eps;
 }
 
-// Bytes a GEMV streams from a weight upload.
-size_t stream_bytes(const Upload* u) { return u->tiled ? (size_t)u->geom.n_wr * u->geom.wr_bytes : u->dev_bytes; }
-
-// L2 prefetch windows of the decode step: MCPO_PF_MB megabytes ahead of a
-// GEMV's own weights (issued once its own copies are), MCPO_PF_ATTN_MB ahead
-// of the attention (which streams no weights); 0 turns prefetching off.
-size_t pf_window_cfg() {
-  static const size_t v = [] {
-    const char* e = getenv("MCPO_PF_MB");
-    return (size_t)((e && *e) ? atoi(e) : 0) << 20;
-  }();
-  return v;
-}
-// 1 (MCPO_KV_PF=1): the q/k/v GEMV prefetches its layer's K/V rows into L2.
-int kv_prefetch_cfg() {
-  static const int v = [] {
-    const char* e = getenv("MCPO_KV_PF");
-    return (e && *e) ? atoi(e) : 0;
-  }();
-  return v;
-}
-
-size_t pf_attn_window_cfg() {
-  static const size_t v = [] {
-    const char* e = getenv("MCPO_PF_ATTN_MB");
-    return (size_t)((e && *e) ? atoi(e) : 0) << 20;
-  }();
-  return v;
-}
-
-// Plans the L2 prefetches of one decode step.  The step's weights in the
-// order the kernels stream them (per layer q, k, v, o, gate, up, down; then
-// the lm_head) form one byte stream; a kernel whose own weights end at
-// stream offset `end` prefetches the bytes from the frontier (where earlier
-// kernels' windows stopped) up to end + window, so HBM keeps streaming up
-// to `window` bytes ahead of consumption while the dependency chain runs.
-struct PfPlanner {
-  std::vector<PfRange> stream;
-  std::vector<unsigned long long> start;
-  unsigned long long total = 0, frontier = 0, window = 0;
-  void add(const Upload* u) {
-    if (!u || !u->dev) return;
-    const unsigned long long b = stream_bytes(u) & ~15ull;
-    if (b == 0 || (reinterpret_cast<uintptr_t>(u->dev) & 15)) return;
-    stream.push_back(PfRange{u->dev, b});
-    start.push_back(total);
-    total += b;
-  }
-  // the stream offset just after upload u (0 when u is not in the stream)
-  unsigned long long end_of(const Upload* u) const {
-    for (size_t i = 0; i < stream.size(); ++i)
-      if (stream[i].p == u->dev) return start[i] + stream[i].bytes;
-    return 0;
-  }
-  PfList next(unsigned long long end) { return next(end, window); }
-  PfList next(unsigned long long end, unsigned long long win) {
-    PfList l{};
-    if (win == 0 || stream.empty()) return l;
-    const unsigned long long lo = frontier > end ? frontier : end;
-    const unsigned long long hi = end + win < total ? end + win : total;
-    for (size_t i = 0; i < stream.size() && lo < hi; ++i) {
-      const unsigned long long a = start[i], b = start[i] + stream[i].bytes;
-      const unsigned long long x = lo > a ? lo : a, y = hi < b ? hi : b;
-      if (x >= y) continue;
-      if (l.n == kMaxPf) break;
-      l.r[l.n++] = PfRange{stream[i].p + (x - a), y - x};
-      frontier = y;
-    }
-    return l;
-  }
-};
-
 #define REC(expr)                            \
   do {                                       \
     cudaError_t e_ = (expr);                 \
@@ -709,21 +636,10 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
                         m.am_grid, s, true));
     return cudaSuccess;
   }
-  PfPlanner pf;
-  pf.window = pf_window_cfg();
-  const unsigned long long pf_attn = pf_attn_window_cfg();
-  if (pf.window || pf_attn) {
-    for (uint32_t li = 0; li < cf.layers; ++li) {
-      const LayerW& L = m.layer[li];
-      for (const Upload* u : {L.q, L.k, L.v, L.o, L.gate, L.up, L.down}) pf.add(u);
-    }
-    if (logits) pf.add(m.out);
-  }
   for (uint32_t li = 0; li < cf.layers; ++li) {
     const LayerW& L = m.layer[li];
     // attention block: RMSNorm -> Q8_1 inside the q/k/v GEMV's prologue
     Upload* qkv[3] = {L.q, L.k, L.v};
-    const unsigned long long qkv_end = pf.stream.empty() ? 0 : pf.end_of(L.v);
     if (groupable(qkv, 3)) {
       GemvArgs a{};
       a.nseg = 3;
@@ -736,16 +652,7 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
       a.err = &m.st->err;
       float* ys[3] = {m.q, m.k, m.v};
       for (int i = 0; i < 3; ++i) gemv_seg_from_geom(qkv[i]->geom, qkv[i]->dev, nullptr, ys[i], kEpiStore, &a.seg[i]);
-      a.pf = pf.next(qkv_end);
       a.trace = trace_next();
-      if (kv_prefetch_cfg()) {
-        const size_t esz = cf.kv_f16 ? 2 : 4;
-        a.kv_k = (const uint8_t*)m.kc + li * m.kv_layer_elems * esz;
-        a.kv_v = (const uint8_t*)m.vc + li * m.kv_layer_elems * esz;
-        a.kv_pos = &m.st->pos;
-        a.kv_row_bytes = (int)(m.kvd * esz);
-        a.kv_ctx = (int)cf.context;
-      }
       REC(launch_gemv(a, m.grid_h, s, true));
     } else {
       REC(launch_rmsnorm_q8_1(m.hidden, L.attn_norm->dev, L.attn_norm->dtype, h, cf.rms_eps, m.normed, m.xq, s, true));
@@ -783,7 +690,6 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
     a.out = m.attn;
     a.out_q8 = (L.o->tiled && hd % 32 == 0) ? m.aq : nullptr;
     a.err = &m.st->err;
-    a.pf = pf.next(qkv_end, pf_attn);
     a.trace = trace_next();
     REC(launch_attention(a, s, true));
     // (head_dim % 32 != 0: the o GEMV quantises the f32 attention output itself)
@@ -800,8 +706,7 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
       o.trace = trace_next();
       REC(launch_gemv(o, m.grid_q, s, true));
     } else {
-      const PfList opf = pf.next(pf.stream.empty() ? 0 : pf.end_of(L.o));
-      REC(model_mv(c, L.o, m.attn, a.out_q8, m.hidden, kEpiAdd, m.tmp, m.grid_q, &m.st->err, &opf, trace_next()));
+      REC(model_mv(c, L.o, m.attn, a.out_q8, m.hidden, kEpiAdd, m.tmp, m.grid_q, &m.st->err, trace_next()));
     }
     // feed-forward block: RMSNorm -> Q8_1 inside the gate/up GEMV, SwiGLU in
     // its epilogue, which also writes the Q8_1 blocks the down GEMV reads
@@ -820,7 +725,6 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
       gemv_seg_from_geom(L.gate->geom, L.gate->dev, L.up->dev, m.fused, kEpiSwiglu, &g.seg[0]);
       if (!tp && L.down->tiled && ffn_q8_cfg()) g.q8_out = m.fq;
       down_q8 = g.q8_out;
-      g.pf = pf.next(pf.stream.empty() ? 0 : pf.end_of(L.up));
       g.trace = trace_next();
       REC(launch_gemv(g, m.grid_h, s, true));
     } else {
@@ -841,8 +745,7 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
       d.trace = trace_next();
       REC(launch_gemv(d, m.grid_f, s, true));
     } else {
-      const PfList dpf = pf.next(pf.stream.empty() ? 0 : pf.end_of(L.down));
-      REC(model_mv(c, L.down, m.fused, down_q8, m.hidden, kEpiAdd, m.tmp, m.grid_f, &m.st->err, &dpf, trace_next()));
+      REC(model_mv(c, L.down, m.fused, down_q8, m.hidden, kEpiAdd, m.tmp, m.grid_f, &m.st->err, trace_next()));
     }
   }
   if (tp && !logits)  // the last exchange still completes the residual stream (hidden_out)
@@ -1556,7 +1459,7 @@ int bind_model(Ctx* c, const minicpmo_qwen3_config* cfg, char* err, size_t cap, 
   m.n_split = attn_n_split((int)lc.kv_heads);
   {
     const char* gt = getenv("MCPO_GRAPH_TRACE");
-    if (gt && gt[0] == '1') {
+    if (MCPO_TRACE && gt && gt[0] == '1') {
       m.trace_launches = 5 * (int)lc.layers + 1;
       m.trace_ctas = std::max(c->sm_count, (int)lc.kv_heads * m.n_split);
       const size_t tb = (size_t)m.trace_launches * m.trace_ctas * 8 * 8;

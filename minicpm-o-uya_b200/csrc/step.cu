@@ -549,7 +549,7 @@ __global__ void __launch_bounds__((kStepMaxConsumers + 1) * 32, 1) k_decode_step
     const StageDesc& sd = sdesc[si & 1];
     if (sd.kind == kStageGemv) {
       const GemvArgs& g = sd.g;
-      gemv_build_x(g, ubase, NC, warp, lane);
+      gemv_build_x<false>(g, ubase, NC, warp, lane);
       cbar(nthr);
       if (threadIdx.x == 0) *reinterpret_cast<volatile int*>(&open_s) = si;
       if (p.trace && threadIdx.x == 0) p.trace[((size_t)si * G + b) * 3 + 1] = globaltimer_ns();

@@ -119,6 +119,12 @@ __device__ __forceinline__ void bulk_load_hint(void* dst, const void* src, uint3
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+// Kernel timelines are compiled in only with MCPO_TRACE=1 (a diagnostic
+// build): even untaken stamp code slows the GEMV's hot loop measurably.
+#ifndef MCPO_TRACE
+#define MCPO_TRACE 0
+#endif
+
 // globaltimer (ns) into t[i] when a timeline is being recorded.
 __device__ __forceinline__ void trace_stamp(unsigned long long* t, int i) {
   if (t) {
