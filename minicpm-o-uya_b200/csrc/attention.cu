@@ -754,6 +754,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2)
         put_pos_row<TT>(buf, s_kpos, s_vpos, (split + S * i) * kSub, pos, fused, hd);
         zero_rows<TT>(buf, (split + S * i) * kSub, n_pos, hd);
       }
+#if MCPO_TRACE
+      if (r == 0 && threadIdx.x == 0) trace_stamp(tr, 6);  // the first round's tiles have landed
+#endif
     } else {
       for (int j = 0; j < bpr; ++j) {
         const int i = r * bpr + j;

@@ -51,9 +51,9 @@ struct AttnArgs {
   int pos_stride;  // ints between sequences' positions at pos_ptr (0: 1)
   int* err;        // raised by a bounded wait that gave up (may be null)
   // optional timeline (builds with MCPO_TRACE=1), [CTA (x fastest, then y,
-  // z)][8] globaltimer ns: start,
-  // past the wait for the previous kernel, the round of blocks begun, done,
-  // blocks done, past the cluster barrier (3 unused)
+  // z)][8] globaltimer ns: start, past the wait for the previous kernel, the
+  // round of blocks begun, done, blocks done, past the cluster barrier, the
+  // first round's tiles landed (1 unused)
   unsigned long long* trace;
 };
 
