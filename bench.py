@@ -487,7 +487,8 @@ def main() -> int:
     ap.add_argument("--layers", type=int, default=0,
                     help="override the layer count (smaller cases of the same shape, for profiler captures)")
     ap.add_argument("--decode-mode", type=int, default=0,
-                    help="0: the library default; 1: one kernel per operation; 2: one persistent kernel per step")
+                    help="0: the library default; 1: one kernel per operation; 2: one persistent kernel per step; "
+                         "3: per layer the attention and one chained GEMV launch")
     ap.add_argument("--batch", type=int, default=0,
                     help="BASELINE config 3: batched decode of this many sequences (2..32), all-Q8_0 weights on the "
                          "tensor cores, f16 KV, prompt 1024 unless --prompt is given")
@@ -684,7 +685,7 @@ def main() -> int:
                      "traffic": traffic, "peak_kind": peak_kind, "kernel": dom_desc,
                      "algorithmic_bytes_per_launch": step_bytes if persistent else dom["bytes"],
                      "gemv_sweep": shapes},
-        "decode_mode": "persistent" if persistent else "per-kernel",
+        "decode_mode": "persistent" if persistent else ("chained" if kernels == 4 + 2 * shape.layers else "per-kernel"),
         "clocks": clk,
     }
     if rank == 0 and world == 1 and args.cpu_sample > 0:

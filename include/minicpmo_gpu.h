@@ -167,7 +167,11 @@ typedef struct minicpmo_qwen3_config {
                                1: one kernel per operation (a CUDA graph of ~5 per
                                layer); 2: one persistent kernel per decode step when
                                the model fits it (all linear weights Q4_K/Q6_K, or
-                               all Q8_0), else 1.  Same results in every mode. */
+                               all Q8_0), else 1; 3: per layer the attention and one
+                               launch chaining the o, gate/up, down and next q/k/v
+                               GEMVs (one GPU, tiled weights, head_dim % 32 == 0;
+                               the bind fails otherwise).  Same results in every
+                               mode. */
     int reserved[5];
 } minicpmo_qwen3_config;
 

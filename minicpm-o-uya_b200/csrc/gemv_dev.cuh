@@ -151,6 +151,24 @@ __device__ __forceinline__ float sb_dot_q80(const uint4* c, const XShared& x, in
 }
 
 
+// One warp per 32-value block; writes the reference's 36-byte block with the
+// sequential f16 sum s (gpu_shim.c:343-378).
+__device__ __forceinline__ void quant_block_warp(float v, uint8_t* dst, int lane) {
+  uint16_t dbits;
+  bool zero;
+  const int q = q8_1_quant_lane(v, &dbits, &zero);
+  const float s = warp_seq_sum(v);
+  const uint16_t sbits = zero ? (uint16_t)0 : f32_to_f16_ref(s);
+  // pack 4 quants per lane group into words
+  const uint32_t qb = (uint32_t)(q & 0xff);
+  uint32_t word = qb << (8 * (lane & 3));
+  word |= __shfl_xor_sync(0xffffffffu, word, 1);
+  word |= __shfl_xor_sync(0xffffffffu, word, 2);
+  uint32_t* o = reinterpret_cast<uint32_t*>(dst);
+  if (lane == 0) o[0] = (uint32_t)dbits | ((uint32_t)sbits << 16);
+  if ((lane & 3) == 0) o[1 + (lane >> 2)] = word;
+}
+
 // Kernel instantiations by the dtypes they can meet (smaller code per kernel).
 enum GemvClass : int { kClassQ4K = 0, kClassQ6K = 1, kClassQ80 = 2, kClassQ4K6K = 3 };
 

@@ -19,6 +19,7 @@
 #include <vector>
 
 #include "attention.cuh"
+#include "chain.cuh"
 #include "step.cuh"
 #include "tp.cuh"
 #include "gemm.cuh"
@@ -117,6 +118,14 @@ struct Model {
   cudaGraphExec_t exec[2] = {nullptr, nullptr};
   int kernels[2] = {0, 0};  // kernel launches recorded in each graph
   int* rec_count = nullptr;
+  // GEMV chains (decode_mode 3): per layer one launch of o, gate/up, down and
+  // the next layer's q/k/v (the last layer's: the lm_head, or nothing)
+  bool chain_ok = false;
+  GemvArgs* chain_stages = nullptr;      // device: [layers + 1][kMaxChain]
+  std::vector<GemvChain> chains;         // [layers] with the lm_head, then the last layer's without
+  std::vector<size_t> chain_smem;
+  unsigned* chain_bar = nullptr;         // [layers][kMaxChain - 1] barrier counters, then the abort word
+  size_t chain_bar_bytes = 0;
   // persistent step kernel (decode_mode 0 when the model fits it)
   bool step_ok = false;
   bool step_q80 = false;
@@ -496,7 +505,7 @@ void free_model(Model* m) {
   void* bufs[] = {m->hidden, m->normed, m->q,     m->k,       m->v,         m->attn,       m->gate,     m->up,
                   m->fused,  m->tmp,    m->logits, m->xq,     m->aq,        m->fq,         m->kc,       m->vc,
                   m->rope_cos, m->rope_sin, m->partial, m->counters, m->am_scratch, m->am_counter, m->st, m->seen,
-                  m->history, m->stages, m->step_scratch, m->step_trace, m->graph_trace, m->tp_epoch, m->tp_step, m->hidden2, m->embed_in,
+                  m->history, m->stages, m->step_scratch, m->step_trace, m->graph_trace, m->chain_stages, m->chain_bar, m->tp_epoch, m->tp_step, m->hidden2, m->embed_in,
                   m->smp_seen, m->smp_io, m->smp_bits, m->smp_st, m->pf_hidden, m->pf_q, m->pf_k, m->pf_v,
                   m->pf_attn, m->pf_fused, m->pf_partial, m->pf_tok, m->pf_pos, m->pf_counters,
                   m->pf_err};
@@ -624,6 +633,10 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
     if (!m.graph_trace || traced >= m.trace_launches) return nullptr;
     return m.graph_trace + (size_t)(traced++) * m.trace_ctas * 8;
   };
+  if (m.chain_ok) {
+    cudaError_t e = cudaMemsetAsync(m.chain_bar, 0, m.chain_bar_bytes, s);
+    if (e != cudaSuccess) return e;
+  }
   if (m.step_ok) {
     // the whole layer chain (and the lm_head) as one persistent kernel
     cudaError_t e = cudaMemsetAsync(m.step_scratch, 0, m.step_scratch_bytes, s);
@@ -640,7 +653,9 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
     const LayerW& L = m.layer[li];
     // attention block: RMSNorm -> Q8_1 inside the q/k/v GEMV's prologue
     Upload* qkv[3] = {L.q, L.k, L.v};
-    if (groupable(qkv, 3)) {
+    if (m.chain_ok && li > 0) {
+      // layer li's q/k/v ran as the last stage of layer li-1's chain
+    } else if (groupable(qkv, 3)) {
       GemvArgs a{};
       a.nseg = 3;
       a.cols = h;
@@ -692,6 +707,11 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
     a.err = &m.st->err;
     a.trace = trace_next();
     REC(launch_attention(a, s, true));
+    if (m.chain_ok) {  // o, gate/up, down and the next layer's q/k/v (or the lm_head) as one launch
+      const size_t ci = (li + 1 == cf.layers && !logits) ? cf.layers : li;
+      REC(launch_gemv_chain(m.chains[ci], c->sm_count, m.chain_smem[ci], s));
+      continue;
+    }
     // (head_dim % 32 != 0: the o GEMV quantises the f32 attention output itself)
     if (tp) {  // row-parallel: this rank's partial pushed to every rank (exchange 2l)
       GemvArgs o{};
@@ -751,7 +771,9 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
   if (tp && !logits)  // the last exchange still completes the residual stream (hidden_out)
     REC(launch_tp_finalize(xchg(nx - 1, m.hidden), m.hidden2, &m.st->err, s));
   if (logits) {
-    if (m.out->tiled) {
+    if (m.chain_ok) {
+      // the lm_head ran as the last stage of the last layer's chain
+    } else if (m.out->tiled) {
       GemvArgs o{};
       o.nseg = 1;
       o.cols = h;
@@ -1171,6 +1193,101 @@ bool build_step_plan(Ctx* c, Model& m) {
   return true;
 }
 
+// The GEMV chains of decode_mode 3 (chain.cuh): needs every layer's q/k/v
+// groupable, a fused gate/up, tiled o/down/lm_head, head_dim % 32 == 0 (the
+// attention writes the o GEMV's Q8_1 input) and one GPU.
+bool build_chain_plan(Ctx* c, Model& m) {
+  const auto& cf = m.cfg;
+  const int h = (int)cf.hidden, L = (int)cf.layers;
+  if (m.tp_world > 1 || cf.head_dim % 32 || !m.out->tiled) return false;
+  for (int li = 0; li < L; ++li) {
+    const LayerW& Ly = m.layer[li];
+    Upload* qkv[3] = {Ly.q, Ly.k, Ly.v};
+    if (!groupable(qkv, 3) || !Ly.o->tiled || !Ly.down->tiled || !Ly.gate->tiled || !Ly.up->tiled ||
+        Ly.gate->dtype != Ly.up->dtype || Ly.gate->rows != Ly.up->rows)
+      return false;
+  }
+  auto qkv_args = [&](int li) {
+    const LayerW& Ly = m.layer[li];
+    GemvArgs a{};
+    a.nseg = 3;
+    a.cols = h;
+    norm_input(&a, m.hidden, Ly.attn_norm, cf.rms_eps);
+    a.err = &m.st->err;
+    Upload* qkv[3] = {Ly.q, Ly.k, Ly.v};
+    float* ys[3] = {m.q, m.k, m.v};
+    for (int i = 0; i < 3; ++i) gemv_seg_from_geom(qkv[i]->geom, qkv[i]->dev, nullptr, ys[i], kEpiStore, &a.seg[i]);
+    return a;
+  };
+  std::vector<GemvArgs> all((size_t)(L + 1) * kMaxChain);
+  std::vector<int> masks(all.size(), 0);
+  m.chains.assign((size_t)L + 1, GemvChain{});
+  m.chain_smem.assign((size_t)L + 1, 0);
+  for (int ci = 0; ci <= L; ++ci) {
+    const int li = ci < L ? ci : L - 1;  // chain L: the last layer without the lm_head
+    const LayerW& Ly = m.layer[li];
+    GemvArgs* st = &all[(size_t)ci * kMaxChain];
+    int* mk = &masks[(size_t)ci * kMaxChain];
+    int n = 0;
+    GemvArgs o{};
+    o.nseg = 1;
+    o.cols = (int)Ly.o->cols;
+    o.input = kInQ8_1;
+    o.xq = m.aq;
+    o.err = &m.st->err;
+    gemv_seg_from_geom(Ly.o->geom, Ly.o->dev, nullptr, m.hidden, kEpiAdd, &o.seg[0]);
+    st[n++] = o;
+    GemvArgs g{};
+    g.nseg = 1;
+    g.cols = h;
+    norm_input(&g, m.hidden, Ly.ffn_norm, cf.rms_eps);
+    g.err = &m.st->err;
+    gemv_seg_from_geom(Ly.gate->geom, Ly.gate->dev, Ly.up->dev, m.fused, kEpiSwiglu, &g.seg[0]);
+    g.q8_out = m.fq;
+    st[n++] = g;
+    GemvArgs d{};
+    d.nseg = 1;
+    d.cols = (int)Ly.down->cols;
+    d.input = kInQ8_1;
+    d.xq = m.fq;
+    d.err = &m.st->err;
+    gemv_seg_from_geom(Ly.down->geom, Ly.down->dev, nullptr, m.hidden, kEpiAdd, &d.seg[0]);
+    st[n++] = d;
+    if (ci < L - 1) {
+      st[n++] = qkv_args(li + 1);
+    } else if (ci == L - 1) {
+      GemvArgs lo{};
+      lo.nseg = 1;
+      lo.cols = h;
+      norm_input(&lo, m.hidden, m.out_norm, cf.rms_eps);
+      lo.err = &m.st->err;
+      gemv_seg_from_geom(m.out->geom, m.out->dev, nullptr, m.logits, kEpiStore, &lo.seg[0]);
+      st[n++] = lo;
+    }
+    for (int i = 0; i < n; ++i)
+      if (gemv_prepare(st[i], &mk[i]) != cudaSuccess) return false;
+    GemvChain ch{};
+    if (!chain_layout(st, mk, n, c->sm_count, &ch, &m.chain_smem[ci])) return false;
+    m.chains[ci] = ch;
+  }
+  m.chain_bar_bytes = ((size_t)(L + 1) * (kMaxChain - 1) + 1) * sizeof(unsigned);
+  if (cudaMalloc((void**)&m.chain_stages, all.size() * sizeof(GemvArgs)) != cudaSuccess ||
+      cudaMemcpy(m.chain_stages, all.data(), all.size() * sizeof(GemvArgs), cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMalloc((void**)&m.chain_bar, m.chain_bar_bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  int* abort = reinterpret_cast<int*>(m.chain_bar + (size_t)(L + 1) * (kMaxChain - 1));
+  for (int ci = 0; ci <= L; ++ci) {
+    GemvChain& ch = m.chains[ci];
+    ch.stages = m.chain_stages + (size_t)ci * kMaxChain;
+    ch.bar = m.chain_bar + (size_t)ci * (kMaxChain - 1);
+    ch.abort = abort;
+    ch.err = &m.st->err;
+  }
+  return true;
+}
+
 int build_graph(Ctx* c, Model& m, int which, char* err, size_t cap) {
   cudaGraph_t g = nullptr;
   if (!cuda_ok(c, cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal), "graph_begin_capture", err, cap))
@@ -1529,6 +1646,12 @@ int bind_model(Ctx* c, const minicpmo_qwen3_config* cfg, char* err, size_t cap, 
     free_model(&m);
     return 0;
   }
+  m.chain_ok = cf.decode_mode == 3 && build_chain_plan(c, m);
+  if (cf.decode_mode == 3 && !m.chain_ok) {
+    snprintf(err, cap, "qwen3_bind: decode_mode 3 needs one GPU, tiled grouped weights and head_dim %% 32 == 0");
+    free_model(&m);
+    return 0;
+  }
   m.step_ok = cf.decode_mode == 2 && m.tp_world == 1 && build_step_plan(c, m);
   if (m.step_ok && (!build_graph(c, m, 0, err, cap) || !build_graph(c, m, 1, err, cap))) {
     // the persistent kernel could not be captured: fall back to the
@@ -1606,6 +1729,7 @@ int minicpmo_gpu_context_create(unsigned int device_index, int debug, void** out
   if (!cuda_ok(c, gemv_init(), "gemv_init", error, error_cap) || !cuda_ok(c, gemm_init(), "gemm_init", error, error_cap) ||
       !cuda_ok(c, attention_init(), "attention_init", error, error_cap) ||
       !cuda_ok(c, decode_step_init(), "decode_step_init", error, error_cap) ||
+      !cuda_ok(c, chain_init(), "chain_init", error, error_cap) ||
       !cuda_ok(c, cudaMalloc((void**)&c->dev_err, sizeof(int)), "error_word_malloc", error, error_cap) ||
       !cuda_ok(c, cudaMemset(c->dev_err, 0, sizeof(int)), "error_word_memset", error, error_cap)) {
     if (c->dev_err) cudaFree(c->dev_err);

@@ -53,7 +53,8 @@ class Qwen3Runtime:
              tp: Optional["TensorParallel"] = None, max_batch: int = 0) -> "Qwen3Runtime":
         """weights: a GGUF path/GgufFile, or a list of (name, dtype, rows, cols, uint8 bytes).
         decode_mode 0: the default (one kernel per operation); 1: one kernel per operation; 2: one
-        persistent kernel per decode step where the model fits it (same results in every mode).
+        persistent kernel per decode step where the model fits it; 3: per layer the attention and one
+        launch chaining the o, gate/up, down and next q/k/v GEMVs (same results in every mode).
         tp: tensor parallelism over the ranks of one node (`TensorParallel`, one process per GPU);
         every rank opens with the same weights and drives the same tokens.
         max_batch 2..32: also bind the batched decode of that many independent sequences

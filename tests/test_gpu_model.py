@@ -203,6 +203,46 @@ def test_persistent_step_matches_per_kernel_graph(pkg, O, kv_f16):
 
 
 
+@pytest.mark.parametrize("mix,kv_f16", [("Q4_K_M", False), ("Q4_K_M", True), ("ALL_Q8_0", False)])
+def test_gemv_chain_matches_per_kernel_graph(pkg, O, mix, kv_f16):
+    """decode_mode 3 (per layer the attention plus one launch chaining the o,
+    gate/up, down and next q/k/v GEMVs through grid barriers) and decode_mode
+    1 give identical logits, tokens and gaps, with and without the logits
+    (the last layer's chain then ends after its down GEMV), and the same
+    device-side greedy loop."""
+    from minicpmo_b200 import gguf
+    from minicpmo_b200.qwen3 import Qwen3Runtime
+
+    shape = small_shape(layers=3, hidden=512, heads=32, kv_heads=8, head_dim=128, ffn=1024, vocab=1024, context=200)
+    tensors = build(pkg, shape, getattr(gguf, mix), seed=4)
+    rt3 = Qwen3Runtime.open(tensors, shape=shape, context=shape.context, kv_f16=kv_f16, decode_mode=3)
+    rt1 = Qwen3Runtime.open(tensors, shape=shape, context=shape.context, kv_f16=kv_f16, decode_mode=1)
+    # embed, seen-set, the first q/k/v, per layer attention + chain, sampler
+    assert rt3.gpu.qwen3_step_kernels(True) == 3 + 2 * shape.layers + 1
+    ids = gguf.prompt_ids(150, shape.vocab, seed=9)
+    l3 = np.empty(shape.vocab, np.float32)
+    l1 = np.empty(shape.vocab, np.float32)
+    for pos in range(150):
+        want = pos % 4 == 0 or pos > 140
+        t3, g3 = rt3.forward(int(ids[pos]), pos, logits=want, want_logits=l3)
+        t1, g1 = rt1.forward(int(ids[pos]), pos, logits=want, want_logits=l1)
+        if want:
+            assert np.array_equal(l3, l1), (pos, rel_row_err(l3, l1))
+            assert (t3, g3) == (t1, g1), pos
+    a = rt3.gpu.qwen3_decode(int(ids[0]), 150, 30)
+    b = rt1.gpu.qwen3_decode(int(ids[0]), 150, 30)
+    assert np.array_equal(a, b)
+    rt3.close()
+    rt1.close()
+
+
+def test_gemv_chain_vs_oracle(pkg, O):
+    """The chained step against the oracle in device order: bit-identical logits."""
+    from minicpmo_b200 import gguf
+
+    run_parity(pkg, O, small_shape(layers=3), gguf.Q4_K_M, steps=24, decode_mode=3)
+
+
 @pytest.mark.parametrize("mix", ["Q4_K_M", "ALL_Q8_0"])
 def test_persistent_step_vs_oracle(pkg, O, mix):
     """The persistent step kernel (both of its weight classes) against the
