@@ -510,8 +510,7 @@ __device__ __forceinline__ void write_unit(float o, int u, int lane, int hb, int
     uint32_t word = ((uint32_t)(q & 0xff)) << (8 * (lane & 3));
     word |= __shfl_xor_sync(0xffffffffu, word, 1);
     word |= __shfl_xor_sync(0xffffffffu, word, 2);
-    float sum = 0.0f;  // the sequential f16 s of the reference block
-    for (int t = 0; t < 32; ++t) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, o, t));
+    const float sum = warp_seq_sum(o);  // the sequential f16 s of the reference block
     uint32_t* ob = reinterpret_cast<uint32_t*>(oq8 + ((size_t)hb * hd / 32 + u) * 36);
     if (lane == 0) ob[0] = (uint32_t)dbits | ((uint32_t)(zero ? (uint16_t)0 : f32_to_f16_ref(sum)) << 16);
     if ((lane & 3) == 0) ob[1 + (lane >> 2)] = word;

@@ -2,8 +2,9 @@
 //
 // Synchronisation:
 //  * stage k+1 starts once every CTA has finished stage k: an arrival
-//    counter per barrier (zeroed before each launch), release by
-//    __threadfence + atomicAdd, acquire by ld.acquire polling; the wait is
+//    counter per barrier (zeroed before each launch), release by a CTA
+//    barrier then thread 0's red.release, acquire by thread 0's
+//    ld.acquire polling then a CTA barrier; the wait is
 //    bounded (1 s of globaltimer), after which the CTA raises the error word
 //    and the abort flag, and the other CTAs leave at their next barrier;
 //  * the producer warp waits for its consumers' free slots with bounded
@@ -25,8 +26,11 @@ namespace mcpo {
 namespace {
 
 constexpr size_t kChainSmemMax = 232448;  // opt-in shared memory per CTA on sm_100
-// Consumer warps at most (+1 producer warp), as the standalone GEMV.
-constexpr int kChainMaxConsumers = 16;
+// Consumer warps at most (+1 producer warp).  Sixteen do not fit beside a
+// 12288-column activation region and two 6.7 KB Q6_K slots per warp, and
+// 512 threads leave each thread 128 registers, which the stage loop needs
+// without spilling.
+constexpr int kChainMaxConsumers = 15;
 
 __device__ __forceinline__ unsigned ld_acquire_gpu_u32(const unsigned* p) {
   unsigned v;
@@ -60,11 +64,15 @@ __device__ __forceinline__ void chain_range(const GemvArgs& a, int b, int G, int
 
 // Barrier k over the grid, for the NC*32 consumer threads (named barrier
 // 1); false when this CTA is to leave (the wait gave up or another CTA did).
+// The CTA barrier orders every consumer's stores of the stage before thread
+// 0's release-add; thread 0's acquire polls, then the CTA barrier, order
+// the next stage's loads after every CTA's arrival (no full fence: a
+// sequentially consistent fence costs microseconds under the weight
+// stream).
 __device__ bool chain_grid_sync(const GemvChain& c, int k, int nthr, volatile int* abort_s) {
-  __threadfence();  // this thread's stores of the stage before the arrival
   asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
   if (threadIdx.x == 0 && !*abort_s) {
-    atomicAdd(c.bar + k, 1u);
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(c.bar + k) : "memory");
     const uint64_t t0 = chain_timer();
     for (unsigned it = 0;; ++it) {
       if (ld_acquire_gpu_u32(c.bar + k) >= gridDim.x) break;
@@ -79,7 +87,6 @@ __device__ bool chain_grid_sync(const GemvChain& c, int k, int nthr, volatile in
         break;
       }
     }
-    __threadfence();
   }
   asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
   return *abort_s == 0;
@@ -88,7 +95,7 @@ __device__ bool chain_grid_sync(const GemvChain& c, int k, int nthr, volatile in
 template <int kClass>
 __global__ void __launch_bounds__((kChainMaxConsumers + 1) * 32, 1) k_gemv_chain(const GemvChain c) {
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ GemvArgs sa;  // the consumers' current stage
+  __shared__ GemvArgs sa[kMaxChain];  // every stage's arguments (consumers)
   __shared__ int abort_s;
   const int NC = c.nc, S = c.S, slot = c.slot;
   uint8_t* xbase = smem;
@@ -145,42 +152,72 @@ __global__ void __launch_bounds__((kChainMaxConsumers + 1) * 32, 1) k_gemv_chain
     return;
   }
 
-  // ---- consumers: the stages in turn
+  // ---- consumers: the stages in turn.  Every stage's arguments are
+  // copied into shared memory once, while the previous kernel finishes.
   const int nthr = NC * 32, tid = threadIdx.x;
+  for (int st = 0; st < c.n; ++st) {
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(c.stages + st);
+    uint32_t* dst = reinterpret_cast<uint32_t*>(&sa[st]);
+    for (int i = tid; i < (int)(sizeof(GemvArgs) / 4); i += nthr) dst[i] = src[i];
+  }
+  asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
   int n = 0;
   for (int st = 0; st < c.n; ++st) {
-    if (st > 0 && !chain_grid_sync(c, st - 1, nthr, &abort_s)) break;
-    {
-      const uint32_t* src = reinterpret_cast<const uint32_t*>(c.stages + st);
-      uint32_t* dst = reinterpret_cast<uint32_t*>(&sa);
-      for (int i = tid; i < (int)(sizeof(GemvArgs) / 4); i += nthr) dst[i] = src[i];
+    const GemvArgs& a = sa[st];
+#if MCPO_TRACE
+    unsigned long long* tr = c.trace ? c.trace + ((size_t)(st / 2) * c.trace_ctas + b) * 8 + (st % 2) * 4 : nullptr;
+#endif
+    // the RMSNorm weights need nothing from earlier stages: loaded before
+    // the wait for them
+    float wpre[8];
+    gemv_norm_weights(a, warp, lane, wpre);
+    if (st == 0) {
+      pdl_wait();  // the first stage's activations come from the previous kernel
+    } else if (!chain_grid_sync(c, st - 1, nthr, &abort_s)) {
+      break;
     }
-    asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
-    if (st == 0) pdl_wait();  // the first stage's activations come from the previous kernel
+#if MCPO_TRACE
+    if (tid == 0) trace_stamp(tr, 0);
+#endif
     int wr0, nwr, blk0, nblk;
-    chain_range(sa, b, G, wr0, nwr, blk0, nblk);
-    gemv_build_x<false>(sa, xbase, NC, warp, lane, nullptr);
+    chain_range(a, b, G, wr0, nwr, blk0, nblk);
+    gemv_build_x<false>(a, xbase, NC, warp, lane, wpre);
     asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
-    const XShared x = gemv_x_view(xbase, sa.cols);
-    if (!gemv_items<kClass, false>(sa, x, ring, full, empty, S, slot, wr0, nwr, NC, warp, lane, n, nullptr,
-                                   sa.q8_out ? q8stage : nullptr, blk0 * 32)) {
+#if MCPO_TRACE
+    if (tid == 0) trace_stamp(tr, 1);
+#endif
+    const XShared x = gemv_x_view(xbase, a.cols);
+    if (!gemv_items<kClass, false>(a, x, ring, full, empty, S, slot, wr0, nwr, NC, warp, lane, n, nullptr,
+                                   a.q8_out ? q8stage : nullptr, blk0 * 32)) {
       atomicExch(c.abort, 1);
     }
-    if (sa.q8_out) {
+#if MCPO_TRACE
+    if (tr) {
       asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
-      const int rows = sa.seg[0].rows;
+      if (tid == 0) trace_stamp(tr, 2);
+    }
+#endif
+    if (a.q8_out) {
+      asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
+      const int rows = a.seg[0].rows;
       for (int bb = warp; bb < nblk; bb += NC) {
         const int r = (blk0 + bb) * 32 + lane;
-        quant_block_warp(r < rows ? q8stage[bb * 32 + lane] : 0.0f, sa.q8_out + (size_t)(blk0 + bb) * 36, lane);
+        quant_block_warp(r < rows ? q8stage[bb * 32 + lane] : 0.0f, a.q8_out + (size_t)(blk0 + bb) * 36, lane);
       }
     }
+#if MCPO_TRACE
+    if (tr) {
+      asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
+      if (tid == 0) trace_stamp(tr, 3);
+    }
+#endif
   }
 }
 
 template <int kClass>
 cudaError_t set_chain_attr() {
   return cudaFuncSetAttribute(k_gemv_chain<kClass>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              (int)(kChainSmemMax - 2048 - sizeof(GemvArgs)));
+                              (int)(kChainSmemMax - 2048 - kMaxChain * sizeof(GemvArgs)));
 }
 
 }  // namespace
@@ -211,7 +248,7 @@ bool chain_layout(const GemvArgs* stages, const int* dtype_masks, int n, int sm_
   if ((mask & 4) && (mask & 3)) return false;
   c->cls = (mask & 4) ? kClassQ80 : (mask & 3) == 3 ? kClassQ4K6K : (mask & 2) ? kClassQ6K : kClassQ4K;
   const size_t xb = gemv_x_bytes_host(cols);
-  const size_t budget = kChainSmemMax - 2048 - sizeof(GemvArgs);
+  const size_t budget = kChainSmemMax - 2048 - kMaxChain * sizeof(GemvArgs);
   const size_t fixed = xb + (size_t)q8 * 4;
   if (fixed >= budget) return false;
   // the deepest ring (up to 4 slots) that still gives every consumer warp

@@ -33,6 +33,11 @@ struct GemvChain {
   unsigned* bar;           // n - 1 grid-barrier arrival counters, zero before the launch
   int* abort;              // set by a CTA that gives up (zero before the launch)
   int* err;                // error word (StepState::err)
+  // MCPO_TRACE builds: per stage and CTA four globaltimer stamps (stage
+  // start, activations ready, rows done, stage done) at
+  // trace[((stage / 2) * trace_ctas + cta) * 8 + (stage % 2) * 4 + i]; null: none
+  unsigned long long* trace;
+  int trace_ctas;
 };
 
 // Kernel class and ring layout of a chain over the given (host-side,

@@ -136,21 +136,6 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1) k_gemv(const Gemv
   float* stage = a.q8_out ? reinterpret_cast<float*>(empty + NC * S) : nullptr;
   gemv_items<kClass, kDots, kTp>(a, x, ring, full, empty, S, slot, wr0, nwr, NC, warp, lane, n, nullptr, stage,
                                  blk0 * 32);
-  if constexpr (kTp) {
-    if (a.seg[0].epi == kEpiTpPush) {
-      // every consumer's remote stores are visible system-wide before the
-      // arrival counts say so (tp_proto.h)
-      __threadfence_system();
-      asm volatile("bar.sync 1, %0;" ::"r"(NC * 32) : "memory");
-      const GemvSeg& s0 = a.seg[0];
-      const int r0 = wr0 * s0.rpw, r1 = min((wr0 + nwr) * s0.rpw, s0.rows);
-      if (threadIdx.x == 0 && r1 > r0)
-        for (int d = 0; d < a.tp.world; ++d)
-          asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(a.tp.dst_arrive[d]),
-                       "r"((unsigned)(r1 - r0))
-                       : "memory");
-    }
-  }
   if (a.q8_out) {
     // every consumer warp arrives here once (also after a wait gave up)
     asm volatile("bar.sync 1, %0;" ::"r"(NC * 32) : "memory");
@@ -383,10 +368,15 @@ cudaError_t gemv_prepare(GemvArgs& a, int* dtypes_mask) {
   const bool push = a.seg[0].epi == kEpiTpPush;
   for (int i = 1; i < a.nseg; ++i)
     if (a.seg[i].epi == kEpiTpPush) return cudaErrorInvalidValue;
-  if ((push || a.input == kInRmsNormTp) && (a.tp.world < 1 || a.tp.world > kTpMaxWorld || a.nvec > 1 || a.dots))
+  if ((push || a.input == kInRmsNormTp) &&
+      (a.tp.world < 1 || a.tp.world > kTpMaxWorld || (a.tp.world & (a.tp.world - 1)) || a.nvec > 1 || a.dots))
     return cudaErrorInvalidValue;
   if (push && (a.nseg != 1 || a.q8_out)) return cudaErrorInvalidValue;
-  if (a.input == kInRmsNormTp && (!a.tp.step || !a.tp.arrive || !a.tp.sum_out || a.tp.rows != a.cols || a.tp.nx < 1))
+  if ((push || a.input == kInRmsNormTp) && (!a.tp.step || a.tp.nx < 1 || a.tp.x < 0 || a.tp.x >= a.tp.nx))
+    return cudaErrorInvalidValue;
+  for (int d = 0; d < a.tp.world; ++d)
+    if ((push && !a.tp.dst[d]) || (a.input == kInRmsNormTp && !a.tp.src[d])) return cudaErrorInvalidValue;
+  if (a.input == kInRmsNormTp && (!a.tp.sum_out || a.tp.rows != a.cols))
     return cudaErrorInvalidValue;
   if ((mask & 8) || ((mask & 4) && (mask & 3))) return cudaErrorInvalidValue;  // no mixed Q8_0 kernel
   a.total_wr = wr;

@@ -252,23 +252,19 @@ __device__ __forceinline__ uint64_t gemv_globaltimer() {
   return t;
 }
 
-// The tensor-parallel summing prologue: thread 0 waits (bounded, 1 s) for
-// every rank's partial of the exchange, then the NC*32 consumer threads
-// write sx[i] = xf[i] + rank-order sum of the partials and this CTA's share
-// of sx to tp.sum_out.  Ends with the consumers synchronised.
+// The tensor-parallel summing prologue: the NC*32 consumer threads write
+// sx[i] = xf[i] + rank-order sum of the partials, each value once every
+// rank's tagged word of it has arrived (bounded wait, 1 s), and this CTA's
+// share of sx to tp.sum_out.  Ends with the consumers synchronised.
 __device__ __forceinline__ void gemv_tp_sum(const GemvArgs& a, float* sx, int tid, int nthr) {
   const TpXchg& t = a.tp;
-  if (tid == 0) {
-    const uint32_t target = tp_target(tp_exchange_index(*t.step, (uint32_t)t.nx, (uint32_t)t.x), (uint32_t)t.rows);
-    const bool ok = tp_wait_all(
-        t.arrive, t.world, target, [](const uint32_t* p) { return ld_acquire_sys_u32(p); },
-        [] { return gemv_globaltimer(); }, 1000000000ull);
-    if (!ok && a.err) atomicExch(a.err, 1);
-  }
-  asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
+  const uint32_t tag = tp_xchg_tag(t, *t.step);
+  const uint64_t deadline = tp_now_ns() + 1000000000ull;
+  bool ok = true;
   const int cols = a.cols;
-  for (int i = tid; i < cols; i += nthr)
-    sx[i] = tp_rank_sum(a.xf[i], t.world, [&](int r) { return __ldcv(t.src[r] + i); });
+  // tp_rank_sum: base + (p_0 + ... + p_{world-1})
+  tp_gather_sums(t, tag, tid, nthr, cols, deadline, &ok, [&](int i, float s) { sx[i] = a.xf[i] + s; });
+  if (!ok && a.err) atomicExch(a.err, 1);
   asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
   const int G = gridDim.x, b = blockIdx.x;
   const int lo = (int)((long long)cols * b / G), hi = (int)((long long)cols * (b + 1) / G);
@@ -497,8 +493,10 @@ __device__ __forceinline__ void gemv_build_x(const GemvArgs& a, uint8_t* xbase, 
     const float eps = a.eps;
     const int part = lane & 3;
     const int ntile = (nblk + 7) / 8;
-    const bool at_once = norm ? ntile <= NC : ntile <= 3 * NC;
-    float xv[3][8], wv[8];
+    // all of a warp's tiles requested at once: up to two with RMSNorm
+    // (their weights in wv, wv1), three without
+    const bool at_once = norm ? ntile <= 2 * NC : ntile <= 3 * NC;
+    float xv[3][8], wv[8], wv1[8];
     auto load_x = [&](int tile, float (&dst)[8]) {
       const int b = tile * 8 + (lane >> 2);
       if (b < nblk) {
@@ -511,10 +509,10 @@ __device__ __forceinline__ void gemv_build_x(const GemvArgs& a, uint8_t* xbase, 
         for (int i = 0; i < 8; ++i) dst[i] = 0.0f;
       }
     };
-    auto load_w = [&](int tile) {
+    auto load_w = [&](int tile, float (&dst)[8]) {
       const int b = tile * 8 + (lane >> 2);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) wv[i] = b < nblk ? load_weight(nw, ndt, b * 32 + part * 8 + i) : 0.0f;
+      for (int i = 0; i < 8; ++i) dst[i] = b < nblk ? load_weight(nw, ndt, b * 32 + part * 8 + i) : 0.0f;
     };
     if (at_once) {
 #pragma unroll
@@ -528,8 +526,9 @@ __device__ __forceinline__ void gemv_build_x(const GemvArgs& a, uint8_t* xbase, 
 #pragma unroll
         for (int i = 0; i < 8; ++i) wv[i] = wpre[i];
       } else {
-        load_w(warp);
+        load_w(warp, wv);
       }
+      if (at_once && warp + NC < ntile) load_w(warp + NC, wv1);
     }
     float inv = 1.0f;
     if (norm) {
@@ -573,7 +572,7 @@ __device__ __forceinline__ void gemv_build_x(const GemvArgs& a, uint8_t* xbase, 
         if (tile < ntile) {
           float x[8];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) x[i] = norm ? __fmul_rn(__fmul_rn(xv[u][i], inv), wv[i]) : xv[u][i];
+          for (int i = 0; i < 8; ++i) x[i] = norm ? __fmul_rn(__fmul_rn(xv[u][i], inv), u == 0 ? wv[i] : wv1[i]) : xv[u][i];
           x_block_quarter(x, tile * 8 + (lane >> 2), nblk, part, nb, xs, xd, xds, xs16);
         }
       }
@@ -584,7 +583,7 @@ __device__ __forceinline__ void gemv_build_x(const GemvArgs& a, uint8_t* xbase, 
         for (int i = 0; i < 8; ++i) x[i] = norm ? __fmul_rn(__fmul_rn(xv[0][i], inv), wv[i]) : xv[0][i];
         if (tile + NC < ntile) {
           load_x(tile + NC, xv[0]);
-          if (norm) load_w(tile + NC);
+          if (norm) load_w(tile + NC, wv);
         }
         x_block_quarter(x, tile * 8 + (lane >> 2), nblk, part, nb, xs, xd, xds, xs16);
       }
@@ -615,6 +614,10 @@ __device__ __forceinline__ bool gemv_items(const GemvArgs& a, const XShared& x, 
   const bool swiglu = a.seg[0].epi == kEpiSwiglu;
   const int ks = a.seg[0].ks;
   const int items = nwr > warp ? (nwr - warp + NC - 1) / NC : 0;
+  uint32_t tag = 0;
+  if constexpr (kTp) {
+    if (a.seg[0].epi == kEpiTpPush) tag = tp_xchg_tag(a.tp, *a.tp.step);
+  }
   for (int item = 0; item < items; ++item) {
     const int wr = wr0 + warp + NC * item;
     const GemvSeg s = seg_of(a, wr);
@@ -648,7 +651,9 @@ __device__ __forceinline__ bool gemv_items(const GemvArgs& a, const XShared& x, 
       const float out = swiglu ? silu_mul_det(g, u) : add ? __fadd_rn(yold, g) : g;
       if constexpr (kTp) {
         if (s.epi == kEpiTpPush) {
-          for (int d = 0; d < a.tp.world; ++d) a.tp.dst[d][row] = out;  // this rank's slot on every rank
+          // this rank's slot on every rank, the value with the exchange's tag
+          const uint64_t w = tp_ll_pack(__float_as_uint(out), tag);
+          for (int d = 0; d < a.tp.world; ++d) tp_st_word(a.tp.dst[d] + row, w);
         } else {
           s.y[row] = out;
           if (stage) stage[row - stage_r0] = out;

@@ -709,7 +709,11 @@ cudaError_t record_step(Ctx* c, Model& m, bool logits) {
     REC(launch_attention(a, s, true));
     if (m.chain_ok) {  // o, gate/up, down and the next layer's q/k/v (or the lm_head) as one launch
       const size_t ci = (li + 1 == cf.layers && !logits) ? cf.layers : li;
-      REC(launch_gemv_chain(m.chains[ci], c->sm_count, m.chain_smem[ci], s));
+      GemvChain ch = m.chains[ci];
+      ch.trace = trace_next();
+      ch.trace_ctas = m.trace_ctas;
+      if (ch.n > 2 && ch.trace) trace_next();  // stages 2, 3 in the next launch slot
+      REC(launch_gemv_chain(ch, c->sm_count, m.chain_smem[ci], s));
       continue;
     }
     // (head_dim % 32 != 0: the o GEMV quantises the f32 attention output itself)
@@ -1425,8 +1429,8 @@ int keep_shards_only(Ctx* c, Model& m, Upload* out_full, char* err, size_t cap) 
 // every rank's exchange buffer (this rank's entry is its own).
 int shard_model(Ctx* c, Model& m, int rank, int world, const uint8_t* peer_handles, char* err, size_t cap) {
   minicpmo_qwen3_config& cf = m.cfg;
-  if (world > kTpMaxWorld || rank < 0 || rank >= world || !peer_handles)
-    return fail(c, err, cap, "error: qwen3 bind_tp: bad rank=%d world=%d", rank, world);
+  if (world > kTpMaxWorld || (world & (world - 1)) || rank < 0 || rank >= world || !peer_handles)
+    return fail(c, err, cap, "error: qwen3 bind_tp: bad rank=%d world=%d (world: 2, 4 or 8)", rank, world);
   if (!c->tp_buf || c->tp_buf_hidden != cf.hidden)
     return fail(c, err, cap, "error: qwen3 bind_tp: export the exchange buffer (tp_buffer) for hidden=%u first", cf.hidden);
   if (cf.heads % world || cf.kv_heads % world || cf.ffn % 256)
@@ -1479,7 +1483,7 @@ int shard_model(Ctx* c, Model& m, int rank, int world, const uint8_t* peer_handl
     }
     p.base[r] = base;
     p.top[r] = reinterpret_cast<float*>(base + TpLayout::top_offset(cf.hidden));
-    p.flag[r] = reinterpret_cast<unsigned*>(base + TpLayout::flag_offset(cf.hidden));
+    p.merge[r] = reinterpret_cast<uint64_t*>(base + TpLayout::merge_offset(cf.hidden));
   }
   if (!cuda_ok(c, cudaMalloc((void**)&m.tp_epoch, sizeof(unsigned)), "tp_epoch_malloc", err, cap) ||
       !cuda_ok(c, cudaMemsetAsync(m.tp_epoch, 0, sizeof(unsigned), c->stream), "tp_epoch_memset", err, cap) ||

@@ -3,10 +3,9 @@
 // The hidden-vector exchanges after the row-parallel o and down GEMVs are
 // fused into those GEMVs (push epilogue) and the GEMV that consumes them
 // (summing prologue); the protocol is in tp_proto.h.  What remains here:
-// the step counter and the sampler merge.  The merge uses a flag per rank:
-// a kernel publishes its epoch with a system-scope release store to its own
-// flag, then acquires every peer's flag, bounded by 1 s of globaltimer; peer
-// data is read with uncached loads.
+// the step counter, the consumer half of an exchange on its own, and the
+// sampler merge, whose per-rank results travel as tagged words too (tag =
+// the merge epoch), so no kernel here fences or waits on a flag.
 #include "tp.cuh"
 
 #include <math.h>
@@ -19,52 +18,20 @@ namespace mcpo {
 
 namespace {
 
-__device__ __forceinline__ uint64_t gtimer() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-// Thread 0: publish epoch e and wait for every peer's; false on timeout.
-__device__ bool publish_and_wait(const TpPeers& p, unsigned e) {
-  __threadfence_system();
-  st_release_sys(p.flag[p.rank], e);
-  const uint64_t t0 = gtimer();
-  for (int r = 0; r < p.world; ++r) {
-    if (r == p.rank) continue;
-    unsigned it = 0;
-    while (ld_acquire_sys(p.flag[r]) < e) {
-      if ((++it & 255u) == 0 && (gtimer() - t0 > 1000000000ull || it > (1u << 24))) return false;
-    }
-  }
-  return true;
-}
+constexpr uint64_t kTpWaitNs = 1000000000ull;
 
 // The consumer half of an exchange on its own (the step without an lm_head):
-// thread 0 waits for every rank's partial, then out = base + rank-order sum.
+// out = base + rank-order sum, each value once every rank's word of it has
+// arrived.
 __global__ void __launch_bounds__(1024) k_tp_finalize(const TpXchg t, const float* base, int* err) {
-  __shared__ int ok_s;
   pdl_wait();
-  if (threadIdx.x == 0) {
-    const uint32_t target = tp_target(tp_exchange_index(*t.step, (uint32_t)t.nx, (uint32_t)t.x), (uint32_t)t.rows);
-    ok_s = tp_wait_all(
-        t.arrive, t.world, target, [](const uint32_t* p) { return ld_acquire_sys(p); }, [] { return gtimer(); },
-        1000000000ull);
-    if (!ok_s && err) atomicExch(err, 1);
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < t.rows; i += blockDim.x)
-    t.sum_out[i] = tp_rank_sum(base[i], t.world, [&](int r) { return __ldcv(t.src[r] + i); });
+  const uint32_t tag = tp_xchg_tag(t, *t.step);
+  const uint64_t deadline = tp_now_ns() + kTpWaitNs;
+  bool ok = true;
+  // tp_rank_sum: base + (p_0 + ... + p_{world-1})
+  tp_gather_sums(t, tag, threadIdx.x, blockDim.x, t.rows, deadline, &ok,
+                 [&](int i, float s) { t.sum_out[i] = base[i] + s; });
+  if (!ok && err) atomicExch(err, 1);
   pdl_launch_dependents();
 }
 
@@ -74,13 +41,37 @@ __global__ void k_tp_step(unsigned* step) {
   pdl_launch_dependents();
 }
 
+// One warp.  Lane d < world sends this rank's sampler result (its own
+// k_argmax wrote `top`) to rank d; lane r < world then waits for rank r's.
 __global__ void k_tp_sample_merge(const TpPeers p, StepState* st, int* history, int history_cap, unsigned* epoch,
                                   int* err) {
+  __shared__ float rb_s[kTpMaxWorld], rs_s[kTpMaxWorld];
+  __shared__ int ri_s[kTpMaxWorld];
   pdl_wait();
-  if (threadIdx.x != 0) return;
-  const unsigned e = *epoch + 1u;
-  *epoch = e;
-  if (!publish_and_wait(p, e)) {
+  const int lane = threadIdx.x;
+  const uint32_t e = tp_tag(*epoch);  // the merge's tag: epochs 0, 1, ... -> tags 1, 2, ...
+  const float* own = p.top[p.rank];
+  if (lane < p.world) {
+    uint64_t* dst = p.merge[lane] + (size_t)p.rank * 4;
+    for (int k = 0; k < 3; ++k) tp_st_word(dst + k, tp_ll_pack(__float_as_uint(own[k]), e));
+  }
+  bool ok = true;
+  if (lane < p.world) {
+    const uint64_t deadline = tp_now_ns() + kTpWaitNs;
+    const uint64_t* src = p.merge[p.rank] + (size_t)lane * 4;
+    uint32_t v[3];
+    for (int k = 0; k < 3; ++k)
+      v[k] = tp_ll_wait(src + k, e, [](const uint64_t* q) { return tp_ld_word(q); }, [] { return tp_now_ns(); },
+                        deadline, &ok);
+    rb_s[lane] = __uint_as_float(v[0]);
+    ri_s[lane] = (int)v[1];
+    rs_s[lane] = __uint_as_float(v[2]);
+  }
+  const bool all_ok = __all_sync(0xffffffffu, ok);
+  __syncwarp();
+  if (lane != 0) return;
+  *epoch = *epoch + 1u;
+  if (!all_ok) {
     atomicExch(err, 1);
     return;
   }
@@ -89,9 +80,9 @@ __global__ void k_tp_sample_merge(const TpPeers p, StepState* st, int* history, 
   float b = -INFINITY, s = -INFINITY;
   int idx = 0x7fffffff;
   for (int r = 0; r < p.world; ++r) {
-    const float rb = __ldcv(p.top[r]);
-    const int ri = __float_as_int(__ldcv(p.top[r] + 1));
-    const float rs = __ldcv(p.top[r] + 2);
+    const float rb = rb_s[r];
+    const int ri = ri_s[r];
+    const float rs = rs_s[r];
     const bool wins = rb > b || (rb == b && ri < idx);
     if (wins) {
       s = fmaxf(fmaxf(s, rs), b);
@@ -121,14 +112,11 @@ __global__ void k_tp_sample_merge(const TpPeers p, StepState* st, int* history, 
 void tp_xchg(const TpPeers& p, int nx, int x, int rows, const unsigned* step, float* sum_out, TpXchg* out) {
   TpXchg t{};
   const int par = x & 1;
-  for (int d = 0; d < p.world; ++d) {
-    t.dst[d] = reinterpret_cast<float*>(p.base[d] + TpLayout::part_offset(par, p.rank, (size_t)rows));
-    t.dst_arrive[d] = reinterpret_cast<unsigned*>(p.base[d] + TpLayout::arrive_offset((size_t)rows)) + p.rank;
-  }
+  for (int d = 0; d < p.world; ++d)
+    t.dst[d] = reinterpret_cast<uint64_t*>(p.base[d] + TpLayout::part_offset(par, p.rank, (size_t)rows));
   uint8_t* own = p.base[p.rank];
   for (int r = 0; r < p.world; ++r)
-    t.src[r] = reinterpret_cast<const float*>(own + TpLayout::part_offset(par, r, (size_t)rows));
-  t.arrive = reinterpret_cast<const unsigned*>(own + TpLayout::arrive_offset((size_t)rows));
+    t.src[r] = reinterpret_cast<const uint64_t*>(own + TpLayout::part_offset(par, r, (size_t)rows));
   t.sum_out = sum_out;
   t.step = step;
   t.world = p.world;
@@ -139,7 +127,8 @@ void tp_xchg(const TpPeers& p, int nx, int x, int rows, const unsigned* step, fl
 }
 
 cudaError_t launch_tp_finalize(const TpXchg& t, const float* base, int* err, cudaStream_t st) {
-  if (t.world < 1 || t.world > kTpMaxWorld || !t.sum_out || !t.step || !t.arrive) return cudaErrorInvalidValue;
+  if (t.world < 1 || t.world > kTpMaxWorld || (t.world & (t.world - 1)) || !t.sum_out || !t.step || !t.src[0])
+    return cudaErrorInvalidValue;
   return launch_k(k_tp_finalize, dim3(1), dim3(1024), 0, st, true, t, base, err);
 }
 

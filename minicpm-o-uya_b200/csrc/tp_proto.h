@@ -4,19 +4,24 @@
 // Every rank of a tensor-parallel decode runs the same sequence of steps,
 // and every step the same number `nx` of exchanges (two per layer: after the
 // row-parallel o and down projections).  In exchange x of step s (the step
-// counter counts from 1) every source rank pushes its partial vector of
+// counter counts from 1) every source rank stores its partial vector of
 // `rows` values into a slot of every rank's exchange buffer (remote stores
-// over NVLink), then adds the number of values it stored to that rank's
-// arrival counter for it.  The consumer of the exchange waits (bounded)
-// until every source's counter reaches the exchange's target, then sums the
-// partials in rank order, so every rank computes identical bits.
+// over NVLink).  Each value travels with the exchange's tag in one
+// naturally aligned 64-bit word (value bits in the low half, tag in the
+// high half), written and read as single-copy-atomic 64-bit accesses: a
+// reader that sees the tag it expects has the value of that exchange, so
+// no fence, release or arrival counter is needed.  The consumer of the
+// exchange waits (bounded) element by element until every source's word
+// carries the tag, then sums the partials in rank order, so every rank
+// computes identical bits.
 //
-// Counters are monotonic 32-bit and compared with wraparound arithmetic,
-// so they are never reset while ranks run.  Slots alternate between two
-// parities by the exchange's global index: a source can only write an
-// exchange's slot again two exchanges later, after every rank has consumed
-// the exchange in between, which it cannot do before this rank has
-// contributed to it, i.e. before this rank finished reading the slot.
+// Tags are the exchange's global index mod 2^32 - 1, plus one: never 0 (the
+// zeroed buffer's content) and different for the two exchanges that can
+// share a slot.  Slots alternate between two parities by the global index:
+// a source can only write an exchange's slot again two exchanges later,
+// after every rank has consumed the exchange in between, which it cannot do
+// before this rank has contributed to it, i.e. before this rank finished
+// reading the slot.
 #pragma once
 
 #include <stdint.h>
@@ -34,28 +39,34 @@ constexpr int kTpMaxWorld = 8;
 // Global index of exchange x of step `step` (step >= 1).
 TP_HD uint32_t tp_exchange_index(uint32_t step, uint32_t nx, uint32_t x) { return (step - 1u) * nx + x; }
 
-// Arrival count at which all `rows` values of exchange `index` have arrived
-// from one source.
-TP_HD uint32_t tp_target(uint32_t index, uint32_t rows) { return (index + 1u) * rows; }
-
-TP_HD bool tp_arrived(uint32_t count, uint32_t target) { return (int32_t)(count - target) >= 0; }
-
 // The slot parity of exchange `index`.
 TP_HD int tp_parity(uint32_t index) { return (int)(index & 1u); }
 
-// Waits until arrive[0..world) all reach `target`.  load(p) is an acquire
-// load of counter p, now() a clock in nanoseconds; gives up (false) once
-// limit_ns have passed or after a fixed number of polls.
+// The tag of exchange `index`: 1 .. 2^32 - 1.
+TP_HD uint32_t tp_tag(uint32_t index) { return index % 0xffffffffu + 1u; }
+
+TP_HD uint64_t tp_ll_pack(uint32_t bits, uint32_t tag) { return (uint64_t)bits | ((uint64_t)tag << 32); }
+TP_HD uint32_t tp_ll_tag(uint64_t w) { return (uint32_t)(w >> 32); }
+TP_HD uint32_t tp_ll_bits(uint64_t w) { return (uint32_t)w; }
+
+// Waits until the word at p carries `tag` and returns its value bits.
+// load(p) is a single-copy-atomic 64-bit load, now() a clock in
+// nanoseconds.  Gives up once now() passes `deadline` (or after a fixed
+// number of polls), clearing *ok; a caller whose *ok is already clear does
+// not wait again.  Returns 0 when it gave up.
 template <typename Load, typename Now>
-TP_HD bool tp_wait_all(const uint32_t* arrive, int world, uint32_t target, Load load, Now now, uint64_t limit_ns) {
-  const uint64_t t0 = now();
+TP_HD uint32_t tp_ll_wait(const uint64_t* p, uint32_t tag, Load load, Now now, uint64_t deadline, bool* ok) {
+  uint64_t w = load(p);
   uint32_t polls = 0;
-  for (int r = 0; r < world; ++r) {
-    while (!tp_arrived(load(arrive + r), target)) {
-      if ((++polls & 255u) == 0u && (now() - t0 > limit_ns || polls > (1u << 26))) return false;
+  while (tp_ll_tag(w) != tag) {
+    if (!*ok) return 0u;
+    if ((++polls & 63u) == 0u && (now() > deadline || polls > (1u << 24))) {
+      *ok = false;
+      return 0u;
     }
+    w = load(p);
   }
-  return true;
+  return tp_ll_bits(w);
 }
 
 // Sum of one value over the ranks' partials, in rank order, then added to

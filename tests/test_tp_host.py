@@ -93,11 +93,12 @@ def test_exchange_protocol_sums_in_rank_order(harness, world):
     assert status == [0] * world and bad == [0] * world
 
 
-def test_exchange_protocol_counters_wrap(harness):
-    """Monotonic 32-bit counters compare with wraparound arithmetic: steps
-    whose arrival counts cross 2^32 run without a reset."""
+def test_exchange_protocol_tags_wrap(harness):
+    """The 32-bit exchange index wraps without a reset: steps whose indices
+    cross 2^32 still tag every value apart from the slot's previous
+    exchange and from the zeroed buffer."""
     nx, rows = 8, 96
-    first = (1 << 32) // (nx * rows) - 5  # the counters wrap a few steps in
+    first = (1 << 32) // nx - 5  # the index wraps a few steps in
     status, bad = _run(harness, 4, steps=12, nx=nx, rows=rows, first_step=first)
     assert status == [0] * 4 and bad == [0] * 4
 

@@ -4,17 +4,20 @@
 // tests/test_tp_host.py with the host compiler.
 //
 // Each of `world` threads plays a rank.  Per step it runs `nx` exchanges:
-// it stores its partial vector into its slot of every rank's buffer (the
-// slot of the exchange's parity), releases the stores by adding the row
-// count to that rank's arrival counter for it, then waits (bounded) for
-// every rank's contribution and checks the rank-order sum value by value.
-// A rank can be "killed" at the start of a step (it leaves between steps,
-// as a crashed process would); the others must then give up after the
-// wait limit and report the error instead of hanging.
+// it stores its partial vector, every value with the exchange's tag in one
+// 64-bit word, into its slot of every rank's buffer (the slot of the
+// exchange's parity), then waits (bounded) value by value for every rank's
+// word to carry the tag and checks the rank-order sum value by value.  The
+// words are written and read with relaxed 64-bit atomics, as the kernels'
+// st/ld.relaxed.sys: no fence or release orders them.  A rank can be
+// "killed" at the start of a step (it leaves between steps, as a crashed
+// process would); the others must then give up after the wait limit and
+// report the error instead of hanging.
 #include <atomic>
 #include <chrono>
 #include <cstdint>
 #include <cstring>
+#include <memory>
 #include <random>
 #include <thread>
 #include <vector>
@@ -26,9 +29,20 @@ using namespace mcpo;
 namespace {
 
 struct RankBuf {
-  std::vector<float> part;  // [2][kTpMaxWorld][rows]
-  std::atomic<uint32_t> arrive[kTpMaxWorld];
+  std::unique_ptr<std::atomic<uint64_t>[]> part;  // [2][kTpMaxWorld][rows] tagged words
 };
+
+uint32_t bits_of(float f) {
+  uint32_t b;
+  std::memcpy(&b, &f, 4);
+  return b;
+}
+
+float float_of(uint32_t b) {
+  float f;
+  std::memcpy(&f, &b, 4);
+  return f;
+}
 
 float value(int rank, uint32_t index, int i) {
   // distinct per (rank, exchange, element), exact in f32
@@ -43,20 +57,19 @@ uint64_t now_ns() {
 
 }  // namespace
 
-// Steps first_step .. first_step + steps - 1 (the counters start where the
-// steps before first_step left them, so a large first_step runs the 32-bit
-// counters across their wraparound).
+// Steps first_step .. first_step + steps - 1 (a large first_step runs the
+// exchange index, and with it the tag, across its wraparound).
 extern "C" int tp_harness_run(int world, unsigned first_step, int steps, int nx, int rows, int kill_rank,
                               int kill_step, unsigned long long limit_ns, int max_skew_us, unsigned seed, int* status,
                               int* mismatches) {
   if (world < 1 || world > kTpMaxWorld || nx < 2 || (nx & 1) || rows < 1 || steps < 1 || first_step < 1) return 0;
   std::vector<RankBuf> buf(world);
-  const uint32_t start = (first_step - 1u) * (uint32_t)nx * (uint32_t)rows;
+  const size_t words = (size_t)2 * kTpMaxWorld * rows;
   for (auto& b : buf) {
-    b.part.assign((size_t)2 * kTpMaxWorld * rows, 0.0f);
-    for (auto& a : b.arrive) a.store(start);
+    b.part.reset(new std::atomic<uint64_t>[words]);
+    for (size_t i = 0; i < words; ++i) b.part[i].store(0);
   }
-  auto slot = [&](int dst, int par, int src) { return buf[dst].part.data() + ((size_t)par * kTpMaxWorld + src) * rows; };
+  auto slot = [&](int dst, int par, int src) { return &buf[dst].part[((size_t)par * kTpMaxWorld + src) * rows]; };
   std::vector<std::thread> th;
   for (int r = 0; r < world; ++r) {
     status[r] = -1;
@@ -73,27 +86,31 @@ extern "C" int tp_harness_run(int world, unsigned first_step, int steps, int nx,
         for (int x = 0; x < nx; ++x) {
           const uint32_t index = tp_exchange_index(step, (uint32_t)nx, (uint32_t)x);
           const int par = tp_parity(index);
+          const uint32_t tag = tp_tag(index);
           for (int d = 0; d < world; ++d) {
-            float* s = slot(d, par, r);
-            for (int i = 0; i < rows; ++i) s[i] = value(r, index, i);
+            std::atomic<uint64_t>* s = slot(d, par, r);
+            for (int i = 0; i < rows; ++i)
+              s[i].store(tp_ll_pack(bits_of(value(r, index, i)), tag), std::memory_order_relaxed);
           }
-          for (int d = 0; d < world; ++d) buf[d].arrive[r].fetch_add((uint32_t)rows, std::memory_order_release);
           if (max_skew_us > 0) std::this_thread::sleep_for(std::chrono::microseconds(skew(rng)));
-          const bool ok = tp_wait_all(
-              reinterpret_cast<const uint32_t*>(buf[r].arrive), world, tp_target(index, (uint32_t)rows),
-              [](const uint32_t* p) {
-                return reinterpret_cast<const std::atomic<uint32_t>*>(p)->load(std::memory_order_acquire);
-              },
-              now_ns, limit_ns);
+          const uint64_t deadline = now_ns() + limit_ns;
+          bool ok = true;
+          for (int i = 0; i < rows && ok; ++i) {
+            const float base = (float)(i % 7);
+            const float got = tp_rank_sum(base, world, [&](int src) {
+              return float_of(tp_ll_wait(
+                  reinterpret_cast<const uint64_t*>(slot(r, par, src) + i), tag,
+                  [](const uint64_t* p) {
+                    return reinterpret_cast<const std::atomic<uint64_t>*>(p)->load(std::memory_order_relaxed);
+                  },
+                  now_ns, deadline, &ok));
+            });
+            const float want = tp_rank_sum(base, world, [&](int src) { return value(src, index, i); });
+            if (ok && std::memcmp(&got, &want, sizeof(float)) != 0) ++mismatches[r];
+          }
           if (!ok) {
             status[r] = 1;
             return;
-          }
-          for (int i = 0; i < rows; ++i) {
-            const float base = (float)(i % 7);
-            const float got = tp_rank_sum(base, world, [&](int src) { return slot(r, par, src)[i]; });
-            const float want = tp_rank_sum(base, world, [&](int src) { return value(src, index, i); });
-            if (std::memcmp(&got, &want, sizeof(float)) != 0) ++mismatches[r];
           }
         }
       }
