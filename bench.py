@@ -307,10 +307,12 @@ def _ncu_traffic(key):
 
 def run_prefill_bench(args, shape, mix) -> int:
     """Prompt prefill on 1 GPU: --prompt seeded ids through qwen3_prefill
-    (passes of up to 4 tokens) and, over the same positions of a reset
-    cache, through one qwen3_forward per id (the reference's
-    qwen3_append_prompt_ids loop).  Host wall time around each call, which
-    synchronises; max(1, --steps // 64) repetitions after one untimed."""
+    (16 ids or more: tensor-core passes of up to 256; fewer: GEMV passes of
+    up to 4) and, over the same positions of a reset cache, through one
+    qwen3_forward per id (the reference's qwen3_append_prompt_ids loop).
+    Host wall time around each call, which synchronises; max(1, --steps //
+    64) repetitions after one untimed (which also builds the tensor-core
+    operand copy of the weights)."""
     import torch
 
     from minicpmo_b200.qwen3 import Qwen3Runtime
@@ -340,10 +342,13 @@ def run_prefill_bench(args, shape, mix) -> int:
     print(json.dumps({
         "metric": f"{metric_name(args.shape).replace('decode', 'prefill')}",
         "value": args.prompt / t_pf, "unit": "tok/s", "n_gpus": 1, "steps": reps, "warmup": 1,
-        "higher_is_better": True, "dtype": "q4_k/q6_k x q8_1 (int8 dp4a, f32 accumulate)",
+        "higher_is_better": True,
+        "dtype": ("q4_k/q6_k x q8_1 (int8 block dots on tcgen05 kind::i8, f32 combine)" if args.prompt >= 16
+                  else "q4_k/q6_k x q8_1 (int8 dp4a, f32 accumulate)"),
         "data": f"synthetic: seeded N(0,0.02) weights quantised Q4_K_M-style, {args.prompt} uniform random prompt ids",
         "config": {"workload": f"{args.shape}-shape Q4_K_M prompt prefill, {args.prompt} ids from position 0",
-                   "layers": shape.layers, "passes": (args.prompt + 3) // 4},
+                   "layers": shape.layers,
+                   "passes": (args.prompt + 255) // 256 if args.prompt >= 16 else (args.prompt + 3) // 4},
         "prefill_s": t_pf, "tokenwise_s": t_tw, "tokenwise_tok_s": args.prompt / t_tw,
         "speedup_vs_tokenwise": t_tw / t_pf, "next_token": int(pf[0][1][0]),
     }), flush=True)

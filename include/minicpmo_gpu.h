@@ -234,10 +234,14 @@ MINICPMO_API int minicpmo_gpu_context_qwen3_sample(void *handle, const uint32_t 
                                       float repeat_penalty, uint32_t *seed_state, uint32_t *out_token, char *error,
                                       size_t error_cap);
 /* Forward the n prompt tokens tokens[0..n) at positions first_pos.. in
- * passes of up to 4 tokens that stream the weights once per pass (the
- * reference prefills token by token, qwen3.uya:2485-2506): every token's
- * arithmetic is that of qwen3_forward, so the KV cache and the last token's
- * logits and greedy sample (flags bit 0 clear) equal those of n forwards.
+ * passes over the weights (the reference prefills token by token,
+ * qwen3.uya:2485-2506): 16 tokens or more in passes of up to 256 with the
+ * projections on the tensor cores (exact int8 block dots, the first call
+ * builds an int8 operand copy of the weights, about 1.1 bytes per weight;
+ * MCPO_PREFILL_TC=0 turns this off), fewer in passes of up to 4 through the
+ * GEMVs.  Every token's arithmetic is that of qwen3_forward, so the KV
+ * cache and the last token's logits and greedy sample (flags bit 0 clear)
+ * equal those of n forwards.
  * The tokens join the penalty's seen set.  Models whose weights are not all
  * in the tiled GEMV layouts (or under tensor parallelism) are refused with
  * an error; use qwen3_forward for them. */

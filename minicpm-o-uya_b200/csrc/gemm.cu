@@ -42,6 +42,7 @@
 
 #include "common.cuh"
 #include "gemv.cuh"
+#include "tcgen05.cuh"
 #include "tma.cuh"
 
 namespace mcpo {
@@ -74,31 +75,12 @@ struct GemmSmem {
   }
 };
 
-// ---- tcgen05 primitives ----
-
-// Shared-memory matrix descriptor, K-major, no swizzle: core matrices of 8
-// rows x 16 bytes stored contiguously (128 bytes); lbo = byte distance
-// between the two 16-byte K-chunks of one MMA (K = 16), sbo = byte distance
-// between consecutive 8-row groups.  Version 1 (sm_100), base offset 0.
-__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
-  return (uint64_t)((saddr >> 4) & 0x3fffu) | ((uint64_t)((lbo >> 4) & 0x3fffu) << 16) |
-         ((uint64_t)((sbo >> 4) & 0x3fffu) << 32) | (1ull << 46);
-}
+// ---- tcgen05 primitives (the shared ones are in tcgen05.cuh) ----
 
 // Instruction descriptor for kind::f16: f16 A and B (K-major), f32
 // accumulator, M = 128, N = n.
 __host__ __device__ constexpr uint32_t umma_idesc_f16(int n) {
   return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kGemmTileRows >> 4) << 24);
-}
-
-__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                         uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
 }
 
 // D (+)= A * B with A (128 x 16 f16, lane = row) in tensor memory at tmem_a.
@@ -126,29 +108,10 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32
 
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// Arrives on `bar` once every tcgen05 operation this thread issued before it
-// has completed.
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
-               : "memory");
-}
 
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 
-// Generic-proxy shared-memory writes become visible to the tensor cores.
-__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(dst_smem)),
-               "r"(ncols)
-               : "memory");
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-}
 
-__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
 
 // 16 consecutive f32 accumulator columns of this thread's lane.
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
@@ -176,16 +139,6 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
   for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// Bounded wait that leaves early once the CTA's abort flag is set.
-__device__ __forceinline__ bool gwait(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_s) {
-  for (int i = 0; i < kWaitLimit; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 63) == 63 && *abort_s) return false;
-  }
-  *abort_s = 1;
-  if (err) atomicExch(err, 1);
-  return false;
-}
 
 // Two signed bytes (positions 0,1 or 2,3 of w, already xor 0x80) as f16x2
 // exactly: 0x6400 | u is 1024 + u, minus 1152 gives u - 128 = q.

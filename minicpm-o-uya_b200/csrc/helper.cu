@@ -20,6 +20,7 @@
 
 #include "attention.cuh"
 #include "chain.cuh"
+#include "pgemm.cuh"
 #include "step.cuh"
 #include "tp.cuh"
 #include "gemm.cuh"
@@ -98,9 +99,20 @@ struct Model {
   uint32_t *smp_seen = nullptr, *smp_io = nullptr, *smp_bits = nullptr;
   size_t smp_seen_cap = 0;
   StepState* smp_st = nullptr;
-  // prompt prefill (qwen3_prefill): up to kGemvMaxVec tokens per pass
+  // prompt prefill (qwen3_prefill): pf_cap tokens per pass (kGemvMaxVec
+  // through the multi-vector GEMVs, kPgChunk through the tensor cores)
   float *pf_hidden = nullptr, *pf_q = nullptr, *pf_k = nullptr, *pf_v = nullptr, *pf_attn = nullptr,
-        *pf_fused = nullptr, *pf_partial = nullptr;
+        *pf_fused = nullptr, *pf_partial = nullptr, *pf_gate = nullptr;
+  int pf_cap = 0;
+  // tensor-core prefill (pgemm.cuh): operand copies of every layer's
+  // linear weights and the activation operands, built at the first prefill
+  // that uses them
+  struct PgLayer {
+    PgemmMat q, k, v, o, gate, up, down;
+  };
+  std::vector<PgLayer> pg;
+  PgemmAct pg_h, pg_q, pg_f;  // activation operands of K = hidden, q columns, ffn
+  bool pg_failed = false;
   int *pf_tok = nullptr, *pf_pos = nullptr, *pf_err = nullptr;
   unsigned* pf_counters = nullptr;
   float* partial = nullptr;
@@ -508,9 +520,15 @@ void free_model(Model* m) {
                   m->history, m->stages, m->step_scratch, m->step_trace, m->graph_trace, m->chain_stages, m->chain_bar, m->tp_epoch, m->tp_step, m->hidden2, m->embed_in,
                   m->smp_seen, m->smp_io, m->smp_bits, m->smp_st, m->pf_hidden, m->pf_q, m->pf_k, m->pf_v,
                   m->pf_attn, m->pf_fused, m->pf_partial, m->pf_tok, m->pf_pos, m->pf_counters,
-                  m->pf_err};
+                  m->pf_err, m->pf_gate};
   for (void* p : bufs)
     if (p) cudaFree(p);
+  for (auto& L : m->pg)
+    for (PgemmMat* w : {&L.q, &L.k, &L.v, &L.o, &L.gate, &L.up, &L.down}) pgemm_free(w);
+  m->pg.clear();
+  pgemm_act_free(&m->pg_h);
+  pgemm_act_free(&m->pg_q);
+  pgemm_act_free(&m->pg_f);
   if (m->st_host) cudaFreeHost(m->st_host);
   for (auto& u : m->shards)
     if (u->dev && !u->view) cudaFree(u->dev);
@@ -1734,6 +1752,7 @@ int minicpmo_gpu_context_create(unsigned int device_index, int debug, void** out
       !cuda_ok(c, attention_init(), "attention_init", error, error_cap) ||
       !cuda_ok(c, decode_step_init(), "decode_step_init", error, error_cap) ||
       !cuda_ok(c, chain_init(), "chain_init", error, error_cap) ||
+      !cuda_ok(c, pgemm_init(), "pgemm_init", error, error_cap) ||
       !cuda_ok(c, cudaMalloc((void**)&c->dev_err, sizeof(int)), "error_word_malloc", error, error_cap) ||
       !cuda_ok(c, cudaMemset(c->dev_err, 0, sizeof(int)), "error_word_memset", error, error_cap)) {
     if (c->dev_err) cudaFree(c->dev_err);
@@ -2522,23 +2541,76 @@ bool prefill_ok(const Model& m) {
   return true;
 }
 
-bool prefill_alloc(Ctx* c, Model& m, char* err, size_t cap) {
-  if (m.pf_hidden) return true;
+// Prefill buffers for `tokens` per pass (reallocated when a pass needs more).
+bool prefill_alloc(Ctx* c, Model& m, int tokens, char* err, size_t cap) {
+  if (m.pf_hidden && m.pf_cap >= tokens) return true;
+  for (void** p : {(void**)&m.pf_hidden, (void**)&m.pf_q, (void**)&m.pf_k, (void**)&m.pf_v, (void**)&m.pf_attn,
+                   (void**)&m.pf_fused, (void**)&m.pf_gate, (void**)&m.pf_tok, (void**)&m.pf_pos,
+                   (void**)&m.pf_partial, (void**)&m.pf_counters, (void**)&m.pf_err})
+    if (*p) cudaFree(*p), *p = nullptr;
+  m.pf_cap = 0;
   const auto& cf = m.cfg;
-  const size_t N = kGemvMaxVec, h = cf.hidden, qd = m.qd, f = cf.ffn, hd = cf.head_dim;
+  const size_t N = (size_t)tokens, h = cf.hidden, qd = m.qd, f = cf.ffn, hd = cf.head_dim;
   struct {
     void** p;
     size_t bytes;
   } allocs[] = {
       {(void**)&m.pf_hidden, N * h * 4}, {(void**)&m.pf_q, N * qd * 4},   {(void**)&m.pf_k, N * qd * 4},
       {(void**)&m.pf_v, N * qd * 4},     {(void**)&m.pf_attn, N * qd * 4}, {(void**)&m.pf_fused, N * f * 4},
-      {(void**)&m.pf_tok, N * 4},        {(void**)&m.pf_pos, N * 4},
+      {(void**)&m.pf_gate, N * f * 4},   {(void**)&m.pf_tok, N * 4},       {(void**)&m.pf_pos, N * 4},
       {(void**)&m.pf_partial, N * attn_partial_floats((int)cf.heads, attn_n_blocks((int)cf.context), (int)hd) * 4},
       {(void**)&m.pf_counters, N * cf.kv_heads * 4}, {(void**)&m.pf_err, 4},
   };
   for (auto& a : allocs)
     if (!cuda_ok(c, cudaMalloc(a.p, a.bytes), "prefill_malloc", err, cap)) return false;
-  return cuda_ok(c, cudaMemsetAsync(m.pf_counters, 0, N * cf.kv_heads * 4, c->stream), "prefill_memset", err, cap);
+  m.pf_cap = tokens;
+  return cuda_ok(c, cudaMemsetAsync(m.pf_counters, 0, N * cf.kv_heads * 4, c->stream), "prefill_memset", err, cap) &&
+         cuda_ok(c, cudaMemsetAsync(m.pf_err, 0, 4, c->stream), "prefill_memset", err, cap);
+}
+
+// Prompts of at least kPgMinTokens take the tensor-core path (MCPO_PREFILL_TC=0
+// turns it off), kPgChunk tokens per pass.
+constexpr int kPgChunk = 256;
+constexpr int kPgMinTokens = 16;
+
+int prefill_tc_cfg() {
+  static const int v = [] {
+    const char* e = getenv("MCPO_PREFILL_TC");
+    return (e && *e) ? (atoi(e) != 0 ? 1 : 0) : 1;
+  }();
+  return v;
+}
+
+// The operand copies for the tensor-core prefill (false: not available, e.g.
+// out of device memory; the multi-vector path is used instead).
+bool pg_build(Ctx* c, Model& m) {
+  if (!m.pg.empty()) return true;
+  if (m.pg_failed) return false;
+  const auto& cf = m.cfg;
+  bool ok = true;
+  m.pg.resize(cf.layers);
+  for (uint32_t li = 0; li < cf.layers && ok; ++li) {
+    const LayerW& L = m.layer[li];
+    Model::PgLayer& P = m.pg[li];
+    const std::pair<Upload*, PgemmMat*> mats[] = {{L.q, &P.q},       {L.k, &P.k},   {L.v, &P.v},      {L.o, &P.o},
+                                                  {L.gate, &P.gate}, {L.up, &P.up}, {L.down, &P.down}};
+    for (const auto& mt : mats)
+      if (ok && pgemm_build(mt.first->geom, mt.first->dev, mt.second, c->stream) != cudaSuccess) ok = false;
+  }
+  ok = ok && pgemm_act_alloc(kPgChunk, (int)cf.hidden, &m.pg_h) == cudaSuccess &&
+       pgemm_act_alloc(kPgChunk, (int)m.qd, &m.pg_q) == cudaSuccess &&
+       pgemm_act_alloc(kPgChunk, (int)cf.ffn, &m.pg_f) == cudaSuccess;
+  if (!ok) {
+    cudaGetLastError();
+    for (auto& L : m.pg)
+      for (PgemmMat* w : {&L.q, &L.k, &L.v, &L.o, &L.gate, &L.up, &L.down}) pgemm_free(w);
+    m.pg.clear();
+    pgemm_act_free(&m.pg_h);
+    pgemm_act_free(&m.pg_q);
+    pgemm_act_free(&m.pg_f);
+    m.pg_failed = true;
+  }
+  return ok;
 }
 
 // The four GEMVs of a layer and k_prompt_qk are launched with programmatic
@@ -2550,20 +2622,22 @@ bool prefill_alloc(Ctx* c, Model& m, char* err, size_t cap) {
 // weights: each token's arithmetic is that of a decode step (same Q8_1
 // activations and dot orders, same attention and norms), so the cache and
 // the last token's logits equal those of token-by-token forwards.
-int prefill_chunk(Ctx* c, Model& m, const uint32_t* toks, int n, size_t p0, bool logits, float penalty, char* err,
-                  size_t cap) {
+// With tc, the projections run on the tensor cores (pgemm.cuh, n <=
+// kPgChunk) with the same bits.
+int prefill_chunk(Ctx* c, Model& m, const uint32_t* toks, int n, size_t p0, bool logits, float penalty, bool tc,
+                  char* err, size_t cap) {
   const auto& cf = m.cfg;
   const int h = (int)cf.hidden, qd = (int)m.qd, f = (int)cf.ffn, hd = (int)cf.head_dim;
   const size_t esz = cf.kv_f16 ? 2 : 4;
   const cudaStream_t s = c->stream;
-  int ht[kGemvMaxVec], hp[kGemvMaxVec];
+  std::vector<int> ht(n), hp(n);
   for (int i = 0; i < n; ++i) {
     ht[i] = (int)toks[i];
     hp[i] = (int)(p0 + i);
   }
   auto ok = [&](cudaError_t e, const char* what) { return cuda_ok(c, e, what, err, cap); };
-  if (!ok(cudaMemcpyAsync(m.pf_tok, ht, n * 4, cudaMemcpyHostToDevice, s), "prefill_tok_h2d") ||
-      !ok(cudaMemcpyAsync(m.pf_pos, hp, n * 4, cudaMemcpyHostToDevice, s), "prefill_pos_h2d") ||
+  if (!ok(cudaMemcpyAsync(m.pf_tok, ht.data(), n * 4, cudaMemcpyHostToDevice, s), "prefill_tok_h2d") ||
+      !ok(cudaMemcpyAsync(m.pf_pos, hp.data(), n * 4, cudaMemcpyHostToDevice, s), "prefill_pos_h2d") ||
       !ok(launch_embed(m.tok->dev, m.tok->geom, m.tok->dtype, (int)m.tok->rows, h, m.pf_tok, 0, m.pf_hidden, s, false, n,
                        1),
           "prefill_embed") ||
@@ -2572,18 +2646,28 @@ int prefill_chunk(Ctx* c, Model& m, const uint32_t* toks, int n, size_t p0, bool
   c->stats.host_to_device_bytes += (size_t)n * 8;
   for (uint32_t li = 0; li < cf.layers; ++li) {
     const LayerW& L = m.layer[li];
-    GemvArgs a{};
-    a.nseg = 3;
-    a.cols = h;
-    norm_input(&a, m.pf_hidden, L.attn_norm, cf.rms_eps);
-    a.err = m.pf_err;
-    a.nvec = n;
-    a.x_stride = h;
-    a.y_stride = qd;
-    Upload* qkv[3] = {L.q, L.k, L.v};
-    float* ys[3] = {m.pf_q, m.pf_k, m.pf_v};
-    for (int i = 0; i < 3; ++i) gemv_seg_from_geom(qkv[i]->geom, qkv[i]->dev, nullptr, ys[i], kEpiStore, &a.seg[i]);
-    if (!ok(launch_gemv(a, m.grid_h, s, true), "prefill_qkv")) return 0;
+    if (tc) {
+      const Model::PgLayer& P = m.pg[li];
+      if (!ok(launch_pgemm_act(m.pf_hidden, h, n, L.attn_norm->dev, L.attn_norm->dtype, cf.rms_eps, m.pg_h, s),
+              "prefill_act_qkv") ||
+          !ok(launch_pgemm(P.q, m.pg_h, n, kPgStore, m.pf_q, qd, nullptr, 0, m.pf_err, s), "prefill_q") ||
+          !ok(launch_pgemm(P.k, m.pg_h, n, kPgStore, m.pf_k, qd, nullptr, 0, m.pf_err, s), "prefill_k") ||
+          !ok(launch_pgemm(P.v, m.pg_h, n, kPgStore, m.pf_v, qd, nullptr, 0, m.pf_err, s), "prefill_v"))
+        return 0;
+    } else {
+      GemvArgs a{};
+      a.nseg = 3;
+      a.cols = h;
+      norm_input(&a, m.pf_hidden, L.attn_norm, cf.rms_eps);
+      a.err = m.pf_err;
+      a.nvec = n;
+      a.x_stride = h;
+      a.y_stride = qd;
+      Upload* qkv[3] = {L.q, L.k, L.v};
+      float* ys[3] = {m.pf_q, m.pf_k, m.pf_v};
+      for (int i = 0; i < 3; ++i) gemv_seg_from_geom(qkv[i]->geom, qkv[i]->dev, nullptr, ys[i], kEpiStore, &a.seg[i]);
+      if (!ok(launch_gemv(a, m.grid_h, s, true), "prefill_qkv")) return 0;
+    }
     uint8_t* kc = (uint8_t*)m.kc + li * m.kv_layer_elems * esz;
     uint8_t* vc = (uint8_t*)m.vc + li * m.kv_layer_elems * esz;
     if (!ok(launch_prompt_qk(m.pf_q, m.pf_k, m.pf_v, qd, n, (int)cf.heads, (int)cf.kv_heads, hd,
@@ -2616,6 +2700,19 @@ int prefill_chunk(Ctx* c, Model& m, const uint32_t* toks, int n, size_t p0, bool
     at.out_bstride = (size_t)qd;
     at.err = m.pf_err;
     if (!ok(launch_attention(at, s, false), "prefill_attention")) return 0;
+    if (tc) {
+      const Model::PgLayer& P = m.pg[li];
+      if (!ok(launch_pgemm_act(m.pf_attn, qd, n, nullptr, 0, 0.0f, m.pg_q, s), "prefill_act_o") ||
+          !ok(launch_pgemm(P.o, m.pg_q, n, kPgAdd, m.pf_hidden, h, nullptr, 0, m.pf_err, s), "prefill_o") ||
+          !ok(launch_pgemm_act(m.pf_hidden, h, n, L.ffn_norm->dev, L.ffn_norm->dtype, cf.rms_eps, m.pg_h, s),
+              "prefill_act_ffn") ||
+          !ok(launch_pgemm(P.gate, m.pg_h, n, kPgStore, m.pf_gate, f, nullptr, 0, m.pf_err, s), "prefill_gate") ||
+          !ok(launch_pgemm(P.up, m.pg_h, n, kPgSwiglu, m.pf_fused, f, m.pf_gate, f, m.pf_err, s), "prefill_up") ||
+          !ok(launch_pgemm_act(m.pf_fused, f, n, nullptr, 0, 0.0f, m.pg_f, s), "prefill_act_down") ||
+          !ok(launch_pgemm(P.down, m.pg_f, n, kPgAdd, m.pf_hidden, h, nullptr, 0, m.pf_err, s), "prefill_down"))
+        return 0;
+      continue;
+    }
     GemvArgs o{};
     o.nseg = 1;
     o.cols = qd;
@@ -2692,13 +2789,17 @@ int minicpmo_gpu_context_qwen3_prefill(void* handle, const uint32_t* tokens, siz
       return fail(c, error, error_cap, "error: qwen3 prefill token=%u >= vocab=%u", tokens[i], m.cfg.vocab);
   if (!prefill_ok(m))
     return fail(c, error, error_cap, "error: qwen3 prefill: this model needs token-by-token forwards");
-  if (!prefill_alloc(c, m, error, error_cap)) return 0;
+  const bool tc = n >= (size_t)kPgMinTokens && prefill_tc_cfg() && pg_build(c, m);
+  const int per = tc ? kPgChunk : kGemvMaxVec;
+  if (!prefill_alloc(c, m, per, error, error_cap)) return 0;
   if (!cuda_ok(c, cudaMemsetAsync(m.pf_err, 0, sizeof(int), c->stream), "prefill_err_clear", error, error_cap))
     return 0;
   const bool want = !(flags & 1);
-  for (size_t i0 = 0; i0 < n; i0 += kGemvMaxVec) {
-    const int cn = (int)(n - i0 < (size_t)kGemvMaxVec ? n - i0 : kGemvMaxVec);
-    if (!prefill_chunk(c, m, tokens + i0, cn, first_pos + i0, want && i0 + cn == n, repeat_penalty, error, error_cap))
+  size_t passes = 0;
+  for (size_t i0 = 0; i0 < n; i0 += (size_t)per, ++passes) {
+    const int cn = (int)(n - i0 < (size_t)per ? n - i0 : (size_t)per);
+    if (!prefill_chunk(c, m, tokens + i0, cn, first_pos + i0, want && i0 + cn == n, repeat_penalty, tc, error,
+                       error_cap))
       return 0;
   }
   StepState* hs = m.st_host;
@@ -2716,7 +2817,7 @@ int minicpmo_gpu_context_qwen3_prefill(void* handle, const uint32_t* tokens, siz
   if (!cuda_ok(c, cudaStreamSynchronize(c->stream), "prefill_sync", error, error_cap)) return 0;
   if (perr || (want && hs->err))
     return fail(c, error, error_cap, "error: qwen3 prefill: a device-side check failed (a bounded wait gave up, or a position outside the cache)");
-  c->stats.attention_kernel_calls += m.cfg.layers * ((n + kGemvMaxVec - 1) / kGemvMaxVec);
+  c->stats.attention_kernel_calls += m.cfg.layers * passes;
   if (out_token) *out_token = want ? (uint32_t)hs->next_token : 0u;
   if (out_top2_gap) *out_top2_gap = want ? hs->gap : 0.0f;
   return 1;

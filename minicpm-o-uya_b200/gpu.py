@@ -387,7 +387,8 @@ class GpuContext:
 
     def qwen3_prefill(self, tokens, first_pos: int, logits: bool = True, penalty: float = 1.0,
                       want_logits: Optional[np.ndarray] = None):
-        """Prompt tokens in passes of up to 4 (qwen3_prefill); the same bits as token-by-token forwards."""
+        """Prompt tokens in passes over the weights (qwen3_prefill: 16 tokens or more on the tensor cores, 256 per
+        pass, else up to 4 per pass through the GEMVs); the same bits as token-by-token forwards."""
         t = np.ascontiguousarray(np.asarray(tokens, dtype=np.uint32))
         out = u32()
         gap = f32()

@@ -396,13 +396,18 @@ def test_layered_q4_k_m_file_matches_oracle(pkg, O, tmp_path, decode_mode):
 @pytest.mark.parametrize(
     "mix,kv_f16,shape_kw,n_prompt",
     [("Q4_K_M", False, {}, 10), ("Q4_K_M", True, {}, 7), ("ALL_Q8_0", False, {}, 4), ("Q4_K_M", False, {"head_dim": 64}, 9),
-     ("Q4_K_M_LAYERED", False, {"layers": 4}, 13), ("Q4_K_M", False, {}, 1)],
+     ("Q4_K_M_LAYERED", False, {"layers": 4}, 13), ("Q4_K_M", False, {}, 1),
+     # 16 tokens or more: the projections on the tensor cores (pgemm.cu)
+     ("Q4_K_M", False, {}, 40), ("Q4_K_M", True, {}, 70), ("ALL_Q8_0", False, {}, 33), ("Q4_K_M", False, {"head_dim": 64}, 16),
+     ("Q4_K_M_LAYERED", False, {"layers": 4}, 57), ("Q4_K_M", False, {"hidden": 1024, "ffn": 3072}, 48)],
 )
 def test_prefill_matches_token_by_token(pkg, O, mix, kv_f16, shape_kw, n_prompt):
-    """qwen3_prefill (prompt tokens in passes of up to 4 over the weights)
-    against the reference's token-by-token prefill (qwen3.uya:2485-2506,
-    which the forward reproduces bit-exactly): the last token's logits and
-    greedy token are bit-identical, and so is every decode step after it
+    """qwen3_prefill against the reference's token-by-token prefill
+    (qwen3.uya:2485-2506, which the forward reproduces bit-exactly): prompts
+    under 16 tokens go through the multi-vector GEMVs (up to 4 tokens per
+    pass over the weights), longer ones through the tensor-core projections
+    (tcgen05 kind::i8, 32-token tiles).  Either way the last token's logits
+    and greedy token are bit-identical, and so is every decode step after it
     (the KV caches agree)."""
     from minicpmo_b200 import gguf
     from minicpmo_b200.qwen3 import Qwen3Runtime
@@ -422,6 +427,38 @@ def test_prefill_matches_token_by_token(pkg, O, mix, kv_f16, shape_kw, n_prompt)
         pos = len(ids) + step
         ta, ga = a.forward(ta, pos, penalty=1.2, want_logits=la)
         tb, gb = b.forward(tb, pos, penalty=1.2, want_logits=lb)
+        assert np.array_equal(la, lb), (step, rel_row_err(la, lb))
+        assert (ta, ga) == (tb, gb), step
+    a.close()
+    b.close()
+
+
+@pytest.mark.parametrize("mix", ["Q4_K_M", "ALL_Q8_0"])
+def test_prefill_tensor_core_passes(pkg, O, mix):
+    """A prompt longer than one tensor-core pass (256 tokens) after a
+    token-by-token start: positions continue across passes, the cache rows
+    of every pass are what the token-by-token forwards write, and the last
+    token's logits and the decode after it are bit-identical."""
+    from minicpmo_b200 import gguf
+    from minicpmo_b200.qwen3 import Qwen3Runtime
+
+    shape = small_shape(context=400, ffn=1024)
+    tensors = build(pkg, shape, getattr(gguf, mix), seed=13)
+    a = Qwen3Runtime.open(tensors, shape=shape, context=shape.context)
+    b = Qwen3Runtime.open(tensors, shape=shape, context=shape.context)
+    ids = [int(t) for t in gguf.prompt_ids(300, shape.vocab, seed=21)]
+    la, lb = np.empty(shape.vocab, np.float32), np.empty(shape.vocab, np.float32)
+    for pos, t in enumerate(ids):
+        ta, ga = a.forward(t, pos, logits=pos == len(ids) - 1, want_logits=la if pos == len(ids) - 1 else None)
+    for pos in range(3):  # the first tokens one by one, the rest in one call
+        b.forward(ids[pos], pos, logits=False)
+    tb, gb = b.gpu.qwen3_prefill(ids[3:], 3, want_logits=lb)
+    assert np.array_equal(la, lb), rel_row_err(la, lb)
+    assert (ta, ga) == (tb, gb)
+    for step in range(4):
+        pos = len(ids) + step
+        ta, ga = a.forward(ta, pos, want_logits=la)
+        tb, gb = b.forward(tb, pos, want_logits=lb)
         assert np.array_equal(la, lb), (step, rel_row_err(la, lb))
         assert (ta, ga) == (tb, gb), step
     a.close()
