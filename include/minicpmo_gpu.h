@@ -363,6 +363,10 @@ MINICPMO_API int minicpmo_gpu_context_qwen3_time_decode(void *handle, uint32_t f
 /* Kernel launches in one decode step's graph (with or without the lm_head
  * and sampler); 0 when no model is bound. */
 MINICPMO_API int minicpmo_gpu_context_qwen3_step_kernels(void *handle, int with_logits);
+/* Prefill passes so far (qwen3_prefill) whose projections ran on the tensor
+ * cores, and in *gemv_passes (may be NULL) those that ran through the
+ * multi-vector GEMVs; -1 when no model is bound. */
+MINICPMO_API long long minicpmo_gpu_context_qwen3_prefill_passes(void *handle, long long *gemv_passes);
 /* With MCPO_STEP_TRACE=1 in the environment at bind time, the persistent
  * step kernel records per stage and CTA the globaltimer (ns) at the start of
  * the stage, when the activations are ready (GEMV stages) and when all of the

@@ -113,6 +113,7 @@ struct Model {
   std::vector<PgLayer> pg;
   PgemmAct pg_h, pg_q, pg_f;  // activation operands of K = hidden, q columns, ffn
   bool pg_failed = false;
+  long long pf_tc_passes = 0, pf_gemv_passes = 0;
   int *pf_tok = nullptr, *pf_pos = nullptr, *pf_err = nullptr;
   unsigned* pf_counters = nullptr;
   float* partial = nullptr;
@@ -2818,6 +2819,7 @@ int minicpmo_gpu_context_qwen3_prefill(void* handle, const uint32_t* tokens, siz
   if (perr || (want && hs->err))
     return fail(c, error, error_cap, "error: qwen3 prefill: a device-side check failed (a bounded wait gave up, or a position outside the cache)");
   c->stats.attention_kernel_calls += m.cfg.layers * passes;
+  (tc ? m.pf_tc_passes : m.pf_gemv_passes) += (long long)passes;
   if (out_token) *out_token = want ? (uint32_t)hs->next_token : 0u;
   if (out_top2_gap) *out_top2_gap = want ? hs->gap : 0.0f;
   return 1;
@@ -3386,6 +3388,13 @@ int minicpmo_gpu_context_qwen3_step_kernels(void* handle, int with_logits) {
   Ctx* c = (Ctx*)handle;
   if (!c || !c->model) return 0;
   return c->model->kernels[with_logits ? 0 : 1];
+}
+
+long long minicpmo_gpu_context_qwen3_prefill_passes(void* handle, long long* gemv_passes) {
+  Ctx* c = (Ctx*)handle;
+  if (!c || !c->model) return -1;
+  if (gemv_passes) *gemv_passes = c->model->pf_gemv_passes;
+  return c->model->pf_tc_passes;
 }
 
 int minicpmo_gpu_context_qwen3_step_trace(void* handle, uint64_t* out, size_t cap, uint32_t* n_stages,

@@ -150,6 +150,7 @@ SIGNATURES = {
     "minicpmo_gpu_context_qwen3_time_decode": (i32, [vp, u32, sz, sz, fptr] + E),
     "minicpmo_gpu_context_tensor_device_bytes": (sz, [vp, vp]),
     "minicpmo_gpu_context_qwen3_step_kernels": (i32, [vp, i32]),
+    "minicpmo_gpu_context_qwen3_prefill_passes": (C.c_longlong, [vp, C.POINTER(C.c_longlong)]),
     "minicpmo_gpu_context_qwen3_step_trace": (i32, [vp, vp, sz, u32ptr, u32ptr]),
     "minicpmo_gpu_context_qwen3_graph_trace": (i32, [vp, vp, sz, u32ptr, u32ptr]),
     "minicpmo_gpu_attention_no_alloc": (i32, [vp, vp, vp, i32, sz, sz, sz, sz, sz, vp, vp] + E),
@@ -525,6 +526,12 @@ class GpuContext:
 
     def qwen3_step_kernels(self, with_logits: bool = True) -> int:
         return int(self.lib.minicpmo_gpu_context_qwen3_step_kernels(self.handle, int(with_logits)))
+
+    def qwen3_prefill_passes(self):
+        """(tensor-core passes, multi-vector GEMV passes) of qwen3_prefill so far."""
+        g = C.c_longlong()
+        tc = self.lib.minicpmo_gpu_context_qwen3_prefill_passes(self.handle, C.byref(g))
+        return int(tc), int(g.value)
 
     def qwen3_step_trace(self):
         """[stage][cta][start, ready, end] ns of the last persistent step (MCPO_STEP_TRACE=1 at bind), or None."""

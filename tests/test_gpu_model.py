@@ -421,6 +421,8 @@ def test_prefill_matches_token_by_token(pkg, O, mix, kv_f16, shape_kw, n_prompt)
     for pos, t in enumerate(ids):
         ta, ga = a.forward(t, pos, logits=pos == len(ids) - 1, penalty=1.2, want_logits=la if pos == len(ids) - 1 else None)
     tb, gb = b.gpu.qwen3_prefill(ids, 0, penalty=1.2, want_logits=lb)
+    tc, gv = b.gpu.qwen3_prefill_passes()
+    assert (tc, gv) == ((1, 0) if n_prompt >= 16 else (0, (n_prompt + 3) // 4))  # the path the test names
     assert np.array_equal(la, lb), rel_row_err(la, lb)
     assert (ta, ga) == (tb, gb)
     for step in range(5):
@@ -453,6 +455,7 @@ def test_prefill_tensor_core_passes(pkg, O, mix):
     for pos in range(3):  # the first tokens one by one, the rest in one call
         b.forward(ids[pos], pos, logits=False)
     tb, gb = b.gpu.qwen3_prefill(ids[3:], 3, want_logits=lb)
+    assert b.gpu.qwen3_prefill_passes() == (2, 0)  # 256 + 41 tokens on the tensor cores
     assert np.array_equal(la, lb), rel_row_err(la, lb)
     assert (ta, ga) == (tb, gb)
     for step in range(4):
