@@ -570,6 +570,19 @@ cudaError_t model_mv(Ctx* c, Upload* w, const float* x, const uint8_t* xq, float
 // MCPO_ATTN_CLUSTER=0); the same bits either way.
 // The gate/up GEMV hands the down GEMV Q8_1 blocks (1, the default) or f32
 // values (tuning override MCPO_FFN_Q8=0); the same bits either way.
+// CTAs per kv head and token of the prompt-prefill attention (the batch
+// alone fills the GPU, so fewer CTAs amortise the per-CTA prologue and
+// merge; the blocks merge in block order whatever the split, so the bits
+// do not change).
+int pf_split_cfg() {
+  static const int v = [] {
+    const char* e = getenv("MCPO_PF_SPLIT");
+    const int x = (e && *e) ? atoi(e) : 1;
+    return x < 1 ? 1 : x;
+  }();
+  return v;
+}
+
 int ffn_q8_cfg() {
   static const int v = [] {
     const char* e = getenv("MCPO_FFN_Q8");
@@ -2689,7 +2702,7 @@ int prefill_chunk(Ctx* c, Model& m, const uint32_t* toks, int n, size_t p0, bool
     at.n_kv = (int)cf.kv_heads;
     at.head_dim = hd;
     at.ctx = (int)cf.context;
-    at.n_split = m.n_split;
+    at.n_split = std::min(m.n_split, pf_split_cfg());
     at.cluster = 0;
     at.scale = 1.0f / sqrtf((float)hd);
     at.partial = m.pf_partial;

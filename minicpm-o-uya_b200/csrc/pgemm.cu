@@ -2,7 +2,8 @@
 //
 // One CTA per (128-row tile, 32-token tile), 18 warps:
 //   warp 0      producer: per super-block, bulk copies of its A, S, B (Bm for
-//               Q6_K) and X tiles into a 3-stage shared-memory ring;
+//               Q6_K) and X tiles into a shared-memory ring (3 stages, 2
+//               for Q6_K);
 //   warp 1      one thread issues the MMAs: per unit (a super-block, half of
 //               one for Q6_K) eight tcgen05.mma kind::i8 (M 128, N 32, K 32),
 //               one per 32-value block (Q6_K: per 16-value group, through
@@ -38,20 +39,28 @@ namespace mcpo {
 
 namespace {
 
-constexpr int kPgStages = 3;
 constexpr int kPgEpiWarps = 16;
 constexpr int kPgThreads = (2 + kPgEpiWarps) * 32;
 constexpr uint32_t kPgTmemCols = 512;  // two buffers x eight 32-column regions
 constexpr int kPgLevels = 6;           // reduction-tree levels for lpr <= 32
-constexpr int kPgBStage = 2 * kPgBBytes;  // room for Q6_K's two masked halves
+// Tree levels 1 .. kPgLevels-1 live in shared memory ([level][token][thread]
+// floats, each thread its own column); level 0 and the lane sums in
+// registers.
+constexpr size_t kPgStackBytes = (size_t)(kPgLevels - 1) * 8 * kPgEpiWarps * 32 * 4;
 
+// Ring stages and their operand bytes (Q6_K: two masked B halves, so one
+// stage fewer fits).
+template <int kDtype>
 struct PgSmem {
+  static constexpr int kStages = kDtype == kQ6_K ? 2 : 3;
+  static constexpr int kBStage = kDtype == kQ6_K ? 2 * kPgBBytes : kPgBBytes;
   __host__ __device__ static constexpr size_t a(int s) { return (size_t)s * kPgABytes; }
-  __host__ __device__ static constexpr size_t b(int s) { return (size_t)kPgStages * kPgABytes + (size_t)s * kPgBStage; }
-  __host__ __device__ static constexpr size_t sc(int s) { return b(kPgStages) + (size_t)s * kPgSBytes; }
-  __host__ __device__ static constexpr size_t x(int s) { return sc(kPgStages) + (size_t)s * kPgXFloats * 4; }
-  __host__ __device__ static constexpr size_t bars() { return x(kPgStages); }
-  __host__ __device__ static constexpr size_t bytes() { return bars() + 8 * (2 * kPgStages + 4 + 1) + 16 + 1024; }
+  __host__ __device__ static constexpr size_t b(int s) { return (size_t)kStages * kPgABytes + (size_t)s * kBStage; }
+  __host__ __device__ static constexpr size_t sc(int s) { return b(kStages) + (size_t)s * kPgSBytes; }
+  __host__ __device__ static constexpr size_t x(int s) { return sc(kStages) + (size_t)s * kPgXFloats * 4; }
+  __host__ __device__ static constexpr size_t stack() { return x(kStages); }
+  __host__ __device__ static constexpr size_t bars() { return stack() + kPgStackBytes; }
+  __host__ __device__ static constexpr size_t bytes() { return bars() + 8 * (2 * kStages + 4 + 1) + 16 + 1024; }
 };
 
 struct PgArgs {
@@ -104,11 +113,34 @@ __device__ __forceinline__ int pg_sb_at(int it, int ks, int levels) {
   return k * (1 << levels) + i;
 }
 
+// A lane sum lands on level kTop of the tree stack: the partials of the
+// levels below (earlier leaves) are added in front of it, level by level.
+// lvl0: level 0 in registers; sst: this thread's column of levels 1.. in
+// shared memory (stride kPgEpiWarps * 32 floats per (level, token)).
+template <int kTop>
+__device__ __forceinline__ void pg_push(float (&lvl0)[8], float* sst, const float (&acc)[8]) {
+  constexpr int kStride = kPgEpiWarps * 32;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    float c = acc[e];
+    if constexpr (kTop == 0) {
+      lvl0[e] = c;
+    } else {
+      c = __fadd_rn(lvl0[e], c);
+#pragma unroll
+      for (int l = 1; l < kTop; ++l) c = __fadd_rn(sst[((l - 1) * 8 + e) * kStride], c);
+      sst[((kTop - 1) * 8 + e) * kStride] = c;
+    }
+  }
+}
+
 template <int kDtype>
 __global__ void __launch_bounds__(kPgThreads, 1) k_pgemm(const PgArgs p) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + PgSmem::bars());
+  using L = PgSmem<kDtype>;
+  constexpr int kPgStages = L::kStages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::bars());
   uint64_t* empty = full + kPgStages;
   uint64_t* acc_full = empty + kPgStages;
   uint64_t* acc_empty = acc_full + 2;
@@ -155,10 +187,10 @@ __global__ void __launch_bounds__(kPgThreads, 1) k_pgemm(const PgArgs p) {
         if (it >= kPgStages && !gwait(&empty[s], (uint32_t)((it / kPgStages) - 1) & 1u, p.err, abort_s)) break;
         const size_t wt = (size_t)tile * nsb + sb, xt = (size_t)ttile * nsb + sb;
         mbar_arrive_expect_tx(&full[s], tx);
-        bulk_load_hint(smem + PgSmem::a(s), p.a + wt * kPgABytes, kPgABytes, &full[s], policy);
-        bulk_load(smem + PgSmem::sc(s), p.s + wt * kPgSBytes, kPgSBytes, &full[s]);
-        bulk_load(smem + PgSmem::b(s), p.b + xt * kBBytes, kBBytes, &full[s]);
-        bulk_load(smem + PgSmem::x(s), p.xs + xt * kPgXFloats, kPgXFloats * 4, &full[s]);
+        bulk_load_hint(smem + L::a(s), p.a + wt * kPgABytes, kPgABytes, &full[s], policy);
+        bulk_load(smem + L::sc(s), p.s + wt * kPgSBytes, kPgSBytes, &full[s]);
+        bulk_load(smem + L::b(s), p.b + xt * kBBytes, kBBytes, &full[s]);
+        bulk_load(smem + L::x(s), p.xs + xt * kPgXFloats, kPgXFloats * 4, &full[s]);
         issued = it + 1;
       }
       for (int it = issued > kPgStages ? issued - kPgStages : 0; it < issued; ++it)
@@ -174,7 +206,7 @@ __global__ void __launch_bounds__(kPgThreads, 1) k_pgemm(const PgArgs p) {
         const int s = it % kPgStages;
         if (!gwait(&full[s], (uint32_t)(it / kPgStages) & 1u, p.err, abort_s)) break;
         tc_fence_after();
-        const uint32_t a0 = smem_addr(smem + PgSmem::a(s)), b0 = smem_addr(smem + PgSmem::b(s));
+        const uint32_t a0 = smem_addr(smem + L::a(s)), b0 = smem_addr(smem + L::b(s));
         for (int h = 0; h < kUnits; ++h, ++u) {
           const int buf = u & 1;
           if (u >= 2 && !gwait(&acc_empty[buf], (uint32_t)((u >> 1) - 1) & 1u, p.err, abort_s)) {
@@ -207,14 +239,10 @@ __global__ void __launch_bounds__(kPgThreads, 1) k_pgemm(const PgArgs p) {
     const int qtr = warp & 3, tg = (warp - 2) >> 2;
     const int rl = qtr * 32 + lane;
     const uint32_t tbase = tmem + ((uint32_t)(qtr * 32) << 16) + (uint32_t)(tg * 8);
-    float stk[kPgLevels][8];
-    float acc[8];
+    float lvl0[8], acc[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      acc[e] = 0.0f;
-#pragma unroll
-      for (int l = 0; l < kPgLevels; ++l) stk[l][e] = 0.0f;
-    }
+    for (int e = 0; e < 8; ++e) acc[e] = lvl0[e] = 0.0f;
+    float* sst = reinterpret_cast<float*>(smem + L::stack()) + (threadIdx.x - 64);
     int cnt = 0, u = 0;
     bool go = true;
     for (int it = 0; it < nsb; ++it) {
@@ -223,8 +251,8 @@ __global__ void __launch_bounds__(kPgThreads, 1) k_pgemm(const PgArgs p) {
         go = false;
         break;
       }
-      const uint4* srow = reinterpret_cast<const uint4*>(smem + PgSmem::sc(s) + (size_t)rl * 32);
-      const float* X = reinterpret_cast<const float*>(smem + PgSmem::x(s)) + tg * 8;  // xd [j*32], xds [256 + j*32]
+      const uint4* srow = reinterpret_cast<const uint4*>(smem + L::sc(s) + (size_t)rl * 32);
+      const float* X = reinterpret_cast<const float*>(smem + L::x(s)) + tg * 8;  // xd [j*32], xds [256 + j*32]
       float v[8];
       if constexpr (kDtype == kQ4_K) {
         const uint4 h = srow[0];
@@ -330,16 +358,15 @@ __global__ void __launch_bounds__(kPgThreads, 1) k_pgemm(const PgArgs p) {
 #pragma unroll
       for (int e = 0; e < 8; ++e) acc[e] = __fadd_rn(k == 0 ? 0.0f : acc[e], v[e]);
       if (k == p.ks - 1) {
-        const int top = __ffs(~cnt) - 1;  // the level the merged value lands on
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          float c = acc[e];
-#pragma unroll
-          for (int l = 0; l < kPgLevels; ++l)
-            if (l < top) c = __fadd_rn(stk[l][e], c);
-#pragma unroll
-          for (int l = 0; l < kPgLevels; ++l)
-            if (l == top) stk[l][e] = c;
+        // the level the merged value lands on (the same for every thread:
+        // one branch, then straight-line code on fixed registers)
+        switch (__ffs(~cnt) - 1) {
+          case 0: pg_push<0>(lvl0, sst, acc); break;
+          case 1: pg_push<1>(lvl0, sst, acc); break;
+          case 2: pg_push<2>(lvl0, sst, acc); break;
+          case 3: pg_push<3>(lvl0, sst, acc); break;
+          case 4: pg_push<4>(lvl0, sst, acc); break;
+          default: pg_push<5>(lvl0, sst, acc); break;
         }
         ++cnt;
       }
@@ -349,10 +376,7 @@ __global__ void __launch_bounds__(kPgThreads, 1) k_pgemm(const PgArgs p) {
       const int row = tile * kPgRows + rl;
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        float val = 0.0f;
-#pragma unroll
-        for (int l = 0; l < kPgLevels; ++l)
-          if (l == p.levels) val = stk[l][e];
+        const float val = p.levels == 0 ? lvl0[e] : sst[((p.levels - 1) * 8 + e) * (kPgEpiWarps * 32)];
         const int t = ttile * kPgTok + tg * 8 + e;
         if (t < p.T && row < p.rows) {
           float* yp = p.y + (size_t)t * p.ldy + row;
@@ -506,7 +530,9 @@ __global__ void __launch_bounds__(256) k_pgemm_act(const float* x, int ldx, int 
 
 template <int kDtype>
 cudaError_t set_pgemm_attr() {
-  return cudaFuncSetAttribute(k_pgemm<kDtype>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PgSmem::bytes());
+  static_assert(PgSmem<kDtype>::bytes() <= 232448, "shared memory per CTA");
+  return cudaFuncSetAttribute(k_pgemm<kDtype>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              (int)PgSmem<kDtype>::bytes());
 }
 
 }  // namespace
@@ -612,11 +638,10 @@ cudaError_t launch_pgemm(const PgemmMat& w, const PgemmAct& x, int T, int epi, f
   p.ldg = ldg;
   p.err = err;
   const dim3 grid(w.tiles, (T + kPgTok - 1) / kPgTok);
-  const size_t smem = PgSmem::bytes();
   switch (w.dtype) {
-    case kQ4_K: return launch_k(k_pgemm<kQ4_K>, grid, dim3(kPgThreads), smem, st, true, p);
-    case kQ6_K: return launch_k(k_pgemm<kQ6_K>, grid, dim3(kPgThreads), smem, st, true, p);
-    case kQ8_0: return launch_k(k_pgemm<kQ8_0>, grid, dim3(kPgThreads), smem, st, true, p);
+    case kQ4_K: return launch_k(k_pgemm<kQ4_K>, grid, dim3(kPgThreads), PgSmem<kQ4_K>::bytes(), st, true, p);
+    case kQ6_K: return launch_k(k_pgemm<kQ6_K>, grid, dim3(kPgThreads), PgSmem<kQ6_K>::bytes(), st, true, p);
+    case kQ8_0: return launch_k(k_pgemm<kQ8_0>, grid, dim3(kPgThreads), PgSmem<kQ8_0>::bytes(), st, true, p);
     default: return cudaErrorInvalidValue;
   }
 }
