@@ -917,6 +917,199 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2)
   }
 }
 
+// ---------------------------------------------------------------------
+// Prompt attention (launch_prompt_attention): grid (n_kv, ceil(T / 8)), 8
+// warps; warp w serves token 8*blockIdx.y + w and the kv head's G q heads.
+// K/V blocks of 32 positions are staged as f32 rows (stride head_dim + 4
+// floats: lanes reading different rows hit different banks) in two
+// buffers; the next block's rows are loaded into registers while the
+// current one is used.  Per (token, head, block) the decode's arithmetic:
+// s = scale * (q . k) as one fma chain in d order, -inf past the token's
+// position, m = max, p = exp(s - m), l = butterfly sum, acc_d = sum p_t v_td
+// in t order, written as the block's partial; then the blocks merge in
+// block order (merge_blocks).
+constexpr int kPaTokens = 8;
+constexpr int kPaHeads = 4;  // q heads scored together by a warp (they share the K loads)
+
+template <int J>
+__host__ __device__ inline int pa_row_stride() {
+  return 32 * J + 4;
+}
+
+template <int J, typename T>
+__host__ __device__ inline size_t pa_smem_bytes(int G) {
+  return ((size_t)kPaTokens * G * 32 * J + (size_t)2 * 2 * 32 * pa_row_stride<J>()) * 4;
+}
+
+// Loads (vals) or stores (st) this thread's share of one K/V block: rows
+// c*32 .. +31 of the kv head, 4 values per chunk; rows at or past `rows`
+// are zeros.
+template <int J, typename T>
+struct PaStage {
+  static constexpr int kChunks = 2 * 32 * 32 * J / 4;  // K and V, 4 values each
+  static constexpr int kPer = kChunks / (8 * 32);        // per thread (256 threads)
+  float4 v[kPer];
+  __device__ __forceinline__ void load(const T* kc, const T* vc, int kv_dim, int kv_off, int c, int rows) {
+    const int hd = 32 * J;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int ch = threadIdx.x + i * 256;
+      const int half = ch / (kChunks / 2), rem = ch % (kChunks / 2);
+      const int r = rem / (hd / 4), q4 = rem % (hd / 4);
+      const int row = c * 32 + r;
+      float4 f = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      if (row < rows) {
+        const T* src = (half ? vc : kc) + (size_t)row * kv_dim + kv_off + q4 * 4;
+        if constexpr (sizeof(T) == 2) {
+          const uint2 u = *reinterpret_cast<const uint2*>(src);
+          const float2 a = h2f2(u.x), b = h2f2(u.y);
+          f = make_float4(a.x, a.y, b.x, b.y);
+        } else {
+          f = *reinterpret_cast<const float4*>(src);
+        }
+      }
+      v[i] = f;
+    }
+  }
+  __device__ __forceinline__ void store(float* buf) const {
+    const int hd = 32 * J, rs = pa_row_stride<J>();
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int ch = threadIdx.x + i * 256;
+      const int half = ch / (kChunks / 2), rem = ch % (kChunks / 2);
+      const int r = rem / (hd / 4), q4 = rem % (hd / 4);
+      *reinterpret_cast<float4*>(buf + (size_t)half * 32 * rs + (size_t)r * rs + q4 * 4) = v[i];
+    }
+  }
+};
+
+template <int J, typename T>
+__global__ void __launch_bounds__(256) k_prompt_attention(const PromptAttnArgs a) {
+  extern __shared__ __align__(16) float pa_smem[];
+  const int hd = 32 * J, rs = pa_row_stride<J>();
+  const int kvh = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int hb = (kvh * a.n_head + a.n_kv - 1) / a.n_kv;
+  const int he = ((kvh + 1) * a.n_head + a.n_kv - 1) / a.n_kv;
+  const int G = he - hb;
+  float* sq = pa_smem;                             // [kPaTokens][G][hd]
+  float* tiles = pa_smem + (size_t)kPaTokens * G * hd;  // [2 buffers][K, V][32][rs]
+  const int t = blockIdx.y * kPaTokens + warp;
+  const bool tok = t < a.T;
+  const int kv_dim = a.n_kv * hd, kv_off = kvh * hd;
+  const int nblk_max = attn_n_blocks(a.ctx), stride_part = attn_part_stride(hd);
+  const T* kc = static_cast<const T*>(a.k_cache);
+  const T* vc = static_cast<const T*>(a.v_cache);
+  pdl_wait();
+  // positions: this warp's token and the CTA's last one
+  __shared__ int maxpos_s;
+  if (threadIdx.x == 0) {
+    int mx = -1;
+    for (int w = 0; w < kPaTokens; ++w) {
+      const int tt = blockIdx.y * kPaTokens + w;
+      if (tt < a.T) mx = max(mx, min(a.pos[tt], a.ctx - 1));
+    }
+    maxpos_s = mx;
+  }
+  for (int i = threadIdx.x; i < kPaTokens * G * hd; i += 256) {
+    const int w = i / (G * hd), rem = i % (G * hd);
+    const int tt = blockIdx.y * kPaTokens + w;
+    sq[i] = tt < a.T ? a.q[(size_t)tt * a.q_stride + (size_t)hb * hd + rem] : 0.0f;
+  }
+  __syncthreads();
+  const int rows = maxpos_s + 1;
+  const int nb_cta = attn_n_blocks(rows);
+  const int pos = tok ? min(a.pos[t], a.ctx - 1) : -1;
+  const int n_pos = pos + 1, nb = tok ? attn_n_blocks(n_pos) : 0;
+
+  PaStage<J, T> stage;
+  if (nb_cta > 0) {
+    stage.load(kc, vc, kv_dim, kv_off, 0, rows);
+    stage.store(tiles);
+  }
+  __syncthreads();
+  for (int c = 0; c < nb_cta; ++c) {
+    const float* kt = tiles + (size_t)(c & 1) * 2 * 32 * rs;
+    const float* vt = kt + (size_t)32 * rs;
+    if (c + 1 < nb_cta) stage.load(kc, vc, kv_dim, kv_off, c + 1, rows);
+    if (c < nb) {
+      const bool valid = c * 32 + lane < n_pos;
+      for (int g0 = 0; g0 < G; g0 += kPaHeads) {
+        float sc[kPaHeads];
+#pragma unroll
+        for (int g = 0; g < kPaHeads; ++g) sc[g] = 0.0f;
+        const float* krow = kt + (size_t)lane * rs;
+#pragma unroll 8
+        for (int d4 = 0; d4 < hd / 4; ++d4) {
+          const float4 k = *reinterpret_cast<const float4*>(krow + d4 * 4);
+#pragma unroll
+          for (int g = 0; g < kPaHeads; ++g) {
+            if (g0 + g < G) {
+              const float4 q = *reinterpret_cast<const float4*>(sq + ((size_t)warp * G + g0 + g) * hd + d4 * 4);
+              sc[g] = __fmaf_rn(q.x, k.x, sc[g]);
+              sc[g] = __fmaf_rn(q.y, k.y, sc[g]);
+              sc[g] = __fmaf_rn(q.z, k.z, sc[g]);
+              sc[g] = __fmaf_rn(q.w, k.w, sc[g]);
+            }
+          }
+        }
+        float p[kPaHeads], acc[kPaHeads][J];
+#pragma unroll
+        for (int g = 0; g < kPaHeads; ++g) {
+          const float s = valid ? __fmul_rn(sc[g], a.scale) : -INFINITY;
+          const float m = warp_max(s);
+          p[g] = valid ? expf_det(__fsub_rn(s, m)) : 0.0f;
+          const float l = __shfl_sync(0xffffffffu, warp_sum(p[g]), 0);
+          if (g0 + g < G && lane == 0) {
+            float* dst = a.partial + (((size_t)t * a.n_head + hb + g0 + g) * nblk_max + c) * stride_part;
+            dst[0] = m;
+            dst[1] = l;
+          }
+#pragma unroll
+          for (int jj = 0; jj < J; ++jj) acc[g][jj] = 0.0f;
+        }
+#pragma unroll 4
+        for (int i = 0; i < 32; ++i) {
+          float v[J];
+          load_v<J, float>(vt + (size_t)i * rs + lane * J, v);
+#pragma unroll
+          for (int g = 0; g < kPaHeads; ++g) {
+            const float pt = __shfl_sync(0xffffffffu, p[g], i);
+#pragma unroll
+            for (int jj = 0; jj < J; ++jj) acc[g][jj] = __fmaf_rn(pt, v[jj], acc[g][jj]);
+          }
+        }
+#pragma unroll
+        for (int g = 0; g < kPaHeads; ++g) {
+          if (g0 + g < G) {
+            float* dst = a.partial + (((size_t)t * a.n_head + hb + g0 + g) * nblk_max + c) * stride_part + 4 + lane * J;
+#pragma unroll
+            for (int jj = 0; jj < J; ++jj) dst[jj] = acc[g][jj];
+          }
+        }
+      }
+    }
+    __syncthreads();  // every warp is done with the buffer the next store overwrites
+    if (c + 1 < nb_cta) stage.store(tiles + (size_t)((c + 1) & 1) * 2 * 32 * rs);
+    __syncthreads();
+  }
+  // merge each (token, head) over its blocks in block order
+  if (tok) {
+    for (int g = 0; g < G; ++g) {
+      const float* hp = a.partial + ((size_t)t * a.n_head + hb + g) * nblk_max * stride_part;
+      for (int u = 0; u < J; ++u) {
+        const int d = u * 32 + lane;
+        const float o = merge_blocks(
+            nb, lane, [&](int c) { return __ldcg(hp + (size_t)c * stride_part); },
+            [&](int c) { return __ldcg(hp + (size_t)c * stride_part + 1); },
+            [&](int c) { return __ldcg(hp + (size_t)c * stride_part + 4 + d); });
+        a.out[(size_t)t * a.out_stride + (size_t)(hb + g) * hd + d] = o;
+      }
+    }
+  }
+  pdl_launch_dependents();
+}
+
+
 // Cluster launch: grid (n_kv, n_split, batch) in clusters of (1, n_split, 1),
 // with programmatic dependent launch when pdl is set.
 template <typename Kern>
@@ -1006,6 +1199,8 @@ cudaError_t init_jt(int dev) {
   cudaError_t e = cudaFuncSetAttribute(k_attention<J, T, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mx);
   if (e != cudaSuccess) return e;
   if constexpr (J >= 2) {
+    e = cudaFuncSetAttribute(k_prompt_attention<J, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, kDynSmemMax);
+    if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(k_attention<J, T, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kDynSmemMax);
     if (e != cudaSuccess) return e;
     const bool nonportable =
@@ -1074,6 +1269,32 @@ cudaError_t init_j(int dev) {
 
 size_t attn_partial_floats(int n_head, int n_blocks, int head_dim) {
   return (size_t)n_head * n_blocks * attn_part_stride(head_dim);
+}
+
+namespace {
+
+template <int J, typename T>
+cudaError_t launch_prompt_attention_jt(const PromptAttnArgs& a, int G, cudaStream_t st) {
+  const size_t smem = pa_smem_bytes<J, T>(G);
+  if (smem > (size_t)kDynSmemMax) return cudaErrorInvalidValue;
+  return launch_k(k_prompt_attention<J, T>, dim3(a.n_kv, (a.T + kPaTokens - 1) / kPaTokens), dim3(256), smem, st, true,
+                  a);
+}
+
+}  // namespace
+
+cudaError_t launch_prompt_attention(const PromptAttnArgs& a, cudaStream_t st) {
+  if (!a.q || !a.k_cache || !a.v_cache || !a.pos || !a.partial || !a.out || a.T < 1 || a.n_kv < 1 ||
+      a.n_head < a.n_kv || a.n_head % a.n_kv || a.n_head / a.n_kv > kGMax || a.ctx < 1 ||
+      (a.head_dim != 64 && a.head_dim != 128 && a.head_dim != 256))
+    return cudaErrorInvalidValue;
+  const int G = a.n_head / a.n_kv;
+  const bool f16 = a.kv_f16 != 0;
+  switch (a.head_dim) {
+    case 64: return f16 ? launch_prompt_attention_jt<2, __half>(a, G, st) : launch_prompt_attention_jt<2, float>(a, G, st);
+    case 128: return f16 ? launch_prompt_attention_jt<4, __half>(a, G, st) : launch_prompt_attention_jt<4, float>(a, G, st);
+    default: return f16 ? launch_prompt_attention_jt<8, __half>(a, G, st) : launch_prompt_attention_jt<8, float>(a, G, st);
+  }
 }
 
 cudaError_t attention_init() {

@@ -70,4 +70,25 @@ size_t attn_partial_floats(int n_head, int n_blocks, int head_dim);
 cudaError_t attention_init();
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st, bool pdl = false);
 
+// Attention of T prompt tokens at positions pos[0..T) over a cache that
+// already holds their K/V rows: per token the decode attention's arithmetic
+// (same blocks, fma orders, softmax and block merge, so the same bits), but
+// one CTA serves 8 tokens of a kv head and reads each K/V block once for
+// them.  head_dim 64, 128 or 256.
+struct PromptAttnArgs {
+  const float* q;  // [T][q_stride], heads of head_dim after QK-norm and RoPE
+  int q_stride;
+  const void* k_cache;  // one layer's cache [ctx][n_kv*head_dim], f32 or f16
+  const void* v_cache;
+  int kv_f16;
+  const int* pos;  // [T]
+  int T;
+  int n_head, n_kv, head_dim, ctx;
+  float scale;
+  float* partial;  // [T][n_head][attn_n_blocks(ctx)][attn_part_stride(head_dim)]
+  float* out;      // [T][out_stride]
+  int out_stride;
+};
+cudaError_t launch_prompt_attention(const PromptAttnArgs& a, cudaStream_t st);
+
 }  // namespace mcpo

@@ -2690,30 +2690,50 @@ int prefill_chunk(Ctx* c, Model& m, const uint32_t* toks, int n, size_t p0, bool
                              m.rope_sin, cf.rope_freq_base, cf.rope_freq_scale, m.pf_pos, kc, vc, cf.kv_f16, s),
             "prefill_qk"))
       return 0;
-    AttnArgs at{};
-    at.q = m.pf_q;
-    at.fuse_norm_rope_append = 0;
-    at.k_cache = kc;
-    at.v_cache = vc;
-    at.kv_f16 = cf.kv_f16;
-    at.pos_ptr = m.pf_pos;
-    at.pos_stride = 1;
-    at.n_head = (int)cf.heads;
-    at.n_kv = (int)cf.kv_heads;
-    at.head_dim = hd;
-    at.ctx = (int)cf.context;
-    at.n_split = std::min(m.n_split, pf_split_cfg());
-    at.cluster = 0;
-    at.scale = 1.0f / sqrtf((float)hd);
-    at.partial = m.pf_partial;
-    at.counters = m.pf_counters;
-    at.out = m.pf_attn;
-    at.batch = n;
-    at.qkv_bstride = (size_t)qd;
-    at.cache_bstride = 0;
-    at.out_bstride = (size_t)qd;
-    at.err = m.pf_err;
-    if (!ok(launch_attention(at, s, false), "prefill_attention")) return 0;
+    if (hd == 64 || hd == 128 || hd == 256) {  // 8 tokens of a kv head per CTA, K/V blocks read once for them
+      PromptAttnArgs pa{};
+      pa.q = m.pf_q;
+      pa.q_stride = qd;
+      pa.k_cache = kc;
+      pa.v_cache = vc;
+      pa.kv_f16 = cf.kv_f16;
+      pa.pos = m.pf_pos;
+      pa.T = n;
+      pa.n_head = (int)cf.heads;
+      pa.n_kv = (int)cf.kv_heads;
+      pa.head_dim = hd;
+      pa.ctx = (int)cf.context;
+      pa.scale = 1.0f / sqrtf((float)hd);
+      pa.partial = m.pf_partial;
+      pa.out = m.pf_attn;
+      pa.out_stride = qd;
+      if (!ok(launch_prompt_attention(pa, s), "prefill_prompt_attention")) return 0;
+    } else {
+      AttnArgs at{};
+      at.q = m.pf_q;
+      at.fuse_norm_rope_append = 0;
+      at.k_cache = kc;
+      at.v_cache = vc;
+      at.kv_f16 = cf.kv_f16;
+      at.pos_ptr = m.pf_pos;
+      at.pos_stride = 1;
+      at.n_head = (int)cf.heads;
+      at.n_kv = (int)cf.kv_heads;
+      at.head_dim = hd;
+      at.ctx = (int)cf.context;
+      at.n_split = std::min(m.n_split, pf_split_cfg());
+      at.cluster = 0;
+      at.scale = 1.0f / sqrtf((float)hd);
+      at.partial = m.pf_partial;
+      at.counters = m.pf_counters;
+      at.out = m.pf_attn;
+      at.batch = n;
+      at.qkv_bstride = (size_t)qd;
+      at.cache_bstride = 0;
+      at.out_bstride = (size_t)qd;
+      at.err = m.pf_err;
+      if (!ok(launch_attention(at, s, false), "prefill_attention")) return 0;
+    }
     if (tc) {
       const Model::PgLayer& P = m.pg[li];
       if (!ok(launch_pgemm_act(m.pf_attn, qd, n, nullptr, 0, 0.0f, m.pg_q, s), "prefill_act_o") ||
