@@ -984,7 +984,7 @@ struct PaStage {
 };
 
 template <int J, typename T>
-__global__ void __launch_bounds__(256) k_prompt_attention(const PromptAttnArgs a) {
+__global__ void __launch_bounds__(256, 2) k_prompt_attention(const PromptAttnArgs a) {
   extern __shared__ __align__(16) float pa_smem[];
   const int hd = 32 * J, rs = pa_row_stride<J>();
   const int kvh = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1200,6 +1200,9 @@ cudaError_t init_jt(int dev) {
   if (e != cudaSuccess) return e;
   if constexpr (J >= 2) {
     e = cudaFuncSetAttribute(k_prompt_attention<J, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, kDynSmemMax);
+    if (e != cudaSuccess) return e;
+    // two CTAs per SM (the staging and the per-token work are latency-bound)
+    e = cudaFuncSetAttribute(k_prompt_attention<J, T>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(k_attention<J, T, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kDynSmemMax);
     if (e != cudaSuccess) return e;
