@@ -375,7 +375,8 @@ def run_batch_bench(args, shape, world, rank, local, dist, barrier) -> int:
     t_gen = time.perf_counter() - t_gen
     t_load = time.perf_counter()
     ctx = max(4096, prompt_len + args.warmup + 2 * args.steps + 8)
-    rt = Qwen3Runtime.open(tensors, shape=shape, device_index=local, context=ctx, kv_f16=True, max_batch=B)
+    rt = Qwen3Runtime.open(tensors, shape=shape, device_index=local, context=ctx, kv_f16=True, max_batch=B,
+                           batch_exact=args.batch_exact)
     t_load = time.perf_counter() - t_load
     g = rt.gpu
     prompts = np.stack([gguf.prompt_ids(prompt_len, shape.vocab, seed=7 + 1000 * rank + b) for b in range(B)])
@@ -439,7 +440,8 @@ def run_batch_bench(args, shape, world, rank, local, dist, barrier) -> int:
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "q8_0 weights and activations as f16 on tcgen05 (f32 accumulate); f16 KV",
+        "dtype": ("q8_0 x q8_1 int8 block dots on tcgen05 kind::i8 (single-sequence bits); f16 KV" if args.batch_exact
+                  else "q8_0 weights and activations as f16 on tcgen05 (f32 accumulate); f16 KV"),
         "data": f"synthetic: seeded N(0,0.02) weights quantised Q8_0, {B} x {prompt_len} uniform random prompt ids",
         "config": {
             "workload": f"qwen3-8b-shape all-Q8_0 batched greedy decode, B={B}, prompt {prompt_len}, f16 KV at "
@@ -497,6 +499,9 @@ def main() -> int:
     ap.add_argument("--batch", type=int, default=0,
                     help="BASELINE config 3: batched decode of this many sequences (2..32), all-Q8_0 weights on the "
                          "tensor cores, f16 KV, prompt 1024 unless --prompt is given")
+    ap.add_argument("--batch-exact", action="store_true",
+                    help="with --batch: the projections as the prompt prefill runs them (int8 block dots; every "
+                         "sequence bit-identical to its single-sequence decode)")
     ap.add_argument("--prefill", action="store_true",
                     help="time the multi-token prompt prefill (qwen3_prefill) of --prompt ids on 1 GPU against "
                          "the token-by-token forwards over the same positions; one JSON line")

@@ -172,7 +172,12 @@ typedef struct minicpmo_qwen3_config {
                                GEMVs (one GPU, tiled weights, head_dim % 32 == 0;
                                the bind fails otherwise).  Same results in every
                                mode. */
-    int reserved[5];
+    int batch_exact;        /* with max_batch: 1 runs the batch's projections as the
+                               prompt prefill does (int8 block dots on the tensor
+                               cores), so every sequence gets the single-sequence
+                               decode's bits (slower: about 0.8x at 32 sequences);
+                               0: f16 operands on the tensor cores (within 1e-3) */
+    int reserved[4];
 } minicpmo_qwen3_config;
 
 MINICPMO_API int minicpmo_gpu_context_qwen3_bind(void *handle, const minicpmo_qwen3_config *config, char *error, size_t error_cap);

@@ -80,6 +80,10 @@ struct BatchState {
   int am_grid = 0;
   cudaGraphExec_t exec[2] = {nullptr, nullptr};
   int kernels[2] = {0, 0};
+  // projections on the prefill tensor-core path (pgemm.cuh): the same bits
+  // as the single-sequence decode; else the f16 tensor-core GEMM (gemm.cuh)
+  bool pg = false;
+  float* gbuf = nullptr;  // gate outputs [B][ffn]
 };
 
 struct Model {
@@ -112,6 +116,7 @@ struct Model {
   };
   std::vector<PgLayer> pg;
   PgemmAct pg_h, pg_q, pg_f;  // activation operands of K = hidden, q columns, ffn
+  PgemmMat pg_out;            // the lm_head's operand copy (batched decode)
   bool pg_failed = false;
   long long pf_tc_passes = 0, pf_gemv_passes = 0;
   int *pf_tok = nullptr, *pf_pos = nullptr, *pf_err = nullptr;
@@ -502,7 +507,7 @@ void free_batch(BatchState* b) {
   for (auto& e : b->exec)
     if (e) cudaGraphExecDestroy(e), e = nullptr;
   void* bufs[] = {b->hidden, b->qkv, b->attn, b->gu, b->logits, b->x16, b->part, b->cnt, b->kc, b->vc,
-                  b->attn_partial, b->attn_counters, b->st, b->am_scratch, b->am_counter, b->history};
+                  b->attn_partial, b->attn_counters, b->st, b->am_scratch, b->am_counter, b->history, b->gbuf};
   for (void* p : bufs)
     if (p) cudaFree(p);
   if (b->st_host) cudaFreeHost(b->st_host);
@@ -530,6 +535,7 @@ void free_model(Model* m) {
   pgemm_act_free(&m->pg_h);
   pgemm_act_free(&m->pg_q);
   pgemm_act_free(&m->pg_f);
+  pgemm_free(&m->pg_out);
   if (m->st_host) cudaFreeHost(m->st_host);
   for (auto& u : m->shards)
     if (u->dev && !u->view) cudaFree(u->dev);
@@ -881,11 +887,21 @@ cudaError_t record_batch_step(Ctx* c, Model& m, bool logits) {
   REC(launch_embed(m.tok->dev, m.tok->geom, m.tok->dtype, (int)m.tok->rows, h, &b.st[0].token, 0, b.hidden, s, true, B,
                    sst));
   const size_t esz = cf.kv_f16 ? 2 : 4;
+  int* perr = &b.st[0].err;
+  const int ldq = (int)b.ldqkv;
   for (uint32_t li = 0; li < cf.layers; ++li) {
     LayerW& L = m.layer[li];
-    REC(launch_rmsnorm_x16(b.hidden, h, L.attn_norm->dev, L.attn_norm->dtype, B, h, cf.rms_eps, N, b.x16, s, true));
-    Upload* qkv[3] = {L.q, L.k, L.v};
-    REC(batch_gemm(c, m, qkv, 3, h, b.qkv, (int)b.ldqkv, kGemmStore));
+    if (b.pg) {
+      const Model::PgLayer& P = m.pg[li];
+      REC(launch_pgemm_act(b.hidden, h, B, L.attn_norm->dev, L.attn_norm->dtype, cf.rms_eps, m.pg_h, s));
+      REC(launch_pgemm(P.q, m.pg_h, B, kPgStore, b.qkv, ldq, nullptr, 0, perr, s));
+      REC(launch_pgemm(P.k, m.pg_h, B, kPgStore, b.qkv + qd, ldq, nullptr, 0, perr, s));
+      REC(launch_pgemm(P.v, m.pg_h, B, kPgStore, b.qkv + qd + kvd, ldq, nullptr, 0, perr, s));
+    } else {
+      REC(launch_rmsnorm_x16(b.hidden, h, L.attn_norm->dev, L.attn_norm->dtype, B, h, cf.rms_eps, N, b.x16, s, true));
+      Upload* qkv[3] = {L.q, L.k, L.v};
+      REC(batch_gemm(c, m, qkv, 3, h, b.qkv, (int)b.ldqkv, kGemmStore));
+    }
     AttnArgs a{};
     a.q = b.qkv;
     a.k = b.qkv + qd;
@@ -922,6 +938,17 @@ cudaError_t record_batch_step(Ctx* c, Model& m, bool logits) {
     a.out_bstride = (size_t)qd;
     a.err = &b.st[0].err;
     REC(launch_attention(a, s, true));
+    if (b.pg) {
+      const Model::PgLayer& P = m.pg[li];
+      REC(launch_pgemm_act(b.attn, qd, B, nullptr, 0, 0.0f, m.pg_q, s));
+      REC(launch_pgemm(P.o, m.pg_q, B, kPgAdd, b.hidden, h, nullptr, 0, perr, s));
+      REC(launch_pgemm_act(b.hidden, h, B, L.ffn_norm->dev, L.ffn_norm->dtype, cf.rms_eps, m.pg_h, s));
+      REC(launch_pgemm(P.gate, m.pg_h, B, kPgStore, b.gbuf, f, nullptr, 0, perr, s));
+      REC(launch_pgemm(P.up, m.pg_h, B, kPgSwiglu, b.gu, f, b.gbuf, f, perr, s));
+      REC(launch_pgemm_act(b.gu, f, B, nullptr, 0, 0.0f, m.pg_f, s));
+      REC(launch_pgemm(P.down, m.pg_f, B, kPgAdd, b.hidden, h, nullptr, 0, perr, s));
+      continue;
+    }
     REC(launch_pack_x16(b.attn, qd, B, qd, N, b.x16, s, true));
     Upload* o[1] = {L.o};
     REC(batch_gemm(c, m, o, 1, qd, b.hidden, h, kGemmAdd));
@@ -933,9 +960,14 @@ cudaError_t record_batch_step(Ctx* c, Model& m, bool logits) {
     REC(batch_gemm(c, m, dn, 1, f, b.hidden, h, kGemmAdd));
   }
   if (logits) {
-    REC(launch_rmsnorm_x16(b.hidden, h, m.out_norm->dev, m.out_norm->dtype, B, h, cf.rms_eps, N, b.x16, s, true));
-    Upload* lm[1] = {m.out};
-    REC(batch_gemm(c, m, lm, 1, h, b.logits, (int)cf.vocab, kGemmStore));
+    if (b.pg) {
+      REC(launch_pgemm_act(b.hidden, h, B, m.out_norm->dev, m.out_norm->dtype, cf.rms_eps, m.pg_h, s));
+      REC(launch_pgemm(m.pg_out, m.pg_h, B, kPgStore, b.logits, (int)cf.vocab, nullptr, 0, perr, s));
+    } else {
+      REC(launch_rmsnorm_x16(b.hidden, h, m.out_norm->dev, m.out_norm->dtype, B, h, cf.rms_eps, N, b.x16, s, true));
+      Upload* lm[1] = {m.out};
+      REC(batch_gemm(c, m, lm, 1, h, b.logits, (int)cf.vocab, kGemmStore));
+    }
     REC(launch_argmax(b.logits, (int)cf.vocab, nullptr, b.am_scratch, b.am_counter, b.st, b.history, b.history_cap,
                       b.am_grid, s, true, 0, nullptr, B));
   }
@@ -966,6 +998,9 @@ int build_batch_graph(Ctx* c, Model& m, int which, char* err, size_t cap) {
 // Batched decode set-up for cfg.max_batch > 1: every linear weight Q8_0
 // (rows a multiple of 128, inputs of 256), a raw-row device copy of each,
 // per-sequence caches and states, and the two step graphs.
+bool pg_build(Ctx* c, Model& m);
+bool prefill_ok(const Model& m);
+
 int bind_batch(Ctx* c, Model& m, char* err, size_t cap) {
   const auto& cf = m.cfg;
   const int B = cf.max_batch;
@@ -1035,6 +1070,18 @@ int bind_batch(Ctx* c, Model& m, char* err, size_t cap) {
   }
   if (!cuda_ok(c, cudaMallocHost((void**)&b.st_host, B * sizeof(StepState)), "qwen3_bind_batch_pinned", err, cap))
     return 0;
+  // batch_exact: the projections on the prefill tensor-core path (the
+  // single-sequence decode's bits)
+  if (cf.batch_exact) {
+    if (!m.out->tiled || !prefill_ok(m) || !pg_build(c, m) ||
+        pgemm_build(m.out->geom, m.out->dev, &m.pg_out, c->stream) != cudaSuccess ||
+        cudaMalloc((void**)&b.gbuf, (size_t)B * f * 4) != cudaSuccess) {
+      cudaGetLastError();
+      return fail(c, err, cap, "error: qwen3 bind: batch_exact needs the tiled weight layouts and device memory for "
+                               "their int8 operand copies");
+    }
+    b.pg = true;
+  }
   memset(b.st_host, 0, B * sizeof(StepState));
   c->stats.kv_device_bytes += 2 * kv_bytes;
   if (!cuda_ok(c, cudaStreamSynchronize(c->stream), "qwen3_bind_batch_sync", err, cap)) return 0;

@@ -29,6 +29,7 @@
 #include "pgemm.cuh"
 
 #include <cuda_fp16.h>
+#include <stdlib.h>
 
 #include "common.cuh"
 #include "gemv.cuh"
@@ -43,6 +44,7 @@ constexpr int kPgEpiWarps = 16;
 constexpr int kPgThreads = (2 + kPgEpiWarps) * 32;
 constexpr uint32_t kPgTmemCols = 512;  // two buffers x eight 32-column regions
 constexpr int kPgLevels = 6;           // reduction-tree levels for lpr <= 32
+constexpr int kPgMaxSplit = 16;        // CTAs per row tile at most (the roots fit a tree-stack column)
 // Tree levels 1 .. kPgLevels-1 live in shared memory ([level][token][thread]
 // floats, each thread its own column); level 0 and the lane sums in
 // registers.
@@ -76,6 +78,13 @@ struct PgArgs {
   const float* gate;
   int ldg;
   int* err;
+  // split over the GEMV lanes (ksplit > 1): CTA z takes the lanes' subtree
+  // z of the reduction tree and writes its root to part; the last CTA of a
+  // (row tile, token tile) adds the roots in tree order (cnt: arrivals,
+  // zero at rest)
+  int ksplit, lsplit;
+  float* part;
+  unsigned* cnt;
 };
 
 // Instruction descriptor of kind::i8: s8 A and B (K-major), s32
@@ -152,8 +161,9 @@ __global__ void __launch_bounds__(kPgThreads, 1) k_pgemm(const PgArgs p) {
   constexpr int kUnits = kQ6 ? 2 : 1;  // MMA units per super-block
   constexpr int kBBytes = kQ6 ? 2 * kPgBBytes : kPgBBytes;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tile = blockIdx.x, ttile = blockIdx.y;
+  const int tile = blockIdx.x, ttile = blockIdx.y, z = blockIdx.z;
   const int nsb = p.nb;
+  const int n_it = nsb >> p.lsplit, it0 = z * n_it, it1 = it0 + n_it;  // this CTA's super-blocks
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kPgStages; ++i) {
@@ -181,20 +191,20 @@ __global__ void __launch_bounds__(kPgThreads, 1) k_pgemm(const PgArgs p) {
       const uint64_t policy = l2_evict_first_policy();
       const uint32_t tx = (uint32_t)(kPgABytes + kPgSBytes + kBBytes + kPgXFloats * 4);
       int issued = 0;
-      for (int it = 0; it < nsb; ++it) {
-        const int sb = pg_sb_at(it, p.ks, p.levels);
-        const int s = it % kPgStages;
-        if (it >= kPgStages && !gwait(&empty[s], (uint32_t)((it / kPgStages) - 1) & 1u, p.err, abort_s)) break;
+      for (int j = 0; j < n_it; ++j) {
+        const int sb = pg_sb_at(it0 + j, p.ks, p.levels);
+        const int s = j % kPgStages;
+        if (j >= kPgStages && !gwait(&empty[s], (uint32_t)((j / kPgStages) - 1) & 1u, p.err, abort_s)) break;
         const size_t wt = (size_t)tile * nsb + sb, xt = (size_t)ttile * nsb + sb;
         mbar_arrive_expect_tx(&full[s], tx);
         bulk_load_hint(smem + L::a(s), p.a + wt * kPgABytes, kPgABytes, &full[s], policy);
         bulk_load(smem + L::sc(s), p.s + wt * kPgSBytes, kPgSBytes, &full[s]);
         bulk_load(smem + L::b(s), p.b + xt * kBBytes, kBBytes, &full[s]);
         bulk_load(smem + L::x(s), p.xs + xt * kPgXFloats, kPgXFloats * 4, &full[s]);
-        issued = it + 1;
+        issued = j + 1;
       }
-      for (int it = issued > kPgStages ? issued - kPgStages : 0; it < issued; ++it)
-        if (!mbar_wait(&full[it % kPgStages], (uint32_t)(it / kPgStages) & 1u, p.err)) break;
+      for (int j = issued > kPgStages ? issued - kPgStages : 0; j < issued; ++j)
+        if (!mbar_wait(&full[j % kPgStages], (uint32_t)(j / kPgStages) & 1u, p.err)) break;
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -202,9 +212,9 @@ __global__ void __launch_bounds__(kPgThreads, 1) k_pgemm(const PgArgs p) {
     if (lane == 0) {
       int u = 0;
       bool ok = true;
-      for (int it = 0; it < nsb && ok; ++it) {
-        const int s = it % kPgStages;
-        if (!gwait(&full[s], (uint32_t)(it / kPgStages) & 1u, p.err, abort_s)) break;
+      for (int j = 0; j < n_it && ok; ++j) {
+        const int s = j % kPgStages;
+        if (!gwait(&full[s], (uint32_t)(j / kPgStages) & 1u, p.err, abort_s)) break;
         tc_fence_after();
         const uint32_t a0 = smem_addr(smem + L::a(s)), b0 = smem_addr(smem + L::b(s));
         for (int h = 0; h < kUnits; ++h, ++u) {
@@ -245,9 +255,9 @@ __global__ void __launch_bounds__(kPgThreads, 1) k_pgemm(const PgArgs p) {
     float* sst = reinterpret_cast<float*>(smem + L::stack()) + (threadIdx.x - 64);
     int cnt = 0, u = 0;
     bool go = true;
-    for (int it = 0; it < nsb; ++it) {
-      const int s = it % kPgStages;
-      if (!__all_sync(0xffffffffu, gwait(&full[s], (uint32_t)(it / kPgStages) & 1u, p.err, abort_s))) {
+    for (int it = it0; it < it1; ++it) {
+      const int s = (it - it0) % kPgStages;
+      if (!__all_sync(0xffffffffu, gwait(&full[s], (uint32_t)((it - it0) / kPgStages) & 1u, p.err, abort_s))) {
         go = false;
         break;
       }
@@ -371,21 +381,55 @@ __global__ void __launch_bounds__(kPgThreads, 1) k_pgemm(const PgArgs p) {
         ++cnt;
       }
     }
-    if (go && !*abort_s) {
+    const int top = p.levels - p.lsplit;  // the level of this CTA's subtree root
+    float val[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) val[e] = top == 0 ? lvl0[e] : sst[((top - 1) * 8 + e) * (kPgEpiWarps * 32)];
+    bool store = go && !*abort_s;
+    if (p.ksplit > 1) {
+      // roots of the subtrees: [z][tile][ttile][token][row]; every CTA
+      // arrives (also after an abort, so the count returns to zero)
+      __shared__ unsigned ticket_s;
+      const size_t tt_idx = (size_t)tile * gridDim.y + ttile, ntt = (size_t)gridDim.x * gridDim.y;
+      float* mine = p.part + (((size_t)z * ntt + tt_idx) * kPgTok + tg * 8) * kPgRows + rl;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) mine[(size_t)e * kPgRows] = val[e];
+      __threadfence();
+      asm volatile("bar.sync 1, %0;" ::"n"(kPgEpiWarps * 32) : "memory");
+      if (threadIdx.x == 64) ticket_s = atomicAdd(p.cnt + tt_idx, 1u);
+      asm volatile("bar.sync 1, %0;" ::"n"(kPgEpiWarps * 32) : "memory");
+      const bool last = ticket_s == (unsigned)(p.ksplit - 1);
+      if (last) {
+        __threadfence();
+        if (threadIdx.x == 64) p.cnt[tt_idx] = 0u;
+        // the upper levels of the butterfly: adjacent roots pairwise, the
+        // earlier one in front (in this thread's column of the tree stack,
+        // which the loop above no longer needs)
+        constexpr int kStride = kPgEpiWarps * 32;
+        for (int e = 0; e < 8; ++e) {
+          for (int q = 0; q < p.ksplit; ++q)
+            sst[q * kStride] = __ldcg(p.part + (((size_t)q * ntt + tt_idx) * kPgTok + tg * 8 + e) * kPgRows + rl);
+          for (int w = 1; w < p.ksplit; w <<= 1)
+            for (int q = 0; q + w < p.ksplit; q += 2 * w) sst[q * kStride] = __fadd_rn(sst[q * kStride], sst[(q + w) * kStride]);
+          val[e] = sst[0];
+        }
+      }
+      store = store && last;
+    }
+    if (store) {
       pdl_wait();  // y and gate come from earlier kernels
       const int row = tile * kPgRows + rl;
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        const float val = p.levels == 0 ? lvl0[e] : sst[((p.levels - 1) * 8 + e) * (kPgEpiWarps * 32)];
         const int t = ttile * kPgTok + tg * 8 + e;
         if (t < p.T && row < p.rows) {
           float* yp = p.y + (size_t)t * p.ldy + row;
           if (p.epi == kPgStore)
-            *yp = val;
+            *yp = val[e];
           else if (p.epi == kPgAdd)
-            *yp = __fadd_rn(*yp, val);
+            *yp = __fadd_rn(*yp, val[e]);
           else
-            *yp = silu_mul_det(p.gate[(size_t)t * p.ldg + row], val);
+            *yp = silu_mul_det(p.gate[(size_t)t * p.ldg + row], val[e]);
         }
       }
     }
@@ -460,11 +504,14 @@ __global__ void __launch_bounds__(kPgRows) k_pgemm_relayout(const uint8_t* src, 
   st[1] = s1;
 }
 
-// One CTA per token slot of the padded token tiles: RMSNorm (optional) and
-// Q8_1 quantisation in the decode GEMV's arithmetic (gemv_build_x: 256
+// One CTA per token slot of the padded token tiles and 64 blocks of 32
+// values: RMSNorm (optional; every CTA of a token computes the row's scale)
+// and Q8_1 quantisation in the decode GEMV's arithmetic (gemv_build_x: 256
 // strided partial sums, halving and warp trees, exact 1/sqrt; per block the
 // reference's variant-B quantiser), written as the B, Bm and X operands.
 // Slots past T are zeros.
+constexpr int kPgActBlocks = 64;
+
 __global__ void __launch_bounds__(256) k_pgemm_act(const float* x, int ldx, int T, int K, const void* nw, int ndt,
                                                    float eps, uint8_t* B, uint8_t* Bm, float* XS) {
   __shared__ float red[256];
@@ -472,6 +519,7 @@ __global__ void __launch_bounds__(256) k_pgemm_act(const float* x, int ldx, int 
   pdl_wait();
   const int n = blockIdx.x, t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const int nb = K / 256, tt = n / kPgTok, nn = n % kPgTok;
+  const int b0 = blockIdx.y * kPgActBlocks;  // this CTA's 32-value blocks
   const bool valid = n < T;
   const float* xr = x + (size_t)(valid ? n : 0) * ldx;
   float inv = 1.0f;
@@ -496,8 +544,8 @@ __global__ void __launch_bounds__(256) k_pgemm_act(const float* x, int ldx, int 
     __syncthreads();
     inv = inv_s;
   }
-  const int nblk = K / 32;
-  for (int bi = warp; bi < nblk; bi += 8) {
+  const int nblk = min(K / 32, b0 + kPgActBlocks);
+  for (int bi = b0 + warp; bi < nblk; bi += 8) {
     int q = 0;
     uint16_t dbits = 0;
     if (valid) {
@@ -585,9 +633,16 @@ cudaError_t pgemm_act_alloc(int tmax, int K, PgemmAct* a) {
   PgemmAct x;
   x.tmax = (int)(tt * kPgTok);
   x.K = K;
-  cudaError_t e = cudaMalloc((void**)&x.b, tt * nb * kPgBBytes);
+  int dev = 0, sms = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  x.split_ctas = sms;
+  if (e == cudaSuccess) e = cudaMalloc((void**)&x.b, tt * nb * kPgBBytes);
   if (e == cudaSuccess) e = cudaMalloc((void**)&x.bm, tt * nb * 2 * kPgBBytes);
   if (e == cudaSuccess) e = cudaMalloc((void**)&x.xs, tt * nb * kPgXFloats * 4);
+  if (e == cudaSuccess) e = cudaMalloc((void**)&x.part, (size_t)sms * kPgTok * kPgRows * 4);
+  if (e == cudaSuccess) e = cudaMalloc((void**)&x.cnt, (size_t)sms * 4);
+  if (e == cudaSuccess) e = cudaMemset(x.cnt, 0, (size_t)sms * 4);
   if (e != cudaSuccess) {
     pgemm_act_free(&x);
     return e;
@@ -601,17 +656,31 @@ void pgemm_act_free(PgemmAct* a) {
   if (a->b) cudaFree(a->b);
   if (a->bm) cudaFree(a->bm);
   if (a->xs) cudaFree(a->xs);
+  if (a->part) cudaFree(a->part);
+  if (a->cnt) cudaFree(a->cnt);
   a->b = a->bm = nullptr;
-  a->xs = nullptr;
+  a->xs = a->part = nullptr;
+  a->cnt = nullptr;
 }
 
 cudaError_t launch_pgemm_act(const float* x, int ldx, int T, const void* norm_w, int norm_dtype, float eps,
                              const PgemmAct& a, cudaStream_t st) {
   if (!x || T < 1 || T > a.tmax || !a.b || !a.bm || !a.xs || ldx < a.K) return cudaErrorInvalidValue;
   const int slots = (T + kPgTok - 1) / kPgTok * kPgTok;
-  return launch_k(k_pgemm_act, dim3(slots), dim3(256), 0, st, true, x, ldx, T, a.K, norm_w, norm_dtype, eps, a.b,
-                  a.bm, a.xs);
+  const int chunks = (a.K / 32 + kPgActBlocks - 1) / kPgActBlocks;
+  return launch_k(k_pgemm_act, dim3(slots, chunks), dim3(256), 0, st, true, x, ldx, T, a.K, norm_w, norm_dtype, eps,
+                  a.b, a.bm, a.xs);
 }
+
+namespace {
+int pgemm_split_cfg() {
+  static const int v = [] {
+    const char* e = getenv("MCPO_PG_SPLIT");
+    return (e && *e) ? (atoi(e) != 0 ? 1 : 0) : 1;
+  }();
+  return v;
+}
+}  // namespace
 
 cudaError_t launch_pgemm(const PgemmMat& w, const PgemmAct& x, int T, int epi, float* y, int ldy, const float* gate,
                          int ldg, int* err, cudaStream_t st) {
@@ -637,7 +706,17 @@ cudaError_t launch_pgemm(const PgemmMat& w, const PgemmAct& x, int T, int epi, f
   p.gate = gate;
   p.ldg = ldg;
   p.err = err;
-  const dim3 grid(w.tiles, (T + kPgTok - 1) / kPgTok);
+  // fewer CTAs than SMs: split each row tile over its lanes (bits do not
+  // change: the subtrees' roots are added in the tree's order)
+  const int ttiles = (T + kPgTok - 1) / kPgTok, ctas = w.tiles * ttiles;
+  int ks = 1;
+  while (pgemm_split_cfg() && x.part && ks * 2 <= w.lpr && ks * 2 <= kPgMaxSplit && ctas * ks * 2 <= x.split_ctas)
+    ks *= 2;
+  p.ksplit = ks;
+  p.lsplit = __builtin_ctz((unsigned)ks);
+  p.part = x.part;
+  p.cnt = x.cnt;
+  const dim3 grid(w.tiles, ttiles, ks);
   switch (w.dtype) {
     case kQ4_K: return launch_k(k_pgemm<kQ4_K>, grid, dim3(kPgThreads), PgSmem<kQ4_K>::bytes(), st, true, p);
     case kQ6_K: return launch_k(k_pgemm<kQ6_K>, grid, dim3(kPgThreads), PgSmem<kQ6_K>::bytes(), st, true, p);

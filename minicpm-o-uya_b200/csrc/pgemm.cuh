@@ -53,6 +53,13 @@ struct PgemmAct {
   uint8_t* b = nullptr;   // [ttiles][nb][kPgBBytes]
   uint8_t* bm = nullptr;  // [ttiles][nb][2][kPgBBytes]
   float* xs = nullptr;    // [ttiles][nb][kPgXFloats]
+  // launches with fewer CTAs than SMs split each row tile over the GEMV
+  // lanes (subtrees of the row's reduction tree) into at most split_ctas
+  // CTAs: their roots (split_ctas x 32 x 128 floats) and per-tile arrival
+  // counts (zero at rest)
+  int split_ctas = 0;
+  float* part = nullptr;
+  unsigned* cnt = nullptr;
 };
 
 enum PgemmEpi : int { kPgStore = 0, kPgAdd = 1, kPgSwiglu = 2 };

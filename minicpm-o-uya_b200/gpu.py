@@ -67,7 +67,8 @@ class Qwen3Config(C.Structure):
         ("kv_f16", i32),
         ("max_batch", i32),
         ("decode_mode", i32),
-        ("reserved", i32 * 5),
+        ("batch_exact", i32),
+        ("reserved", i32 * 4),
     ]
 
 

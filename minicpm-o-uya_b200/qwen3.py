@@ -50,7 +50,8 @@ class Qwen3Runtime:
     @classmethod
     def open(cls, weights, shape: Optional[Qwen3Shape] = None, device_index: int = 0, kv_f16: bool = False,
              context: Optional[int] = None, debug: bool = False, decode_mode: int = 0,
-             tp: Optional["TensorParallel"] = None, max_batch: int = 0) -> "Qwen3Runtime":
+             tp: Optional["TensorParallel"] = None, max_batch: int = 0,
+             batch_exact: bool = False) -> "Qwen3Runtime":
         """weights: a GGUF path/GgufFile, or a list of (name, dtype, rows, cols, uint8 bytes).
         decode_mode 0: the default (one kernel per operation); 1: one kernel per operation; 2: one
         persistent kernel per decode step where the model fits it; 3: per layer the attention and one
@@ -85,6 +86,7 @@ class Qwen3Runtime:
         cfg.kv_f16 = int(kv_f16)
         cfg.decode_mode = int(decode_mode)
         cfg.max_batch = int(max_batch)
+        cfg.batch_exact = int(bool(batch_exact))
         if tp is not None and tp.world > 1:
             handles = tp.all_gather(gpu.tp_buffer(shape.hidden))
             gpu.qwen3_bind_tp(cfg, tp.rank, tp.world, handles)
