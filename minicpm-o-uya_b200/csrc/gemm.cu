@@ -11,19 +11,23 @@
 //               128 rows x 8 blocks of a (row tile, K-tile) pair are one
 //               34816-byte block) and one bulk copy of the f16 activation
 //               tile (N x 256, already in the operand layout);
-//   warps 2..9  dequantise: thread = (row, quarter of the K-tile), q * d in
+//   warps 5..20 dequantise: thread = (row, quarter of the K-tile), q * d in
 //               f16 (int8 -> f16 exactly via the 0x6400 exponent trick, one
 //               rounding in the multiply), stored into the A stage in tensor
 //               memory (lane = row, tcgen05.st) -- no shared-memory operand;
-//   warp 1      one elected thread issues tcgen05.mma kind::f16 (M = 128,
-//               N = sequences, K = 16) with A read from tensor memory, into
-//               a 128 x N f32 accumulator in tensor memory, and releases
-//               stages with tcgen05.commit;
-//   epilogue    warps 2..9 read the accumulator with tcgen05.ld (lane = row,
-//               each warp half of the sequence columns)
-//               and store / add Y, or, with K split over several CTAs, write
-//               partial sums that the last CTA of the row tile adds in split
-//               order (deterministic).
+//   warps 1..4  MMA issue, one elected thread per warp and quarter q of
+//               every K-tile: tcgen05.mma kind::f16 (M = 128, N = sequences,
+//               K = 16) with A read from tensor memory, into the quarter's
+//               own 128 x N f32 accumulator in tensor memory; stages are
+//               released with tcgen05.commit.  A thread's MMAs follow one
+//               another about 230 cycles apart at any N (measured on the
+//               B200), while MMAs issued by different warps overlap, so four
+//               issuers carry four times the MMA rate of one;
+//   epilogue    warps 5..20 read the four accumulators with tcgen05.ld (lane
+//               = row, each warp a quarter of the sequence columns), add them
+//               in quarter order and store / add Y, or, with K split over
+//               several CTAs, write partial sums that the last CTA of the row
+//               tile adds in split order (deterministic).
 //
 // All waits are bounded (mbarrier try_wait with an iteration limit); a wait
 // that gives up raises the error word and a shared abort flag, the other
@@ -54,14 +58,21 @@ constexpr int kActStages = 4;   // f16 activation tiles in flight
 constexpr int kAStages = 8;     // f16 operand quarter-tiles (128 rows x 64 K) in tensor memory: two K-tiles
 constexpr int kRowPiece = 272;  // bytes of 256 values of one Q8_0 row
 constexpr int kRawBytes = kGemmTileRows * kRowPiece;     // 34816
-constexpr int kDqWarps = 8;  // dequantising / epilogue warps: 4 per 128-value half of a K-tile
-constexpr int kThreads = (2 + kDqWarps) * 32;
-// Tensor memory: the 128 x N f32 accumulator in columns [0, 32); A stage s
-// (128 rows x 64 f16, two per 32-bit column) in columns [32 + 32s, 64 + 32s)
-// -- quarter q of K-tile i in stage q + 4 (i & 1), so the dequantising warps
-// run a K-tile ahead of the MMAs.
+constexpr int kIssuers = 4;   // MMA issuing warps, one per 64-value quarter of a K-tile
+constexpr int kDqWarps = 16;  // dequantising / epilogue warps: 4 per quarter of a K-tile
+constexpr int kDq0 = 1 + kIssuers;  // first dequantising warp
+// the activation producer: a warp of its own, because a lane blocked in a
+// wait (the dependency wait, an mbarrier try_wait) holds up the other
+// divergent paths of its warp -- here the weight copies
+constexpr int kActWarp = kDq0 + kDqWarps;
+constexpr int kThreads = (kActWarp + 1) * 32;
+// Tensor memory: one 128 x N f32 accumulator per issuer (quarter q's in
+// columns [qN, qN + N)); A stage s (128 rows x 64 f16, two per 32-bit
+// column) in columns [128 + 32s, 160 + 32s) -- quarter q of K-tile i in
+// stage q + 4 (i & 1), so the dequantising warps run a K-tile ahead of the
+// MMAs.
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTmemA = 32;
+constexpr uint32_t kTmemA = kIssuers * kGemmMaxN;
 
 __host__ __device__ constexpr size_t act_bytes(int N) { return (size_t)N * kGemmKTile * 2; }
 
@@ -113,32 +124,26 @@ __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.
 
 
 
-// 16 consecutive f32 accumulator columns of this thread's lane.
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr)
-      : "memory");
+// NC (4 or 8) consecutive f32 accumulator columns of this thread's lane.
+template <int NC>
+__device__ __forceinline__ void tmem_ldn(uint32_t taddr, float (&v)[NC]) {
+  static_assert(NC == 4 || NC == 8, "4 or 8 columns");
+  uint32_t r[NC];
+  if constexpr (NC == 8) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr)
+                 : "memory");
+  } else {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(taddr)
+                 : "memory");
+  }
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+  for (int i = 0; i < NC; ++i) v[i] = __uint_as_float(r[i]);
 }
-
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
-  uint32_t r[8];
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-               : "r"(taddr)
-               : "memory");
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
-}
-
 
 // Two signed bytes (positions 0,1 or 2,3 of w, already xor 0x80) as f16x2
 // exactly: 0x6400 | u is 1024 + u, minus 1152 gives u - 128 = q.
@@ -219,13 +224,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_q80(const GemmArgs a) {
     }
     for (int i = 0; i < kActStages; ++i) {
       mbar_init(&x_full[i], 1);
-      mbar_init(&x_empty[i], 1);  // released by the MMA commit
+      mbar_init(&x_empty[i], kIssuers);  // released by the issuers' MMA commits
     }
     for (int i = 0; i < kAStages; ++i) {
-      mbar_init(&a_full[i], kDqWarps / 2);  // the four warps of one group
+      mbar_init(&a_full[i], kDqWarps / 4);  // the four warps of one group
       mbar_init(&a_empty[i], 1);
     }
-    mbar_init(acc_full, 1);
+    mbar_init(acc_full, kIssuers);
     *abort_s = 0;
     mbar_fence_init();
   }
@@ -236,10 +241,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_q80(const GemmArgs a) {
   const uint32_t tmem = *tmem_s;
 
   if (warp == 0) {
-    // ---- producer: lane 0 streams the weight tiles (they do not depend on
-    // the previous kernel, so it starts at once), lane 1 the activation
-    // tiles (after the dependency wait); independent rings, so weights run
-    // ahead as far as their ring allows.
+    // ---- weight producer (lane 0): the weights do not depend on the
+    // previous kernel, so it starts at once and runs ahead as far as its
+    // ring allows; the activation tiles come from warp kActWarp after the
+    // dependency wait, on a ring of their own.
     if (lane == 0) {
       // this row tile's block list in its segment
       int R = row0;
@@ -265,7 +270,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_q80(const GemmArgs a) {
       }
       for (int i = issued > kRawStages ? issued - kRawStages : 0; i < issued; ++i)
         if (!mbar_wait(&raw_full[i % kRawStages], (uint32_t)(i / kRawStages) & 1u, a.err)) break;
-    } else if (lane == 1) {
+    }
+    __syncwarp();
+  } else if (warp == kActWarp) {
+    if (lane == 0) {
       pdl_wait();
       int issued = 0;
       for (int i = 0; i < nkt; ++i) {
@@ -280,65 +288,61 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_q80(const GemmArgs a) {
         if (!mbar_wait(&x_full[i % kActStages], (uint32_t)(i / kActStages) & 1u, a.err)) break;
     }
     __syncwarp();
-  } else if (warp == 1) {
-    // ---- MMA issuer (one thread) ----
+  } else if (warp < kDq0) {
+    // ---- MMA issuers: lane 0 of warp 1 + q issues quarter q of every K-tile ----
     if (lane == 0) {
+      const int q = warp - 1;
       const uint32_t idesc = umma_idesc_f16(N);
       const uint32_t sbo = 128, lbo_b = (N / 8) * 128;
-      bool ok = true;
-      for (int i = 0; i < nkt && ok; ++i) {
+      const uint32_t acc = tmem + (uint32_t)(q * N);
+      for (int i = 0; i < nkt; ++i) {
         const int s = i % kActStages;
         if (!gwait(&x_full[s], (uint32_t)(i / kActStages) & 1u, a.err, abort_s)) break;
-        for (int qt = 0; qt < 4; ++qt) {
-          const int sa = qt + 4 * (i & 1);
-          if (!gwait(&a_full[sa], (uint32_t)(i >> 1) & 1u, a.err, abort_s)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t a_tm = tmem + kTmemA + (uint32_t)sa * 32;  // 4 columns of K per 8 values
-          const uint32_t b_base = smem_addr(act_st + (size_t)s * act_bytes(N)) + (uint32_t)(qt * 8) * lbo_b;
+        const int sa = q + 4 * (i & 1);
+        if (!gwait(&a_full[sa], (uint32_t)(i >> 1) & 1u, a.err, abort_s)) break;
+        tc_fence_after();
+        const uint32_t a_tm = tmem + kTmemA + (uint32_t)sa * 32;  // 4 columns of K per 8 values
+        const uint32_t b_base = smem_addr(act_st + (size_t)s * act_bytes(N)) + (uint32_t)(q * 8) * lbo_b;
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t bd = umma_desc(b_base + kk * 2 * lbo_b, lbo_b, sbo);
-            umma_f16_ts(tmem, a_tm + (uint32_t)kk * 8, bd, idesc, (i | qt | kk) != 0 ? 1u : 0u);
-          }
-          umma_commit(&a_empty[sa]);
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint64_t bd = umma_desc(b_base + kk * 2 * lbo_b, lbo_b, sbo);
+          umma_f16_ts(acc, a_tm + (uint32_t)kk * 8, bd, idesc, (i | kk) != 0 ? 1u : 0u);
         }
-        if (ok) umma_commit(&x_empty[s]);
+        umma_commit(&a_empty[sa]);
+        umma_commit(&x_empty[s]);
       }
       // after every MMA issued, on every path: the epilogue reads the
-      // accumulator (or, on abort, only waits) before tensor memory is freed
+      // accumulators (or, on abort, only waits) before tensor memory is freed
       umma_commit(acc_full);
     }
     __syncwarp();
   } else {
     // ---- dequantising warps, then the epilogue (waits warp-uniform).  Warp
-    // w belongs to group h = (w-2)/4, which converts quarters h and h+2 of
-    // every K-tile (A stages h and h+2: while the tensor cores read one, the
-    // group fills the other) for rows 32*(w%4) .. +31 (= its tensor-memory
-    // lane quarter); in the epilogue it takes sequence columns
-    // [h*N/2, h*N/2 + N/2).
-    const int h = (warp - 2) >> 2;
+    // w belongs to group h = (w-5)/4, which converts quarter h of every
+    // K-tile (A stages h and h+4 alternate: while the tensor cores read one,
+    // the group fills the other) for rows 32*(w%4) .. +31 (= its
+    // tensor-memory lane quarter); in the epilogue it takes sequence columns
+    // [h*N/4, h*N/4 + N/4).
+    const int h = (warp - kDq0) >> 2;
     const int r = ((warp & 3) << 5) | lane;
     for (int i = 0; i < nkt; ++i) {
       const int s = i % kRawStages;
       if (!__all_sync(0xffffffffu, gwait(&raw_full[s], (uint32_t)(i / kRawStages) & 1u, a.err, abort_s))) break;
       bool ok = true;
-      for (int t = 0; t < 2 && ok; ++t) {
-        const int qt = h + 2 * t, sa = qt + 4 * (i & 1);
+      {
+        const int qt = h, sa = qt + 4 * (i & 1);
         if (i > 1 && !__all_sync(0xffffffffu, gwait(&a_empty[sa], (uint32_t)(((i >> 1) - 1) & 1), a.err, abort_s))) {
           ok = false;
-          break;
+        } else {
+          uint32_t aw[32];
+          dequant_quarter(raw_st + (size_t)s * kRawBytes, aw, r, qt);
+          tc_fence_after();  // after the MMAs that read this stage before (a_empty)
+          tmem_st32(tmem + ((uint32_t)((warp & 3) * 32) << 16) + kTmemA + (uint32_t)sa * 32, aw);
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&a_full[sa]);
         }
-        uint32_t aw[32];
-        dequant_quarter(raw_st + (size_t)s * kRawBytes, aw, r, qt);
-        tc_fence_after();  // after the MMAs that read this stage before (a_empty)
-        tmem_st32(tmem + ((uint32_t)((warp & 3) * 32) << 16) + kTmemA + (uint32_t)sa * 32, aw);
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&a_full[sa]);
       }
       if (!ok) break;
       __syncwarp();
@@ -346,17 +350,19 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_q80(const GemmArgs a) {
     }
     const bool go = __all_sync(0xffffffffu, mbar_wait(acc_full, 0u, a.err) && !*abort_s);
     tc_fence_after();
-    constexpr int NH = N / 2;
+    constexpr int NH = N / 4;
     const int c0 = h * NH;
     float v[NH];
 #pragma unroll
     for (int c = 0; c < NH; ++c) v[c] = 0.0f;
     if (go) {
       const uint32_t taddr = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)c0;
-      if constexpr (NH == 16) {
-        tmem_ld16(taddr, v);
-      } else {
-        tmem_ld8(taddr, v);
+#pragma unroll
+      for (int q = 0; q < kIssuers; ++q) {
+        float u[NH];
+        tmem_ldn<NH>(taddr + (uint32_t)(q * N), u);
+#pragma unroll
+        for (int c = 0; c < NH; ++c) v[c] = q == 0 ? u[c] : __fadd_rn(v[c], u[c]);
       }
     }
     const int row = row0 + r;
@@ -377,7 +383,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_q80(const GemmArgs a) {
       for (int n = 0; n < NH; ++n) a.partial[((size_t)split * N + c0 + n) * a.rows_total + row] = v[n];
       __threadfence();
       asm volatile("bar.sync 1, %0;" ::"n"(kDqWarps * 32) : "memory");
-      if (warp == 2 && lane == 0) ticket_s = atomicAdd(&a.counters[tile], 1u);
+      if (warp == kDq0 && lane == 0) ticket_s = atomicAdd(&a.counters[tile], 1u);
       asm volatile("bar.sync 1, %0;" ::"n"(kDqWarps * 32) : "memory");
       if (ticket_s == (unsigned)(a.ksplit - 1)) {
         __threadfence();
@@ -399,7 +405,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_q80(const GemmArgs a) {
             *y = a.epi == kGemmAdd ? __fadd_rn(*y, sum[n]) : sum[n];
           }
         }
-        if (warp == 2 && lane == 0) a.counters[tile] = 0u;
+        if (warp == kDq0 && lane == 0) a.counters[tile] = 0u;
       }
     }
   }
