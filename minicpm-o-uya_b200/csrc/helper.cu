@@ -605,12 +605,13 @@ int attn_cluster_cfg() {
   return v;
 }
 
-// CTAs per kv head and sequence of the batched attention: 4 once the batch
-// supplies 64 or more (sequence, kv head) pairs (measured best at B = 8 and
-// B = 32 with 8 kv heads), else about four CTAs per SM over the batch, at
-// most the single-sequence count; MCPO_ATTN_BATCH_SPLIT overrides.  The
-// batched attention merges through global memory (16-CTA clusters of many
-// sequences schedule poorly).
+// CTAs per kv head and sequence of the batched attention: as many as fit
+// one wave at two CTAs per SM over the batch's (sequence, kv head) pairs,
+// at least one and at most the single-sequence count (8B shape, 8 kv heads,
+// position ~1040: B = 32 runs 5159 tok/s with one CTA per pair against
+// 4735 / 4702 / 4542 / 4079 with 4 / 2 / 8 / 16); MCPO_ATTN_BATCH_SPLIT
+// overrides.  The batched attention merges through global memory (16-CTA
+// clusters of many sequences schedule poorly).
 int attn_batch_split_cfg(int single, int batch, int n_kv, int sms) {
   static const int v = [] {
     const char* e = getenv("MCPO_ATTN_BATCH_SPLIT");
@@ -618,7 +619,7 @@ int attn_batch_split_cfg(int single, int batch, int n_kv, int sms) {
   }();
   if (v >= 1 && v <= kAttnMaxCluster) return v;
   const int pairs = batch * n_kv;
-  const int per = pairs >= 64 ? 4 : (pairs > 0 ? (4 * sms + pairs - 1) / pairs : single);
+  const int per = pairs > 0 ? (2 * sms) / pairs : single;
   return per < 1 ? 1 : (per < single ? per : single);
 }
 
