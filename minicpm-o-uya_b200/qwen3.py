@@ -255,12 +255,13 @@ class Qwen3Runtime:
 
 
 def format_bench_lines(r: Dict[str, float], repetitions: int, stats: dict) -> List[str]:
-    """The reference's bench rate lines (qwen3.uya:2378-2399, 2950-2971)."""
+    """The reference's bench rate lines (qwen3.uya:2374-2399, 2950-2971), in its integer arithmetic:
+    times are whole microseconds, the rate is units * 10^9 // micros (tokens/s x 1000)."""
     def rate(label, units, us):
-        scaled = int(units * 1e9 // us) if us else 0
-        ms = int(us)
+        micros = int(us)
+        scaled = units * 1_000_000_000 // micros if micros else 0
         return (f"bench {label}: {scaled // 1000}.{scaled % 1000:03d} tokens/s units={units} "
-                f"ms={ms // 1000}.{ms % 1000:03d} repetitions={repetitions}")
+                f"ms={micros // 1000}.{micros % 1000:03d} repetitions={repetitions}")
 
     return [
         rate("text_prompt", int(r["prompt_tokens"]), r["prompt_us"]),

@@ -120,6 +120,35 @@ def test_device_decode_matches_host_loop(pkg, O):
     rt.close()
 
 
+def test_runtime_bench_and_output_lines(pkg, O):
+    """Qwen3Runtime.bench (the reference's `bench` loop, qwen3.uya:2774-2973: prompt, then n_gen
+    decode steps feeding the seed ids cyclically) and its output lines with the context's stats."""
+    from minicpmo_b200 import gguf
+    from minicpmo_b200.qwen3 import Qwen3Runtime, format_bench_lines
+
+    shape = small_shape()
+    tensors = build(pkg, shape, gguf.Q4_K_M)
+    rt = Qwen3Runtime.open(tensors, shape=shape, context=shape.context)
+    prompt = gguf.prompt_ids(9, shape.vocab, seed=5)
+    r = rt.bench(prompt, n_gen=6, repetitions=2)
+    assert r["prompt_tokens"] == 18 and r["decode_tokens"] == 12
+    assert r["prompt_us"] > 0 and r["decode_us"] > 0 and 0 < r["first_token_us"] <= r["decode_us"]
+    assert rt.total_tokens == 9 + 6  # each repetition starts from an empty context
+    stats = rt.gpu.snapshot()
+    lines = format_bench_lines(r, 2, stats)
+    assert lines[0].startswith("bench text_prompt: ") and " units=18 " in lines[0]
+    assert lines[1].startswith("bench text_decode: ") and " units=12 " in lines[1]
+    assert f"weights_uploaded={stats['uploaded_weight_count']}" in lines[3]
+    assert stats["uploaded_weight_count"] >= len(tensors) and lines[-1] == "bench: PASS"
+    # the same prompt after bench gives the tokens of a fresh context
+    rt.reset()
+    a = rt.append_prompt_ids(prompt)
+    rt2 = Qwen3Runtime.open(tensors, shape=shape, context=shape.context)
+    assert rt2.append_prompt_ids(prompt) == a
+    rt.close()
+    rt2.close()
+
+
 def test_slot_api_forward_matches_fused(pkg, O):
     """Drive the reference's per-op orchestration (qwen3_forward_embedding_runtime_cuda,
     qwen3.uya:1865-1918) through the 19-symbol ABI and compare with the fused step."""
