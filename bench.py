@@ -676,7 +676,8 @@ def main() -> int:
         "dtype": "q4_k/q6_k x q8_1 (int8 dp4a, f32 accumulate)",
         "data": "synthetic: seeded N(0,0.02) weights quantised Q4_K_M-style, 512 uniform random prompt ids",
         "config": {
-            "workload": f"{args.shape}-shape Q4_K_M greedy decode after a {args.prompt}-token prompt (BASELINE config 2)",
+            "workload": f"{args.shape}-shape Q4_K_M greedy decode after a {args.prompt}-token prompt "
+                        f"(BASELINE config {4 if args.shape == 'qwen3-32b' else 0 if args.shape == 'qwen3-0.6b' else 2})",
             "layers": shape.layers, "hidden": shape.hidden, "heads": shape.heads, "kv_heads": shape.kv_heads,
             "ffn": shape.ffn, "vocab": shape.vocab, "prompt": args.prompt, "decode_positions": [start_pos, start_pos + args.steps],
             "kv_cache": "f32",
