@@ -6,11 +6,14 @@
 // keep up with, so the weights are dequantised to f16 into tensor memory and
 // multiplied on the tensor cores with f32 accumulation in tensor memory:
 //
-//   warp 0      producer: per 256-value K-tile, one bulk copy of the tile's
-//               Q8_0 bytes (the weights are re-tiled at upload so that the
-//               128 rows x 8 blocks of a (row tile, K-tile) pair are one
-//               34816-byte block) and one bulk copy of the f16 activation
-//               tile (N x 256, already in the operand layout);
+//   warp 0      weight producer: per 256-value K-tile, one bulk copy of the
+//               tile's Q8_0 bytes (the weights are re-tiled at upload so
+//               that the 128 rows x 8 blocks of a (row tile, K-tile) pair
+//               are one 34816-byte block), started before the dependency
+//               wait (the weights do not depend on the previous kernel);
+//   warp 21     activation producer: per K-tile one bulk copy of the f16
+//               activation tile (N x 256, already in the operand layout),
+//               after the dependency wait;
 //   warps 5..20 dequantise: thread = (row, quarter of the K-tile), q * d in
 //               f16 (int8 -> f16 exactly via the 0x6400 exponent trick, one
 //               rounding in the multiply), stored into the A stage in tensor
